@@ -1,0 +1,309 @@
+#!/usr/bin/env python3
+"""Benchmark of the quantized Dense forward path on B200.
+
+Metric: quant Dense weight GB/s (GEMV, % HBM). Workload at N=1: BASELINE
+config 2 -- Dense GEMV 4096->4096, batch 1, FP4 (E2M1, 2 codes/byte, reference layout),
+W ~ N(0, 0.02), x ~ N(0, 1), seed 1. One step = one forward pass through a chain of 64
+distinct 4096x4096 FP4 layers (layer i's post is layer i+1's x), so each step streams
+512 MiB of packed weights -- more than the 126 MB L2, no flush needed. Weights are random
+(synthetic; the reference ships no checkpoints).
+
+  value  weight GB/s with x/weights resident in HBM (device-pointer entry point, PDL chain)
+  e2e    the same metric through the reference-facing C ABI welvet_dense_execute, host
+         buffers (pinned), H2D of x and D2H of pre/post inside the timed region
+N > 1 (torchrun): every rank runs its own chain (independent layers, weak scaling, no
+collective on the data path); value = all ranks' bytes / max-over-ranks time.
+
+--impl reference times the reference semantics on the host cores (the oracle port of
+kernels.cu:130-161 with the reference decode), the only CPU implementation of this path.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+IN = OUT = 4096
+LAYERS = 64
+DTYPE_FP4 = 16
+SIGMA = 0.02
+SEED = 1
+WEIGHT_BYTES_PER_LAYER = OUT * IN // 2  # FP4: 0.5 B / weight
+
+
+def peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def traffic_from_profile():
+    """Per-launch DRAM bytes of the GEMV from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", "gemv_fp4_4096x4096_b1.md")
+    try:
+        for ln in open(p):
+            if ln.startswith("dram_bytes_per_launch:"):
+                return int(ln.split(":")[1].strip())
+    except Exception:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.rows.append([c.strip() for c in ln.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            for i, n in enumerate(names):
+                if len(r) > 4 + i and r[4 + i].lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+def cpu_baseline(seconds: float = 10.0):
+    """The oracle port of the reference semantics on all host threads, on a bounded sample:
+    whole 4096x4096 FP4 layers of the same workload until ~`seconds` of CPU time."""
+    import oracle as O
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(SEED)
+    w = (rng.standard_normal((OUT, IN)) * SIGMA).astype(np.float32)
+    raw, sc = O.pack(DTYPE_FP4, w)
+    x = rng.standard_normal((1, IN)).astype(np.float32)
+    O.dense_forward(DTYPE_FP4, raw, sc, x, IN, OUT, -1, None, threads)  # warm
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        O.dense_forward(DTYPE_FP4, raw, sc, x, IN, OUT, -1, None, threads)
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": n * WEIGHT_BYTES_PER_LAYER / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} forwards of one 4096x4096 FP4 layer, B=1 ({dt:.1f} s): reference decode + "
+                      f"sequential fp64 dot (oracle/oracle.c), rows split over {threads} threads"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import oracle as O
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(SEED)
+    w = (rng.standard_normal((OUT, IN)) * SIGMA).astype(np.float32)
+    raw, sc = O.pack(DTYPE_FP4, w)
+    x = rng.standard_normal((1, IN)).astype(np.float32)
+    for _ in range(args.warmup):
+        O.dense_forward(DTYPE_FP4, raw, sc, x, IN, OUT, -1, None, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.dense_forward(DTYPE_FP4, raw, sc, x, IN, OUT, -1, None, threads)
+    dt = time.perf_counter() - t0
+    val = args.steps * WEIGHT_BYTES_PER_LAYER / dt / 1e9
+    line = {"metric": "quant Dense weight GB/s (GEMV)", "value": val, "unit": "GB/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp4 codes, fp64 accumulate",
+            "data": "synthetic",
+            "config": {"workload": "C2 Dense GEMV 4096->4096 B=1 FP4 (one layer per step on the host)",
+                       "global_batch": 1, "parallelism": "host threads"},
+            "cpu_baseline": {"value": val, "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": "one 4096x4096 FP4 layer forward per step: reference decode + sequential "
+                                       "fp64 dot (oracle/oracle.c; the reference ships no host matvec)"},
+            "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    import welvet.cuda_b200 as W
+    W.cuda_init()
+
+    # ---- mount LAYERS distinct layers (weights generated on the device, per rank seed)
+    g = torch.Generator(device="cuda").manual_seed(SEED * 1000 + rank)
+    sessions = []
+    for _ in range(LAYERS):
+        wdev = torch.randn((OUT, IN), device="cuda", generator=g) * SIGMA
+        sessions.append(W.DenseSession(wdev, 1, DTYPE_FP4))
+        del wdev
+    torch.cuda.synchronize()
+    x0 = torch.randn((1, IN), device="cuda", generator=g)
+    acts = [torch.zeros((1, OUT), device="cuda") for _ in range(2)]
+    pre = torch.zeros((1, OUT), device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step():
+        x = x0
+        for i, s in enumerate(sessions):
+            y = acts[i & 1]
+            s.execute_device(x, pre, y, stream)
+            x = y
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        barrier()
+    ms = e0.elapsed_time(e1)
+    ms = max_over_ranks(ms)
+    launches = args.steps * LAYERS
+    bytes_per_step = LAYERS * WEIGHT_BYTES_PER_LAYER
+    value = world * bytes_per_step * args.steps / (ms / 1e3) / 1e9
+    per_launch_s = (ms / 1e3) / launches
+
+    # ---- e2e through the reference-facing ABI (host buffers, pinned)
+    xh = torch.randn((1, IN)).pin_memory()
+    bufs = [torch.zeros((1, OUT)).pin_memory() for _ in range(2)]
+    preh = torch.zeros((1, OUT)).pin_memory()
+    xh_np, bufs_np, preh_np = xh.numpy(), [b.numpy() for b in bufs], preh.numpy()
+    e2e_steps = max(1, min(args.steps, 20))
+
+    def e2e_step():
+        x = xh_np
+        for i, s in enumerate(sessions):
+            y = bufs_np[i & 1]
+            s.execute(x, preh_np, y)
+            x = y
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    t_e2e = max_over_ranks(time.perf_counter() - t0)
+    e2e_val = world * bytes_per_step * e2e_steps / t_e2e / 1e9
+
+    pk, pk_kind = peaks()
+    achieved = WEIGHT_BYTES_PER_LAYER / per_launch_s / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / pk["hbm_gbs"], "traffic": traffic_from_profile(),
+                "peak_source": f"{pk_kind} hbm_gbs (MEASURED_PEAKS.json)" if pk_kind == "measured" else "fallback",
+                "kernel": "k_gemv<FP4,B=1> (welvet/cuda_b200/csrc/gemv.cu)",
+                "algorithmic_bytes_per_launch": WEIGHT_BYTES_PER_LAYER}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.cpu_seconds)
+
+    if rank == 0:
+        line = {"metric": "quant Dense weight GB/s (GEMV)", "value": value, "unit": "GB/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp4 codes, fp32/fp64 accumulate",
+                "data": "synthetic",
+                "config": {"workload": "C2 Dense GEMV 4096->4096 B=1 FP4 (W~N(0,0.02), seed 1), 64 distinct layers "
+                                       "chained per step",
+                           "global_batch": world, "seq_len": 1, "parallelism": f"replicas x{world}",
+                           "l2": "inputs larger than L2 (512 MiB of packed weights per step)",
+                           "bytes_per_step_per_gpu": bytes_per_step},
+                "roofline": roofline,
+                "cpu_baseline": cpu,
+                "e2e": {"value": e2e_val, "unit": "GB/s", "h2d_bytes_per_step": LAYERS * IN * 4,
+                        "d2h_bytes_per_step": LAYERS * OUT * 4 * 2, "steps": e2e_steps,
+                        "api": "welvet_dense_execute (host pinned buffers, synchronous per layer)"},
+                "gpu_launches": launches,
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    for s in sessions:
+        s.release()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,106 @@
+#pragma once
+
+/*
+ * welvet_b200.h -- additive entry points of libwelvet_b200.so. None of these exists in the
+ * reference; they extend its Dense-session ABI (include/welvet_c.h:81-86) with device
+ * pointers, CUDA streams, a native-bytes mount, persistent SwiGLU / MHA cells, a device-
+ * resident volume chain and the codec kernels, without changing any reference symbol.
+ *
+ * Device-pointer calls run asynchronously on the given stream (`stream` is a cudaStream_t;
+ * NULL selects the session's own stream) and must not overlap another call on the same
+ * session. Host-pointer calls are synchronous like the reference ABI.
+ */
+
+#include "welvet_c.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Library build identifier, e.g. "welvet-b200 0.1 sm_100a". */
+WELVET_API const char* welvet_b200_build_id(void);
+
+/* ---------------------------------------------------------------- Dense */
+
+/* Like welvet_dense_mount, with W_dev a device pointer to the float32 matrix (no H2D copy
+ * of the unquantized weights). bias stays a host pointer. */
+WELVET_API welvet_status welvet_b200_dense_mount_device(int32_t batch, int32_t in, int32_t out,
+                                                        int32_t act, int32_t dtype, const float* W_dev,
+                                                        const double* bias, size_t bias_len,
+                                                        welvet_dense_session** sess_out);
+
+/* Mount from a FormatNone store already packed in the reference layout (native bytes and
+ * per-tensor scale, e.g. read back from an NWS1 snapshot). */
+WELVET_API welvet_status welvet_b200_dense_mount_native(int32_t batch, int32_t in, int32_t out,
+                                                        int32_t act, int32_t dtype,
+                                                        const uint8_t* native, size_t native_len,
+                                                        float scale, const double* bias,
+                                                        size_t bias_len,
+                                                        welvet_dense_session** sess_out);
+
+/* Forward with device pointers: x_dev [batch][in], pre_dev/post_dev [batch][out]. */
+WELVET_API welvet_status welvet_b200_dense_execute_device(welvet_dense_session* sess,
+                                                          const float* x_dev, float* pre_dev,
+                                                          float* post_dev, void* stream);
+
+/* The session's authoritative host store: dtype, rows (= out), cols (= in), scale and the
+ * native bytes in the reference layout (FP4: low nibble = even flat index). Float32 stores
+ * return their float payload. *native_len is always set; the bytes are copied when
+ * cap >= *native_len. */
+WELVET_API welvet_status welvet_b200_dense_store(welvet_dense_session* sess, int32_t* dtype,
+                                                 int32_t* rows, int32_t* cols, float* scale,
+                                                 uint8_t* native_out, size_t cap,
+                                                 size_t* native_len);
+
+/* ---------------------------------------------------------------- codecs (device buffers) */
+
+/* FormatNone encode of n float32 values (device) to reference-layout bytes (device) and the
+ * per-tensor scale (device float). Bit-exact with the reference host codec. */
+WELVET_API welvet_status welvet_b200_codec_encode(int32_t dtype, const float* w_dev, int64_t n,
+                                                  uint8_t* native_dev, float* scale_dev,
+                                                  void* stream);
+/* Reference-semantics decode of n elements (device) to float32 (device). */
+WELVET_API welvet_status welvet_b200_codec_decode(int32_t dtype, const uint8_t* native_dev,
+                                                  int64_t n, float scale, float* out_dev,
+                                                  void* stream);
+/* Exhaustive-encode digest: sum over float32 bit patterns i in [start, start+count) of
+ * splitmix64((i << 8) | code(i)) mod 2^64; codec 0 = E4M3, 1 = E5M2, 2 = FP4. Synchronous. */
+WELVET_API welvet_status welvet_b200_codec_digest(int32_t codec, uint64_t start, uint64_t count,
+                                                  uint64_t* digest);
+/* Every code through the GEMV's vector decoders (after device canonicalisation):
+ * FP4 -> 512 floats (256 bytes, low nibble first), FP8E4M3/FP8E5M2/Int8 -> 256 floats. */
+WELVET_API welvet_status welvet_b200_codec_selftest_decode(int32_t dtype, float* out_host);
+
+/* ---------------------------------------------------------------- SwiGLU cell */
+
+typedef struct welvet_b200_swiglu welvet_b200_swiglu;
+/* Gate/Up [intermediate x input], Down [input x intermediate] float32; weights_on_device
+ * selects device or host pointers. */
+WELVET_API welvet_status welvet_b200_swiglu_mount(int32_t input_dim, int32_t intermediate_dim,
+                                                  int32_t dtype, const float* Gate, const float* Up,
+                                                  const float* Down, int32_t weights_on_device,
+                                                  welvet_b200_swiglu** out);
+/* rows = batch*seq. h_dev [rows][intermediate] may be NULL; y_dev [rows][input]. */
+WELVET_API welvet_status welvet_b200_swiglu_execute_device(welvet_b200_swiglu* s, int32_t rows,
+                                                           const float* x_dev, float* h_dev,
+                                                           float* y_dev, void* stream);
+WELVET_API void welvet_b200_swiglu_release(welvet_b200_swiglu* s);
+
+/* ---------------------------------------------------------------- MHA cell */
+
+typedef struct welvet_b200_mha welvet_b200_mha;
+WELVET_API welvet_status welvet_b200_mha_mount(int32_t d_model, int32_t num_heads,
+                                               int32_t num_kv_heads, int32_t head_dim,
+                                               int32_t max_seq_len, int32_t mask, int32_t pos,
+                                               int32_t dtype, const float* Q, const float* K,
+                                               const float* V, const float* O,
+                                               int32_t weights_on_device, welvet_b200_mha** out);
+/* x_dev [batch*seq][d_model] -> attn_dev [batch*seq][q_dim] (may be NULL), y_dev [..][d_model]. */
+WELVET_API welvet_status welvet_b200_mha_execute_device(welvet_b200_mha* s, int32_t batch,
+                                                        int32_t seq, const float* x_dev,
+                                                        float* attn_dev, float* y_dev, void* stream);
+WELVET_API void welvet_b200_mha_release(welvet_b200_mha* s);
+
+#ifdef __cplusplus
+}
+#endif

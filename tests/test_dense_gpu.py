@@ -1,0 +1,311 @@
+"""GPU parity: the sm_100a library, called through its C ABI, against the oracle and the
+reference's golden fixtures (and, where oracle/_ref travelled with the tree, against the
+reference's own CUDA Dense path run on the same GPU).
+
+Tolerance for Dense outputs (fp32 products accumulated per 16-byte vector, then fp64):
+    |pre - pre_oracle| <= 2^-18 * sum_k |W[o,k] x[k]| + 2 ulp(pre_oracle)
+codecs and stores: bit exact.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, pack_cases
+
+pytestmark = pytest.mark.gpu
+
+TOL_REL = 2.0 ** -18
+ACTS = [-1, 0, 1, 2, 3, 4, 5, 6]
+
+
+def ulp(a):
+    return np.spacing(np.abs(np.asarray(a, np.float32))).astype(np.float64)
+
+
+def lipschitz(act, v):
+    v = np.abs(np.asarray(v, np.float64))
+    return {-1: 1.0, 0: 1.0, 1: 1.1, 2: 1.13, 3: 1.0, 4: 0.25, 5: 1.0}.get(act, None) if act != 6 else 2 * v + 1
+
+
+def check_dense(pre, post, ref, act, what=""):
+    pre_o, post_o, y64, sabs = ref
+    pre = np.asarray(pre, np.float32).reshape(pre_o.shape)
+    post = np.asarray(post, np.float32).reshape(post_o.shape)
+    err = np.abs(pre.astype(np.float64) - pre_o.astype(np.float64))
+    bound = TOL_REL * sabs + 2 * ulp(pre_o)
+    bad = ~(err <= bound)
+    both_nan = np.isnan(pre) & np.isnan(pre_o)
+    bad &= ~both_nan
+    assert not bad.any(), f"{what} pre: {bad.sum()} outside tolerance, worst {np.nanmax(err - bound)}"
+    L = lipschitz(act, pre_o)
+    perr = np.abs(post.astype(np.float64) - post_o.astype(np.float64))
+    pbound = L * bound + 2 * ulp(post_o) + 1e-300
+    pbad = ~(perr <= pbound) & ~(np.isnan(post) & np.isnan(post_o))
+    assert not pbad.any(), f"{what} post: {pbad.sum()} outside tolerance"
+    return float(np.mean(pre.view(np.uint32) == pre_o.view(np.uint32)))
+
+
+# ---------------------------------------------------------------- codecs
+
+def test_hot_path_decoders_match_reference_tables(wb):
+    """Hardware e2m1/e4m3/e5m2 converters on canonical codes == reference decode, per lane."""
+    t = json.load(open(os.path.join(GOLDEN, "codec_tables.json")))
+    fp4 = np.array(t["fp4"], np.uint32).view(np.float32)
+    got = wb.codec_selftest_decode(wb.FP4)
+    want = np.array([fp4[(b >> (4 * i)) & 0xF] for b in range(256) for i in range(2)], np.float32)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    for dt, key in ((wb.FP8E4M3, "e4m3"), (wb.FP8E5M2, "e5m2")):
+        got = wb.codec_selftest_decode(dt)
+        want = np.array(t[key], np.uint32).view(np.float32)
+        nan = np.isnan(want)
+        assert np.array_equal(np.isnan(got), nan), key
+        assert np.array_equal(got[~nan].view(np.uint32), want[~nan].view(np.uint32)), key
+    got = wb.codec_selftest_decode(wb.INT8)
+    assert np.array_equal(got, np.arange(256).astype(np.uint8).view(np.int8).astype(np.float32))
+
+
+def test_exhaustive_encode_digests(wb):
+    """Every float32 bit pattern through the GPU encoders == the reference codec."""
+    d = json.load(open(os.path.join(GOLDEN, "encode_digests.json")))
+    n = 1 << d["chunk_bits"]
+    for codec, row in enumerate(d["digests"]):
+        got = [format(wb.codec_digest(codec, c * n, n), "016x") for c in range(len(row))]
+        mism = [c for c in range(len(row)) if got[c] != row[c]]
+        assert not mism, f"codec {d['codecs'][codec]}: chunks {mism[:8]} differ"
+
+
+def test_device_encode_and_decode_bit_exact(wb, packs):
+    import torch
+    for name, dt, rows, cols, scale, w, raw, dec in pack_cases(packs):
+        wt = torch.from_numpy(w).cuda()
+        nat = torch.zeros(raw.size, dtype=torch.uint8, device="cuda")
+        sc = torch.zeros(1, dtype=torch.float32, device="cuda")
+        wb.codec_encode(dt, wt, nat, sc)
+        torch.cuda.synchronize()
+        assert np.array_equal(nat.cpu().numpy(), raw), name
+        assert sc.cpu().numpy().view(np.uint32)[0] == np.float32(scale).view(np.uint32), name
+        out = torch.zeros(rows * cols, dtype=torch.float32, device="cuda")
+        wb.codec_decode(dt, nat, rows * cols, scale, out)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy().astype(np.float64)
+        want = dec.ravel()
+        nan = np.isnan(want)
+        assert np.array_equal(np.isnan(got), nan), name
+        assert np.array_equal(got[~nan].view(np.uint64), want[~nan].view(np.uint64)), name
+
+
+def test_mount_store_is_reference_bytes(wb, packs):
+    """welvet_dense_mount keeps an authoritative host store byte-identical to the reference."""
+    for name, dt, rows, cols, scale, w, raw, dec in pack_cases(packs):
+        s = wb.DenseSession(w.reshape(rows, cols), 1, dt)
+        sdt, r, c, sc, buf = s.store()
+        s.release()
+        assert (sdt, r, c) == (dt, rows, cols), name
+        assert np.array_equal(buf, raw), name
+        assert np.float32(sc).view(np.uint32) == np.float32(scale).view(np.uint32), name
+
+
+# ---------------------------------------------------------------- Dense forward
+
+def _case(oracle, dt, out, in_, batch, sigma, seed, act=-1, with_bias=True, bias_len=None):
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((out, in_)) * sigma).astype(np.float32)
+    x = rng.standard_normal((batch, in_)).astype(np.float32)
+    bias = None
+    if with_bias:
+        bias = rng.standard_normal(out if bias_len is None else bias_len) * 0.1
+    if dt == oracle.FLOAT32:
+        raw, sc = w.view(np.uint8).ravel(), 1.0
+    else:
+        raw, sc = oracle.pack(dt, w)
+    ref = oracle.dense_forward(dt, raw, sc, x, in_, out, act, bias)
+    return w, x, bias, ref
+
+
+@pytest.mark.parametrize("dt", [16, 4, 5, 9, 1])
+@pytest.mark.parametrize("shape", [(64, 96, 1), (7, 13, 1), (33, 130, 3), (130, 257, 2), (96, 64, 9), (1, 1, 1),
+                                   (300, 4100, 4), (5, 33, 5)])
+def test_dense_forward_parity(wb, oracle, dt, shape):
+    out, in_, batch = shape
+    for act in ACTS if shape == (64, 96, 1) else [-1, 0]:
+        w, x, bias, ref = _case(oracle, dt, out, in_, batch, 2.0, out * 1000 + in_ + act, act)
+        pre, post = wb.dense_forward_f32(w, x, dt, act, bias)
+        check_dense(pre, post, ref, act, f"dt={dt} shape={shape} act={act}")
+
+
+def test_bias_shorter_and_longer_than_out(wb, oracle):
+    """Only rows o < bias_len get a bias (src/cuda/kernels.cu:154-157)."""
+    for blen in (3, 50):
+        w, x, bias, ref = _case(oracle, oracle.FP8E4M3, 20, 40, 2, 2.0, 7, 0, True, blen)
+        pre, post = wb.dense_forward_f32(w, x, oracle.FP8E4M3, 0, bias)
+        check_dense(pre, post, ref, 0, f"bias_len={blen}")
+
+
+def test_c1_config(wb, oracle):
+    """Dense 256->128 E4M3, W~N(0,0.05), bias~N(0,0.01), x~U[-1,1], seed 0."""
+    rng = np.random.default_rng(0)
+    w = (rng.standard_normal((128, 256)) * 0.05).astype(np.float32)
+    bias = rng.standard_normal(128) * 0.01
+    x = rng.uniform(-1, 1, (1, 256)).astype(np.float32)
+    raw, sc = oracle.pack(oracle.FP8E4M3, w)
+    for act in (-1, 0):
+        ref = oracle.dense_forward(oracle.FP8E4M3, raw, sc, x, 256, 128, act, bias)
+        s = wb.DenseSession(w, 1, oracle.FP8E4M3, act, bias)
+        pre, post = s.execute(x)
+        frac = check_dense(pre, post, ref, act, "C1")
+        assert frac > 0.9, frac
+        s.release()
+
+
+@pytest.mark.parametrize("dt,sigma", [(16, 0.02), (16, 2.0), (9, 0.02), (4, 0.02), (5, 2.0)])
+def test_c2_full_size(wb, oracle, dt, sigma):
+    """BASELINE config 2 shape (4096->4096, B=1, x~N(0,1), seed 1); FP4 at sigma 0.02 is all
+    zero codes (reference FP4 has no scale), sigma 2.0 is the non-degenerate companion."""
+    rng = np.random.default_rng(1)
+    w = (rng.standard_normal((4096, 4096)) * sigma).astype(np.float32)
+    x = rng.standard_normal((1, 4096)).astype(np.float32)
+    raw, sc = oracle.pack(dt, w)
+    ref = oracle.dense_forward(dt, raw, sc, x, 4096, 4096, -1, None)
+    s = wb.DenseSession(w, 1, dt)
+    pre, post = s.execute(x)
+    frac = check_dense(pre, post, ref, -1, f"C2 dt={dt} sigma={sigma}")
+    if dt == 16 and sigma == 0.02:
+        assert not np.any(pre)  # every FP4 code is 0
+    else:
+        assert frac > 0.5, frac
+    s.release()
+
+
+def test_execute_device_matches_host(wb, oracle):
+    import torch
+    w, x, bias, ref = _case(oracle, oracle.FP4, 512, 1024, 3, 2.0, 3, 1)
+    s = wb.DenseSession(w, 3, oracle.FP4, 1, bias)
+    pre_h, post_h = s.execute(x)
+    xd = torch.from_numpy(x).cuda()
+    pre_d = torch.zeros(3, 512, device="cuda")
+    post_d = torch.zeros(3, 512, device="cuda")
+    s.execute_device(xd, pre_d, post_d)
+    torch.cuda.synchronize()
+    assert np.array_equal(pre_d.cpu().numpy(), pre_h) and np.array_equal(post_d.cpu().numpy(), post_h)
+    # weights mounted from device memory produce the same store and outputs
+    s2 = wb.DenseSession(torch.from_numpy(w).cuda(), 3, oracle.FP4, 1, bias)
+    assert np.array_equal(s2.store()[4], s.store()[4])
+    pre2, post2 = s2.execute(x)
+    assert np.array_equal(pre2, pre_h)
+    s.release()
+    s2.release()
+
+
+def test_mount_native_bytes(wb, oracle, packs):
+    for name, dt, rows, cols, scale, w, raw, dec in pack_cases(packs):
+        if "specials" in name:
+            continue
+        rng = np.random.default_rng(rows + cols)
+        x = rng.standard_normal((2, cols)).astype(np.float32)
+        ref = oracle.dense_forward(dt, raw, scale, x, cols, rows, -1, None)
+        s = wb.DenseSession(None, 2, dt, native=raw, scale=scale, shape=(rows, cols))
+        pre, post = s.execute(x)
+        check_dense(pre, post, ref, -1, name)
+        s.release()
+
+
+def test_status_codes(wb):
+    w = np.ones((4, 4), np.float32)
+    x = np.ones((1, 4), np.float32)
+    with pytest.raises(wb.WelvetError) as e:
+        wb.dense_forward_f32(w, x, 26)  # NF4: not on this path
+    assert e.value.code == wb.UNSUPPORTED
+    with pytest.raises(wb.WelvetError) as e:
+        wb.dense_forward_f32(np.ones((0, 4), np.float32), x, wb.FP4)
+    assert e.value.code == wb.INVALID
+
+
+# ---------------------------------------------------------------- cells
+
+def test_swiglu_parity(wb, oracle):
+    rng = np.random.default_rng(2)
+    d, inter, batch, seq = 96, 160, 2, 3
+    for dt in (oracle.FP8E4M3, oracle.FP4, oracle.INT8):
+        G, U, D = [(rng.standard_normal(s) * 0.5).astype(np.float32) for s in ((inter, d), (inter, d), (d, inter))]
+        x = rng.standard_normal((batch * seq, d)).astype(np.float32)
+        pre, post = wb.swiglu_forward_f32(G, U, D, x, batch, seq, dt)
+        rg, sg = oracle.pack(dt, G)
+        ru, su = oracle.pack(dt, U)
+        rd, sd = oracle.pack(dt, D)
+        gp, _, _, _ = oracle.dense_forward(dt, rg, sg, x, d, inter)
+        _, upp, _, _ = oracle.dense_forward(dt, ru, su, x, d, inter)
+        h = oracle.swiglu_product(gp, upp)
+        np.testing.assert_allclose(pre.reshape(h.shape), h, rtol=2e-5, atol=2e-5 * np.abs(h).max())
+        ref = oracle.dense_forward(dt, rd, sd, pre.reshape(h.shape), inter, d)
+        check_dense(post, post, ref, -1, f"swiglu down dt={dt}")
+
+
+def test_rmsnorm_parity(wb, oracle):
+    rng = np.random.default_rng(3)
+    batch, seq, dim = 2, 5, 200
+    g = rng.standard_normal(dim).astype(np.float32)
+    x = rng.standard_normal(batch * seq * dim).astype(np.float32)
+    pre, post = wb.rmsnorm_forward_f32(g, x, batch, seq, dim, 1e-6, wb.FLOAT32)
+    xx = x.reshape(-1, dim).astype(np.float64)
+    inv = 1.0 / np.sqrt((xx * xx).sum(1, keepdims=True) / dim + 1e-6)
+    np.testing.assert_allclose(pre.reshape(-1, dim), (xx * inv).astype(np.float32), rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(post.reshape(-1, dim), (xx * inv * g.astype(np.float64)).astype(np.float32),
+                               rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(batch=2, seq=6, d=32, nh=4, nkv=2, hd=8, msl=8, mask=1, pos=0),   # ring wraps across batches
+    dict(batch=1, seq=5, d=24, nh=3, nkv=3, hd=8, msl=16, mask=2, pos=2),  # bidirectional + ALiBi
+    dict(batch=3, seq=4, d=32, nh=2, nkv=1, hd=16, msl=4, mask=1, pos=3),  # RoPE+ALiBi, GQA, msl == seq
+])
+def test_mha_parity(wb, oracle, cfg):
+    from oracle.attention import attention
+    rng = np.random.default_rng(4)
+    c = cfg
+    qd, kvd = c["nh"] * c["hd"], c["nkv"] * c["hd"]
+    Q = (rng.standard_normal((qd, c["d"])) * 0.3).astype(np.float32)
+    K = (rng.standard_normal((kvd, c["d"])) * 0.3).astype(np.float32)
+    V = (rng.standard_normal((kvd, c["d"])) * 0.3).astype(np.float32)
+    O = (rng.standard_normal((c["d"], qd)) * 0.3).astype(np.float32)
+    x = rng.standard_normal((c["batch"] * c["seq"], c["d"])).astype(np.float32)
+    dt = oracle.FP8E4M3
+    pre, post = wb.mha_forward_f32(Q, K, V, O, x, c["batch"], c["seq"], c["d"], c["nh"], c["nkv"], c["hd"],
+                                   c["msl"], c["mask"], c["pos"], dt)
+    proj = []
+    for M, rows in ((Q, qd), (K, kvd), (V, kvd)):
+        r, s = oracle.pack(dt, M)
+        proj.append(oracle.dense_forward(dt, r, s, x, c["d"], rows)[1])
+    att = attention(*proj, c["batch"], c["seq"], c["nh"], c["nkv"], c["hd"], c["msl"], c["mask"], c["pos"])
+    np.testing.assert_allclose(pre.reshape(att.shape), att, rtol=1e-4, atol=1e-5)
+    r, s = oracle.pack(dt, O)
+    ref = oracle.dense_forward(dt, r, s, pre.reshape(att.shape), qd, c["d"])
+    check_dense(post, post, ref, -1, "mha O")
+
+
+# ---------------------------------------------------------------- against the reference's own CUDA path
+
+@pytest.mark.skipif(not __import__("oracle").ref_available(), reason="oracle/_ref not built")
+def test_dense_vs_reference_cuda_kernel(wb, oracle):
+    """Same seeded inputs through the reference's resident session (its fp64 kernel, rebuilt
+    for sm_100a) and through this library: outputs within the stated tolerance of each other
+    and of the fp64 oracle."""
+    import ctypes
+    R = oracle.ref()
+    for dt in (oracle.FP8E4M3, oracle.FP4, oracle.INT8, oracle.FP8E5M2):
+        w, x, bias, ref = _case(oracle, dt, 256, 512, 2, 2.0, 11, 2)
+        sess = ctypes.c_void_p()
+        msg = ctypes.create_string_buffer(256)
+        wp = w.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        bp = bias.ctypes.data_as(ctypes.POINTER(ctypes.c_double))
+        assert R.ref_dense_mount(2, 512, 256, 2, dt, wp, bp, bias.size, ctypes.byref(sess), msg, 256) == 0, msg.value
+        pre_r = np.zeros((2, 256), np.float32)
+        post_r = np.zeros((2, 256), np.float32)
+        f = lambda a: a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        assert R.ref_dense_execute(sess, f(x), f(pre_r), f(post_r), msg, 256) == 0, msg.value
+        R.ref_dense_release(sess)
+        # the reference kernel itself agrees with the oracle bit for bit on pre
+        assert np.array_equal(pre_r, ref[0])
+        pre, post = wb.dense_forward_f32(w, x, dt, 2, bias)
+        check_dense(pre, post, (pre_r, post_r, ref[2], ref[3]), 2, f"vs reference dt={dt}")

@@ -1,0 +1,344 @@
+"""welvet.cuda_b200 -- Python host binding of libwelvet_b200.so (the sm_100a library).
+
+The functions here mirror the reference's C ABI (include/welvet_c.h) one for one, with the
+same argument meaning and the same status codes, raising `WelvetError` for a non-zero
+status. Device-pointer variants accept torch CUDA tensors. There is no CPU path: importing
+this module without the built library raises ImportError.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from ctypes import POINTER, byref, c_char, c_double, c_float, c_int32, c_int64, c_size_t, c_uint8, c_uint64, c_void_p
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libwelvet_b200.so")
+
+# DType ids (reference include/welvet/dtype.hpp:9-44) served on the GPU.
+FLOAT32, FP8E4M3, FP8E5M2, INT8, FP4 = 1, 4, 5, 9, 16
+DTYPES = {"float32": FLOAT32, "fp8e4m3": FP8E4M3, "fp8e5m2": FP8E5M2, "int8": INT8, "fp4": FP4}
+# Activation ids (reference include/welvet/activate.hpp:8-17).
+LINEAR, RELU, SILU, GELU, TANH, SIGMOID, LEAKY_RELU, RELU2 = -1, 0, 1, 2, 3, 4, 5, 6
+# Status codes (reference include/welvet_c.h:26-29).
+OK, INVALID, UNSUPPORTED, GAP, INTERNAL = 0, 1, 2, 3, 4
+
+
+class welvet_status(ctypes.Structure):
+    _fields_ = [("code", c_int32), ("message", c_char * 256)]
+
+
+class WelvetError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"welvet status {code}: {message}")
+        self.code = code
+        self.message = message
+
+
+def build() -> None:
+    """Compile libwelvet_b200.so for sm_100a (nvcc; no GPU needed)."""
+    subprocess.run(["make", "-C", os.path.join(HERE, "csrc"), "-j8", "-s"], check=True)
+
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"welvet.cuda_b200: {LIB_PATH} is not built (run welvet.cuda_b200.build() / make -C "
+                      f"welvet/cuda_b200/csrc); there is no CPU fallback")
+
+_L = ctypes.CDLL(LIB_PATH)
+
+_f32p, _f64p, _u8p = POINTER(c_float), POINTER(c_double), POINTER(c_uint8)
+_ST = welvet_status
+
+
+def _sig(name, res, *args):
+    fn = getattr(_L, name)
+    fn.restype = res
+    fn.argtypes = list(args)
+    return fn
+
+
+_sig("welvet_version", ctypes.c_char_p)
+_sig("welvet_runtime_identity", ctypes.c_char_p)
+_sig("welvet_b200_build_id", ctypes.c_char_p)
+_sig("welvet_cuda_init", _ST)
+_sig("welvet_cuda_available", c_int32)
+_sig("welvet_gaps_count", c_int32)
+_sig("welvet_gaps_done", c_int32)
+_sig("welvet_dense_forward_f32", _ST, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p,
+     c_size_t, c_void_p, c_void_p, c_void_p)
+_sig("welvet_dense_mount", _ST, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_size_t,
+     POINTER(c_void_p))
+_sig("welvet_b200_dense_mount_device", _ST, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p,
+     c_size_t, POINTER(c_void_p))
+_sig("welvet_b200_dense_mount_native", _ST, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_size_t,
+     c_float, c_void_p, c_size_t, POINTER(c_void_p))
+_sig("welvet_dense_execute", _ST, c_void_p, c_void_p, c_void_p, c_void_p)
+_sig("welvet_b200_dense_execute_device", _ST, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p)
+_sig("welvet_dense_release", None, c_void_p)
+_sig("welvet_b200_dense_store", _ST, c_void_p, POINTER(c_int32), POINTER(c_int32), POINTER(c_int32),
+     POINTER(c_float), c_void_p, c_size_t, POINTER(c_size_t))
+_sig("welvet_rmsnorm_forward_f32", _ST, c_int32, c_int32, c_int32, c_double, c_int32, c_int32, c_void_p, c_void_p,
+     c_void_p, c_void_p)
+_sig("welvet_swiglu_forward_f32", _ST, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p,
+     c_void_p, c_void_p, c_void_p, c_void_p)
+_sig("welvet_mha_forward_f32", _ST, *([c_int32] * 11), *([c_void_p] * 7))
+_sig("welvet_b200_codec_encode", _ST, c_int32, c_void_p, c_int64, c_void_p, c_void_p, c_void_p)
+_sig("welvet_b200_codec_decode", _ST, c_int32, c_void_p, c_int64, c_float, c_void_p, c_void_p)
+_sig("welvet_b200_codec_digest", _ST, c_int32, c_uint64, c_uint64, POINTER(c_uint64))
+_sig("welvet_b200_codec_selftest_decode", _ST, c_int32, c_void_p)
+_sig("welvet_b200_swiglu_mount", _ST, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_int32,
+     POINTER(c_void_p))
+_sig("welvet_b200_swiglu_execute_device", _ST, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p)
+_sig("welvet_b200_swiglu_release", None, c_void_p)
+_sig("welvet_b200_mha_mount", _ST, *([c_int32] * 8), *([c_void_p] * 4), c_int32, POINTER(c_void_p))
+_sig("welvet_b200_mha_execute_device", _ST, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p)
+_sig("welvet_b200_mha_release", None, c_void_p)
+
+
+def lib() -> ctypes.CDLL:
+    return _L
+
+
+def check(st: welvet_status) -> None:
+    if st.code != OK:
+        raise WelvetError(st.code, st.message.decode(errors="replace"))
+
+
+def _np_ptr(a):
+    return None if a is None else a.ctypes.data_as(c_void_p)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _dev_ptr(t) -> int:
+    """Device pointer of a torch CUDA tensor (contiguous)."""
+    if not t.is_cuda or not t.is_contiguous():
+        raise ValueError("expected a contiguous CUDA tensor")
+    return t.data_ptr()
+
+
+def _stream_ptr(stream) -> c_void_p:
+    if stream is None:
+        import torch
+        return c_void_p(torch.cuda.current_stream().cuda_stream)
+    return c_void_p(getattr(stream, "cuda_stream", stream))
+
+
+def version() -> str:
+    return _L.welvet_version().decode()
+
+
+def runtime_identity() -> str:
+    return _L.welvet_runtime_identity().decode()
+
+
+def cuda_init() -> None:
+    check(_L.welvet_cuda_init())
+
+
+def cuda_available() -> bool:
+    return bool(_L.welvet_cuda_available())
+
+
+# ------------------------------------------------------------------ Dense
+
+def dense_forward_f32(W: np.ndarray, x: np.ndarray, dtype: int, act: int = LINEAR, bias=None):
+    """welvet_dense_forward_f32: W [out, in] float32, x [batch, in] -> (pre, post) [batch, out]."""
+    W = _f32(W)
+    out, in_ = W.shape
+    x = _f32(x).reshape(-1, in_)
+    batch = x.shape[0]
+    pre = np.zeros((batch, out), np.float32)
+    post = np.zeros((batch, out), np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float64)
+    check(_L.welvet_dense_forward_f32(batch, in_, out, act, dtype, 0, _np_ptr(W), _np_ptr(b),
+                                      0 if b is None else b.size, _np_ptr(x), _np_ptr(pre), _np_ptr(post)))
+    return pre, post
+
+
+class DenseSession:
+    """welvet_dense_mount / execute / release (+ device-pointer extensions)."""
+
+    def __init__(self, W, batch: int, dtype: int, act: int = LINEAR, bias=None, *, native=None, scale: float = 1.0,
+                 shape=None):
+        self._h = c_void_p()
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float64)
+        blen = 0 if b is None else b.size
+        if native is not None:
+            out, in_ = shape
+            raw = np.ascontiguousarray(native, dtype=np.uint8)
+            check(_L.welvet_b200_dense_mount_native(batch, in_, out, act, dtype, _np_ptr(raw), raw.size, scale,
+                                                    _np_ptr(b), blen, byref(self._h)))
+        elif hasattr(W, "is_cuda"):
+            out, in_ = W.shape
+            check(_L.welvet_b200_dense_mount_device(batch, in_, out, act, dtype, c_void_p(_dev_ptr(W)), _np_ptr(b),
+                                                    blen, byref(self._h)))
+        else:
+            W = _f32(W)
+            out, in_ = W.shape
+            check(_L.welvet_dense_mount(batch, in_, out, act, dtype, _np_ptr(W), _np_ptr(b), blen, byref(self._h)))
+        self.batch, self.in_, self.out, self.dtype = batch, in_, out, dtype
+
+    def execute(self, x: np.ndarray, pre: np.ndarray | None = None, post: np.ndarray | None = None):
+        x = _f32(x)
+        if pre is None:
+            pre = np.zeros((self.batch, self.out), np.float32)
+        if post is None:
+            post = np.zeros((self.batch, self.out), np.float32)
+        check(_L.welvet_dense_execute(self._h, _np_ptr(x), _np_ptr(pre), _np_ptr(post)))
+        return pre, post
+
+    def execute_device(self, x, pre, post, stream=None) -> None:
+        check(_L.welvet_b200_dense_execute_device(self._h, c_void_p(_dev_ptr(x)), c_void_p(_dev_ptr(pre)),
+                                                  c_void_p(_dev_ptr(post)), _stream_ptr(stream)))
+
+    def store(self):
+        """(dtype, rows, cols, scale, native bytes in the reference layout)."""
+        dt, r, c, sc, ln = c_int32(), c_int32(), c_int32(), c_float(), c_size_t()
+        check(_L.welvet_b200_dense_store(self._h, byref(dt), byref(r), byref(c), byref(sc), None, 0, byref(ln)))
+        buf = np.zeros(ln.value, np.uint8)
+        check(_L.welvet_b200_dense_store(self._h, byref(dt), byref(r), byref(c), byref(sc), _np_ptr(buf), buf.size,
+                                         byref(ln)))
+        return dt.value, r.value, c.value, sc.value, buf
+
+    def release(self) -> None:
+        if self._h:
+            _L.welvet_dense_release(self._h)
+            self._h = c_void_p()
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------------ cells
+
+def rmsnorm_forward_f32(gamma, x, batch: int, seq: int, dim: int, eps: float = 1e-6, dtype: int = FLOAT32):
+    g = _f32(gamma)
+    x = _f32(x)
+    pre = np.zeros(batch * seq * dim, np.float32)
+    post = np.zeros_like(pre)
+    check(_L.welvet_rmsnorm_forward_f32(batch, seq, dim, eps, dtype, 0, _np_ptr(g), _np_ptr(x), _np_ptr(pre),
+                                        _np_ptr(post)))
+    return pre, post
+
+
+def swiglu_forward_f32(G, U, D, x, batch: int, seq: int, dtype: int):
+    G, U, D, x = _f32(G), _f32(U), _f32(D), _f32(x)
+    inter, in_ = G.shape
+    pre = np.zeros(batch * seq * inter, np.float32)
+    post = np.zeros(batch * seq * in_, np.float32)
+    check(_L.welvet_swiglu_forward_f32(batch, seq, in_, inter, dtype, 0, _np_ptr(G), _np_ptr(U), _np_ptr(D),
+                                       _np_ptr(x), _np_ptr(pre), _np_ptr(post)))
+    return pre, post
+
+
+def mha_forward_f32(Q, K, V, O, x, batch: int, seq: int, d_model: int, num_heads: int, num_kv_heads: int = 0,
+                    head_dim: int = 0, max_seq_len: int = 0, mask: int = 1, pos: int = 0, dtype: int = FLOAT32):
+    Q, K, V, O, x = _f32(Q), _f32(K), _f32(V), _f32(O), _f32(x)
+    hd = head_dim if head_dim > 0 else d_model // num_heads
+    q_dim = num_heads * hd
+    pre = np.zeros(batch * seq * q_dim, np.float32)
+    post = np.zeros(batch * seq * d_model, np.float32)
+    check(_L.welvet_mha_forward_f32(batch, seq, d_model, num_heads, num_kv_heads, head_dim, max_seq_len, mask, pos,
+                                    dtype, 0, _np_ptr(Q), _np_ptr(K), _np_ptr(V), _np_ptr(O), _np_ptr(x),
+                                    _np_ptr(pre), _np_ptr(post)))
+    return pre, post
+
+
+class SwigluCell:
+    """Persistent SwiGLU cell (welvet_b200_swiglu_*): weights as torch CUDA tensors or numpy."""
+
+    def __init__(self, G, U, D, dtype: int):
+        self._h = c_void_p()
+        on_dev = hasattr(G, "is_cuda")
+        if on_dev:
+            ptrs = [c_void_p(_dev_ptr(t)) for t in (G, U, D)]
+            self._keep = None
+        else:
+            self._keep = [_f32(t) for t in (G, U, D)]
+            ptrs = [_np_ptr(t) for t in self._keep]
+        inter, in_ = G.shape
+        check(_L.welvet_b200_swiglu_mount(in_, inter, dtype, *ptrs, 1 if on_dev else 0, byref(self._h)))
+        self._keep = None
+        self.in_, self.inter = in_, inter
+
+    def execute_device(self, x, y, h=None, stream=None) -> None:
+        rows = x.shape[0]
+        check(_L.welvet_b200_swiglu_execute_device(self._h, rows, c_void_p(_dev_ptr(x)),
+                                                   None if h is None else c_void_p(_dev_ptr(h)),
+                                                   c_void_p(_dev_ptr(y)), _stream_ptr(stream)))
+
+    def release(self):
+        if self._h:
+            _L.welvet_b200_swiglu_release(self._h)
+            self._h = c_void_p()
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+
+class MhaCell:
+    """Persistent MHA cell (welvet_b200_mha_*)."""
+
+    def __init__(self, Q, K, V, O, d_model: int, num_heads: int, num_kv_heads: int = 0, head_dim: int = 0,
+                 max_seq_len: int = 0, mask: int = 1, pos: int = 0, dtype: int = FLOAT32):
+        self._h = c_void_p()
+        on_dev = hasattr(Q, "is_cuda")
+        if on_dev:
+            ptrs = [c_void_p(_dev_ptr(t)) for t in (Q, K, V, O)]
+        else:
+            keep = [_f32(t) for t in (Q, K, V, O)]
+            ptrs = [_np_ptr(t) for t in keep]
+        check(_L.welvet_b200_mha_mount(d_model, num_heads, num_kv_heads, head_dim, max_seq_len, mask, pos, dtype,
+                                       *ptrs, 1 if on_dev else 0, byref(self._h)))
+
+    def execute_device(self, x, batch: int, seq: int, y, attn=None, stream=None) -> None:
+        check(_L.welvet_b200_mha_execute_device(self._h, batch, seq, c_void_p(_dev_ptr(x)),
+                                                None if attn is None else c_void_p(_dev_ptr(attn)),
+                                                c_void_p(_dev_ptr(y)), _stream_ptr(stream)))
+
+    def release(self):
+        if self._h:
+            _L.welvet_b200_mha_release(self._h)
+            self._h = c_void_p()
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------------ codecs
+
+def codec_digest(codec: int, start: int, count: int) -> int:
+    d = c_uint64()
+    check(_L.welvet_b200_codec_digest(codec, start, count, byref(d)))
+    return int(d.value)
+
+
+def codec_selftest_decode(dtype: int) -> np.ndarray:
+    out = np.zeros(512 if dtype == FP4 else 256, np.float32)
+    check(_L.welvet_b200_codec_selftest_decode(dtype, _np_ptr(out)))
+    return out
+
+
+def codec_encode(dtype: int, w, native, scale, stream=None) -> None:
+    """Device encode: w float32 CUDA tensor -> native uint8 CUDA tensor, scale float32[1] CUDA tensor."""
+    check(_L.welvet_b200_codec_encode(dtype, c_void_p(_dev_ptr(w)), w.numel(), c_void_p(_dev_ptr(native)),
+                                      c_void_p(_dev_ptr(scale)), _stream_ptr(stream)))
+
+
+def codec_decode(dtype: int, native, n: int, scale: float, out, stream=None) -> None:
+    check(_L.welvet_b200_codec_decode(dtype, c_void_p(_dev_ptr(native)), n, scale, c_void_p(_dev_ptr(out)),
+                                      _stream_ptr(stream)))

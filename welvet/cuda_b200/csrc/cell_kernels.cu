@@ -1,0 +1,264 @@
+// cell_kernels.cu -- the non-projection kernels of the RMSNorm / MHA cells (sm_100a), in
+// float64 like the reference, but parallel instead of one thread per token / one thread
+// for the whole attention.
+//
+//   rmsnorm_forward   src/cuda/kernels.cu:172-204 (norm_forward_f64 with center = 0)
+//   mha rope prep     src/cuda/kernels.cu:487-505 (mha_apply_rope at the global position)
+//   mha attention     src/cuda/kernels.cu:536-632 (mha_attention_forward_f64, ModeSelf)
+//
+// Attention semantics kept from the reference: batches run in order against one KV ring of
+// max_seq_len slots; token (b, s) has global position p = b*seq + s and is written to slot
+// p % msl before batch b's queries run; a query of batch b scans k_pos in [0, (b+1)*seq)
+// and, for an allowed k_pos, reads slot k_pos % msl -- which then holds the latest position
+// p' <= (b+1)*seq-1 with p' == k_pos (mod msl). Masks and ALiBi use k_pos; RoPE of the key
+// was applied at p'. The running max starts at -1e9 as in the reference.
+#include "cell_kernels.hpp"
+
+namespace wb {
+namespace {
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ double warp_max_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// One warp per token.
+__global__ void k_rmsnorm(const float* __restrict__ x, const double* __restrict__ gamma,
+                          float* __restrict__ pre, float* __restrict__ post, int n_tok, int dim,
+                          double eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= n_tok) return;
+  const float* xt = x + static_cast<int64_t>(warp) * dim;
+  double ss = 0.0;
+  for (int i = lane; i < dim; i += 32) {
+    const double v = static_cast<double>(xt[i]);
+    ss += v * v;
+  }
+  ss = warp_sum_d(ss);
+  const double inv = 1.0 / sqrt(ss / static_cast<double>(dim) + eps);
+  float* pt = pre + static_cast<int64_t>(warp) * dim;
+  float* qt = post + static_cast<int64_t>(warp) * dim;
+  for (int i = lane; i < dim; i += 32) {
+    const double xh = static_cast<double>(xt[i]) * inv;
+    pt[i] = static_cast<float>(xh);
+    qt[i] = static_cast<float>(xh * gamma[i]);
+  }
+}
+
+// Widen projections to f64 and rotate Q and K at each token's global position.
+// One thread per (token, head, d < half) pair, plus plain copies for V / unrotated tails.
+__global__ void k_rope_prep(const float* __restrict__ q, const float* __restrict__ k,
+                            const float* __restrict__ v, double* __restrict__ Qr,
+                            double* __restrict__ Kr, double* __restrict__ Vd, int bs, int num_heads,
+                            int num_kv, int head_dim, int use_rope, double theta) {
+  const int q_dim = num_heads * head_dim;
+  const int kv_dim = num_kv * head_dim;
+  const int64_t total = static_cast<int64_t>(bs) * (q_dim + 2 * kv_dim);
+  const int half = head_dim / 2;
+  const bool rot = use_rope && half > 0 && theta > 0.0;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int tok = static_cast<int>(t / (q_dim + 2 * kv_dim));
+    int c = static_cast<int>(t - static_cast<int64_t>(tok) * (q_dim + 2 * kv_dim));
+    const float* src;
+    double* dst;
+    int width;
+    bool rotate = rot;
+    if (c < q_dim) {
+      src = q + static_cast<int64_t>(tok) * q_dim; dst = Qr + static_cast<int64_t>(tok) * q_dim; width = q_dim;
+    } else if (c < q_dim + kv_dim) {
+      c -= q_dim;
+      src = k + static_cast<int64_t>(tok) * kv_dim; dst = Kr + static_cast<int64_t>(tok) * kv_dim; width = kv_dim;
+    } else {
+      c -= q_dim + kv_dim;
+      src = v + static_cast<int64_t>(tok) * kv_dim; dst = Vd + static_cast<int64_t>(tok) * kv_dim; width = kv_dim;
+      rotate = false;
+    }
+    (void)width;
+    const int d = c % head_dim;
+    const int base = c - d;
+    if (!rotate || d >= 2 * half) {
+      dst[c] = static_cast<double>(src[c]);
+      continue;
+    }
+    const int dd = d < half ? d : d - half;
+    const double angle = static_cast<double>(tok) /
+                         pow(theta, static_cast<double>(2 * dd) / static_cast<double>(head_dim));
+    const double cs = cos(angle);
+    const double sn = sin(angle);
+    const double v0 = static_cast<double>(src[base + dd]);
+    const double v1 = static_cast<double>(src[base + dd + half]);
+    dst[c] = d < half ? v0 * cs - v1 * sn : v0 * sn + v1 * cs;
+  }
+}
+
+__device__ __forceinline__ bool attn_allow(int q_pos, int k_pos, int mask, int window, int msl,
+                                           int prefix_len, int window_causal) {
+  if (mask == 2) return true;
+  if (mask == 3) {
+    const int w = window > 0 ? window : msl;
+    if (window_causal) return k_pos <= q_pos && k_pos >= q_pos - w + 1;
+    int d = q_pos - k_pos;
+    if (d < 0) d = -d;
+    return d < w;
+  }
+  if (mask == 4) {
+    if (q_pos < prefix_len && k_pos < prefix_len) return true;
+    return k_pos <= q_pos;
+  }
+  return k_pos <= q_pos;
+}
+
+__device__ __forceinline__ double alibi(int head, int num_heads, int q_pos, int k_pos) {
+  const int n = num_heads <= 0 ? 1 : num_heads;
+  const double slope = pow(2.0, -static_cast<double>(head + 1) * 8.0 / static_cast<double>(n));
+  const int diff = q_pos - k_pos;
+  return -slope * static_cast<double>(diff < 0 ? -diff : diff);
+}
+
+constexpr int kMaxHeadDim = 256;
+
+// One warp per (token, head). Lanes score 32 keys at a time (one each), then the warp
+// folds them into an online softmax with lanes owning head_dim/32 output dimensions.
+__global__ void k_attention(const double* __restrict__ Qr, const double* __restrict__ Kr,
+                            const double* __restrict__ Vd, float* __restrict__ out, int batch,
+                            int seq, int num_heads, int num_kv, int head_dim, int msl, int mask,
+                            int use_alibi, int use_sigmoid, int window, int prefix_len,
+                            int window_causal, double scale) {
+  __shared__ double qs[4][kMaxHeadDim];
+  const int wib = threadIdx.x >> 5;
+  const int warp = blockIdx.x * 4 + wib;
+  const int lane = threadIdx.x & 31;
+  const int bs = batch * seq;
+  if (warp >= bs * num_heads) return;
+  const int tok = warp / num_heads;
+  const int h = warp - tok * num_heads;
+  const int b = tok / seq;
+  const int q_pos = tok;  // b*seq + s
+  const int kv_len = (b + 1) * seq;
+  const int q_dim = num_heads * head_dim;
+  const int kv_dim = num_kv * head_dim;
+  const int kvh = h / (num_heads / num_kv);
+  for (int d = lane; d < head_dim; d += 32) qs[wib][d] = Qr[static_cast<int64_t>(tok) * q_dim + h * head_dim + d];
+  __syncwarp();
+
+  constexpr int kPer = kMaxHeadDim / 32;
+  double acc[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) acc[i] = 0.0;
+  double m = -1e9;  // running max (reference initial value)
+  double l = 0.0;   // running sum of exp(score - m)
+  int n = 0;
+
+  for (int k0 = 0; k0 < kv_len; k0 += 32) {
+    const int k_pos = k0 + lane;
+    bool ok = k_pos < kv_len && attn_allow(q_pos, k_pos, mask, window, msl, prefix_len, window_causal);
+    double score = 0.0;
+    int p = 0;
+    if (ok) {
+      const int slot = k_pos % msl;
+      p = slot + msl * ((kv_len - 1 - slot) / msl);  // latest position written to this slot
+      const double* kr = Kr + static_cast<int64_t>(p) * kv_dim + kvh * head_dim;
+      double dot = 0.0;
+      for (int d = 0; d < head_dim; ++d) dot += qs[wib][d] * kr[d];
+      score = dot * scale + (use_alibi ? alibi(h, num_heads, q_pos, k_pos) : 0.0);
+    }
+    const unsigned okmask = __ballot_sync(0xffffffffu, ok);
+    if (okmask == 0) continue;
+    n += __popc(okmask);
+    double w;
+    if (use_sigmoid) {
+      w = ok ? 1.0 / (1.0 + exp(-score)) : 0.0;
+    } else {
+      const double cm = warp_max_d(ok ? score : -INFINITY);
+      const double m_new = fmax(m, cm);
+      const double corr = exp(m - m_new);
+      w = ok ? exp(score - m_new) : 0.0;
+      l = l * corr + warp_sum_d(w);
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) acc[i] *= corr;
+      m = m_new;
+    }
+    // Fold the chunk's weighted V rows: lanes own dims lane, lane+32, ...
+    unsigned rem = okmask;
+    while (rem) {
+      const int j = __ffs(rem) - 1;
+      rem &= rem - 1;
+      const double wj = __shfl_sync(0xffffffffu, w, j);
+      const int pj = __shfl_sync(0xffffffffu, p, j);
+      const double* vr = Vd + static_cast<int64_t>(pj) * kv_dim + kvh * head_dim;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int d = lane + 32 * i;
+        if (d < head_dim) acc[i] += wj * vr[d];
+      }
+    }
+  }
+  float* o = out + static_cast<int64_t>(tok) * q_dim + h * head_dim;
+  const double inv = (n == 0 || use_sigmoid) ? 1.0 : 1.0 / l;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int d = lane + 32 * i;
+    if (d < head_dim) o[d] = n == 0 ? 0.0f : static_cast<float>(acc[i] * inv);
+  }
+}
+
+// h = float(double(float(SiLU(double(g)))) * double(up)) -- src/cuda/kernels.cu:296-305.
+__global__ void k_swiglu_product(const float* __restrict__ g, const float* __restrict__ u,
+                                 float* __restrict__ h, int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const double x = static_cast<double>(g[i]);
+    const float gf = static_cast<float>(x / (1.0 + exp(-x)));
+    h[i] = static_cast<float>(static_cast<double>(gf) * static_cast<double>(u[i]));
+  }
+}
+
+} // namespace
+
+Status launch_rmsnorm(const float* x, const double* gamma, float* pre, float* post, int n_tok, int dim,
+                      double eps, cudaStream_t st) {
+  const int threads = 256;
+  const int blocks = static_cast<int>((static_cast<int64_t>(n_tok) * 32 + threads - 1) / threads);
+  k_rmsnorm<<<blocks, threads, 0, st>>>(x, gamma, pre, post, n_tok, dim, eps);
+  return cuda_status(cudaGetLastError(), "rmsnorm launch");
+}
+
+Status launch_mha_attention(const float* q, const float* k, const float* v, double* Qr, double* Kr,
+                            double* Vd, float* out, const AttnParams& p, cudaStream_t st) {
+  if (p.head_dim > kMaxHeadDim) return Status::Unsupported("mha: head_dim > 256");
+  const int bs = p.batch * p.seq;
+  const int64_t total = static_cast<int64_t>(bs) * (p.num_heads + 2 * p.num_kv) * p.head_dim;
+  int blocks = static_cast<int>((total + 255) / 256);
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  const bool use_rope = p.pos_kind == 0 || p.pos_kind == 3;
+  k_rope_prep<<<blocks, 256, 0, st>>>(q, k, v, Qr, Kr, Vd, bs, p.num_heads, p.num_kv, p.head_dim,
+                                      use_rope ? 1 : 0, p.rope_theta);
+  WB_CUDA(cudaGetLastError());
+  double scale = p.scale_override;
+  if (scale <= 0.0) scale = 1.0 / sqrt(static_cast<double>(p.head_dim));
+  const int warps = bs * p.num_heads;
+  const bool use_alibi = p.pos_kind == 2 || p.pos_kind == 3;
+  k_attention<<<(warps + 3) / 4, 128, 0, st>>>(Qr, Kr, Vd, out, p.batch, p.seq, p.num_heads, p.num_kv,
+                                              p.head_dim, p.max_seq_len, p.mask, use_alibi ? 1 : 0,
+                                              p.softmax_kind == 1 ? 1 : 0, p.window, p.prefix_len,
+                                              p.window_causal, scale);
+  return cuda_status(cudaGetLastError(), "attention launch");
+}
+
+Status launch_swiglu_product(const float* g, const float* u, float* h, int64_t n, cudaStream_t st) {
+  int blocks = static_cast<int>((n + 255) / 256);
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  k_swiglu_product<<<blocks, 256, 0, st>>>(g, u, h, n);
+  return cuda_status(cudaGetLastError(), "swiglu product launch");
+}
+
+} // namespace wb

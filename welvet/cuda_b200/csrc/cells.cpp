@@ -1,0 +1,246 @@
+// cells.cpp -- SwiGLU / MHA / RMSNorm cells over the packed Dense mirror.
+//
+// SwiGLU (src/layers/swiglu/swiglu.cpp:87-136): the reference runs Gate and Up as two Dense
+// forwards, copies both back to the host, launches the SiLU product with a per-call
+// allocation and runs Down. Here Gate and Up stream in one fused GEMV whose epilogue writes
+// h directly (padded for Down), and Down reads h on the device.
+// MHA (src/layers/mha/mha.cpp:123-183): Q/K/V Dense, attention core, O Dense -- all on the
+// device with no host round trip.
+#include "cells.hpp"
+
+#include "codec.hpp"
+#include "gemv.hpp"
+
+#include <cmath>
+#include <vector>
+
+namespace wb {
+
+namespace {
+template <typename T>
+void free_dev(T*& p) {
+  if (p) cudaFree(p);
+  p = nullptr;
+}
+} // namespace
+
+void SwigluCell::release_work() {
+  cudaSetDevice(device);
+  free_dev(x_pad);
+  free_dev(h_pad);
+  bs = 0;
+}
+
+Status swiglu_mount(int device, int in, int inter, DType dt, const float* G, const float* U, const float* D,
+                    bool w_is_device, SwigluCell* c, cudaStream_t st) {
+  if (in <= 0 || inter <= 0) return Status::Invalid("swiglu: need InputDim>0 and IntermediateDim>0");
+  c->device = device;
+  c->in = in;
+  c->inter = inter;
+  Status s = mount_dense(device, inter, in, dt, -1, G, w_is_device, nullptr, 0, &c->sg, &c->gate, st);
+  if (!s.ok()) return Status::Err(s.code, "swiglu Gate: " + s.message);
+  s = mount_dense(device, inter, in, dt, -1, U, w_is_device, nullptr, 0, &c->su, &c->up, st);
+  if (!s.ok()) return Status::Err(s.code, "swiglu Up: " + s.message);
+  s = mount_dense(device, in, inter, dt, -1, D, w_is_device, nullptr, 0, &c->sd, &c->down, st);
+  if (!s.ok()) return Status::Err(s.code, "swiglu Down: " + s.message);
+  return Status::Ok();
+}
+
+Status swiglu_reserve(SwigluCell* c, int bs, cudaStream_t st) {
+  if (c->bs >= bs) return Status::Ok();
+  c->release_work();
+  WB_CUDA(cudaSetDevice(c->device));
+  const size_t xb = static_cast<size_t>(bs) * c->gate.x_stride * 4;
+  const size_t hb = static_cast<size_t>(bs) * c->down.x_stride * 4;
+  WB_CUDA(cudaMalloc(&c->x_pad, xb));
+  WB_CUDA(cudaMemsetAsync(c->x_pad, 0, xb, st));
+  WB_CUDA(cudaMalloc(&c->h_pad, hb));
+  WB_CUDA(cudaMemsetAsync(c->h_pad, 0, hb, st));
+  c->bs = bs;
+  return Status::Ok();
+}
+
+Status swiglu_forward_device(SwigluCell* c, int bs, const float* x, float* h, float* y, cudaStream_t st,
+                             bool pdl) {
+  WB_TRY(swiglu_reserve(c, bs, st));
+  const float* xs = x;
+  int64_t xst = c->in;
+  if (!(c->gate.x_stride == c->in && (reinterpret_cast<uintptr_t>(x) & 15) == 0)) {
+    WB_CUDA(cudaMemcpy2DAsync(c->x_pad, static_cast<size_t>(c->gate.x_stride) * 4, x,
+                              static_cast<size_t>(c->in) * 4, static_cast<size_t>(c->in) * 4,
+                              static_cast<size_t>(bs), cudaMemcpyDeviceToDevice, st));
+    xs = c->x_pad;
+    xst = c->gate.x_stride;
+    pdl = false;
+  }
+  GemvArgs a;
+  a.dtype = c->gate.dtype;
+  a.W = c->gate.W;
+  a.W2 = c->up.W;
+  a.row_stride = c->gate.row_stride;
+  a.rows = c->inter;
+  a.cols = c->in;
+  a.scale = c->gate.scale;
+  a.scale2 = c->up.scale;
+  a.x = xs;
+  a.x_stride = xst;
+  a.batch = bs;
+  a.pre = c->h_pad;
+  a.post = nullptr;
+  a.ld_out = c->down.x_stride;
+  WB_TRY(launch_gemv(a, st, pdl));
+
+  GemvArgs d;
+  d.dtype = c->down.dtype;
+  d.W = c->down.W;
+  d.row_stride = c->down.row_stride;
+  d.rows = c->in;
+  d.cols = c->inter;
+  d.scale = c->down.scale;
+  d.x = c->h_pad;
+  d.x_stride = c->down.x_stride;
+  d.batch = bs;
+  d.pre = y;   // Linear, no bias: pre == post, written by the same thread
+  d.post = y;
+  d.ld_out = c->in;
+  WB_TRY(launch_gemv(d, st, true));
+  if (h) {
+    WB_CUDA(cudaMemcpy2DAsync(h, static_cast<size_t>(c->inter) * 4, c->h_pad,
+                              static_cast<size_t>(c->down.x_stride) * 4, static_cast<size_t>(c->inter) * 4,
+                              static_cast<size_t>(bs), cudaMemcpyDeviceToDevice, st));
+  }
+  return Status::Ok();
+}
+
+Status mha_validate(MhaConfig* cfg) {
+  if (cfg->d_model <= 0 || cfg->num_heads <= 0) return Status::Invalid("mha: need DModel>0 and NumHeads>0");
+  if (cfg->head_dim <= 0) {
+    if (cfg->d_model % cfg->num_heads != 0) return Status::Invalid("mha: HeadDim unset and DModel%NumHeads!=0");
+    cfg->head_dim = cfg->d_model / cfg->num_heads;
+  }
+  if (cfg->num_kv_heads <= 0) cfg->num_kv_heads = cfg->num_heads;
+  if (cfg->num_heads % cfg->num_kv_heads != 0) return Status::Invalid("mha: NumHeads not divisible by NumKVHeads");
+  if (cfg->max_seq_len <= 0) cfg->max_seq_len = 512;
+  if (cfg->mask == 0) cfg->mask = 1;
+  if (cfg->rope_theta <= 0) cfg->rope_theta = 10000;
+  if (cfg->softmax != 0 && cfg->softmax != 1) return Status::Invalid("mha: unknown Softmax");
+  return Status::Ok();
+}
+
+void MhaCell::release_work() {
+  cudaSetDevice(device);
+  free_dev(x_pad); free_dev(qb); free_dev(kb); free_dev(vb); free_dev(attn); free_dev(attn_pad);
+  free_dev(Qr); free_dev(Kr); free_dev(Vd);
+  bs = 0;
+}
+
+Status mha_mount(int device, const MhaConfig& cfg_in, DType dt, const float* Q, const float* K, const float* V,
+                 const float* O, bool w_is_device, MhaCell* c, cudaStream_t st) {
+  MhaConfig cfg = cfg_in;
+  WB_TRY(mha_validate(&cfg));
+  c->device = device;
+  c->cfg = cfg;
+  const int d = cfg.d_model, qd = cfg.num_heads * cfg.head_dim, kvd = cfg.num_kv_heads * cfg.head_dim;
+  Status s = mount_dense(device, qd, d, dt, -1, Q, w_is_device, nullptr, 0, &c->sq, &c->q, st);
+  if (!s.ok()) return Status::Err(s.code, "mha Q: " + s.message);
+  s = mount_dense(device, kvd, d, dt, -1, K, w_is_device, nullptr, 0, &c->sk, &c->k, st);
+  if (!s.ok()) return Status::Err(s.code, "mha K: " + s.message);
+  s = mount_dense(device, kvd, d, dt, -1, V, w_is_device, nullptr, 0, &c->sv, &c->v, st);
+  if (!s.ok()) return Status::Err(s.code, "mha V: " + s.message);
+  s = mount_dense(device, d, qd, dt, -1, O, w_is_device, nullptr, 0, &c->so, &c->o, st);
+  if (!s.ok()) return Status::Err(s.code, "mha O: " + s.message);
+  return Status::Ok();
+}
+
+Status mha_reserve(MhaCell* c, int bs, cudaStream_t st) {
+  if (c->bs >= bs) return Status::Ok();
+  c->release_work();
+  WB_CUDA(cudaSetDevice(c->device));
+  const MhaConfig& g = c->cfg;
+  const size_t qd = static_cast<size_t>(g.num_heads) * g.head_dim, kvd = static_cast<size_t>(g.num_kv_heads) * g.head_dim;
+  const size_t n = static_cast<size_t>(bs);
+  WB_CUDA(cudaMalloc(&c->x_pad, n * c->q.x_stride * 4));
+  WB_CUDA(cudaMemsetAsync(c->x_pad, 0, n * c->q.x_stride * 4, st));
+  WB_CUDA(cudaMalloc(&c->qb, n * qd * 4));
+  WB_CUDA(cudaMalloc(&c->kb, n * kvd * 4));
+  WB_CUDA(cudaMalloc(&c->vb, n * kvd * 4));
+  WB_CUDA(cudaMalloc(&c->attn, n * qd * 4));
+  WB_CUDA(cudaMalloc(&c->attn_pad, n * c->o.x_stride * 4));
+  WB_CUDA(cudaMemsetAsync(c->attn_pad, 0, n * c->o.x_stride * 4, st));
+  WB_CUDA(cudaMalloc(&c->Qr, n * qd * 8));
+  WB_CUDA(cudaMalloc(&c->Kr, n * kvd * 8));
+  WB_CUDA(cudaMalloc(&c->Vd, n * kvd * 8));
+  c->bs = bs;
+  return Status::Ok();
+}
+
+static Status dense_into(const DeviceDense& d, int bs, const float* x_padded, float* out, cudaStream_t st) {
+  GemvArgs a;
+  a.dtype = d.dtype;
+  a.W = d.W;
+  a.row_stride = d.row_stride;
+  a.rows = d.rows;
+  a.cols = d.cols;
+  a.scale = d.scale;
+  a.x = x_padded;
+  a.x_stride = d.x_stride;
+  a.batch = bs;
+  a.pre = out;
+  a.post = out;
+  a.ld_out = d.rows;
+  return launch_gemv(a, st, true);
+}
+
+Status mha_forward_device(MhaCell* c, int batch, int seq, const float* x, float* attn, float* y, cudaStream_t st) {
+  const MhaConfig& g = c->cfg;
+  if (batch <= 0 || seq <= 0) return Status::Invalid("mha: bad batch/seq");
+  if (seq > g.max_seq_len) return Status::Invalid("mha: seq > MaxSeqLen");
+  const int bs = batch * seq;
+  WB_TRY(mha_reserve(c, bs, st));
+  WB_CUDA(cudaMemcpy2DAsync(c->x_pad, static_cast<size_t>(c->q.x_stride) * 4, x, static_cast<size_t>(g.d_model) * 4,
+                            static_cast<size_t>(g.d_model) * 4, static_cast<size_t>(bs), cudaMemcpyDeviceToDevice, st));
+  WB_TRY(dense_into(c->q, bs, c->x_pad, c->qb, st));
+  WB_TRY(dense_into(c->k, bs, c->x_pad, c->kb, st));
+  WB_TRY(dense_into(c->v, bs, c->x_pad, c->vb, st));
+  AttnParams p;
+  p.batch = batch; p.seq = seq; p.num_heads = g.num_heads; p.num_kv = g.num_kv_heads; p.head_dim = g.head_dim;
+  p.max_seq_len = g.max_seq_len; p.mask = g.mask; p.pos_kind = g.pos; p.softmax_kind = g.softmax;
+  p.window = g.window; p.prefix_len = g.prefix_len; p.window_causal = g.window_causal;
+  p.rope_theta = g.rope_theta; p.scale_override = g.scale_override;
+  float* attn_out = attn ? attn : c->attn;
+  WB_TRY(launch_mha_attention(c->qb, c->kb, c->vb, c->Qr, c->Kr, c->Vd, attn_out, p, st));
+  const int qd = g.num_heads * g.head_dim;
+  WB_CUDA(cudaMemcpy2DAsync(c->attn_pad, static_cast<size_t>(c->o.x_stride) * 4, attn_out, static_cast<size_t>(qd) * 4,
+                            static_cast<size_t>(qd) * 4, static_cast<size_t>(bs), cudaMemcpyDeviceToDevice, st));
+  return dense_into(c->o, bs, c->attn_pad, y, st);
+}
+
+Status rmsnorm_gamma(int device, int dim, DType dt, const float* gamma, double** gamma64_dev, cudaStream_t st) {
+  WeightStore s;
+  DeviceDense d;
+  WB_TRY(mount_dense(device, 1, dim, dt, -1, gamma, false, nullptr, 0, &s, &d, st));
+  // decode_row_f64 of the store: weight_at -> float -> double
+  std::vector<double> g(static_cast<size_t>(dim));
+  if (dt == DType::Float32) {
+    for (int i = 0; i < dim; ++i) g[static_cast<size_t>(i)] = static_cast<double>(s.f32[static_cast<size_t>(i)]);
+  } else {
+    float* dec = nullptr;
+    uint8_t* nat = nullptr;
+    WB_CUDA(cudaMalloc(&dec, static_cast<size_t>(dim) * 4));
+    WB_CUDA(cudaMalloc(&nat, s.native.size()));
+    Status stt = cuda_status(cudaMemcpyAsync(nat, s.native.data(), s.native.size(), cudaMemcpyHostToDevice, st), "gamma h2d");
+    if (stt.ok()) stt = decode_ref(dt, nat, dim, s.scale, dec, st);
+    std::vector<float> f(static_cast<size_t>(dim));
+    if (stt.ok()) stt = cuda_status(cudaMemcpyAsync(f.data(), dec, static_cast<size_t>(dim) * 4, cudaMemcpyDeviceToHost, st), "gamma d2h");
+    if (stt.ok()) stt = cuda_status(cudaStreamSynchronize(st), "gamma sync");
+    cudaFree(dec);
+    cudaFree(nat);
+    WB_TRY(stt);
+    for (int i = 0; i < dim; ++i) g[static_cast<size_t>(i)] = static_cast<double>(f[static_cast<size_t>(i)]);
+  }
+  WB_CUDA(cudaMalloc(gamma64_dev, static_cast<size_t>(dim) * 8));
+  WB_CUDA(cudaMemcpyAsync(*gamma64_dev, g.data(), static_cast<size_t>(dim) * 8, cudaMemcpyHostToDevice, st));
+  return cuda_status(cudaStreamSynchronize(st), "gamma sync");
+}
+
+} // namespace wb

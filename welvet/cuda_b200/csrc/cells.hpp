@@ -1,0 +1,66 @@
+// cells.hpp -- SwiGLU, MHA and RMSNorm cells built from the Dense mirror.
+//
+// Reference interfaces mirrored:
+//   swiglu::Layer / new_configured / forward   include/welvet/swiglu.hpp:20-31
+//   mha::Config / validate / Layer / forward   include/welvet/mha.hpp:40-84
+//   rmsnorm forward                            src/layers/rmsnorm/rmsnorm.cpp:60-113
+#pragma once
+
+#include "cell_kernels.hpp"
+#include "dense.hpp"
+
+namespace wb {
+
+struct SwigluCell {
+  int device = 0;
+  int in = 0, inter = 0;
+  WeightStore sg, su, sd;
+  DeviceDense gate, up, down;  // Linear, no bias (src/layers/swiglu/swiglu.cpp:74-82)
+  // work buffers for `bs` rows
+  int bs = 0;
+  float* x_pad = nullptr;  // [bs][gate.x_stride]
+  float* h_pad = nullptr;  // [bs][down.x_stride] (padding stays zero)
+  void release_work();
+  ~SwigluCell() { release_work(); }
+};
+
+Status swiglu_mount(int device, int in, int inter, DType dt, const float* G, const float* U, const float* D,
+                    bool w_is_device, SwigluCell* c, cudaStream_t st);
+Status swiglu_reserve(SwigluCell* c, int bs, cudaStream_t st);
+// x [bs][in] (device) -> h [bs][inter] (the reference's pre) and y [bs][in] (post).
+// h may be nullptr (h stays in the cell's padded work buffer).
+Status swiglu_forward_device(SwigluCell* c, int bs, const float* x, float* h, float* y, cudaStream_t st,
+                             bool pdl);
+
+struct MhaConfig {
+  int d_model = 0, num_heads = 0, num_kv_heads = 0, head_dim = 0, max_seq_len = 0;
+  int mask = 1, pos = 0, softmax = 0, window = 0, prefix_len = 0, window_causal = 1;
+  double rope_theta = 10000.0, scale_override = 0.0;
+};
+
+// src/layers/mha/mha.cpp:57-85 (defaults and divisibility checks).
+Status mha_validate(MhaConfig* cfg);
+
+struct MhaCell {
+  int device = 0;
+  MhaConfig cfg;
+  WeightStore sq, sk, sv, so;
+  DeviceDense q, k, v, o;
+  int bs = 0;
+  float *x_pad = nullptr, *qb = nullptr, *kb = nullptr, *vb = nullptr, *attn = nullptr, *attn_pad = nullptr;
+  double *Qr = nullptr, *Kr = nullptr, *Vd = nullptr;
+  void release_work();
+  ~MhaCell() { release_work(); }
+};
+
+Status mha_mount(int device, const MhaConfig& cfg, DType dt, const float* Q, const float* K, const float* V,
+                 const float* O, bool w_is_device, MhaCell* c, cudaStream_t st);
+Status mha_reserve(MhaCell* c, int bs, cudaStream_t st);
+// x [batch*seq][d_model] (device) -> attn [bs][q_dim] (pre) and y [bs][d_model] (post).
+Status mha_forward_device(MhaCell* c, int batch, int seq, const float* x, float* attn, float* y,
+                          cudaStream_t st);
+
+// gamma f32 [dim] quantized with `dt` then decoded to f64 as the reference's gamma store.
+Status rmsnorm_gamma(int device, int dim, DType dt, const float* gamma, double** gamma64_dev, cudaStream_t st);
+
+} // namespace wb

@@ -1,0 +1,339 @@
+// dense.cpp -- Dense layer mount / execute over the packed device mirror.
+//
+// Mount follows the reference's resident session (src/layers/dense/session.cpp:34-69):
+// float32 W -> FormatNone store (WeightStore::make, src/weights/store.cpp:7-22) -> device.
+// Here the encode runs as GPU kernels (bit-exact with the host codec) and the native bytes
+// are copied back so the host store stays authoritative, as in the reference. Execute keeps
+// resident_execute's contract (src/cuda/kernels.cu:873-915): host x in, host pre/post out,
+// synchronous; plus an asynchronous device-pointer variant.
+#include "dense.hpp"
+
+#include "codec.hpp"
+#include "gemv.hpp"
+
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <sstream>
+
+namespace wb {
+
+namespace {
+
+template <typename T>
+void free_dev(T*& p) {
+  if (p) cudaFree(p);
+  p = nullptr;
+}
+
+struct DevBuf {  // scoped temporary device allocation
+  void* p = nullptr;
+  ~DevBuf() { if (p) cudaFree(p); }
+};
+
+} // namespace
+
+DeviceDense& DeviceDense::operator=(DeviceDense&& o) noexcept {
+  if (this == &o) return *this;
+  release();
+  device = o.device; dtype = o.dtype; rows = o.rows; cols = o.cols;
+  row_stride = o.row_stride; x_stride = o.x_stride; W = o.W; scale = o.scale;
+  bias = o.bias; bias_len = o.bias_len; act = o.act;
+  o.W = nullptr; o.bias = nullptr;
+  return *this;
+}
+
+void DeviceDense::release() {
+  if (W || bias) {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(device);
+    free_dev(W);
+    free_dev(bias);
+    cudaSetDevice(cur);
+  }
+}
+
+void DenseIO::release() {
+  free_dev(x);
+  free_dev(pre);
+  free_dev(post);
+  batch = 0;
+}
+
+int64_t mirror_row_stride(DType dt, int cols) { return round_up(row_bytes(dt, cols), 16); }
+
+int64_t activation_stride(DType dt, int cols) {
+  return mirror_row_stride(dt, cols) / 16 * elems_per_16B(dt);
+}
+
+static Status check_dims(int rows, int cols, int32_t dtype) {
+  if (rows <= 0 || cols <= 0) return Status::Invalid("dense: bad dims");
+  if (!dtype_on_path(dtype))
+    return Status::Unsupported(std::string("dense CUDA (b200) unsupported dtype id ") + std::to_string(dtype));
+  if (static_cast<int64_t>(rows) * cols > (static_cast<int64_t>(1) << 31) - 1)
+    return Status::Invalid("dense: rows*cols exceeds the reference's int element count");
+  return Status::Ok();
+}
+
+static Status finish_mirror(int device, int rows, int cols, DType dt, int act, const uint8_t* native_dev,
+                            float scale, const double* bias, size_t bias_len, WeightStore* store,
+                            DeviceDense* dev, cudaStream_t st) {
+  DeviceDense d;
+  d.device = device;
+  d.dtype = dt;
+  d.rows = rows;
+  d.cols = cols;
+  d.row_stride = mirror_row_stride(dt, cols);
+  d.x_stride = activation_stride(dt, cols);
+  d.scale = scale;
+  d.act = act;
+  WB_CUDA(cudaMalloc(&d.W, static_cast<size_t>(d.row_stride) * rows));
+  WB_TRY(build_mirror(dt, native_dev, rows, cols, d.row_stride, d.W, st));
+  store->bias.clear();
+  if (bias && bias_len > 0) {
+    store->bias.assign(bias, bias + bias_len);
+    d.bias_len = static_cast<int>(bias_len);
+    WB_CUDA(cudaMalloc(&d.bias, bias_len * sizeof(double)));
+    WB_CUDA(cudaMemcpyAsync(d.bias, bias, bias_len * sizeof(double), cudaMemcpyHostToDevice, st));
+  }
+  WB_CUDA(cudaStreamSynchronize(st));
+  *dev = std::move(d);
+  return Status::Ok();
+}
+
+Status mount_dense(int device, int rows, int cols, DType dt, int act, const float* W, bool w_is_device,
+                   const double* bias, size_t bias_len, WeightStore* store, DeviceDense* dev,
+                   cudaStream_t st) {
+  WB_TRY(check_dims(rows, cols, static_cast<int32_t>(dt)));
+  if (!W) return Status::Invalid("null mount args");
+  WB_CUDA(cudaSetDevice(device));
+  const int64_t n = static_cast<int64_t>(rows) * cols;
+  DevBuf wtmp, ntmp, small;
+  const float* wdev = W;
+  if (!w_is_device) {
+    WB_CUDA(cudaMalloc(&wtmp.p, static_cast<size_t>(n) * 4));
+    WB_CUDA(cudaMemcpyAsync(wtmp.p, W, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, st));
+    wdev = static_cast<const float*>(wtmp.p);
+  }
+  const int64_t nb = native_bytes(dt, n);
+  WB_CUDA(cudaMalloc(&ntmp.p, static_cast<size_t>(nb)));
+  WB_CUDA(cudaMalloc(&small.p, 16));
+  float* scale_dev = static_cast<float*>(small.p);
+  unsigned int* absmax = reinterpret_cast<unsigned int*>(static_cast<char*>(small.p) + 8);
+  uint8_t* native_dev = static_cast<uint8_t*>(ntmp.p);
+  WB_TRY(encode_native(dt, wdev, n, native_dev, scale_dev, absmax, st));
+
+  store->dtype = dt;
+  store->format = 0;
+  store->rows = rows;
+  store->cols = cols;
+  float scale = 1.0f;
+  if (dt == DType::Float32) {
+    store->native.clear();
+    store->f32.resize(static_cast<size_t>(n));
+    WB_CUDA(cudaMemcpyAsync(store->f32.data(), wdev, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost, st));
+  } else {
+    store->f32.clear();
+    store->native.resize(static_cast<size_t>(nb));
+    WB_CUDA(cudaMemcpyAsync(store->native.data(), native_dev, static_cast<size_t>(nb), cudaMemcpyDeviceToHost, st));
+    WB_CUDA(cudaMemcpyAsync(&scale, scale_dev, sizeof(float), cudaMemcpyDeviceToHost, st));
+  }
+  WB_CUDA(cudaStreamSynchronize(st));
+  store->scale = scale;
+  return finish_mirror(device, rows, cols, dt, act, native_dev, scale, bias, bias_len, store, dev, st);
+}
+
+Status mount_dense_native(int device, int rows, int cols, DType dt, int act, const uint8_t* native,
+                          size_t native_len, float scale, const double* bias, size_t bias_len,
+                          WeightStore* store, DeviceDense* dev, cudaStream_t st) {
+  WB_TRY(check_dims(rows, cols, static_cast<int32_t>(dt)));
+  if (!native) return Status::Invalid("null native bytes");
+  const int64_t n = static_cast<int64_t>(rows) * cols;
+  const int64_t nb = native_bytes(dt, n);
+  if (static_cast<int64_t>(native_len) < nb) return Status::Invalid(std::string(dtype_name(static_cast<int32_t>(dt))) + " short");
+  WB_CUDA(cudaSetDevice(device));
+  DevBuf ntmp;
+  WB_CUDA(cudaMalloc(&ntmp.p, static_cast<size_t>(nb)));
+  WB_CUDA(cudaMemcpyAsync(ntmp.p, native, static_cast<size_t>(nb), cudaMemcpyHostToDevice, st));
+  store->dtype = dt;
+  store->format = 0;
+  store->rows = rows;
+  store->cols = cols;
+  store->scale = dt == DType::Float32 ? 1.0f : scale;
+  if (dt == DType::Float32) {
+    store->native.clear();
+    store->f32.assign(reinterpret_cast<const float*>(native), reinterpret_cast<const float*>(native) + n);
+  } else {
+    store->f32.clear();
+    store->native.assign(native, native + nb);
+  }
+  // weight_at treats a zero scale as 1 (src/weights/native_codec.cpp:514-515).
+  const float eff = (store->scale == 0.0f) ? 1.0f : store->scale;
+  return finish_mirror(device, rows, cols, dt, act, static_cast<const uint8_t*>(ntmp.p), eff, bias,
+                       bias_len, store, dev, st);
+}
+
+Status alloc_io(const DeviceDense& d, int batch, DenseIO* io, cudaStream_t st) {
+  io->release();
+  io->batch = batch;
+  const size_t xb = static_cast<size_t>(batch) * static_cast<size_t>(d.x_stride) * 4;
+  const size_t yb = static_cast<size_t>(batch) * static_cast<size_t>(d.rows) * 4;
+  WB_CUDA(cudaMalloc(&io->x, xb));
+  WB_CUDA(cudaMemsetAsync(io->x, 0, xb, st));
+  WB_CUDA(cudaMalloc(&io->pre, yb));
+  WB_CUDA(cudaMalloc(&io->post, yb));
+  return Status::Ok();
+}
+
+Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x_ld, float* pre,
+                      float* post, DenseIO* io, cudaStream_t st, bool pdl) {
+  if (batch <= 0 || !x || !pre || !post) return Status::Invalid("null execute args");
+  const float* xs = x;
+  int64_t xst = x_ld;
+  const bool direct = d.cols == d.x_stride && x_ld == d.cols && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  if (!direct) {
+    if (!io || !io->x || io->batch < batch) return Status::Internal("dense: no staging buffer for this batch");
+    WB_CUDA(cudaMemcpy2DAsync(io->x, static_cast<size_t>(d.x_stride) * 4, x, static_cast<size_t>(x_ld) * 4,
+                              static_cast<size_t>(d.cols) * 4, static_cast<size_t>(batch),
+                              cudaMemcpyDeviceToDevice, st));
+    xs = io->x;
+    xst = d.x_stride;
+    pdl = false;
+  }
+  GemvArgs a;
+  a.dtype = d.dtype;
+  a.W = d.W;
+  a.row_stride = d.row_stride;
+  a.rows = d.rows;
+  a.cols = d.cols;
+  a.scale = d.scale;
+  a.x = xs;
+  a.x_stride = xst;
+  a.batch = batch;
+  a.pre = pre;
+  a.post = post;
+  a.ld_out = d.rows;
+  a.bias = d.bias;
+  a.bias_len = d.bias_len;
+  a.act = d.act;
+  return launch_gemv(a, st, pdl);
+}
+
+DenseSession::~DenseSession() {
+  cudaSetDevice(device);
+  if (stream) cudaStreamSynchronize(stream);
+  io.release();
+  dev.release();
+  if (stream) cudaStreamDestroy(stream);
+}
+
+Status library_device(int* device) {
+  static std::once_flag once;
+  static int dev = 0;
+  static Status st;
+  std::call_once(once, [] {
+    int count = 0;
+    st = cuda_status(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+    if (!st.ok()) return;
+    if (count <= 0) {
+      st = Status::Unsupported("no CUDA device available");
+      return;
+    }
+    const char* env = std::getenv("WELVET_B200_DEVICE");
+    if (env && *env) {
+      dev = std::atoi(env);
+    } else {
+      st = cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
+    }
+    if (st.ok() && (dev < 0 || dev >= count)) st = Status::Invalid("WELVET_B200_DEVICE out of range");
+  });
+  *device = dev;
+  return st;
+}
+
+std::string runtime_identity() {
+  int d = 0;
+  if (!library_device(&d).ok()) return "cuda:unavailable";
+  cudaDeviceProp p{};
+  if (cudaGetDeviceProperties(&p, d) != cudaSuccess) return "cuda:unavailable";
+  std::ostringstream os;
+  os << "cuda:" << p.name << ":idx=" << d << ":sm=" << p.major << "." << p.minor << ":mem=" << p.totalGlobalMem;
+  return os.str();
+}
+
+static Status new_session(int32_t batch, DenseSession** out) {
+  if (!out) return Status::Invalid("null mount args");
+  if (batch <= 0) return Status::Invalid("bad dims");
+  auto* s = new DenseSession();
+  Status st = library_device(&s->device);
+  if (st.ok()) st = cuda_status(cudaSetDevice(s->device), "cudaSetDevice");
+  if (st.ok()) st = cuda_status(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "stream");
+  if (!st.ok()) {
+    delete s;
+    return st;
+  }
+  s->batch = batch;
+  *out = s;
+  return Status::Ok();
+}
+
+Status session_mount(int32_t batch, int32_t in, int32_t out, int32_t act, int32_t dtype, const float* W,
+                     bool w_is_device, const double* bias, size_t bias_len, DenseSession** out_sess) {
+  if (!out_sess || !W) return Status::Invalid("null mount args");
+  WB_TRY(check_dims(out, in, dtype));
+  DenseSession* s = nullptr;
+  WB_TRY(new_session(batch, &s));
+  Status st = mount_dense(s->device, out, in, static_cast<DType>(dtype), act, W, w_is_device, bias, bias_len,
+                          &s->store, &s->dev, s->stream);
+  if (st.ok()) st = alloc_io(s->dev, batch, &s->io, s->stream);
+  if (st.ok()) st = cuda_status(cudaStreamSynchronize(s->stream), "mount sync");
+  if (!st.ok()) {
+    delete s;
+    return st;
+  }
+  *out_sess = s;
+  return Status::Ok();
+}
+
+Status session_mount_native(int32_t batch, int32_t in, int32_t out, int32_t act, int32_t dtype,
+                            const uint8_t* native, size_t native_len, float scale, const double* bias,
+                            size_t bias_len, DenseSession** out_sess) {
+  if (!out_sess || !native) return Status::Invalid("null mount args");
+  WB_TRY(check_dims(out, in, dtype));
+  DenseSession* s = nullptr;
+  WB_TRY(new_session(batch, &s));
+  Status st = mount_dense_native(s->device, out, in, static_cast<DType>(dtype), act, native, native_len, scale,
+                                 bias, bias_len, &s->store, &s->dev, s->stream);
+  if (st.ok()) st = alloc_io(s->dev, batch, &s->io, s->stream);
+  if (st.ok()) st = cuda_status(cudaStreamSynchronize(s->stream), "mount sync");
+  if (!st.ok()) {
+    delete s;
+    return st;
+  }
+  *out_sess = s;
+  return Status::Ok();
+}
+
+Status session_execute(DenseSession* s, const float* x, float* pre, float* post) {
+  if (!s || !x || !pre || !post) return Status::Invalid("null execute args");
+  WB_CUDA(cudaSetDevice(s->device));
+  const DeviceDense& d = s->dev;
+  WB_CUDA(cudaMemcpy2DAsync(s->io.x, static_cast<size_t>(d.x_stride) * 4, x, static_cast<size_t>(d.cols) * 4,
+                            static_cast<size_t>(d.cols) * 4, static_cast<size_t>(s->batch),
+                            cudaMemcpyHostToDevice, s->stream));
+  WB_TRY(forward_device(d, s->batch, s->io.x, d.x_stride, s->io.pre, s->io.post, &s->io, s->stream, false));
+  const size_t yb = static_cast<size_t>(s->batch) * static_cast<size_t>(d.rows) * 4;
+  WB_CUDA(cudaMemcpyAsync(pre, s->io.pre, yb, cudaMemcpyDeviceToHost, s->stream));
+  WB_CUDA(cudaMemcpyAsync(post, s->io.post, yb, cudaMemcpyDeviceToHost, s->stream));
+  return cuda_status(cudaStreamSynchronize(s->stream), "dense sync");
+}
+
+Status session_execute_device(DenseSession* s, const float* x, float* pre, float* post, cudaStream_t st) {
+  if (!s || !x || !pre || !post) return Status::Invalid("null execute args");
+  WB_CUDA(cudaSetDevice(s->device));
+  if (!st) st = s->stream;
+  return forward_device(s->dev, s->batch, x, s->dev.cols, pre, post, &s->io, st, true);
+}
+
+} // namespace wb

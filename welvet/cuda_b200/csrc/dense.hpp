@@ -1,0 +1,113 @@
+// dense.hpp -- Dense layer: host WeightStore, device mirror, resident session.
+//
+// Reference interfaces mirrored (same field meaning and error behaviour):
+//   WeightStore          include/welvet/weights.hpp:18-26
+//   dense::Layer         include/welvet/dense.hpp:13-51  (lazy device mirror, invalidation)
+//   dense::Session       src/layers/dense/session.cpp:10-18, :34-82
+//   cuda::ResidentDense  include/welvet/cuda/matvec.hpp:14-25
+// What differs by design: the device mirror holds the packed codes (row-padded, canonical)
+// instead of a host-decoded fp64 matrix, codecs run on the GPU, and every call works on the
+// session's own stream instead of the default stream.
+#pragma once
+
+#include "common.hpp"
+
+#include <vector>
+
+namespace wb {
+
+// Authoritative host store, field for field the reference's FormatNone WeightStore.
+struct WeightStore {
+  DType dtype = DType::Float32;
+  int32_t format = 0;            // QuantFormat::None
+  int rows = 0;                  // out
+  int cols = 0;                  // in
+  std::vector<float> f32;        // Float32 payload
+  std::vector<uint8_t> native;   // FP8 / FP4 / Int8 payload, reference layout
+  float scale = 1.0f;
+  std::vector<double> bias;
+};
+
+// Device-resident mirror of one Dense layer's weights.
+struct DeviceDense {
+  int device = 0;
+  DType dtype = DType::Float32;
+  int rows = 0, cols = 0;
+  int64_t row_stride = 0;   // bytes per padded mirror row (multiple of 16)
+  int64_t x_stride = 0;     // floats per padded activation row this layer consumes
+  uint8_t* W = nullptr;     // mirror [rows][row_stride]
+  float scale = 1.0f;
+  double* bias = nullptr;   // [bias_len]
+  int bias_len = 0;
+  int act = -1;
+
+  DeviceDense() = default;
+  DeviceDense(const DeviceDense&) = delete;
+  DeviceDense& operator=(const DeviceDense&) = delete;
+  DeviceDense(DeviceDense&& o) noexcept { *this = std::move(o); }
+  DeviceDense& operator=(DeviceDense&& o) noexcept;
+  ~DeviceDense() { release(); }
+  void release();
+};
+
+// Padded geometry of a layer's mirror rows and of the activations it reads.
+int64_t mirror_row_stride(DType dt, int cols);
+int64_t activation_stride(DType dt, int cols);
+
+// Quantize host float32 weights W[rows*cols] on the GPU into `store` (reference bytes and
+// scale, copied back to the host) and build the device mirror. `w_is_device` selects whether
+// W is a device pointer (no H2D copy of the float32 matrix).
+Status mount_dense(int device, int rows, int cols, DType dt, int act, const float* W, bool w_is_device,
+                   const double* bias, size_t bias_len, WeightStore* store, DeviceDense* dev,
+                   cudaStream_t st);
+
+// Mirror from reference-layout native bytes (+ scale), as a stored model is re-mounted
+// (src/interop/model_session.cpp:135-153 reads native bytes and scale back into a store).
+Status mount_dense_native(int device, int rows, int cols, DType dt, int act, const uint8_t* native,
+                          size_t native_len, float scale, const double* bias, size_t bias_len,
+                          WeightStore* store, DeviceDense* dev, cudaStream_t st);
+
+// Device buffers for one batch size: padded x, pre, post.
+struct DenseIO {
+  int batch = 0;
+  float* x = nullptr;     // [batch][x_stride], padding zero
+  float* pre = nullptr;   // [batch][rows]
+  float* post = nullptr;  // [batch][rows]
+  void release();
+};
+
+Status alloc_io(const DeviceDense& d, int batch, DenseIO* io, cudaStream_t st);
+
+// y = Dense(x) on the device: x [batch][x_ld] (any alignment; staged into io.x when it is
+// not already padded), outputs [batch][rows] into pre/post (device pointers).
+Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x_ld, float* pre,
+                      float* post, DenseIO* io, cudaStream_t st, bool pdl);
+
+struct DenseSession {
+  int device = 0;
+  int batch = 0;
+  cudaStream_t stream = nullptr;
+  WeightStore store;
+  DeviceDense dev;
+  DenseIO io;
+  ~DenseSession();
+};
+
+Status session_mount(int32_t batch, int32_t in, int32_t out, int32_t act, int32_t dtype,
+                     const float* W, bool w_is_device, const double* bias, size_t bias_len,
+                     DenseSession** out_sess);
+Status session_mount_native(int32_t batch, int32_t in, int32_t out, int32_t act, int32_t dtype,
+                            const uint8_t* native, size_t native_len, float scale,
+                            const double* bias, size_t bias_len, DenseSession** out_sess);
+// Host buffers in and out, synchronous (the reference's resident_execute contract).
+Status session_execute(DenseSession* s, const float* x, float* pre, float* post);
+// Device buffers on a caller stream (nullptr = the session stream), asynchronous.
+Status session_execute_device(DenseSession* s, const float* x, float* pre, float* post,
+                              cudaStream_t st);
+
+// Library device selection: the device current on the first call of the process (0 unless
+// the host application selected another), unless WELVET_B200_DEVICE is set.
+Status library_device(int* device);
+std::string runtime_identity();
+
+} // namespace wb
