@@ -23,7 +23,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -61,54 +60,58 @@ def traffic_from_profile():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """SM clock and clock-event (throttle) reasons of one GPU, polled through NVML (the data
+    nvidia-smi's clocks.sm / clocks_event_reasons.* report) every ~2 ms while the timed
+    region runs -- short timed regions still get samples. Read-only."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, index: int):
         self.index = index
-        self.rows = []
-        self.proc = None
+        self.sm = []
+        self.mask = 0
+        self.max_mhz = None
+        self.err = None
+        self._stop = threading.Event()
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.index), "-lms", "200"], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml as N
+            N.nvmlInit()
+            self.N = N
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = int(vis.split(",")[self.index]) if vis and vis.split(",")[self.index].isdigit() else self.index
+            self.h = N.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+            self.t = threading.Thread(target=self._poll, daemon=True)
             self.t.start()
-        except Exception:
-            self.proc = None
+        except Exception as e:  # no NVML: reported as unsampled
+            self.err = str(e)
         return self
 
-    def _read(self):
-        for ln in self.proc.stdout:
-            self.rows.append([c.strip() for c in ln.split(",")])
+    def _poll(self):
+        N = self.N
+        while not self._stop.is_set():
+            try:
+                self.sm.append(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM))
+                self.mask |= N.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception as e:
+                self.err = str(e)
+                return
+            time.sleep(0.002)
 
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self._stop.set()
+        if hasattr(self, "t"):
             self.t.join(timeout=2)
 
     def summary(self):
-        if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = set()
-        for r in self.rows:
-            for i, n in enumerate(names):
-                if len(r) > 4 + i and r[4 + i].lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(self.rows)}
+        if not self.sm:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "error": self.err}
+        reasons = sorted(n for n, bit in self.REASONS.items() if self.mask & bit)
+        return {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.sm), "source": "NVML (nvmlDeviceGetClockInfo / GetCurrentClocksEventReasons)"}
 
 
 def cpu_baseline(seconds: float = 10.0):
@@ -193,10 +196,11 @@ def run_ours(args):
     stream = torch.cuda.current_stream()
 
     def step():
+        st = torch.cuda.current_stream()  # the capture stream while a graph is recorded
         x = x0
         for i, s in enumerate(sessions):
             y = acts[i & 1]
-            s.execute_device(x, pre, y, stream)
+            s.execute_device(x, pre, y, st)
             x = y
 
     def barrier():
@@ -211,8 +215,21 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    # The 64 launches of a step are captured once in a CUDA graph (the programmatic
+    # dependent-launch edges between consecutive GEMVs are kept) and replayed per step.
+    step()
+    torch.cuda.synchronize()
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        stream = torch.cuda.current_stream()
+        run = graph.replay
+    else:
+        run = step
     for _ in range(args.warmup):
-        step()
+        run()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -220,7 +237,7 @@ def run_ours(args):
         barrier()
         e0.record(stream)
         for _ in range(args.steps):
-            step()
+            run()
         e1.record(stream)
         barrier()
     ms = e0.elapsed_time(e1)
@@ -299,6 +316,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="launch the step's kernels one by one")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -7,8 +7,8 @@
  * resident volume chain and the codec kernels, without changing any reference symbol.
  *
  * Device-pointer calls run asynchronously on the given stream (`stream` is a cudaStream_t;
- * NULL selects the session's own stream) and must not overlap another call on the same
- * session. Host-pointer calls are synchronous like the reference ABI.
+ * 0 is the legacy default stream, as everywhere in CUDA) and must not overlap another call
+ * on the same session. Host-pointer calls are synchronous like the reference ABI.
  */
 
 #include "welvet_c.h"

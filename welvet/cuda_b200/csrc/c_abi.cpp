@@ -293,7 +293,7 @@ welvet_status welvet_b200_swiglu_execute_device(welvet_b200_swiglu* s, int32_t r
   return guarded([&] {
     if (!s || rows <= 0 || !x_dev || !y_dev) return wb::Status::Invalid("swiglu: invalid argument");
     WB_CUDA(cudaSetDevice(s->cell.device));
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : s->stream;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
     return wb::swiglu_forward_device(&s->cell, rows, x_dev, h_dev, y_dev, st, true);
   });
 }
@@ -372,7 +372,7 @@ welvet_status welvet_b200_mha_execute_device(welvet_b200_mha* s, int32_t batch, 
   return guarded([&] {
     if (!s || !x_dev || !y_dev) return wb::Status::Invalid("mha: invalid argument");
     WB_CUDA(cudaSetDevice(s->cell.device));
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : s->stream;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
     return wb::mha_forward_device(&s->cell, batch, seq, x_dev, attn_dev, y_dev, st);
   });
 }

@@ -88,6 +88,7 @@ Status swiglu_forward_device(SwigluCell* c, int bs, const float* x, float* h, fl
   a.pre = c->h_pad;
   a.post = nullptr;
   a.ld_out = c->down.x_stride;
+  a.exact = c->gate.exact && c->up.exact;
   WB_TRY(launch_gemv(a, st, pdl));
 
   GemvArgs d;
@@ -103,6 +104,7 @@ Status swiglu_forward_device(SwigluCell* c, int bs, const float* x, float* h, fl
   d.pre = y;   // Linear, no bias: pre == post, written by the same thread
   d.post = y;
   d.ld_out = c->in;
+  d.exact = c->down.exact;
   WB_TRY(launch_gemv(d, st, true));
   if (h) {
     WB_CUDA(cudaMemcpy2DAsync(h, static_cast<size_t>(c->inter) * 4, c->h_pad,
@@ -188,6 +190,7 @@ static Status dense_into(const DeviceDense& d, int bs, const float* x_padded, fl
   a.pre = out;
   a.post = out;
   a.ld_out = d.rows;
+  a.exact = d.exact;
   return launch_gemv(a, st, true);
 }
 

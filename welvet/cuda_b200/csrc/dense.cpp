@@ -9,7 +9,9 @@
 #include "dense.hpp"
 
 #include "codec.hpp"
+#include "gemm_tc.hpp"
 #include "gemv.hpp"
+#include "gemv_tc.hpp"
 
 #include <cstdlib>
 #include <cstring>
@@ -37,18 +39,19 @@ DeviceDense& DeviceDense::operator=(DeviceDense&& o) noexcept {
   if (this == &o) return *this;
   release();
   device = o.device; dtype = o.dtype; rows = o.rows; cols = o.cols;
-  row_stride = o.row_stride; x_stride = o.x_stride; W = o.W; scale = o.scale;
-  bias = o.bias; bias_len = o.bias_len; act = o.act;
-  o.W = nullptr; o.bias = nullptr;
+  row_stride = o.row_stride; x_stride = o.x_stride; W = o.W; Wt = o.Wt; scale = o.scale;
+  bias = o.bias; bias_len = o.bias_len; act = o.act; exact = o.exact;
+  o.W = nullptr; o.Wt = nullptr; o.bias = nullptr;
   return *this;
 }
 
 void DeviceDense::release() {
-  if (W || bias) {
+  if (W || Wt || bias) {
     int cur = 0;
     cudaGetDevice(&cur);
     cudaSetDevice(device);
     free_dev(W);
+    free_dev(Wt);
     free_dev(bias);
     cudaSetDevice(cur);
   }
@@ -58,7 +61,44 @@ void DenseIO::release() {
   free_dev(x);
   free_dev(pre);
   free_dev(post);
+  free_dev(scratch);
+  free_dev(gscratch);
+  free_dev(err);
+  scratch_bytes = 0;
+  gscratch_bytes = 0;
   batch = 0;
+}
+
+bool use_gemv_tc(const DeviceDense& d, int batch) {
+  const char* env = std::getenv("WELVET_B200_GEMV");
+  if (env && std::strcmp(env, "simt") == 0) return false;
+  return batch >= 1 && batch <= 4 && !d.exact && d.Wt != nullptr;
+}
+
+Status alloc_gemv_scratch(const DeviceDense& d, void** scratch, size_t* bytes, cudaStream_t st) {
+  *bytes = gemv_tc_scratch_bytes(d.dtype, d.rows, d.cols);
+  WB_CUDA(cudaMalloc(scratch, *bytes));
+  return gemv_tc_scratch_init(*scratch, d.dtype, d.rows, d.cols, st);
+}
+
+int xsplit_policy() {
+  const char* env = std::getenv("WELVET_B200_XSPLIT");
+  if (env && env[0] >= '1' && env[0] <= '3') return env[0] - '0';
+  return 3;
+}
+
+bool use_tensor_path(const DeviceDense& d, int batch) {
+  const char* env = std::getenv("WELVET_B200_BATCHED");
+  if (env && std::strcmp(env, "gemv") == 0) return false;
+  if (env && std::strcmp(env, "tc") == 0) return !d.exact && gemm_supported(d.dtype);
+  return batch > 4 && !d.exact && gemm_supported(d.dtype);
+}
+
+bool exact_policy(int rows, int cols) {
+  const char* env = std::getenv("WELVET_B200_EXACT");
+  if (env && env[0] == '1') return true;
+  if (env && env[0] == '0') return false;
+  return static_cast<int64_t>(rows) * cols <= (static_cast<int64_t>(1) << 20);
 }
 
 int64_t mirror_row_stride(DType dt, int cols) { return round_up(row_bytes(dt, cols), 16); }
@@ -88,8 +128,13 @@ static Status finish_mirror(int device, int rows, int cols, DType dt, int act, c
   d.x_stride = activation_stride(dt, cols);
   d.scale = scale;
   d.act = act;
+  d.exact = exact_policy(rows, cols);
   WB_CUDA(cudaMalloc(&d.W, static_cast<size_t>(d.row_stride) * rows));
   WB_TRY(build_mirror(dt, native_dev, rows, cols, d.row_stride, d.W, st));
+  if (gemv_tc_supported(dt) && !d.exact) {
+    WB_CUDA(cudaMalloc(&d.Wt, static_cast<size_t>(tiled_geom(dt, rows, cols).bytes())));
+    WB_TRY(build_tiled_mirror(dt, native_dev, rows, cols, d.Wt, st));
+  }
   store->bias.clear();
   if (bias && bias_len > 0) {
     store->bias.assign(bias, bias + bias_len);
@@ -183,14 +228,67 @@ Status alloc_io(const DeviceDense& d, int batch, DenseIO* io, cudaStream_t st) {
   WB_CUDA(cudaMemsetAsync(io->x, 0, xb, st));
   WB_CUDA(cudaMalloc(&io->pre, yb));
   WB_CUDA(cudaMalloc(&io->post, yb));
+  WB_CUDA(cudaMalloc(&io->err, sizeof(int)));
+  WB_CUDA(cudaMemsetAsync(io->err, 0, sizeof(int), st));
+  if (use_tensor_path(d, batch)) {
+    io->scratch_bytes = gemm_scratch_bytes(batch, d.cols, d.rows, xsplit_policy());
+    WB_CUDA(cudaMalloc(&io->scratch, io->scratch_bytes));
+  } else if (use_gemv_tc(d, batch)) {
+    WB_TRY(alloc_gemv_scratch(d, &io->gscratch, &io->gscratch_bytes, st));
+  }
   return Status::Ok();
 }
 
 Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x_ld, float* pre,
                       float* post, DenseIO* io, cudaStream_t st, bool pdl) {
   if (batch <= 0 || !x || !pre || !post) return Status::Invalid("null execute args");
-  const float* xs = x;
+  const float* xs = x;  // the tensor-core paths read x in any layout
   int64_t xst = x_ld;
+  const bool pdl_in = pdl;
+  if (use_tensor_path(d, batch) && io && io->scratch) {
+    GemmArgs g;
+    g.dtype = d.dtype;
+    g.W = d.W;
+    g.row_stride = d.row_stride;
+    g.rows = d.rows;
+    g.cols = d.cols;
+    g.scale = d.scale;
+    g.x = xs;
+    g.x_ld = xst;
+    g.M = batch;
+    g.pre = pre;
+    g.post = post;
+    g.ld_out = d.rows;
+    g.bias = d.bias;
+    g.bias_len = d.bias_len;
+    g.act = d.act;
+    g.xsplit = xsplit_policy();
+    g.scratch = io->scratch;
+    g.scratch_bytes = io->scratch_bytes;
+    g.err = io->err;
+    return launch_gemm_tc(g, st);
+  }
+  if (use_gemv_tc(d, batch) && io && io->gscratch) {
+    GemvTcArgs g;
+    g.dtype = d.dtype;
+    g.Wt = d.Wt;
+    g.rows = d.rows;
+    g.cols = d.cols;
+    g.scale = d.scale;
+    g.x = x;  // any layout: the kernel reads x with bounds checks, no staging needed
+    g.x_ld = x_ld;
+    g.batch = batch;
+    g.pre = pre;
+    g.post = post;
+    g.ld_out = d.rows;
+    g.bias = d.bias;
+    g.bias_len = d.bias_len;
+    g.act = d.act;
+    g.scratch = io->gscratch;
+    g.scratch_bytes = io->gscratch_bytes;
+    return launch_gemv_tc(g, st, pdl_in);
+  }
+  // The SIMT GEMV reads x in 16-byte vectors over the padded row: stage unpadded inputs.
   const bool direct = d.cols == d.x_stride && x_ld == d.cols && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
   if (!direct) {
     if (!io || !io->x || io->batch < batch) return Status::Internal("dense: no staging buffer for this batch");
@@ -217,6 +315,7 @@ Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x
   a.bias = d.bias;
   a.bias_len = d.bias_len;
   a.act = d.act;
+  a.exact = d.exact;
   return launch_gemv(a, st, pdl);
 }
 
@@ -326,13 +425,23 @@ Status session_execute(DenseSession* s, const float* x, float* pre, float* post)
   const size_t yb = static_cast<size_t>(s->batch) * static_cast<size_t>(d.rows) * 4;
   WB_CUDA(cudaMemcpyAsync(pre, s->io.pre, yb, cudaMemcpyDeviceToHost, s->stream));
   WB_CUDA(cudaMemcpyAsync(post, s->io.post, yb, cudaMemcpyDeviceToHost, s->stream));
-  return cuda_status(cudaStreamSynchronize(s->stream), "dense sync");
+  WB_CUDA(cudaStreamSynchronize(s->stream));
+  return check_pipeline_error(s->io, s->stream);
+}
+
+Status check_pipeline_error(DenseIO& io, cudaStream_t st) {
+  if (!io.err || !io.scratch) return Status::Ok();
+  int e = 0;
+  WB_CUDA(cudaMemcpyAsync(&e, io.err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  WB_CUDA(cudaStreamSynchronize(st));
+  if (e == 0) return Status::Ok();
+  WB_CUDA(cudaMemsetAsync(io.err, 0, sizeof(int), st));
+  return Status::Internal("tensor-core pipeline wait timed out (stage code " + std::to_string(e) + ")");
 }
 
 Status session_execute_device(DenseSession* s, const float* x, float* pre, float* post, cudaStream_t st) {
   if (!s || !x || !pre || !post) return Status::Invalid("null execute args");
   WB_CUDA(cudaSetDevice(s->device));
-  if (!st) st = s->stream;
   return forward_device(s->dev, s->batch, x, s->dev.cols, pre, post, &s->io, st, true);
 }
 

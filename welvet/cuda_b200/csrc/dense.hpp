@@ -36,10 +36,12 @@ struct DeviceDense {
   int64_t row_stride = 0;   // bytes per padded mirror row (multiple of 16)
   int64_t x_stride = 0;     // floats per padded activation row this layer consumes
   uint8_t* W = nullptr;     // mirror [rows][row_stride]
+  uint8_t* Wt = nullptr;    // fragment-tiled mirror for the small-batch tensor GEMV (gemv_tc.hpp)
   float scale = 1.0f;
   double* bias = nullptr;   // [bias_len]
   int bias_len = 0;
   int act = -1;
+  bool exact = false;       // fp64-accumulating GEMV (see exact_policy)
 
   DeviceDense() = default;
   DeviceDense(const DeviceDense&) = delete;
@@ -49,6 +51,11 @@ struct DeviceDense {
   ~DeviceDense() { release(); }
   void release();
 };
+
+// Whether a layer of rows x cols weights runs the fp64-accumulating GEMV: forced by
+// WELVET_B200_EXACT=1 / =0, otherwise for layers of at most 2^20 weights (latency-bound
+// sizes where fp64 costs nothing). Read at mount.
+bool exact_policy(int rows, int cols);
 
 // Padded geometry of a layer's mirror rows and of the activations it reads.
 int64_t mirror_row_stride(DType dt, int cols);
@@ -67,16 +74,33 @@ Status mount_dense_native(int device, int rows, int cols, DType dt, int act, con
                           size_t native_len, float scale, const double* bias, size_t bias_len,
                           WeightStore* store, DeviceDense* dev, cudaStream_t st);
 
-// Device buffers for one batch size: padded x, pre, post.
+// Device buffers for one batch size: padded x, pre, post, and the tensor-core path's scratch.
 struct DenseIO {
   int batch = 0;
   float* x = nullptr;     // [batch][x_stride], padding zero
   float* pre = nullptr;   // [batch][rows]
   float* post = nullptr;  // [batch][rows]
+  void* scratch = nullptr;  // gemm_scratch_bytes(batch, cols, rows, xsplit)
+  size_t scratch_bytes = 0;
+  void* gscratch = nullptr; // gemv_tc_scratch_bytes(dtype, rows, cols); counters zeroed
+  size_t gscratch_bytes = 0;
+  int* err = nullptr;     // device error word of the tensor-core path
   void release();
 };
 
+// Batched path selection: batches above this size run the tcgen05 GEMM (FP8/FP4/Int8 layers
+// that are not in exact mode); WELVET_B200_BATCHED=gemv keeps every batch on the GEMV.
+bool use_tensor_path(const DeviceDense& d, int batch);
+// Batches of 1..4 on quantized, non-exact layers run the tensor-core GEMV (gemv_tc.hpp);
+// WELVET_B200_GEMV=simt keeps them on the SIMT GEMV.
+bool use_gemv_tc(const DeviceDense& d, int batch);
+Status alloc_gemv_scratch(const DeviceDense& d, void** scratch, size_t* bytes, cudaStream_t st);
+// Number of f16 planes x is split into on the tensor path (WELVET_B200_XSPLIT, default 3).
+int xsplit_policy();
+
 Status alloc_io(const DeviceDense& d, int batch, DenseIO* io, cudaStream_t st);
+// Synchronizes `st` and reports (then clears) a timed-out tensor-core pipeline wait.
+Status check_pipeline_error(DenseIO& io, cudaStream_t st);
 
 // y = Dense(x) on the device: x [batch][x_ld] (any alignment; staged into io.x when it is
 // not already padded), outputs [batch][rows] into pre/post (device pointers).
@@ -101,7 +125,7 @@ Status session_mount_native(int32_t batch, int32_t in, int32_t out, int32_t act,
                             const double* bias, size_t bias_len, DenseSession** out_sess);
 // Host buffers in and out, synchronous (the reference's resident_execute contract).
 Status session_execute(DenseSession* s, const float* x, float* pre, float* post);
-// Device buffers on a caller stream (nullptr = the session stream), asynchronous.
+// Device buffers on a caller stream (0 = the legacy default stream), asynchronous.
 Status session_execute_device(DenseSession* s, const float* x, float* pre, float* post,
                               cudaStream_t st);
 

@@ -1,0 +1,48 @@
+// gemm_tc.hpp -- batched dequant GEMM on the 5th-generation tensor cores (tcgen05 / TMEM).
+#pragma once
+
+#include "common.hpp"
+
+#include <cuda_fp16.h>
+
+namespace wb {
+
+// y[t][o] = sum_k W[o][k] x[t][k] for t < M tokens, over the packed device mirror.
+//
+// Numerics: x is split per token into `xsplit` f16 planes after scaling by a power of two
+// (x * 2^e = p0 + p1 + p2); FP8/FP4/Int8 weights are exact in f16, so each product is exact
+// and the tensor core accumulates in fp32. xsplit = 3 carries all 24 bits of every x
+// element (only fp32 accumulation error remains); 2 carries 22 bits, 1 carries 11 bits.
+struct GemmArgs {
+  DType dtype = DType::FP4;
+  const uint8_t* W = nullptr;   // mirror [rows][row_stride]
+  int64_t row_stride = 0;
+  int rows = 0;                 // out
+  int cols = 0;                 // in (K)
+  float scale = 1.0f;           // Int8 per-tensor scale
+  const float* x = nullptr;     // [M][x_ld]
+  int64_t x_ld = 0;
+  int M = 0;
+  float* pre = nullptr;         // [M][ld_out]
+  float* post = nullptr;        // [M][ld_out] (may equal pre when act is Linear and no bias)
+  int64_t ld_out = 0;
+  const double* bias = nullptr;
+  int bias_len = 0;
+  int act = -1;
+  int xsplit = 3;
+  // scratch (device): see gemm_scratch_bytes
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  int* err = nullptr;           // device error word (0 = ok), may be nullptr
+};
+
+// Token tile (B rows per plane) used for M tokens; the MMA N is xsplit * tile.
+int gemm_token_tile(int M, int xsplit);
+// Bytes of scratch a launch with these sizes needs (planes, per-token scales, split-K partials).
+size_t gemm_scratch_bytes(int M, int cols, int rows, int xsplit);
+
+bool gemm_supported(DType dt);
+
+Status launch_gemm_tc(const GemmArgs& a, cudaStream_t st);
+
+} // namespace wb

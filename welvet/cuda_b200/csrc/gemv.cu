@@ -105,7 +105,62 @@ __device__ __forceinline__ void dot_vector(const uint4 (&wv)[kRows], const float
   }
 }
 
-template <int kDt, int kB, bool kDual>
+// Exact variant: every product is formed and accumulated in fp64 (products of the decoded
+// weight and x are exact in fp64), in increasing k within a lane; Int8 weights are
+// dequantized first as the reference does, float(q) * scale in fp32
+// (src/weights/native_codec.cpp:565-568). Used for small, latency-bound layers.
+template <int kDt, int kB>
+__device__ __forceinline__ void dot_vector_exact(const uint4 (&wv)[kRows], const float* __restrict__ xv,
+                                                 int64_t xs, float wscale, double (&acc)[kRows][kB]) {
+  if constexpr (kDt == 1) {
+#pragma unroll
+    for (int b = 0; b < kB; ++b) {
+      const float4 xq = __ldg(reinterpret_cast<const float4*>(xv + b * xs));
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        double p = acc[r][b];
+        p = fma(static_cast<double>(__uint_as_float(wv[r].x)), static_cast<double>(xq.x), p);
+        p = fma(static_cast<double>(__uint_as_float(wv[r].y)), static_cast<double>(xq.y), p);
+        p = fma(static_cast<double>(__uint_as_float(wv[r].z)), static_cast<double>(xq.z), p);
+        p = fma(static_cast<double>(__uint_as_float(wv[r].w)), static_cast<double>(xq.w), p);
+        acc[r][b] = p;
+      }
+    }
+  } else {
+    constexpr int EPW = Geo<kDt>::EPW;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float wf[kRows][EPW];
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        decode_word<kDt>(word_of(wv[r], j), wf[r]);
+        if (kDt == 9) {
+#pragma unroll
+          for (int e = 0; e < EPW; ++e) wf[r][e] = __fmul_rn(wf[r][e], wscale);
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        float x[EPW];
+        const float* xp = xv + b * xs + j * EPW;
+#pragma unroll
+        for (int q = 0; q < EPW / 4; ++q) {
+          const float4 t = __ldg(reinterpret_cast<const float4*>(xp) + q);
+          x[4 * q + 0] = t.x; x[4 * q + 1] = t.y; x[4 * q + 2] = t.z; x[4 * q + 3] = t.w;
+        }
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+          double p = acc[r][b];
+#pragma unroll
+          for (int e = 0; e < EPW; ++e) p = fma(static_cast<double>(wf[r][e]), static_cast<double>(x[e]), p);
+          acc[r][b] = p;
+        }
+      }
+    }
+  }
+}
+
+template <int kDt, int kB, bool kDual, bool kExact>
 __global__ void __launch_bounds__(kWarps * 32) k_gemv(const GemvArgs a) {
   constexpr int EPV = Geo<kDt>::EPV;
   asm volatile("griddepcontrol.launch_dependents;");
@@ -166,6 +221,11 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv(const GemvArgs a) {
         const int64_t v = v0 + 32 * u;
         if (v < nvec) {
           const float* xv = a.x + v * EPV;
+          if constexpr (kExact) {
+            dot_vector_exact<kDt, kB>(wv[u], xv, a.x_stride, a.scale, acc);
+            if (kDual) dot_vector_exact<kDt, kB>(wv2[u], xv, a.x_stride, a.scale2, acc2);
+            continue;
+          }
           float part[kRows][kB];
 #pragma unroll
           for (int r = 0; r < kRows; ++r)
@@ -207,7 +267,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv(const GemvArgs a) {
         if (lane == r * kB + b && o < a.rows) {
           const int64_t idx = static_cast<int64_t>(b) * a.ld_out + o;
           double sum = acc[r][b];
-          if (kDt == 9) sum *= static_cast<double>(a.scale);
+          if (kDt == 9 && !kExact) sum *= static_cast<double>(a.scale);
           if (!kDual) {
             // src/cuda/kernels.cu:141-160: pre = float(sum); v = double(pre) (+ bias, then
             // pre = float(v)); post = float(act(v)).
@@ -221,7 +281,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv(const GemvArgs a) {
             a.post[idx] = static_cast<float>(activate(a.act, v));
           } else {
             double up = acc2[r][b];
-            if (kDt == 9) up *= static_cast<double>(a.scale2);
+            if (kDt == 9 && !kExact) up *= static_cast<double>(a.scale2);
             // Gate/Up are Linear without bias: gate_pre = float(sum), up_post = float(sum);
             // h = float(double(float(SiLU(double(gate_pre)))) * double(up_post)).
             const float gate_pre = static_cast<float>(sum);
@@ -234,7 +294,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv(const GemvArgs a) {
   }
 }
 
-template <int kDt, int kB, bool kDual>
+template <int kDt, int kB, bool kDual, bool kExact>
 Status launch_t(const GemvArgs& a, cudaStream_t st, bool pdl) {
   const int ngroups = (a.rows + kRows - 1) / kRows;
   int grid = (ngroups + kWarps - 1) / kWarps;
@@ -249,18 +309,23 @@ Status launch_t(const GemvArgs& a, cudaStream_t st, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cuda_status(cudaLaunchKernelEx(&cfg, k_gemv<kDt, kB, kDual>, a), "gemv launch");
+  return cuda_status(cudaLaunchKernelEx(&cfg, k_gemv<kDt, kB, kDual, kExact>, a), "gemv launch");
+}
+
+template <int kDt, bool kDual, bool kExact>
+Status launch_e(const GemvArgs& a, cudaStream_t st, bool pdl) {
+  switch (a.batch) {
+  case 1: return launch_t<kDt, 1, kDual, kExact>(a, st, pdl);
+  case 2: return launch_t<kDt, 2, kDual, kExact>(a, st, pdl);
+  case 3: return launch_t<kDt, 3, kDual, kExact>(a, st, pdl);
+  case 4: return launch_t<kDt, 4, kDual, kExact>(a, st, pdl);
+  default: return Status::Internal("gemv: batch chunk must be 1..4");
+  }
 }
 
 template <int kDt, bool kDual>
 Status launch_b(const GemvArgs& a, cudaStream_t st, bool pdl) {
-  switch (a.batch) {
-  case 1: return launch_t<kDt, 1, kDual>(a, st, pdl);
-  case 2: return launch_t<kDt, 2, kDual>(a, st, pdl);
-  case 3: return launch_t<kDt, 3, kDual>(a, st, pdl);
-  case 4: return launch_t<kDt, 4, kDual>(a, st, pdl);
-  default: return Status::Internal("gemv: batch chunk must be 1..4");
-  }
+  return a.exact ? launch_e<kDt, kDual, true>(a, st, pdl) : launch_e<kDt, kDual, false>(a, st, pdl);
 }
 
 template <bool kDual>

@@ -26,6 +26,7 @@ struct GemvArgs {
   const double* bias = nullptr; // f64 [bias_len]; applies to rows o < bias_len
   int bias_len = 0;
   int act = -1;
+  bool exact = false;           // fp64 products and accumulation (small layers)
 };
 
 // Elements covered by 16 bytes of the mirror.

@@ -1,0 +1,527 @@
+// gemv_tc.cu -- small-batch dequant GEMV on the tensor cores' register path (sm_100a).
+//
+// Replaces, for 1..4 tokens, the reference's dense_matvec_f64_batch + dense_bias_act
+// (src/cuda/kernels.cu:130-161) over a host-decoded fp64 W. It streams the packed codes once:
+//
+//  * Weights come from a fragment-tiled mirror: one 16-byte load per lane and row group
+//    holds that lane's mma.m16n8k16 A fragments for 4 (FP4) or 2 (FP8/Int8) K blocks; each
+//    code byte becomes one f16x2 A register through cvt.rn.f16x2.{e2m1x2,e4m3x2,e5m2x2} (Int8
+//    through an exact f16 bias trick). FP8/FP4/Int8 values are exact in f16.
+//  * x is split per token into two f16 planes after scaling by a power of two chosen from
+//    the warp's own K slice (x * 2^e = h0 + h1, 22 significant bits); the planes sit in the
+//    MMA's N columns (n = 2 * token + plane), so each thread's D fragment holds both planes of
+//    one token. Products are exact, accumulation is fp32 within a chunk and fp64 across
+//    chunks, warps and CTAs: |y - y_fp64| <= ~2^-22 * sum_k |W x| before the final rounding.
+//  * A warp owns 64 rows x a K slice; all its weight loads for the first chunk are issued
+//    before griddepcontrol.wait (programmatic dependent launch: the weights do not depend on
+//    the previous kernel), so a chained layer streams its weights while the previous one
+//    finishes. Split-K across CTAs is reduced deterministically: every CTA writes its f64
+//    partial to scratch, and the last CTA to arrive (per-row-set counter) sums the partials
+//    in split order and runs the epilogue (bias / activation, or the SwiGLU product, as in
+//    src/cuda/kernels.cu:147-161 and :296-305), then resets the counter.
+#include "gemv_tc.hpp"
+#include "codec.cuh"
+
+namespace wb {
+namespace {
+
+constexpr int kWarps = 4;   // warps per CTA (K slices of one row set)
+constexpr int kRG = 4;      // row groups of 16 rows per warp -> 64-row sets
+constexpr int kRowsPerSet = kRG * 16;
+
+struct Plan {
+  TiledGeom g;
+  int64_t row_sets = 0;
+  int64_t chunks = 0;       // chunks of 2 units along K
+  int cpw = 1;              // chunks per warp
+  int splits = 1;
+  int64_t rows_p = 0;       // row_sets * 64
+};
+
+Plan make_plan(DType dt, int rows, int cols) {
+  Plan p;
+  p.g = tiled_geom(dt, rows, cols);
+  p.row_sets = (p.g.row_groups + kRG - 1) / kRG;
+  p.chunks = (p.g.units_k + 1) / 2;
+  p.rows_p = p.row_sets * kRowsPerSet;
+  int cpw = 1;
+  while (true) {
+    const int64_t splits = (p.chunks + kWarps * cpw - 1) / (kWarps * cpw);
+    if (p.row_sets * splits <= 8 * 148 || cpw >= p.chunks) break;
+    cpw *= 2;
+  }
+  p.cpw = cpw;
+  p.splits = static_cast<int>((p.chunks + kWarps * cpw - 1) / (kWarps * cpw));
+  return p;
+}
+
+struct KArgs {
+  const uint8_t* Wt;
+  const uint8_t* Wt2;
+  int rows, cols;
+  int64_t units_k;
+  int64_t row_groups;
+  int64_t chunks;
+  int cpw, splits;
+  int64_t rows_p;
+  float scale, scale2;
+  const float* x;
+  int64_t x_ld;
+  float* pre;
+  float* post;
+  int64_t ld_out;
+  const double* bias;
+  int bias_len;
+  int act;
+  double* partial;          // [splits][rows_p][2][4]
+  unsigned int* counters;   // [row_sets]
+};
+
+__device__ __forceinline__ uint4 ld_stream(const uint8_t* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// A fragment of K block j (within a unit) from the lane's 16-byte unit word set.
+template <int kDt>
+__device__ __forceinline__ void a_frag(const uint4& u, int j, uint32_t (&a)[4]) {
+  if constexpr (kDt == 16) {
+    const uint32_t w = j == 0 ? u.x : (j == 1 ? u.y : (j == 2 ? u.z : u.w));
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+        "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+        : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+        : "r"(w));
+  } else {
+    const uint32_t w0 = j == 0 ? u.x : u.z;
+    const uint32_t w1 = j == 0 ? u.y : u.w;
+    if constexpr (kDt == 4) {
+      asm("{\n\t.reg .b16 l0, h0, l1, h1;\n\t"
+          "mov.b32 {l0, h0}, %4;\n\t"
+          "mov.b32 {l1, h1}, %5;\n\t"
+          "cvt.rn.f16x2.e4m3x2 %0, l0;\n\t"
+          "cvt.rn.f16x2.e4m3x2 %1, h0;\n\t"
+          "cvt.rn.f16x2.e4m3x2 %2, l1;\n\t"
+          "cvt.rn.f16x2.e4m3x2 %3, h1;\n\t}"
+          : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+          : "r"(w0), "r"(w1));
+    } else if constexpr (kDt == 5) {
+      asm("{\n\t.reg .b16 l0, h0, l1, h1;\n\t"
+          "mov.b32 {l0, h0}, %4;\n\t"
+          "mov.b32 {l1, h1}, %5;\n\t"
+          "cvt.rn.f16x2.e5m2x2 %0, l0;\n\t"
+          "cvt.rn.f16x2.e5m2x2 %1, h0;\n\t"
+          "cvt.rn.f16x2.e5m2x2 %2, l1;\n\t"
+          "cvt.rn.f16x2.e5m2x2 %3, h1;\n\t}"
+          : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+          : "r"(w0), "r"(w1));
+    } else {  // Int8: f16 bits 0x6400 | (q ^ 0x80) = 1152 + q, minus 1152
+      const uint32_t u0 = w0 ^ 0x80808080u, u1 = w1 ^ 0x80808080u;
+      const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+      uint32_t p[4] = {__byte_perm(u0, 0x64646464u, 0x4140), __byte_perm(u0, 0x64646464u, 0x4342),
+                       __byte_perm(u1, 0x64646464u, 0x4140), __byte_perm(u1, 0x64646464u, 0x4342)};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __half2 h = __hsub2(*reinterpret_cast<__half2*>(&p[i]), bias);
+        a[i] = *reinterpret_cast<uint32_t*>(&h);
+      }
+    }
+  }
+}
+
+// Two x values (token b, k and k+1) scaled by s and reduced to plane `plane` as f16x2.
+__device__ __forceinline__ uint32_t x_plane_pair(float v0, float v1, float s, int plane) {
+  float a = v0 * s, b = v1 * s;
+  const bool fa = isfinite(a), fb = isfinite(b);
+  if (!fa) a = v0;  // Inf / NaN pass through plane 0 (w * Inf as in fp64)
+  if (!fb) b = v1;
+  __half2 h0 = __floats2half2_rn(a, b);
+  if (plane == 0) return *reinterpret_cast<uint32_t*>(&h0);
+  const float2 f0 = __half22float2(h0);
+  const float ra = fa ? a - f0.x : 0.0f, rb = fb ? b - f0.y : 0.0f;
+  __half2 h1 = __floats2half2_rn(ra, rb);
+  return *reinterpret_cast<uint32_t*>(&h1);
+}
+
+__device__ __forceinline__ float xval(const KArgs& a, int b, int64_t k) {
+  return k < a.cols ? __ldg(a.x + b * a.x_ld + k) : 0.0f;
+}
+
+__device__ __forceinline__ void write_out(const KArgs& a, int o, int b, double y, double y2, bool dual) {
+  const int64_t idx = static_cast<int64_t>(b) * a.ld_out + o;
+  if (!dual) {
+    float pre = static_cast<float>(y);
+    double v = static_cast<double>(pre);
+    if (a.bias != nullptr && o < a.bias_len) {
+      v += a.bias[o];
+      pre = static_cast<float>(v);
+    }
+    a.pre[idx] = pre;
+    a.post[idx] = static_cast<float>(activate(a.act, v));
+  } else {
+    const float gate_pre = static_cast<float>(y);
+    const float up_post = static_cast<float>(y2);
+    const float g = static_cast<float>(activate(1, static_cast<double>(gate_pre)));
+    a.pre[idx] = static_cast<float>(static_cast<double>(g) * static_cast<double>(up_post));
+  }
+}
+
+template <int kDt, int kB, bool kDual>
+__global__ void __launch_bounds__(kWarps * 32) k_gemv_tc(const KArgs a) {
+  constexpr int KBPU = kDt == 16 ? 4 : 2;       // K blocks of 16 per unit
+  constexpr int UK = KBPU * 16;                 // K elements per unit
+  constexpr int CK = 2 * UK;                    // K elements per chunk
+  __shared__ double red[kWarps][kRowsPerSet][2][4];
+  __shared__ int last_flag;
+
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int64_t rs = blockIdx.x;
+  const int split = blockIdx.y;
+  const int64_t rg0 = rs * kRG;
+  const int64_t c0 = (static_cast<int64_t>(split) * kWarps + warp) * a.cpw;
+  int64_t c1 = c0 + a.cpw;
+  if (c1 > a.chunks) c1 = a.chunks;
+
+  auto load_chunk = [&](int64_t c, uint4 (&buf)[2][kRG], uint4 (&buf2)[2][kRG]) {
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int64_t unit = 2 * c + u;
+#pragma unroll
+      for (int r = 0; r < kRG; ++r) {
+        const bool ok = unit < a.units_k && rg0 + r < a.row_groups;
+        const int64_t off = ((rg0 + r) * a.units_k + unit) * 512 + lane * 16;
+        buf[u][r] = ok ? ld_stream(a.Wt + off) : make_uint4(0, 0, 0, 0);
+        if (kDual) buf2[u][r] = ok ? ld_stream(a.Wt2 + off) : make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+
+  uint4 bufA[2][kRG], bufA2[2][kRG];
+  uint4 bufB[2][kRG], bufB2[2][kRG];
+  if (c0 < c1) load_chunk(c0, bufA, bufA2);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  // per-token power-of-two scale over this warp's K slice
+  const int64_t klo = c0 * CK;
+  int64_t khi = c1 * CK;
+  if (khi > a.cols) khi = a.cols;
+  float sc[kB], sinv[kB];
+#pragma unroll
+  for (int b = 0; b < kB; ++b) {
+    float m = 0.0f;
+    for (int64_t k = klo + lane; k < khi; k += 32) {
+      const float v = fabsf(__ldg(a.x + b * a.x_ld + k));
+      if (v > m && v <= 3.402823466e+38f) m = v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    int e = 0;
+    if (m > 0.0f) {
+      e = 14 - ilogbf(m);  // m * 2^e in [2^14, 2^15): far from f16 overflow (65504)
+      e = e > 126 ? 126 : (e < -126 ? -126 : e);
+    }
+    sc[b] = ldexpf(1.0f, e);
+    sinv[b] = ldexpf(1.0f, -e);
+  }
+  const int bn = g >> 1, pn = g & 1;      // the B column this lane supplies
+  const bool col_active = bn < kB;
+  float s_col = 1.0f;
+#pragma unroll
+  for (int b = 0; b < kB; ++b)
+    if (bn == b) s_col = sc[b];
+  float sinv_t = 0.0f;
+#pragma unroll
+  for (int b = 0; b < kB; ++b)
+    if (t == b) sinv_t = sinv[b];
+
+  double acc[kRG][2], acc2[kRG][2];
+#pragma unroll
+  for (int r = 0; r < kRG; ++r) acc[r][0] = acc[r][1] = acc2[r][0] = acc2[r][1] = 0.0;
+
+  auto compute_chunk = [&](int64_t c, const uint4 (&buf)[2][kRG], const uint4 (&buf2)[2][kRG]) {
+    float d[kRG][4], d2[kRG][4];
+#pragma unroll
+    for (int r = 0; r < kRG; ++r)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) d[r][i] = d2[r][i] = 0.0f;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+#pragma unroll
+      for (int j = 0; j < KBPU; ++j) {
+        const int64_t kb = (2 * c + u) * KBPU + j;
+        const int64_t k = kb * 16 + 2 * t;
+        uint32_t b0 = 0u, b1 = 0u;
+        if (col_active) {
+          b0 = x_plane_pair(xval(a, bn, k), xval(a, bn, k + 1), s_col, pn);
+          b1 = x_plane_pair(xval(a, bn, k + 8), xval(a, bn, k + 9), s_col, pn);
+        }
+#pragma unroll
+        for (int r = 0; r < kRG; ++r) {
+          uint32_t af[4];
+          a_frag<kDt>(buf[u][r], j, af);
+          mma16816(d[r], af, b0, b1);
+          if (kDual) {
+            a_frag<kDt>(buf2[u][r], j, af);
+            mma16816(d2[r], af, b0, b1);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kRG; ++r) {
+      acc[r][0] += (static_cast<double>(d[r][0]) + static_cast<double>(d[r][1])) * sinv_t;
+      acc[r][1] += (static_cast<double>(d[r][2]) + static_cast<double>(d[r][3])) * sinv_t;
+      if (kDual) {
+        acc2[r][0] += (static_cast<double>(d2[r][0]) + static_cast<double>(d2[r][1])) * sinv_t;
+        acc2[r][1] += (static_cast<double>(d2[r][2]) + static_cast<double>(d2[r][3])) * sinv_t;
+      }
+    }
+  };
+
+  for (int64_t c = c0; c < c1; c += 2) {
+    if (c + 1 < c1) load_chunk(c + 1, bufB, bufB2);
+    compute_chunk(c, bufA, bufA2);
+    if (c + 1 < c1) {
+      if (c + 2 < c1) load_chunk(c + 2, bufA, bufA2);
+      compute_chunk(c + 1, bufB, bufB2);
+    }
+  }
+
+  // ---- CTA reduction over the 4 K slices (fixed order)
+  if (t < kB) {
+#pragma unroll
+    for (int r = 0; r < kRG; ++r) {
+      red[warp][r * 16 + g][0][t] = acc[r][0];
+      red[warp][r * 16 + g + 8][0][t] = acc[r][1];
+      if (kDual) {
+        red[warp][r * 16 + g][1][t] = acc2[r][0];
+        red[warp][r * 16 + g + 8][1][t] = acc2[r][1];
+      }
+    }
+  }
+  __syncthreads();
+  const int nout = kRowsPerSet * kB;
+  if (a.splits == 1) {
+    for (int i = threadIdx.x; i < nout; i += blockDim.x) {
+      const int row = i / kB, b = i - row * kB;
+      const int o = static_cast<int>(rs * kRowsPerSet + row);
+      if (o >= a.rows) continue;
+      double y = 0.0, y2 = 0.0;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        y += red[w][row][0][b];
+        if (kDual) y2 += red[w][row][1][b];
+      }
+      if (kDt == 9) { y *= static_cast<double>(a.scale); y2 *= static_cast<double>(a.scale2); }
+      write_out(a, o, b, y, y2, kDual);
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < nout; i += blockDim.x) {
+    const int row = i / kB, b = i - row * kB;
+    double y = 0.0, y2 = 0.0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      y += red[w][row][0][b];
+      if (kDual) y2 += red[w][row][1][b];
+    }
+    const int64_t base = ((static_cast<int64_t>(split) * a.rows_p) + rs * kRowsPerSet + row) * 8;
+    a.partial[base + b] = y;
+    if (kDual) a.partial[base + 4 + b] = y2;
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(&a.counters[rs], 1u);
+    last_flag = prev == static_cast<unsigned>(a.splits - 1);
+  }
+  __syncthreads();
+  if (!last_flag) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < nout; i += blockDim.x) {
+    const int row = i / kB, b = i - row * kB;
+    const int o = static_cast<int>(rs * kRowsPerSet + row);
+    if (o >= a.rows) continue;
+    double y = 0.0, y2 = 0.0;
+    for (int s = 0; s < a.splits; ++s) {
+      const int64_t base = ((static_cast<int64_t>(s) * a.rows_p) + rs * kRowsPerSet + row) * 8;
+      y += __ldcg(a.partial + base + b);
+      if (kDual) y2 += __ldcg(a.partial + base + 4 + b);
+    }
+    if (kDt == 9) { y *= static_cast<double>(a.scale); y2 *= static_cast<double>(a.scale2); }
+    write_out(a, o, b, y, y2, kDual);
+  }
+  if (threadIdx.x == 0) a.counters[rs] = 0u;  // ready for the next launch
+}
+
+// One thread per output byte of the tiled mirror.
+template <int kDt>
+__global__ void k_build_tiled(const uint8_t* __restrict__ native, int rows, int cols, int64_t units_k,
+                              int64_t total, uint8_t* __restrict__ out) {
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t unit_idx = t >> 9;
+    const int within = static_cast<int>(t & 511);
+    const int lane = within >> 4;
+    const int g = lane >> 2, tt = lane & 3;
+    const int64_t rg = unit_idx / units_k, unit = unit_idx - rg * units_k;
+    uint32_t byte = 0;
+    if (kDt == 16) {
+      const int j = (within >> 2) & 3;        // K block within the unit
+      const int pair = within & 3;            // fragment elements 2*pair, 2*pair+1
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int i = 2 * pair + h;
+        const int64_t row = rg * 16 + g + 8 * ((i >> 1) & 1);
+        const int64_t k = unit * 64 + j * 16 + 2 * tt + (i & 1) + 8 * (i >> 2);
+        uint32_t code = 0;
+        if (row < rows && k < cols) {
+          const int64_t f = row * cols + k;
+          code = (native[f >> 1] >> ((f & 1) * 4)) & 0xF;
+        }
+        byte |= code << (4 * h);
+      }
+    } else {
+      const int j = (within >> 3) & 1;
+      const int i = within & 7;
+      const int64_t row = rg * 16 + g + 8 * ((i >> 1) & 1);
+      const int64_t k = unit * 32 + j * 16 + 2 * tt + (i & 1) + 8 * (i >> 2);
+      if (row < rows && k < cols) {
+        const uint32_t c = native[row * cols + k];
+        byte = kDt == 4 ? canon_e4m3(c) : (kDt == 5 ? canon_e5m2(c) : c);
+      }
+    }
+    out[t] = static_cast<uint8_t>(byte);
+  }
+}
+
+template <int kDt, int kB, bool kDual>
+Status launch_t(const KArgs& k, const Plan& pl, cudaStream_t st, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(pl.row_sets), static_cast<unsigned>(pl.splits));
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cuda_status(cudaLaunchKernelEx(&cfg, k_gemv_tc<kDt, kB, kDual>, k), "gemv_tc launch");
+}
+
+template <int kDt, bool kDual>
+Status launch_b(const KArgs& k, const Plan& pl, int batch, cudaStream_t st, bool pdl) {
+  switch (batch) {
+  case 1: return launch_t<kDt, 1, kDual>(k, pl, st, pdl);
+  case 2: return launch_t<kDt, 2, kDual>(k, pl, st, pdl);
+  case 3: return launch_t<kDt, 3, kDual>(k, pl, st, pdl);
+  case 4: return launch_t<kDt, 4, kDual>(k, pl, st, pdl);
+  default: return Status::Internal("gemv_tc: batch must be 1..4");
+  }
+}
+
+template <bool kDual>
+Status launch_d(DType dt, const KArgs& k, const Plan& pl, int batch, cudaStream_t st, bool pdl) {
+  switch (dt) {
+  case DType::FP4: return launch_b<16, kDual>(k, pl, batch, st, pdl);
+  case DType::FP8E4M3: return launch_b<4, kDual>(k, pl, batch, st, pdl);
+  case DType::FP8E5M2: return launch_b<5, kDual>(k, pl, batch, st, pdl);
+  case DType::Int8: return launch_b<9, kDual>(k, pl, batch, st, pdl);
+  default: return Status::Unsupported("gemv_tc: dtype");
+  }
+}
+
+} // namespace
+
+bool gemv_tc_supported(DType dt) {
+  return dt == DType::FP4 || dt == DType::FP8E4M3 || dt == DType::FP8E5M2 || dt == DType::Int8;
+}
+
+TiledGeom tiled_geom(DType dt, int rows, int cols) {
+  TiledGeom g;
+  g.unit_k = dt == DType::FP4 ? 64 : 32;
+  g.row_groups = (rows + 15) / 16;
+  g.units_k = (cols + g.unit_k - 1) / g.unit_k;
+  return g;
+}
+
+Status build_tiled_mirror(DType dt, const uint8_t* native, int rows, int cols, uint8_t* tiled, cudaStream_t st) {
+  const TiledGeom g = tiled_geom(dt, rows, cols);
+  const int64_t total = g.bytes();
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 64) blocks = 148 * 64;
+  const unsigned gb = static_cast<unsigned>(blocks);
+  switch (dt) {
+  case DType::FP4: k_build_tiled<16><<<gb, 256, 0, st>>>(native, rows, cols, g.units_k, total, tiled); break;
+  case DType::FP8E4M3: k_build_tiled<4><<<gb, 256, 0, st>>>(native, rows, cols, g.units_k, total, tiled); break;
+  case DType::FP8E5M2: k_build_tiled<5><<<gb, 256, 0, st>>>(native, rows, cols, g.units_k, total, tiled); break;
+  case DType::Int8: k_build_tiled<9><<<gb, 256, 0, st>>>(native, rows, cols, g.units_k, total, tiled); break;
+  default: return Status::Unsupported("tiled mirror: dtype");
+  }
+  return cuda_status(cudaGetLastError(), "tiled mirror launch");
+}
+
+size_t gemv_tc_scratch_bytes(DType dt, int rows, int cols) {
+  const Plan pl = make_plan(dt, rows, cols);
+  const size_t part = pl.splits > 1 ? static_cast<size_t>(pl.splits) * pl.rows_p * 8 * sizeof(double) : 0;
+  return round_up(static_cast<int64_t>(part), 256) + static_cast<size_t>(pl.row_sets) * sizeof(unsigned int);
+}
+
+Status gemv_tc_scratch_init(void* scratch, DType dt, int rows, int cols, cudaStream_t st) {
+  const Plan pl = make_plan(dt, rows, cols);
+  const size_t part = pl.splits > 1 ? static_cast<size_t>(pl.splits) * pl.rows_p * 8 * sizeof(double) : 0;
+  uint8_t* c = static_cast<uint8_t*>(scratch) + round_up(static_cast<int64_t>(part), 256);
+  return cuda_status(cudaMemsetAsync(c, 0, static_cast<size_t>(pl.row_sets) * sizeof(unsigned int), st),
+                     "gemv_tc counters");
+}
+
+Status launch_gemv_tc(const GemvTcArgs& a, cudaStream_t st, bool pdl) {
+  if (!gemv_tc_supported(a.dtype)) return Status::Unsupported("gemv_tc: dtype");
+  if (a.rows <= 0 || a.cols <= 0 || a.batch < 1 || a.batch > 4) return Status::Invalid("gemv_tc: bad dims");
+  const Plan pl = make_plan(a.dtype, a.rows, a.cols);
+  const size_t need = gemv_tc_scratch_bytes(a.dtype, a.rows, a.cols);
+  if (!a.scratch || a.scratch_bytes < need) return Status::Internal("gemv_tc: scratch too small");
+  const size_t part = pl.splits > 1 ? static_cast<size_t>(pl.splits) * pl.rows_p * 8 * sizeof(double) : 0;
+  KArgs k{};
+  k.Wt = a.Wt;
+  k.Wt2 = a.Wt2;
+  k.rows = a.rows;
+  k.cols = a.cols;
+  k.units_k = pl.g.units_k;
+  k.row_groups = pl.g.row_groups;
+  k.chunks = pl.chunks;
+  k.cpw = pl.cpw;
+  k.splits = pl.splits;
+  k.rows_p = pl.rows_p;
+  k.scale = a.scale;
+  k.scale2 = a.scale2;
+  k.x = a.x;
+  k.x_ld = a.x_ld;
+  k.pre = a.pre;
+  k.post = a.post;
+  k.ld_out = a.ld_out;
+  k.bias = a.bias;
+  k.bias_len = a.bias_len;
+  k.act = a.act;
+  k.partial = reinterpret_cast<double*>(a.scratch);
+  k.counters = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(a.scratch) + round_up(static_cast<int64_t>(part), 256));
+  return a.Wt2 ? launch_d<true>(a.dtype, k, pl, a.batch, st, pdl) : launch_d<false>(a.dtype, k, pl, a.batch, st, pdl);
+}
+
+} // namespace wb

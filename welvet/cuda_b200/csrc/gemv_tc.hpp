@@ -1,0 +1,51 @@
+// gemv_tc.hpp -- small-batch (1..4 tokens) dequant GEMV on the tensor cores' register path.
+#pragma once
+
+#include "common.hpp"
+
+namespace wb {
+
+// Fragment-tiled weight mirror: rows in groups of 16, K in units of 64 (FP4) or 32 (FP8 /
+// Int8) elements; each 512-byte unit holds, for every lane of a warp, the codes of its
+// mma.m16n8k16 A fragments for 4 (FP4) or 2 (FP8 / Int8) consecutive 16-wide K blocks.
+struct TiledGeom {
+  int64_t row_groups = 0;   // ceil(rows / 16)
+  int64_t units_k = 0;      // K units per row group
+  int unit_k = 0;           // elements of K per unit (64 or 32)
+  int64_t bytes() const { return row_groups * units_k * 512; }
+};
+
+TiledGeom tiled_geom(DType dt, int rows, int cols);
+bool gemv_tc_supported(DType dt);
+
+// Build the tiled mirror from reference-layout native bytes (FP8 codes canonicalised).
+Status build_tiled_mirror(DType dt, const uint8_t* native, int rows, int cols, uint8_t* tiled, cudaStream_t st);
+
+struct GemvTcArgs {
+  DType dtype = DType::FP4;
+  const uint8_t* Wt = nullptr;   // tiled mirror
+  const uint8_t* Wt2 = nullptr;  // SwiGLU Up (same geometry) or nullptr
+  int rows = 0, cols = 0;
+  float scale = 1.0f, scale2 = 1.0f;  // Int8 per-tensor scales
+  const float* x = nullptr;      // [batch][x_ld], any alignment
+  int64_t x_ld = 0;
+  int batch = 1;                 // 1..4
+  float* pre = nullptr;          // [batch][ld_out]  (SwiGLU: h)
+  float* post = nullptr;
+  int64_t ld_out = 0;
+  const double* bias = nullptr;
+  int bias_len = 0;
+  int act = -1;
+  void* scratch = nullptr;       // gemv_tc_scratch_bytes(); counters must start at zero
+  size_t scratch_bytes = 0;
+};
+
+// Scratch of one layer: split-K partials (f64) and per-row-set arrival counters. The
+// counters are left at zero by every completed launch.
+size_t gemv_tc_scratch_bytes(DType dt, int rows, int cols);
+// Zero the counters of a freshly allocated scratch block.
+Status gemv_tc_scratch_init(void* scratch, DType dt, int rows, int cols, cudaStream_t st);
+
+Status launch_gemv_tc(const GemvTcArgs& a, cudaStream_t st, bool pdl);
+
+} // namespace wb
