@@ -348,3 +348,48 @@ def test_simt_gemv_still_correct(wb, oracle, dt, monkeypatch):
     w, x, bias, ref = _case(oracle, dt, 300, 4100, 3, 2.0, 5, 1)
     pre, post = wb.dense_forward_f32(w, x, dt, 1, bias)
     check_dense(pre, post, ref, 1, f"simt dt={dt}")
+
+
+@pytest.mark.parametrize("rows", [1, 3, 24])  # 1..4: fused Gate/Up tensor GEMV; 24: tcgen05 GEMM
+@pytest.mark.parametrize("dt", [16, 4, 9])
+def test_swiglu_tensor_paths(wb, oracle, dt, rows, monkeypatch):
+    monkeypatch.setenv("WELVET_B200_EXACT", "0")
+    rng = np.random.default_rng(20 + rows)
+    d, inter = 256, 640
+    G, U, D = [(rng.standard_normal(s) * 0.5).astype(np.float32) for s in ((inter, d), (inter, d), (d, inter))]
+    x = rng.standard_normal((rows, d)).astype(np.float32)
+    pre, post = wb.swiglu_forward_f32(G, U, D, x, rows, 1, dt)
+    rg, sg = oracle.pack(dt, G)
+    ru, su = oracle.pack(dt, U)
+    rd, sd = oracle.pack(dt, D)
+    gp, _, _, gsa = oracle.dense_forward(dt, rg, sg, x, d, inter)
+    _, upp, _, usa = oracle.dense_forward(dt, ru, su, x, d, inter)
+    h = oracle.swiglu_product(gp, upp)
+    # h error: gate/up each within 2^-18 * sum|Wx|, propagated through SiLU (slope <= 1.1) and the product
+    hb = 1.1 * TOL_REL * gsa * np.abs(upp) + TOL_REL * usa * np.abs(h / np.where(upp == 0, 1, upp)) + 4 * ulp(h)
+    assert np.all(np.abs(pre.reshape(h.shape) - h) <= hb + 1e-30)
+    ref = oracle.dense_forward(dt, rd, sd, pre.reshape(h.shape), inter, d)
+    check_dense(post, post, ref, -1, f"swiglu down dt={dt} rows={rows}")
+
+
+@pytest.mark.parametrize("batch,seq", [(1, 3), (2, 16)])
+def test_mha_tensor_paths(wb, oracle, batch, seq, monkeypatch):
+    monkeypatch.setenv("WELVET_B200_EXACT", "0")
+    from oracle.attention import attention
+    rng = np.random.default_rng(40 + seq)
+    d, nh, nkv, hd, msl = 64, 4, 2, 16, 16
+    qd, kvd = nh * hd, nkv * hd
+    Q, K, V = [(rng.standard_normal((r, d)) * 0.3).astype(np.float32) for r in (qd, kvd, kvd)]
+    O = (rng.standard_normal((d, qd)) * 0.3).astype(np.float32)
+    x = rng.standard_normal((batch * seq, d)).astype(np.float32)
+    dt = oracle.FP4
+    pre, post = wb.mha_forward_f32(Q, K, V, O, x, batch, seq, d, nh, nkv, hd, msl, 1, 0, dt)
+    proj = []
+    for M, r in ((Q, qd), (K, kvd), (V, kvd)):
+        raw, s = oracle.pack(dt, M)
+        proj.append(oracle.dense_forward(dt, raw, s, x, d, r)[1])
+    att = attention(*proj, batch, seq, nh, nkv, hd, msl, 1, 0)
+    np.testing.assert_allclose(pre.reshape(att.shape), att, rtol=1e-4, atol=1e-5)
+    raw, s = oracle.pack(dt, O)
+    ref = oracle.dense_forward(dt, raw, s, pre.reshape(att.shape), qd, d)
+    check_dense(post, post, ref, -1, "mha O (tensor paths)")

@@ -328,6 +328,8 @@ welvet_status welvet_swiglu_forward_f32(int32_t batch, int32_t seq, int32_t inpu
       st = wb::cuda_status(cudaMemcpyAsync(post, yb.p, static_cast<size_t>(rows) * input_dim * 4,
                                            cudaMemcpyDeviceToHost, s->stream), "d2h post");
     if (st.ok()) st = wb::cuda_status(cudaStreamSynchronize(s->stream), "swiglu sync");
+    for (wb::DenseIO* io : {&s->cell.io_gate, &s->cell.io_up, &s->cell.io_down})
+      if (st.ok()) st = wb::check_pipeline_error(*io, s->stream);
     delete s;
     return st;
   });
@@ -407,6 +409,8 @@ welvet_status welvet_mha_forward_f32(int32_t batch, int32_t seq, int32_t d_model
     if (st.ok())
       st = wb::cuda_status(cudaMemcpyAsync(post, yb.p, rows * d_model * 4, cudaMemcpyDeviceToHost, s->stream), "d2h post");
     if (st.ok()) st = wb::cuda_status(cudaStreamSynchronize(s->stream), "mha sync");
+    for (wb::DenseIO* io : {&s->cell.io_q, &s->cell.io_k, &s->cell.io_v, &s->cell.io_o})
+      if (st.ok()) st = wb::check_pipeline_error(*io, s->stream);
     delete s;
     return st;
   });

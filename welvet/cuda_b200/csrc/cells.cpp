@@ -9,7 +9,9 @@
 #include "cells.hpp"
 
 #include "codec.hpp"
+#include "gemm_tc.hpp"
 #include "gemv.hpp"
+#include "gemv_tc.hpp"
 
 #include <cmath>
 #include <vector>
@@ -28,6 +30,11 @@ void SwigluCell::release_work() {
   cudaSetDevice(device);
   free_dev(x_pad);
   free_dev(h_pad);
+  free_dev(g_buf);
+  free_dev(u_buf);
+  io_gate.release();
+  io_up.release();
+  io_down.release();
   bs = 0;
 }
 
@@ -56,62 +63,98 @@ Status swiglu_reserve(SwigluCell* c, int bs, cudaStream_t st) {
   WB_CUDA(cudaMemsetAsync(c->x_pad, 0, xb, st));
   WB_CUDA(cudaMalloc(&c->h_pad, hb));
   WB_CUDA(cudaMemsetAsync(c->h_pad, 0, hb, st));
+  if (use_tensor_path(c->gate, bs)) {
+    WB_CUDA(cudaMalloc(&c->g_buf, static_cast<size_t>(bs) * c->inter * 4));
+    WB_CUDA(cudaMalloc(&c->u_buf, static_cast<size_t>(bs) * c->inter * 4));
+    WB_TRY(alloc_io(c->gate, bs, &c->io_gate, st));
+    WB_TRY(alloc_io(c->up, bs, &c->io_up, st));
+  }
+  WB_TRY(alloc_io(c->down, bs, &c->io_down, st));
   c->bs = bs;
   return Status::Ok();
 }
 
+// x [bs][in] -> h [bs][inter] (= SiLU(Gate x) * (Up x), the reference's pre) -> y = Down h.
 Status swiglu_forward_device(SwigluCell* c, int bs, const float* x, float* h, float* y, cudaStream_t st,
                              bool pdl) {
   WB_TRY(swiglu_reserve(c, bs, st));
-  const float* xs = x;
-  int64_t xst = c->in;
-  if (!(c->gate.x_stride == c->in && (reinterpret_cast<uintptr_t>(x) & 15) == 0)) {
-    WB_CUDA(cudaMemcpy2DAsync(c->x_pad, static_cast<size_t>(c->gate.x_stride) * 4, x,
-                              static_cast<size_t>(c->in) * 4, static_cast<size_t>(c->in) * 4,
-                              static_cast<size_t>(bs), cudaMemcpyDeviceToDevice, st));
-    xs = c->x_pad;
-    xst = c->gate.x_stride;
-    pdl = false;
+  const float* hsrc = nullptr;  // h as Down's input
+  int64_t h_ld = 0;
+  if (use_gemv_tc(c->gate, bs) && c->up.Wt) {
+    // 1..4 rows: Gate and Up stream together through the tensor-core GEMV, whose epilogue
+    // writes h directly.
+    GemvTcArgs a;
+    a.dtype = c->gate.dtype;
+    a.Wt = c->gate.Wt;
+    a.Wt2 = c->up.Wt;
+    a.rows = c->inter;
+    a.cols = c->in;
+    a.scale = c->gate.scale;
+    a.scale2 = c->up.scale;
+    a.x = x;
+    a.x_ld = c->in;
+    a.batch = bs;
+    a.pre = h ? h : c->h_pad;
+    a.post = nullptr;
+    a.ld_out = h ? c->inter : c->down.x_stride;
+    WB_TRY(launch_gemv_tc(a, st, pdl));
+    hsrc = a.pre;
+    h_ld = a.ld_out;
+  } else if (use_tensor_path(c->gate, bs) && c->g_buf) {
+    // batched: Gate and Up on the tcgen05 GEMM, then the reference's SiLU product.
+    WB_TRY(forward_device(c->gate, bs, x, c->in, c->g_buf, c->g_buf, &c->io_gate, st, false));
+    WB_TRY(forward_device(c->up, bs, x, c->in, c->u_buf, c->u_buf, &c->io_up, st, false));
+    float* hout = h ? h : c->h_pad;
+    const int64_t ld = h ? c->inter : c->down.x_stride;
+    if (ld == c->inter) {
+      WB_TRY(launch_swiglu_product(c->g_buf, c->u_buf, hout, static_cast<int64_t>(bs) * c->inter, st));
+    } else {
+      WB_TRY(launch_swiglu_product(c->g_buf, c->u_buf, c->g_buf, static_cast<int64_t>(bs) * c->inter, st));
+      WB_CUDA(cudaMemcpy2DAsync(hout, static_cast<size_t>(ld) * 4, c->g_buf, static_cast<size_t>(c->inter) * 4,
+                                static_cast<size_t>(c->inter) * 4, static_cast<size_t>(bs),
+                                cudaMemcpyDeviceToDevice, st));
+    }
+    hsrc = hout;
+    h_ld = ld;
+  } else {
+    // exact / Float32 layers: SIMT GEMV over x padded to the mirror's row length
+    const float* xs = x;
+    int64_t xst = c->in;
+    if (!(c->gate.x_stride == c->in && (reinterpret_cast<uintptr_t>(x) & 15) == 0)) {
+      WB_CUDA(cudaMemcpy2DAsync(c->x_pad, static_cast<size_t>(c->gate.x_stride) * 4, x,
+                                static_cast<size_t>(c->in) * 4, static_cast<size_t>(c->in) * 4,
+                                static_cast<size_t>(bs), cudaMemcpyDeviceToDevice, st));
+      xs = c->x_pad;
+      xst = c->gate.x_stride;
+      pdl = false;
+    }
+    GemvArgs a;
+    a.dtype = c->gate.dtype;
+    a.W = c->gate.W;
+    a.W2 = c->up.W;
+    a.row_stride = c->gate.row_stride;
+    a.rows = c->inter;
+    a.cols = c->in;
+    a.scale = c->gate.scale;
+    a.scale2 = c->up.scale;
+    a.x = xs;
+    a.x_stride = xst;
+    a.batch = bs;
+    a.pre = c->h_pad;
+    a.post = nullptr;
+    a.ld_out = c->down.x_stride;
+    a.exact = c->gate.exact && c->up.exact;
+    WB_TRY(launch_gemv(a, st, pdl));
+    if (h) {
+      WB_CUDA(cudaMemcpy2DAsync(h, static_cast<size_t>(c->inter) * 4, c->h_pad,
+                                static_cast<size_t>(c->down.x_stride) * 4, static_cast<size_t>(c->inter) * 4,
+                                static_cast<size_t>(bs), cudaMemcpyDeviceToDevice, st));
+    }
+    hsrc = c->h_pad;
+    h_ld = c->down.x_stride;
   }
-  GemvArgs a;
-  a.dtype = c->gate.dtype;
-  a.W = c->gate.W;
-  a.W2 = c->up.W;
-  a.row_stride = c->gate.row_stride;
-  a.rows = c->inter;
-  a.cols = c->in;
-  a.scale = c->gate.scale;
-  a.scale2 = c->up.scale;
-  a.x = xs;
-  a.x_stride = xst;
-  a.batch = bs;
-  a.pre = c->h_pad;
-  a.post = nullptr;
-  a.ld_out = c->down.x_stride;
-  a.exact = c->gate.exact && c->up.exact;
-  WB_TRY(launch_gemv(a, st, pdl));
-
-  GemvArgs d;
-  d.dtype = c->down.dtype;
-  d.W = c->down.W;
-  d.row_stride = c->down.row_stride;
-  d.rows = c->in;
-  d.cols = c->inter;
-  d.scale = c->down.scale;
-  d.x = c->h_pad;
-  d.x_stride = c->down.x_stride;
-  d.batch = bs;
-  d.pre = y;   // Linear, no bias: pre == post, written by the same thread
-  d.post = y;
-  d.ld_out = c->in;
-  d.exact = c->down.exact;
-  WB_TRY(launch_gemv(d, st, true));
-  if (h) {
-    WB_CUDA(cudaMemcpy2DAsync(h, static_cast<size_t>(c->inter) * 4, c->h_pad,
-                              static_cast<size_t>(c->down.x_stride) * 4, static_cast<size_t>(c->inter) * 4,
-                              static_cast<size_t>(bs), cudaMemcpyDeviceToDevice, st));
-  }
-  return Status::Ok();
+  // Down: Linear, no bias, so pre == post (written by the same thread).
+  return forward_device(c->down, bs, hsrc, h_ld, y, y, &c->io_down, st, true);
 }
 
 Status mha_validate(MhaConfig* cfg) {
@@ -133,6 +176,7 @@ void MhaCell::release_work() {
   cudaSetDevice(device);
   free_dev(x_pad); free_dev(qb); free_dev(kb); free_dev(vb); free_dev(attn); free_dev(attn_pad);
   free_dev(Qr); free_dev(Kr); free_dev(Vd);
+  io_q.release(); io_k.release(); io_v.release(); io_o.release();
   bs = 0;
 }
 
@@ -172,26 +216,12 @@ Status mha_reserve(MhaCell* c, int bs, cudaStream_t st) {
   WB_CUDA(cudaMalloc(&c->Qr, n * qd * 8));
   WB_CUDA(cudaMalloc(&c->Kr, n * kvd * 8));
   WB_CUDA(cudaMalloc(&c->Vd, n * kvd * 8));
+  WB_TRY(alloc_io(c->q, bs, &c->io_q, st));
+  WB_TRY(alloc_io(c->k, bs, &c->io_k, st));
+  WB_TRY(alloc_io(c->v, bs, &c->io_v, st));
+  WB_TRY(alloc_io(c->o, bs, &c->io_o, st));
   c->bs = bs;
   return Status::Ok();
-}
-
-static Status dense_into(const DeviceDense& d, int bs, const float* x_padded, float* out, cudaStream_t st) {
-  GemvArgs a;
-  a.dtype = d.dtype;
-  a.W = d.W;
-  a.row_stride = d.row_stride;
-  a.rows = d.rows;
-  a.cols = d.cols;
-  a.scale = d.scale;
-  a.x = x_padded;
-  a.x_stride = d.x_stride;
-  a.batch = bs;
-  a.pre = out;
-  a.post = out;
-  a.ld_out = d.rows;
-  a.exact = d.exact;
-  return launch_gemv(a, st, true);
 }
 
 Status mha_forward_device(MhaCell* c, int batch, int seq, const float* x, float* attn, float* y, cudaStream_t st) {
@@ -200,11 +230,9 @@ Status mha_forward_device(MhaCell* c, int batch, int seq, const float* x, float*
   if (seq > g.max_seq_len) return Status::Invalid("mha: seq > MaxSeqLen");
   const int bs = batch * seq;
   WB_TRY(mha_reserve(c, bs, st));
-  WB_CUDA(cudaMemcpy2DAsync(c->x_pad, static_cast<size_t>(c->q.x_stride) * 4, x, static_cast<size_t>(g.d_model) * 4,
-                            static_cast<size_t>(g.d_model) * 4, static_cast<size_t>(bs), cudaMemcpyDeviceToDevice, st));
-  WB_TRY(dense_into(c->q, bs, c->x_pad, c->qb, st));
-  WB_TRY(dense_into(c->k, bs, c->x_pad, c->kb, st));
-  WB_TRY(dense_into(c->v, bs, c->x_pad, c->vb, st));
+  WB_TRY(forward_device(c->q, bs, x, g.d_model, c->qb, c->qb, &c->io_q, st, false));
+  WB_TRY(forward_device(c->k, bs, x, g.d_model, c->kb, c->kb, &c->io_k, st, false));
+  WB_TRY(forward_device(c->v, bs, x, g.d_model, c->vb, c->vb, &c->io_v, st, false));
   AttnParams p;
   p.batch = batch; p.seq = seq; p.num_heads = g.num_heads; p.num_kv = g.num_kv_heads; p.head_dim = g.head_dim;
   p.max_seq_len = g.max_seq_len; p.mask = g.mask; p.pos_kind = g.pos; p.softmax_kind = g.softmax;
@@ -213,9 +241,7 @@ Status mha_forward_device(MhaCell* c, int batch, int seq, const float* x, float*
   float* attn_out = attn ? attn : c->attn;
   WB_TRY(launch_mha_attention(c->qb, c->kb, c->vb, c->Qr, c->Kr, c->Vd, attn_out, p, st));
   const int qd = g.num_heads * g.head_dim;
-  WB_CUDA(cudaMemcpy2DAsync(c->attn_pad, static_cast<size_t>(c->o.x_stride) * 4, attn_out, static_cast<size_t>(qd) * 4,
-                            static_cast<size_t>(qd) * 4, static_cast<size_t>(bs), cudaMemcpyDeviceToDevice, st));
-  return dense_into(c->o, bs, c->attn_pad, y, st);
+  return forward_device(c->o, bs, attn_out, qd, y, y, &c->io_o, st, false);
 }
 
 Status rmsnorm_gamma(int device, int dim, DType dt, const float* gamma, double** gamma64_dev, cudaStream_t st) {

@@ -20,6 +20,9 @@ struct SwigluCell {
   int bs = 0;
   float* x_pad = nullptr;  // [bs][gate.x_stride]
   float* h_pad = nullptr;  // [bs][down.x_stride] (padding stays zero)
+  float* g_buf = nullptr;  // [bs][inter] gate output (tensor-core GEMM path)
+  float* u_buf = nullptr;  // [bs][inter] up output
+  DenseIO io_gate, io_up, io_down;  // per-projection staging and scratch
   void release_work();
   ~SwigluCell() { release_work(); }
 };
@@ -49,6 +52,7 @@ struct MhaCell {
   int bs = 0;
   float *x_pad = nullptr, *qb = nullptr, *kb = nullptr, *vb = nullptr, *attn = nullptr, *attn_pad = nullptr;
   double *Qr = nullptr, *Kr = nullptr, *Vd = nullptr;
+  DenseIO io_q, io_k, io_v, io_o;  // per-projection staging and scratch
   void release_work();
   ~MhaCell() { release_work(); }
 };

@@ -62,10 +62,8 @@ void DenseIO::release() {
   free_dev(pre);
   free_dev(post);
   free_dev(scratch);
-  free_dev(gscratch);
   free_dev(err);
   scratch_bytes = 0;
-  gscratch_bytes = 0;
   batch = 0;
 }
 
@@ -73,12 +71,6 @@ bool use_gemv_tc(const DeviceDense& d, int batch) {
   const char* env = std::getenv("WELVET_B200_GEMV");
   if (env && std::strcmp(env, "simt") == 0) return false;
   return batch >= 1 && batch <= 4 && !d.exact && d.Wt != nullptr;
-}
-
-Status alloc_gemv_scratch(const DeviceDense& d, void** scratch, size_t* bytes, cudaStream_t st) {
-  *bytes = gemv_tc_scratch_bytes(d.dtype, d.rows, d.cols);
-  WB_CUDA(cudaMalloc(scratch, *bytes));
-  return gemv_tc_scratch_init(*scratch, d.dtype, d.rows, d.cols, st);
 }
 
 int xsplit_policy() {
@@ -233,8 +225,6 @@ Status alloc_io(const DeviceDense& d, int batch, DenseIO* io, cudaStream_t st) {
   if (use_tensor_path(d, batch)) {
     io->scratch_bytes = gemm_scratch_bytes(batch, d.cols, d.rows, xsplit_policy());
     WB_CUDA(cudaMalloc(&io->scratch, io->scratch_bytes));
-  } else if (use_gemv_tc(d, batch)) {
-    WB_TRY(alloc_gemv_scratch(d, &io->gscratch, &io->gscratch_bytes, st));
   }
   return Status::Ok();
 }
@@ -268,7 +258,7 @@ Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x
     g.err = io->err;
     return launch_gemm_tc(g, st);
   }
-  if (use_gemv_tc(d, batch) && io && io->gscratch) {
+  if (use_gemv_tc(d, batch)) {
     GemvTcArgs g;
     g.dtype = d.dtype;
     g.Wt = d.Wt;
@@ -284,8 +274,6 @@ Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x
     g.bias = d.bias;
     g.bias_len = d.bias_len;
     g.act = d.act;
-    g.scratch = io->gscratch;
-    g.scratch_bytes = io->gscratch_bytes;
     return launch_gemv_tc(g, st, pdl_in);
   }
   // The SIMT GEMV reads x in 16-byte vectors over the padded row: stage unpadded inputs.

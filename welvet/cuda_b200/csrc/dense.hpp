@@ -82,8 +82,6 @@ struct DenseIO {
   float* post = nullptr;  // [batch][rows]
   void* scratch = nullptr;  // gemm_scratch_bytes(batch, cols, rows, xsplit)
   size_t scratch_bytes = 0;
-  void* gscratch = nullptr; // gemv_tc_scratch_bytes(dtype, rows, cols); counters zeroed
-  size_t gscratch_bytes = 0;
   int* err = nullptr;     // device error word of the tensor-core path
   void release();
 };
@@ -94,7 +92,6 @@ bool use_tensor_path(const DeviceDense& d, int batch);
 // Batches of 1..4 on quantized, non-exact layers run the tensor-core GEMV (gemv_tc.hpp);
 // WELVET_B200_GEMV=simt keeps them on the SIMT GEMV.
 bool use_gemv_tc(const DeviceDense& d, int batch);
-Status alloc_gemv_scratch(const DeviceDense& d, void** scratch, size_t* bytes, cudaStream_t st);
 // Number of f16 planes x is split into on the tensor path (WELVET_B200_XSPLIT, default 3).
 int xsplit_policy();
 

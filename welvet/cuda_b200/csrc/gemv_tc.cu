@@ -8,34 +8,40 @@
 //    code byte becomes one f16x2 A register through cvt.rn.f16x2.{e2m1x2,e4m3x2,e5m2x2} (Int8
 //    through an exact f16 bias trick). FP8/FP4/Int8 values are exact in f16.
 //  * x is split per token into two f16 planes after scaling by a power of two chosen from
-//    the warp's own K slice (x * 2^e = h0 + h1, 22 significant bits); the planes sit in the
+//    the CTA's own K range (x * 2^e = h0 + h1, 22 significant bits); the planes sit in the
 //    MMA's N columns (n = 2 * token + plane), so each thread's D fragment holds both planes of
-//    one token. Products are exact, accumulation is fp32 within a chunk and fp64 across
-//    chunks, warps and CTAs: |y - y_fp64| <= ~2^-22 * sum_k |W x| before the final rounding.
-//  * A warp owns 64 rows x a K slice; all its weight loads for the first chunk are issued
-//    before griddepcontrol.wait (programmatic dependent launch: the weights do not depend on
-//    the previous kernel), so a chained layer streams its weights while the previous one
-//    finishes. Split-K across CTAs is reduced deterministically: every CTA writes its f64
-//    partial to scratch, and the last CTA to arrive (per-row-set counter) sums the partials
-//    in split order and runs the epilogue (bias / activation, or the SwiGLU product, as in
-//    src/cuda/kernels.cu:147-161 and :296-305), then resets the counter.
+//    one token. The CTA's 128 threads build these B fragments once into shared memory.
+//    Products are exact, accumulation is fp32 within a chunk and fp64 across chunks, warps
+//    and CTAs: |y - y_fp64| <= ~2^-22 * sum_k |W x| before the final rounding.
+//  * A CTA owns 64 rows x a K range, its 4 warps a quarter each. All of a warp's weight
+//    loads for its first chunk are issued before griddepcontrol.wait (programmatic dependent
+//    launch: the weights do not depend on the previous kernel), so a chained layer streams
+//    its weights while the previous one finishes.
+//  * The K ranges of one 64-row set are the CTAs of one thread-block cluster (up to 8); their
+//    fp64 partials are summed in rank order by rank 0 through distributed shared memory,
+//    which then runs the epilogue (bias / activation, or the SwiGLU product, as in
+//    src/cuda/kernels.cu:147-161 and :296-305). No global scratch and no atomics: the result
+//    is deterministic.
 #include "gemv_tc.hpp"
 #include "codec.cuh"
+
+#include <cooperative_groups.h>
 
 namespace wb {
 namespace {
 
-constexpr int kWarps = 4;   // warps per CTA (K slices of one row set)
+constexpr int kWarps = 4;   // warps per CTA (K slices of the CTA's K range)
 constexpr int kRG = 4;      // row groups of 16 rows per warp -> 64-row sets
 constexpr int kRowsPerSet = kRG * 16;
+constexpr int kMaxCluster = 8;
 
 struct Plan {
   TiledGeom g;
   int64_t row_sets = 0;
   int64_t chunks = 0;       // chunks of 2 units along K
   int cpw = 1;              // chunks per warp
-  int splits = 1;
-  int64_t rows_p = 0;       // row_sets * 64
+  int csize = 1;            // CTAs per cluster (split of K)
+  int nkb_cta = 0;          // K blocks of 16 per CTA
 };
 
 Plan make_plan(DType dt, int rows, int cols) {
@@ -43,15 +49,11 @@ Plan make_plan(DType dt, int rows, int cols) {
   p.g = tiled_geom(dt, rows, cols);
   p.row_sets = (p.g.row_groups + kRG - 1) / kRG;
   p.chunks = (p.g.units_k + 1) / 2;
-  p.rows_p = p.row_sets * kRowsPerSet;
-  int cpw = 1;
-  while (true) {
-    const int64_t splits = (p.chunks + kWarps * cpw - 1) / (kWarps * cpw);
-    if (p.row_sets * splits <= 8 * 148 || cpw >= p.chunks) break;
-    cpw *= 2;
-  }
-  p.cpw = cpw;
-  p.splits = static_cast<int>((p.chunks + kWarps * cpw - 1) / (kWarps * cpw));
+  p.cpw = static_cast<int>((p.chunks + kWarps * kMaxCluster - 1) / (kWarps * kMaxCluster));
+  if (p.cpw < 1) p.cpw = 1;
+  p.csize = static_cast<int>((p.chunks + kWarps * p.cpw - 1) / (kWarps * p.cpw));
+  const int kbpu = dt == DType::FP4 ? 4 : 2;
+  p.nkb_cta = kWarps * p.cpw * 2 * kbpu;
   return p;
 }
 
@@ -62,8 +64,7 @@ struct KArgs {
   int64_t units_k;
   int64_t row_groups;
   int64_t chunks;
-  int cpw, splits;
-  int64_t rows_p;
+  int cpw, csize, nkb_cta;
   float scale, scale2;
   const float* x;
   int64_t x_ld;
@@ -73,8 +74,6 @@ struct KArgs {
   const double* bias;
   int bias_len;
   int act;
-  double* partial;          // [splits][rows_p][2][4]
-  unsigned int* counters;   // [row_sets]
 };
 
 __device__ __forceinline__ uint4 ld_stream(const uint8_t* p) {
@@ -93,7 +92,7 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// A fragment of K block j (within a unit) from the lane's 16-byte unit word set.
+// A fragment of K block j (within a unit) from the lane's 16-byte share of the unit.
 template <int kDt>
 __device__ __forceinline__ void a_frag(const uint4& u, int j, uint32_t (&a)[4]) {
   if constexpr (kDt == 16) {
@@ -143,7 +142,7 @@ __device__ __forceinline__ void a_frag(const uint4& u, int j, uint32_t (&a)[4]) 
   }
 }
 
-// Two x values (token b, k and k+1) scaled by s and reduced to plane `plane` as f16x2.
+// Two x values scaled by s and reduced to plane `plane` (0: f16 rounding, 1: its residual).
 __device__ __forceinline__ uint32_t x_plane_pair(float v0, float v1, float s, int plane) {
   float a = v0 * s, b = v1 * s;
   const bool fa = isfinite(a), fb = isfinite(b);
@@ -155,10 +154,6 @@ __device__ __forceinline__ uint32_t x_plane_pair(float v0, float v1, float s, in
   const float ra = fa ? a - f0.x : 0.0f, rb = fb ? b - f0.y : 0.0f;
   __half2 h1 = __floats2half2_rn(ra, rb);
   return *reinterpret_cast<uint32_t*>(&h1);
-}
-
-__device__ __forceinline__ float xval(const KArgs& a, int b, int64_t k) {
-  return k < a.cols ? __ldg(a.x + b * a.x_ld + k) : 0.0f;
 }
 
 __device__ __forceinline__ void write_out(const KArgs& a, int o, int b, double y, double y2, bool dual) {
@@ -183,18 +178,21 @@ __device__ __forceinline__ void write_out(const KArgs& a, int o, int b, double y
 template <int kDt, int kB, bool kDual>
 __global__ void __launch_bounds__(kWarps * 32) k_gemv_tc(const KArgs a) {
   constexpr int KBPU = kDt == 16 ? 4 : 2;       // K blocks of 16 per unit
-  constexpr int UK = KBPU * 16;                 // K elements per unit
-  constexpr int CK = 2 * UK;                    // K elements per chunk
-  __shared__ double red[kWarps][kRowsPerSet][2][4];
-  __shared__ int last_flag;
+  constexpr int CK = 2 * KBPU * 16;             // K elements per chunk
+  constexpr int NCOL = 2 * kB;                  // B columns in use: n = 2 * token + plane
+  __shared__ double red[kWarps][kRowsPerSet][kDual ? 2 : 1][kB];
+  __shared__ double cta_part[kRowsPerSet][kDual ? 2 : 1][kB];
+  __shared__ float smax[kWarps][kB];
+  extern __shared__ uint2 frag[];                // [nkb_cta][NCOL][4]
 
   asm volatile("griddepcontrol.launch_dependents;");
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
-  const int64_t rs = blockIdx.x;
-  const int split = blockIdx.y;
+  const int rank = blockIdx.x;                  // K split = rank in the cluster
+  const int64_t rs = blockIdx.y;
   const int64_t rg0 = rs * kRG;
-  const int64_t c0 = (static_cast<int64_t>(split) * kWarps + warp) * a.cpw;
+  const int64_t cta_c0 = static_cast<int64_t>(rank) * kWarps * a.cpw;
+  const int64_t c0 = cta_c0 + static_cast<int64_t>(warp) * a.cpw;
   int64_t c1 = c0 + a.cpw;
   if (c1 > a.chunks) c1 = a.chunks;
 
@@ -214,41 +212,64 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_tc(const KArgs a) {
 
   uint4 bufA[2][kRG], bufA2[2][kRG];
   uint4 bufB[2][kRG], bufB2[2][kRG];
-  if (c0 < c1) load_chunk(c0, bufA, bufA2);
+  if (c0 < c1) load_chunk(c0, bufA, bufA2);  // weights do not depend on the previous kernel
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  // per-token power-of-two scale over this warp's K slice
-  const int64_t klo = c0 * CK;
-  int64_t khi = c1 * CK;
+  // ---- per-CTA, per-token power-of-two scale over the CTA's K range
+  const int64_t klo = cta_c0 * CK;
+  int64_t khi = klo + static_cast<int64_t>(kWarps) * a.cpw * CK;
   if (khi > a.cols) khi = a.cols;
-  float sc[kB], sinv[kB];
 #pragma unroll
   for (int b = 0; b < kB; ++b) {
     float m = 0.0f;
-    for (int64_t k = klo + lane; k < khi; k += 32) {
+    for (int64_t k = klo + tid; k < khi; k += kWarps * 32) {
       const float v = fabsf(__ldg(a.x + b * a.x_ld + k));
       if (v > m && v <= 3.402823466e+38f) m = v;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) smax[warp][b] = m;
+  }
+  __syncthreads();
+  float sc[kB], sinv[kB];
+#pragma unroll
+  for (int b = 0; b < kB; ++b) {
+    float m = fmaxf(fmaxf(smax[0][b], smax[1][b]), fmaxf(smax[2][b], smax[3][b]));
     int e = 0;
     if (m > 0.0f) {
-      e = 14 - ilogbf(m);  // m * 2^e in [2^14, 2^15): far from f16 overflow (65504)
+      e = 14 - ilogbf(m);  // m * 2^e in [2^14, 2^15), below the f16 maximum 65504
       e = e > 126 ? 126 : (e < -126 ? -126 : e);
     }
     sc[b] = ldexpf(1.0f, e);
     sinv[b] = ldexpf(1.0f, -e);
   }
-  const int bn = g >> 1, pn = g & 1;      // the B column this lane supplies
-  const bool col_active = bn < kB;
-  float s_col = 1.0f;
+
+  // ---- B fragments of the CTA's K range, built once by all 128 threads
+  const int nent = a.nkb_cta * NCOL * 4;
+  for (int e = tid; e < nent; e += kWarps * 32) {
+    const int kbl = e / (NCOL * 4);
+    const int rem = e - kbl * (NCOL * 4);
+    const int n = rem >> 2, tt = rem & 3;
+    const int b = n >> 1, p = n & 1;
+    const int64_t k = klo + static_cast<int64_t>(kbl) * 16 + 2 * tt;
+    const float* xr = a.x + b * a.x_ld;
+    const float v0 = k < khi ? __ldg(xr + k) : 0.0f;
+    const float v1 = k + 1 < khi ? __ldg(xr + k + 1) : 0.0f;
+    const float v8 = k + 8 < khi ? __ldg(xr + k + 8) : 0.0f;
+    const float v9 = k + 9 < khi ? __ldg(xr + k + 9) : 0.0f;
+    float s = sc[0];
 #pragma unroll
-  for (int b = 0; b < kB; ++b)
-    if (bn == b) s_col = sc[b];
+    for (int q = 1; q < kB; ++q)
+      if (b == q) s = sc[q];
+    frag[e] = make_uint2(x_plane_pair(v0, v1, s, p), x_plane_pair(v8, v9, s, p));
+  }
+  __syncthreads();
+
   float sinv_t = 0.0f;
 #pragma unroll
   for (int b = 0; b < kB; ++b)
     if (t == b) sinv_t = sinv[b];
+  const bool col_active = g < NCOL;
 
   double acc[kRG][2], acc2[kRG][2];
 #pragma unroll
@@ -260,25 +281,21 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_tc(const KArgs a) {
     for (int r = 0; r < kRG; ++r)
 #pragma unroll
       for (int i = 0; i < 4; ++i) d[r][i] = d2[r][i] = 0.0f;
+    const int kb_base = static_cast<int>(c - cta_c0) * 2 * KBPU;
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
 #pragma unroll
       for (int j = 0; j < KBPU; ++j) {
-        const int64_t kb = (2 * c + u) * KBPU + j;
-        const int64_t k = kb * 16 + 2 * t;
-        uint32_t b0 = 0u, b1 = 0u;
-        if (col_active) {
-          b0 = x_plane_pair(xval(a, bn, k), xval(a, bn, k + 1), s_col, pn);
-          b1 = x_plane_pair(xval(a, bn, k + 8), xval(a, bn, k + 9), s_col, pn);
-        }
+        uint2 bf = make_uint2(0u, 0u);
+        if (col_active) bf = frag[((kb_base + u * KBPU + j) * NCOL + g) * 4 + t];
 #pragma unroll
         for (int r = 0; r < kRG; ++r) {
           uint32_t af[4];
           a_frag<kDt>(buf[u][r], j, af);
-          mma16816(d[r], af, b0, b1);
+          mma16816(d[r], af, bf.x, bf.y);
           if (kDual) {
             a_frag<kDt>(buf2[u][r], j, af);
-            mma16816(d2[r], af, b0, b1);
+            mma16816(d2[r], af, bf.x, bf.y);
           }
         }
       }
@@ -303,71 +320,49 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_tc(const KArgs a) {
     }
   }
 
-  // ---- CTA reduction over the 4 K slices (fixed order)
+  // ---- CTA reduction over its 4 K slices (fixed order)
   if (t < kB) {
 #pragma unroll
     for (int r = 0; r < kRG; ++r) {
       red[warp][r * 16 + g][0][t] = acc[r][0];
       red[warp][r * 16 + g + 8][0][t] = acc[r][1];
       if (kDual) {
-        red[warp][r * 16 + g][1][t] = acc2[r][0];
-        red[warp][r * 16 + g + 8][1][t] = acc2[r][1];
+        red[warp][r * 16 + g][kDual ? 1 : 0][t] = acc2[r][0];
+        red[warp][r * 16 + g + 8][kDual ? 1 : 0][t] = acc2[r][1];
       }
     }
   }
   __syncthreads();
-  const int nout = kRowsPerSet * kB;
-  if (a.splits == 1) {
-    for (int i = threadIdx.x; i < nout; i += blockDim.x) {
+  constexpr int M = kDual ? 2 : 1;
+  for (int i = tid; i < kRowsPerSet * M * kB; i += kWarps * 32) {
+    const int row = i / (M * kB), rem = i - row * M * kB, m = rem / kB, b = rem - m * kB;
+    double y = 0.0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) y += red[w][row][m][b];
+    cta_part[row][m][b] = y;
+  }
+
+  // ---- cluster reduction over the K splits through distributed shared memory
+  namespace cg = cooperative_groups;
+  if (a.csize > 1) cg::this_cluster().sync();
+  else __syncthreads();
+  if (rank == 0) {
+    for (int i = tid; i < kRowsPerSet * kB; i += kWarps * 32) {
       const int row = i / kB, b = i - row * kB;
       const int o = static_cast<int>(rs * kRowsPerSet + row);
-      if (o >= a.rows) continue;
       double y = 0.0, y2 = 0.0;
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        y += red[w][row][0][b];
-        if (kDual) y2 += red[w][row][1][b];
+      for (int r = 0; r < a.csize; ++r) {
+        const double (*part)[M][kB] = cta_part;
+        if (a.csize > 1) part = cg::this_cluster().map_shared_rank(cta_part, r);
+        y += part[row][0][b];
+        if (kDual) y2 += part[row][M - 1][b];
       }
+      if (o >= a.rows) continue;
       if (kDt == 9) { y *= static_cast<double>(a.scale); y2 *= static_cast<double>(a.scale2); }
       write_out(a, o, b, y, y2, kDual);
     }
-    return;
   }
-  for (int i = threadIdx.x; i < nout; i += blockDim.x) {
-    const int row = i / kB, b = i - row * kB;
-    double y = 0.0, y2 = 0.0;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      y += red[w][row][0][b];
-      if (kDual) y2 += red[w][row][1][b];
-    }
-    const int64_t base = ((static_cast<int64_t>(split) * a.rows_p) + rs * kRowsPerSet + row) * 8;
-    a.partial[base + b] = y;
-    if (kDual) a.partial[base + 4 + b] = y2;
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(&a.counters[rs], 1u);
-    last_flag = prev == static_cast<unsigned>(a.splits - 1);
-  }
-  __syncthreads();
-  if (!last_flag) return;
-  __threadfence();
-  for (int i = threadIdx.x; i < nout; i += blockDim.x) {
-    const int row = i / kB, b = i - row * kB;
-    const int o = static_cast<int>(rs * kRowsPerSet + row);
-    if (o >= a.rows) continue;
-    double y = 0.0, y2 = 0.0;
-    for (int s = 0; s < a.splits; ++s) {
-      const int64_t base = ((static_cast<int64_t>(s) * a.rows_p) + rs * kRowsPerSet + row) * 8;
-      y += __ldcg(a.partial + base + b);
-      if (kDual) y2 += __ldcg(a.partial + base + 4 + b);
-    }
-    if (kDt == 9) { y *= static_cast<double>(a.scale); y2 *= static_cast<double>(a.scale2); }
-    write_out(a, o, b, y, y2, kDual);
-  }
-  if (threadIdx.x == 0) a.counters[rs] = 0u;  // ready for the next launch
+  if (a.csize > 1) cg::this_cluster().sync();  // keep every rank's shared memory alive for rank 0
 }
 
 // One thread per output byte of the tiled mirror.
@@ -414,15 +409,28 @@ __global__ void k_build_tiled(const uint8_t* __restrict__ native, int rows, int 
 template <int kDt, int kB, bool kDual>
 Status launch_t(const KArgs& k, const Plan& pl, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(pl.row_sets), static_cast<unsigned>(pl.splits));
+  cfg.gridDim = dim3(static_cast<unsigned>(pl.csize), static_cast<unsigned>(pl.row_sets));
   cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = static_cast<size_t>(pl.nkb_cta) * 2 * kB * 4 * sizeof(uint2);
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeClusterDimension;
+  attr[n].val.clusterDim.x = static_cast<unsigned>(pl.csize);
+  attr[n].val.clusterDim.y = 1;
+  attr[n].val.clusterDim.z = 1;
+  ++n;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cuda_status(cudaLaunchKernelEx(&cfg, k_gemv_tc<kDt, kB, kDual>, k), "gemv_tc launch");
+  cfg.numAttrs = n;
+  auto kern = k_gemv_tc<kDt, kB, kDual>;
+  if (cfg.dynamicSmemBytes > 48 * 1024)
+    WB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(cfg.dynamicSmemBytes)));
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, k), "gemv_tc launch");
 }
 
 template <int kDt, bool kDual>
@@ -477,27 +485,10 @@ Status build_tiled_mirror(DType dt, const uint8_t* native, int rows, int cols, u
   return cuda_status(cudaGetLastError(), "tiled mirror launch");
 }
 
-size_t gemv_tc_scratch_bytes(DType dt, int rows, int cols) {
-  const Plan pl = make_plan(dt, rows, cols);
-  const size_t part = pl.splits > 1 ? static_cast<size_t>(pl.splits) * pl.rows_p * 8 * sizeof(double) : 0;
-  return round_up(static_cast<int64_t>(part), 256) + static_cast<size_t>(pl.row_sets) * sizeof(unsigned int);
-}
-
-Status gemv_tc_scratch_init(void* scratch, DType dt, int rows, int cols, cudaStream_t st) {
-  const Plan pl = make_plan(dt, rows, cols);
-  const size_t part = pl.splits > 1 ? static_cast<size_t>(pl.splits) * pl.rows_p * 8 * sizeof(double) : 0;
-  uint8_t* c = static_cast<uint8_t*>(scratch) + round_up(static_cast<int64_t>(part), 256);
-  return cuda_status(cudaMemsetAsync(c, 0, static_cast<size_t>(pl.row_sets) * sizeof(unsigned int), st),
-                     "gemv_tc counters");
-}
-
 Status launch_gemv_tc(const GemvTcArgs& a, cudaStream_t st, bool pdl) {
   if (!gemv_tc_supported(a.dtype)) return Status::Unsupported("gemv_tc: dtype");
   if (a.rows <= 0 || a.cols <= 0 || a.batch < 1 || a.batch > 4) return Status::Invalid("gemv_tc: bad dims");
   const Plan pl = make_plan(a.dtype, a.rows, a.cols);
-  const size_t need = gemv_tc_scratch_bytes(a.dtype, a.rows, a.cols);
-  if (!a.scratch || a.scratch_bytes < need) return Status::Internal("gemv_tc: scratch too small");
-  const size_t part = pl.splits > 1 ? static_cast<size_t>(pl.splits) * pl.rows_p * 8 * sizeof(double) : 0;
   KArgs k{};
   k.Wt = a.Wt;
   k.Wt2 = a.Wt2;
@@ -507,8 +498,8 @@ Status launch_gemv_tc(const GemvTcArgs& a, cudaStream_t st, bool pdl) {
   k.row_groups = pl.g.row_groups;
   k.chunks = pl.chunks;
   k.cpw = pl.cpw;
-  k.splits = pl.splits;
-  k.rows_p = pl.rows_p;
+  k.csize = pl.csize;
+  k.nkb_cta = pl.nkb_cta;
   k.scale = a.scale;
   k.scale2 = a.scale2;
   k.x = a.x;
@@ -519,8 +510,6 @@ Status launch_gemv_tc(const GemvTcArgs& a, cudaStream_t st, bool pdl) {
   k.bias = a.bias;
   k.bias_len = a.bias_len;
   k.act = a.act;
-  k.partial = reinterpret_cast<double*>(a.scratch);
-  k.counters = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(a.scratch) + round_up(static_cast<int64_t>(part), 256));
   return a.Wt2 ? launch_d<true>(a.dtype, k, pl, a.batch, st, pdl) : launch_d<false>(a.dtype, k, pl, a.batch, st, pdl);
 }
 

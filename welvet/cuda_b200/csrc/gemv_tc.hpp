@@ -36,16 +36,11 @@ struct GemvTcArgs {
   const double* bias = nullptr;
   int bias_len = 0;
   int act = -1;
-  void* scratch = nullptr;       // gemv_tc_scratch_bytes(); counters must start at zero
-  size_t scratch_bytes = 0;
 };
 
-// Scratch of one layer: split-K partials (f64) and per-row-set arrival counters. The
-// counters are left at zero by every completed launch.
-size_t gemv_tc_scratch_bytes(DType dt, int rows, int cols);
-// Zero the counters of a freshly allocated scratch block.
-Status gemv_tc_scratch_init(void* scratch, DType dt, int rows, int cols, cudaStream_t st);
-
+// Launches on `st` with a thread-block cluster per 64-row set (split-K reduced in
+// distributed shared memory); with pdl=true it may overlap the previous kernel (weights are
+// prefetched before griddepcontrol.wait; x is read and outputs written after it).
 Status launch_gemv_tc(const GemvTcArgs& a, cudaStream_t st, bool pdl);
 
 } // namespace wb
