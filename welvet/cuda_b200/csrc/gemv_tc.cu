@@ -49,8 +49,11 @@ Plan make_plan(DType dt, int rows, int cols) {
   p.g = tiled_geom(dt, rows, cols);
   p.row_sets = (p.g.row_groups + kRG - 1) / kRG;
   p.chunks = (p.g.units_k + 1) / 2;
+  // At least two chunks per warp: both are loaded before griddepcontrol.wait, and a launch
+  // then takes about half of the GPU's CTA slots, so the next launch can co-reside and
+  // prefetch its weights.
   p.cpw = static_cast<int>((p.chunks + kWarps * kMaxCluster - 1) / (kWarps * kMaxCluster));
-  if (p.cpw < 1) p.cpw = 1;
+  if (p.cpw < 2) p.cpw = 2;
   p.csize = static_cast<int>((p.chunks + kWarps * p.cpw - 1) / (kWarps * p.cpw));
   const int kbpu = dt == DType::FP4 ? 4 : 2;
   p.nkb_cta = kWarps * p.cpw * 2 * kbpu;
@@ -212,19 +215,28 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_tc(const KArgs a) {
 
   uint4 bufA[2][kRG], bufA2[2][kRG];
   uint4 bufB[2][kRG], bufB2[2][kRG];
-  if (c0 < c1) load_chunk(c0, bufA, bufA2);  // weights do not depend on the previous kernel
+  // The first two chunks' weights are requested before waiting on the previous kernel:
+  // they do not depend on it.
+  if (c0 < c1) load_chunk(c0, bufA, bufA2);
+  if (c0 + 1 < c1) load_chunk(c0 + 1, bufB, bufB2);
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  // ---- per-CTA, per-token power-of-two scale over the CTA's K range
+  // ---- the CTA's x slice, read from global memory once into shared memory (zero past
+  //      `cols`), with the per-token maximum taken on the way
   const int64_t klo = cta_c0 * CK;
-  int64_t khi = klo + static_cast<int64_t>(kWarps) * a.cpw * CK;
+  const int kspan = a.nkb_cta * 16;
+  int64_t khi = klo + kspan;
   if (khi > a.cols) khi = a.cols;
+  float* xs = reinterpret_cast<float*>(frag + a.nkb_cta * NCOL * 4);  // [kB][kspan]
 #pragma unroll
   for (int b = 0; b < kB; ++b) {
     float m = 0.0f;
-    for (int64_t k = klo + tid; k < khi; k += kWarps * 32) {
-      const float v = fabsf(__ldg(a.x + b * a.x_ld + k));
-      if (v > m && v <= 3.402823466e+38f) m = v;
+    for (int i = tid; i < kspan; i += kWarps * 32) {
+      const int64_t k = klo + i;
+      const float v = k < khi ? __ldg(a.x + b * a.x_ld + k) : 0.0f;
+      xs[b * kspan + i] = v;
+      const float av = fabsf(v);
+      if (av > m && av <= 3.402823466e+38f) m = av;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -251,12 +263,8 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_tc(const KArgs a) {
     const int rem = e - kbl * (NCOL * 4);
     const int n = rem >> 2, tt = rem & 3;
     const int b = n >> 1, p = n & 1;
-    const int64_t k = klo + static_cast<int64_t>(kbl) * 16 + 2 * tt;
-    const float* xr = a.x + b * a.x_ld;
-    const float v0 = k < khi ? __ldg(xr + k) : 0.0f;
-    const float v1 = k + 1 < khi ? __ldg(xr + k + 1) : 0.0f;
-    const float v8 = k + 8 < khi ? __ldg(xr + k + 8) : 0.0f;
-    const float v9 = k + 9 < khi ? __ldg(xr + k + 9) : 0.0f;
+    const float* xr = xs + b * kspan + kbl * 16 + 2 * tt;
+    const float v0 = xr[0], v1 = xr[1], v8 = xr[8], v9 = xr[9];
     float s = sc[0];
 #pragma unroll
     for (int q = 1; q < kB; ++q)
@@ -311,12 +319,14 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_tc(const KArgs a) {
     }
   };
 
+  // chunk c sits in bufA when c - c0 is even, in bufB when odd; the chunk two ahead is
+  // requested as soon as its buffer is free.
   for (int64_t c = c0; c < c1; c += 2) {
-    if (c + 1 < c1) load_chunk(c + 1, bufB, bufB2);
     compute_chunk(c, bufA, bufA2);
+    if (c + 2 < c1) load_chunk(c + 2, bufA, bufA2);
     if (c + 1 < c1) {
-      if (c + 2 < c1) load_chunk(c + 2, bufA, bufA2);
       compute_chunk(c + 1, bufB, bufB2);
+      if (c + 3 < c1) load_chunk(c + 3, bufB, bufB2);
     }
   }
 
@@ -411,7 +421,9 @@ Status launch_t(const KArgs& k, const Plan& pl, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(pl.csize), static_cast<unsigned>(pl.row_sets));
   cfg.blockDim = dim3(kWarps * 32);
-  cfg.dynamicSmemBytes = static_cast<size_t>(pl.nkb_cta) * 2 * kB * 4 * sizeof(uint2);
+  // B fragments [nkb_cta][2 kB][4] uint2, then the x slice [kB][16 nkb_cta] float
+  cfg.dynamicSmemBytes = static_cast<size_t>(pl.nkb_cta) * 2 * kB * 4 * sizeof(uint2) +
+                         static_cast<size_t>(pl.nkb_cta) * 16 * kB * sizeof(float);
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   int n = 0;
