@@ -43,6 +43,21 @@ WELVET_API welvet_status welvet_b200_dense_execute_device(welvet_dense_session* 
                                                           const float* x_dev, float* pre_dev,
                                                           float* post_dev, void* stream);
 
+/* No counterpart in the reference. welvet_b200_dense_execute_device without any allocation,
+ * for callers that cannot call cudaMalloc while they run a forward: a serving loop that must
+ * not stall on an allocation (cudaMalloc can synchronize the device), code that runs while a
+ * CUDA graph is being captured, or a framework that owns all device memory up front. It runs
+ * the batched tensor-core forward (a session of batch > 4, FP8/FP4/Int8, outside exact mode;
+ * other sessions get status 2) with the scratch of that kernel -- x split into f16 planes,
+ * per-token scales, split-K partials -- in one static 32 MiB device array that the library
+ * holds on every GPU that loads it until the process exits; a call needing more returns
+ * status 1. The first call on a device looks up the array's device address and should be
+ * made before any stream capture. All calls share the array: calls whose kernels overlap on
+ * one GPU (other streams or threads) race and must be serialized by the caller. */
+WELVET_API welvet_status welvet_b200_dense_execute_device_noalloc(welvet_dense_session* sess,
+                                                                  const float* x_dev, float* pre_dev,
+                                                                  float* post_dev, void* stream);
+
 /* The session's authoritative host store: dtype, rows (= out), cols (= in), scale and the
  * native bytes in the reference layout (FP4: low nibble = even flat index). Float32 stores
  * return their float payload. *native_len is always set; the bytes are copied when

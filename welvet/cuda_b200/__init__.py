@@ -76,6 +76,7 @@ _sig("welvet_b200_dense_mount_native", _ST, c_int32, c_int32, c_int32, c_int32, 
      c_float, c_void_p, c_size_t, POINTER(c_void_p))
 _sig("welvet_dense_execute", _ST, c_void_p, c_void_p, c_void_p, c_void_p)
 _sig("welvet_b200_dense_execute_device", _ST, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p)
+_sig("welvet_b200_dense_execute_device_noalloc", _ST, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p)
 _sig("welvet_dense_release", None, c_void_p)
 _sig("welvet_b200_dense_store", _ST, c_void_p, POINTER(c_int32), POINTER(c_int32), POINTER(c_int32),
      POINTER(c_float), c_void_p, c_size_t, POINTER(c_size_t))
@@ -195,6 +196,14 @@ class DenseSession:
     def execute_device(self, x, pre, post, stream=None) -> None:
         check(_L.welvet_b200_dense_execute_device(self._h, c_void_p(_dev_ptr(x)), c_void_p(_dev_ptr(pre)),
                                                   c_void_p(_dev_ptr(post)), _stream_ptr(stream)))
+
+    def execute_device_noalloc(self, x, pre, post, stream=None) -> None:
+        """execute_device for callers that cannot allocate device memory during a forward
+        (allocation-free serving loops, stream capture, frameworks owning all device memory):
+        batched sessions only, scratch in the library's static 32 MiB device array; calls
+        that overlap on one GPU race on that array."""
+        check(_L.welvet_b200_dense_execute_device_noalloc(self._h, c_void_p(_dev_ptr(x)), c_void_p(_dev_ptr(pre)),
+                                                          c_void_p(_dev_ptr(post)), _stream_ptr(stream)))
 
     def store(self):
         """(dtype, rows, cols, scale, native bytes in the reference layout)."""

@@ -190,6 +190,14 @@ welvet_status welvet_b200_dense_execute_device(welvet_dense_session* sess, const
   });
 }
 
+welvet_status welvet_b200_dense_execute_device_noalloc(welvet_dense_session* sess, const float* x_dev,
+                                                       float* pre_dev, float* post_dev, void* stream) {
+  return guarded([&] {
+    if (!sess) return wb::Status::Invalid("null execute args");
+    return wb::session_execute_device_noalloc(sess->s, x_dev, pre_dev, post_dev, static_cast<cudaStream_t>(stream));
+  });
+}
+
 void welvet_dense_release(welvet_dense_session* sess) {
   if (!sess) return;
   delete sess->s;

@@ -427,6 +427,36 @@ Status check_pipeline_error(DenseIO& io, cudaStream_t st) {
   return Status::Internal("tensor-core pipeline wait timed out (stage code " + std::to_string(e) + ")");
 }
 
+// The batched tensor-core forward with its scratch in the library's static device array
+// (gemm_tc.hpp: launch_gemm_tc_static) instead of the session's: makes no allocation.
+Status session_execute_device_noalloc(DenseSession* s, const float* x, float* pre, float* post, cudaStream_t st) {
+  if (!s || !x || !pre || !post) return Status::Invalid("null execute args");
+  const DeviceDense& d = s->dev;
+  if (!use_tensor_path(d, s->batch))
+    return Status::Unsupported("allocation-free forward serves the batched tensor-core path only "
+                               "(FP8/FP4/Int8 sessions with batch > 4 outside exact mode)");
+  WB_CUDA(cudaSetDevice(s->device));
+  GemmArgs g;
+  g.dtype = d.dtype;
+  g.W = d.W;
+  g.row_stride = d.row_stride;
+  g.rows = d.rows;
+  g.cols = d.cols;
+  g.scale = d.scale;
+  g.x = x;
+  g.x_ld = d.cols;
+  g.M = s->batch;
+  g.pre = pre;
+  g.post = post;
+  g.ld_out = d.rows;
+  g.bias = d.bias;
+  g.bias_len = d.bias_len;
+  g.act = d.act;
+  g.xsplit = xsplit_policy();
+  g.err = s->io.err;
+  return launch_gemm_tc_static(g, st);
+}
+
 Status session_execute_device(DenseSession* s, const float* x, float* pre, float* post, cudaStream_t st) {
   if (!s || !x || !pre || !post) return Status::Invalid("null execute args");
   WB_CUDA(cudaSetDevice(s->device));

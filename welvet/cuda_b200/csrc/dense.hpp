@@ -126,6 +126,11 @@ Status session_execute(DenseSession* s, const float* x, float* pre, float* post)
 Status session_execute_device(DenseSession* s, const float* x, float* pre, float* post,
                               cudaStream_t st);
 
+// Same forward for batched sessions (> 4 tokens on the tcgen05 path), with the GEMM's scratch
+// in the library's fixed static device array: no allocation of any kind.
+Status session_execute_device_noalloc(DenseSession* s, const float* x, float* pre, float* post,
+                                      cudaStream_t st);
+
 // Library device selection: the device current on the first call of the process (0 unless
 // the host application selected another), unless WELVET_B200_DEVICE is set.
 Status library_device(int* device);

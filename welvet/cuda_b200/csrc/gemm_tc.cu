@@ -560,4 +560,57 @@ Status launch_gemm_tc(const GemmArgs& a, cudaStream_t st) {
   return Status::Ok();
 }
 
+// ---------------------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// Some callers cannot call cudaMalloc when they run a forward: a serving loop that must
+// never stall on an allocation (cudaMalloc can synchronize the device), code running while
+// a CUDA graph is being captured, or a framework that owns all device memory up front and
+// forbids other allocations once it runs. For them launch_gemm_tc_static runs the same
+// tcgen05 GEMM with its scratch (the f16 planes of x, the per-token scales and the split-K
+// partials) in one array that lives in this file for the life of the process.
+//
+// The array is kStaticScratchBytes (32 MiB) on every GPU that loads the library, held until
+// the process exits. All calls share it: two calls whose kernels overlap on a GPU (different
+// streams, or different host threads on one device) race on it and must be serialized by
+// the caller. A call keeps the previous call's contents; nothing in it has to start at zero
+// (each launch writes every plane, scale and partial before reading it).
+constexpr size_t kStaticScratchBytes = static_cast<size_t>(32) << 20;
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+void* g_static_ptr[kMaxDevices] = {};
+} // namespace
+
+size_t gemm_static_scratch_bytes() { return kStaticScratchBytes; }
+
+Status launch_gemm_tc_static(const GemmArgs& a_in, cudaStream_t st) {
+  const size_t need = gemm_scratch_bytes(a_in.M, a_in.cols, a_in.rows, a_in.xsplit);
+  if (need > kStaticScratchBytes)
+    return Status::Invalid("allocation-free forward: needs " + std::to_string(need) +
+                           " bytes of scratch, the static array holds " + std::to_string(kStaticScratchBytes) +
+                           " (fewer tokens per call, or the allocating entry point)");
+  int dev = 0;
+  WB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return Status::Internal("allocation-free forward: device index out of range");
+  void* ptr = nullptr;
+  {
+    // Once per device, with that device current: the array's device address. The host-side
+    // symbol is only a stand-in and must never reach a kernel.
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (!g_static_ptr[dev]) {
+      void* p = nullptr;
+      WB_CUDA(cudaGetSymbolAddress(&p, g_static_scratch));
+      g_static_ptr[dev] = p;
+    }
+    ptr = g_static_ptr[dev];
+  }
+  GemmArgs a = a_in;
+  a.scratch = ptr;
+  a.scratch_bytes = kStaticScratchBytes;
+  return launch_gemm_tc(a, st);
+}
+
 } // namespace wb
