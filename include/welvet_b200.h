@@ -116,6 +116,68 @@ WELVET_API welvet_status welvet_b200_mha_execute_device(welvet_b200_mha* s, int3
                                                         float* attn_dev, float* y_dev, void* stream);
 WELVET_API void welvet_b200_mha_release(welvet_b200_mha* s);
 
+/* ---------------------------------------------------------------- volume (Grid) */
+
+/* A depth x rows x cols x layers_per_cell grid of cells (reference architecture::Grid,
+ * include/welvet/architecture.hpp:100-141; non-positive dimensions become 1) run in hop order
+ * z, y, x, l with activations kept on the device (reference runtime::forward::volume_dense,
+ * src/runtime/forward.cpp:98-156). Coordinates out of range return status 1. */
+typedef struct welvet_b200_volume welvet_b200_volume;
+WELVET_API welvet_status welvet_b200_volume_create(int32_t depth, int32_t rows, int32_t cols,
+                                                   int32_t layers_per_cell, welvet_b200_volume** out);
+WELVET_API welvet_status welvet_b200_volume_bind_dense(welvet_b200_volume* v, int32_t z, int32_t y,
+                                                       int32_t x, int32_t l, int32_t in, int32_t out,
+                                                       int32_t act, int32_t dtype, const float* W,
+                                                       const double* bias, size_t bias_len,
+                                                       int32_t weights_on_device);
+WELVET_API welvet_status welvet_b200_volume_bind_dense_native(welvet_b200_volume* v, int32_t z,
+                                                              int32_t y, int32_t x, int32_t l,
+                                                              int32_t in, int32_t out, int32_t act,
+                                                              int32_t dtype, const uint8_t* native,
+                                                              size_t native_len, float scale,
+                                                              const double* bias, size_t bias_len);
+WELVET_API welvet_status welvet_b200_volume_bind_swiglu(welvet_b200_volume* v, int32_t z, int32_t y,
+                                                        int32_t x, int32_t l, int32_t input_dim,
+                                                        int32_t intermediate_dim, int32_t dtype,
+                                                        const float* Gate, const float* Up,
+                                                        const float* Down, int32_t weights_on_device);
+WELVET_API welvet_status welvet_b200_volume_bind_mha(welvet_b200_volume* v, int32_t z, int32_t y,
+                                                     int32_t x, int32_t l, int32_t d_model,
+                                                     int32_t num_heads, int32_t num_kv_heads,
+                                                     int32_t head_dim, int32_t max_seq_len,
+                                                     int32_t mask, int32_t pos, int32_t seq,
+                                                     int32_t dtype, const float* Q, const float* K,
+                                                     const float* V, const float* O,
+                                                     int32_t weights_on_device);
+WELVET_API welvet_status welvet_b200_volume_bind_rmsnorm(welvet_b200_volume* v, int32_t z, int32_t y,
+                                                         int32_t x, int32_t l, int32_t dim, double eps,
+                                                         int32_t dtype, const float* gamma);
+/* reference architecture::set_remote_link (src/architecture/grid.cpp:97-107) */
+WELVET_API welvet_status welvet_b200_volume_set_remote_link(welvet_b200_volume* v, int32_t z, int32_t y,
+                                                            int32_t x, int32_t l, int32_t tz,
+                                                            int32_t ty, int32_t tx, int32_t tl);
+WELVET_API welvet_status welvet_b200_volume_set_disabled(welvet_b200_volume* v, int32_t z, int32_t y,
+                                                         int32_t x, int32_t l, int32_t disabled);
+WELVET_API int32_t welvet_b200_volume_hops(welvet_b200_volume* v);
+/* Runs hops [hop_begin, hop_end) (-1 = to the end) on `rows` rows of x_dev [rows][in_width];
+ * the last executed cell's post goes to out_dev (may be NULL), its width to *out_width. */
+WELVET_API welvet_status welvet_b200_volume_forward_device(welvet_b200_volume* v, int32_t rows,
+                                                           const float* x_dev, int32_t in_width,
+                                                           int32_t hop_begin, int32_t hop_end,
+                                                           float* out_dev, int32_t* out_width,
+                                                           void* stream);
+/* Host-buffer forward over every hop, synchronous; out_host holds rows x out_cap floats. */
+WELVET_API welvet_status welvet_b200_volume_forward_f32(welvet_b200_volume* v, int32_t rows,
+                                                        const float* x_host, int32_t in_width,
+                                                        float* out_host, size_t out_cap,
+                                                        int32_t* out_width);
+/* Device pointers of a cell's last pre / post ([rows][width]), for per-step records. */
+WELVET_API welvet_status welvet_b200_volume_cell_outputs(welvet_b200_volume* v, int32_t z, int32_t y,
+                                                         int32_t x, int32_t l, const float** pre,
+                                                         int32_t* pre_width, const float** post,
+                                                         int32_t* post_width);
+WELVET_API void welvet_b200_volume_release(welvet_b200_volume* v);
+
 #ifdef __cplusplus
 }
 #endif
