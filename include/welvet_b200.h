@@ -166,7 +166,8 @@ WELVET_API welvet_status welvet_b200_volume_forward_device(welvet_b200_volume* v
                                                            int32_t hop_begin, int32_t hop_end,
                                                            float* out_dev, int32_t* out_width,
                                                            void* stream);
-/* Host-buffer forward over every hop, synchronous; out_host holds rows x out_cap floats. */
+/* Host-buffer forward over every hop, synchronous. out_host receives the last executed cell's
+   post densely as [rows][*out_width]; out_cap is its capacity in floats. */
 WELVET_API welvet_status welvet_b200_volume_forward_f32(welvet_b200_volume* v, int32_t rows,
                                                         const float* x_host, int32_t in_width,
                                                         float* out_host, size_t out_cap,

@@ -320,14 +320,18 @@ def test_dense_vs_reference_cuda_kernel(wb, oracle):
 GEMM_TOL = {"3": 2.0 ** -16, "2": 2.0 ** -15, "1": 2.0 ** -9}
 
 
+@pytest.mark.parametrize("kernel", ["tmem", "smem"])
 @pytest.mark.parametrize("xsplit", ["3", "2", "1"])
 @pytest.mark.parametrize("dt", [16, 4, 5, 9])
-@pytest.mark.parametrize("shape", [(128, 64, 8), (300, 1000, 16), (256, 4096, 64), (130, 257, 100), (1024, 512, 5)])
-def test_tensor_core_path_parity(wb, oracle, dt, shape, xsplit, monkeypatch):
+@pytest.mark.parametrize("shape", [(128, 64, 8), (300, 1000, 16), (256, 4096, 64), (130, 257, 100), (1024, 512, 5),
+                                   (200, 640, 300), (384, 192, 520)])
+def test_tensor_core_path_parity(wb, oracle, dt, shape, xsplit, kernel, monkeypatch):
     """Batches above 4 run the tcgen05 GEMM (f16 planes of x, exact products, fp32 tensor
-    accumulation). Error normalised by sum_k |W x| stays under the stated bound per x split."""
+    accumulation), with the dequantised weights in TMEM (default) or in shared memory. Error
+    normalised by sum_k |W x| stays under the stated bound per x split."""
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
     monkeypatch.setenv("WELVET_B200_XSPLIT", xsplit)
+    monkeypatch.setenv("WELVET_B200_GEMM", kernel)
     out, in_, batch = shape
     w, x, bias, ref = _case(oracle, dt, out, in_, batch, 2.0, out + in_ + batch, 0)
     pre, post = wb.dense_forward_f32(w, x, dt, 0, bias)
@@ -338,6 +342,37 @@ def test_tensor_core_path_parity(wb, oracle, dt, shape, xsplit, monkeypatch):
     assert norm <= GEMM_TOL[xsplit], norm
     relu = np.maximum(pre.astype(np.float64), 0)
     assert np.allclose(post, relu.astype(np.float32))
+
+
+@pytest.mark.parametrize("dt", [4, 16])
+def test_adaptive_x_planes(wb, oracle, dt, monkeypatch):
+    """A token block whose x is exact in one f16 plane runs one plane: the same bits as a
+    forced single plane, and within the three-plane bound of the fp64 oracle. A block with
+    full fp32 x next to it runs three planes without changing the first block's results."""
+    monkeypatch.setenv("WELVET_B200_EXACT", "0")
+    rng = np.random.default_rng(77)
+    out, in_, M = 256, 512, 300
+    w = (rng.standard_normal((out, in_)) * 2.0).astype(np.float32)
+    xb = rng.standard_normal((M, in_)).astype(np.float32)
+    xb = (xb.view(np.uint32) & np.uint32(0xFFFF0000)).view(np.float32)  # bf16 values
+    xb[np.abs(xb) < 1e-6] = 0.0  # far below a token's max, a bf16 value can need a second f16 plane
+    runs = {}
+    for xs in ("3", "1"):
+        monkeypatch.setenv("WELVET_B200_XSPLIT", xs)
+        runs[xs] = wb.dense_forward_f32(w, xb, dt)[0]
+    assert np.array_equal(runs["3"].view(np.uint32), runs["1"].view(np.uint32))
+    raw, sc = oracle.pack(dt, w)
+    ref = oracle.dense_forward(dt, raw, sc, xb, in_, out)
+    err = np.abs(runs["3"].astype(np.float64) - ref[0].astype(np.float64)) - 2 * ulp(ref[0])
+    assert float(np.max(err / np.maximum(ref[3], 1e-300))) <= GEMM_TOL["3"]
+    xm = xb.copy()
+    xm[256:] = rng.standard_normal((M - 256, in_)).astype(np.float32)
+    monkeypatch.setenv("WELVET_B200_XSPLIT", "3")
+    mixed = wb.dense_forward_f32(w, xm, dt)[0]
+    assert np.array_equal(mixed[:256].view(np.uint32), runs["3"][:256].view(np.uint32))
+    ref = oracle.dense_forward(dt, raw, sc, xm, in_, out)
+    err = np.abs(mixed.astype(np.float64) - ref[0].astype(np.float64)) - 2 * ulp(ref[0])
+    assert float(np.max(err / np.maximum(ref[3], 1e-300))) <= GEMM_TOL["3"]
 
 
 @pytest.mark.parametrize("dt", [16, 4, 9])

@@ -39,19 +39,20 @@ DeviceDense& DeviceDense::operator=(DeviceDense&& o) noexcept {
   if (this == &o) return *this;
   release();
   device = o.device; dtype = o.dtype; rows = o.rows; cols = o.cols;
-  row_stride = o.row_stride; x_stride = o.x_stride; W = o.W; Wt = o.Wt; scale = o.scale;
+  row_stride = o.row_stride; x_stride = o.x_stride; W = o.W; Wt = o.Wt; Wg = o.Wg; scale = o.scale;
   bias = o.bias; bias_len = o.bias_len; act = o.act; exact = o.exact;
-  o.W = nullptr; o.Wt = nullptr; o.bias = nullptr;
+  o.W = nullptr; o.Wt = nullptr; o.Wg = nullptr; o.bias = nullptr;
   return *this;
 }
 
 void DeviceDense::release() {
-  if (W || Wt || bias) {
+  if (W || Wt || Wg || bias) {
     int cur = 0;
     cudaGetDevice(&cur);
     cudaSetDevice(device);
     free_dev(W);
     free_dev(Wt);
+    free_dev(Wg);
     free_dev(bias);
     cudaSetDevice(cur);
   }
@@ -126,6 +127,10 @@ static Status finish_mirror(int device, int rows, int cols, DType dt, int act, c
   if (gemv_tc_supported(dt) && !d.exact) {
     WB_CUDA(cudaMalloc(&d.Wt, static_cast<size_t>(tiled_geom(dt, rows, cols).bytes())));
     WB_TRY(build_tiled_mirror(dt, native_dev, rows, cols, d.Wt, st));
+  }
+  if (gemm_supported(dt) && !d.exact) {
+    WB_CUDA(cudaMalloc(&d.Wg, gemm_mirror_bytes(dt, rows, cols)));
+    WB_TRY(build_gemm_mirror(dt, d.W, rows, d.row_stride, cols, d.Wg, st));
   }
   store->bias.clear();
   if (bias && bias_len > 0) {
@@ -239,6 +244,7 @@ Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x
     GemmArgs g;
     g.dtype = d.dtype;
     g.W = d.W;
+    g.Wg = d.Wg;
     g.row_stride = d.row_stride;
     g.rows = d.rows;
     g.cols = d.cols;
@@ -439,6 +445,7 @@ Status session_execute_device_noalloc(DenseSession* s, const float* x, float* pr
   GemmArgs g;
   g.dtype = d.dtype;
   g.W = d.W;
+  g.Wg = d.Wg;
   g.row_stride = d.row_stride;
   g.rows = d.rows;
   g.cols = d.cols;

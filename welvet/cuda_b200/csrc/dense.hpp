@@ -37,6 +37,7 @@ struct DeviceDense {
   int64_t x_stride = 0;     // floats per padded activation row this layer consumes
   uint8_t* W = nullptr;     // mirror [rows][row_stride]
   uint8_t* Wt = nullptr;    // fragment-tiled mirror for the small-batch tensor GEMV (gemv_tc.hpp)
+  uint8_t* Wg = nullptr;    // 128-row tiled mirror for the batched tcgen05 GEMM (gemm_tc.hpp)
   float scale = 1.0f;
   double* bias = nullptr;   // [bias_len]
   int bias_len = 0;

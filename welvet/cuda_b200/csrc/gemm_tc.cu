@@ -1,31 +1,37 @@
 // gemm_tc.cu -- batched dequant GEMM on sm_100a tensor cores (tcgen05.mma kind::f16, TMEM).
 //
-// Replaces, for batch >= 8 tokens, the reference's per-output fp64 loop
-// (src/cuda/kernels.cu:130-145) over a host-decoded fp64 W. The packed mirror is read once
-// per token tile:
+// Replaces, for batches above 4 tokens, the reference's per-output fp64 loop
+// (src/cuda/kernels.cu:130-145) over a host-decoded fp64 W. Two kernels:
 //
-//   warp 0      TMA producer: the raw packed W tile (128 rows x 64 k) and the activation
-//               tile of every x plane (T tokens x 64 k, f16, SWIZZLE_128B) per stage; also
-//               allocates / frees the TMEM accumulator.
-//   warp 1      MMA issuer (one thread): 4 x tcgen05.mma (K = 16 each) per stage, A and B from
-//               shared memory, fp32 accumulation in TMEM; tcgen05.commit frees the stage.
-//   warps 2..5  converters: raw codes -> f16 (hardware e2m1/e4m3/e5m2 -> f16x2 converters,
-//               Int8 via an exact f16 bias trick) written in the UMMA K-major SWIZZLE_128B
-//               layout; then the epilogue: tcgen05.ld of the accumulator, the planes of each
-//               token combined in fp64, per-token 2^-e and Int8 scale applied, then bias /
-//               activation exactly as the reference's dense_bias_act (kernels.cu:147-161).
+//   k_gemm_tm (default)  the dequantised weight tile is the MMA's A operand in TMEM: converter
+//                        warps read the packed codes (one row per thread) from a deep ring of
+//                        raw W tiles (bulk copies of the GEMM mirror), convert with the
+//                        hardware e2m1/e4m3/e5m2 -> f16x2 converters (Int8 via an exact f16
+//                        bias trick) and write them with tcgen05.st; the x planes are the B
+//                        operand, TMA-loaded into shared memory. See the comment above it.
+//   k_gemm_tc            the same GEMM with A in shared memory (WELVET_B200_GEMM=smem), kept
+//                        for comparison.
 //
-// The x planes ride in the N dimension of one MMA ([plane][token] rows of B), so each A tile
-// is read from shared memory once per K step. Every mbarrier wait is bounded by
-// %globaltimer (2 s); on expiry the kernel records an error word and winds down, it never
-// spins forever. No TMA multicast is used.
+// x is split per token into f16 planes after a power-of-two scale (x * 2^e = p0 + p1 + p2,
+// k_split_x); the planes ride in the N dimension of one MMA. FP8/FP4/Int8 codes are exact in
+// f16, so every product is exact and the tensor core accumulates in fp32; planes are
+// combined in fp64 in the epilogue, which then applies the per-token 2^-e, the Int8 scale,
+// and bias / activation exactly as the reference's dense_bias_act (kernels.cu:147-161).
+//
+// Every mbarrier wait is bounded by %globaltimer (2 s); on expiry the kernel records an error
+// word and winds down, it never spins forever. No TMA multicast is used.
 #include "gemm_tc.hpp"
 #include "codec.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
+#include <tuple>
+#include <vector>
 
 namespace wb {
 namespace {
@@ -92,8 +98,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait: false (and the error word set) once kWaitNs of wall time has passed.
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  if (mbar_try_wait(bar, parity)) return true;
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* err, int code) {
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -103,6 +108,24 @@ __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
     }
   }
 }
+
+// The common case (phase already complete) stays inline; the bounded loop is out of line.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, err, code);
+}
+
+// Ring position without divisions: slot and phase bit advance together.
+struct Ring {
+  int slot = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void step(int n) {
+    if (++slot == n) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -200,7 +223,10 @@ __device__ __forceinline__ uint4 codes_to_f16x8(const uint8_t* raw_row, int j) {
   return o;
 }
 
-__device__ __forceinline__ void write_out(const KParams& p, int t, int o, double y) {
+// The reference epilogue (src/cuda/kernels.cu:147-161): pre = float(y); with bias
+// v = double(pre) + bias and pre = float(v); post = float(act(v)).
+template <typename Params>
+__device__ __forceinline__ void write_out(const Params& p, int t, int o, double y) {
   const int64_t idx = static_cast<int64_t>(t) * p.ld_out + o;
   float pre = static_cast<float>(y);
   double v = static_cast<double>(pre);
@@ -349,6 +375,418 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// A in tensor memory (the default batched kernel).
+//
+// The dequantised weight tile is the MMA's A operand and lives in TMEM, not shared memory:
+// each converter thread owns one weight row (one TMEM lane), reads that row's packed codes
+// from the TMA-loaded raw tile, converts them in registers and writes them with tcgen05.st.
+// Shared memory then carries only the packed bytes (0.5 or 1 B per weight) and the x
+// planes, instead of packed bytes + the f16 tile written by the converters + the f16 tile
+// read by the tensor core. The raw tile is loaded with the 32-byte (FP4) or 64-byte (8-bit)
+// swizzle so that 32 threads reading 32 rows hit 32 distinct banks.
+//
+// x planes: the split kernel records per token how many planes are non-zero; a CTA runs
+// with the largest count P over its token block (so an x that is exact in f16 after the
+// per-token power of two costs one plane, and the sums equal the three-plane sums since the
+// skipped planes are exactly zero). A pass covers T = min(block, 384 / P) tokens: all P x T
+// accumulator columns live in TMEM at once (one or two MMAs of N <= 256 per K step), so each
+// weight stage is converted once per pass and a block of up to 384 / P tokens streams its
+// weights once.
+//
+// TMEM columns: accumulators [0, 384) at most, then the A stages (32 columns = 64 f16 per
+// row each) up to column 512.
+//
+// Three rings decouple the pipeline: raw W tiles (deep, so that many DRAM reads are in flight;
+// a slot is free again as soon as the converters have read it), x-plane tiles (freed by the
+// MMA) and TMEM A stages (freed by the MMA).
+//
+// Warps: 0 W producer, 1 MMA issuer, 2 x producer, 3..10 converters in two groups of four (one
+// warp per TMEM lane quarter in each group) taking alternate stages, then all eight run the
+// epilogue.
+constexpr int kTmThreads = 352;
+constexpr uint32_t kTmemCols = 512;
+constexpr int kTmAccMax = 384;
+
+struct TmParams {
+  const uint8_t* Wg;           // GEMM mirror: [rows/128][nkb_total][128][kbb]
+  int rows, cols, M, xsplit;
+  int TB;                      // tokens per CTA block (multiple of 16, <= 256)
+  int tpass[3];                // tokens per pass for 1, 2, 3 planes
+  int nkb_total, kb_per_split, splits;
+  int kbb;                     // packed bytes per row per stage (FP4 32, 8-bit 64)
+  uint32_t x_bytes, w_bytes;    // one x-ring slot (P x T x 128 B at most), one W-ring slot (128 x kbb)
+  uint32_t a_col;              // first A stage column (after the accumulators)
+  int nacc[3];                 // independent accumulators for 1, 2, 3 planes
+  int sx, sw;                  // stages (x slot + TMEM A slot each) and W-ring slots
+  int w_evict_first;           // 1 when no other CTA reads this CTA's weight rows
+  const float* scale_inv;      // [Mp]
+  const int* pcnt;             // [Mp] planes needed per token
+  float w_scale;
+  float* pre;
+  float* post;
+  int64_t ld_out;
+  const double* bias;
+  int bias_len;
+  int act;
+  double* partial;             // [splits][M][rows] when splits > 1
+  int* err;
+};
+
+__device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* tm, int x, int y, int z,
+                                                 uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)),
+        "l"(policy)
+      : "memory");
+}
+
+// Contiguous global -> shared copy (16-byte aligned, size a multiple of 16), no tensor map.
+__device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                               uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16, fp32 accumulate.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                           uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+      ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+        "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+        "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+// One row's 64 codes of a stage -> 32 f16x2 words (k ascending, low half = even k).
+// `tile` is the stage's raw tile, row r at r * kbb with the TMA swizzle applied.
+template <int kDt>
+__device__ __forceinline__ void convert_row(const uint8_t* tile, int r, uint32_t (&v)[32]) {
+  if constexpr (kDt == 16) {
+    // 32-byte rows, SWIZZLE_32B: 16-byte chunk j sits at j ^ ((r >> 2) & 1)
+    const int sw = (r >> 2) & 1;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint4 c = *reinterpret_cast<const uint4*>(tile + r * 32 + ((j ^ sw) << 4));
+      const uint32_t w4[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+            "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+            "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+            "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+            "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+            "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+            : "=r"(v[j * 16 + q * 4 + 0]), "=r"(v[j * 16 + q * 4 + 1]), "=r"(v[j * 16 + q * 4 + 2]),
+              "=r"(v[j * 16 + q * 4 + 3])
+            : "r"(w4[q]));
+      }
+    }
+  } else {
+    // 64-byte rows, SWIZZLE_64B: 16-byte chunk j sits at j ^ ((r >> 1) & 3)
+    const int sw = (r >> 1) & 3;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 c = *reinterpret_cast<const uint4*>(tile + r * 64 + ((j ^ sw) << 4));
+      const uint32_t w4[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t* o = &v[j * 8 + q * 2];
+        if constexpr (kDt == 4) {
+          asm("{\n\t.reg .b16 l, h;\n\t"
+              "mov.b32 {l, h}, %2;\n\t"
+              "cvt.rn.f16x2.e4m3x2 %0, l;\n\t"
+              "cvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+              : "=r"(o[0]), "=r"(o[1])
+              : "r"(w4[q]));
+        } else if constexpr (kDt == 5) {
+          asm("{\n\t.reg .b16 l, h;\n\t"
+              "mov.b32 {l, h}, %2;\n\t"
+              "cvt.rn.f16x2.e5m2x2 %0, l;\n\t"
+              "cvt.rn.f16x2.e5m2x2 %1, h;\n\t}"
+              : "=r"(o[0]), "=r"(o[1])
+              : "r"(w4[q]));
+        } else {  // Int8: f16 bits 0x6400 | (q ^ 0x80) = 1152 + q, minus 1152 -> q exactly
+          const uint32_t u = w4[q] ^ 0x80808080u;
+          const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+          uint32_t p0 = __byte_perm(u, 0x64646464u, 0x4140), p1 = __byte_perm(u, 0x64646464u, 0x4342);
+          __half2 h0 = __hsub2(*reinterpret_cast<__half2*>(&p0), bias);
+          __half2 h1 = __hsub2(*reinterpret_cast<__half2*>(&p1), bias);
+          o[0] = *reinterpret_cast<uint32_t*>(&h0);
+          o[1] = *reinterpret_cast<uint32_t*>(&h1);
+        }
+      }
+    }
+  }
+}
+
+// Lane 0 of the warp waits (bounded), the rest of the warp waits at __syncwarp: a few
+// threads polling an mbarrier instead of whole warps.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, err, code);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
+template <int kDt>
+__global__ void __launch_bounds__(kTmThreads, 1)
+    k_gemm_tm(const __grid_constant__ CUtensorMap tm_x1, const __grid_constant__ CUtensorMap tm_x2,
+              const __grid_constant__ CUtensorMap tm_x3, const TmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = p.sx, Sw = p.sw;
+  uint8_t* xring = smem;                                   // S x p.x_bytes
+  uint8_t* wring = smem + S * p.x_bytes;                   // Sw x p.w_bytes
+  uint64_t* bars = reinterpret_cast<uint64_t*>(wring + Sw * p.w_bytes);
+  uint64_t* w_full = bars;                 // W producer -> converters (tx)
+  uint64_t* w_empty = w_full + Sw;         // converter warps (4) -> W producer
+  uint64_t* s_full = w_empty + Sw;         // x producer (1 + tx) and converter warps (4) -> MMA
+  uint64_t* s_free = s_full + S;           // MMA commit -> x producer and converters
+  uint64_t* acc_full = s_free + S;         // MMA commit -> epilogue
+  uint64_t* acc_empty = acc_full + 1;      // epilogue warps (8) -> MMA
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  int* s_planes = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int t_begin = blockIdx.x * p.TB;   // token block varies fastest: CTAs sharing weight rows run together
+  const int tile_m = blockIdx.y;
+  const int split = blockIdx.z;
+  const int kb0 = split * p.kb_per_split;
+  int nkb = p.nkb_total - kb0;
+  if (nkb > p.kb_per_split) nkb = p.kb_per_split;
+  int t_count = p.M - t_begin;
+  if (t_count > p.TB) t_count = p.TB;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Sw; ++s) {
+      mbar_init(&w_full[s], 1);
+      mbar_init(&w_empty[s], 4);
+    }
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&s_full[s], 5);
+      mbar_init(&s_free[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 8);
+    *s_planes = 1;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  {
+    int mp = 1;
+    for (int i = threadIdx.x; i < t_count; i += kTmThreads) mp = max(mp, p.pcnt[t_begin + i]);
+    if (mp > 1) atomicMax(s_planes, mp);
+  }
+  __syncthreads();
+  const uint32_t tmem = *tmem_slot;
+  const int P = min(*s_planes, p.xsplit);
+  const int T = p.tpass[P - 1];
+  const int npass = (t_count + T - 1) / T;
+  const int ntot = P * T;                  // B rows = columns of one accumulator
+  const int n0 = ntot < 256 ? ntot : 256;  // first MMA's N; the second covers [n0, ntot)
+  const int nacc = p.nacc[P - 1];          // independent accumulators (k steps round robin)
+  const int iters = npass * nkb;
+
+  // Loops keep their ring slots and phase bits as running state (Ring): no divisions on the
+  // single-thread critical paths.
+  if (warp == 0) {
+    // ------------------------------------------------------------------ W producer
+    if (lane == 0) {
+      uint64_t pol;
+      if (p.w_evict_first)
+        asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+      else
+        asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
+      const uint32_t wb = p.w_bytes;
+      const uint8_t* wfirst = p.Wg + (static_cast<int64_t>(tile_m) * p.nkb_total + kb0) * wb;
+      Ring w;
+      int i = 0, issued = 0;
+      for (int it = 0; it < iters; ++it) {
+        if (!mbar_wait(&w_empty[w.slot], w.phase ^ 1u, p.err, 11)) break;
+        mbar_expect_tx(&w_full[w.slot], wb);
+        bulk_load_hint(wring + w.slot * wb, wfirst + static_cast<int64_t>(i) * wb, wb, &w_full[w.slot], pol);
+        ++issued;
+        w.step(Sw);
+        if (++i == nkb) i = 0;
+      }
+      // tail: the converters released every slot this thread filled before the CTA exits
+      Ring t;
+      for (int it = 0; it < issued; ++it) {
+        if (it >= issued - Sw) mbar_wait(&w_empty[t.slot], t.phase, p.err, 12);
+        t.step(Sw);
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ x producer
+    if (lane == 0) {
+      uint64_t pol;
+      asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+      const CUtensorMap* tmx = P == 1 ? &tm_x1 : (P == 2 ? &tm_x2 : &tm_x3);
+      const uint32_t tx = static_cast<uint32_t>(ntot * 128);
+      Ring r;
+      int issued = 0;
+      bool ok = true;
+      for (int pass = 0; pass < npass && ok; ++pass) {
+        const int t0 = t_begin + pass * T;
+        for (int i = 0; i < nkb; ++i) {
+          if (!mbar_wait(&s_free[r.slot], r.phase ^ 1u, p.err, 18)) { ok = false; break; }
+          mbar_expect_tx(&s_full[r.slot], tx);
+          uint8_t* dst = xring + r.slot * p.x_bytes;
+          for (int q = 0; q < P; ++q) tma_load_3d_hint(dst + q * T * 128, tmx, (kb0 + i) * kBK, t0, q, &s_full[r.slot], pol);
+          ++issued;
+          r.step(S);
+        }
+      }
+      // tail: the MMA consumed every stage this thread filled before the CTA exits
+      Ring t;
+      for (int it = 0; it < issued; ++it) {
+        if (it >= issued - S) mbar_wait(&s_free[t.slot], t.phase, p.err, 19);
+        t.step(S);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc0 =
+          (1u << 4) | (static_cast<uint32_t>(n0 >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
+      const uint32_t idesc1 =
+          (1u << 4) | (static_cast<uint32_t>((ntot - n0) >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
+      const uint64_t bd_base = desc_sw128(smem_u32(xring));
+      const uint64_t bd_step = static_cast<uint64_t>(p.x_bytes >> 4);   // one x slot, in 16-byte units
+      const uint64_t bd_n0 = static_cast<uint64_t>((n0 * 128) >> 4);     // rows [n0, ntot) of a slot
+      Ring r;
+      Ring last;
+      bool any = false;
+      bool ok = true;
+      for (int pass = 0; pass < npass && ok; ++pass) {
+        if (pass > 0) {
+          if (!mbar_wait(acc_empty, static_cast<uint32_t>(pass - 1) & 1u, p.err, 13)) break;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        }
+        int j = 0;       // accumulator of the next k step (round robin over nacc)
+        int first = 0;   // k steps issued this pass (each accumulator starts fresh on its first)
+        for (int i = 0; i < nkb; ++i) {
+          if (!mbar_wait(&s_full[r.slot], r.phase, p.err, 14)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint64_t bd = bd_base + bd_step * static_cast<uint64_t>(r.slot);
+          const uint32_t a = tmem + p.a_col + 32u * static_cast<uint32_t>(r.slot);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {  // 16 k per MMA: 8 TMEM columns of A, 32 bytes of B
+            const uint32_t d = tmem + static_cast<uint32_t>(j * ntot);
+            const uint32_t acc = first >= nacc ? 1u : 0u;
+            mma_f16_ts(d, a + 8u * k, bd + 2 * k, idesc0, acc);
+            if (ntot > n0) mma_f16_ts(d + static_cast<uint32_t>(n0), a + 8u * k, bd + bd_n0 + 2 * k, idesc1, acc);
+            if (++j == nacc) j = 0;
+            ++first;
+          }
+          mma_commit(&s_free[r.slot]);
+          last = r;
+          any = true;
+          r.step(S);
+        }
+        if (ok) mma_commit(acc_full);
+      }
+      // drain: the last MMAs issued have completed before TMEM can be released
+      if (any) mbar_wait(&s_free[last.slot], last.phase, p.err, 15);
+    }
+  } else if (warp >= 3) {
+    // ------------------------------------------------------------------ converters, then epilogue
+    const int cw = warp - 3;             // 0..7
+    const int grp = cw >> 2;             // converter group: takes the iterations with it % 2 == grp
+    const int q = warp & 3;              // TMEM lane quarter of this warp
+    const int r = q * 32 + lane;         // weight row within the tile = TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const int o = tile_m * 128 + r;
+    Ring w, st;
+    int it = 0;
+    bool ok = true;
+    for (int pass = 0; pass < npass && ok; ++pass) {
+      for (int i = 0; i < nkb; ++i, ++it, w.step(Sw), st.step(S)) {
+        if ((it & 1) != grp) continue;
+        if (!warp_wait(&w_full[w.slot], w.phase, p.err, 16)) { ok = false; break; }
+        uint32_t v[32];
+        convert_row<kDt>(wring + w.slot * p.w_bytes, r, v);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&w_empty[w.slot]);
+        if (!warp_wait(&s_free[st.slot], st.phase ^ 1u, p.err, 21)) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        tmem_st32(tmem + lane_base + p.a_col + 32u * static_cast<uint32_t>(st.slot), v);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_full[st.slot]);
+      }
+      if (!ok) break;
+      // ------------------------------------------------------------ epilogue of this pass
+      if (!warp_wait(acc_full, static_cast<uint32_t>(pass) & 1u, p.err, 17)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int t_pass = t_begin + pass * T;
+      for (int tc = grp * 16; tc < T; tc += 32) {
+        double y[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) y[e] = 0.0;
+        for (int pl = 0; pl < P; ++pl) {
+          for (int jj = 0; jj < nacc; ++jj) {
+            uint32_t v[16];
+            tmem_ld16(tmem + lane_base + static_cast<uint32_t>(jj * ntot + pl * T + tc), v);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+            for (int e = 0; e < 16; ++e) y[e] += static_cast<double>(__uint_as_float(v[e]));
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int t = t_pass + tc + e;
+          if (t >= t_begin + t_count || o >= p.rows) continue;
+          double yy = y[e] * static_cast<double>(p.scale_inv[t]);
+          if (kDt == 9) yy *= static_cast<double>(p.w_scale);
+          if (p.splits > 1) {
+            p.partial[(static_cast<int64_t>(split) * p.M + t) * p.rows + o] = yy;
+          } else {
+            write_out(p, t, o, yy);
+          }
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
 // Sum of the split-K partials in a fixed order, then the reference epilogue.
 __global__ void k_splitk_reduce(const KParams p) {
   const int64_t n = static_cast<int64_t>(p.M) * p.rows;
@@ -360,22 +798,34 @@ __global__ void k_splitk_reduce(const KParams p) {
   }
 }
 
-// x [M][x_ld] f32 -> planes [xsplit][Mp][Kp] f16 (x * 2^e = p0 + p1 + p2) and 2^-e per token.
-// One warp per token row; rows >= M and columns >= K are zero.
-__global__ void k_split_x(const float* __restrict__ x, int64_t x_ld, int M, int K, int Mp, int Kp, int xsplit,
-                          __half* __restrict__ planes, float* __restrict__ scale_inv) {
-  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
+// x [M][x_ld] f32 -> planes [xsplit][Mp][Kp] f16 (x * 2^e = p0 + p1 + p2) and 2^-e per token;
+// pcnt[t] (when given) = planes that hold a non-zero value for token t, at most xsplit.
+// One 256-thread block per token row (grid = Mp); rows >= M and columns >= K are zero.
+constexpr int kSplitThreads = 256;
+__global__ void __launch_bounds__(kSplitThreads)
+    k_split_x(const float* __restrict__ x, int64_t x_ld, int M, int K, int Mp, int Kp, int xsplit,
+              __half* __restrict__ planes, float* __restrict__ scale_inv, int* __restrict__ pcnt) {
+  __shared__ float s_max[kSplitThreads / 32];
+  __shared__ int s_nz;
+  const int t = blockIdx.x;
   if (t >= Mp) return;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* xr = x + static_cast<int64_t>(t) * x_ld;
+  const bool live = t < M;
   float amax = 0.0f;
-  if (t < M)
-    for (int k = lane; k < K; k += 32) {
+  if (live)
+    for (int k = tid; k < K; k += kSplitThreads) {
       const float a = fabsf(xr[k]);
       if (a > amax && a <= 3.402823466e+38f) amax = a;
     }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  if (lane == 0) s_max[warp] = amax;
+  if (tid == 0) s_nz = 0;
+  __syncthreads();
+  amax = s_max[0];
+#pragma unroll
+  for (int w = 1; w < kSplitThreads / 32; ++w) amax = fmaxf(amax, s_max[w]);
   int e = 0;
   if (amax > 0.0f) {
     e = 13 - ilogbf(amax);  // amax * 2^e in [2^13, 2^14)
@@ -383,11 +833,12 @@ __global__ void k_split_x(const float* __restrict__ x, int64_t x_ld, int M, int 
     if (e < -126) e = -126;
   }
   const float s = ldexpf(1.0f, e);
-  if (lane == 0) scale_inv[t] = ldexpf(1.0f, -e);
+  if (tid == 0) scale_inv[t] = ldexpf(1.0f, -e);
   const int64_t plane = static_cast<int64_t>(Mp) * Kp;
   __half* p0 = planes + static_cast<int64_t>(t) * Kp;
-  for (int k = lane; k < Kp; k += 32) {
-    const float v = (t < M && k < K) ? xr[k] : 0.0f;
+  bool nz1 = false, nz2 = false;
+  for (int k = tid; k < Kp; k += kSplitThreads) {
+    const float v = (live && k < K) ? xr[k] : 0.0f;
     __half h0, h1 = __float2half_rn(0.0f), h2 = __float2half_rn(0.0f);
     if (isfinite(v)) {
       const float vs = v * s;
@@ -402,6 +853,18 @@ __global__ void k_split_x(const float* __restrict__ x, int64_t x_ld, int M, int 
     p0[k] = h0;
     if (xsplit > 1) p0[plane + k] = h1;
     if (xsplit > 2) p0[2 * plane + k] = h2;
+    nz1 |= (__half_as_ushort(h1) & 0x7fff) != 0;
+    nz2 |= (__half_as_ushort(h2) & 0x7fff) != 0;
+  }
+  if (pcnt) {
+    const int f = (nz1 ? 1 : 0) | (nz2 ? 2 : 0);
+    if (f) atomicOr(&s_nz, f);
+    __syncthreads();
+    if (tid == 0) {
+      int n = (s_nz & 2) ? 3 : ((s_nz & 1) ? 2 : 1);
+      if (n > xsplit) n = xsplit;
+      pcnt[t] = n;
+    }
   }
 }
 
@@ -429,6 +892,22 @@ Status make_map_2d(CUtensorMap* tm, CUtensorMapDataType dt, void* base, uint64_t
   CUresult r = enc(tm, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return Status::Internal("cuTensorMapEncodeTiled failed: " + std::to_string(static_cast<int>(r)));
+  return Status::Ok();
+}
+
+// [planes][Mp][Kp] f16 planes of x: box {64 k, T tokens, 1 plane}, SWIZZLE_128B; tokens past
+// Mp read as zero.
+Status make_map_planes(CUtensorMap* tm, void* base, uint64_t Kp, uint64_t Mp, uint64_t planes, uint32_t T) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return Status::Internal("cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {Kp, Mp, planes};
+  cuuint64_t strides[2] = {Kp * 2, Kp * Mp * 2};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(kBK), T, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return Status::Internal("cuTensorMapEncodeTiled (planes) failed: " + std::to_string(static_cast<int>(r)));
   return Status::Ok();
 }
 
@@ -471,7 +950,135 @@ Plan make_plan(int M, int cols, int rows, int xsplit, DType dt) {
   return pl;
 }
 
+struct TmPlan {
+  int TB, tpass[3], nacc[3], Mp, Kp, nkb, splits, kb_per_split, kbb, acc_cols;
+  int sx, sw;
+  uint32_t x_bytes, w_bytes, a_col;
+  size_t smem;
+  size_t planes_bytes, scale_bytes, pcnt_bytes, partial_bytes;
+};
+
+// Split-K count for `tiles` CTAs of `nkb` k-blocks: the one (1..16) that makes the last wave
+// over 148 SMs fullest, as long as the fp64 partials it writes and reads stay under a
+// quarter of the weight bytes.
+int tm_splits(int tiles, int nkb, int M, int rows, double weight_bytes) {
+  if (tiles >= 148) return 1;
+  int best = 1;
+  double best_eff = 0.0;
+  for (int s = 1; s <= 16 && s <= nkb / 2; ++s) {
+    if (s > 1 && 16.0 * s * M * static_cast<double>(rows) > 0.25 * weight_bytes) break;
+    const int ctas = tiles * s;
+    const int waves = (ctas + 147) / 148;
+    const double eff = static_cast<double>(ctas) / (waves * 148.0);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
+}
+
+TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt) {
+  TmPlan pl{};
+  const int m16 = static_cast<int>(round_up(M, 16));
+  pl.TB = m16 < 256 ? m16 : 256;
+  pl.acc_cols = 0;
+  int xrows = 0;
+  for (int P = 1; P <= 3; ++P) {
+    const int cap = (kTmAccMax / P) & ~15;  // 384, 192, 128
+    pl.tpass[P - 1] = pl.TB < cap ? pl.TB : cap;
+    const int ntot = P * pl.tpass[P - 1];
+    // independent accumulators so that short MMAs do not wait on each other's results
+    pl.nacc[P - 1] = ntot <= 64 ? 4 : (ntot <= 128 ? 2 : 1);
+    if (P <= xsplit) {
+      pl.acc_cols = std::max(pl.acc_cols, pl.nacc[P - 1] * ntot);
+      xrows = std::max(xrows, ntot);
+    }
+  }
+  pl.Mp = m16;
+  pl.Kp = static_cast<int>(round_up(cols, kBK));
+  pl.nkb = pl.Kp / kBK;
+  pl.kbb = dt == DType::FP4 ? kBK / 2 : kBK;
+  pl.x_bytes = static_cast<uint32_t>(round_up(static_cast<int64_t>(xrows) * 128, 1024));
+  pl.w_bytes = static_cast<uint32_t>(kBM * pl.kbb);
+  pl.a_col = static_cast<uint32_t>(round_up(pl.acc_cols, 32));
+  // stages (an x slot + a TMEM A slot each): as many as TMEM and shared memory allow, up to 8,
+  // keeping room for 8 W slots; then the W ring takes the rest (up to 32). 1 KB aligns the
+  // base, 1 KB holds the barriers (at most 2*32 + 2*8 + 2 of them).
+  const int64_t budget = 227 * 1024 - 2048;
+  pl.sx = (static_cast<int>(kTmemCols) - static_cast<int>(pl.a_col)) / 32;
+  if (pl.sx > 8) pl.sx = 8;
+  while (pl.sx > 2 && pl.sx * static_cast<int64_t>(pl.x_bytes) + 8 * static_cast<int64_t>(pl.w_bytes) > budget)
+    --pl.sx;
+  pl.sw = static_cast<int>((budget - pl.sx * static_cast<int64_t>(pl.x_bytes)) / pl.w_bytes);
+  if (pl.sw > 32) pl.sw = 32;
+  pl.smem = static_cast<size_t>(pl.sx) * pl.x_bytes + static_cast<size_t>(pl.sw) * pl.w_bytes + 2048;
+  // At least half the SM's shared memory, so that one CTA (and its 512 TMEM columns) runs per
+  // SM: a second CTA on the SM would only stall in tcgen05.alloc.
+  if (pl.smem < 116 * 1024) pl.smem = 116 * 1024;
+  const int tiles = static_cast<int>(((rows + kBM - 1) / kBM) * static_cast<int64_t>((M + pl.TB - 1) / pl.TB));
+  const double wbytes = static_cast<double>(rows) * pl.Kp * (dt == DType::FP4 ? 0.5 : 1.0);
+  const int splits = tm_splits(tiles, pl.nkb, M, rows, wbytes);
+  pl.kb_per_split = (pl.nkb + splits - 1) / splits;
+  pl.splits = (pl.nkb + pl.kb_per_split - 1) / pl.kb_per_split;
+  pl.planes_bytes = static_cast<size_t>(round_up(static_cast<int64_t>(xsplit) * pl.Mp * pl.Kp * 2, 1024));
+  pl.scale_bytes = static_cast<size_t>(round_up(static_cast<int64_t>(pl.Mp) * 4, 1024));
+  pl.pcnt_bytes = pl.scale_bytes;
+  pl.partial_bytes = pl.splits > 1 ? static_cast<size_t>(pl.splits) * M * rows * 8 : 0;
+  return pl;
+}
+
+// Which batched kernel runs: A in TMEM (default) or A in shared memory
+// (WELVET_B200_GEMM=smem, kept for comparison).
+bool gemm_a_in_smem() {
+  const char* e = std::getenv("WELVET_B200_GEMM");
+  return e && std::strcmp(e, "smem") == 0;
+}
+
 } // namespace
+
+namespace {
+// One thread per 16-byte chunk of the GEMM mirror; see build_gemm_mirror.
+__global__ void k_build_gemm_mirror(const uint8_t* __restrict__ W, int64_t row_stride, int rows, int nkb, int kbb,
+                                    int64_t nchunks, uint8_t* __restrict__ Wg) {
+  const int cpr = kbb >> 4;  // chunks per row per stage
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nchunks;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int j = static_cast<int>(i % cpr);
+    int64_t rest = i / cpr;
+    const int r = static_cast<int>(rest % 128);
+    rest /= 128;
+    const int kb = static_cast<int>(rest % nkb);
+    const int64_t tile = rest / nkb;
+    const int64_t row = tile * 128 + r;
+    const int64_t src = static_cast<int64_t>(kb) * kbb + j * 16;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (row < rows && src + 16 <= row_stride) v = *reinterpret_cast<const uint4*>(W + row * row_stride + src);
+    const int sw = kbb == 32 ? ((r >> 2) & 1) : ((r >> 1) & 3);
+    *reinterpret_cast<uint4*>(Wg + ((tile * nkb + kb) * 128 + r) * kbb + ((j ^ sw) << 4)) = v;
+  }
+}
+} // namespace
+
+size_t gemm_mirror_bytes(DType dt, int rows, int cols) {
+  const int64_t tiles = (rows + kBM - 1) / kBM;
+  const int64_t nkb = (cols + kBK - 1) / kBK;
+  const int64_t kbb = dt == DType::FP4 ? kBK / 2 : kBK;
+  return static_cast<size_t>(tiles * nkb * kBM * kbb);
+}
+
+Status build_gemm_mirror(DType dt, const uint8_t* W, int rows, int64_t row_stride, int cols, uint8_t* Wg,
+                         cudaStream_t st) {
+  if (!gemm_supported(dt)) return Status::Unsupported("gemm mirror: dtype");
+  if (!W || !Wg || row_stride % 16 != 0) return Status::Internal("gemm mirror: bad arguments");
+  const int nkb = (cols + kBK - 1) / kBK;
+  const int kbb = dt == DType::FP4 ? kBK / 2 : kBK;
+  const int64_t nchunks = static_cast<int64_t>(gemm_mirror_bytes(dt, rows, cols) / 16);
+  int64_t blocks = (nchunks + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  k_build_gemm_mirror<<<static_cast<unsigned>(blocks), 256, 0, st>>>(W, row_stride, rows, nkb, kbb, nchunks, Wg);
+  return cuda_status(cudaGetLastError(), "gemm mirror build");
+}
 
 bool gemm_supported(DType dt) {
   return dt == DType::FP4 || dt == DType::FP8E4M3 || dt == DType::FP8E5M2 || dt == DType::Int8;
@@ -485,17 +1092,108 @@ int gemm_token_tile(int M, int xsplit) {
 }
 
 size_t gemm_scratch_bytes(int M, int cols, int rows, int xsplit) {
-  const Plan pl = make_plan(M, cols, rows, xsplit, DType::FP8E4M3);
-  const Plan p4 = make_plan(M, cols, rows, xsplit, DType::FP4);
-  const size_t a = pl.planes_bytes + pl.scale_bytes + pl.partial_bytes;
-  const size_t b = p4.planes_bytes + p4.scale_bytes + p4.partial_bytes;
-  return a > b ? a : b;
+  size_t need = 0;
+  for (DType dt : {DType::FP8E4M3, DType::FP4}) {
+    const Plan pl = make_plan(M, cols, rows, xsplit, dt);
+    const TmPlan tp = make_tm_plan(M, cols, rows, xsplit, dt);
+    need = std::max(need, pl.planes_bytes + pl.scale_bytes + pl.partial_bytes);
+    need = std::max(need, tp.planes_bytes + tp.scale_bytes + tp.pcnt_bytes + tp.partial_bytes);
+  }
+  return need;
 }
 
-Status launch_gemm_tc(const GemmArgs& a, cudaStream_t st) {
-  if (!gemm_supported(a.dtype)) return Status::Unsupported("gemm_tc: dtype");
-  if (a.M <= 0 || a.rows <= 0 || a.cols <= 0) return Status::Invalid("gemm_tc: bad dims");
-  if (a.xsplit < 1 || a.xsplit > 3) return Status::Invalid("gemm_tc: xsplit must be 1..3");
+namespace {
+
+// cudaFuncSetAttribute is a driver call on every use; do it once per kernel, device and size.
+Status set_max_smem(const void* kern, size_t bytes) {
+  static std::mutex mu;
+  static std::vector<std::tuple<const void*, int, size_t>> done;
+  int dev = 0;
+  WB_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& d : done)
+    if (std::get<0>(d) == kern && std::get<1>(d) == dev && std::get<2>(d) >= bytes) return Status::Ok();
+  WB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)));
+  for (auto& d : done)
+    if (std::get<0>(d) == kern && std::get<1>(d) == dev) {
+      std::get<2>(d) = bytes;
+      return Status::Ok();
+    }
+  done.emplace_back(kern, dev, bytes);
+  return Status::Ok();
+}
+
+Status launch_tm(const GemmArgs& a, cudaStream_t st) {
+  if (!a.Wg || (reinterpret_cast<uintptr_t>(a.Wg) & 15) != 0)
+    return Status::Internal("gemm_tc: the layer has no GEMM mirror (16-byte aligned)");
+  const TmPlan pl = make_tm_plan(a.M, a.cols, a.rows, a.xsplit, a.dtype);
+  if (pl.sw < 2 || pl.sx < 2 || pl.a_col + 32u * pl.sx > kTmemCols)
+    return Status::Internal("gemm_tc: pipeline does not fit on the SM");
+  const size_t need = pl.planes_bytes + pl.scale_bytes + pl.pcnt_bytes + pl.partial_bytes;
+  if (!a.scratch || a.scratch_bytes < need) return Status::Internal("gemm_tc: scratch too small");
+  uint8_t* scr = static_cast<uint8_t*>(a.scratch);
+  __half* planes = reinterpret_cast<__half*>(scr);
+  float* scale_inv = reinterpret_cast<float*>(scr + pl.planes_bytes);
+  int* pcnt = reinterpret_cast<int*>(scr + pl.planes_bytes + pl.scale_bytes);
+  double* partial =
+      pl.splits > 1 ? reinterpret_cast<double*>(scr + pl.planes_bytes + pl.scale_bytes + pl.pcnt_bytes) : nullptr;
+
+  k_split_x<<<pl.Mp, kSplitThreads, 0, st>>>(a.x, a.x_ld, a.M, a.cols, pl.Mp, pl.Kp, a.xsplit, planes, scale_inv,
+                                             pcnt);
+  WB_CUDA(cudaGetLastError());
+
+  CUtensorMap tm_x[3];
+  for (int P = 1; P <= 3; ++P) {
+    const int q = P <= a.xsplit ? P : 1;  // maps for plane counts above xsplit are never used
+    WB_TRY(make_map_planes(&tm_x[P - 1], planes, static_cast<uint64_t>(pl.Kp), static_cast<uint64_t>(pl.Mp),
+                           static_cast<uint64_t>(a.xsplit), static_cast<uint32_t>(pl.tpass[q - 1])));
+  }
+
+  TmParams p{};
+  p.Wg = a.Wg;
+  p.rows = a.rows; p.cols = a.cols; p.M = a.M; p.xsplit = a.xsplit;
+  p.TB = pl.TB;
+  for (int i = 0; i < 3; ++i) p.tpass[i] = pl.tpass[i];
+  p.nkb_total = pl.nkb; p.kb_per_split = pl.kb_per_split; p.splits = pl.splits; p.kbb = pl.kbb;
+  p.x_bytes = pl.x_bytes; p.w_bytes = pl.w_bytes; p.a_col = pl.a_col;
+  p.sx = pl.sx; p.sw = pl.sw;
+  for (int i = 0; i < 3; ++i) p.nacc[i] = pl.nacc[i];
+  p.w_evict_first = (a.M + pl.TB - 1) / pl.TB == 1 ? 1 : 0;
+  p.scale_inv = scale_inv; p.pcnt = pcnt; p.w_scale = a.scale;
+  p.pre = a.pre; p.post = a.post; p.ld_out = a.ld_out;
+  p.bias = a.bias; p.bias_len = a.bias_len; p.act = a.act;
+  p.partial = partial; p.err = a.err;
+
+  const size_t smem = pl.smem;
+  dim3 grid(static_cast<unsigned>((a.M + pl.TB - 1) / pl.TB), static_cast<unsigned>((a.rows + kBM - 1) / kBM),
+            static_cast<unsigned>(pl.splits));
+  if (grid.y > 65535) return Status::Invalid("gemm_tc: too many weight rows for one launch");
+  auto launch = [&](auto kern) -> Status {
+    WB_TRY(set_max_smem(reinterpret_cast<const void*>(kern), smem));
+    kern<<<grid, kTmThreads, smem, st>>>(tm_x[0], tm_x[1], tm_x[2], p);
+    return cuda_status(cudaGetLastError(), "gemm_tc (tmem) launch");
+  };
+  switch (a.dtype) {
+  case DType::FP4: WB_TRY(launch(k_gemm_tm<16>)); break;
+  case DType::FP8E4M3: WB_TRY(launch(k_gemm_tm<4>)); break;
+  case DType::FP8E5M2: WB_TRY(launch(k_gemm_tm<5>)); break;
+  case DType::Int8: WB_TRY(launch(k_gemm_tm<9>)); break;
+  default: return Status::Unsupported("gemm_tc: dtype");
+  }
+  if (pl.splits > 1) {
+    KParams r{};
+    r.rows = a.rows; r.M = a.M; r.splits = pl.splits; r.partial = partial;
+    r.pre = a.pre; r.post = a.post; r.ld_out = a.ld_out; r.bias = a.bias; r.bias_len = a.bias_len; r.act = a.act;
+    const int64_t n = static_cast<int64_t>(a.M) * a.rows;
+    int blocks = static_cast<int>((n + 255) / 256);
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    k_splitk_reduce<<<blocks, 256, 0, st>>>(r);
+    WB_CUDA(cudaGetLastError());
+  }
+  return Status::Ok();
+}
+
+Status launch_smem(const GemmArgs& a, cudaStream_t st) {
   const Plan pl = make_plan(a.M, a.cols, a.rows, a.xsplit, a.dtype);
   if (pl.stages < 2) return Status::Internal("gemm_tc: stage does not fit in shared memory");
   const size_t need = pl.planes_bytes + pl.scale_bytes + pl.partial_bytes;
@@ -507,7 +1205,8 @@ Status launch_gemm_tc(const GemmArgs& a, cudaStream_t st) {
 
   {
     const int warps = pl.Mp;
-    k_split_x<<<(warps + 7) / 8, 256, 0, st>>>(a.x, a.x_ld, a.M, a.cols, pl.Mp, pl.Kp, a.xsplit, planes, scale_inv);
+    k_split_x<<<warps, kSplitThreads, 0, st>>>(a.x, a.x_ld, a.M, a.cols, pl.Mp, pl.Kp, a.xsplit, planes, scale_inv,
+                                               nullptr);
     WB_CUDA(cudaGetLastError());
   }
 
@@ -558,6 +1257,15 @@ Status launch_gemm_tc(const GemmArgs& a, cudaStream_t st) {
     WB_CUDA(cudaGetLastError());
   }
   return Status::Ok();
+}
+
+} // namespace
+
+Status launch_gemm_tc(const GemmArgs& a, cudaStream_t st) {
+  if (!gemm_supported(a.dtype)) return Status::Unsupported("gemm_tc: dtype");
+  if (a.M <= 0 || a.rows <= 0 || a.cols <= 0) return Status::Invalid("gemm_tc: bad dims");
+  if (a.xsplit < 1 || a.xsplit > 3) return Status::Invalid("gemm_tc: xsplit must be 1..3");
+  return gemm_a_in_smem() ? launch_smem(a, st) : launch_tm(a, st);
 }
 
 // ---------------------------------------------------------------------------------------

@@ -16,6 +16,7 @@ namespace wb {
 struct GemmArgs {
   DType dtype = DType::FP4;
   const uint8_t* W = nullptr;   // mirror [rows][row_stride]
+  const uint8_t* Wg = nullptr;  // GEMM mirror (build_gemm_mirror); required by the default kernel
   int64_t row_stride = 0;
   int rows = 0;                 // out
   int cols = 0;                 // in (K)
@@ -42,6 +43,15 @@ int gemm_token_tile(int M, int xsplit);
 size_t gemm_scratch_bytes(int M, int cols, int rows, int xsplit);
 
 bool gemm_supported(DType dt);
+
+// The GEMM mirror: the row-major mirror cut into tiles of 128 rows x 64 k, each stored as one
+// contiguous block ([rows/128][K/64][128][bytes of 64 codes]) so that a pipeline stage is
+// one bulk copy, with the 16-byte chunks of row r at chunk ^ swizzle(r) (the 32-byte
+// swizzle for FP4 rows, 64-byte for 8-bit rows) so that one thread per row reads shared
+// memory without bank conflicts. Rows and k past the layer are zero.
+size_t gemm_mirror_bytes(DType dt, int rows, int cols);
+Status build_gemm_mirror(DType dt, const uint8_t* W, int rows, int64_t row_stride, int cols, uint8_t* Wg,
+                         cudaStream_t st);
 
 Status launch_gemm_tc(const GemmArgs& a, cudaStream_t st);
 

@@ -190,7 +190,8 @@ welvet_status welvet_b200_volume_forward_f32(welvet_b200_volume* h, int32_t rows
     WB_CUDA(cudaMemcpyAsync(xb.p, x_host, xbytes, cudaMemcpyHostToDevice, v->stream));
     int ow = 0;
     WB_TRY(wb::volume_forward_device(v, rows, static_cast<float*>(xb.p), in_width, 0, -1, nullptr, &ow, v->stream));
-    if (static_cast<size_t>(ow) > out_cap) return wb::Status::Invalid("runtime.forward: output buffer too small");
+    if (static_cast<size_t>(ow) * static_cast<size_t>(rows) > out_cap)
+      return wb::Status::Invalid("runtime.forward: output buffer too small");
     // the last executed cell's post is the output (src/runtime/forward.cpp:153)
     int last = -1;
     for (int i = wb::volume_hops(*v) - 1; i >= 0 && last < 0; --i)

@@ -122,13 +122,15 @@ class Volume:
         return ow.value
 
     def forward_f32(self, x, out_width_cap: int):
+        """Host x [rows][in] -> host output [rows][out width]; out_width_cap bounds the width."""
         import numpy as np
         x = _f32(x)
-        out = np.zeros((x.shape[0], out_width_cap), np.float32)
+        rows = x.shape[0]
+        out = np.zeros(rows * out_width_cap, np.float32)  # filled as [rows][out width], densely
         ow = c_int32()
-        check(_L.welvet_b200_volume_forward_f32(self._h, x.shape[0], _np_ptr(x), x.shape[1], _np_ptr(out),
-                                                out_width_cap, byref(ow)))
-        return out[:, :ow.value].copy()
+        check(_L.welvet_b200_volume_forward_f32(self._h, rows, _np_ptr(x), x.shape[1], _np_ptr(out), out.size,
+                                                byref(ow)))
+        return out[:rows * ow.value].reshape(rows, ow.value).copy()
 
     def cell_outputs(self, coord):
         pre, post = c_void_p(), c_void_p()
