@@ -9,9 +9,17 @@ executes), so each step streams 512 MiB of packed weights -- more than the 126 M
 flush needed. The same 64 layers run as a dependent chain are reported under "chain". Weights are random
 (synthetic; the reference ships no checkpoints).
 
-  value  weight GB/s with x/weights resident in HBM (device-pointer entry point, PDL chain)
-  e2e    the same metric through the reference-facing C ABI welvet_dense_execute, host
-         buffers (pinned), H2D of x and D2H of pre/post inside the timed region
+  value    weight GB/s with x/weights resident in HBM: the 64 forwards go out through
+           welvet_b200_dense_execute_group_device, i.e. the tensor-core GEMV kernel over
+           32 layers per launch (blockIdx.z = layer), two launches per step
+  e2e      the same metric through the reference-facing C ABI welvet_dense_execute, host
+           buffers (pinned), H2D of x and D2H of pre/post inside the timed region, one
+           synchronous call per layer
+  branches the same 64 forwards as 64 single-layer launches on 8 graph branches
+  chain    the same 64 layers as a dependent chain (layer i's post is layer i+1's x)
+  batched  the other half of the metric, TFLOP/s of the batched tcgen05 path: BASELINE
+           config 3's SwiGLU cell (d 4096, hidden 14336, FP8 E4M3, W ~ N(0, 0.02)) at
+           M = 512 tokens of N(0, 1) activations rounded to bf16, seed 2
 N > 1 (torchrun): every rank runs its own chain (independent layers, weak scaling, no
 collective on the data path); value = all ranks' bytes / max-over-ranks time.
 
@@ -199,6 +207,13 @@ def run_ours(args):
     streams = [torch.cuda.Stream() for _ in range(NSTREAMS)]
     outs = [(torch.zeros((1, OUT), device="cuda"), torch.zeros((1, OUT), device="cuda")) for _ in range(NSTREAMS)]
 
+    xs_group = [x0] * LAYERS
+    outs_group = [(torch.zeros((1, OUT), device="cuda"), torch.zeros((1, OUT), device="cuda")) for _ in range(LAYERS)]
+
+    def step_group():
+        # the 64 independent forwards as grouped launches (32 layers per launch)
+        W.dense_execute_group(sessions, xs_group, [o[0] for o in outs_group], [o[1] for o in outs_group])
+
     def step_independent():
         # 64 independent forwards (the reference's --bench loop repeats independent executes),
         # one per distinct weight set, spread over 8 stream branches that the graph runs
@@ -235,8 +250,8 @@ def run_ours(args):
         return float(t.item())
 
     def capture(fn):
-        # The 64 launches of a step are captured once in a CUDA graph (PDL edges between
-        # consecutive GEMVs of one stream are kept) and replayed per step.
+        # A step's launches are captured once in a CUDA graph (PDL edges between consecutive
+        # GEMVs of one stream are kept) and replayed per step.
         fn()
         torch.cuda.synchronize()
         if args.no_graph:
@@ -248,10 +263,12 @@ def run_ours(args):
         return graph.replay
 
     graphs = []
-    run = capture(step_independent)
+    run = capture(step_group)
+    run_branches = capture(step_independent)
     run_chain = capture(step_chain)
     for _ in range(args.warmup):
         run()
+        run_branches()
         run_chain()
     barrier()
     stream = torch.cuda.current_stream()
@@ -266,10 +283,26 @@ def run_ours(args):
         barrier()
     ms = e0.elapsed_time(e1)
     ms = max_over_ranks(ms)
-    launches = args.steps * LAYERS
+    group_per_launch = 32
+    launches_per_step = (LAYERS + group_per_launch - 1) // group_per_launch
+    launches = args.steps * launches_per_step
     bytes_per_step = LAYERS * WEIGHT_BYTES_PER_LAYER
     value = world * bytes_per_step * args.steps / (ms / 1e3) / 1e9
     per_launch_s = (ms / 1e3) / launches
+
+    def timed(fn, steps):
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        barrier()
+        a0.record(stream)
+        for _ in range(steps):
+            fn()
+        a1.record(stream)
+        barrier()
+        return max_over_ranks(a0.elapsed_time(a1))
+
+    ms_br = timed(run_branches, args.steps)
+    branches_val = world * bytes_per_step * args.steps / (ms_br / 1e3) / 1e9
 
     # the same 64 layers as a dependent chain (layer i's post is layer i+1's x)
     c0 = torch.cuda.Event(enable_timing=True)
@@ -305,13 +338,23 @@ def run_ours(args):
     t_e2e = max_over_ranks(time.perf_counter() - t0)
     e2e_val = world * bytes_per_step * e2e_steps / t_e2e / 1e9
 
+    # ---- batched path: C3 SwiGLU cell at M = 512 (tcgen05 GEMMs for gate, up and down)
+    batched = run_batched(args, torch, W, rank, barrier, max_over_ranks, stream) if not args.no_batched else None
+
     pk, pk_kind = peaks()
-    achieved = WEIGHT_BYTES_PER_LAYER / per_launch_s / 1e9
+    bytes_per_launch = group_per_launch * WEIGHT_BYTES_PER_LAYER
+    achieved = bytes_per_launch / per_launch_s / 1e9
+    tr = traffic_from_profile()
     roofline = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / pk["hbm_gbs"], "traffic": traffic_from_profile(),
+                "frac": achieved / pk["hbm_gbs"], "traffic": None if tr is None else tr * group_per_launch,
                 "peak_source": f"{pk_kind} hbm_gbs (MEASURED_PEAKS.json)" if pk_kind == "measured" else "fallback",
-                "kernel": "k_gemv<FP4,B=1> (welvet/cuda_b200/csrc/gemv.cu)",
-                "algorithmic_bytes_per_launch": WEIGHT_BYTES_PER_LAYER}
+                "kernel": "k_gemv_tc<FP4,B=1> over 32 layers per launch (welvet/cuda_b200/csrc/gemv_tc.cu)",
+                "algorithmic_bytes_per_launch": bytes_per_launch,
+                "traffic_note": "ncu DRAM bytes of one single-layer launch x 32 layers"}
+    if batched is not None:
+        batched["frac"] = batched["value"] / pk["bf16_tflops"]
+        batched["peak"] = pk["bf16_tflops"]
+        batched["peak_source"] = f"{pk_kind} bf16_tflops (burst, MEASURED_PEAKS.json)"
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -323,7 +366,7 @@ def run_ours(args):
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp4 codes, fp32/fp64 accumulate",
                 "data": "synthetic",
                 "config": {"workload": "C2 Dense GEMV 4096->4096 B=1 FP4 (W~N(0,0.02), seed 1): 64 independent "
-                                       "forwards of 64 distinct weight sets per step",
+                                       "forwards of 64 distinct weight sets per step, grouped 32 layers per launch",
                            "global_batch": world, "seq_len": 1, "parallelism": f"replicas x{world}",
                            "l2": "inputs larger than L2 (512 MiB of packed weights per step)",
                            "bytes_per_step_per_gpu": bytes_per_step},
@@ -332,8 +375,11 @@ def run_ours(args):
                 "e2e": {"value": e2e_val, "unit": "GB/s", "h2d_bytes_per_step": LAYERS * IN * 4,
                         "d2h_bytes_per_step": LAYERS * OUT * 4 * 2, "steps": e2e_steps,
                         "api": "welvet_dense_execute (host pinned buffers, synchronous per layer)"},
+                "branches": {"value": branches_val, "unit": "GB/s", "ms_per_step": ms_br / args.steps,
+                             "what": "the same 64 forwards as 64 single-layer launches on 8 CUDA-graph branches"},
                 "chain": {"value": chain_val, "unit": "GB/s", "ms_per_step": ms_chain / args.steps,
                           "what": "the same 64 layers as a dependent chain, layer i's post feeding layer i+1"},
+                "batched": batched,
                 "gpu_launches": launches,
                 "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
@@ -346,6 +392,45 @@ def run_ours(args):
     return 0
 
 
+def run_batched(args, torch, W, rank, barrier, max_over_ranks, stream):
+    """C3 SwiGLU cell (4096 -> 14336 -> 4096, FP8 E4M3) at M = 512 tokens: TFLOP/s of the
+    tcgen05 GEMM path (2 * M * 3 * 4096 * 14336 flops per forward). Weights are 176 MB, more
+    than L2; the cell's forward is captured in a CUDA graph."""
+    d, hid, m = 4096, 14336, 512
+    g = torch.Generator(device="cuda").manual_seed(2 * 1000 + rank)
+    ws = [torch.randn(s, device="cuda", generator=g) * SIGMA for s in ((hid, d), (hid, d), (d, hid))]
+    cell = W.SwigluCell(ws[0], ws[1], ws[2], 4)
+    del ws
+    x = torch.randn((m, d), device="cuda", generator=g).to(torch.bfloat16).float()
+    y = torch.zeros((m, d), device="cuda")
+    h = torch.zeros((m, hid), device="cuda")
+    cell.execute_device(x, y, h)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        cell.execute_device(x, y, h)
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    steps = max(5, min(args.steps, 50))
+    a0 = torch.cuda.Event(enable_timing=True)
+    a1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    a0.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    a1.record(stream)
+    barrier()
+    ms = max_over_ranks(a0.elapsed_time(a1)) / steps
+    flops = 2.0 * m * 3 * d * hid
+    del graph
+    cell.release()
+    return {"value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_forward": ms, "steps": steps,
+            "config": "C3 SwiGLU cell d=4096 hidden=14336 FP8 E4M3 W~N(0,0.02), M=512 tokens, x~N(0,1) "
+                      "rounded to bf16, seed 2",
+            "kernels": "k_split_x + k_gemm_tm<FP8 E4M3> (gate, up, down) + k_swiglu_product",
+            "l2": "176 MB of FP8 weights per forward (more than L2)"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -355,6 +440,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch the step's kernels one by one")
+    ap.add_argument("--no-batched", action="store_true", help="skip the batched (SwiGLU M=512) measurement")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

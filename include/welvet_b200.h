@@ -43,6 +43,17 @@ WELVET_API welvet_status welvet_b200_dense_execute_device(welvet_dense_session* 
                                                           const float* x_dev, float* pre_dev,
                                                           float* post_dev, void* stream);
 
+/* No counterpart in the reference (which runs one session per call, src/interop/c_abi.cpp
+ * welvet_dense_execute). n independent forwards on one stream: sessions i = 0..n-1 read
+ * x_dev[i] and write pre_dev[i] / post_dev[i] (device pointers, as in
+ * welvet_b200_dense_execute_device). Sessions that share dtype, shape and batch (1..4) and
+ * run the small-batch tensor GEMV go out in grouped launches of up to 32 layers, one kernel
+ * over all of them; otherwise each session runs on its own. Asynchronous on `stream`. */
+WELVET_API welvet_status welvet_b200_dense_execute_group_device(welvet_dense_session* const* sessions, int32_t n,
+                                                                const float* const* x_dev,
+                                                                float* const* pre_dev,
+                                                                float* const* post_dev, void* stream);
+
 /* No counterpart in the reference. welvet_b200_dense_execute_device without any allocation,
  * for callers that cannot call cudaMalloc while they run a forward: a serving loop that must
  * not stall on an allocation (cudaMalloc can synchronize the device), code that runs while a

@@ -77,6 +77,8 @@ _sig("welvet_b200_dense_mount_native", _ST, c_int32, c_int32, c_int32, c_int32, 
 _sig("welvet_dense_execute", _ST, c_void_p, c_void_p, c_void_p, c_void_p)
 _sig("welvet_b200_dense_execute_device", _ST, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p)
 _sig("welvet_b200_dense_execute_device_noalloc", _ST, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p)
+_sig("welvet_b200_dense_execute_group_device", _ST, POINTER(c_void_p), c_int32, POINTER(c_void_p),
+     POINTER(c_void_p), POINTER(c_void_p), c_void_p)
 _sig("welvet_dense_release", None, c_void_p)
 _sig("welvet_b200_dense_store", _ST, c_void_p, POINTER(c_int32), POINTER(c_int32), POINTER(c_int32),
      POINTER(c_float), c_void_p, c_size_t, POINTER(c_size_t))
@@ -224,6 +226,20 @@ class DenseSession:
             self.release()
         except Exception:
             pass
+
+
+def dense_execute_group(sessions, xs, pres, posts, stream=None) -> None:
+    """n independent forwards (device tensors) in grouped launches where the sessions share
+    dtype, shape and a batch of 1..4 (welvet_b200_dense_execute_group_device)."""
+    n = len(sessions)
+    if not (len(xs) == len(pres) == len(posts) == n):
+        raise ValueError("dense_execute_group: one x, pre and post per session")
+    arr = c_void_p * n
+    hs = arr(*[s._h.value for s in sessions])
+    xp = arr(*[_dev_ptr(t) for t in xs])
+    pp = arr(*[_dev_ptr(t) for t in pres])
+    qp = arr(*[_dev_ptr(t) for t in posts])
+    check(_L.welvet_b200_dense_execute_group_device(hs, n, xp, pp, qp, _stream_ptr(stream)))
 
 
 # ------------------------------------------------------------------ cells

@@ -190,6 +190,20 @@ welvet_status welvet_b200_dense_execute_device(welvet_dense_session* sess, const
   });
 }
 
+welvet_status welvet_b200_dense_execute_group_device(welvet_dense_session* const* sessions, int32_t n,
+                                                     const float* const* x_dev, float* const* pre_dev,
+                                                     float* const* post_dev, void* stream) {
+  return guarded([&] {
+    if (n < 0 || (n > 0 && !sessions)) return wb::Status::Invalid("null group execute args");
+    std::vector<wb::DenseSession*> ss(static_cast<size_t>(n));
+    for (int32_t i = 0; i < n; ++i) {
+      if (!sessions[i]) return wb::Status::Invalid("null group execute args");
+      ss[static_cast<size_t>(i)] = sessions[i]->s;
+    }
+    return wb::session_execute_group(ss.data(), n, x_dev, pre_dev, post_dev, static_cast<cudaStream_t>(stream));
+  });
+}
+
 welvet_status welvet_b200_dense_execute_device_noalloc(welvet_dense_session* sess, const float* x_dev,
                                                        float* pre_dev, float* post_dev, void* stream) {
   return guarded([&] {

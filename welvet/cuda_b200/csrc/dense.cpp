@@ -10,6 +10,8 @@
 
 #include "codec.hpp"
 #include "gemm_tc.hpp"
+
+#include <vector>
 #include "gemv.hpp"
 #include "gemv_tc.hpp"
 
@@ -462,6 +464,41 @@ Status session_execute_device_noalloc(DenseSession* s, const float* x, float* pr
   g.xsplit = xsplit_policy();
   g.err = s->io.err;
   return launch_gemm_tc_static(g, st);
+}
+
+Status session_execute_group(DenseSession* const* s, int n, const float* const* x, float* const* pre,
+                             float* const* post, cudaStream_t st) {
+  if (n < 0 || (n > 0 && (!s || !x || !pre || !post))) return Status::Invalid("null group execute args");
+  if (n == 0) return Status::Ok();
+  for (int i = 0; i < n; ++i)
+    if (!s[i] || !x[i] || !pre[i] || !post[i]) return Status::Invalid("null group execute args");
+  WB_CUDA(cudaSetDevice(s[0]->device));
+  const DeviceDense& d0 = s[0]->dev;
+  bool grouped = use_gemv_tc(d0, s[0]->batch);
+  for (int i = 1; i < n && grouped; ++i) {
+    const DeviceDense& d = s[i]->dev;
+    grouped = s[i]->device == s[0]->device && s[i]->batch == s[0]->batch && d.dtype == d0.dtype &&
+              d.rows == d0.rows && d.cols == d0.cols && use_gemv_tc(d, s[i]->batch);
+  }
+  if (!grouped) {
+    for (int i = 0; i < n; ++i) WB_TRY(session_execute_device(s[i], x[i], pre[i], post[i], st));
+    return Status::Ok();
+  }
+  std::vector<GemvGroupLayer> layers(static_cast<size_t>(n));
+  for (int i = 0; i < n; ++i) {
+    const DeviceDense& d = s[i]->dev;
+    GemvGroupLayer& L = layers[static_cast<size_t>(i)];
+    L.Wt = d.Wt;
+    L.x = x[i];
+    L.pre = pre[i];
+    L.post = post[i];
+    L.bias = d.bias;
+    L.bias_len = d.bias_len;
+    L.act = d.act;
+    L.scale = d.scale;
+  }
+  return launch_gemv_tc_group(d0.dtype, d0.rows, d0.cols, s[0]->batch, d0.cols, d0.rows, layers.data(), n, st,
+                              true);
 }
 
 Status session_execute_device(DenseSession* s, const float* x, float* pre, float* post, cudaStream_t st) {

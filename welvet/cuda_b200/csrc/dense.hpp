@@ -127,6 +127,12 @@ Status session_execute(DenseSession* s, const float* x, float* pre, float* post)
 Status session_execute_device(DenseSession* s, const float* x, float* pre, float* post,
                               cudaStream_t st);
 
+// n independent forwards on one stream: sessions that share dtype, shape and batch and run
+// the small-batch tensor GEMV go out together in grouped launches (up to 32 layers each);
+// any others run one by one. x[i], pre[i], post[i] are device pointers of session i.
+Status session_execute_group(DenseSession* const* s, int n, const float* const* x, float* const* pre,
+                             float* const* post, cudaStream_t st);
+
 // Same forward for batched sessions (> 4 tokens on the tcgen05 path), with the GEMM's scratch
 // in the library's fixed static device array: no allocation of any kind.
 Status session_execute_device_noalloc(DenseSession* s, const float* x, float* pre, float* post,

@@ -42,9 +42,15 @@ struct Plan {
   int cpw = 1;              // chunks per warp
   int csize = 1;            // CTAs per cluster (split of K)
   int nkb_cta = 0;          // K blocks of 16 per CTA
+  int64_t grid_y = 0;       // CTAs along the row sets (a CTA loops over row sets grid_y apart)
 };
 
-Plan make_plan(DType dt, int rows, int cols) {
+// grouped = false: one layer per launch, latency first -- the K range is split over up to 8
+// CTAs of a cluster so that a single small layer spreads over many SMs.
+// grouped = true: many layers per launch fill the GPU by themselves, so each CTA streams a
+// longer K range (up to 8 chunks per warp, double-buffered) and the fixed cost of a CTA (x
+// staging, fragment build, reduction, epilogue) is paid over more bytes.
+Plan make_plan(DType dt, int rows, int cols, bool grouped = false) {
   Plan p;
   p.g = tiled_geom(dt, rows, cols);
   p.row_sets = (p.g.row_groups + kRG - 1) / kRG;
@@ -53,10 +59,16 @@ Plan make_plan(DType dt, int rows, int cols) {
   // then takes about half of the GPU's CTA slots, so the next launch can co-reside and
   // prefetch its weights.
   p.cpw = static_cast<int>((p.chunks + kWarps * kMaxCluster - 1) / (kWarps * kMaxCluster));
+  if (grouped) {
+    const int64_t per_warp = (p.chunks + kWarps - 1) / kWarps;
+    const int longer = static_cast<int>(per_warp < 8 ? per_warp : 8);
+    if (longer > p.cpw) p.cpw = longer;  // never fewer chunks than the cluster limit needs
+  }
   if (p.cpw < 2) p.cpw = 2;
   p.csize = static_cast<int>((p.chunks + kWarps * p.cpw - 1) / (kWarps * p.cpw));
   const int kbpu = dt == DType::FP4 ? 4 : 2;
   p.nkb_cta = kWarps * p.cpw * 2 * kbpu;
+  p.grid_y = p.row_sets;
   return p;
 }
 
@@ -178,8 +190,27 @@ __device__ __forceinline__ void write_out(const KArgs& a, int o, int b, double y
   }
 }
 
-template <int kDt, int kB, bool kDual>
-__global__ void __launch_bounds__(kWarps * 32) k_gemv_tc(const KArgs a) {
+// Layers of one grouped launch (same shape and dtype): blockIdx.z picks the layer.
+template <int kL>
+struct GroupArgs {
+  KArgs a;
+  GemvGroupLayer layer[kL];
+};
+
+template <int kDt, int kB, bool kDual, int kL>
+__global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : 4) k_gemv_tc(const __grid_constant__ GroupArgs<kL> ga) {
+  KArgs a = ga.a;
+  if constexpr (kL > 1) {
+    const GemvGroupLayer& L = ga.layer[blockIdx.z];
+    a.Wt = L.Wt;
+    a.x = L.x;
+    a.pre = L.pre;
+    a.post = L.post;
+    a.bias = L.bias;
+    a.bias_len = L.bias_len;
+    a.act = L.act;
+    a.scale = L.scale;
+  }
   constexpr int KBPU = kDt == 16 ? 4 : 2;       // K blocks of 16 per unit
   constexpr int CK = 2 * KBPU * 16;             // K elements per chunk
   constexpr int NCOL = 2 * kB;                  // B columns in use: n = 2 * token + plane
@@ -192,14 +223,15 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_tc(const KArgs a) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int rank = blockIdx.x;                  // K split = rank in the cluster
-  const int64_t rs = blockIdx.y;
-  const int64_t rg0 = rs * kRG;
+  // Row sets of this CTA: blockIdx.y, blockIdx.y + gridDim.y, ... (one per CTA unless a
+  // grouped launch gives each CTA several, which then share the x slice and B fragments).
+  int64_t rs = blockIdx.y;
   const int64_t cta_c0 = static_cast<int64_t>(rank) * kWarps * a.cpw;
   const int64_t c0 = cta_c0 + static_cast<int64_t>(warp) * a.cpw;
   int64_t c1 = c0 + a.cpw;
   if (c1 > a.chunks) c1 = a.chunks;
 
-  auto load_chunk = [&](int64_t c, uint4 (&buf)[2][kRG], uint4 (&buf2)[2][kRG]) {
+  auto load_chunk = [&](int64_t rg0, int64_t c, uint4 (&buf)[2][kRG], uint4 (&buf2)[2][kRG]) {
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int64_t unit = 2 * c + u;
@@ -217,8 +249,8 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_tc(const KArgs a) {
   uint4 bufB[2][kRG], bufB2[2][kRG];
   // The first two chunks' weights are requested before waiting on the previous kernel:
   // they do not depend on it.
-  if (c0 < c1) load_chunk(c0, bufA, bufA2);
-  if (c0 + 1 < c1) load_chunk(c0 + 1, bufB, bufB2);
+  if (c0 < c1) load_chunk(rs * kRG, c0, bufA, bufA2);
+  if (c0 + 1 < c1) load_chunk(rs * kRG, c0 + 1, bufB, bufB2);
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---- the CTA's x slice, read from global memory once into shared memory (zero past
@@ -280,8 +312,6 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_tc(const KArgs a) {
   const bool col_active = g < NCOL;
 
   double acc[kRG][2], acc2[kRG][2];
-#pragma unroll
-  for (int r = 0; r < kRG; ++r) acc[r][0] = acc[r][1] = acc2[r][0] = acc2[r][1] = 0.0;
 
   auto compute_chunk = [&](int64_t c, const uint4 (&buf)[2][kRG], const uint4 (&buf2)[2][kRG]) {
     float d[kRG][4], d2[kRG][4];
@@ -319,15 +349,27 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_tc(const KArgs a) {
     }
   };
 
+  namespace cg = cooperative_groups;
+  constexpr int M = kDual ? 2 : 1;
+  const int64_t nrs = (a.row_groups + kRG - 1) / kRG;
+  for (; rs < nrs; rs += gridDim.y) {
+    const int64_t rg0 = rs * kRG;
+#pragma unroll
+    for (int r = 0; r < kRG; ++r) acc[r][0] = acc[r][1] = acc2[r][0] = acc2[r][1] = 0.0;
   // chunk c sits in bufA when c - c0 is even, in bufB when odd; the chunk two ahead is
   // requested as soon as its buffer is free.
   for (int64_t c = c0; c < c1; c += 2) {
     compute_chunk(c, bufA, bufA2);
-    if (c + 2 < c1) load_chunk(c + 2, bufA, bufA2);
+    if (c + 2 < c1) load_chunk(rg0, c + 2, bufA, bufA2);
     if (c + 1 < c1) {
       compute_chunk(c + 1, bufB, bufB2);
-      if (c + 3 < c1) load_chunk(c + 3, bufB, bufB2);
+      if (c + 3 < c1) load_chunk(rg0, c + 3, bufB, bufB2);
     }
+  }
+  // the next row set's first two chunks stream in while this one is reduced and written
+  if (rs + gridDim.y < nrs) {
+    if (c0 < c1) load_chunk((rs + gridDim.y) * kRG, c0, bufA, bufA2);
+    if (c0 + 1 < c1) load_chunk((rs + gridDim.y) * kRG, c0 + 1, bufB, bufB2);
   }
 
   // ---- CTA reduction over its 4 K slices (fixed order)
@@ -343,7 +385,6 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_tc(const KArgs a) {
     }
   }
   __syncthreads();
-  constexpr int M = kDual ? 2 : 1;
   for (int i = tid; i < kRowsPerSet * M * kB; i += kWarps * 32) {
     const int row = i / (M * kB), rem = i - row * M * kB, m = rem / kB, b = rem - m * kB;
     double y = 0.0;
@@ -353,7 +394,6 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_tc(const KArgs a) {
   }
 
   // ---- cluster reduction over the K splits through distributed shared memory
-  namespace cg = cooperative_groups;
   if (a.csize > 1) cg::this_cluster().sync();
   else __syncthreads();
   if (rank == 0) {
@@ -373,6 +413,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv_tc(const KArgs a) {
     }
   }
   if (a.csize > 1) cg::this_cluster().sync();  // keep every rank's shared memory alive for rank 0
+  }
 }
 
 // One thread per output byte of the tiled mirror.
@@ -416,10 +457,10 @@ __global__ void k_build_tiled(const uint8_t* __restrict__ native, int rows, int 
   }
 }
 
-template <int kDt, int kB, bool kDual>
-Status launch_t(const KArgs& k, const Plan& pl, cudaStream_t st, bool pdl) {
+template <int kDt, int kB, bool kDual, int kL>
+Status launch_t(const GroupArgs<kL>& k, int nl, const Plan& pl, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(pl.csize), static_cast<unsigned>(pl.row_sets));
+  cfg.gridDim = dim3(static_cast<unsigned>(pl.csize), static_cast<unsigned>(pl.grid_y), static_cast<unsigned>(nl));
   cfg.blockDim = dim3(kWarps * 32);
   // B fragments [nkb_cta][2 kB][4] uint2, then the x slice [kB][16 nkb_cta] float
   cfg.dynamicSmemBytes = static_cast<size_t>(pl.nkb_cta) * 2 * kB * 4 * sizeof(uint2) +
@@ -439,30 +480,30 @@ Status launch_t(const KArgs& k, const Plan& pl, cudaStream_t st, bool pdl) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  auto kern = k_gemv_tc<kDt, kB, kDual>;
+  auto kern = k_gemv_tc<kDt, kB, kDual, kL>;
   if (cfg.dynamicSmemBytes > 48 * 1024)
     WB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(cfg.dynamicSmemBytes)));
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, k), "gemv_tc launch");
 }
 
-template <int kDt, bool kDual>
-Status launch_b(const KArgs& k, const Plan& pl, int batch, cudaStream_t st, bool pdl) {
+template <int kDt, bool kDual, int kL>
+Status launch_b(const GroupArgs<kL>& k, int nl, const Plan& pl, int batch, cudaStream_t st, bool pdl) {
   switch (batch) {
-  case 1: return launch_t<kDt, 1, kDual>(k, pl, st, pdl);
-  case 2: return launch_t<kDt, 2, kDual>(k, pl, st, pdl);
-  case 3: return launch_t<kDt, 3, kDual>(k, pl, st, pdl);
-  case 4: return launch_t<kDt, 4, kDual>(k, pl, st, pdl);
+  case 1: return launch_t<kDt, 1, kDual, kL>(k, nl, pl, st, pdl);
+  case 2: return launch_t<kDt, 2, kDual, kL>(k, nl, pl, st, pdl);
+  case 3: return launch_t<kDt, 3, kDual, kL>(k, nl, pl, st, pdl);
+  case 4: return launch_t<kDt, 4, kDual, kL>(k, nl, pl, st, pdl);
   default: return Status::Internal("gemv_tc: batch must be 1..4");
   }
 }
 
-template <bool kDual>
-Status launch_d(DType dt, const KArgs& k, const Plan& pl, int batch, cudaStream_t st, bool pdl) {
+template <bool kDual, int kL>
+Status launch_d(DType dt, const GroupArgs<kL>& k, int nl, const Plan& pl, int batch, cudaStream_t st, bool pdl) {
   switch (dt) {
-  case DType::FP4: return launch_b<16, kDual>(k, pl, batch, st, pdl);
-  case DType::FP8E4M3: return launch_b<4, kDual>(k, pl, batch, st, pdl);
-  case DType::FP8E5M2: return launch_b<5, kDual>(k, pl, batch, st, pdl);
-  case DType::Int8: return launch_b<9, kDual>(k, pl, batch, st, pdl);
+  case DType::FP4: return launch_b<16, kDual, kL>(k, nl, pl, batch, st, pdl);
+  case DType::FP8E4M3: return launch_b<4, kDual, kL>(k, nl, pl, batch, st, pdl);
+  case DType::FP8E5M2: return launch_b<5, kDual, kL>(k, nl, pl, batch, st, pdl);
+  case DType::Int8: return launch_b<9, kDual, kL>(k, nl, pl, batch, st, pdl);
   default: return Status::Unsupported("gemv_tc: dtype");
   }
 }
@@ -522,7 +563,43 @@ Status launch_gemv_tc(const GemvTcArgs& a, cudaStream_t st, bool pdl) {
   k.bias = a.bias;
   k.bias_len = a.bias_len;
   k.act = a.act;
-  return a.Wt2 ? launch_d<true>(a.dtype, k, pl, a.batch, st, pdl) : launch_d<false>(a.dtype, k, pl, a.batch, st, pdl);
+  GroupArgs<1> g{};
+  g.a = k;
+  return a.Wt2 ? launch_d<true, 1>(a.dtype, g, 1, pl, a.batch, st, pdl)
+               : launch_d<false, 1>(a.dtype, g, 1, pl, a.batch, st, pdl);
+}
+
+Status launch_gemv_tc_group(DType dt, int rows, int cols, int batch, int64_t x_ld, int64_t ld_out,
+                            const GemvGroupLayer* layers, int n, cudaStream_t st, bool pdl) {
+  if (!gemv_tc_supported(dt)) return Status::Unsupported("gemv_tc: dtype");
+  if (rows <= 0 || cols <= 0 || batch < 1 || batch > 4 || n < 0 || (n > 0 && !layers))
+    return Status::Invalid("gemv_tc group: bad arguments");
+  Plan pl = make_plan(dt, rows, cols, true);
+  for (int l0 = 0; l0 < n; l0 += kGemvGroupMax) {
+    const int nl = n - l0 < kGemvGroupMax ? n - l0 : kGemvGroupMax;
+    // one 64-row set per CTA: many short CTAs balance over the SMs better than fewer long
+    // ones (measured: 3 row sets per CTA left a partial second wave)
+    pl.grid_y = pl.row_sets;
+    GroupArgs<kGemvGroupMax> g{};
+    KArgs& k = g.a;
+    k.rows = rows;
+    k.cols = cols;
+    k.units_k = pl.g.units_k;
+    k.row_groups = pl.g.row_groups;
+    k.chunks = pl.chunks;
+    k.cpw = pl.cpw;
+    k.csize = pl.csize;
+    k.nkb_cta = pl.nkb_cta;
+    k.x_ld = x_ld;
+    k.ld_out = ld_out;
+    for (int i = 0; i < nl; ++i) {
+      const GemvGroupLayer& L = layers[l0 + i];
+      if (!L.Wt || !L.x || !L.pre || !L.post) return Status::Invalid("gemv_tc group: null layer pointer");
+      g.layer[i] = L;
+    }
+    WB_TRY((launch_d<false, kGemvGroupMax>(dt, g, nl, pl, batch, st, pdl)));
+  }
+  return Status::Ok();
 }
 
 } // namespace wb

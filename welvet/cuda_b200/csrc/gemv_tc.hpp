@@ -43,4 +43,22 @@ struct GemvTcArgs {
 // prefetched before griddepcontrol.wait; x is read and outputs written after it).
 Status launch_gemv_tc(const GemvTcArgs& a, cudaStream_t st, bool pdl);
 
+// Independent layers of one shape and dtype in one launch (blockIdx.z = layer): the same
+// kernel over a grid that fills the GPU, for several forwards that do not depend on each
+// other (parallel projections, layers of different sequences). Launches of at most
+// kGemvGroupMax layers each; every layer reads its own x and writes its own outputs.
+struct GemvGroupLayer {
+  const uint8_t* Wt = nullptr;   // tiled mirror
+  const float* x = nullptr;      // [batch][x_ld]
+  float* pre = nullptr;          // [batch][ld_out]
+  float* post = nullptr;
+  const double* bias = nullptr;
+  int bias_len = 0;
+  int act = -1;
+  float scale = 1.0f;            // Int8 per-tensor scale
+};
+constexpr int kGemvGroupMax = 32;
+Status launch_gemv_tc_group(DType dt, int rows, int cols, int batch, int64_t x_ld, int64_t ld_out,
+                            const GemvGroupLayer* layers, int n, cudaStream_t st, bool pdl);
+
 } // namespace wb
