@@ -434,10 +434,10 @@ def test_mha_tensor_paths(wb, oracle, batch, seq, monkeypatch):
 
 @pytest.mark.parametrize("dt,out,in_,n", [(16, 4096, 256, 40), (4, 2048, 4096, 33)])
 def test_grouped_gemv_matches_single_launches(wb, oracle, dt, out, in_, n, monkeypatch):
-    """welvet_b200_dense_execute_group_device: n layers (launches of up to 32; CTAs looping
-    over several 64-row sets, with and without a K-split cluster) give the same bits as each
-    session's own launch and stay within tolerance of the oracle; a group mixing shapes runs
-    one by one with the same results."""
+    """welvet_b200_dense_execute_group_device: n layers (launches of up to 32, with and
+    without a K-split cluster) each stay within tolerance of the fp64 oracle, as do the
+    sessions' own single-layer launches (which split K differently, for latency); a group
+    mixing shapes runs one by one with the single-layer results."""
     import torch
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
     gen = torch.Generator(device="cuda").manual_seed(91 + dt)
@@ -451,15 +451,15 @@ def test_grouped_gemv_matches_single_launches(wb, oracle, dt, out, in_, n, monke
     wb.dense_execute_group(sess, xs, pre_g, post_g)
     torch.cuda.synchronize()
     for i in range(n):
-        pre_s = torch.zeros((1, out), device="cuda")
-        post_s = torch.zeros((1, out), device="cuda")
-        sess[i].execute_device(xs[i], pre_s, post_s)
-        torch.cuda.synchronize()
-        assert torch.equal(pre_g[i], pre_s) and torch.equal(post_g[i], post_s), i
-    for i in (0, n // 2, n - 1):
         raw, sc = oracle.pack(dt, ws[i].cpu().numpy())
         ref = oracle.dense_forward(dt, raw, sc, xs[i].cpu().numpy(), in_, out, 2, biases[i])
         check_dense(pre_g[i].cpu().numpy(), post_g[i].cpu().numpy(), ref, 2, f"grouped layer {i}")
+        if i in (0, n // 2, n - 1):
+            pre_s = torch.zeros((1, out), device="cuda")
+            post_s = torch.zeros((1, out), device="cuda")
+            sess[i].execute_device(xs[i], pre_s, post_s)
+            torch.cuda.synchronize()
+            check_dense(pre_s.cpu().numpy(), post_s.cpu().numpy(), ref, 2, f"single layer {i}")
     # mixed shapes: one-by-one path
     w2 = torch.randn((200, in_), device="cuda", generator=gen) * 2.0
     s2 = wb.DenseSession(w2, 1, dt)
@@ -469,7 +469,10 @@ def test_grouped_gemv_matches_single_launches(wb, oracle, dt, out, in_, n, monke
     post_m = torch.zeros((1, out), device="cuda")
     wb.dense_execute_group([sess[3], s2], [xs[3], xs[4]], [pre_m, p2], [post_m, q2])
     torch.cuda.synchronize()
-    assert torch.equal(pre_m, pre_g[3])
+    pre_s = torch.zeros((1, out), device="cuda")
+    sess[3].execute_device(xs[3], pre_s, torch.zeros((1, out), device="cuda"))
+    torch.cuda.synchronize()
+    assert torch.equal(pre_m, pre_s)
     raw, sc = oracle.pack(dt, w2.cpu().numpy())
     ref = oracle.dense_forward(dt, raw, sc, xs[4].cpu().numpy(), in_, 200)
     check_dense(p2.cpu().numpy(), q2.cpu().numpy(), ref, -1, "mixed group")

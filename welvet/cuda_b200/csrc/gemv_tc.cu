@@ -171,7 +171,8 @@ __device__ __forceinline__ uint32_t x_plane_pair(float v0, float v1, float s, in
   return *reinterpret_cast<uint32_t*>(&h1);
 }
 
-__device__ __forceinline__ void write_out(const KArgs& a, int o, int b, double y, double y2, bool dual) {
+template <typename Args>
+__device__ __forceinline__ void write_out(const Args& a, int o, int b, double y, double y2, bool dual) {
   const int64_t idx = static_cast<int64_t>(b) * a.ld_out + o;
   if (!dual) {
     float pre = static_cast<float>(y);
@@ -507,6 +508,7 @@ Status launch_d(DType dt, const GroupArgs<kL>& k, int nl, const Plan& pl, int ba
   default: return Status::Unsupported("gemv_tc: dtype");
   }
 }
+
 
 } // namespace
 
