@@ -57,8 +57,8 @@ def peaks():
 
 
 def traffic_from_profile():
-    """Per-launch DRAM bytes of the GEMV from the committed ncu summary, if present."""
-    p = os.path.join(ROOT, "profiles", "gemv_fp4_4096x4096_b1.md")
+    """DRAM bytes of one grouped GEMV launch (32 layers) from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "gemv_tc_grouped_fp4_4096x4096_b1_32layers.md")
     try:
         for ln in open(p):
             if ln.startswith("dram_bytes_per_launch:"):
@@ -346,11 +346,10 @@ def run_ours(args):
     achieved = bytes_per_launch / per_launch_s / 1e9
     tr = traffic_from_profile()
     roofline = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / pk["hbm_gbs"], "traffic": None if tr is None else tr * group_per_launch,
+                "frac": achieved / pk["hbm_gbs"], "traffic": tr,
                 "peak_source": f"{pk_kind} hbm_gbs (MEASURED_PEAKS.json)" if pk_kind == "measured" else "fallback",
                 "kernel": "k_gemv_tc<FP4,B=1> over 32 layers per launch (welvet/cuda_b200/csrc/gemv_tc.cu)",
-                "algorithmic_bytes_per_launch": bytes_per_launch,
-                "traffic_note": "ncu DRAM bytes of one single-layer launch x 32 layers"}
+                "algorithmic_bytes_per_launch": bytes_per_launch}
     if batched is not None:
         batched["frac"] = batched["value"] / pk["bf16_tflops"]
         batched["peak"] = pk["bf16_tflops"]
@@ -431,6 +430,62 @@ def run_batched(args, torch, W, rank, barrier, max_over_ranks, stream):
             "l2": "176 MB of FP8 weights per forward (more than L2)"}
 
 
+def run_case(args):
+    """--case: one kernel's workload alone, for timing and ncu captures (prints one JSON line
+    with the case's own numbers, not the benchmark line). Weights ~N(0, 0.02) generated on
+    the device; x ~N(0, 1) (rounded to bf16 with --x bf16); L2 flushed before each rep.
+      gemv   one Dense layer rows x cols, --tokens 1..4, single launches
+      group  --layers independent layers rows x cols, B=1, grouped launches
+      gemm   one Dense layer rows x cols, --tokens > 4 (tcgen05 path)"""
+    import torch
+    import welvet.cuda_b200 as W
+    W.cuda_init()
+    g = torch.Generator(device="cuda").manual_seed(SEED)
+    n_layers = args.layers if args.case == "group" else 1
+    tokens = 1 if args.case == "group" else args.tokens
+    sess = []
+    for _ in range(n_layers):
+        w = torch.randn((args.rows, args.cols), device="cuda", generator=g) * SIGMA
+        sess.append(W.DenseSession(w, tokens, args.dtype))
+        del w
+    x = torch.randn((tokens, args.cols), device="cuda", generator=g)
+    if args.x == "bf16":
+        x = x.to(torch.bfloat16).float()
+    outs = [(torch.zeros((tokens, args.rows), device="cuda"), torch.zeros((tokens, args.rows), device="cuda"))
+            for _ in range(n_layers)]
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+
+    def fwd():
+        if args.case == "group":
+            W.dense_execute_group(sess, [x] * n_layers, [o[0] for o in outs], [o[1] for o in outs])
+        else:
+            sess[0].execute_device(x, outs[0][0], outs[0][1])
+
+    fwd()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(args.reps):
+        flush.zero_()
+        torch.cuda._sleep(200000)  # the GPU stays busy while the host enqueues the forward
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fwd()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    us = statistics.median(ts)
+    wbytes = args.rows * args.cols * n_layers * (0.5 if args.dtype == DTYPE_FP4 else 1.0)
+    line = {"case": args.case, "dtype": args.dtype, "rows": args.rows, "cols": args.cols, "layers": n_layers,
+            "tokens": tokens, "x": args.x, "reps": args.reps, "us_median": round(us, 2),
+            "weight_GBps": round(wbytes / us / 1e3, 1),
+            "TFLOPs": round(2.0 * tokens * args.rows * args.cols * n_layers / us / 1e6, 2)}
+    print(json.dumps(line), flush=True)
+    for s in sess:
+        s.release()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -441,7 +496,17 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch the step's kernels one by one")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched (SwiGLU M=512) measurement")
+    ap.add_argument("--case", choices=["gemv", "group", "gemm"], help="time one kernel's workload (see run_case)")
+    ap.add_argument("--dtype", type=int, default=DTYPE_FP4, help="--case: 16 FP4, 4 E4M3, 5 E5M2, 9 Int8")
+    ap.add_argument("--rows", type=int, default=OUT)
+    ap.add_argument("--cols", type=int, default=IN)
+    ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--x", choices=["f32", "bf16"], default="f32")
+    ap.add_argument("--reps", type=int, default=5)
     args = ap.parse_args()
+    if args.case:
+        return run_case(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
