@@ -430,6 +430,102 @@ def run_batched(args, torch, W, rank, barrier, max_over_ranks, stream):
             "l2": "176 MB of FP8 weights per forward (more than L2)"}
 
 
+def run_case_multi(args):
+    """--case sharded | pipeline: BASELINE config 5 on 1..N GPUs (torchrun; one process per GPU).
+      sharded   Dense rows x cols FP4 (default 65536 x 16384) split by output rows over the
+                ranks, --tokens 1 or 256; each rank's slice then NCCL all-gather
+      pipeline  volume 2x2x2 with 4 Dense 4096x4096 FP4 + ReLU layers per cell, batch 64:
+                cells placed over the ranks in hop order, --micro rows per micro-batch,
+                activations sent rank to rank
+    Prints one JSON line (rank 0): time per forward (max over ranks) and aggregate rates."""
+    import datetime
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    import torch.distributed as dist
+    dist.init_process_group("nccl" if world > 1 else "gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            **({} if world > 1 else {"init_method": "tcp://127.0.0.1:29731"}))
+    import welvet.cuda_b200 as W
+    from welvet.cuda_b200 import volume as V
+    W.cuda_init()
+    g = torch.Generator(device="cuda").manual_seed(4 * 1000 + rank)
+    stream = torch.cuda.current_stream()
+    out = {"case": args.case, "n_gpus": world}
+    if args.case == "sharded":
+        rows, cols, tokens = args.rows, args.cols, args.tokens
+        a, b = V.ColumnShardedDense.shard_rows(rows, world, rank)
+        w = torch.randn((b - a, cols), device="cuda", generator=g) * SIGMA
+        sess = W.DenseSession(w, tokens, DTYPE_FP4)
+        del w
+        x = torch.randn((tokens, cols), device="cuda", generator=torch.Generator(device="cuda").manual_seed(4))
+        pre = torch.empty((tokens, b - a), device="cuda")
+        post = torch.empty((tokens, b - a), device="cuda")
+
+        def local_fn(xd):
+            sess.execute_device(xd, pre, post, stream)
+            return pre
+
+        sd = V.ColumnShardedDense(local_fn, rows)
+        step = lambda: sd.forward(x)
+        compute = lambda: local_fn(x)
+        flops = 2.0 * tokens * rows * cols
+        wbytes = rows * cols * 0.5
+    else:
+        lpc, cells, width, batch = 4, 8, 4096, 64
+        vol = V.Volume(2, 2, 2, lpc)
+        b, e = V.stage_plan(cells, lpc, world)[rank]
+        for h in range(b, e):
+            w = torch.randn((width, width), device="cuda", generator=g) * SIGMA
+            vol.bind_dense(vol.coord(h), w, 0, DTYPE_FP4)
+            del w
+        x = torch.randn((batch, width), device="cuda", generator=torch.Generator(device="cuda").manual_seed(4))
+
+        def runner(xin):
+            o = torch.empty_like(xin)
+            vol.forward_device(xin, o, b, e, stream=stream)
+            return o
+
+        pv = V.PipelinedVolume(runner, width, [width] * world)
+        step = lambda: pv.forward(x, micro=args.micro)
+        compute = None
+        flops = 2.0 * batch * cells * lpc * width * width
+        wbytes = cells * lpc * width * width * 0.5
+
+    def timed(fn, reps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX) if world > 1 else None
+        return float(t.item())
+
+    ms = timed(step, args.reps)
+    out.update({"ms_per_forward": ms, "TFLOPs": flops / (ms / 1e3) / 1e12, "weight_GBps": wbytes / (ms / 1e3) / 1e9,
+                "tokens": args.tokens if args.case == "sharded" else 64,
+                "micro": args.micro if args.case == "pipeline" else None})
+    if compute is not None:
+        out["compute_ms"] = timed(compute, args.reps)
+        gathered = torch.empty((world * args.tokens, (args.rows // world)), device="cuda")
+        src = torch.empty((args.tokens, args.rows // world), device="cuda")
+        out["gather_ms"] = timed(lambda: dist.all_gather_into_tensor(gathered, src) if world > 1 else None, args.reps)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def run_case(args):
     """--case: one kernel's workload alone, for timing and ncu captures (prints one JSON line
     with the case's own numbers, not the benchmark line). Weights ~N(0, 0.02) generated on
@@ -496,7 +592,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch the step's kernels one by one")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched (SwiGLU M=512) measurement")
-    ap.add_argument("--case", choices=["gemv", "group", "gemm"], help="time one kernel's workload (see run_case)")
+    ap.add_argument("--case", choices=["gemv", "group", "gemm", "sharded", "pipeline"],
+                    help="time one workload alone (see run_case / run_case_multi)")
+    ap.add_argument("--micro", type=int, default=16, help="--case pipeline: rows per micro-batch")
     ap.add_argument("--dtype", type=int, default=DTYPE_FP4, help="--case: 16 FP4, 4 E4M3, 5 E5M2, 9 Int8")
     ap.add_argument("--rows", type=int, default=OUT)
     ap.add_argument("--cols", type=int, default=IN)
@@ -505,6 +603,8 @@ def main():
     ap.add_argument("--x", choices=["f32", "bf16"], default="f32")
     ap.add_argument("--reps", type=int, default=5)
     args = ap.parse_args()
+    if args.case in ("sharded", "pipeline"):
+        return run_case_multi(args)
     if args.case:
         return run_case(args)
     if args.impl == "reference":

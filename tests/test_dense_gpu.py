@@ -385,12 +385,15 @@ def test_simt_gemv_still_correct(wb, oracle, dt, monkeypatch):
     check_dense(pre, post, ref, 1, f"simt dt={dt}")
 
 
-@pytest.mark.parametrize("rows", [1, 3, 24])  # 1..4: fused Gate/Up tensor GEMV; 24: tcgen05 GEMM
+@pytest.mark.parametrize("rows,d,inter", [(1, 256, 640), (3, 256, 640), (24, 256, 640), (300, 256, 640),
+                                          (24, 2048, 96)])
 @pytest.mark.parametrize("dt", [16, 4, 9])
-def test_swiglu_tensor_paths(wb, oracle, dt, rows, monkeypatch):
+def test_swiglu_tensor_paths(wb, oracle, dt, rows, d, inter, monkeypatch):
+    """1..4 rows: Gate and Up fused in the tensor GEMV; more: one tcgen05 GEMM over the
+    interleaved Gate/Up pair mirror writing h in its epilogue (300 rows: several token
+    blocks; d = 2048 with a narrow intermediate: split-K with the paired reduce)."""
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
     rng = np.random.default_rng(20 + rows)
-    d, inter = 256, 640
     G, U, D = [(rng.standard_normal(s) * 0.5).astype(np.float32) for s in ((inter, d), (inter, d), (d, inter))]
     x = rng.standard_normal((rows, d)).astype(np.float32)
     pre, post = wb.swiglu_forward_f32(G, U, D, x, rows, 1, dt)

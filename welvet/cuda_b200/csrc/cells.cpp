@@ -26,12 +26,20 @@ void free_dev(T*& p) {
 }
 } // namespace
 
+SwigluCell::~SwigluCell() {
+  release_work();
+  cudaSetDevice(device);
+  free_dev(Wg_pair);
+}
+
 void SwigluCell::release_work() {
   cudaSetDevice(device);
   free_dev(x_pad);
   free_dev(h_pad);
   free_dev(g_buf);
   free_dev(u_buf);
+  free_dev(pair_scratch);
+  pair_scratch_bytes = 0;
   io_gate.release();
   io_up.release();
   io_down.release();
@@ -50,6 +58,14 @@ Status swiglu_mount(int device, int in, int inter, DType dt, const float* G, con
   if (!s.ok()) return Status::Err(s.code, "swiglu Up: " + s.message);
   s = mount_dense(device, in, inter, dt, -1, D, w_is_device, nullptr, 0, &c->sd, &c->down, st);
   if (!s.ok()) return Status::Err(s.code, "swiglu Down: " + s.message);
+  if (c->gate.Wg && c->up.Wg && c->gate.row_stride == c->up.row_stride) {
+    // Gate and Up run batched as one pair GEMM; their own GEMM mirrors are then unused
+    WB_CUDA(cudaMalloc(&c->Wg_pair, gemm_mirror_bytes(dt, 2 * inter, in)));
+    WB_TRY(build_gemm_pair_mirror(dt, c->gate.W, c->up.W, inter, c->gate.row_stride, in, c->Wg_pair, st));
+    WB_CUDA(cudaStreamSynchronize(st));
+    free_dev(c->gate.Wg);
+    free_dev(c->up.Wg);
+  }
   return Status::Ok();
 }
 
@@ -64,10 +80,15 @@ Status swiglu_reserve(SwigluCell* c, int bs, cudaStream_t st) {
   WB_CUDA(cudaMalloc(&c->h_pad, hb));
   WB_CUDA(cudaMemsetAsync(c->h_pad, 0, hb, st));
   if (use_tensor_path(c->gate, bs)) {
-    WB_CUDA(cudaMalloc(&c->g_buf, static_cast<size_t>(bs) * c->inter * 4));
-    WB_CUDA(cudaMalloc(&c->u_buf, static_cast<size_t>(bs) * c->inter * 4));
-    WB_TRY(alloc_io(c->gate, bs, &c->io_gate, st));
-    WB_TRY(alloc_io(c->up, bs, &c->io_up, st));
+    WB_TRY(alloc_io(c->gate, bs, &c->io_gate, st));  // error word (and the unfused path's scratch)
+    if (c->Wg_pair && gemm_uses_tmem()) {
+      c->pair_scratch_bytes = gemm_scratch_bytes(bs, c->in, 2 * c->inter, xsplit_policy());
+      WB_CUDA(cudaMalloc(&c->pair_scratch, c->pair_scratch_bytes));
+    } else {
+      WB_CUDA(cudaMalloc(&c->g_buf, static_cast<size_t>(bs) * c->inter * 4));
+      WB_CUDA(cudaMalloc(&c->u_buf, static_cast<size_t>(bs) * c->inter * 4));
+      WB_TRY(alloc_io(c->up, bs, &c->io_up, st));
+    }
   }
   WB_TRY(alloc_io(c->down, bs, &c->io_down, st));
   c->bs = bs;
@@ -100,6 +121,32 @@ Status swiglu_forward_device(SwigluCell* c, int bs, const float* x, float* h, fl
     WB_TRY(launch_gemv_tc(a, st, pdl));
     hsrc = a.pre;
     h_ld = a.ld_out;
+  } else if (use_tensor_path(c->gate, bs) && c->pair_scratch) {
+    // batched: Gate and Up as one pair GEMM (2 x inter interleaved rows) whose epilogue
+    // writes h = SiLU(gate)·up directly
+    float* hout = h ? h : c->h_pad;
+    const int64_t ld = h ? c->inter : c->down.x_stride;
+    GemmArgs g;
+    g.dtype = c->gate.dtype;
+    g.Wg = c->Wg_pair;
+    g.row_stride = c->gate.row_stride;
+    g.rows = 2 * c->inter;
+    g.cols = c->in;
+    g.scale = c->gate.scale;
+    g.scale2 = c->up.scale;
+    g.x = x;
+    g.x_ld = c->in;
+    g.M = bs;
+    g.pair = true;
+    g.h = hout;
+    g.ld_h = ld;
+    g.xsplit = xsplit_policy();
+    g.scratch = c->pair_scratch;
+    g.scratch_bytes = c->pair_scratch_bytes;
+    g.err = c->io_gate.err;
+    WB_TRY(launch_gemm_tc(g, st));
+    hsrc = hout;
+    h_ld = ld;
   } else if (use_tensor_path(c->gate, bs) && c->g_buf) {
     // batched: Gate and Up on the tcgen05 GEMM, then the reference's SiLU product.
     WB_TRY(forward_device(c->gate, bs, x, c->in, c->g_buf, c->g_buf, &c->io_gate, st, false));

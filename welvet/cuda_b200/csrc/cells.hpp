@@ -20,11 +20,17 @@ struct SwigluCell {
   int bs = 0;
   float* x_pad = nullptr;  // [bs][gate.x_stride]
   float* h_pad = nullptr;  // [bs][down.x_stride] (padding stays zero)
-  float* g_buf = nullptr;  // [bs][inter] gate output (tensor-core GEMM path)
+  float* g_buf = nullptr;  // [bs][inter] gate output (tensor-core GEMM path, unfused)
   float* u_buf = nullptr;  // [bs][inter] up output
   DenseIO io_gate, io_up, io_down;  // per-projection staging and scratch
+  // Gate/Up pair mirror for the batched path: one tcgen05 GEMM over 2 x inter interleaved
+  // rows whose epilogue writes h (gemm_tc.hpp, GemmArgs::pair); built at mount when the
+  // layers take the tensor-core path.
+  uint8_t* Wg_pair = nullptr;
+  void* pair_scratch = nullptr;  // that GEMM's scratch for `bs` rows
+  size_t pair_scratch_bytes = 0;
   void release_work();
-  ~SwigluCell() { release_work(); }
+  ~SwigluCell();
 };
 
 Status swiglu_mount(int device, int in, int inter, DType dt, const float* G, const float* U, const float* D,

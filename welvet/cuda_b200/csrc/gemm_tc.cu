@@ -61,6 +61,9 @@ struct KParams {
   int act;
   double* partial;             // [splits][M][rows] when splits > 1
   int* err;
+  int pair;                    // SwiGLU Gate/Up pair reduce (see TmParams)
+  float* h;
+  int64_t ld_h;
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
@@ -161,6 +164,17 @@ __device__ __forceinline__ uint4 codes_to_f16x8(const uint8_t* raw_row, int j) {
 
 // The reference epilogue (src/cuda/kernels.cu:147-161): pre = float(y); with bias
 // v = double(pre) + bias and pre = float(v); post = float(act(v)).
+// SwiGLU product of one Gate/Up pair (src/cuda/kernels.cu:296-305 with the Dense
+// epilogues of Linear Gate and Up before it): gate_pre = float(y_gate), up = float(y_up),
+// h = float(double(float(SiLU(double(gate_pre)))) * double(up)).
+template <typename Params>
+__device__ __forceinline__ void write_pair(const Params& p, int t, int i, double y_gate, double y_up) {
+  const float gate_pre = static_cast<float>(y_gate);
+  const float up = static_cast<float>(y_up);
+  const float g = static_cast<float>(activate(1, static_cast<double>(gate_pre)));
+  p.h[static_cast<int64_t>(t) * p.ld_h + i] = static_cast<float>(static_cast<double>(g) * static_cast<double>(up));
+}
+
 template <typename Params>
 __device__ __forceinline__ void write_out(const Params& p, int t, int o, double y) {
   const int64_t idx = static_cast<int64_t>(t) * p.ld_out + o;
@@ -367,6 +381,10 @@ struct TmParams {
   int act;
   double* partial;             // [splits][M][rows] when splits > 1
   int* err;
+  int pair;                    // SwiGLU Gate/Up pair: rows 2i / 2i+1, epilogue writes h
+  float w_scale2;              // Up's Int8 scale (pair mode)
+  float* h;
+  int64_t ld_h;
 };
 
 __device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* tm, int x, int y, int z,
@@ -682,12 +700,19 @@ __global__ void __launch_bounds__(kTmThreads, 1)
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int t = t_pass + tc + e;
-          if (t >= t_begin + t_count || o >= p.rows) continue;
-          double yy = y[e] * static_cast<double>(p.scale_inv[t]);
-          if (kDt == 9) yy *= static_cast<double>(p.w_scale);
+          const bool valid = t < t_begin + t_count && o < p.rows;
+          double yy = 0.0;
+          if (valid) {
+            yy = y[e] * static_cast<double>(p.scale_inv[t]);
+            if (kDt == 9) yy *= static_cast<double>((p.pair && (o & 1)) ? p.w_scale2 : p.w_scale);
+          }
           if (p.splits > 1) {
-            p.partial[(static_cast<int64_t>(split) * p.M + t) * p.rows + o] = yy;
-          } else {
+            if (valid) p.partial[(static_cast<int64_t>(split) * p.M + t) * p.rows + o] = yy;
+          } else if (p.pair) {
+            // Up row o + 1 sits in the next lane (rows of a 128-row tile are lanes)
+            const double up = __shfl_xor_sync(0xffffffffu, yy, 1);
+            if (valid && (o & 1) == 0) write_pair(p, t, o >> 1, yy, up);
+          } else if (valid) {
             write_out(p, t, o, yy);
           }
         }
@@ -709,6 +734,22 @@ __global__ void __launch_bounds__(kTmThreads, 1)
 // Sum of the split-K partials in a fixed order, then the reference epilogue.
 __global__ void k_splitk_reduce(const KParams p) {
   const int64_t n = static_cast<int64_t>(p.M) * p.rows;
+  if (p.pair) {  // one thread per (token, Gate/Up pair)
+    const int half = p.rows / 2;
+    const int64_t np = static_cast<int64_t>(p.M) * half;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < np;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      const int t = static_cast<int>(i / half), j = static_cast<int>(i % half);
+      const int64_t base = static_cast<int64_t>(t) * p.rows + 2 * j;
+      double yg = 0.0, yu = 0.0;
+      for (int s = 0; s < p.splits; ++s) {
+        yg += p.partial[s * n + base];
+        yu += p.partial[s * n + base + 1];
+      }
+      write_pair(p, t, j, yg, yu);
+    }
+    return;
+  }
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     double y = 0.0;
@@ -877,20 +918,22 @@ struct TmPlan {
   size_t planes_bytes, scale_bytes, pcnt_bytes, partial_bytes;
 };
 
-// Split-K count for `tiles` CTAs of `nkb` k-blocks: the one (1..16) that makes the last wave
-// over 148 SMs fullest, as long as the fp64 partials it writes and reads stay under a
-// quarter of the weight bytes.
-int tm_splits(int tiles, int nkb, int M, int rows, double weight_bytes) {
-  if (tiles >= 148) return 1;
+// Split-K count (1..8) for `tiles` CTAs of `nkb` k-blocks, from a time model: one CTA per SM,
+// a 64-k stage costs ~0.7 us (measured per-stage period of k_gemm_tm), so the GEMM takes
+// waves(s) * 0.7 us * nkb / s; with s > 1 the fp64 partials (s x M x rows x 8 B) are written
+// and read back once (at the measured HBM rate) and the reduce launch costs ~5 us.
+int tm_splits(int tiles, int nkb, int M, int rows) {
+  const double stage_us = 0.7, hbm_bytes_per_us = 6.5e6, reduce_us = 5.0;
   int best = 1;
-  double best_eff = 0.0;
-  for (int s = 1; s <= 16 && s <= nkb / 2; ++s) {
-    if (s > 1 && 16.0 * s * M * static_cast<double>(rows) > 0.25 * weight_bytes) break;
+  double best_t = 0.0;
+  for (int s = 1; s <= 8 && s <= nkb; ++s) {
     const int ctas = tiles * s;
     const int waves = (ctas + 147) / 148;
-    const double eff = static_cast<double>(ctas) / (waves * 148.0);
-    if (eff > best_eff + 0.02) {
-      best_eff = eff;
+    const int stages = (nkb + s - 1) / s;
+    double t = waves * stage_us * stages;
+    if (s > 1) t += 2.0 * s * static_cast<double>(M) * rows * 8.0 / hbm_bytes_per_us + reduce_us;
+    if (s == 1 || t < best_t * 0.97) {
+      best_t = t;
       best = s;
     }
   }
@@ -936,8 +979,7 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt) {
   // SM: a second CTA on the SM would only stall in tcgen05.alloc.
   if (pl.smem < 116 * 1024) pl.smem = 116 * 1024;
   const int tiles = static_cast<int>(((rows + kBM - 1) / kBM) * static_cast<int64_t>((M + pl.TB - 1) / pl.TB));
-  const double wbytes = static_cast<double>(rows) * pl.Kp * (dt == DType::FP4 ? 0.5 : 1.0);
-  const int splits = tm_splits(tiles, pl.nkb, M, rows, wbytes);
+  const int splits = tm_splits(tiles, pl.nkb, M, rows);
   pl.kb_per_split = (pl.nkb + splits - 1) / splits;
   pl.splits = (pl.nkb + pl.kb_per_split - 1) / pl.kb_per_split;
   pl.planes_bytes = static_cast<size_t>(round_up(static_cast<int64_t>(xsplit) * pl.Mp * pl.Kp * 2, 1024));
@@ -958,8 +1000,11 @@ bool gemm_a_in_smem() {
 
 namespace {
 // One thread per 16-byte chunk of the GEMM mirror; see build_gemm_mirror.
-__global__ void k_build_gemm_mirror(const uint8_t* __restrict__ W, int64_t row_stride, int rows, int nkb, int kbb,
-                                    int64_t nchunks, uint8_t* __restrict__ Wg) {
+// W2 != nullptr: pair mirror, destination row 2i from W row i, 2i+1 from W2 row i (`rows`
+// counts the destination rows).
+__global__ void k_build_gemm_mirror(const uint8_t* __restrict__ W, const uint8_t* __restrict__ W2,
+                                    int64_t row_stride, int rows, int nkb, int kbb, int64_t nchunks,
+                                    uint8_t* __restrict__ Wg) {
   const int cpr = kbb >> 4;  // chunks per row per stage
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nchunks;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -972,7 +1017,10 @@ __global__ void k_build_gemm_mirror(const uint8_t* __restrict__ W, int64_t row_s
     const int64_t row = tile * 128 + r;
     const int64_t src = static_cast<int64_t>(kb) * kbb + j * 16;
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (row < rows && src + 16 <= row_stride) v = *reinterpret_cast<const uint4*>(W + row * row_stride + src);
+    if (row < rows && src + 16 <= row_stride) {
+      const uint8_t* base = W2 ? ((row & 1) ? W2 : W) + (row >> 1) * row_stride : W + row * row_stride;
+      v = *reinterpret_cast<const uint4*>(base + src);
+    }
     const int sw = kbb == 32 ? ((r >> 2) & 1) : ((r >> 1) & 3);
     *reinterpret_cast<uint4*>(Wg + ((tile * nkb + kb) * 128 + r) * kbb + ((j ^ sw) << 4)) = v;
   }
@@ -995,9 +1043,27 @@ Status build_gemm_mirror(DType dt, const uint8_t* W, int rows, int64_t row_strid
   const int64_t nchunks = static_cast<int64_t>(gemm_mirror_bytes(dt, rows, cols) / 16);
   int64_t blocks = (nchunks + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
-  k_build_gemm_mirror<<<static_cast<unsigned>(blocks), 256, 0, st>>>(W, row_stride, rows, nkb, kbb, nchunks, Wg);
+  k_build_gemm_mirror<<<static_cast<unsigned>(blocks), 256, 0, st>>>(W, nullptr, row_stride, rows, nkb, kbb, nchunks,
+                                                                      Wg);
   return cuda_status(cudaGetLastError(), "gemm mirror build");
 }
+
+Status build_gemm_pair_mirror(DType dt, const uint8_t* Wgate, const uint8_t* Wup, int inter, int64_t row_stride,
+                              int cols, uint8_t* Wg, cudaStream_t st) {
+  if (!gemm_supported(dt)) return Status::Unsupported("gemm pair mirror: dtype");
+  if (!Wgate || !Wup || !Wg || row_stride % 16 != 0 || inter <= 0) return Status::Internal("gemm pair mirror: bad arguments");
+  const int rows = 2 * inter;
+  const int nkb = (cols + kBK - 1) / kBK;
+  const int kbb = dt == DType::FP4 ? kBK / 2 : kBK;
+  const int64_t nchunks = static_cast<int64_t>(gemm_mirror_bytes(dt, rows, cols) / 16);
+  int64_t blocks = (nchunks + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  k_build_gemm_mirror<<<static_cast<unsigned>(blocks), 256, 0, st>>>(Wgate, Wup, row_stride, rows, nkb, kbb, nchunks,
+                                                                      Wg);
+  return cuda_status(cudaGetLastError(), "gemm pair mirror build");
+}
+
+bool gemm_uses_tmem() { return !gemm_a_in_smem(); }
 
 bool gemm_supported(DType dt) {
   return dt == DType::FP4 || dt == DType::FP8E4M3 || dt == DType::FP8E5M2 || dt == DType::Int8;
@@ -1082,6 +1148,7 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
   p.pre = a.pre; p.post = a.post; p.ld_out = a.ld_out;
   p.bias = a.bias; p.bias_len = a.bias_len; p.act = a.act;
   p.partial = partial; p.err = a.err;
+  p.pair = a.pair ? 1 : 0; p.w_scale2 = a.scale2; p.h = a.h; p.ld_h = a.ld_h;
 
   const size_t smem = pl.smem;
   dim3 grid(static_cast<unsigned>((a.M + pl.TB - 1) / pl.TB), static_cast<unsigned>((a.rows + kBM - 1) / kBM),
@@ -1103,6 +1170,7 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
     KParams r{};
     r.rows = a.rows; r.M = a.M; r.splits = pl.splits; r.partial = partial;
     r.pre = a.pre; r.post = a.post; r.ld_out = a.ld_out; r.bias = a.bias; r.bias_len = a.bias_len; r.act = a.act;
+    r.pair = a.pair ? 1 : 0; r.h = a.h; r.ld_h = a.ld_h;
     const int64_t n = static_cast<int64_t>(a.M) * a.rows;
     int blocks = static_cast<int>((n + 255) / 256);
     if (blocks > 148 * 16) blocks = 148 * 16;
@@ -1184,6 +1252,8 @@ Status launch_gemm_tc(const GemmArgs& a, cudaStream_t st) {
   if (!gemm_supported(a.dtype)) return Status::Unsupported("gemm_tc: dtype");
   if (a.M <= 0 || a.rows <= 0 || a.cols <= 0) return Status::Invalid("gemm_tc: bad dims");
   if (a.xsplit < 1 || a.xsplit > 3) return Status::Invalid("gemm_tc: xsplit must be 1..3");
+  if (a.pair && (gemm_a_in_smem() || !a.h || a.rows % 2 != 0 || a.ld_h < a.rows / 2))
+    return Status::Invalid("gemm_tc: the Gate/Up pair mode needs the TMEM kernel, an h buffer and even rows");
   return gemm_a_in_smem() ? launch_smem(a, st) : launch_tm(a, st);
 }
 

@@ -35,6 +35,14 @@ struct GemmArgs {
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
   int* err = nullptr;           // device error word (0 = ok), may be nullptr
+  // SwiGLU Gate/Up pair (k_gemm_tm only): Wg is a pair mirror (rows 2i = Gate row i,
+  // 2i+1 = Up row i, rows = 2 x intermediate) and the epilogue writes
+  // h[t][i] = SiLU(gate)·up with the reference's rounding (src/cuda/kernels.cu:296-305)
+  // instead of pre/post; `scale` / `scale2` are Gate's / Up's Int8 scales.
+  bool pair = false;
+  float scale2 = 1.0f;
+  float* h = nullptr;           // [M][ld_h]
+  int64_t ld_h = 0;
 };
 
 // Token tile (B rows per plane) used for M tokens; the MMA N is xsplit * tile.
@@ -52,6 +60,13 @@ bool gemm_supported(DType dt);
 size_t gemm_mirror_bytes(DType dt, int rows, int cols);
 Status build_gemm_mirror(DType dt, const uint8_t* W, int rows, int64_t row_stride, int cols, uint8_t* Wg,
                          cudaStream_t st);
+// The pair mirror of a SwiGLU cell (gemm_mirror_bytes(dt, 2 * inter, cols) bytes) from the
+// row-major mirrors of Gate and Up (same geometry).
+Status build_gemm_pair_mirror(DType dt, const uint8_t* Wgate, const uint8_t* Wup, int inter, int64_t row_stride,
+                              int cols, uint8_t* Wg, cudaStream_t st);
+// Whether launches use the TMEM kernel (the pair mode needs it): false only when
+// WELVET_B200_GEMM=smem selects the shared-memory variant.
+bool gemm_uses_tmem();
 
 Status launch_gemm_tc(const GemmArgs& a, cudaStream_t st);
 

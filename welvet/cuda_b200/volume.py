@@ -219,7 +219,8 @@ class PipelinedVolume:
             result = torch.cat(outs, dim=0).contiguous()
         else:
             result = torch.empty((rows, ow), dtype=torch.float32, device=dev)
-        dist.broadcast(result, src=world - 1, group=self.group)
+        if world > 1:
+            dist.broadcast(result, src=world - 1, group=self.group)
         return result
 
 
@@ -250,6 +251,8 @@ class ColumnShardedDense:
     def forward(self, x):
         import torch
         y = self.local(x).contiguous()  # [rows][shard]
+        if self.world == 1:
+            return y
         rows = y.shape[0]
         # [world*rows][shard]: rank slices concatenated along dim 0 (the layout every backend accepts)
         gathered = torch.empty((self.world * rows, self.shard), dtype=y.dtype, device=y.device)
