@@ -58,7 +58,7 @@ WELVET_API welvet_status welvet_b200_dense_execute_group_device(welvet_dense_ses
  * for callers that cannot call cudaMalloc while they run a forward: a serving loop that must
  * not stall on an allocation (cudaMalloc can synchronize the device), code that runs while a
  * CUDA graph is being captured, or a framework that owns all device memory up front. It runs
- * the batched tensor-core forward (a session of batch > 4, FP8/FP4/Int8, outside exact mode;
+ * the batched tensor-core forward (a session of batch > 8, FP8/FP4/Int8, outside exact mode;
  * other sessions get status 2) with the scratch of that kernel -- x split into f16 planes,
  * per-token scales, split-K partials -- in one static 32 MiB device array that the library
  * holds on every GPU that loads it until the process exits; a call needing more returns

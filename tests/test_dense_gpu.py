@@ -202,6 +202,36 @@ def test_execute_device_matches_host(wb, oracle):
     s2.release()
 
 
+@pytest.mark.parametrize("dt,batch", [(16, 1), (4, 3), (16, 24)])
+def test_host_execute_graph_replay(wb, oracle, dt, batch, monkeypatch):
+    """welvet_dense_execute: the first call runs directly, later calls replay the session's
+    recorded graph over pinned staging buffers -- every call's outputs equal a direct
+    computation of the same input bit for bit, whatever ran before."""
+    monkeypatch.setenv("WELVET_B200_EXACT", "0")
+    rng = np.random.default_rng(77 + batch)
+    out, in_ = 640, 1024
+    w = (rng.standard_normal((out, in_)) * 2.0).astype(np.float32)
+    bias = rng.standard_normal(out)
+    xs = [rng.standard_normal((batch, in_)).astype(np.float32) for _ in range(3)]
+    s = wb.DenseSession(w, batch, dt, wb.RELU, bias)
+    got = [s.execute(x) for x in (xs[0], xs[1], xs[2], xs[0], xs[1])]
+    s.release()
+    for i, x in enumerate((xs[0], xs[1], xs[2])):
+        fresh = wb.DenseSession(w, batch, dt, wb.RELU, bias)
+        ref_pre, ref_post = fresh.execute(x)  # a first call: the direct path
+        fresh.release()
+        for j in [k for k, y in enumerate((0, 1, 2, 0, 1)) if y == i]:
+            assert np.array_equal(got[j][0].view(np.uint32), ref_pre.view(np.uint32)), (i, j)
+            assert np.array_equal(got[j][1].view(np.uint32), ref_post.view(np.uint32)), (i, j)
+    raw, sc = oracle.pack(dt, w)
+    ref = oracle.dense_forward(dt, raw, sc, xs[2], in_, out, wb.RELU, bias)
+    if batch <= 8:  # tensor GEMV bound
+        check_dense(got[2][0], got[2][1], ref, wb.RELU, "graph replay")
+    else:  # tcgen05 GEMM bound
+        err = np.abs(got[2][0].astype(np.float64) - ref[0].astype(np.float64)) - 2 * ulp(ref[0])
+        assert float(np.max(err / np.maximum(ref[3], 1e-300))) <= GEMM_TOL["3"]
+
+
 def test_mount_native_bytes(wb, oracle, packs):
     for name, dt, rows, cols, scale, w, raw, dec in pack_cases(packs):
         if "specials" in name:
@@ -332,6 +362,7 @@ def test_tensor_core_path_parity(wb, oracle, dt, shape, xsplit, kernel, monkeypa
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
     monkeypatch.setenv("WELVET_B200_XSPLIT", xsplit)
     monkeypatch.setenv("WELVET_B200_GEMM", kernel)
+    monkeypatch.setenv("WELVET_B200_BATCHED", "tc")  # batches of 5..8 would otherwise take the GEMV
     out, in_, batch = shape
     w, x, bias, ref = _case(oracle, dt, out, in_, batch, 2.0, out + in_ + batch, 0)
     pre, post = wb.dense_forward_f32(w, x, dt, 0, bias)
@@ -342,6 +373,17 @@ def test_tensor_core_path_parity(wb, oracle, dt, shape, xsplit, kernel, monkeypa
     assert norm <= GEMM_TOL[xsplit], norm
     relu = np.maximum(pre.astype(np.float64), 0)
     assert np.allclose(post, relu.astype(np.float32))
+
+
+@pytest.mark.parametrize("batch", [5, 6, 7, 8])
+@pytest.mark.parametrize("dt", [16, 4, 9])
+def test_gemv_two_n_tiles(wb, oracle, dt, batch, monkeypatch):
+    """5..8 tokens on the tensor GEMV (two n8 tiles of x per A fragment), single launches
+    with the K range split over a cluster: within the GEMV bound of the fp64 oracle."""
+    monkeypatch.setenv("WELVET_B200_EXACT", "0")
+    w, x, bias, ref = _case(oracle, dt, 1040, 1536, batch, 2.0, 50 + batch, 4)
+    pre, post = wb.dense_forward_f32(w, x, dt, 4, bias)
+    check_dense(pre, post, ref, 4, f"gemv dt={dt} batch={batch}")
 
 
 @pytest.mark.parametrize("dt", [4, 16])

@@ -14,6 +14,7 @@
 #include "gemv_tc.hpp"
 
 #include <cmath>
+#include <cstdlib>
 #include <vector>
 
 namespace wb {
@@ -69,6 +70,16 @@ Status swiglu_mount(int device, int in, int inter, DType dt, const float* G, con
   return Status::Ok();
 }
 
+// SwiGLU's own batch split: the fused Gate/Up tensor GEMV takes 1..4 rows, the Gate/Up pair
+// GEMM (tcgen05) every larger batch of quantized, non-exact layers.
+static bool swiglu_dual_gemv(const SwigluCell* c, int bs) {
+  return bs <= 4 && use_gemv_tc(c->gate, bs) && c->up.Wt;
+}
+static bool swiglu_batched(const SwigluCell* c, int bs) {
+  if (std::getenv("WELVET_B200_BATCHED") != nullptr) return use_tensor_path(c->gate, bs);
+  return bs > 4 && !c->gate.exact && gemm_supported(c->gate.dtype);
+}
+
 Status swiglu_reserve(SwigluCell* c, int bs, cudaStream_t st) {
   if (c->bs >= bs) return Status::Ok();
   c->release_work();
@@ -79,7 +90,7 @@ Status swiglu_reserve(SwigluCell* c, int bs, cudaStream_t st) {
   WB_CUDA(cudaMemsetAsync(c->x_pad, 0, xb, st));
   WB_CUDA(cudaMalloc(&c->h_pad, hb));
   WB_CUDA(cudaMemsetAsync(c->h_pad, 0, hb, st));
-  if (use_tensor_path(c->gate, bs)) {
+  if (swiglu_batched(c, bs)) {
     WB_TRY(alloc_io(c->gate, bs, &c->io_gate, st));  // error word (and the unfused path's scratch)
     if (c->Wg_pair && gemm_uses_tmem()) {
       c->pair_scratch_bytes = gemm_scratch_bytes(bs, c->in, 2 * c->inter, xsplit_policy());
@@ -101,7 +112,7 @@ Status swiglu_forward_device(SwigluCell* c, int bs, const float* x, float* h, fl
   WB_TRY(swiglu_reserve(c, bs, st));
   const float* hsrc = nullptr;  // h as Down's input
   int64_t h_ld = 0;
-  if (use_gemv_tc(c->gate, bs) && c->up.Wt) {
+  if (swiglu_dual_gemv(c, bs)) {
     // 1..4 rows: Gate and Up stream together through the tensor-core GEMV, whose epilogue
     // writes h directly.
     GemvTcArgs a;
@@ -121,7 +132,7 @@ Status swiglu_forward_device(SwigluCell* c, int bs, const float* x, float* h, fl
     WB_TRY(launch_gemv_tc(a, st, pdl));
     hsrc = a.pre;
     h_ld = a.ld_out;
-  } else if (use_tensor_path(c->gate, bs) && c->pair_scratch) {
+  } else if (swiglu_batched(c, bs) && c->pair_scratch) {
     // batched: Gate and Up as one pair GEMM (2 x inter interleaved rows) whose epilogue
     // writes h = SiLU(gate)·up directly
     float* hout = h ? h : c->h_pad;
@@ -147,7 +158,7 @@ Status swiglu_forward_device(SwigluCell* c, int bs, const float* x, float* h, fl
     WB_TRY(launch_gemm_tc(g, st));
     hsrc = hout;
     h_ld = ld;
-  } else if (use_tensor_path(c->gate, bs) && c->g_buf) {
+  } else if (swiglu_batched(c, bs) && c->g_buf) {
     // batched: Gate and Up on the tcgen05 GEMM, then the reference's SiLU product.
     WB_TRY(forward_device(c->gate, bs, x, c->in, c->g_buf, c->g_buf, &c->io_gate, st, false));
     WB_TRY(forward_device(c->up, bs, x, c->in, c->u_buf, c->u_buf, &c->io_up, st, false));

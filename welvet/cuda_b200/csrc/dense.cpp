@@ -10,8 +10,6 @@
 
 #include "codec.hpp"
 #include "gemm_tc.hpp"
-
-#include <vector>
 #include "gemv.hpp"
 #include "gemv_tc.hpp"
 
@@ -19,6 +17,7 @@
 #include <cstring>
 #include <mutex>
 #include <sstream>
+#include <vector>
 
 namespace wb {
 
@@ -73,7 +72,7 @@ void DenseIO::release() {
 bool use_gemv_tc(const DeviceDense& d, int batch) {
   const char* env = std::getenv("WELVET_B200_GEMV");
   if (env && std::strcmp(env, "simt") == 0) return false;
-  return batch >= 1 && batch <= 4 && !d.exact && d.Wt != nullptr;
+  return batch >= 1 && batch <= kGemvMaxBatch && !d.exact && d.Wt != nullptr;
 }
 
 int xsplit_policy() {
@@ -86,7 +85,7 @@ bool use_tensor_path(const DeviceDense& d, int batch) {
   const char* env = std::getenv("WELVET_B200_BATCHED");
   if (env && std::strcmp(env, "gemv") == 0) return false;
   if (env && std::strcmp(env, "tc") == 0) return !d.exact && gemm_supported(d.dtype);
-  return batch > 4 && !d.exact && gemm_supported(d.dtype);
+  return batch > kGemvMaxBatch && !d.exact && gemm_supported(d.dtype);
 }
 
 bool exact_policy(int rows, int cols) {
@@ -318,6 +317,10 @@ Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x
 DenseSession::~DenseSession() {
   cudaSetDevice(device);
   if (stream) cudaStreamSynchronize(stream);
+  if (graph) cudaGraphExecDestroy(graph);
+  for (void* p : {static_cast<void*>(x_pin), static_cast<void*>(pre_pin), static_cast<void*>(post_pin),
+                  static_cast<void*>(err_pin)})
+    if (p) cudaFreeHost(p);
   io.release();
   dev.release();
   if (stream) cudaStreamDestroy(stream);
@@ -410,10 +413,60 @@ Status session_mount_native(int32_t batch, int32_t in, int32_t out, int32_t act,
   return Status::Ok();
 }
 
+namespace {
+// Records the host-buffer forward of `s` as a graph over its pinned staging buffers.
+Status build_execute_graph(DenseSession* s) {
+  const DeviceDense& d = s->dev;
+  const size_t xb = static_cast<size_t>(s->batch) * static_cast<size_t>(d.cols) * 4;
+  const size_t yb = static_cast<size_t>(s->batch) * static_cast<size_t>(d.rows) * 4;
+  WB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&s->x_pin), xb, cudaHostAllocDefault));
+  WB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&s->pre_pin), yb, cudaHostAllocDefault));
+  WB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&s->post_pin), yb, cudaHostAllocDefault));
+  WB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&s->err_pin), sizeof(int), cudaHostAllocDefault));
+  *s->err_pin = 0;
+  cudaGraph_t g = nullptr;
+  WB_CUDA(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+  Status st = cuda_status(cudaMemcpy2DAsync(s->io.x, static_cast<size_t>(d.x_stride) * 4, s->x_pin,
+                                            static_cast<size_t>(d.cols) * 4, static_cast<size_t>(d.cols) * 4,
+                                            static_cast<size_t>(s->batch), cudaMemcpyHostToDevice, s->stream),
+                          "capture h2d");
+  if (st.ok()) st = forward_device(d, s->batch, s->io.x, d.x_stride, s->io.pre, s->io.post, &s->io, s->stream, false);
+  if (st.ok()) st = cuda_status(cudaMemcpyAsync(s->pre_pin, s->io.pre, yb, cudaMemcpyDeviceToHost, s->stream), "capture d2h");
+  if (st.ok()) st = cuda_status(cudaMemcpyAsync(s->post_pin, s->io.post, yb, cudaMemcpyDeviceToHost, s->stream), "capture d2h");
+  if (st.ok() && s->io.err && s->io.scratch)
+    st = cuda_status(cudaMemcpyAsync(s->err_pin, s->io.err, sizeof(int), cudaMemcpyDeviceToHost, s->stream), "capture d2h");
+  const cudaError_t end = cudaStreamEndCapture(s->stream, &g);
+  if (st.ok()) st = cuda_status(end, "end capture");
+  if (st.ok()) st = cuda_status(cudaGraphInstantiate(&s->graph, g, 0), "graph instantiate");
+  if (g) cudaGraphDestroy(g);
+  cudaGetLastError();  // a failed capture leaves nothing pending for the direct path
+  return st;
+}
+} // namespace
+
 Status session_execute(DenseSession* s, const float* x, float* pre, float* post) {
   if (!s || !x || !pre || !post) return Status::Invalid("null execute args");
   WB_CUDA(cudaSetDevice(s->device));
   const DeviceDense& d = s->dev;
+  if (s->graph_state == 0 && s->calls >= 1) s->graph_state = build_execute_graph(s).ok() ? 1 : -1;
+  ++s->calls;
+  if (s->graph_state == 1) {
+    const size_t xb = static_cast<size_t>(s->batch) * static_cast<size_t>(d.cols) * 4;
+    const size_t yb = static_cast<size_t>(s->batch) * static_cast<size_t>(d.rows) * 4;
+    std::memcpy(s->x_pin, x, xb);
+    WB_CUDA(cudaGraphLaunch(s->graph, s->stream));
+    WB_CUDA(cudaStreamSynchronize(s->stream));
+    std::memcpy(pre, s->pre_pin, yb);
+    std::memcpy(post, s->post_pin, yb);
+    if (*s->err_pin != 0) {
+      const int e = *s->err_pin;
+      *s->err_pin = 0;
+      WB_CUDA(cudaMemsetAsync(s->io.err, 0, sizeof(int), s->stream));
+      WB_CUDA(cudaStreamSynchronize(s->stream));
+      return Status::Internal("tensor-core pipeline wait timed out (stage code " + std::to_string(e) + ")");
+    }
+    return Status::Ok();
+  }
   WB_CUDA(cudaMemcpy2DAsync(s->io.x, static_cast<size_t>(d.x_stride) * 4, x, static_cast<size_t>(d.cols) * 4,
                             static_cast<size_t>(d.cols) * 4, static_cast<size_t>(s->batch),
                             cudaMemcpyHostToDevice, s->stream));
@@ -442,7 +495,7 @@ Status session_execute_device_noalloc(DenseSession* s, const float* x, float* pr
   const DeviceDense& d = s->dev;
   if (!use_tensor_path(d, s->batch))
     return Status::Unsupported("allocation-free forward serves the batched tensor-core path only "
-                               "(FP8/FP4/Int8 sessions with batch > 4 outside exact mode)");
+                               "(FP8/FP4/Int8 sessions with batch > 8 outside exact mode)");
   WB_CUDA(cudaSetDevice(s->device));
   GemmArgs g;
   g.dtype = d.dtype;
@@ -474,7 +527,7 @@ Status session_execute_group(DenseSession* const* s, int n, const float* const* 
     if (!s[i] || !x[i] || !pre[i] || !post[i]) return Status::Invalid("null group execute args");
   WB_CUDA(cudaSetDevice(s[0]->device));
   const DeviceDense& d0 = s[0]->dev;
-  bool grouped = use_gemv_tc(d0, s[0]->batch);
+  bool grouped = s[0]->batch <= 4 && use_gemv_tc(d0, s[0]->batch);
   for (int i = 1; i < n && grouped; ++i) {
     const DeviceDense& d = s[i]->dev;
     grouped = s[i]->device == s[0]->device && s[i]->batch == s[0]->batch && d.dtype == d0.dtype &&

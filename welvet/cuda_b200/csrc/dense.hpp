@@ -11,6 +11,7 @@
 #pragma once
 
 #include "common.hpp"
+#include "gemv_tc.hpp"
 
 #include <vector>
 
@@ -90,7 +91,7 @@ struct DenseIO {
 // Batched path selection: batches above this size run the tcgen05 GEMM (FP8/FP4/Int8 layers
 // that are not in exact mode); WELVET_B200_BATCHED=gemv keeps every batch on the GEMV.
 bool use_tensor_path(const DeviceDense& d, int batch);
-// Batches of 1..4 on quantized, non-exact layers run the tensor-core GEMV (gemv_tc.hpp);
+// Batches of 1..8 on quantized, non-exact layers run the tensor-core GEMV (gemv_tc.hpp);
 // WELVET_B200_GEMV=simt keeps them on the SIMT GEMV.
 bool use_gemv_tc(const DeviceDense& d, int batch);
 // Number of f16 planes x is split into on the tensor path (WELVET_B200_XSPLIT, default 3).
@@ -112,6 +113,18 @@ struct DenseSession {
   WeightStore store;
   DeviceDense dev;
   DenseIO io;
+  // Host-buffer execute (session_execute): after a first direct call, the device side --
+  // H2D of x from pinned staging, the forward, D2H of pre / post (and of the error word) --
+  // is one CUDA graph replayed per call; the caller's buffers are copied to / from the
+  // staging on the host. `graph_state` 0: not built yet, 1: built, -1: capture failed (the
+  // direct path is used).
+  int calls = 0;
+  int graph_state = 0;
+  cudaGraphExec_t graph = nullptr;
+  float* x_pin = nullptr;
+  float* pre_pin = nullptr;
+  float* post_pin = nullptr;
+  int* err_pin = nullptr;
   ~DenseSession();
 };
 
@@ -133,7 +146,7 @@ Status session_execute_device(DenseSession* s, const float* x, float* pre, float
 Status session_execute_group(DenseSession* const* s, int n, const float* const* x, float* const* pre,
                              float* const* post, cudaStream_t st);
 
-// Same forward for batched sessions (> 4 tokens on the tcgen05 path), with the GEMM's scratch
+// Same forward for batched sessions (> 8 tokens on the tcgen05 path), with the GEMM's scratch
 // in the library's fixed static device array: no allocation of any kind.
 Status session_execute_device_noalloc(DenseSession* s, const float* x, float* pre, float* post,
                                       cudaStream_t st);

@@ -1,6 +1,6 @@
 // gemv_tc.cu -- small-batch dequant GEMV on the tensor cores' register path (sm_100a).
 //
-// Replaces, for 1..4 tokens, the reference's dense_matvec_f64_batch + dense_bias_act
+// Replaces, for 1..8 tokens, the reference's dense_matvec_f64_batch + dense_bias_act
 // (src/cuda/kernels.cu:130-161) over a host-decoded fp64 W. It streams the packed codes once:
 //
 //  * Weights come from a fragment-tiled mirror: one 16-byte load per lane and row group
@@ -10,7 +10,8 @@
 //  * x is split per token into two f16 planes after scaling by a power of two chosen from
 //    the CTA's own K range (x * 2^e = h0 + h1, 22 significant bits); the planes sit in the
 //    MMA's N columns (n = 2 * token + plane), so each thread's D fragment holds both planes of
-//    one token. The CTA's 128 threads build these B fragments once into shared memory.
+//    one token. Up to 4 tokens fill one n8 tile; 5..8 tokens use two, and each converted A
+//    fragment then feeds two MMAs. The CTA's 128 threads build these B fragments once into shared memory.
 //    Products are exact, accumulation is fp32 within a chunk and fp64 across chunks, warps
 //    and CTAs: |y - y_fp64| <= ~2^-22 * sum_k |W x| before the final rounding.
 //  * A CTA owns 64 rows x a K range, its 4 warps a quarter each. All of a warp's weight
@@ -26,6 +27,10 @@
 #include "codec.cuh"
 
 #include <cooperative_groups.h>
+
+#include <mutex>
+#include <tuple>
+#include <vector>
 
 namespace wb {
 namespace {
@@ -199,7 +204,7 @@ struct GroupArgs {
 };
 
 template <int kDt, int kB, bool kDual, int kL>
-__global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : 4) k_gemv_tc(const __grid_constant__ GroupArgs<kL> ga) {
+__global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_gemv_tc(const __grid_constant__ GroupArgs<kL> ga) {
   KArgs a = ga.a;
   if constexpr (kL > 1) {
     const GemvGroupLayer& L = ga.layer[blockIdx.z];
@@ -215,6 +220,7 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : 4) k_gemv_tc(const __
   constexpr int KBPU = kDt == 16 ? 4 : 2;       // K blocks of 16 per unit
   constexpr int CK = 2 * KBPU * 16;             // K elements per chunk
   constexpr int NCOL = 2 * kB;                  // B columns in use: n = 2 * token + plane
+  constexpr int NT = (NCOL + 7) / 8;            // n8 tiles per A fragment (tokens 4 nt .. 4 nt + 3)
   __shared__ double red[kWarps][kRowsPerSet][kDual ? 2 : 1][kB];
   __shared__ double cta_part[kRowsPerSet][kDual ? 2 : 1][kB];
   __shared__ float smax[kWarps][kB];
@@ -306,48 +312,62 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : 4) k_gemv_tc(const __
   }
   __syncthreads();
 
-  float sinv_t = 0.0f;
+  // thread (g, t) holds, in n tile nt, both planes of token 4 nt + t for rows g and g + 8
+  float sinv_t[NT];
 #pragma unroll
-  for (int b = 0; b < kB; ++b)
-    if (t == b) sinv_t = sinv[b];
-  const bool col_active = g < NCOL;
+  for (int nt = 0; nt < NT; ++nt) {
+    sinv_t[nt] = 0.0f;
+#pragma unroll
+    for (int b = 0; b < kB; ++b)
+      if (4 * nt + t == b) sinv_t[nt] = sinv[b];
+  }
 
-  double acc[kRG][2], acc2[kRG][2];
+  double acc[kRG][2][NT], acc2[kRG][2][NT];
 
   auto compute_chunk = [&](int64_t c, const uint4 (&buf)[2][kRG], const uint4 (&buf2)[2][kRG]) {
-    float d[kRG][4], d2[kRG][4];
+    float d[kRG][NT][4], d2[kRG][NT][4];
 #pragma unroll
     for (int r = 0; r < kRG; ++r)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) d[r][i] = d2[r][i] = 0.0f;
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) d[r][nt][i] = d2[r][nt][i] = 0.0f;
     const int kb_base = static_cast<int>(c - cta_c0) * 2 * KBPU;
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
 #pragma unroll
       for (int j = 0; j < KBPU; ++j) {
-        uint2 bf = make_uint2(0u, 0u);
-        if (col_active) bf = frag[((kb_base + u * KBPU + j) * NCOL + g) * 4 + t];
+        uint2 bf[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int col = 8 * nt + g;
+          bf[nt] = col < NCOL ? frag[((kb_base + u * KBPU + j) * NCOL + col) * 4 + t] : make_uint2(0u, 0u);
+        }
 #pragma unroll
         for (int r = 0; r < kRG; ++r) {
           uint32_t af[4];
           a_frag<kDt>(buf[u][r], j, af);
-          mma16816(d[r], af, bf.x, bf.y);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) mma16816(d[r][nt], af, bf[nt].x, bf[nt].y);
           if (kDual) {
             a_frag<kDt>(buf2[u][r], j, af);
-            mma16816(d2[r], af, bf.x, bf.y);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) mma16816(d2[r][nt], af, bf[nt].x, bf[nt].y);
           }
         }
       }
     }
 #pragma unroll
-    for (int r = 0; r < kRG; ++r) {
-      acc[r][0] += (static_cast<double>(d[r][0]) + static_cast<double>(d[r][1])) * sinv_t;
-      acc[r][1] += (static_cast<double>(d[r][2]) + static_cast<double>(d[r][3])) * sinv_t;
-      if (kDual) {
-        acc2[r][0] += (static_cast<double>(d2[r][0]) + static_cast<double>(d2[r][1])) * sinv_t;
-        acc2[r][1] += (static_cast<double>(d2[r][2]) + static_cast<double>(d2[r][3])) * sinv_t;
+    for (int r = 0; r < kRG; ++r)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        acc[r][0][nt] += (static_cast<double>(d[r][nt][0]) + static_cast<double>(d[r][nt][1])) * sinv_t[nt];
+        acc[r][1][nt] += (static_cast<double>(d[r][nt][2]) + static_cast<double>(d[r][nt][3])) * sinv_t[nt];
+        if (kDual) {
+          acc2[r][0][nt] += (static_cast<double>(d2[r][nt][0]) + static_cast<double>(d2[r][nt][1])) * sinv_t[nt];
+          acc2[r][1][nt] += (static_cast<double>(d2[r][nt][2]) + static_cast<double>(d2[r][nt][3])) * sinv_t[nt];
+        }
       }
-    }
   };
 
   namespace cg = cooperative_groups;
@@ -356,7 +376,9 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : 4) k_gemv_tc(const __
   for (; rs < nrs; rs += gridDim.y) {
     const int64_t rg0 = rs * kRG;
 #pragma unroll
-    for (int r = 0; r < kRG; ++r) acc[r][0] = acc[r][1] = acc2[r][0] = acc2[r][1] = 0.0;
+    for (int r = 0; r < kRG; ++r)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) acc[r][0][nt] = acc[r][1][nt] = acc2[r][0][nt] = acc2[r][1][nt] = 0.0;
   // chunk c sits in bufA when c - c0 is even, in bufB when odd; the chunk two ahead is
   // requested as soon as its buffer is free.
   for (int64_t c = c0; c < c1; c += 2) {
@@ -374,14 +396,18 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : 4) k_gemv_tc(const __
   }
 
   // ---- CTA reduction over its 4 K slices (fixed order)
-  if (t < kB) {
 #pragma unroll
-    for (int r = 0; r < kRG; ++r) {
-      red[warp][r * 16 + g][0][t] = acc[r][0];
-      red[warp][r * 16 + g + 8][0][t] = acc[r][1];
-      if (kDual) {
-        red[warp][r * 16 + g][kDual ? 1 : 0][t] = acc2[r][0];
-        red[warp][r * 16 + g + 8][kDual ? 1 : 0][t] = acc2[r][1];
+  for (int nt = 0; nt < NT; ++nt) {
+    const int tok = 4 * nt + t;
+    if (tok < kB) {
+#pragma unroll
+      for (int r = 0; r < kRG; ++r) {
+        red[warp][r * 16 + g][0][tok] = acc[r][0][nt];
+        red[warp][r * 16 + g + 8][0][tok] = acc[r][1][nt];
+        if (kDual) {
+          red[warp][r * 16 + g][kDual ? 1 : 0][tok] = acc2[r][0][nt];
+          red[warp][r * 16 + g + 8][kDual ? 1 : 0][tok] = acc2[r][1][nt];
+        }
       }
     }
   }
@@ -458,6 +484,27 @@ __global__ void k_build_tiled(const uint8_t* __restrict__ native, int rows, int 
   }
 }
 
+// The 48 KB default covers static + dynamic shared memory together, so every launch opts in
+// to its dynamic size (the reduction arrays are static). One driver call per kernel, device
+// and size, cached.
+Status allow_dynamic_smem(const void* kern, size_t bytes) {
+  static std::mutex mu;
+  static std::vector<std::tuple<const void*, int, size_t>> done;
+  int dev = 0;
+  WB_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& d : done)
+    if (std::get<0>(d) == kern && std::get<1>(d) == dev && std::get<2>(d) >= bytes) return Status::Ok();
+  WB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)));
+  for (auto& d : done)
+    if (std::get<0>(d) == kern && std::get<1>(d) == dev) {
+      std::get<2>(d) = bytes;
+      return Status::Ok();
+    }
+  done.emplace_back(kern, dev, bytes);
+  return Status::Ok();
+}
+
 template <int kDt, int kB, bool kDual, int kL>
 Status launch_t(const GroupArgs<kL>& k, int nl, const Plan& pl, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
@@ -482,8 +529,7 @@ Status launch_t(const GroupArgs<kL>& k, int nl, const Plan& pl, cudaStream_t st,
   cfg.attrs = attr;
   cfg.numAttrs = n;
   auto kern = k_gemv_tc<kDt, kB, kDual, kL>;
-  if (cfg.dynamicSmemBytes > 48 * 1024)
-    WB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(cfg.dynamicSmemBytes)));
+  WB_TRY(allow_dynamic_smem(reinterpret_cast<const void*>(kern), cfg.dynamicSmemBytes));
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, k), "gemv_tc launch");
 }
 
@@ -494,7 +540,17 @@ Status launch_b(const GroupArgs<kL>& k, int nl, const Plan& pl, int batch, cudaS
   case 2: return launch_t<kDt, 2, kDual, kL>(k, nl, pl, st, pdl);
   case 3: return launch_t<kDt, 3, kDual, kL>(k, nl, pl, st, pdl);
   case 4: return launch_t<kDt, 4, kDual, kL>(k, nl, pl, st, pdl);
-  default: return Status::Internal("gemv_tc: batch must be 1..4");
+  default:
+    if constexpr (!kDual && kL == 1) {
+      switch (batch) {
+      case 5: return launch_t<kDt, 5, false, 1>(k, nl, pl, st, pdl);
+      case 6: return launch_t<kDt, 6, false, 1>(k, nl, pl, st, pdl);
+      case 7: return launch_t<kDt, 7, false, 1>(k, nl, pl, st, pdl);
+      case 8: return launch_t<kDt, 8, false, 1>(k, nl, pl, st, pdl);
+      default: break;
+      }
+    }
+    return Status::Internal("gemv_tc: batch must be 1..8 (1..4 for the fused Gate/Up and grouped launches)");
   }
 }
 
@@ -542,7 +598,8 @@ Status build_tiled_mirror(DType dt, const uint8_t* native, int rows, int cols, u
 
 Status launch_gemv_tc(const GemvTcArgs& a, cudaStream_t st, bool pdl) {
   if (!gemv_tc_supported(a.dtype)) return Status::Unsupported("gemv_tc: dtype");
-  if (a.rows <= 0 || a.cols <= 0 || a.batch < 1 || a.batch > 4) return Status::Invalid("gemv_tc: bad dims");
+  if (a.rows <= 0 || a.cols <= 0 || a.batch < 1 || a.batch > (a.Wt2 ? 4 : kGemvMaxBatch))
+    return Status::Invalid("gemv_tc: bad dims");
   const Plan pl = make_plan(a.dtype, a.rows, a.cols);
   KArgs k{};
   k.Wt = a.Wt;

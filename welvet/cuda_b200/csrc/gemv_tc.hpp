@@ -1,4 +1,4 @@
-// gemv_tc.hpp -- small-batch (1..4 tokens) dequant GEMV on the tensor cores' register path.
+// gemv_tc.hpp -- small-batch (1..8 tokens) dequant GEMV on the tensor cores' register path.
 #pragma once
 
 #include "common.hpp"
@@ -21,6 +21,10 @@ bool gemv_tc_supported(DType dt);
 // Build the tiled mirror from reference-layout native bytes (FP8 codes canonicalised).
 Status build_tiled_mirror(DType dt, const uint8_t* native, int rows, int cols, uint8_t* tiled, cudaStream_t st);
 
+// Tokens per launch: up to 8 for one layer (two n8 tiles of x per A fragment), up to 4 for
+// the fused Gate/Up (SwiGLU) form and for grouped launches.
+constexpr int kGemvMaxBatch = 8;
+
 struct GemvTcArgs {
   DType dtype = DType::FP4;
   const uint8_t* Wt = nullptr;   // tiled mirror
@@ -29,7 +33,7 @@ struct GemvTcArgs {
   float scale = 1.0f, scale2 = 1.0f;  // Int8 per-tensor scales
   const float* x = nullptr;      // [batch][x_ld], any alignment
   int64_t x_ld = 0;
-  int batch = 1;                 // 1..4
+  int batch = 1;                 // 1..8 (1..4 with Wt2)
   float* pre = nullptr;          // [batch][ld_out]  (SwiGLU: h)
   float* post = nullptr;
   int64_t ld_out = 0;
