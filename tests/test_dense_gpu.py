@@ -202,30 +202,57 @@ def test_execute_device_matches_host(wb, oracle):
     s2.release()
 
 
-@pytest.mark.parametrize("dt,batch", [(16, 1), (4, 3), (16, 24)])
-def test_host_execute_graph_replay(wb, oracle, dt, batch, monkeypatch):
-    """welvet_dense_execute: the first call runs directly, later calls replay the session's
-    recorded graph over pinned staging buffers -- every call's outputs equal a direct
+def _pinned_like(a):
+    import torch
+    t = torch.empty(a.shape, dtype=torch.float32).pin_memory()
+    v = t.numpy()
+    v[...] = a
+    return t, v
+
+
+@pytest.mark.parametrize("pinned", [False, True], ids=["pageable", "pinned"])
+@pytest.mark.parametrize("dt,batch,in_,exact", [(16, 1, 1024, "0"), (4, 3, 1024, "0"), (16, 24, 1024, "0"),
+                                                (9, 2, 1001, "0"), (5, 2, 1001, "1"), (16, 12, 333, "0")])
+def test_host_execute_graph_replay(wb, oracle, dt, batch, in_, exact, pinned, monkeypatch):
+    """welvet_dense_execute: the first call runs directly (copy-engine transfers), later calls
+    replay a graph over mapped staging (pageable caller buffers) or over the pinned caller
+    buffers themselves (one graph per buffer triple) -- every call's outputs equal a direct
     computation of the same input bit for bit, whatever ran before."""
-    monkeypatch.setenv("WELVET_B200_EXACT", "0")
-    rng = np.random.default_rng(77 + batch)
-    out, in_ = 640, 1024
+    monkeypatch.setenv("WELVET_B200_EXACT", exact)
+    rng = np.random.default_rng(77 + batch + in_)
+    out = 640 if in_ == 1024 else 200
     w = (rng.standard_normal((out, in_)) * 2.0).astype(np.float32)
     bias = rng.standard_normal(out)
     xs = [rng.standard_normal((batch, in_)).astype(np.float32) for _ in range(3)]
     s = wb.DenseSession(w, batch, dt, wb.RELU, bias)
-    got = [s.execute(x) for x in (xs[0], xs[1], xs[2], xs[0], xs[1])]
+    # pinned: five buffer triples, reused with new contents (graph hits) and past the four
+    # graphs a session keeps (eviction and re-recording)
+    seq_x, seq_buf = (0, 1, 2, 0, 1, 2, 0, 1), (0, 1, 2, 3, 4, 0, 4, 1)
+    bufs = [tuple(_pinned_like(np.zeros(shape, np.float32)) for shape in ((batch, in_), (batch, out), (batch, out)))
+            for _ in range(5)]
+
+    def call(i, b):
+        if not pinned:
+            return s.execute(xs[i])
+        (_, vx), (_, vp), (_, vq) = bufs[b]
+        vx[...] = xs[i]
+        vp[...] = np.nan
+        vq[...] = np.nan
+        s.execute(vx, vp, vq)
+        return vp.copy(), vq.copy()
+
+    got = [call(i, b) for i, b in zip(seq_x, seq_buf)]
     s.release()
     for i, x in enumerate((xs[0], xs[1], xs[2])):
         fresh = wb.DenseSession(w, batch, dt, wb.RELU, bias)
         ref_pre, ref_post = fresh.execute(x)  # a first call: the direct path
         fresh.release()
-        for j in [k for k, y in enumerate((0, 1, 2, 0, 1)) if y == i]:
+        for j in [k for k, y in enumerate(seq_x) if y == i]:
             assert np.array_equal(got[j][0].view(np.uint32), ref_pre.view(np.uint32)), (i, j)
             assert np.array_equal(got[j][1].view(np.uint32), ref_post.view(np.uint32)), (i, j)
     raw, sc = oracle.pack(dt, w)
     ref = oracle.dense_forward(dt, raw, sc, xs[2], in_, out, wb.RELU, bias)
-    if batch <= 8:  # tensor GEMV bound
+    if batch <= 8:  # GEMV bound (the exact SIMT path is far inside it)
         check_dense(got[2][0], got[2][1], ref, wb.RELU, "graph replay")
     else:  # tcgen05 GEMM bound
         err = np.abs(got[2][0].astype(np.float64) - ref[0].astype(np.float64)) - 2 * ulp(ref[0])

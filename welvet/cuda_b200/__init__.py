@@ -110,11 +110,25 @@ def check(st: welvet_status) -> None:
 
 
 def _np_ptr(a):
-    return None if a is None else a.ctypes.data_as(c_void_p)
+    # the array interface's address is far cheaper than ndarray.ctypes on a per-call path
+    return None if a is None else a.__array_interface__["data"][0]
 
 
 def _f32(a) -> np.ndarray:
+    if type(a) is np.ndarray and a.dtype == np.float32 and a.flags.c_contiguous:
+        return a
     return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _out_f32(a, n: int, shape, what: str) -> np.ndarray:
+    """A caller-supplied output array (written in place by the library) or a new one."""
+    if a is None:
+        return np.zeros(shape, np.float32)
+    if not (type(a) is np.ndarray and a.dtype == np.float32 and a.flags.c_contiguous and a.flags.writeable):
+        raise ValueError(f"{what}: expected a writable C-contiguous float32 array")
+    if a.size != n:
+        raise ValueError(f"{what}: expected {n} elements, got {a.size}")
+    return a
 
 
 def _dev_ptr(t) -> int:
@@ -187,12 +201,17 @@ class DenseSession:
         self.batch, self.in_, self.out, self.dtype = batch, in_, out, dtype
 
     def execute(self, x: np.ndarray, pre: np.ndarray | None = None, post: np.ndarray | None = None):
+        """welvet_dense_execute: x holds batch x in floats; pre / post (batch x out floats, written
+        in place; allocated when None) receive the pre-activation and the output."""
         x = _f32(x)
-        if pre is None:
-            pre = np.zeros((self.batch, self.out), np.float32)
-        if post is None:
-            post = np.zeros((self.batch, self.out), np.float32)
-        check(_L.welvet_dense_execute(self._h, _np_ptr(x), _np_ptr(pre), _np_ptr(post)))
+        if x.size != self.batch * self.in_:
+            raise ValueError(f"execute: x has {x.size} elements, the session takes {self.batch} x {self.in_}")
+        n = self.batch * self.out
+        pre = _out_f32(pre, n, (self.batch, self.out), "pre")
+        post = _out_f32(post, n, (self.batch, self.out), "post")
+        st = _L.welvet_dense_execute(self._h, _np_ptr(x), _np_ptr(pre), _np_ptr(post))
+        if st.code != OK:
+            raise WelvetError(st.code, st.message.decode(errors="replace"))
         return pre, post
 
     def execute_device(self, x, pre, post, stream=None) -> None:

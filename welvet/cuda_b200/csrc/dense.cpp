@@ -283,8 +283,10 @@ Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x
     g.act = d.act;
     return launch_gemv_tc(g, st, pdl_in);
   }
-  // The SIMT GEMV reads x in 16-byte vectors over the padded row: stage unpadded inputs.
-  const bool direct = d.cols == d.x_stride && x_ld == d.cols && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  // The SIMT GEMV reads x in 16-byte vectors over the padded row: stage unpadded inputs (the
+  // session's own staging rows keep zero pads).
+  const bool own = io && x == io->x && x_ld == d.x_stride && io->batch >= batch;
+  const bool direct = own || (d.cols == d.x_stride && x_ld == d.cols && (reinterpret_cast<uintptr_t>(x) & 15) == 0);
   if (!direct) {
     if (!io || !io->x || io->batch < batch) return Status::Internal("dense: no staging buffer for this batch");
     WB_CUDA(cudaMemcpy2DAsync(io->x, static_cast<size_t>(d.x_stride) * 4, x, static_cast<size_t>(x_ld) * 4,
@@ -318,6 +320,7 @@ DenseSession::~DenseSession() {
   cudaSetDevice(device);
   if (stream) cudaStreamSynchronize(stream);
   if (graph) cudaGraphExecDestroy(graph);
+  for (auto& g : caller_graphs) cudaGraphExecDestroy(g.exec);
   for (void* p : {static_cast<void*>(x_pin), static_cast<void*>(pre_pin), static_cast<void*>(post_pin),
                   static_cast<void*>(err_pin)})
     if (p) cudaFreeHost(p);
@@ -414,57 +417,137 @@ Status session_mount_native(int32_t batch, int32_t in, int32_t out, int32_t act,
 }
 
 namespace {
-// Records the host-buffer forward of `s` as a graph over its pinned staging buffers.
-Status build_execute_graph(DenseSession* s) {
+// The device side of a host-buffer forward over device-accessible host memory (mapped pinned
+// buffers), moving no data with copy-engine transfers: a staging kernel reads x over the bus
+// with all its loads in flight at once into the session's padded x (a GEMV, launched as its
+// programmatic dependent, streams its weights meanwhile); the epilogues store pre / post
+// straight into host memory. Only the GEMM pipeline's error word is copied back (4 bytes, to
+// err_pin).
+Status enqueue_mapped_execute(DenseSession* s, const float* x_dev, float* pre_dev, float* post_dev) {
   const DeviceDense& d = s->dev;
-  const size_t xb = static_cast<size_t>(s->batch) * static_cast<size_t>(d.cols) * 4;
-  const size_t yb = static_cast<size_t>(s->batch) * static_cast<size_t>(d.rows) * 4;
-  WB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&s->x_pin), xb, cudaHostAllocDefault));
-  WB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&s->pre_pin), yb, cudaHostAllocDefault));
-  WB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&s->post_pin), yb, cudaHostAllocDefault));
-  WB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&s->err_pin), sizeof(int), cudaHostAllocDefault));
-  *s->err_pin = 0;
+  WB_TRY(launch_stage_rows(s->io.x, d.x_stride, x_dev, d.cols, d.cols, s->batch, s->stream));
+  WB_TRY(forward_device(d, s->batch, s->io.x, d.x_stride, pre_dev, post_dev, &s->io, s->stream, true));
+  if (s->io.err && s->io.scratch)
+    WB_CUDA(cudaMemcpyAsync(s->err_pin, s->io.err, sizeof(int), cudaMemcpyDeviceToHost, s->stream));
+  return Status::Ok();
+}
+
+// Records enqueue_mapped_execute over the given device addresses as a graph.
+Status record_execute_graph(DenseSession* s, const float* x_dev, float* pre_dev, float* post_dev,
+                            cudaGraphExec_t* exec) {
   cudaGraph_t g = nullptr;
   WB_CUDA(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
-  Status st = cuda_status(cudaMemcpy2DAsync(s->io.x, static_cast<size_t>(d.x_stride) * 4, s->x_pin,
-                                            static_cast<size_t>(d.cols) * 4, static_cast<size_t>(d.cols) * 4,
-                                            static_cast<size_t>(s->batch), cudaMemcpyHostToDevice, s->stream),
-                          "capture h2d");
-  if (st.ok()) st = forward_device(d, s->batch, s->io.x, d.x_stride, s->io.pre, s->io.post, &s->io, s->stream, false);
-  if (st.ok()) st = cuda_status(cudaMemcpyAsync(s->pre_pin, s->io.pre, yb, cudaMemcpyDeviceToHost, s->stream), "capture d2h");
-  if (st.ok()) st = cuda_status(cudaMemcpyAsync(s->post_pin, s->io.post, yb, cudaMemcpyDeviceToHost, s->stream), "capture d2h");
-  if (st.ok() && s->io.err && s->io.scratch)
-    st = cuda_status(cudaMemcpyAsync(s->err_pin, s->io.err, sizeof(int), cudaMemcpyDeviceToHost, s->stream), "capture d2h");
+  Status st = enqueue_mapped_execute(s, x_dev, pre_dev, post_dev);
   const cudaError_t end = cudaStreamEndCapture(s->stream, &g);
   if (st.ok()) st = cuda_status(end, "end capture");
-  if (st.ok()) st = cuda_status(cudaGraphInstantiate(&s->graph, g, 0), "graph instantiate");
+  if (st.ok()) st = cuda_status(cudaGraphInstantiate(exec, g, 0), "graph instantiate");
   if (g) cudaGraphDestroy(g);
   cudaGetLastError();  // a failed capture leaves nothing pending for the direct path
   return st;
 }
+
+// Allocates the session's mapped staging and records the graph over it.
+Status build_execute_graph(DenseSession* s) {
+  const DeviceDense& d = s->dev;
+  const size_t xb = static_cast<size_t>(s->batch) * static_cast<size_t>(d.cols) * 4;
+  const size_t yb = static_cast<size_t>(s->batch) * static_cast<size_t>(d.rows) * 4;
+  WB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&s->x_pin), xb, cudaHostAllocMapped));
+  WB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&s->pre_pin), yb, cudaHostAllocMapped));
+  WB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&s->post_pin), yb, cudaHostAllocMapped));
+  WB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&s->err_pin), sizeof(int), cudaHostAllocMapped));
+  *s->err_pin = 0;
+  float *x_dev = nullptr, *pre_dev = nullptr, *post_dev = nullptr;
+  WB_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&x_dev), s->x_pin, 0));
+  WB_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&pre_dev), s->pre_pin, 0));
+  WB_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&post_dev), s->post_pin, 0));
+  return record_execute_graph(s, x_dev, pre_dev, post_dev, &s->graph);
+}
+
+// The graph over pinned caller buffers at these device addresses: a kept one, or a new
+// recording that replaces the least recently used. nullptr when recording fails.
+cudaGraphExec_t caller_graph(DenseSession* s, const float* x_dev, float* pre_dev, float* post_dev) {
+  auto& gs = s->caller_graphs;
+  const uint64_t now = static_cast<uint64_t>(s->calls);
+  for (auto& g : gs)
+    if (g.x == x_dev && g.pre == pre_dev && g.post == post_dev) {
+      g.used = now;
+      return g.exec;
+    }
+  cudaGraphExec_t exec = nullptr;
+  if (!record_execute_graph(s, x_dev, pre_dev, post_dev, &exec).ok()) return nullptr;
+  DenseSession::ExecGraph e;
+  e.x = x_dev;
+  e.pre = pre_dev;
+  e.post = post_dev;
+  e.exec = exec;
+  e.used = now;
+  if (static_cast<int>(gs.size()) < DenseSession::kMaxExecGraphs) {
+    gs.push_back(e);
+  } else {
+    size_t lru = 0;
+    for (size_t i = 1; i < gs.size(); ++i)
+      if (gs[i].used < gs[lru].used) lru = i;
+    cudaGraphExecDestroy(gs[lru].exec);
+    gs[lru] = e;
+  }
+  return exec;
+}
+
+// The address under which the current device reads host buffer p, when p lies in pinned host
+// memory mapped into the device's address space (cudaHostAlloc / cudaHostRegister); nullptr
+// for pageable memory.
+void* mapped_address(const void* p) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
+}
+
+Status finish_mapped_execute(DenseSession* s) {
+  WB_CUDA(cudaStreamSynchronize(s->stream));
+  if (*s->err_pin == 0) return Status::Ok();
+  const int e = *s->err_pin;
+  *s->err_pin = 0;
+  WB_CUDA(cudaMemsetAsync(s->io.err, 0, sizeof(int), s->stream));
+  WB_CUDA(cudaStreamSynchronize(s->stream));
+  return Status::Internal("tensor-core pipeline wait timed out (stage code " + std::to_string(e) + ")");
+}
 } // namespace
+
+// WELVET_B200_EXEC_GRAPH=0 keeps the host-buffer execute on the direct path.
+static bool exec_graph_policy() {
+  const char* env = std::getenv("WELVET_B200_EXEC_GRAPH");
+  return !(env && env[0] == '0');
+}
 
 Status session_execute(DenseSession* s, const float* x, float* pre, float* post) {
   if (!s || !x || !pre || !post) return Status::Invalid("null execute args");
   WB_CUDA(cudaSetDevice(s->device));
   const DeviceDense& d = s->dev;
-  if (s->graph_state == 0 && s->calls >= 1) s->graph_state = build_execute_graph(s).ok() ? 1 : -1;
+  if (s->graph_state == 0 && s->calls >= 1)
+    s->graph_state = exec_graph_policy() && build_execute_graph(s).ok() ? 1 : -1;
   ++s->calls;
   if (s->graph_state == 1) {
+    // Pinned caller buffers are read and written where they lie; others go through the
+    // session's mapped staging and its recorded graph.
+    auto* xd = static_cast<const float*>(mapped_address(x));
+    auto* pd = static_cast<float*>(mapped_address(pre));
+    auto* qd = static_cast<float*>(mapped_address(post));
+    if (xd && pd && qd) {
+      if (cudaGraphExec_t exec = caller_graph(s, xd, pd, qd)) {
+        WB_CUDA(cudaGraphLaunch(exec, s->stream));
+        return finish_mapped_execute(s);
+      }
+    }
     const size_t xb = static_cast<size_t>(s->batch) * static_cast<size_t>(d.cols) * 4;
     const size_t yb = static_cast<size_t>(s->batch) * static_cast<size_t>(d.rows) * 4;
     std::memcpy(s->x_pin, x, xb);
     WB_CUDA(cudaGraphLaunch(s->graph, s->stream));
-    WB_CUDA(cudaStreamSynchronize(s->stream));
+    WB_TRY(finish_mapped_execute(s));
     std::memcpy(pre, s->pre_pin, yb);
     std::memcpy(post, s->post_pin, yb);
-    if (*s->err_pin != 0) {
-      const int e = *s->err_pin;
-      *s->err_pin = 0;
-      WB_CUDA(cudaMemsetAsync(s->io.err, 0, sizeof(int), s->stream));
-      WB_CUDA(cudaStreamSynchronize(s->stream));
-      return Status::Internal("tensor-core pipeline wait timed out (stage code " + std::to_string(e) + ")");
-    }
     return Status::Ok();
   }
   WB_CUDA(cudaMemcpy2DAsync(s->io.x, static_cast<size_t>(d.x_stride) * 4, x, static_cast<size_t>(d.cols) * 4,

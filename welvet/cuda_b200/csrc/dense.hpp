@@ -113,14 +113,22 @@ struct DenseSession {
   WeightStore store;
   DeviceDense dev;
   DenseIO io;
-  // Host-buffer execute (session_execute): after a first direct call, the device side --
-  // H2D of x from pinned staging, the forward, D2H of pre / post (and of the error word) --
-  // is one CUDA graph replayed per call; the caller's buffers are copied to / from the
-  // staging on the host. `graph_state` 0: not built yet, 1: built, -1: capture failed (the
-  // direct path is used).
+  // Host-buffer execute (session_execute): after a first direct call, the device side of a
+  // call is a CUDA graph replayed per call, recorded over device-accessible host memory: the
+  // caller's own buffers when they are pinned (one graph per buffer triple, the most recent
+  // kMaxExecGraphs kept), else the session's mapped staging, to and from which the caller's
+  // buffers are copied on the host. `graph_state` 0: not built yet, 1: built, -1: capture
+  // failed (the direct path is used).
+  struct ExecGraph {
+    const void *x = nullptr, *pre = nullptr, *post = nullptr;  // device addresses recorded
+    cudaGraphExec_t exec = nullptr;
+    uint64_t used = 0;
+  };
+  static constexpr int kMaxExecGraphs = 4;
   int calls = 0;
   int graph_state = 0;
-  cudaGraphExec_t graph = nullptr;
+  cudaGraphExec_t graph = nullptr;      // over the staging buffers
+  std::vector<ExecGraph> caller_graphs;  // over pinned caller buffers
   float* x_pin = nullptr;
   float* pre_pin = nullptr;
   float* post_pin = nullptr;

@@ -342,6 +342,42 @@ Status launch_d(const GemvArgs& a, cudaStream_t st, bool pdl) {
 
 } // namespace
 
+namespace {
+__global__ void __launch_bounds__(256) k_stage_rows(float* __restrict__ dst, int64_t dst_ld,
+                                                    const float* __restrict__ src, int64_t src_ld, int cols,
+                                                    int rows, bool vec) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  if (vec) {  // 16-byte rows: cols, both leading dimensions and both bases multiples of 4 floats
+    const int c4 = cols >> 2;
+    const int64_t n = static_cast<int64_t>(rows) * c4;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+      const int64_t r = i / c4, c = (i - r * c4) << 2;
+      *reinterpret_cast<float4*>(dst + r * dst_ld + c) = *reinterpret_cast<const float4*>(src + r * src_ld + c);
+    }
+  } else {
+    const int64_t n = static_cast<int64_t>(rows) * cols;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+      const int64_t r = i / cols, c = i - r * cols;
+      dst[r * dst_ld + c] = src[r * src_ld + c];
+    }
+  }
+}
+} // namespace
+
+Status launch_stage_rows(float* dst, int64_t dst_ld, const float* src, int64_t src_ld, int cols, int rows,
+                         cudaStream_t st) {
+  if (!dst || !src || cols <= 0 || rows <= 0 || dst_ld < cols || src_ld < cols)
+    return Status::Invalid("stage rows: bad arguments");
+  const bool vec = (cols & 3) == 0 && (dst_ld & 3) == 0 && (src_ld & 3) == 0 &&
+                   ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0;
+  const int64_t units = static_cast<int64_t>(rows) * (vec ? cols / 4 : cols);
+  int64_t blocks = (units + 255) / 256;
+  if (blocks > 4 * 148) blocks = 4 * 148;
+  k_stage_rows<<<static_cast<int>(blocks), 256, 0, st>>>(dst, dst_ld, src, src_ld, cols, rows, vec);
+  return cuda_status(cudaGetLastError(), "stage rows launch");
+}
+
 Status launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
   if (a.rows <= 0 || a.cols <= 0 || a.batch <= 0) return Status::Invalid("gemv: bad dims");
   if (a.row_stride % 16 != 0) return Status::Internal("gemv: row stride must be a multiple of 16");

@@ -43,4 +43,11 @@ inline int elems_per_16B(DType dt) {
 // griddepcontrol.wait and reads x / writes outputs after it.
 Status launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl);
 
+// Copies `rows` rows of `cols` floats from src (leading dimension src_ld, any memory the device
+// can read, mapped pinned host memory included) into dst (leading dimension dst_ld); the pad
+// columns of dst are left as they are. The kernel releases its dependents at once, so a
+// following launch made with pdl=true starts streaming its weights while x is in flight.
+Status launch_stage_rows(float* dst, int64_t dst_ld, const float* src, int64_t src_ld, int cols, int rows,
+                         cudaStream_t st);
+
 } // namespace wb
