@@ -13,7 +13,7 @@ flush needed. The same 64 layers run as a dependent chain are reported under "ch
            welvet_b200_dense_execute_group_device, i.e. the tensor-core GEMV kernel over
            32 layers per launch (blockIdx.z = layer), two launches per step
   e2e      the same metric through the reference-facing C ABI welvet_dense_execute, host
-           buffers (pinned), H2D of x and D2H of pre/post inside the timed region, one
+           buffers (pinned), x in and pre/post out over the bus inside the timed region, one
            synchronous call per layer
   branches the same 64 forwards as 64 single-layer launches on 8 graph branches
   chain    the same 64 layers as a dependent chain (layer i's post is layer i+1's x)
@@ -29,6 +29,7 @@ kernels.cu:130-161 with the reference decode), the only CPU implementation of th
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -320,14 +321,22 @@ def run_ours(args):
     xh = torch.randn((1, IN)).pin_memory()
     bufs = [torch.zeros((1, OUT)).pin_memory() for _ in range(2)]
     preh = torch.zeros((1, OUT)).pin_memory()
-    xh_np, bufs_np, preh_np = xh.numpy(), [b.numpy() for b in bufs], preh.numpy()
     e2e_steps = max(1, min(args.steps, 20))
+    # The C ABI itself, as a cgo / FFI caller of the reference binds it: arguments prepared
+    # once, the status checked on every call.
+    c_execute = W.lib().welvet_dense_execute
+    handles = [s._h for s in sessions]
+    p_x, p_pre = ctypes.c_void_p(xh.data_ptr()), ctypes.c_void_p(preh.data_ptr())
+    p_post = [ctypes.c_void_p(b.data_ptr()) for b in bufs]
 
     def e2e_step():
-        # welvet_dense_execute on each of the 64 layers: H2D x, forward, D2H pre and post,
-        # synchronize -- the reference's resident-session contract and --bench loop.
-        for i, s in enumerate(sessions):
-            s.execute(xh_np, preh_np, bufs_np[i & 1])
+        # welvet_dense_execute on each of the 64 layers: x in from host memory, forward, pre
+        # and post out to host memory, synchronize -- the reference's resident-session
+        # contract and --bench loop.
+        for i, h in enumerate(handles):
+            st = c_execute(h, p_x, p_pre, p_post[i & 1])
+            if st.code != 0:
+                raise W.WelvetError(st.code, st.message.decode(errors="replace"))
 
     for _ in range(2):
         e2e_step()
@@ -373,7 +382,7 @@ def run_ours(args):
                 "cpu_baseline": cpu,
                 "e2e": {"value": e2e_val, "unit": "GB/s", "h2d_bytes_per_step": LAYERS * IN * 4,
                         "d2h_bytes_per_step": LAYERS * OUT * 4 * 2, "steps": e2e_steps,
-                        "api": "welvet_dense_execute (host pinned buffers, synchronous per layer)"},
+                        "api": "welvet_dense_execute via ctypes (host pinned buffers, synchronous per layer)"},
                 "branches": {"value": branches_val, "unit": "GB/s", "ms_per_step": ms_br / args.steps,
                              "what": "the same 64 forwards as 64 single-layer launches on 8 CUDA-graph branches"},
                 "chain": {"value": chain_val, "unit": "GB/s", "ms_per_step": ms_chain / args.steps,

@@ -15,7 +15,8 @@ from ctypes import POINTER, byref, c_char, c_double, c_float, c_int32, c_int64, 
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libwelvet_b200.so")
+# WELVET_B200_LIB names another build of the library to load instead of the in-tree one.
+LIB_PATH = os.environ.get("WELVET_B200_LIB") or os.path.join(HERE, "libwelvet_b200.so")
 
 # DType ids (reference include/welvet/dtype.hpp:9-44) served on the GPU.
 FLOAT32, FP8E4M3, FP8E5M2, INT8, FP4 = 1, 4, 5, 9, 16
@@ -109,13 +110,23 @@ def check(st: welvet_status) -> None:
         raise WelvetError(st.code, st.message.decode(errors="replace"))
 
 
+_F32 = np.dtype(np.float32)
+
+
 def _np_ptr(a):
-    # the array interface's address is far cheaper than ndarray.ctypes on a per-call path
-    return None if a is None else a.__array_interface__["data"][0]
+    """Address of an array's data. A ctypes view of a writable buffer is several times cheaper
+    than ndarray.ctypes or the array interface on a per-call path; read-only arrays take the
+    slower route."""
+    if a is None:
+        return None
+    try:
+        return ctypes.addressof(c_char.from_buffer(a))
+    except (TypeError, ValueError):
+        return a.ctypes.data
 
 
 def _f32(a) -> np.ndarray:
-    if type(a) is np.ndarray and a.dtype == np.float32 and a.flags.c_contiguous:
+    if type(a) is np.ndarray and a.dtype is _F32 and a.flags.c_contiguous:
         return a
     return np.ascontiguousarray(a, dtype=np.float32)
 
@@ -124,7 +135,7 @@ def _out_f32(a, n: int, shape, what: str) -> np.ndarray:
     """A caller-supplied output array (written in place by the library) or a new one."""
     if a is None:
         return np.zeros(shape, np.float32)
-    if not (type(a) is np.ndarray and a.dtype == np.float32 and a.flags.c_contiguous and a.flags.writeable):
+    if not (type(a) is np.ndarray and a.dtype is _F32 and a.flags.c_contiguous and a.flags.writeable):
         raise ValueError(f"{what}: expected a writable C-contiguous float32 array")
     if a.size != n:
         raise ValueError(f"{what}: expected {n} elements, got {a.size}")

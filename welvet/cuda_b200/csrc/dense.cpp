@@ -65,6 +65,7 @@ void DenseIO::release() {
   free_dev(post);
   free_dev(scratch);
   free_dev(err);
+  free_dev(prep);
   scratch_bytes = 0;
   batch = 0;
 }
@@ -231,6 +232,9 @@ Status alloc_io(const DeviceDense& d, int batch, DenseIO* io, cudaStream_t st) {
   if (use_tensor_path(d, batch)) {
     io->scratch_bytes = gemm_scratch_bytes(batch, d.cols, d.rows, xsplit_policy());
     WB_CUDA(cudaMalloc(&io->scratch, io->scratch_bytes));
+  }
+  if (use_gemv_tc(d, batch)) {
+    if (const size_t pb = gemv_group_prep_bytes(d.dtype, d.rows, d.cols, batch)) WB_CUDA(cudaMalloc(&io->prep, pb));
   }
   return Status::Ok();
 }
@@ -632,6 +636,7 @@ Status session_execute_group(DenseSession* const* s, int n, const float* const* 
     L.bias_len = d.bias_len;
     L.act = d.act;
     L.scale = d.scale;
+    L.prep = s[i]->io.prep;  // one session's layer at a time: its scratch is free
   }
   return launch_gemv_tc_group(d0.dtype, d0.rows, d0.cols, s[0]->batch, d0.cols, d0.rows, layers.data(), n, st,
                               true);

@@ -85,6 +85,7 @@ struct DenseIO {
   void* scratch = nullptr;  // gemm_scratch_bytes(batch, cols, rows, xsplit)
   size_t scratch_bytes = 0;
   int* err = nullptr;     // device error word of the tensor-core path
+  void* prep = nullptr;   // gemv_group_prep_bytes: x prepared once per grouped launch (batch <= 4)
   void release();
 };
 

@@ -94,6 +94,8 @@ struct KArgs {
   const double* bias;
   int bias_len;
   int act;
+  const uint2* frags;   // prepared B fragments [csize * nkb_cta][2 kB][4] (nullptr: built per CTA)
+  const float* fscale;  // prepared 2^-e per K segment and token [csize][kB]
 };
 
 __device__ __forceinline__ uint4 ld_stream(const uint8_t* p) {
@@ -162,18 +164,30 @@ __device__ __forceinline__ void a_frag(const uint4& u, int j, uint32_t (&a)[4]) 
   }
 }
 
-// Two x values scaled by s and reduced to plane `plane` (0: f16 rounding, 1: its residual).
-__device__ __forceinline__ uint32_t x_plane_pair(float v0, float v1, float s, int plane) {
+// Two x values scaled by s, split into plane 0 (their f16 rounding) and plane 1 (the f16
+// rounding of the residual).
+__device__ __forceinline__ void x_planes(float v0, float v1, float s, uint32_t& p0, uint32_t& p1) {
   float a = v0 * s, b = v1 * s;
   const bool fa = isfinite(a), fb = isfinite(b);
   if (!fa) a = v0;  // Inf / NaN pass through plane 0 (w * Inf as in fp64)
   if (!fb) b = v1;
   __half2 h0 = __floats2half2_rn(a, b);
-  if (plane == 0) return *reinterpret_cast<uint32_t*>(&h0);
   const float2 f0 = __half22float2(h0);
   const float ra = fa ? a - f0.x : 0.0f, rb = fb ? b - f0.y : 0.0f;
   __half2 h1 = __floats2half2_rn(ra, rb);
-  return *reinterpret_cast<uint32_t*>(&h1);
+  p0 = *reinterpret_cast<uint32_t*>(&h0);
+  p1 = *reinterpret_cast<uint32_t*>(&h1);
+}
+
+// Exponent e of the per-token power-of-two scale of a K range whose largest finite |x| is m:
+// m * 2^e lies in [2^14, 2^15), below the f16 maximum 65504.
+__device__ __forceinline__ int x_scale_exp(float m) {
+  int e = 0;
+  if (m > 0.0f) {
+    e = 14 - ilogbf(m);
+    e = e > 126 ? 126 : (e < -126 ? -126 : e);
+  }
+  return e;
 }
 
 template <typename Args>
@@ -216,6 +230,9 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
     a.bias_len = L.bias_len;
     a.act = L.act;
     a.scale = L.scale;
+    a.frags = static_cast<const uint2*>(L.prep);
+    a.fscale = L.prep ? reinterpret_cast<const float*>(a.frags + static_cast<int64_t>(a.csize) * a.nkb_cta * 8 * kB)
+                      : nullptr;
   }
   constexpr int KBPU = kDt == 16 ? 4 : 2;       // K blocks of 16 per unit
   constexpr int CK = 2 * KBPU * 16;             // K elements per chunk
@@ -260,57 +277,98 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
   if (c0 + 1 < c1) load_chunk(rs * kRG, c0 + 1, bufB, bufB2);
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
+  // B fragments of this CTA's K range, in shared memory: a grouped launch has them prepared
+  // once per layer and each warp copies its own K quarter (one round of 16-byte loads from
+  // L2); one layer per launch builds them here from the CTA's x slice
+  float sinv[kB];
+  if constexpr (kL > 1) {
+#pragma unroll
+    for (int b = 0; b < kB; ++b) sinv[b] = __ldg(a.fscale + rank * kB + b);
+    if (c0 < c1) {
+      const int64_t kb_lo = (c0 - cta_c0) * 2 * KBPU, nkb = (c1 - c0) * 2 * KBPU;
+      const uint4* src = reinterpret_cast<const uint4*>(a.frags + (rank * a.nkb_cta + kb_lo) * NCOL * 4);
+      uint4* dst = reinterpret_cast<uint4*>(frag + kb_lo * NCOL * 4);
+      const int n16 = static_cast<int>(nkb * NCOL * 2);  // NCOL * 4 uint2 per K block
+      for (int i = lane; i < n16; i += 32) dst[i] = __ldg(src + i);
+    }
+    __syncwarp();
+  } else {
   // ---- the CTA's x slice, read from global memory once into shared memory (zero past
   //      `cols`), with the per-token maximum taken on the way
   const int64_t klo = cta_c0 * CK;
   const int kspan = a.nkb_cta * 16;
   int64_t khi = klo + kspan;
   if (khi > a.cols) khi = a.cols;
-  float* xs = reinterpret_cast<float*>(frag + a.nkb_cta * NCOL * 4);  // [kB][kspan]
+  float* xs = reinterpret_cast<float*>(frag + a.nkb_cta * NCOL * 4);  // [kB][kspan], 16-byte aligned
+  // klo and kspan are multiples of 64: 16-byte vectors whenever x's rows are 16-byte aligned
+  const bool xvec = ((reinterpret_cast<uintptr_t>(a.x) | (static_cast<uintptr_t>(a.x_ld) * 4)) & 15) == 0;
 #pragma unroll
   for (int b = 0; b < kB; ++b) {
     float m = 0.0f;
-    for (int i = tid; i < kspan; i += kWarps * 32) {
-      const int64_t k = klo + i;
-      const float v = k < khi ? __ldg(a.x + b * a.x_ld + k) : 0.0f;
-      xs[b * kspan + i] = v;
-      const float av = fabsf(v);
-      if (av > m && av <= 3.402823466e+38f) m = av;
+    const float* xb = a.x + b * a.x_ld;
+    if (xvec) {
+      for (int i = 4 * tid; i < kspan; i += 4 * kWarps * 32) {
+        const int64_t k = klo + i;
+        float4 v;
+        if (k + 3 < khi) {
+          v = __ldg(reinterpret_cast<const float4*>(xb + k));
+        } else {
+          v.x = k < khi ? __ldg(xb + k) : 0.0f;
+          v.y = k + 1 < khi ? __ldg(xb + k + 1) : 0.0f;
+          v.z = k + 2 < khi ? __ldg(xb + k + 2) : 0.0f;
+          v.w = 0.0f;
+        }
+        *reinterpret_cast<float4*>(xs + b * kspan + i) = v;
+        const float a4[4] = {fabsf(v.x), fabsf(v.y), fabsf(v.z), fabsf(v.w)};
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (a4[q] > m && a4[q] <= 3.402823466e+38f) m = a4[q];
+      }
+    } else {
+      for (int i = tid; i < kspan; i += kWarps * 32) {
+        const int64_t k = klo + i;
+        const float v = k < khi ? __ldg(xb + k) : 0.0f;
+        xs[b * kspan + i] = v;
+        const float av = fabsf(v);
+        if (av > m && av <= 3.402823466e+38f) m = av;
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (lane == 0) smax[warp][b] = m;
   }
   __syncthreads();
-  float sc[kB], sinv[kB];
+  float sc[kB];
 #pragma unroll
   for (int b = 0; b < kB; ++b) {
-    float m = fmaxf(fmaxf(smax[0][b], smax[1][b]), fmaxf(smax[2][b], smax[3][b]));
-    int e = 0;
-    if (m > 0.0f) {
-      e = 14 - ilogbf(m);  // m * 2^e in [2^14, 2^15), below the f16 maximum 65504
-      e = e > 126 ? 126 : (e < -126 ? -126 : e);
-    }
+    const int e = x_scale_exp(fmaxf(fmaxf(smax[0][b], smax[1][b]), fmaxf(smax[2][b], smax[3][b])));
     sc[b] = ldexpf(1.0f, e);
     sinv[b] = ldexpf(1.0f, -e);
   }
 
-  // ---- B fragments of the CTA's K range, built once by all 128 threads
-  const int nent = a.nkb_cta * NCOL * 4;
+  // ---- B fragments of the CTA's K range, built once by all 128 threads: entry (kbl, n, tt)
+  //      holds x[k], x[k+1] (k = 16 kbl + 2 tt) and x[k+8], x[k+9] of column n = 2 token + plane;
+  //      one thread makes both planes of one (kbl, token, tt)
+  const int nent = a.nkb_cta * kB * 4;
   for (int e = tid; e < nent; e += kWarps * 32) {
-    const int kbl = e / (NCOL * 4);
-    const int rem = e - kbl * (NCOL * 4);
-    const int n = rem >> 2, tt = rem & 3;
-    const int b = n >> 1, p = n & 1;
+    const int kbl = e / (kB * 4);
+    const int rem = e - kbl * (kB * 4);
+    const int b = rem >> 2, tt = rem & 3;
     const float* xr = xs + b * kspan + kbl * 16 + 2 * tt;
-    const float v0 = xr[0], v1 = xr[1], v8 = xr[8], v9 = xr[9];
+    const float2 lo = *reinterpret_cast<const float2*>(xr), hi = *reinterpret_cast<const float2*>(xr + 8);
     float s = sc[0];
 #pragma unroll
     for (int q = 1; q < kB; ++q)
       if (b == q) s = sc[q];
-    frag[e] = make_uint2(x_plane_pair(v0, v1, s, p), x_plane_pair(v8, v9, s, p));
+    uint32_t l0, l1, h0, h1;
+    x_planes(lo.x, lo.y, s, l0, l1);
+    x_planes(hi.x, hi.y, s, h0, h1);
+    uint2* dst = frag + (kbl * NCOL + 2 * b) * 4 + tt;
+    dst[0] = make_uint2(l0, h0);  // plane 0
+    dst[4] = make_uint2(l1, h1);  // plane 1
   }
   __syncthreads();
+  }
 
   // thread (g, t) holds, in n tile nt, both planes of token 4 nt + t for rows g and g + 8
   float sinv_t[NT];
@@ -341,7 +399,8 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           const int col = 8 * nt + g;
-          bf[nt] = col < NCOL ? frag[((kb_base + u * KBPU + j) * NCOL + col) * 4 + t] : make_uint2(0u, 0u);
+          const int fi = ((kb_base + u * KBPU + j) * NCOL + col) * 4 + t;
+          bf[nt] = col < NCOL ? frag[fi] : make_uint2(0u, 0u);
         }
 #pragma unroll
         for (int r = 0; r < kRG; ++r) {
@@ -484,6 +543,94 @@ __global__ void k_build_tiled(const uint8_t* __restrict__ native, int rows, int 
   }
 }
 
+// Prepares the x of grouped layers once per layer: block (seg, layer) takes the largest finite
+// |x| of K segment seg per token, the power-of-two scale of that segment, and writes the f16
+// B fragments of the segment in the layout the GEMV's CTAs use -- exactly what each CTA of
+// that segment would build itself.
+template <int kL>
+struct PrepArgs {
+  int cols = 0, nkb_cta = 0;
+  int64_t x_ld = 0;
+  const float* x[kL] = {};
+  uint2* frags[kL] = {};
+  float* fscale[kL] = {};
+};
+
+constexpr int kPrepThreads = 256;
+
+template <int kB, int kL>
+__global__ void __launch_bounds__(kPrepThreads) k_prep_x(const __grid_constant__ PrepArgs<kL> pa) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // x may be the previous kernel's output
+  constexpr int NCOL = 2 * kB;
+  __shared__ float smax[kPrepThreads / 32][kB];
+  __shared__ float ssc[kB];
+  const int seg = blockIdx.x, layer = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float* x = pa.x[layer];
+  const int kspan = pa.nkb_cta * 16;
+  const int64_t klo = static_cast<int64_t>(seg) * kspan;
+  const int64_t khi = klo + kspan < pa.cols ? klo + kspan : pa.cols;
+#pragma unroll
+  for (int b = 0; b < kB; ++b) {
+    float m = 0.0f;
+    for (int64_t k = klo + tid; k < khi; k += kPrepThreads) {
+      const float av = fabsf(__ldg(x + b * pa.x_ld + k));
+      if (av > m && av <= 3.402823466e+38f) m = av;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) smax[warp][b] = m;
+  }
+  __syncthreads();
+  if (tid < kB) {
+    float m = smax[0][tid];
+#pragma unroll
+    for (int w = 1; w < kPrepThreads / 32; ++w) m = fmaxf(m, smax[w][tid]);
+    const int e = x_scale_exp(m);
+    ssc[tid] = ldexpf(1.0f, e);
+    pa.fscale[layer][seg * kB + tid] = ldexpf(1.0f, -e);
+  }
+  __syncthreads();
+  uint2* fr = pa.frags[layer] + static_cast<int64_t>(seg) * pa.nkb_cta * NCOL * 4;
+  const int nent = pa.nkb_cta * kB * 4;
+  for (int e = tid; e < nent; e += kPrepThreads) {
+    const int kbl = e / (kB * 4);
+    const int rem = e - kbl * (kB * 4);
+    const int b = rem >> 2, tt = rem & 3;
+    const int64_t k = klo + kbl * 16 + 2 * tt;
+    const float* xb = x + b * pa.x_ld;
+    const float v0 = k < khi ? __ldg(xb + k) : 0.0f, v1 = k + 1 < khi ? __ldg(xb + k + 1) : 0.0f;
+    const float v8 = k + 8 < khi ? __ldg(xb + k + 8) : 0.0f, v9 = k + 9 < khi ? __ldg(xb + k + 9) : 0.0f;
+    uint32_t l0, l1, h0, h1;
+    x_planes(v0, v1, ssc[b], l0, l1);
+    x_planes(v8, v9, ssc[b], h0, h1);
+    uint2* dst = fr + (kbl * NCOL + 2 * b) * 4 + tt;
+    dst[0] = make_uint2(l0, h0);  // plane 0
+    dst[4] = make_uint2(l1, h1);  // plane 1
+  }
+}
+
+template <int kL>
+Status launch_prep(const PrepArgs<kL>& pa, int csize, int nl, int batch, cudaStream_t st, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(csize), static_cast<unsigned>(nl), 1);
+  cfg.blockDim = dim3(kPrepThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  switch (batch) {
+  case 1: return cuda_status(cudaLaunchKernelEx(&cfg, k_prep_x<1, kL>, pa), "gemv_tc prep launch");
+  case 2: return cuda_status(cudaLaunchKernelEx(&cfg, k_prep_x<2, kL>, pa), "gemv_tc prep launch");
+  case 3: return cuda_status(cudaLaunchKernelEx(&cfg, k_prep_x<3, kL>, pa), "gemv_tc prep launch");
+  case 4: return cuda_status(cudaLaunchKernelEx(&cfg, k_prep_x<4, kL>, pa), "gemv_tc prep launch");
+  default: return Status::Internal("gemv_tc prep: batch must be 1..4");
+  }
+}
+
 // The 48 KB default covers static + dynamic shared memory together, so every launch opts in
 // to its dynamic size (the reduction arrays are static). One driver call per kernel, device
 // and size, cached.
@@ -506,13 +653,14 @@ Status allow_dynamic_smem(const void* kern, size_t bytes) {
 }
 
 template <int kDt, int kB, bool kDual, int kL>
-Status launch_t(const GroupArgs<kL>& k, int nl, const Plan& pl, cudaStream_t st, bool pdl) {
+Status launch_t(const GroupArgs<kL>& k, int nl, const Plan& pl, cudaStream_t st, bool pdl, bool prepared) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(pl.csize), static_cast<unsigned>(pl.grid_y), static_cast<unsigned>(nl));
   cfg.blockDim = dim3(kWarps * 32);
-  // B fragments [nkb_cta][2 kB][4] uint2, then the x slice [kB][16 nkb_cta] float
+  // B fragments [nkb_cta][2 kB][4] uint2, then the x slice [kB][16 nkb_cta] float (not when
+  // the fragments are prepared)
   cfg.dynamicSmemBytes = static_cast<size_t>(pl.nkb_cta) * 2 * kB * 4 * sizeof(uint2) +
-                         static_cast<size_t>(pl.nkb_cta) * 16 * kB * sizeof(float);
+                         (prepared ? 0 : static_cast<size_t>(pl.nkb_cta) * 16 * kB * sizeof(float));
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   int n = 0;
@@ -534,19 +682,20 @@ Status launch_t(const GroupArgs<kL>& k, int nl, const Plan& pl, cudaStream_t st,
 }
 
 template <int kDt, bool kDual, int kL>
-Status launch_b(const GroupArgs<kL>& k, int nl, const Plan& pl, int batch, cudaStream_t st, bool pdl) {
+Status launch_b(const GroupArgs<kL>& k, int nl, const Plan& pl, int batch, cudaStream_t st, bool pdl,
+                bool prepared) {
   switch (batch) {
-  case 1: return launch_t<kDt, 1, kDual, kL>(k, nl, pl, st, pdl);
-  case 2: return launch_t<kDt, 2, kDual, kL>(k, nl, pl, st, pdl);
-  case 3: return launch_t<kDt, 3, kDual, kL>(k, nl, pl, st, pdl);
-  case 4: return launch_t<kDt, 4, kDual, kL>(k, nl, pl, st, pdl);
+  case 1: return launch_t<kDt, 1, kDual, kL>(k, nl, pl, st, pdl, prepared);
+  case 2: return launch_t<kDt, 2, kDual, kL>(k, nl, pl, st, pdl, prepared);
+  case 3: return launch_t<kDt, 3, kDual, kL>(k, nl, pl, st, pdl, prepared);
+  case 4: return launch_t<kDt, 4, kDual, kL>(k, nl, pl, st, pdl, prepared);
   default:
     if constexpr (!kDual && kL == 1) {
       switch (batch) {
-      case 5: return launch_t<kDt, 5, false, 1>(k, nl, pl, st, pdl);
-      case 6: return launch_t<kDt, 6, false, 1>(k, nl, pl, st, pdl);
-      case 7: return launch_t<kDt, 7, false, 1>(k, nl, pl, st, pdl);
-      case 8: return launch_t<kDt, 8, false, 1>(k, nl, pl, st, pdl);
+      case 5: return launch_t<kDt, 5, false, 1>(k, nl, pl, st, pdl, prepared);
+      case 6: return launch_t<kDt, 6, false, 1>(k, nl, pl, st, pdl, prepared);
+      case 7: return launch_t<kDt, 7, false, 1>(k, nl, pl, st, pdl, prepared);
+      case 8: return launch_t<kDt, 8, false, 1>(k, nl, pl, st, pdl, prepared);
       default: break;
       }
     }
@@ -555,12 +704,13 @@ Status launch_b(const GroupArgs<kL>& k, int nl, const Plan& pl, int batch, cudaS
 }
 
 template <bool kDual, int kL>
-Status launch_d(DType dt, const GroupArgs<kL>& k, int nl, const Plan& pl, int batch, cudaStream_t st, bool pdl) {
+Status launch_d(DType dt, const GroupArgs<kL>& k, int nl, const Plan& pl, int batch, cudaStream_t st, bool pdl,
+                bool prepared = false) {
   switch (dt) {
-  case DType::FP4: return launch_b<16, kDual, kL>(k, nl, pl, batch, st, pdl);
-  case DType::FP8E4M3: return launch_b<4, kDual, kL>(k, nl, pl, batch, st, pdl);
-  case DType::FP8E5M2: return launch_b<5, kDual, kL>(k, nl, pl, batch, st, pdl);
-  case DType::Int8: return launch_b<9, kDual, kL>(k, nl, pl, batch, st, pdl);
+  case DType::FP4: return launch_b<16, kDual, kL>(k, nl, pl, batch, st, pdl, prepared);
+  case DType::FP8E4M3: return launch_b<4, kDual, kL>(k, nl, pl, batch, st, pdl, prepared);
+  case DType::FP8E5M2: return launch_b<5, kDual, kL>(k, nl, pl, batch, st, pdl, prepared);
+  case DType::Int8: return launch_b<9, kDual, kL>(k, nl, pl, batch, st, pdl, prepared);
   default: return Status::Unsupported("gemv_tc: dtype");
   }
 }
@@ -633,12 +783,33 @@ Status launch_gemv_tc_group(DType dt, int rows, int cols, int batch, int64_t x_l
   if (!gemv_tc_supported(dt)) return Status::Unsupported("gemv_tc: dtype");
   if (rows <= 0 || cols <= 0 || batch < 1 || batch > 4 || n < 0 || (n > 0 && !layers))
     return Status::Invalid("gemv_tc group: bad arguments");
+  for (int i = 0; i < n; ++i) {
+    const GemvGroupLayer& L = layers[i];
+    if (!L.Wt || !L.x || !L.pre || !L.post || !L.prep) return Status::Invalid("gemv_tc group: null layer pointer");
+  }
   Plan pl = make_plan(dt, rows, cols, true);
+  // one 64-row set per CTA: many short CTAs balance over the SMs better than fewer long
+  // ones (measured: 3 row sets per CTA left a partial second wave)
+  pl.grid_y = pl.row_sets;
+  // The layers are independent: every layer's x is prepared first (one small launch per 32
+  // layers), then the GEMV launches follow as programmatic dependents, so each one's CTAs
+  // start streaming weights while the launch before it drains.
+  const int64_t nfr = static_cast<int64_t>(pl.csize) * pl.nkb_cta * 8 * batch;
   for (int l0 = 0; l0 < n; l0 += kGemvGroupMax) {
     const int nl = n - l0 < kGemvGroupMax ? n - l0 : kGemvGroupMax;
-    // one 64-row set per CTA: many short CTAs balance over the SMs better than fewer long
-    // ones (measured: 3 row sets per CTA left a partial second wave)
-    pl.grid_y = pl.row_sets;
+    PrepArgs<kGemvGroupMax> pa;
+    pa.cols = cols;
+    pa.nkb_cta = pl.nkb_cta;
+    pa.x_ld = x_ld;
+    for (int i = 0; i < nl; ++i) {
+      pa.x[i] = layers[l0 + i].x;
+      pa.frags[i] = static_cast<uint2*>(layers[l0 + i].prep);
+      pa.fscale[i] = reinterpret_cast<float*>(pa.frags[i] + nfr);
+    }
+    WB_TRY(launch_prep(pa, pl.csize, nl, batch, st, pdl || l0 > 0));
+  }
+  for (int l0 = 0; l0 < n; l0 += kGemvGroupMax) {
+    const int nl = n - l0 < kGemvGroupMax ? n - l0 : kGemvGroupMax;
     GroupArgs<kGemvGroupMax> g{};
     KArgs& k = g.a;
     k.rows = rows;
@@ -651,14 +822,17 @@ Status launch_gemv_tc_group(DType dt, int rows, int cols, int batch, int64_t x_l
     k.nkb_cta = pl.nkb_cta;
     k.x_ld = x_ld;
     k.ld_out = ld_out;
-    for (int i = 0; i < nl; ++i) {
-      const GemvGroupLayer& L = layers[l0 + i];
-      if (!L.Wt || !L.x || !L.pre || !L.post) return Status::Invalid("gemv_tc group: null layer pointer");
-      g.layer[i] = L;
-    }
-    WB_TRY((launch_d<false, kGemvGroupMax>(dt, g, nl, pl, batch, st, pdl)));
+    for (int i = 0; i < nl; ++i) g.layer[i] = layers[l0 + i];
+    WB_TRY((launch_d<false, kGemvGroupMax>(dt, g, nl, pl, batch, st, true, true)));
   }
   return Status::Ok();
+}
+
+size_t gemv_group_prep_bytes(DType dt, int rows, int cols, int batch) {
+  if (!gemv_tc_supported(dt) || rows <= 0 || cols <= 0 || batch < 1 || batch > 4) return 0;
+  const Plan pl = make_plan(dt, rows, cols, true);
+  return static_cast<size_t>(pl.csize) * pl.nkb_cta * 8 * batch * sizeof(uint2) +
+         static_cast<size_t>(pl.csize) * batch * sizeof(float);
 }
 
 } // namespace wb

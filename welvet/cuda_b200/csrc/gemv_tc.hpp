@@ -60,8 +60,14 @@ struct GemvGroupLayer {
   int bias_len = 0;
   int act = -1;
   float scale = 1.0f;            // Int8 per-tensor scale
+  void* prep = nullptr;          // gemv_group_prep_bytes of device scratch (required)
 };
 constexpr int kGemvGroupMax = 32;
+// Device bytes a grouped layer needs to have its x prepared once: its f16 B fragments and
+// per-K-segment scales. A grouped launch first runs a small kernel that prepares each
+// layer's x, then the GEMV, whose CTAs (one per 64 rows) read the fragments instead of each
+// staging x and building them.
+size_t gemv_group_prep_bytes(DType dt, int rows, int cols, int batch);
 Status launch_gemv_tc_group(DType dt, int rows, int cols, int batch, int64_t x_ld, int64_t ld_out,
                             const GemvGroupLayer* layers, int n, cudaStream_t st, bool pdl);
 
