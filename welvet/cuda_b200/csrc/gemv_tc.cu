@@ -36,7 +36,7 @@ namespace wb {
 namespace {
 
 constexpr int kWarps = 4;   // warps per CTA (K slices of the CTA's K range)
-constexpr int kRG = 4;      // row groups of 16 rows per warp -> 64-row sets
+constexpr int kRG = TiledGeom::kSetGroups;  // row groups of 16 rows per warp -> 64-row sets
 constexpr int kRowsPerSet = kRG * 16;
 constexpr int kMaxCluster = 8;
 
@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
 #pragma unroll
       for (int r = 0; r < kRG; ++r) {
         const bool ok = unit < a.units_k && rg0 + r < a.row_groups;
-        const int64_t off = ((rg0 + r) * a.units_k + unit) * 512 + lane * 16;
+        const int64_t off = (((rg0 / kRG) * a.units_k + unit) * kRG + r) * 512 + lane * 16;
         buf[u][r] = ok ? ld_stream(a.Wt + off) : make_uint4(0, 0, 0, 0);
         if (kDual) buf2[u][r] = ok ? ld_stream(a.Wt2 + off) : make_uint4(0, 0, 0, 0);
       }
@@ -508,11 +508,13 @@ __global__ void k_build_tiled(const uint8_t* __restrict__ native, int rows, int 
                               int64_t total, uint8_t* __restrict__ out) {
   for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
        t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t unit_idx = t >> 9;
+    const int64_t unit_idx = t >> 9;  // (row set * units_k + unit) * 4 + row group in the set
     const int within = static_cast<int>(t & 511);
     const int lane = within >> 4;
     const int g = lane >> 2, tt = lane & 3;
-    const int64_t rg = unit_idx / units_k, unit = unit_idx - rg * units_k;
+    const int64_t q = unit_idx / TiledGeom::kSetGroups;
+    const int64_t set = q / units_k, unit = q - set * units_k;
+    const int64_t rg = set * TiledGeom::kSetGroups + (unit_idx - q * TiledGeom::kSetGroups);
     uint32_t byte = 0;
     if (kDt == 16) {
       const int j = (within >> 2) & 3;        // K block within the unit

@@ -8,11 +8,17 @@ namespace wb {
 // Fragment-tiled weight mirror: rows in groups of 16, K in units of 64 (FP4) or 32 (FP8 /
 // Int8) elements; each 512-byte unit holds, for every lane of a warp, the codes of its
 // mma.m16n8k16 A fragments for 4 (FP4) or 2 (FP8 / Int8) consecutive 16-wide K blocks.
+// Units are ordered [row set of 4 row groups][K unit][row group in the set]: a warp that
+// streams a K range of one 64-row set reads one contiguous run of bytes (DRAM rows are
+// opened once per 2 KB instead of once per 512-byte unit). Row groups are padded to a
+// multiple of 4 with zero codes.
 struct TiledGeom {
+  static constexpr int kSetGroups = 4;
   int64_t row_groups = 0;   // ceil(rows / 16)
   int64_t units_k = 0;      // K units per row group
   int unit_k = 0;           // elements of K per unit (64 or 32)
-  int64_t bytes() const { return row_groups * units_k * 512; }
+  int64_t row_sets() const { return (row_groups + kSetGroups - 1) / kSetGroups; }
+  int64_t bytes() const { return row_sets() * kSetGroups * units_k * 512; }
 };
 
 TiledGeom tiled_geom(DType dt, int rows, int cols);
