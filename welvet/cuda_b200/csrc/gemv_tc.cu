@@ -250,10 +250,13 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
   // Row sets of this CTA: blockIdx.y, blockIdx.y + gridDim.y, ... (one per CTA unless a
   // grouped launch gives each CTA several, which then share the x slice and B fragments).
   int64_t rs = blockIdx.y;
+  // The CTA's chunks [cta_c0, c1) are dealt to its warps in turn (warp w: cta_c0 + w,
+  // + kWarps, ...), so the four warps advance through one contiguous run of the mirror.
   const int64_t cta_c0 = static_cast<int64_t>(rank) * kWarps * a.cpw;
-  const int64_t c0 = cta_c0 + static_cast<int64_t>(warp) * a.cpw;
-  int64_t c1 = c0 + a.cpw;
+  const int64_t c0 = cta_c0 + warp;
+  int64_t c1 = cta_c0 + static_cast<int64_t>(kWarps) * a.cpw;
   if (c1 > a.chunks) c1 = a.chunks;
+  constexpr int CS = kWarps;  // chunk stride of a warp
 
   auto load_chunk = [&](int64_t rg0, int64_t c, uint4 (&buf)[2][kRG], uint4 (&buf2)[2][kRG]) {
 #pragma unroll
@@ -274,7 +277,7 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
   // The first two chunks' weights are requested before waiting on the previous kernel:
   // they do not depend on it.
   if (c0 < c1) load_chunk(rs * kRG, c0, bufA, bufA2);
-  if (c0 + 1 < c1) load_chunk(rs * kRG, c0 + 1, bufB, bufB2);
+  if (c0 + CS < c1) load_chunk(rs * kRG, c0 + CS, bufB, bufB2);
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // B fragments of this CTA's K range, in shared memory: a grouped launch has them prepared
@@ -284,14 +287,14 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
   if constexpr (kL > 1) {
 #pragma unroll
     for (int b = 0; b < kB; ++b) sinv[b] = __ldg(a.fscale + rank * kB + b);
-    if (c0 < c1) {
-      const int64_t kb_lo = (c0 - cta_c0) * 2 * KBPU, nkb = (c1 - c0) * 2 * KBPU;
-      const uint4* src = reinterpret_cast<const uint4*>(a.frags + (rank * a.nkb_cta + kb_lo) * NCOL * 4);
-      uint4* dst = reinterpret_cast<uint4*>(frag + kb_lo * NCOL * 4);
+    if (cta_c0 < c1) {
+      const int64_t nkb = (c1 - cta_c0) * 2 * KBPU;
+      const uint4* src = reinterpret_cast<const uint4*>(a.frags + rank * a.nkb_cta * NCOL * 4);
+      uint4* dst = reinterpret_cast<uint4*>(frag);
       const int n16 = static_cast<int>(nkb * NCOL * 2);  // NCOL * 4 uint2 per K block
-      for (int i = lane; i < n16; i += 32) dst[i] = __ldg(src + i);
+      for (int i = tid; i < n16; i += kWarps * 32) dst[i] = __ldg(src + i);
     }
-    __syncwarp();
+    __syncthreads();
   } else {
   // ---- the CTA's x slice, read from global memory once into shared memory (zero past
   //      `cols`), with the per-token maximum taken on the way
@@ -438,20 +441,20 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
     for (int r = 0; r < kRG; ++r)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) acc[r][0][nt] = acc[r][1][nt] = acc2[r][0][nt] = acc2[r][1][nt] = 0.0;
-  // chunk c sits in bufA when c - c0 is even, in bufB when odd; the chunk two ahead is
-  // requested as soon as its buffer is free.
-  for (int64_t c = c0; c < c1; c += 2) {
+  // the warp's chunks alternate between bufA and bufB; the chunk two ahead is requested as
+  // soon as its buffer is free.
+  for (int64_t c = c0; c < c1; c += 2 * CS) {
     compute_chunk(c, bufA, bufA2);
-    if (c + 2 < c1) load_chunk(rg0, c + 2, bufA, bufA2);
-    if (c + 1 < c1) {
-      compute_chunk(c + 1, bufB, bufB2);
-      if (c + 3 < c1) load_chunk(rg0, c + 3, bufB, bufB2);
+    if (c + 2 * CS < c1) load_chunk(rg0, c + 2 * CS, bufA, bufA2);
+    if (c + CS < c1) {
+      compute_chunk(c + CS, bufB, bufB2);
+      if (c + 3 * CS < c1) load_chunk(rg0, c + 3 * CS, bufB, bufB2);
     }
   }
   // the next row set's first two chunks stream in while this one is reduced and written
   if (rs + gridDim.y < nrs) {
     if (c0 < c1) load_chunk((rs + gridDim.y) * kRG, c0, bufA, bufA2);
-    if (c0 + 1 < c1) load_chunk((rs + gridDim.y) * kRG, c0 + 1, bufB, bufB2);
+    if (c0 + CS < c1) load_chunk((rs + gridDim.y) * kRG, c0 + CS, bufB, bufB2);
   }
 
   // ---- CTA reduction over its 4 K slices (fixed order)
