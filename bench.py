@@ -520,17 +520,53 @@ def run_case_multi(args):
     return 0
 
 
+def run_case_swiglu(args, torch, W, g):
+    d, hid, m = args.cols, args.rows, args.tokens
+    ws = [torch.randn(sh, device="cuda", generator=g) * SIGMA for sh in ((hid, d), (hid, d), (d, hid))]
+    cell = W.SwigluCell(ws[0], ws[1], ws[2], args.dtype)
+    del ws
+    x = torch.randn((m, d), device="cuda", generator=g)
+    if args.x == "bf16":
+        x = x.to(torch.bfloat16).float()
+    y = torch.zeros((m, d), device="cuda")
+    h = torch.zeros((m, hid), device="cuda")
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+    cell.execute_device(x, y, h)
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(args.reps):
+        flush.zero_()
+        torch.cuda._sleep(200000)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        cell.execute_device(x, y, h)
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    us = statistics.median(ts)
+    wbytes = 3 * d * hid * (0.5 if args.dtype == DTYPE_FP4 else 1.0)
+    print(json.dumps({"case": "swiglu", "dtype": args.dtype, "d": d, "hidden": hid, "tokens": m, "x": args.x,
+                      "reps": args.reps, "us_median": round(us, 2), "weight_GBps": round(wbytes / us / 1e3, 1),
+                      "TFLOPs": round(2.0 * m * 3 * d * hid / us / 1e6, 2)}), flush=True)
+    cell.release()
+    return 0
+
+
 def run_case(args):
     """--case: one kernel's workload alone, for timing and ncu captures (prints one JSON line
     with the case's own numbers, not the benchmark line). Weights ~N(0, 0.02) generated on
     the device; x ~N(0, 1) (rounded to bf16 with --x bf16); L2 flushed before each rep.
       gemv   one Dense layer rows x cols, --tokens 1..4, single launches
       group  --layers independent layers rows x cols, B=1, grouped launches
-      gemm   one Dense layer rows x cols, --tokens > 4 (tcgen05 path)"""
+      gemm   one Dense layer rows x cols, --tokens > 8 (tcgen05 path)
+      swiglu one SwiGLU cell, d = cols, hidden = rows, --tokens (Gate/Up pair GEMM, Down GEMM)"""
     import torch
     import welvet.cuda_b200 as W
     W.cuda_init()
     g = torch.Generator(device="cuda").manual_seed(SEED)
+    if args.case == "swiglu":
+        return run_case_swiglu(args, torch, W, g)
     n_layers = args.layers if args.case == "group" else 1
     tokens = 1 if args.case == "group" else args.tokens
     sess = []
@@ -586,7 +622,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch the step's kernels one by one")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched (SwiGLU M=512) measurement")
-    ap.add_argument("--case", choices=["gemv", "group", "gemm", "sharded", "pipeline"],
+    ap.add_argument("--case", choices=["gemv", "group", "gemm", "swiglu", "sharded", "pipeline"],
                     help="time one workload alone (see run_case / run_case_multi)")
     ap.add_argument("--micro", type=int, default=16, help="--case pipeline: rows per micro-batch")
     ap.add_argument("--dtype", type=int, default=DTYPE_FP4, help="--case: 16 FP4, 4 E4M3, 5 E5M2, 9 Int8")

@@ -204,14 +204,10 @@ __device__ __forceinline__ void dec_i8x4(uint32_t w, float* f) {
   f[3] = u2f(__byte_perm(u, 0x4b000000u, 0x7443)) - 8388736.0f;
 }
 
-// Activation in float64 (the reference's activate_dev, src/cuda/kernels.cu:22-46), calling
-// CUDA's double exp/tanh exactly as the reference does.
-__device__ __forceinline__ double activate(int act, double x) {
+// The transcendental activations, out of line: inlined into unrolled epilogues they made the
+// code of a 16-output step large enough to stall on instruction fetch.
+static __device__ __noinline__ double activate_transcendental(int act, double x) {
   switch (act) {
-  case -1: return x;
-  case 0: return x < 0.0 ? 0.0 : x;
-  case 6: return x < 0.0 ? 0.0 : x * x;
-  case 5: return x < 0.0 ? 0.01 * x : x;
   case 1: return x / (1.0 + exp(-x));
   case 2: {
     const double k = 0.7978845608028654;
@@ -220,6 +216,18 @@ __device__ __forceinline__ double activate(int act, double x) {
   case 3: return tanh(x);
   case 4: return 1.0 / (1.0 + exp(-x));
   default: return x;
+  }
+}
+
+// Activation in float64 (the reference's activate_dev, src/cuda/kernels.cu:22-46), calling
+// CUDA's double exp/tanh exactly as the reference does.
+__device__ __forceinline__ double activate(int act, double x) {
+  switch (act) {
+  case -1: return x;
+  case 0: return x < 0.0 ? 0.0 : x;
+  case 6: return x < 0.0 ? 0.0 : x * x;
+  case 5: return x < 0.0 ? 0.01 * x : x;
+  default: return activate_transcendental(act, x);
   }
 }
 

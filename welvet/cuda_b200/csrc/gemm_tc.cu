@@ -175,6 +175,32 @@ __device__ __forceinline__ void write_pair(const Params& p, int t, int i, double
   p.h[static_cast<int64_t>(t) * p.ld_h + i] = static_cast<float>(static_cast<double>(g) * static_cast<double>(up));
 }
 
+// The values write_out / write_pair store, for an epilogue that stages them first.
+template <typename Params>
+__device__ __forceinline__ void out_values(const Params& p, int o, double y, float& pre, float& post) {
+  pre = static_cast<float>(y);
+  double v = static_cast<double>(pre);
+  if (p.bias != nullptr && o < p.bias_len) {
+    v += p.bias[o];
+    pre = static_cast<float>(v);
+  }
+  post = static_cast<float>(activate(p.act, v));
+}
+
+// pair_value with SiLU's exp inline (the GEMM epilogue overlaps a few of them).
+__device__ __forceinline__ float pair_value_inline(float gate_pre, float up) {
+  const double x = static_cast<double>(gate_pre);
+  const float g = static_cast<float>(x / (1.0 + exp(-x)));
+  return static_cast<float>(static_cast<double>(g) * static_cast<double>(up));
+}
+
+__device__ __forceinline__ float pair_value(double y_gate, double y_up) {
+  const float gate_pre = static_cast<float>(y_gate);
+  const float up = static_cast<float>(y_up);
+  const float g = static_cast<float>(activate(1, static_cast<double>(gate_pre)));
+  return static_cast<float>(static_cast<double>(g) * static_cast<double>(up));
+}
+
 template <typename Params>
 __device__ __forceinline__ void write_out(const Params& p, int t, int o, double y) {
   const int64_t idx = static_cast<int64_t>(t) * p.ld_out + o;
@@ -385,7 +411,26 @@ struct TmParams {
   float w_scale2;              // Up's Int8 scale (pair mode)
   float* h;
   int64_t ld_h;
+  int tma_out;                 // last pass stores through shared memory with bulk tensor stores
+  int tma_post;                // ... and post has its own map (post != pre)
 };
+
+// Epilogue staging of one converter group (4 warps, 128 rows): 2 buffers x {pre, post} x 16
+// tokens x 128 rows of fp32, in the ring memory the last pass no longer uses.
+constexpr uint32_t kStageBuf = 16 * 128 * 4;
+constexpr uint32_t kStageGroup = 2 * 2 * kStageBuf;
+
+__device__ __forceinline__ void named_bar(uint32_t id, uint32_t n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// Outputs are written once and not read again by the GEMM: evict-first in L2, so that they
+// do not push out the x planes every row tile re-reads.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, const void* src, int x, int y, uint64_t pol) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;"
+               ::"l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_u32(src)), "l"(pol)
+               : "memory");
+}
 
 __device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* tm, int x, int y, int z,
                                                  uint64_t* bar, uint64_t policy) {
@@ -485,7 +530,8 @@ __device__ __forceinline__ void convert_row(const uint8_t* tile, int r, uint32_t
 template <int kDt>
 __global__ void __launch_bounds__(kTmThreads, 1)
     k_gemm_tm(const __grid_constant__ CUtensorMap tm_x1, const __grid_constant__ CUtensorMap tm_x2,
-              const __grid_constant__ CUtensorMap tm_x3, const TmParams p) {
+              const __grid_constant__ CUtensorMap tm_x3, const __grid_constant__ CUtensorMap tm_o1,
+              const __grid_constant__ CUtensorMap tm_o2, const TmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = p.sx, Sw = p.sw;
@@ -684,7 +730,18 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       if (!warp_wait(acc_full, static_cast<uint32_t>(pass) & 1u, p.err, 17)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int t_pass = t_begin + pass * T;
-      for (int tc = grp * 16; tc < T; tc += 32) {
+      // The last pass may stage its outputs in the (now idle) ring memory and leave them to
+      // bulk tensor stores, which drain while the SM moves on; the CTA only waits for the
+      // stores to have read shared memory.
+      const bool staged = p.tma_out && pass == npass - 1;
+      float* stage = reinterpret_cast<float*>(smem + grp * kStageGroup);
+      const bool issuer = q == 0 && lane == 0;  // one thread of the group issues its stores
+      int chunk = 0;
+      for (int tc = grp * 16; tc < T; tc += 32, ++chunk) {
+        // Chunks are 16-token aligned within the block: one that starts past the block's
+        // tokens holds none of them (and may hold the next block's, which a staged store must
+        // not overwrite). Uniform over the group, so its barriers stay matched.
+        if (t_pass + tc >= t_begin + t_count) break;
         double y[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) y[e] = 0.0;
@@ -697,6 +754,11 @@ __global__ void __launch_bounds__(kTmThreads, 1)
             for (int e = 0; e < 16; ++e) y[e] += static_cast<double>(__uint_as_float(v[e]));
           }
         }
+        float* s1 = stage + (chunk & 1) * 2 * (kStageBuf / 4);
+        float* s2 = s1 + kStageBuf / 4;
+        // phase 1 (unrolled, cheap): each sum scaled in fp64, then kept as the float the
+        // reference rounds it to (pre = float(y); Gate and Up are floats before the product)
+        float pf[16], uf[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int t = t_pass + tc + e;
@@ -708,15 +770,67 @@ __global__ void __launch_bounds__(kTmThreads, 1)
           }
           if (p.splits > 1) {
             if (valid) p.partial[(static_cast<int64_t>(split) * p.M + t) * p.rows + o] = yy;
-          } else if (p.pair) {
-            // Up row o + 1 sits in the next lane (rows of a 128-row tile are lanes)
-            const double up = __shfl_xor_sync(0xffffffffu, yy, 1);
-            if (valid && (o & 1) == 0) write_pair(p, t, o >> 1, yy, up);
-          } else if (valid) {
-            write_out(p, t, o, yy);
+          }
+          pf[e] = static_cast<float>(yy);
+          // Up row o + 1 sits in the next lane (rows of a 128-row tile are lanes)
+          if (p.pair) uf[e] = __shfl_xor_sync(0xffffffffu, pf[e], 1);
+        }
+        if (p.splits > 1) continue;
+        if (staged) {
+          // buffer chunk & 1 was last stored two chunks ago: its reads must be done
+          if (issuer && chunk >= 2) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          named_bar(1 + grp, 128);
+        }
+        // phase 2 (the bias / activation / SwiGLU code appears once or a few times, not 16)
+        if (p.pair) {
+          // both lanes of a Gate/Up pair work: the Gate lane takes tokens 0..7 of the chunk,
+          // the Up lane 8..15 (each lane holds its row's value and, in uf, its partner's)
+          const bool up_lane = (o & 1) != 0;
+          const int e0 = up_lane ? 8 : 0;
+#pragma unroll 4
+          for (int k = 0; k < 8; ++k) {
+            const int e = e0 + k;
+            const int t = t_pass + tc + e;
+            const bool valid = t < t_begin + t_count && o < p.rows;
+            const float h = pair_value_inline(up_lane ? uf[e] : pf[e], up_lane ? pf[e] : uf[e]);
+            if (staged) s1[e * 64 + (r >> 1)] = h;
+            else if (valid) p.h[static_cast<int64_t>(t) * p.ld_h + (o >> 1)] = h;
+          }
+        } else {
+#pragma unroll 1
+          for (int e = 0; e < 16; ++e) {
+            const int t = t_pass + tc + e;
+            const bool valid = t < t_begin + t_count && o < p.rows;
+            float a = 0.0f, b = 0.0f;
+            if (valid) out_values(p, o, pf[e], a, b);
+            if (staged) {
+              s1[e * 128 + r] = a;
+              s2[e * 128 + r] = b;
+            } else if (valid) {
+              const int64_t idx = static_cast<int64_t>(t) * p.ld_out + o;
+              p.pre[idx] = a;
+              p.post[idx] = b;
+            }
+          }
+        }
+        if (staged) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          named_bar(1 + grp, 128);
+          if (issuer) {
+            const int ty = t_pass + tc;
+            uint64_t pol;
+            asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+            if (p.pair) {
+              tma_store_2d(&tm_o1, s1, tile_m * 64, ty, pol);
+            } else {
+              tma_store_2d(&tm_o1, s1, tile_m * 128, ty, pol);
+              if (p.tma_post) tma_store_2d(&tm_o2, s2, tile_m * 128, ty, pol);
+            }
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
           }
         }
       }
+      if (staged && issuer) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);
@@ -1150,13 +1264,42 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
   p.partial = partial; p.err = a.err;
   p.pair = a.pair ? 1 : 0; p.w_scale2 = a.scale2; p.h = a.h; p.ld_h = a.ld_h;
 
+  // Outputs through bulk tensor stores (the last pass stages them in the idle ring memory):
+  // fp32 rows whose pitch is a multiple of 16 bytes at 16-byte aligned bases.
+  CUtensorMap tm_o[2] = {tm_x[0], tm_x[0]};  // placeholders when the epilogue stores directly
+  {
+    auto aligned = [](const void* ptr, int64_t ld) {
+      return ptr != nullptr && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && (ld * 4) % 16 == 0;
+    };
+    const uint64_t ring = static_cast<uint64_t>(pl.sx) * pl.x_bytes + static_cast<uint64_t>(pl.sw) * pl.w_bytes;
+    bool ok = pl.splits == 1 && ring >= 2 * kStageGroup;
+    if (ok && a.pair) {
+      ok = aligned(a.h, a.ld_h) &&
+           make_map_2d(&tm_o[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.h, static_cast<uint64_t>(a.rows / 2),
+                       static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.ld_h) * 4, kBM / 2, 16,
+                       CU_TENSOR_MAP_SWIZZLE_NONE).ok();
+    } else if (ok) {
+      ok = aligned(a.pre, a.ld_out) && aligned(a.post, a.ld_out) &&
+           make_map_2d(&tm_o[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.pre, static_cast<uint64_t>(a.rows),
+                       static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.ld_out) * 4, kBM, 16,
+                       CU_TENSOR_MAP_SWIZZLE_NONE).ok();
+      p.tma_post = ok && a.post != a.pre;
+      if (p.tma_post)
+        ok = make_map_2d(&tm_o[1], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.post, static_cast<uint64_t>(a.rows),
+                         static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.ld_out) * 4, kBM, 16,
+                         CU_TENSOR_MAP_SWIZZLE_NONE).ok();
+    }
+    p.tma_out = ok ? 1 : 0;
+    if (!ok) p.tma_post = 0;
+  }
+
   const size_t smem = pl.smem;
   dim3 grid(static_cast<unsigned>((a.M + pl.TB - 1) / pl.TB), static_cast<unsigned>((a.rows + kBM - 1) / kBM),
             static_cast<unsigned>(pl.splits));
   if (grid.y > 65535) return Status::Invalid("gemm_tc: too many weight rows for one launch");
   auto launch = [&](auto kern) -> Status {
     WB_TRY(set_max_smem(reinterpret_cast<const void*>(kern), smem));
-    kern<<<grid, kTmThreads, smem, st>>>(tm_x[0], tm_x[1], tm_x[2], p);
+    kern<<<grid, kTmThreads, smem, st>>>(tm_x[0], tm_x[1], tm_x[2], tm_o[0], tm_o[1], p);
     return cuda_status(cudaGetLastError(), "gemm_tc (tmem) launch");
   };
   switch (a.dtype) {
