@@ -595,6 +595,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
   const int n0 = ntot < 256 ? ntot : 256;  // first MMA's N; the second covers [n0, ntot)
   const int nacc = p.nacc[P - 1];          // independent accumulators (k steps round robin)
   const int iters = npass * nkb;
+  // Epilogue sums that are single fp32 values (one plane, one accumulator, no Int8 scale, no
+  // split partials) are scaled in fp32; others are summed and scaled in fp64.
+  const bool f32_sums = P == 1 && nacc == 1 && kDt != 9 && p.splits == 1;
+  const bool plain_act = p.bias == nullptr && (p.act == -1 || p.act == 0 || p.act == 6);
 
   // Loops keep their ring slots and phase bits as running state (Ring): no divisions on the
   // single-thread critical paths.
@@ -742,38 +746,61 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         // tokens holds none of them (and may hold the next block's, which a staged store must
         // not overwrite). Uniform over the group, so its barriers stay matched.
         if (t_pass + tc >= t_begin + t_count) break;
-        double y[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) y[e] = 0.0;
-        for (int pl = 0; pl < P; ++pl) {
-          for (int jj = 0; jj < nacc; ++jj) {
-            uint32_t v[16];
-            tmem_ld16(tmem + lane_base + static_cast<uint32_t>(jj * ntot + pl * T + tc), v);
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-            for (int e = 0; e < 16; ++e) y[e] += static_cast<double>(__uint_as_float(v[e]));
-          }
-        }
         float* s1 = stage + (chunk & 1) * 2 * (kStageBuf / 4);
         float* s2 = s1 + kStageBuf / 4;
-        // phase 1 (unrolled, cheap): each sum scaled in fp64, then kept as the float the
-        // reference rounds it to (pre = float(y); Gate and Up are floats before the product)
+        // phase 1 (unrolled, cheap): each sum scaled, then kept as the float the reference
+        // rounds it to (pre = float(y); Gate and Up are floats before the product)
         float pf[16], uf[16];
+        if (f32_sums) {
+          // one plane, one accumulator: the sum is one fp32 value and the scale a power of two,
+          // so the fp32 product is the rounding of the exact (fp64) product
+          uint32_t v[16];
+          tmem_ld16(tmem + lane_base + static_cast<uint32_t>(tc), v);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          const float4* sc4 = reinterpret_cast<const float4*>(p.scale_inv + t_pass + tc);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int t = t_pass + tc + e;
-          const bool valid = t < t_begin + t_count && o < p.rows;
-          double yy = 0.0;
-          if (valid) {
-            yy = y[e] * static_cast<double>(p.scale_inv[t]);
-            if (kDt == 9) yy *= static_cast<double>((p.pair && (o & 1)) ? p.w_scale2 : p.w_scale);
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const float4 sc = __ldg(sc4 + e4);  // scale_inv holds Mp (multiple of 16) entries
+            const float scv[4] = {sc.x, sc.y, sc.z, sc.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int e = 4 * e4 + j;
+              const bool valid = t_pass + tc + e < t_begin + t_count && o < p.rows;
+              pf[e] = valid ? __uint_as_float(v[e]) * scv[j] : 0.0f;
+            }
           }
-          if (p.splits > 1) {
-            if (valid) p.partial[(static_cast<int64_t>(split) * p.M + t) * p.rows + o] = yy;
+        } else {
+          double y[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) y[e] = 0.0;
+          for (int pl = 0; pl < P; ++pl) {
+            for (int jj = 0; jj < nacc; ++jj) {
+              uint32_t v[16];
+              tmem_ld16(tmem + lane_base + static_cast<uint32_t>(jj * ntot + pl * T + tc), v);
+              asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+              for (int e = 0; e < 16; ++e) y[e] += static_cast<double>(__uint_as_float(v[e]));
+            }
           }
-          pf[e] = static_cast<float>(yy);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int t = t_pass + tc + e;
+            const bool valid = t < t_begin + t_count && o < p.rows;
+            double yy = 0.0;
+            if (valid) {
+              yy = y[e] * static_cast<double>(p.scale_inv[t]);
+              if (kDt == 9) yy *= static_cast<double>((p.pair && (o & 1)) ? p.w_scale2 : p.w_scale);
+            }
+            if (p.splits > 1) {
+              if (valid) p.partial[(static_cast<int64_t>(split) * p.M + t) * p.rows + o] = yy;
+            }
+            pf[e] = static_cast<float>(yy);
+          }
+        }
+        if (p.pair) {
           // Up row o + 1 sits in the next lane (rows of a 128-row tile are lanes)
-          if (p.pair) uf[e] = __shfl_xor_sync(0xffffffffu, pf[e], 1);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) uf[e] = __shfl_xor_sync(0xffffffffu, pf[e], 1);
         }
         if (p.splits > 1) continue;
         if (staged) {
@@ -802,7 +829,16 @@ __global__ void __launch_bounds__(kTmThreads, 1)
             const int t = t_pass + tc + e;
             const bool valid = t < t_begin + t_count && o < p.rows;
             float a = 0.0f, b = 0.0f;
-            if (valid) out_values(p, o, pf[e], a, b);
+            if (valid) {
+              if (plain_act) {
+                // Linear / ReLU / ReLU2 without bias: the float results of the fp64 reference
+                // expressions (x < 0 ? 0 : x, x * x of a float is exact in fp64)
+                a = pf[e];
+                b = p.act == -1 ? a : (a < 0.0f ? 0.0f : (p.act == 0 ? a : a * a));
+              } else {
+                out_values(p, o, pf[e], a, b);
+              }
+            }
             if (staged) {
               s1[e * 128 + r] = a;
               s2[e * 128 + r] = b;
