@@ -808,37 +808,48 @@ __global__ void __launch_bounds__(kTmThreads, 1)
           if (issuer && chunk >= 2) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
           named_bar(1 + grp, 128);
         }
-        // phase 2 (the bias / activation / SwiGLU code appears once or a few times, not 16)
+        // phase 2: the outputs. pf / uf are only indexed by constants here (kept in registers);
+        // the general bias / activation epilogue runs on a copy one output per iteration so
+        // that its fp64 code appears once.
         if (p.pair) {
           // both lanes of a Gate/Up pair work: the Gate lane takes tokens 0..7 of the chunk,
           // the Up lane 8..15 (each lane holds its row's value and, in uf, its partner's)
           const bool up_lane = (o & 1) != 0;
-          const int e0 = up_lane ? 8 : 0;
-#pragma unroll 4
+#pragma unroll
           for (int k = 0; k < 8; ++k) {
-            const int e = e0 + k;
+            const int e = (up_lane ? 8 : 0) + k;
             const int t = t_pass + tc + e;
             const bool valid = t < t_begin + t_count && o < p.rows;
-            const float h = pair_value_inline(up_lane ? uf[e] : pf[e], up_lane ? pf[e] : uf[e]);
+            const float h = pair_value_inline(up_lane ? uf[8 + k] : pf[k], up_lane ? pf[8 + k] : uf[k]);
             if (staged) s1[e * 64 + (r >> 1)] = h;
             else if (valid) p.h[static_cast<int64_t>(t) * p.ld_h + (o >> 1)] = h;
           }
+        } else if (plain_act) {
+          // Linear / ReLU / ReLU2 without bias: the float results of the fp64 reference
+          // expressions (x < 0 ? 0 : x; x * x of a float is exact in fp64)
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float a = pf[e];
+            const float b = p.act == -1 ? a : (a < 0.0f ? 0.0f : (p.act == 0 ? a : a * a));
+            if (staged) {
+              s1[e * 128 + r] = a;
+              if (p.tma_post) s2[e * 128 + r] = b;
+            } else if (t_pass + tc + e < t_begin + t_count && o < p.rows) {
+              const int64_t idx = static_cast<int64_t>(t_pass + tc + e) * p.ld_out + o;
+              p.pre[idx] = a;
+              p.post[idx] = b;
+            }
+          }
         } else {
+          float pg[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) pg[e] = pf[e];
 #pragma unroll 1
           for (int e = 0; e < 16; ++e) {
             const int t = t_pass + tc + e;
             const bool valid = t < t_begin + t_count && o < p.rows;
             float a = 0.0f, b = 0.0f;
-            if (valid) {
-              if (plain_act) {
-                // Linear / ReLU / ReLU2 without bias: the float results of the fp64 reference
-                // expressions (x < 0 ? 0 : x, x * x of a float is exact in fp64)
-                a = pf[e];
-                b = p.act == -1 ? a : (a < 0.0f ? 0.0f : (p.act == 0 ? a : a * a));
-              } else {
-                out_values(p, o, pf[e], a, b);
-              }
-            }
+            if (valid) out_values(p, o, pg[e], a, b);
             if (staged) {
               s1[e * 128 + r] = a;
               s2[e * 128 + r] = b;
