@@ -70,19 +70,17 @@ __global__ void k_rope_prep(const float* __restrict__ q, const float* __restrict
     int c = static_cast<int>(t - static_cast<int64_t>(tok) * (q_dim + 2 * kv_dim));
     const float* src;
     double* dst;
-    int width;
     bool rotate = rot;
     if (c < q_dim) {
-      src = q + static_cast<int64_t>(tok) * q_dim; dst = Qr + static_cast<int64_t>(tok) * q_dim; width = q_dim;
+      src = q + static_cast<int64_t>(tok) * q_dim; dst = Qr + static_cast<int64_t>(tok) * q_dim;
     } else if (c < q_dim + kv_dim) {
       c -= q_dim;
-      src = k + static_cast<int64_t>(tok) * kv_dim; dst = Kr + static_cast<int64_t>(tok) * kv_dim; width = kv_dim;
+      src = k + static_cast<int64_t>(tok) * kv_dim; dst = Kr + static_cast<int64_t>(tok) * kv_dim;
     } else {
       c -= q_dim + kv_dim;
-      src = v + static_cast<int64_t>(tok) * kv_dim; dst = Vd + static_cast<int64_t>(tok) * kv_dim; width = kv_dim;
+      src = v + static_cast<int64_t>(tok) * kv_dim; dst = Vd + static_cast<int64_t>(tok) * kv_dim;
       rotate = false;
     }
-    (void)width;
     const int d = c % head_dim;
     const int base = c - d;
     if (!rotate || d >= 2 * half) {

@@ -187,19 +187,15 @@ __device__ __forceinline__ void out_values(const Params& p, int o, double y, flo
   post = static_cast<float>(activate(p.act, v));
 }
 
-// pair_value with SiLU's exp inline (the GEMM epilogue overlaps a few of them).
+// The SwiGLU product of one Gate/Up pair from the floats the reference rounds Gate and Up to
+// (src/cuda/kernels.cu:296-305), SiLU in fp64 with its exp inline so that the GEMM epilogue
+// overlaps a few of them.
 __device__ __forceinline__ float pair_value_inline(float gate_pre, float up) {
   const double x = static_cast<double>(gate_pre);
   const float g = static_cast<float>(x / (1.0 + exp(-x)));
   return static_cast<float>(static_cast<double>(g) * static_cast<double>(up));
 }
 
-__device__ __forceinline__ float pair_value(double y_gate, double y_up) {
-  const float gate_pre = static_cast<float>(y_gate);
-  const float up = static_cast<float>(y_up);
-  const float g = static_cast<float>(activate(1, static_cast<double>(gate_pre)));
-  return static_cast<float>(static_cast<double>(g) * static_cast<double>(up));
-}
 
 template <typename Params>
 __device__ __forceinline__ void write_out(const Params& p, int t, int o, double y) {
@@ -413,7 +409,52 @@ struct TmParams {
   int64_t ld_h;
   int tma_out;                 // last pass stores through shared memory with bulk tensor stores
   int tma_post;                // ... and post has its own map (post != pre)
+  // Tail schedule (tail_first >= 0): whole tiles for items below tail_first, then each of the
+  // last tiles' K range cut tail_s ways, writing fp64 partials [tail tile][split][TB][128]
+  // to `partial`.
+  int tiles_t, tail_first, tail_s, tail_kbps;
+  int tiles, n_items;           // work items: tiles (x splits), or whole tiles then tail slices
 };
+
+// Token blocks whose plane counts a CTA keeps in shared memory (more blocks: every block runs
+// with xsplit planes).
+constexpr int kTmMaxBlocks = 1024;
+
+// One work item of the persistent GEMM: a tile (128 weight rows x TB tokens) or one K slice
+// of it. The roles of a CTA take items blockIdx.x, + gridDim.x, ... in the same order.
+struct TmItem {
+  int tb, tile_m, t_begin, t_count, kb0, nkb, split, tail_idx;
+  bool tail, part;
+  int P, T, npass, ntot, nacc;  // filled in by the kernel from the block's plane count
+};
+
+__device__ __forceinline__ TmItem decode_item(const TmParams& p, int q) {
+  TmItem it{};
+  int tile;
+  if (p.tail_first >= 0 && q >= p.tail_first) {
+    const int j = q - p.tail_first;
+    it.tail_idx = j / p.tail_s;
+    it.split = j - it.tail_idx * p.tail_s;
+    tile = p.tail_first + it.tail_idx;
+    it.kb0 = it.split * p.tail_kbps;
+    it.nkb = min(p.tail_kbps, p.nkb_total - it.kb0);
+    it.tail = true;
+  } else if (p.splits > 1) {
+    it.split = q / p.tiles;
+    tile = q - it.split * p.tiles;
+    it.kb0 = it.split * p.kb_per_split;
+    it.nkb = min(p.kb_per_split, p.nkb_total - it.kb0);
+  } else {
+    tile = q;
+    it.nkb = p.nkb_total;
+  }
+  it.part = it.tail || p.splits > 1;
+  it.tb = tile % p.tiles_t;  // token block varies fastest: items sharing weight rows run together
+  it.tile_m = tile / p.tiles_t;
+  it.t_begin = it.tb * p.TB;
+  it.t_count = min(p.TB, p.M - it.t_begin);
+  return it;
+}
 
 // Epilogue staging of one converter group (4 warps, 128 rows): 2 buffers x {pre, post} x 16
 // tokens x 128 rows of fp32, in the ring memory the last pass no longer uses.
@@ -545,18 +586,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
   uint64_t* acc_full = s_free + S;         // MMA commit -> epilogue
   uint64_t* acc_empty = acc_full + 1;      // epilogue warps (8) -> MMA
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
-  int* s_planes = reinterpret_cast<int*>(tmem_slot + 1);
+  int* s_pblk = reinterpret_cast<int*>(tmem_slot + 1);  // planes needed per token block
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int t_begin = blockIdx.x * p.TB;   // token block varies fastest: CTAs sharing weight rows run together
-  const int tile_m = blockIdx.y;
-  const int split = blockIdx.z;
-  const int kb0 = split * p.kb_per_split;
-  int nkb = p.nkb_total - kb0;
-  if (nkb > p.kb_per_split) nkb = p.kb_per_split;
-  int t_count = p.M - t_begin;
-  if (t_count > p.TB) t_count = p.TB;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Sw; ++s) {
@@ -569,9 +602,11 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 8);
-    *s_planes = 1;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  const bool pblk_ok = p.tiles_t <= kTmMaxBlocks;
+  if (pblk_ok)
+    for (int b = threadIdx.x; b < p.tiles_t; b += kTmThreads) s_pblk[b] = 1;
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(kTmemCols)
@@ -581,27 +616,28 @@ __global__ void __launch_bounds__(kTmThreads, 1)
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  {
-    int mp = 1;
-    for (int i = threadIdx.x; i < t_count; i += kTmThreads) mp = max(mp, p.pcnt[t_begin + i]);
-    if (mp > 1) atomicMax(s_planes, mp);
-  }
+  if (pblk_ok)
+    for (int t = threadIdx.x; t < p.M; t += kTmThreads) {
+      const int n = p.pcnt[t];
+      if (n > 1) atomicMax(&s_pblk[t / p.TB], n);
+    }
   __syncthreads();
   const uint32_t tmem = *tmem_slot;
-  const int P = min(*s_planes, p.xsplit);
-  const int T = p.tpass[P - 1];
-  const int npass = (t_count + T - 1) / T;
-  const int ntot = P * T;                  // B rows = columns of one accumulator
-  const int n0 = ntot < 256 ? ntot : 256;  // first MMA's N; the second covers [n0, ntot)
-  const int nacc = p.nacc[P - 1];          // independent accumulators (k steps round robin)
-  const int iters = npass * nkb;
-  // Epilogue sums that are single fp32 values (one plane, one accumulator, no Int8 scale, no
-  // split partials) are scaled in fp32; others are summed and scaled in fp64.
-  const bool f32_sums = P == 1 && nacc == 1 && kDt != 9 && p.splits == 1;
+  const int first_item = blockIdx.x, item_step = gridDim.x;
+  // the work item q as this CTA's roles see it: tile, K range, token range, planes
+  auto item = [&](int q) {
+    TmItem it = decode_item(p, q);
+    it.P = pblk_ok ? min(s_pblk[it.tb], p.xsplit) : p.xsplit;
+    it.T = p.tpass[it.P - 1];
+    it.npass = (it.t_count + it.T - 1) / it.T;
+    it.ntot = it.P * it.T;
+    it.nacc = p.nacc[it.P - 1];
+    return it;
+  };
   const bool plain_act = p.bias == nullptr && (p.act == -1 || p.act == 0 || p.act == 6);
 
-  // Loops keep their ring slots and phase bits as running state (Ring): no divisions on the
-  // single-thread critical paths.
+  // Loops keep their ring slots and phase bits as running state (Ring), across the passes and
+  // the work items of this CTA: no divisions on the single-thread critical paths.
   if (warp == 0) {
     // ------------------------------------------------------------------ W producer
     if (lane == 0) {
@@ -611,21 +647,25 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       else
         asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
       const uint32_t wb = p.w_bytes;
-      const uint8_t* wfirst = p.Wg + (static_cast<int64_t>(tile_m) * p.nkb_total + kb0) * wb;
       Ring w;
-      int i = 0, issued = 0;
-      for (int it = 0; it < iters; ++it) {
-        if (!mbar_wait(&w_empty[w.slot], w.phase ^ 1u, p.err, 11)) break;
-        mbar_expect_tx(&w_full[w.slot], wb);
-        bulk_load_hint(wring + w.slot * wb, wfirst + static_cast<int64_t>(i) * wb, wb, &w_full[w.slot], pol);
-        ++issued;
-        w.step(Sw);
-        if (++i == nkb) i = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int qi = first_item; qi < p.n_items && ok; qi += item_step) {
+        const TmItem it = item(qi);
+        const uint8_t* wfirst = p.Wg + (static_cast<int64_t>(it.tile_m) * p.nkb_total + it.kb0) * wb;
+        for (int pass = 0; pass < it.npass && ok; ++pass)
+          for (int i = 0; i < it.nkb; ++i) {
+            if (!mbar_wait(&w_empty[w.slot], w.phase ^ 1u, p.err, 11)) { ok = false; break; }
+            mbar_expect_tx(&w_full[w.slot], wb);
+            bulk_load_hint(wring + w.slot * wb, wfirst + static_cast<int64_t>(i) * wb, wb, &w_full[w.slot], pol);
+            ++issued;
+            w.step(Sw);
+          }
       }
       // tail: the converters released every slot this thread filled before the CTA exits
       Ring t;
-      for (int it = 0; it < issued; ++it) {
-        if (it >= issued - Sw) mbar_wait(&w_empty[t.slot], t.phase, p.err, 12);
+      for (int k = 0; k < issued; ++k) {
+        if (k >= issued - Sw) mbar_wait(&w_empty[t.slot], t.phase, p.err, 12);
         t.step(Sw);
       }
     }
@@ -634,70 +674,81 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     if (lane == 0) {
       uint64_t pol;
       asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
-      const CUtensorMap* tmx = P == 1 ? &tm_x1 : (P == 2 ? &tm_x2 : &tm_x3);
-      const uint32_t tx = static_cast<uint32_t>(ntot * 128);
       Ring r;
       int issued = 0;
       bool ok = true;
-      for (int pass = 0; pass < npass && ok; ++pass) {
-        const int t0 = t_begin + pass * T;
-        for (int i = 0; i < nkb; ++i) {
-          if (!mbar_wait(&s_free[r.slot], r.phase ^ 1u, p.err, 18)) { ok = false; break; }
-          mbar_expect_tx(&s_full[r.slot], tx);
-          uint8_t* dst = xring + r.slot * p.x_bytes;
-          for (int q = 0; q < P; ++q) tma_load_3d_hint(dst + q * T * 128, tmx, (kb0 + i) * kBK, t0, q, &s_full[r.slot], pol);
-          ++issued;
-          r.step(S);
+      for (int qi = first_item; qi < p.n_items && ok; qi += item_step) {
+        const TmItem it = item(qi);
+        const CUtensorMap* tmx = it.P == 1 ? &tm_x1 : (it.P == 2 ? &tm_x2 : &tm_x3);
+        const uint32_t tx = static_cast<uint32_t>(it.ntot * 128);
+        for (int pass = 0; pass < it.npass && ok; ++pass) {
+          const int t0 = it.t_begin + pass * it.T;
+          for (int i = 0; i < it.nkb; ++i) {
+            if (!mbar_wait(&s_free[r.slot], r.phase ^ 1u, p.err, 18)) { ok = false; break; }
+            mbar_expect_tx(&s_full[r.slot], tx);
+            uint8_t* dst = xring + r.slot * p.x_bytes;
+            for (int pl = 0; pl < it.P; ++pl)
+              tma_load_3d_hint(dst + pl * it.T * 128, tmx, (it.kb0 + i) * kBK, t0, pl, &s_full[r.slot], pol);
+            ++issued;
+            r.step(S);
+          }
         }
       }
       // tail: the MMA consumed every stage this thread filled before the CTA exits
       Ring t;
-      for (int it = 0; it < issued; ++it) {
-        if (it >= issued - S) mbar_wait(&s_free[t.slot], t.phase, p.err, 19);
+      for (int k = 0; k < issued; ++k) {
+        if (k >= issued - S) mbar_wait(&s_free[t.slot], t.phase, p.err, 19);
         t.step(S);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc0 =
-          (1u << 4) | (static_cast<uint32_t>(n0 >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
-      const uint32_t idesc1 =
-          (1u << 4) | (static_cast<uint32_t>((ntot - n0) >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
       const uint64_t bd_base = desc_sw128(smem_u32(xring));
       const uint64_t bd_step = static_cast<uint64_t>(p.x_bytes >> 4);   // one x slot, in 16-byte units
-      const uint64_t bd_n0 = static_cast<uint64_t>((n0 * 128) >> 4);     // rows [n0, ntot) of a slot
       Ring r;
       Ring last;
       bool any = false;
       bool ok = true;
-      for (int pass = 0; pass < npass && ok; ++pass) {
-        if (pass > 0) {
-          if (!mbar_wait(acc_empty, static_cast<uint32_t>(pass - 1) & 1u, p.err, 13)) break;
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        }
-        int j = 0;       // accumulator of the next k step (round robin over nacc)
-        int first = 0;   // k steps issued this pass (each accumulator starts fresh on its first)
-        for (int i = 0; i < nkb; ++i) {
-          if (!mbar_wait(&s_full[r.slot], r.phase, p.err, 14)) { ok = false; break; }
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint64_t bd = bd_base + bd_step * static_cast<uint64_t>(r.slot);
-          const uint32_t a = tmem + p.a_col + 32u * static_cast<uint32_t>(r.slot);
-#pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {  // 16 k per MMA: 8 TMEM columns of A, 32 bytes of B
-            const uint32_t d = tmem + static_cast<uint32_t>(j * ntot);
-            const uint32_t acc = first >= nacc ? 1u : 0u;
-            mma_f16_ts(d, a + 8u * k, bd + 2 * k, idesc0, acc);
-            if (ntot > n0) mma_f16_ts(d + static_cast<uint32_t>(n0), a + 8u * k, bd + bd_n0 + 2 * k, idesc1, acc);
-            if (++j == nacc) j = 0;
-            ++first;
+      uint32_t fills = 0;  // accumulator fills so far (one per pass of every item)
+      for (int qi = first_item; qi < p.n_items && ok; qi += item_step) {
+        const TmItem it = item(qi);
+        const int n0 = it.ntot < 256 ? it.ntot : 256;  // first MMA's N; the second covers [n0, ntot)
+        const uint32_t idesc0 =
+            (1u << 4) | (static_cast<uint32_t>(n0 >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
+        const uint32_t idesc1 =
+            (1u << 4) | (static_cast<uint32_t>((it.ntot - n0) >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
+        const uint64_t bd_n0 = static_cast<uint64_t>((n0 * 128) >> 4);  // rows [n0, ntot) of a slot
+        for (int pass = 0; pass < it.npass && ok; ++pass) {
+          if (fills > 0) {  // the epilogue has read the previous fill
+            if (!mbar_wait(acc_empty, (fills - 1) & 1u, p.err, 13)) { ok = false; break; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           }
-          mma_commit(&s_free[r.slot]);
-          last = r;
-          any = true;
-          r.step(S);
+          int j = 0;       // accumulator of the next k step (round robin over nacc)
+          int first = 0;   // k steps issued this pass (each accumulator starts fresh on its first)
+          for (int i = 0; i < it.nkb; ++i) {
+            if (!mbar_wait(&s_full[r.slot], r.phase, p.err, 14)) { ok = false; break; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint64_t bd = bd_base + bd_step * static_cast<uint64_t>(r.slot);
+            const uint32_t a = tmem + p.a_col + 32u * static_cast<uint32_t>(r.slot);
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {  // 16 k per MMA: 8 TMEM columns of A, 32 bytes of B
+              const uint32_t d = tmem + static_cast<uint32_t>(j * it.ntot);
+              const uint32_t acc = first >= it.nacc ? 1u : 0u;
+              mma_f16_ts(d, a + 8u * k, bd + 2 * k, idesc0, acc);
+              if (it.ntot > n0)
+                mma_f16_ts(d + static_cast<uint32_t>(n0), a + 8u * k, bd + bd_n0 + 2 * k, idesc1, acc);
+              if (++j == it.nacc) j = 0;
+              ++first;
+            }
+            mma_commit(&s_free[r.slot]);
+            last = r;
+            any = true;
+            r.step(S);
+          }
+          if (ok) mma_commit(acc_full);
+          ++fills;
         }
-        if (ok) mma_commit(acc_full);
       }
       // drain: the last MMAs issued have completed before TMEM can be released
       if (any) mbar_wait(&s_free[last.slot], last.phase, p.err, 15);
@@ -705,182 +756,197 @@ __global__ void __launch_bounds__(kTmThreads, 1)
   } else if (warp >= 3) {
     // ------------------------------------------------------------------ converters, then epilogue
     const int cw = warp - 3;             // 0..7
-    const int grp = cw >> 2;             // converter group: takes the iterations with it % 2 == grp
+    const int grp = cw >> 2;             // converter group: takes the stages with index % 2 == grp
     const int q = warp & 3;              // TMEM lane quarter of this warp
     const int r = q * 32 + lane;         // weight row within the tile = TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    const int o = tile_m * 128 + r;
     Ring w, st;
-    int it = 0;
+    int stage_idx = 0;
+    uint32_t fills = 0;
     bool ok = true;
-    for (int pass = 0; pass < npass && ok; ++pass) {
-      for (int i = 0; i < nkb; ++i, ++it, w.step(Sw), st.step(S)) {
-        if ((it & 1) != grp) continue;
-        if (!warp_wait(&w_full[w.slot], w.phase, p.err, 16)) { ok = false; break; }
-        uint32_t v[32];
-        convert_row<kDt>(wring + w.slot * p.w_bytes, r, v);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&w_empty[w.slot]);
-        if (!warp_wait(&s_free[st.slot], st.phase ^ 1u, p.err, 21)) { ok = false; break; }
+    for (int qi = first_item; qi < p.n_items && ok; qi += item_step) {
+      const TmItem it = item(qi);
+      const int tile_m = it.tile_m, t_begin = it.t_begin, t_count = it.t_count, T = it.T, P = it.P;
+      const int nacc = it.nacc, ntot = it.ntot, npass = it.npass, split = it.split, tail_idx = it.tail_idx;
+      const bool tail = it.tail, part = it.part;
+      const bool last_item = qi + item_step >= p.n_items;
+      const int o = tile_m * 128 + r;
+      // Epilogue sums that are single fp32 values (one plane, one accumulator, no Int8 scale,
+      // no partials) are scaled in fp32; others are summed and scaled in fp64.
+      const bool f32_sums = P == 1 && nacc == 1 && kDt != 9 && !part;
+      for (int pass = 0; pass < npass && ok; ++pass) {
+        for (int i = 0; i < it.nkb; ++i, ++stage_idx, w.step(Sw), st.step(S)) {
+          if ((stage_idx & 1) != grp) continue;
+          if (!warp_wait(&w_full[w.slot], w.phase, p.err, 16)) { ok = false; break; }
+          uint32_t v[32];
+          convert_row<kDt>(wring + w.slot * p.w_bytes, r, v);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&w_empty[w.slot]);
+          if (!warp_wait(&s_free[st.slot], st.phase ^ 1u, p.err, 21)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          tmem_st32(tmem + lane_base + p.a_col + 32u * static_cast<uint32_t>(st.slot), v);
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_full[st.slot]);
+        }
+        if (!ok) break;
+        // ------------------------------------------------------------ epilogue of this pass
+        if (!warp_wait(acc_full, fills & 1u, p.err, 17)) { ok = false; break; }
+        ++fills;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        tmem_st32(tmem + lane_base + p.a_col + 32u * static_cast<uint32_t>(st.slot), v);
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        const int t_pass = t_begin + pass * T;
+        // The CTA's last pass may stage its outputs in the (then idle) ring memory and leave
+        // them to bulk tensor stores; the CTA only waits for the stores to have read shared
+        // memory. Earlier outputs are stored directly and drain while the next item runs.
+        const bool staged = p.tma_out && !part && last_item && pass == npass - 1;
+        float* stage = reinterpret_cast<float*>(smem + grp * kStageGroup);
+        const bool issuer = q == 0 && lane == 0;  // one thread of the group issues its stores
+        int chunk = 0;
+        for (int tc = grp * 16; tc < T; tc += 32, ++chunk) {
+          // Chunks are 16-token aligned within the block: one that starts past the block's
+          // tokens holds none of them (and may hold the next block's, which a staged store must
+          // not overwrite). Uniform over the group, so its barriers stay matched.
+          if (t_pass + tc >= t_begin + t_count) break;
+          float* s1 = stage + (chunk & 1) * 2 * (kStageBuf / 4);
+          float* s2 = s1 + kStageBuf / 4;
+          // phase 1 (unrolled, cheap): each sum scaled, then kept as the float the reference
+          // rounds it to (pre = float(y); Gate and Up are floats before the product)
+          float pf[16], uf[16];
+          if (f32_sums) {
+            // one plane, one accumulator: the sum is one fp32 value and the scale a power of two,
+            // so the fp32 product is the rounding of the exact (fp64) product
+            uint32_t v[16];
+            tmem_ld16(tmem + lane_base + static_cast<uint32_t>(tc), v);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            const float4* sc4 = reinterpret_cast<const float4*>(p.scale_inv + t_pass + tc);
+#pragma unroll
+            for (int e4 = 0; e4 < 4; ++e4) {
+              const float4 sc = __ldg(sc4 + e4);  // scale_inv holds Mp (multiple of 16) entries
+              const float scv[4] = {sc.x, sc.y, sc.z, sc.w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int e = 4 * e4 + j;
+                const bool valid = t_pass + tc + e < t_begin + t_count && o < p.rows;
+                pf[e] = valid ? __uint_as_float(v[e]) * scv[j] : 0.0f;
+              }
+            }
+          } else {
+            double y[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) y[e] = 0.0;
+            for (int pl = 0; pl < P; ++pl) {
+              for (int jj = 0; jj < nacc; ++jj) {
+                uint32_t v[16];
+                tmem_ld16(tmem + lane_base + static_cast<uint32_t>(jj * ntot + pl * T + tc), v);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int e = 0; e < 16; ++e) y[e] += static_cast<double>(__uint_as_float(v[e]));
+              }
+            }
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int t = t_pass + tc + e;
+              const bool valid = t < t_begin + t_count && o < p.rows;
+              double yy = 0.0;
+              if (valid) {
+                yy = y[e] * static_cast<double>(p.scale_inv[t]);
+                if (kDt == 9) yy *= static_cast<double>((p.pair && (o & 1)) ? p.w_scale2 : p.w_scale);
+              }
+              if (tail) {
+                if (valid)
+                  p.partial[((static_cast<int64_t>(tail_idx) * p.tail_s + split) * p.TB + (t - t_begin)) * 128 + r] = yy;
+              } else if (p.splits > 1) {
+                if (valid) p.partial[(static_cast<int64_t>(split) * p.M + t) * p.rows + o] = yy;
+              }
+              pf[e] = static_cast<float>(yy);
+            }
+          }
+          if (p.pair) {
+            // Up row o + 1 sits in the next lane (rows of a 128-row tile are lanes)
+#pragma unroll
+            for (int e = 0; e < 16; ++e) uf[e] = __shfl_xor_sync(0xffffffffu, pf[e], 1);
+          }
+          if (part) continue;
+          if (staged) {
+            // buffer chunk & 1 was last stored two chunks ago: its reads must be done
+            if (issuer && chunk >= 2) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+            named_bar(1 + grp, 128);
+          }
+          // phase 2: the outputs. pf / uf are only indexed by constants here (kept in registers);
+          // the general bias / activation epilogue runs on a copy one output per iteration so
+          // that its fp64 code appears once.
+          if (p.pair) {
+            // both lanes of a Gate/Up pair work: the Gate lane takes tokens 0..7 of the chunk,
+            // the Up lane 8..15 (each lane holds its row's value and, in uf, its partner's)
+            const bool up_lane = (o & 1) != 0;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int e = (up_lane ? 8 : 0) + k;
+              const int t = t_pass + tc + e;
+              const bool valid = t < t_begin + t_count && o < p.rows;
+              const float h = pair_value_inline(up_lane ? uf[8 + k] : pf[k], up_lane ? pf[8 + k] : uf[k]);
+              if (staged) s1[e * 64 + (r >> 1)] = h;
+              else if (valid) p.h[static_cast<int64_t>(t) * p.ld_h + (o >> 1)] = h;
+            }
+          } else if (plain_act) {
+            // Linear / ReLU / ReLU2 without bias: the float results of the fp64 reference
+            // expressions (x < 0 ? 0 : x; x * x of a float is exact in fp64)
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float a = pf[e];
+              const float b = p.act == -1 ? a : (a < 0.0f ? 0.0f : (p.act == 0 ? a : a * a));
+              if (staged) {
+                s1[e * 128 + r] = a;
+                if (p.tma_post) s2[e * 128 + r] = b;
+              } else if (t_pass + tc + e < t_begin + t_count && o < p.rows) {
+                const int64_t idx = static_cast<int64_t>(t_pass + tc + e) * p.ld_out + o;
+                p.pre[idx] = a;
+                p.post[idx] = b;
+              }
+            }
+          } else {
+            float pg[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) pg[e] = pf[e];
+#pragma unroll 1
+            for (int e = 0; e < 16; ++e) {
+              const int t = t_pass + tc + e;
+              const bool valid = t < t_begin + t_count && o < p.rows;
+              float a = 0.0f, b = 0.0f;
+              if (valid) out_values(p, o, pg[e], a, b);
+              if (staged) {
+                s1[e * 128 + r] = a;
+                s2[e * 128 + r] = b;
+              } else if (valid) {
+                const int64_t idx = static_cast<int64_t>(t) * p.ld_out + o;
+                p.pre[idx] = a;
+                p.post[idx] = b;
+              }
+            }
+          }
+          if (staged) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            named_bar(1 + grp, 128);
+            if (issuer) {
+              const int ty = t_pass + tc;
+              uint64_t pol;
+              asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+              if (p.pair) {
+                tma_store_2d(&tm_o1, s1, tile_m * 64, ty, pol);
+              } else {
+                tma_store_2d(&tm_o1, s1, tile_m * 128, ty, pol);
+                if (p.tma_post) tma_store_2d(&tm_o2, s2, tile_m * 128, ty, pol);
+              }
+              asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            }
+          }
+        }
+        if (staged && issuer) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s_full[st.slot]);
+        if (lane == 0) mbar_arrive(acc_empty);
       }
-      if (!ok) break;
-      // ------------------------------------------------------------ epilogue of this pass
-      if (!warp_wait(acc_full, static_cast<uint32_t>(pass) & 1u, p.err, 17)) break;
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int t_pass = t_begin + pass * T;
-      // The last pass may stage its outputs in the (now idle) ring memory and leave them to
-      // bulk tensor stores, which drain while the SM moves on; the CTA only waits for the
-      // stores to have read shared memory.
-      const bool staged = p.tma_out && pass == npass - 1;
-      float* stage = reinterpret_cast<float*>(smem + grp * kStageGroup);
-      const bool issuer = q == 0 && lane == 0;  // one thread of the group issues its stores
-      int chunk = 0;
-      for (int tc = grp * 16; tc < T; tc += 32, ++chunk) {
-        // Chunks are 16-token aligned within the block: one that starts past the block's
-        // tokens holds none of them (and may hold the next block's, which a staged store must
-        // not overwrite). Uniform over the group, so its barriers stay matched.
-        if (t_pass + tc >= t_begin + t_count) break;
-        float* s1 = stage + (chunk & 1) * 2 * (kStageBuf / 4);
-        float* s2 = s1 + kStageBuf / 4;
-        // phase 1 (unrolled, cheap): each sum scaled, then kept as the float the reference
-        // rounds it to (pre = float(y); Gate and Up are floats before the product)
-        float pf[16], uf[16];
-        if (f32_sums) {
-          // one plane, one accumulator: the sum is one fp32 value and the scale a power of two,
-          // so the fp32 product is the rounding of the exact (fp64) product
-          uint32_t v[16];
-          tmem_ld16(tmem + lane_base + static_cast<uint32_t>(tc), v);
-          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-          const float4* sc4 = reinterpret_cast<const float4*>(p.scale_inv + t_pass + tc);
-#pragma unroll
-          for (int e4 = 0; e4 < 4; ++e4) {
-            const float4 sc = __ldg(sc4 + e4);  // scale_inv holds Mp (multiple of 16) entries
-            const float scv[4] = {sc.x, sc.y, sc.z, sc.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int e = 4 * e4 + j;
-              const bool valid = t_pass + tc + e < t_begin + t_count && o < p.rows;
-              pf[e] = valid ? __uint_as_float(v[e]) * scv[j] : 0.0f;
-            }
-          }
-        } else {
-          double y[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) y[e] = 0.0;
-          for (int pl = 0; pl < P; ++pl) {
-            for (int jj = 0; jj < nacc; ++jj) {
-              uint32_t v[16];
-              tmem_ld16(tmem + lane_base + static_cast<uint32_t>(jj * ntot + pl * T + tc), v);
-              asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-              for (int e = 0; e < 16; ++e) y[e] += static_cast<double>(__uint_as_float(v[e]));
-            }
-          }
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int t = t_pass + tc + e;
-            const bool valid = t < t_begin + t_count && o < p.rows;
-            double yy = 0.0;
-            if (valid) {
-              yy = y[e] * static_cast<double>(p.scale_inv[t]);
-              if (kDt == 9) yy *= static_cast<double>((p.pair && (o & 1)) ? p.w_scale2 : p.w_scale);
-            }
-            if (p.splits > 1) {
-              if (valid) p.partial[(static_cast<int64_t>(split) * p.M + t) * p.rows + o] = yy;
-            }
-            pf[e] = static_cast<float>(yy);
-          }
-        }
-        if (p.pair) {
-          // Up row o + 1 sits in the next lane (rows of a 128-row tile are lanes)
-#pragma unroll
-          for (int e = 0; e < 16; ++e) uf[e] = __shfl_xor_sync(0xffffffffu, pf[e], 1);
-        }
-        if (p.splits > 1) continue;
-        if (staged) {
-          // buffer chunk & 1 was last stored two chunks ago: its reads must be done
-          if (issuer && chunk >= 2) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-          named_bar(1 + grp, 128);
-        }
-        // phase 2: the outputs. pf / uf are only indexed by constants here (kept in registers);
-        // the general bias / activation epilogue runs on a copy one output per iteration so
-        // that its fp64 code appears once.
-        if (p.pair) {
-          // both lanes of a Gate/Up pair work: the Gate lane takes tokens 0..7 of the chunk,
-          // the Up lane 8..15 (each lane holds its row's value and, in uf, its partner's)
-          const bool up_lane = (o & 1) != 0;
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int e = (up_lane ? 8 : 0) + k;
-            const int t = t_pass + tc + e;
-            const bool valid = t < t_begin + t_count && o < p.rows;
-            const float h = pair_value_inline(up_lane ? uf[8 + k] : pf[k], up_lane ? pf[8 + k] : uf[k]);
-            if (staged) s1[e * 64 + (r >> 1)] = h;
-            else if (valid) p.h[static_cast<int64_t>(t) * p.ld_h + (o >> 1)] = h;
-          }
-        } else if (plain_act) {
-          // Linear / ReLU / ReLU2 without bias: the float results of the fp64 reference
-          // expressions (x < 0 ? 0 : x; x * x of a float is exact in fp64)
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float a = pf[e];
-            const float b = p.act == -1 ? a : (a < 0.0f ? 0.0f : (p.act == 0 ? a : a * a));
-            if (staged) {
-              s1[e * 128 + r] = a;
-              if (p.tma_post) s2[e * 128 + r] = b;
-            } else if (t_pass + tc + e < t_begin + t_count && o < p.rows) {
-              const int64_t idx = static_cast<int64_t>(t_pass + tc + e) * p.ld_out + o;
-              p.pre[idx] = a;
-              p.post[idx] = b;
-            }
-          }
-        } else {
-          float pg[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) pg[e] = pf[e];
-#pragma unroll 1
-          for (int e = 0; e < 16; ++e) {
-            const int t = t_pass + tc + e;
-            const bool valid = t < t_begin + t_count && o < p.rows;
-            float a = 0.0f, b = 0.0f;
-            if (valid) out_values(p, o, pg[e], a, b);
-            if (staged) {
-              s1[e * 128 + r] = a;
-              s2[e * 128 + r] = b;
-            } else if (valid) {
-              const int64_t idx = static_cast<int64_t>(t) * p.ld_out + o;
-              p.pre[idx] = a;
-              p.post[idx] = b;
-            }
-          }
-        }
-        if (staged) {
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          named_bar(1 + grp, 128);
-          if (issuer) {
-            const int ty = t_pass + tc;
-            uint64_t pol;
-            asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-            if (p.pair) {
-              tma_store_2d(&tm_o1, s1, tile_m * 64, ty, pol);
-            } else {
-              tma_store_2d(&tm_o1, s1, tile_m * 128, ty, pol);
-              if (p.tma_post) tma_store_2d(&tm_o2, s2, tile_m * 128, ty, pol);
-            }
-            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-          }
-        }
-      }
-      if (staged && issuer) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty);
     }
   }
 
@@ -916,6 +982,47 @@ __global__ void k_splitk_reduce(const KParams p) {
     double y = 0.0;
     for (int s = 0; s < p.splits; ++s) y += p.partial[s * n + i];
     write_out(p, static_cast<int>(i / p.rows), static_cast<int>(i % p.rows), y);
+  }
+}
+
+// Sum of the tail tiles' K-slice partials ([tail tile][split][TB][128] fp64) in split order,
+// then the epilogue of write_out / write_pair. One thread per (tail tile, token, row) -- per
+// Gate/Up pair in pair mode.
+struct TailParams {
+  int rows, M, TB, tiles_t, tail_first, tail_s, ntail;
+  const double* partial;
+  float* pre;
+  float* post;
+  int64_t ld_out;
+  const double* bias;
+  int bias_len;
+  int act;
+  int pair;
+  float* h;
+  int64_t ld_h;
+};
+
+__global__ void k_tail_reduce(const TailParams p) {
+  const int per_tile = p.TB * (p.pair ? 64 : 128);
+  const int64_t n = static_cast<int64_t>(p.ntail) * per_tile;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int k = static_cast<int>(i / per_tile);
+    const int rem = static_cast<int>(i - static_cast<int64_t>(k) * per_tile);
+    const int tile = p.tail_first + k;
+    const int t = (tile % p.tiles_t) * p.TB + rem / (p.pair ? 64 : 128);
+    const int r = p.pair ? 2 * (rem % 64) : rem % 128;
+    const int o = (tile / p.tiles_t) * 128 + r;
+    if (t >= p.M || o >= p.rows) continue;
+    const double* base = p.partial + (static_cast<int64_t>(k) * p.tail_s * p.TB + (t % p.TB)) * 128 + r;
+    const int64_t stride = static_cast<int64_t>(p.TB) * 128;
+    double y = 0.0, y2 = 0.0;
+    for (int sp = 0; sp < p.tail_s; ++sp) {
+      y += base[sp * stride];
+      if (p.pair) y2 += base[sp * stride + 1];
+    }
+    if (p.pair) write_pair(p, t, o >> 1, y, y2);
+    else write_out(p, t, o, y);
   }
 }
 
@@ -1073,6 +1180,8 @@ Plan make_plan(int M, int cols, int rows, int xsplit, DType dt) {
 
 struct TmPlan {
   int TB, tpass[3], nacc[3], Mp, Kp, nkb, splits, kb_per_split, kbb, acc_cols;
+  int tiles_t, tiles, tail_first, tail_s, tail_kbps;  // tail schedule (tail_first < 0: none)
+  int pblk_bytes;                                      // per-token-block plane counts (shared memory)
   int sx, sw;
   uint32_t x_bytes, w_bytes, a_col;
   size_t smem;
@@ -1101,7 +1210,7 @@ int tm_splits(int tiles, int nkb, int M, int rows) {
   return best;
 }
 
-TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt) {
+TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_tail = true) {
   TmPlan pl{};
   const int m16 = static_cast<int>(round_up(M, 16));
   pl.TB = m16 < 256 ? m16 : 256;
@@ -1128,14 +1237,16 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt) {
   // stages (an x slot + a TMEM A slot each): as many as TMEM and shared memory allow, up to 8,
   // keeping room for 8 W slots; then the W ring takes the rest (up to 32). 1 KB aligns the
   // base, 1 KB holds the barriers (at most 2*32 + 2*8 + 2 of them).
-  const int64_t budget = 227 * 1024 - 2048;
+  const int tiles_t_plan = (M + pl.TB - 1) / pl.TB;
+  pl.pblk_bytes = static_cast<int>(round_up(static_cast<int64_t>(std::min(tiles_t_plan, kTmMaxBlocks)) * 4, 16));
+  const int64_t budget = 227 * 1024 - 2048 - pl.pblk_bytes;
   pl.sx = (static_cast<int>(kTmemCols) - static_cast<int>(pl.a_col)) / 32;
   if (pl.sx > 8) pl.sx = 8;
   while (pl.sx > 2 && pl.sx * static_cast<int64_t>(pl.x_bytes) + 8 * static_cast<int64_t>(pl.w_bytes) > budget)
     --pl.sx;
   pl.sw = static_cast<int>((budget - pl.sx * static_cast<int64_t>(pl.x_bytes)) / pl.w_bytes);
   if (pl.sw > 32) pl.sw = 32;
-  pl.smem = static_cast<size_t>(pl.sx) * pl.x_bytes + static_cast<size_t>(pl.sw) * pl.w_bytes + 2048;
+  pl.smem = static_cast<size_t>(pl.sx) * pl.x_bytes + static_cast<size_t>(pl.sw) * pl.w_bytes + 2048 + pl.pblk_bytes;
   // At least half the SM's shared memory, so that one CTA (and its 512 TMEM columns) runs per
   // SM: a second CTA on the SM would only stall in tcgen05.alloc.
   if (pl.smem < 116 * 1024) pl.smem = 116 * 1024;
@@ -1147,6 +1258,26 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt) {
   pl.scale_bytes = static_cast<size_t>(round_up(static_cast<int64_t>(pl.Mp) * 4, 1024));
   pl.pcnt_bytes = pl.scale_bytes;
   pl.partial_bytes = pl.splits > 1 ? static_cast<size_t>(pl.splits) * M * rows * 8 : 0;
+  // A last, partly filled wave of whole tiles (up to half the SMs) costs as long as a full
+  // one: those tiles are cut along K instead (into at most 8 slices, one wave of items in
+  // all), and their fp64 partials summed by a small reduce launch.
+  pl.tiles_t = (M + pl.TB - 1) / pl.TB;
+  pl.tiles = tiles;
+  pl.tail_first = -1;
+  pl.tail_s = 1;
+  pl.tail_kbps = pl.nkb;
+  const int ntail = tiles % 148;
+  if (allow_tail && pl.splits == 1 && tiles > 148 && ntail > 0 && ntail <= 74 && pl.nkb >= 2) {
+    int s = 148 / ntail;
+    if (s > 8) s = 8;
+    if (s > pl.nkb) s = pl.nkb;
+    if (s >= 2) {
+      pl.tail_kbps = (pl.nkb + s - 1) / s;
+      pl.tail_s = (pl.nkb + pl.tail_kbps - 1) / pl.tail_kbps;  // every slice non-empty
+      pl.tail_first = tiles - ntail;
+      pl.partial_bytes = static_cast<size_t>(ntail) * pl.tail_s * pl.TB * 128 * 8;
+    }
+  }
   return pl;
 }
 
@@ -1237,11 +1368,11 @@ int gemm_token_tile(int M, int xsplit) {
   return t;
 }
 
-size_t gemm_scratch_bytes(int M, int cols, int rows, int xsplit) {
+size_t gemm_scratch_bytes(int M, int cols, int rows, int xsplit, bool tail) {
   size_t need = 0;
   for (DType dt : {DType::FP8E4M3, DType::FP4}) {
     const Plan pl = make_plan(M, cols, rows, xsplit, dt);
-    const TmPlan tp = make_tm_plan(M, cols, rows, xsplit, dt);
+    const TmPlan tp = make_tm_plan(M, cols, rows, xsplit, dt, tail);
     need = std::max(need, pl.planes_bytes + pl.scale_bytes + pl.partial_bytes);
     need = std::max(need, tp.planes_bytes + tp.scale_bytes + tp.pcnt_bytes + tp.partial_bytes);
   }
@@ -1272,17 +1403,22 @@ Status set_max_smem(const void* kern, size_t bytes) {
 Status launch_tm(const GemmArgs& a, cudaStream_t st) {
   if (!a.Wg || (reinterpret_cast<uintptr_t>(a.Wg) & 15) != 0)
     return Status::Internal("gemm_tc: the layer has no GEMM mirror (16-byte aligned)");
-  const TmPlan pl = make_tm_plan(a.M, a.cols, a.rows, a.xsplit, a.dtype);
+  TmPlan pl = make_tm_plan(a.M, a.cols, a.rows, a.xsplit, a.dtype);
   if (pl.sw < 2 || pl.sx < 2 || pl.a_col + 32u * pl.sx > kTmemCols)
     return Status::Internal("gemm_tc: pipeline does not fit on the SM");
-  const size_t need = pl.planes_bytes + pl.scale_bytes + pl.pcnt_bytes + pl.partial_bytes;
+  size_t need = pl.planes_bytes + pl.scale_bytes + pl.pcnt_bytes + pl.partial_bytes;
+  if (pl.tail_first >= 0 && a.scratch_bytes < need) {  // no room for the tail partials
+    pl = make_tm_plan(a.M, a.cols, a.rows, a.xsplit, a.dtype, false);
+    need = pl.planes_bytes + pl.scale_bytes + pl.pcnt_bytes + pl.partial_bytes;
+  }
   if (!a.scratch || a.scratch_bytes < need) return Status::Internal("gemm_tc: scratch too small");
   uint8_t* scr = static_cast<uint8_t*>(a.scratch);
   __half* planes = reinterpret_cast<__half*>(scr);
   float* scale_inv = reinterpret_cast<float*>(scr + pl.planes_bytes);
   int* pcnt = reinterpret_cast<int*>(scr + pl.planes_bytes + pl.scale_bytes);
-  double* partial =
-      pl.splits > 1 ? reinterpret_cast<double*>(scr + pl.planes_bytes + pl.scale_bytes + pl.pcnt_bytes) : nullptr;
+  double* partial = pl.splits > 1 || pl.tail_first >= 0
+                        ? reinterpret_cast<double*>(scr + pl.planes_bytes + pl.scale_bytes + pl.pcnt_bytes)
+                        : nullptr;
 
   k_split_x<<<pl.Mp, kSplitThreads, 0, st>>>(a.x, a.x_ld, a.M, a.cols, pl.Mp, pl.Kp, a.xsplit, planes, scale_inv,
                                              pcnt);
@@ -1310,6 +1446,9 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
   p.bias = a.bias; p.bias_len = a.bias_len; p.act = a.act;
   p.partial = partial; p.err = a.err;
   p.pair = a.pair ? 1 : 0; p.w_scale2 = a.scale2; p.h = a.h; p.ld_h = a.ld_h;
+  p.tiles_t = pl.tiles_t; p.tail_first = pl.tail_first; p.tail_s = pl.tail_s; p.tail_kbps = pl.tail_kbps;
+  p.tiles = pl.tiles;
+  p.n_items = pl.tail_first >= 0 ? pl.tail_first + (pl.tiles - pl.tail_first) * pl.tail_s : pl.tiles * pl.splits;
 
   // Outputs through bulk tensor stores (the last pass stages them in the idle ring memory):
   // fp32 rows whose pitch is a multiple of 16 bytes at 16-byte aligned bases.
@@ -1341,9 +1480,14 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
   }
 
   const size_t smem = pl.smem;
-  dim3 grid(static_cast<unsigned>((a.M + pl.TB - 1) / pl.TB), static_cast<unsigned>((a.rows + kBM - 1) / kBM),
-            static_cast<unsigned>(pl.splits));
-  if (grid.y > 65535) return Status::Invalid("gemm_tc: too many weight rows for one launch");
+  // persistent: one CTA per SM (or per item when there are fewer), each looping over items
+  int sms = 148;
+  {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms < 1) sms = 148;
+  }
+  const dim3 grid(static_cast<unsigned>(p.n_items < sms ? p.n_items : sms), 1, 1);
   auto launch = [&](auto kern) -> Status {
     WB_TRY(set_max_smem(reinterpret_cast<const void*>(kern), smem));
     kern<<<grid, kTmThreads, smem, st>>>(tm_x[0], tm_x[1], tm_x[2], tm_o[0], tm_o[1], p);
@@ -1355,6 +1499,17 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
   case DType::FP8E5M2: WB_TRY(launch(k_gemm_tm<5>)); break;
   case DType::Int8: WB_TRY(launch(k_gemm_tm<9>)); break;
   default: return Status::Unsupported("gemm_tc: dtype");
+  }
+  if (pl.tail_first >= 0) {
+    const int ntail = pl.tiles - pl.tail_first;
+    TailParams r{};
+    r.rows = a.rows; r.M = a.M; r.TB = pl.TB; r.tiles_t = pl.tiles_t; r.tail_first = pl.tail_first;
+    r.tail_s = pl.tail_s; r.ntail = ntail; r.partial = partial;
+    r.pre = a.pre; r.post = a.post; r.ld_out = a.ld_out; r.bias = a.bias; r.bias_len = a.bias_len; r.act = a.act;
+    r.pair = a.pair ? 1 : 0; r.h = a.h; r.ld_h = a.ld_h;
+    const int64_t n = static_cast<int64_t>(ntail) * pl.TB * (a.pair ? 64 : 128);
+    k_tail_reduce<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(r);
+    WB_CUDA(cudaGetLastError());
   }
   if (pl.splits > 1) {
     KParams r{};
@@ -1474,7 +1629,7 @@ void* g_static_ptr[kMaxDevices] = {};
 size_t gemm_static_scratch_bytes() { return kStaticScratchBytes; }
 
 Status launch_gemm_tc_static(const GemmArgs& a_in, cudaStream_t st) {
-  const size_t need = gemm_scratch_bytes(a_in.M, a_in.cols, a_in.rows, a_in.xsplit);
+  const size_t need = gemm_scratch_bytes(a_in.M, a_in.cols, a_in.rows, a_in.xsplit, false);
   if (need > kStaticScratchBytes)
     return Status::Invalid("allocation-free forward: needs " + std::to_string(need) +
                            " bytes of scratch, the static array holds " + std::to_string(kStaticScratchBytes) +

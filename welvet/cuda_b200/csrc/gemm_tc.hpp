@@ -47,8 +47,10 @@ struct GemmArgs {
 
 // Token tile (B rows per plane) used for M tokens; the MMA N is xsplit * tile.
 int gemm_token_tile(int M, int xsplit);
-// Bytes of scratch a launch with these sizes needs (planes, per-token scales, split-K partials).
-size_t gemm_scratch_bytes(int M, int cols, int rows, int xsplit);
+// Bytes of scratch a launch with these sizes needs (planes, per-token scales, split-K partials;
+// with `tail`, room for the K slices of a last partial wave's tiles, which the launch uses
+// when the scratch it is given holds them).
+size_t gemm_scratch_bytes(int M, int cols, int rows, int xsplit, bool tail = true);
 
 bool gemm_supported(DType dt);
 

@@ -224,28 +224,28 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv(const GemvArgs a) {
           if constexpr (kExact) {
             dot_vector_exact<kDt, kB>(wv[u], xv, a.x_stride, a.scale, acc);
             if (kDual) dot_vector_exact<kDt, kB>(wv2[u], xv, a.x_stride, a.scale2, acc2);
-            continue;
-          }
-          float part[kRows][kB];
-#pragma unroll
-          for (int r = 0; r < kRows; ++r)
-#pragma unroll
-            for (int b = 0; b < kB; ++b) part[r][b] = 0.0f;
-          dot_vector<kDt, kB>(wv[u], xv, a.x_stride, part);
-#pragma unroll
-          for (int r = 0; r < kRows; ++r)
-#pragma unroll
-            for (int b = 0; b < kB; ++b) acc[r][b] += static_cast<double>(part[r][b]);
-          if (kDual) {
+          } else {
+            float part[kRows][kB];
 #pragma unroll
             for (int r = 0; r < kRows; ++r)
 #pragma unroll
               for (int b = 0; b < kB; ++b) part[r][b] = 0.0f;
-            dot_vector<kDt, kB>(wv2[u], xv, a.x_stride, part);
+            dot_vector<kDt, kB>(wv[u], xv, a.x_stride, part);
 #pragma unroll
             for (int r = 0; r < kRows; ++r)
 #pragma unroll
-              for (int b = 0; b < kB; ++b) acc2[r][b] += static_cast<double>(part[r][b]);
+              for (int b = 0; b < kB; ++b) acc[r][b] += static_cast<double>(part[r][b]);
+            if (kDual) {
+#pragma unroll
+              for (int r = 0; r < kRows; ++r)
+#pragma unroll
+                for (int b = 0; b < kB; ++b) part[r][b] = 0.0f;
+              dot_vector<kDt, kB>(wv2[u], xv, a.x_stride, part);
+#pragma unroll
+              for (int r = 0; r < kRows; ++r)
+#pragma unroll
+                for (int b = 0; b < kB; ++b) acc2[r][b] += static_cast<double>(part[r][b]);
+            }
           }
         }
       }
