@@ -104,6 +104,15 @@ typedef struct welvet_model_session welvet_model_session;
 typedef struct welvet_cuda_blob { uint8_t* data; size_t size; } welvet_cuda_blob;
 WELVET_API int32_t welvet_model_abi_version(void);
 WELVET_API void welvet_cuda_blob_free(welvet_cuda_blob*);
+/* reference include/welvet_c.h:48-49 and the release of model_session.cpp -- a WMN1 model
+ * descriptor (Stack or Grid root of Dense / RMSNorm / SwiGLU / MHA children, weights from its
+ * store section) mounted on the GPU; forward takes and returns tensor records (int32 rank,
+ * int32 dims, float32 data), the output blob freed with welvet_cuda_blob_free. Other roots
+ * and child kinds: status 3. The other welvet_model_* entry points (training) are gaps. */
+WELVET_API welvet_status welvet_model_mount(const uint8_t* descriptor, size_t size, welvet_model_session** out);
+WELVET_API welvet_status welvet_model_forward(welvet_model_session* s, const uint8_t* input, size_t size,
+                                              welvet_cuda_blob* out);
+WELVET_API void welvet_model_release(welvet_model_session* s);
 
 #ifdef __cplusplus
 }

@@ -52,7 +52,7 @@ def test_out_of_scope_entry_points_return_gap():
     class St(ctypes.Structure):
         _fields_ = [("code", ctypes.c_int32), ("message", ctypes.c_char * 256)]
 
-    for name in ("welvet_layernorm_forward_f32", "welvet_dense_normalbp_f32", "welvet_model_mount"):
+    for name in ("welvet_layernorm_forward_f32", "welvet_dense_normalbp_f32", "welvet_model_train_mse"):
         fn = getattr(L, name)
         fn.restype = St
         fn.argtypes = []
@@ -73,3 +73,43 @@ def test_no_gpu_is_reported_not_faked():
     L = ctypes.CDLL(LIB)
     L.welvet_cuda_available.restype = ctypes.c_int32
     assert L.welvet_cuda_available() == 0
+
+
+def test_model_descriptor_checks_without_cuda():
+    """welvet_model_mount reads the WMN1 descriptor before touching the GPU: bad arguments,
+    versions and layouts are status 1, model roots and child kinds off this path status 3
+    (src/interop/model_session.cpp:317-396; include/welvet/interop/child_wire.hpp)."""
+    import struct
+    from wmn1 import dense_child, descriptor, store_f32
+
+    L = ctypes.CDLL(LIB)
+
+    class St(ctypes.Structure):
+        _fields_ = [("code", ctypes.c_int32), ("message", ctypes.c_char * 256)]
+
+    L.welvet_model_mount.restype = St
+    L.welvet_model_mount.argtypes = [ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]
+
+    def mount(b):
+        h = ctypes.c_void_p()
+        st = L.welvet_model_mount(b, len(b), ctypes.byref(h))
+        assert not h.value
+        return st.code, st.message.decode()
+
+    code, msg = mount(b"")
+    assert code == 1 and "invalid mount arguments" in msg
+    good = descriptor(0, [dense_child(4, 3, -1, 1, [0.5] * 12)], [store_f32(3, 4, [0.5] * 12)])
+    code, msg = mount(b"XXXX" + good[4:])
+    assert code == 1 and "descriptor version" in msg
+    code, msg = mount(good + b"\0\0\0\0")
+    assert code == 1 and "trailing" in msg
+    code, msg = mount(good[:-8])
+    assert code == 1
+    par = bytearray(good)
+    par[4:8] = struct.pack("<i", 1)  # Parallel root
+    assert mount(bytes(par))[0] == 3
+    ln = struct.pack("<i", 3) + struct.pack("<iid", 4, 1, 1e-5) + struct.pack("<4f", 1, 1, 1, 1) * 2
+    code, msg = mount(descriptor(0, [ln], []))  # LayerNorm child
+    assert code == 3 and "kind 3" in msg
+    code, msg = mount(descriptor(0, [dense_child(4, 3, -1, 1, [0.5] * 12)], []))  # no stores
+    assert code == 1 and "store count" in msg

@@ -381,11 +381,13 @@ GEMM_TOL = {"3": 2.0 ** -16, "2": 2.0 ** -15, "1": 2.0 ** -9}
 @pytest.mark.parametrize("xsplit", ["3", "2", "1"])
 @pytest.mark.parametrize("dt", [16, 4, 5, 9])
 @pytest.mark.parametrize("shape", [(128, 64, 8), (300, 1000, 16), (256, 4096, 64), (130, 257, 100), (1024, 512, 5),
-                                   (200, 640, 300), (384, 192, 520)])
+                                   (200, 640, 300), (384, 192, 520), (9600, 256, 300)])
 def test_tensor_core_path_parity(wb, oracle, dt, shape, xsplit, kernel, monkeypatch):
-    """Batches above 4 run the tcgen05 GEMM (f16 planes of x, exact products, fp32 tensor
-    accumulation), with the dequantised weights in TMEM (default) or in shared memory. Error
-    normalised by sum_k |W x| stays under the stated bound per x split."""
+    """Batches above 8 run the tcgen05 GEMM (f16 planes of x, exact products, fp32 tensor
+    accumulation), with the dequantised weights in TMEM (default, persistent CTAs looping
+    over tiles) or in shared memory. Error normalised by sum_k |W x| stays under the stated
+    bound per x split. 9600 x 256 at 300 tokens: 150 tiles over two token blocks, the last
+    two cut along K (tail launch)."""
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
     monkeypatch.setenv("WELVET_B200_XSPLIT", xsplit)
     monkeypatch.setenv("WELVET_B200_GEMM", kernel)
@@ -455,12 +457,13 @@ def test_simt_gemv_still_correct(wb, oracle, dt, monkeypatch):
 
 
 @pytest.mark.parametrize("rows,d,inter", [(1, 256, 640), (3, 256, 640), (24, 256, 640), (300, 256, 640),
-                                          (24, 2048, 96)])
+                                          (24, 2048, 96), (16, 256, 9600)])
 @pytest.mark.parametrize("dt", [16, 4, 9])
 def test_swiglu_tensor_paths(wb, oracle, dt, rows, d, inter, monkeypatch):
     """1..4 rows: Gate and Up fused in the tensor GEMV; more: one tcgen05 GEMM over the
     interleaved Gate/Up pair mirror writing h in its epilogue (300 rows: several token
-    blocks; d = 2048 with a narrow intermediate: split-K with the paired reduce)."""
+    blocks; d = 2048 with a narrow intermediate: split-K with the paired reduce; 9600: 150
+    pair tiles, the last two cut along K and reduced by the tail launch)."""
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
     rng = np.random.default_rng(20 + rows)
     G, U, D = [(rng.standard_normal(s) * 0.5).astype(np.float32) for s in ((inter, d), (inter, d), (d, inter))]

@@ -374,6 +374,62 @@ class MhaCell:
             pass
 
 
+# ------------------------------------------------------------------ model sessions
+
+
+class welvet_cuda_blob(ctypes.Structure):
+    _fields_ = [("data", ctypes.POINTER(c_uint8)), ("size", c_size_t)]
+
+
+_sig("welvet_model_mount", _ST, c_void_p, c_size_t, POINTER(c_void_p))
+_sig("welvet_model_forward", _ST, c_void_p, c_void_p, c_size_t, POINTER(welvet_cuda_blob))
+_sig("welvet_model_release", None, c_void_p)
+_sig("welvet_cuda_blob_free", None, POINTER(welvet_cuda_blob))
+
+
+def tensor_record(x) -> bytes:
+    """The reference's tensor record: int32 rank, int32 dims, float32 data (little-endian)."""
+    x = np.ascontiguousarray(x, dtype="<f4")
+    return np.array([x.ndim, *x.shape], dtype="<i4").tobytes() + x.tobytes()
+
+
+def parse_tensor_record(b: bytes) -> np.ndarray:
+    rank = int(np.frombuffer(b, dtype="<i4", count=1)[0])
+    dims = np.frombuffer(b, dtype="<i4", count=rank, offset=4)
+    return np.frombuffer(b, dtype="<f4", offset=4 * (1 + rank)).reshape(tuple(int(d) for d in dims)).copy()
+
+
+class ModelSession:
+    """welvet_model_mount / welvet_model_forward / welvet_model_release: a stored WMN1 model
+    (Stack or Grid root of Dense, RMSNorm, SwiGLU and MHA children) resident on the GPU."""
+
+    def __init__(self, descriptor: bytes):
+        self._h = c_void_p()
+        buf = ctypes.create_string_buffer(bytes(descriptor), len(descriptor))
+        check(_L.welvet_model_mount(ctypes.addressof(buf), len(descriptor), byref(self._h)))
+
+    def forward(self, x) -> np.ndarray:
+        rec = tensor_record(x)
+        buf = ctypes.create_string_buffer(rec, len(rec))
+        blob = welvet_cuda_blob()
+        check(_L.welvet_model_forward(self._h, ctypes.addressof(buf), len(rec), byref(blob)))
+        try:
+            return parse_tensor_record(ctypes.string_at(blob.data, blob.size))
+        finally:
+            _L.welvet_cuda_blob_free(byref(blob))
+
+    def release(self) -> None:
+        if self._h:
+            _L.welvet_model_release(self._h)
+            self._h = c_void_p()
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+
 # ------------------------------------------------------------------ codecs
 
 def codec_digest(codec: int, start: int, count: int) -> int:

@@ -7,6 +7,7 @@
 #include "cells.hpp"
 #include "codec.hpp"
 #include "dense.hpp"
+#include "model.hpp"
 
 #include <cstdio>
 #include <cstdlib>
@@ -18,6 +19,9 @@
 
 struct welvet_dense_session {
   wb::DenseSession* s;
+};
+struct welvet_model_session {
+  wb::ModelSession* s;
 };
 struct welvet_b200_swiglu {
   wb::SwigluCell cell;
@@ -88,8 +92,8 @@ struct DevPtr {
 
 wb::Status gap(const char* what) { return wb::Status::Err(wb::StatusCode::Gap, std::string("gap? ") + what + " (not on the b200 quantized forward path)"); }
 
-constexpr int32_t kGapSymbols = 56;  // the status-3 stubs at the end of this file
-constexpr int32_t kServedSymbols = 15;  // reference symbols served on the GPU
+constexpr int32_t kGapSymbols = 54;  // the status-3 stubs at the end of this file
+constexpr int32_t kServedSymbols = 17;  // reference symbols served on the GPU
 
 } // namespace
 
@@ -128,6 +132,52 @@ void welvet_cuda_blob_free(welvet_cuda_blob* b) {
   std::free(b->data);
   b->data = nullptr;
   b->size = 0;
+}
+
+// ------------------------------------------------------------------------- model sessions
+
+welvet_status welvet_model_mount(const uint8_t* descriptor, size_t size, welvet_model_session** out) {
+  if (out) *out = nullptr;
+  try {
+    wb::ModelSession* m = nullptr;
+    const wb::Status st = wb::model_mount(descriptor, size, &m);
+    if (!st.ok()) return to_c(st);
+    if (!out) {
+      delete m;
+      return to_c(wb::Status::Invalid("invalid mount arguments"));
+    }
+    *out = new welvet_model_session{m};
+    return to_c(st);
+  } catch (const std::exception& e) {
+    return to_c(wb::Status::Internal(e.what()));
+  }
+}
+
+welvet_status welvet_model_forward(welvet_model_session* s, const uint8_t* input, size_t size,
+                                   welvet_cuda_blob* out) {
+  try {
+    if (!s || !s->s || !input || !out) return to_c(wb::Status::Invalid("invalid forward arguments"));
+    out->data = nullptr;
+    out->size = 0;
+    std::vector<uint8_t> bytes;
+    const wb::Status st = wb::model_forward(s->s, input, size, &bytes);
+    if (!st.ok()) return to_c(st);
+    // the blob is malloc'ed as the reference's (model_session.cpp:123-134): welvet_cuda_blob_free
+    void* p = std::malloc(bytes.size());
+    if (!p && !bytes.empty()) return to_c(wb::Status::Internal("out of host memory"));
+    if (!bytes.empty()) std::memcpy(p, bytes.data(), bytes.size());
+    out->data = static_cast<uint8_t*>(p);
+    out->size = bytes.size();
+    return to_c(st);
+  } catch (const std::exception& e) {
+    return to_c(wb::Status::Internal(e.what()));
+  }
+}
+
+void welvet_model_release(welvet_model_session* s) {
+  if (!s) return;
+  delete s->s;
+  delete s;
 }
 
 // ------------------------------------------------------------------------- Dense
@@ -506,8 +556,6 @@ welvet_status welvet_b200_codec_selftest_decode(int32_t dtype, float* out_host) 
 #define WB_GAP(name) \
   WELVET_API welvet_status name() { return to_c(gap(#name)); }
 
-WB_GAP(welvet_model_mount)
-WB_GAP(welvet_model_forward)
 WB_GAP(welvet_model_train_credit)
 WB_GAP(welvet_model_dense_proxy)
 WB_GAP(welvet_model_forward_pair)
@@ -559,7 +607,6 @@ WB_GAP(welvet_kmeans_forward_f32)
 WB_GAP(welvet_parallel_forward_f32)
 WB_GAP(welvet_seqmix_kind_name)
 
-WELVET_API void welvet_model_release() {}
 WELVET_API int32_t welvet_seqmix_mha_kind() { return -1; }
 WELVET_API int32_t welvet_seqmix_mamba_kind() { return -1; }
 WELVET_API int32_t welvet_seqmix_gdn_kind() { return -1; }

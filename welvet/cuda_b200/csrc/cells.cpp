@@ -47,17 +47,39 @@ void SwigluCell::release_work() {
   bs = 0;
 }
 
+Status mount_dense_src(int device, int rows, int cols, DType dt, int act, const WeightSrc& w,
+                       const double* bias, size_t bias_len, WeightStore* store, DeviceDense* dev,
+                       cudaStream_t st) {
+  if (w.native)
+    return mount_dense_native(device, rows, cols, dt, act, w.native, w.native_len, w.scale, bias, bias_len, store,
+                              dev, st);
+  return mount_dense(device, rows, cols, dt, act, w.f32, w.f32_on_device, bias, bias_len, store, dev, st);
+}
+
+static WeightSrc f32_src(const float* W, bool on_device) {
+  WeightSrc s;
+  s.f32 = W;
+  s.f32_on_device = on_device;
+  return s;
+}
+
 Status swiglu_mount(int device, int in, int inter, DType dt, const float* G, const float* U, const float* D,
                     bool w_is_device, SwigluCell* c, cudaStream_t st) {
+  const WeightSrc w[3] = {f32_src(G, w_is_device), f32_src(U, w_is_device), f32_src(D, w_is_device)};
+  return swiglu_mount_src(device, in, inter, dt, w, c, st);
+}
+
+Status swiglu_mount_src(int device, int in, int inter, DType dt, const WeightSrc (&w)[3], SwigluCell* c,
+                        cudaStream_t st) {
   if (in <= 0 || inter <= 0) return Status::Invalid("swiglu: need InputDim>0 and IntermediateDim>0");
   c->device = device;
   c->in = in;
   c->inter = inter;
-  Status s = mount_dense(device, inter, in, dt, -1, G, w_is_device, nullptr, 0, &c->sg, &c->gate, st);
+  Status s = mount_dense_src(device, inter, in, dt, -1, w[0], nullptr, 0, &c->sg, &c->gate, st);
   if (!s.ok()) return Status::Err(s.code, "swiglu Gate: " + s.message);
-  s = mount_dense(device, inter, in, dt, -1, U, w_is_device, nullptr, 0, &c->su, &c->up, st);
+  s = mount_dense_src(device, inter, in, dt, -1, w[1], nullptr, 0, &c->su, &c->up, st);
   if (!s.ok()) return Status::Err(s.code, "swiglu Up: " + s.message);
-  s = mount_dense(device, in, inter, dt, -1, D, w_is_device, nullptr, 0, &c->sd, &c->down, st);
+  s = mount_dense_src(device, in, inter, dt, -1, w[2], nullptr, 0, &c->sd, &c->down, st);
   if (!s.ok()) return Status::Err(s.code, "swiglu Down: " + s.message);
   if (c->gate.Wg && c->up.Wg && c->gate.row_stride == c->up.row_stride) {
     // Gate and Up run batched as one pair GEMM; their own GEMM mirrors are then unused
@@ -240,18 +262,25 @@ void MhaCell::release_work() {
 
 Status mha_mount(int device, const MhaConfig& cfg_in, DType dt, const float* Q, const float* K, const float* V,
                  const float* O, bool w_is_device, MhaCell* c, cudaStream_t st) {
+  const WeightSrc w[4] = {f32_src(Q, w_is_device), f32_src(K, w_is_device), f32_src(V, w_is_device),
+                          f32_src(O, w_is_device)};
+  return mha_mount_src(device, cfg_in, dt, w, c, st);
+}
+
+Status mha_mount_src(int device, const MhaConfig& cfg_in, DType dt, const WeightSrc (&w)[4], MhaCell* c,
+                     cudaStream_t st) {
   MhaConfig cfg = cfg_in;
   WB_TRY(mha_validate(&cfg));
   c->device = device;
   c->cfg = cfg;
   const int d = cfg.d_model, qd = cfg.num_heads * cfg.head_dim, kvd = cfg.num_kv_heads * cfg.head_dim;
-  Status s = mount_dense(device, qd, d, dt, -1, Q, w_is_device, nullptr, 0, &c->sq, &c->q, st);
+  Status s = mount_dense_src(device, qd, d, dt, -1, w[0], nullptr, 0, &c->sq, &c->q, st);
   if (!s.ok()) return Status::Err(s.code, "mha Q: " + s.message);
-  s = mount_dense(device, kvd, d, dt, -1, K, w_is_device, nullptr, 0, &c->sk, &c->k, st);
+  s = mount_dense_src(device, kvd, d, dt, -1, w[1], nullptr, 0, &c->sk, &c->k, st);
   if (!s.ok()) return Status::Err(s.code, "mha K: " + s.message);
-  s = mount_dense(device, kvd, d, dt, -1, V, w_is_device, nullptr, 0, &c->sv, &c->v, st);
+  s = mount_dense_src(device, kvd, d, dt, -1, w[2], nullptr, 0, &c->sv, &c->v, st);
   if (!s.ok()) return Status::Err(s.code, "mha V: " + s.message);
-  s = mount_dense(device, d, qd, dt, -1, O, w_is_device, nullptr, 0, &c->so, &c->o, st);
+  s = mount_dense_src(device, d, qd, dt, -1, w[3], nullptr, 0, &c->so, &c->o, st);
   if (!s.ok()) return Status::Err(s.code, "mha O: " + s.message);
   return Status::Ok();
 }
@@ -303,20 +332,35 @@ Status mha_forward_device(MhaCell* c, int batch, int seq, const float* x, float*
 }
 
 Status rmsnorm_gamma(int device, int dim, DType dt, const float* gamma, double** gamma64_dev, cudaStream_t st) {
-  WeightStore s;
-  DeviceDense d;
-  WB_TRY(mount_dense(device, 1, dim, dt, -1, gamma, false, nullptr, 0, &s, &d, st));
+  return rmsnorm_gamma_src(device, dim, dt, f32_src(gamma, false), gamma64_dev, st);
+}
+
+Status rmsnorm_gamma_src(int device, int dim, DType dt, const WeightSrc& w, double** gamma64_dev, cudaStream_t st) {
+  if (dim <= 0) return Status::Invalid("rmsnorm: invalid argument");
   // decode_row_f64 of the store: weight_at -> float -> double
   std::vector<double> g(static_cast<size_t>(dim));
   if (dt == DType::Float32) {
-    for (int i = 0; i < dim; ++i) g[static_cast<size_t>(i)] = static_cast<double>(s.f32[static_cast<size_t>(i)]);
+    if (!w.f32 || w.f32_on_device) return Status::Invalid("rmsnorm: float32 gamma must be host values");
+    for (int i = 0; i < dim; ++i) g[static_cast<size_t>(i)] = static_cast<double>(w.f32[static_cast<size_t>(i)]);
   } else {
+    // the store's native bytes: given, or the reference codec applied to the float values
+    WeightStore s;
+    DeviceDense d;
+    const uint8_t* native = w.native;
+    size_t native_len = w.native_len;
+    float scale = w.scale;
+    if (!native) {
+      WB_TRY(mount_dense(device, 1, dim, dt, -1, w.f32, w.f32_on_device, nullptr, 0, &s, &d, st));
+      native = s.native.data();
+      native_len = s.native.size();
+      scale = s.scale;
+    }
     float* dec = nullptr;
     uint8_t* nat = nullptr;
     WB_CUDA(cudaMalloc(&dec, static_cast<size_t>(dim) * 4));
-    WB_CUDA(cudaMalloc(&nat, s.native.size()));
-    Status stt = cuda_status(cudaMemcpyAsync(nat, s.native.data(), s.native.size(), cudaMemcpyHostToDevice, st), "gamma h2d");
-    if (stt.ok()) stt = decode_ref(dt, nat, dim, s.scale, dec, st);
+    WB_CUDA(cudaMalloc(&nat, native_len));
+    Status stt = cuda_status(cudaMemcpyAsync(nat, native, native_len, cudaMemcpyHostToDevice, st), "gamma h2d");
+    if (stt.ok()) stt = decode_ref(dt, nat, dim, scale, dec, st);
     std::vector<float> f(static_cast<size_t>(dim));
     if (stt.ok()) stt = cuda_status(cudaMemcpyAsync(f.data(), dec, static_cast<size_t>(dim) * 4, cudaMemcpyDeviceToHost, st), "gamma d2h");
     if (stt.ok()) stt = cuda_status(cudaStreamSynchronize(st), "gamma sync");

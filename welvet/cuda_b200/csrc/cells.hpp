@@ -11,6 +11,20 @@
 
 namespace wb {
 
+// A weight matrix as a cell mount reads it: float32 values (host or device) quantized at
+// mount, or reference-layout native bytes with their scale (a stored model's store section,
+// src/interop/model_session.cpp:135-153).
+struct WeightSrc {
+  const float* f32 = nullptr;
+  bool f32_on_device = false;
+  const uint8_t* native = nullptr;
+  size_t native_len = 0;
+  float scale = 1.0f;
+};
+Status mount_dense_src(int device, int rows, int cols, DType dt, int act, const WeightSrc& w,
+                       const double* bias, size_t bias_len, WeightStore* store, DeviceDense* dev,
+                       cudaStream_t st);
+
 struct SwigluCell {
   int device = 0;
   int in = 0, inter = 0;
@@ -35,6 +49,9 @@ struct SwigluCell {
 
 Status swiglu_mount(int device, int in, int inter, DType dt, const float* G, const float* U, const float* D,
                     bool w_is_device, SwigluCell* c, cudaStream_t st);
+// The same from weight sources Gate, Up, Down.
+Status swiglu_mount_src(int device, int in, int inter, DType dt, const WeightSrc (&w)[3], SwigluCell* c,
+                        cudaStream_t st);
 Status swiglu_reserve(SwigluCell* c, int bs, cudaStream_t st);
 // x [bs][in] (device) -> h [bs][inter] (the reference's pre) and y [bs][in] (post).
 // h may be nullptr (h stays in the cell's padded work buffer).
@@ -65,6 +82,9 @@ struct MhaCell {
 
 Status mha_mount(int device, const MhaConfig& cfg, DType dt, const float* Q, const float* K, const float* V,
                  const float* O, bool w_is_device, MhaCell* c, cudaStream_t st);
+// The same from weight sources Q, K, V, O.
+Status mha_mount_src(int device, const MhaConfig& cfg, DType dt, const WeightSrc (&w)[4], MhaCell* c,
+                     cudaStream_t st);
 Status mha_reserve(MhaCell* c, int bs, cudaStream_t st);
 // x [batch*seq][d_model] (device) -> attn [bs][q_dim] (pre) and y [bs][d_model] (post).
 Status mha_forward_device(MhaCell* c, int batch, int seq, const float* x, float* attn, float* y,
@@ -72,5 +92,7 @@ Status mha_forward_device(MhaCell* c, int batch, int seq, const float* x, float*
 
 // gamma f32 [dim] quantized with `dt` then decoded to f64 as the reference's gamma store.
 Status rmsnorm_gamma(int device, int dim, DType dt, const float* gamma, double** gamma64_dev, cudaStream_t st);
+// The same from a weight source (host float32 or native bytes).
+Status rmsnorm_gamma_src(int device, int dim, DType dt, const WeightSrc& w, double** gamma64_dev, cudaStream_t st);
 
 } // namespace wb

@@ -131,11 +131,21 @@ Status volume_bind_dense_native(Volume* v, int idx, int in, int out, int act, DT
 
 Status volume_bind_swiglu(Volume* v, int idx, int in, int inter, DType dt, const float* G, const float* U,
                           const float* D, bool w_dev) {
+  WeightSrc w[3];
+  const float* m[3] = {G, U, D};
+  for (int i = 0; i < 3; ++i) {
+    w[i].f32 = m[i];
+    w[i].f32_on_device = w_dev;
+  }
+  return volume_bind_swiglu_src(v, idx, in, inter, dt, w);
+}
+
+Status volume_bind_swiglu_src(Volume* v, int idx, int in, int inter, DType dt, const WeightSrc (&w)[3]) {
   WB_TRY(check_idx(v, idx));
   VolumeCell& c = v->cells[static_cast<size_t>(idx)];
   reset_cell(c);
   c.swiglu = std::make_unique<SwigluCell>();
-  WB_TRY(swiglu_mount(v->device, in, inter, dt, G, U, D, w_dev, c.swiglu.get(), v->stream));
+  WB_TRY(swiglu_mount_src(v->device, in, inter, dt, w, c.swiglu.get(), v->stream));
   c.op = OpKind::SwiGLU;
   c.in_width = in;
   c.out_width = in;
@@ -145,12 +155,22 @@ Status volume_bind_swiglu(Volume* v, int idx, int in, int inter, DType dt, const
 
 Status volume_bind_mha(Volume* v, int idx, const MhaConfig& cfg, int seq, DType dt, const float* Q, const float* K,
                        const float* V, const float* O, bool w_dev) {
+  WeightSrc w[4];
+  const float* m[4] = {Q, K, V, O};
+  for (int i = 0; i < 4; ++i) {
+    w[i].f32 = m[i];
+    w[i].f32_on_device = w_dev;
+  }
+  return volume_bind_mha_src(v, idx, cfg, seq, dt, w);
+}
+
+Status volume_bind_mha_src(Volume* v, int idx, const MhaConfig& cfg, int seq, DType dt, const WeightSrc (&w)[4]) {
   WB_TRY(check_idx(v, idx));
   if (seq <= 0) return Status::Invalid("mha: bad seq");
   VolumeCell& c = v->cells[static_cast<size_t>(idx)];
   reset_cell(c);
   c.mha = std::make_unique<MhaCell>();
-  WB_TRY(mha_mount(v->device, cfg, dt, Q, K, V, O, w_dev, c.mha.get(), v->stream));
+  WB_TRY(mha_mount_src(v->device, cfg, dt, w, c.mha.get(), v->stream));
   c.op = OpKind::MHA;
   c.mha_seq = seq;
   c.in_width = c.mha->cfg.d_model;
@@ -159,12 +179,27 @@ Status volume_bind_mha(Volume* v, int idx, const MhaConfig& cfg, int seq, DType 
   return Status::Ok();
 }
 
-Status volume_bind_rmsnorm(Volume* v, int idx, int dim, double eps, DType dt, const float* gamma) {
+Status volume_set_mha_seq(Volume* v, int idx, int seq) {
   WB_TRY(check_idx(v, idx));
+  VolumeCell& c = v->cells[static_cast<size_t>(idx)];
+  if (c.op != OpKind::MHA || seq <= 0) return Status::Invalid("mha: bad seq");
+  c.mha_seq = seq;
+  return Status::Ok();
+}
+
+Status volume_bind_rmsnorm(Volume* v, int idx, int dim, double eps, DType dt, const float* gamma) {
   if (dim <= 0 || !gamma) return Status::Invalid("rmsnorm: invalid argument");
+  WeightSrc w;
+  w.f32 = gamma;
+  return volume_bind_rmsnorm_src(v, idx, dim, eps, dt, w);
+}
+
+Status volume_bind_rmsnorm_src(Volume* v, int idx, int dim, double eps, DType dt, const WeightSrc& gamma) {
+  WB_TRY(check_idx(v, idx));
+  if (dim <= 0) return Status::Invalid("rmsnorm: invalid argument");
   VolumeCell& c = v->cells[static_cast<size_t>(idx)];
   reset_cell(c);
-  WB_TRY(rmsnorm_gamma(v->device, dim, dt, gamma, &c.gamma64, v->stream));
+  WB_TRY(rmsnorm_gamma_src(v->device, dim, dt, gamma, &c.gamma64, v->stream));
   c.op = OpKind::RMSNorm;
   c.eps = eps <= 0.0 ? 1e-6 : eps;
   c.in_width = c.out_width = c.pre_width = dim;

@@ -68,6 +68,12 @@ Status volume_bind_swiglu(Volume* v, int idx, int in, int inter, DType dt, const
 Status volume_bind_mha(Volume* v, int idx, const MhaConfig& cfg, int seq, DType dt, const float* Q, const float* K,
                        const float* V, const float* O, bool w_dev);
 Status volume_bind_rmsnorm(Volume* v, int idx, int dim, double eps, DType dt, const float* gamma);
+// The same cells from weight sources (float32 values or a stored model's native bytes).
+Status volume_bind_swiglu_src(Volume* v, int idx, int in, int inter, DType dt, const WeightSrc (&w)[3]);
+Status volume_bind_mha_src(Volume* v, int idx, const MhaConfig& cfg, int seq, DType dt, const WeightSrc (&w)[4]);
+Status volume_bind_rmsnorm_src(Volume* v, int idx, int dim, double eps, DType dt, const WeightSrc& gamma);
+// Tokens per sequence of an MHA cell (rows = batch * seq), as the input shape of a forward sets it.
+Status volume_set_mha_seq(Volume* v, int idx, int seq);
 Status volume_set_remote_link(Volume* v, int idx, int target);
 Status volume_set_disabled(Volume* v, int idx, bool disabled);
 
