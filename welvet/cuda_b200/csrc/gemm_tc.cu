@@ -456,10 +456,12 @@ __device__ __forceinline__ TmItem decode_item(const TmParams& p, int q) {
   return it;
 }
 
-// Epilogue staging of one converter group (4 warps, 128 rows): 2 buffers x {pre, post} x 16
-// tokens x 128 rows of fp32, in the ring memory the last pass no longer uses.
+// Epilogue staging of one converter group (4 warps, 128 rows): {pre, post} x 16 tokens x 128
+// rows of fp32 (h: 16 x 64) for the chunk a bulk tensor store writes out; a dedicated area
+// after the rings holds both groups' buffers.
 constexpr uint32_t kStageBuf = 16 * 128 * 4;
-constexpr uint32_t kStageGroup = 2 * 2 * kStageBuf;
+constexpr uint32_t kStageGroup = 2 * kStageBuf;
+constexpr uint32_t kStageArea = 2 * kStageGroup;
 
 __device__ __forceinline__ void named_bar(uint32_t id, uint32_t n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
@@ -578,7 +580,8 @@ __global__ void __launch_bounds__(kTmThreads, 1)
   const int S = p.sx, Sw = p.sw;
   uint8_t* xring = smem;                                   // S x p.x_bytes
   uint8_t* wring = smem + S * p.x_bytes;                   // Sw x p.w_bytes
-  uint64_t* bars = reinterpret_cast<uint64_t*>(wring + Sw * p.w_bytes);
+  uint8_t* stage_area = wring + Sw * p.w_bytes;             // kStageArea
+  uint64_t* bars = reinterpret_cast<uint64_t*>(stage_area + kStageArea);
   uint64_t* w_full = bars;                 // W producer -> converters (tx)
   uint64_t* w_empty = w_full + Sw;         // converter warps (4) -> W producer
   uint64_t* s_full = w_empty + Sw;         // x producer (1 + tx) and converter warps (4) -> MMA
@@ -769,7 +772,6 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       const int tile_m = it.tile_m, t_begin = it.t_begin, t_count = it.t_count, T = it.T, P = it.P;
       const int nacc = it.nacc, ntot = it.ntot, npass = it.npass, split = it.split, tail_idx = it.tail_idx;
       const bool tail = it.tail, part = it.part;
-      const bool last_item = qi + item_step >= p.n_items;
       const int o = tile_m * 128 + r;
       // Epilogue sums that are single fp32 values (one plane, one accumulator, no Int8 scale,
       // no partials) are scaled in fp32; others are summed and scaled in fp64.
@@ -796,11 +798,11 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         ++fills;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int t_pass = t_begin + pass * T;
-        // The CTA's last pass may stage its outputs in the (then idle) ring memory and leave
-        // them to bulk tensor stores; the CTA only waits for the stores to have read shared
-        // memory. Earlier outputs are stored directly and drain while the next item runs.
-        const bool staged = p.tma_out && !part && last_item && pass == npass - 1;
-        float* stage = reinterpret_cast<float*>(smem + grp * kStageGroup);
+        // Outputs go through the group's staging buffer to bulk tensor stores: the epilogue
+        // only reads TMEM and fills shared memory, the accumulator is released at once and the
+        // writes drain while the next item's MMAs run.
+        const bool staged = p.tma_out && !part;
+        float* stage = reinterpret_cast<float*>(stage_area + grp * kStageGroup);
         const bool issuer = q == 0 && lane == 0;  // one thread of the group issues its stores
         int chunk = 0;
         for (int tc = grp * 16; tc < T; tc += 32, ++chunk) {
@@ -808,8 +810,8 @@ __global__ void __launch_bounds__(kTmThreads, 1)
           // tokens holds none of them (and may hold the next block's, which a staged store must
           // not overwrite). Uniform over the group, so its barriers stay matched.
           if (t_pass + tc >= t_begin + t_count) break;
-          float* s1 = stage + (chunk & 1) * 2 * (kStageBuf / 4);
-          float* s2 = s1 + kStageBuf / 4;
+          float* s1 = stage;
+          float* s2 = stage + kStageBuf / 4;
           // phase 1 (unrolled, cheap): each sum scaled, then kept as the float the reference
           // rounds it to (pre = float(y); Gate and Up are floats before the product)
           float pf[16], uf[16];
@@ -869,8 +871,8 @@ __global__ void __launch_bounds__(kTmThreads, 1)
           }
           if (part) continue;
           if (staged) {
-            // buffer chunk & 1 was last stored two chunks ago: its reads must be done
-            if (issuer && chunk >= 2) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+            // the buffer's previous store (this item's last chunk or an earlier item's) has read it
+            if (issuer) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
             named_bar(1 + grp, 128);
           }
           // phase 2: the outputs. pf / uf are only indexed by constants here (kept in registers);
@@ -942,12 +944,13 @@ __global__ void __launch_bounds__(kTmThreads, 1)
             }
           }
         }
-        if (staged && issuer) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(acc_empty);
       }
     }
+    // the staging buffers stay valid until the last stores have read them
+    if (q == 0 && lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
   }
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -1235,18 +1238,20 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_
   pl.w_bytes = static_cast<uint32_t>(kBM * pl.kbb);
   pl.a_col = static_cast<uint32_t>(round_up(pl.acc_cols, 32));
   // stages (an x slot + a TMEM A slot each): as many as TMEM and shared memory allow, up to 8,
-  // keeping room for 8 W slots; then the W ring takes the rest (up to 32). 1 KB aligns the
-  // base, 1 KB holds the barriers (at most 2*32 + 2*8 + 2 of them).
+  // keeping room for 4 W slots; then the W ring takes the rest (up to 32). 1 KB aligns the
+  // base, 1 KB holds the barriers (at most 2*32 + 2*8 + 2 of them); the epilogue staging and
+  // the per-token-block plane counts take their own space.
   const int tiles_t_plan = (M + pl.TB - 1) / pl.TB;
   pl.pblk_bytes = static_cast<int>(round_up(static_cast<int64_t>(std::min(tiles_t_plan, kTmMaxBlocks)) * 4, 16));
-  const int64_t budget = 227 * 1024 - 2048 - pl.pblk_bytes;
+  const int64_t budget = 227 * 1024 - 2048 - pl.pblk_bytes - kStageArea;
   pl.sx = (static_cast<int>(kTmemCols) - static_cast<int>(pl.a_col)) / 32;
   if (pl.sx > 8) pl.sx = 8;
-  while (pl.sx > 2 && pl.sx * static_cast<int64_t>(pl.x_bytes) + 8 * static_cast<int64_t>(pl.w_bytes) > budget)
+  while (pl.sx > 2 && pl.sx * static_cast<int64_t>(pl.x_bytes) + 4 * static_cast<int64_t>(pl.w_bytes) > budget)
     --pl.sx;
   pl.sw = static_cast<int>((budget - pl.sx * static_cast<int64_t>(pl.x_bytes)) / pl.w_bytes);
   if (pl.sw > 32) pl.sw = 32;
-  pl.smem = static_cast<size_t>(pl.sx) * pl.x_bytes + static_cast<size_t>(pl.sw) * pl.w_bytes + 2048 + pl.pblk_bytes;
+  pl.smem = static_cast<size_t>(pl.sx) * pl.x_bytes + static_cast<size_t>(pl.sw) * pl.w_bytes + 2048 + pl.pblk_bytes +
+            kStageArea;
   // At least half the SM's shared memory, so that one CTA (and its 512 TMEM columns) runs per
   // SM: a second CTA on the SM would only stall in tcgen05.alloc.
   if (pl.smem < 116 * 1024) pl.smem = 116 * 1024;
@@ -1450,15 +1455,14 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
   p.tiles = pl.tiles;
   p.n_items = pl.tail_first >= 0 ? pl.tail_first + (pl.tiles - pl.tail_first) * pl.tail_s : pl.tiles * pl.splits;
 
-  // Outputs through bulk tensor stores (the last pass stages them in the idle ring memory):
+  // Outputs through bulk tensor stores (the epilogue stages them in its own shared memory):
   // fp32 rows whose pitch is a multiple of 16 bytes at 16-byte aligned bases.
   CUtensorMap tm_o[2] = {tm_x[0], tm_x[0]};  // placeholders when the epilogue stores directly
   {
     auto aligned = [](const void* ptr, int64_t ld) {
       return ptr != nullptr && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && (ld * 4) % 16 == 0;
     };
-    const uint64_t ring = static_cast<uint64_t>(pl.sx) * pl.x_bytes + static_cast<uint64_t>(pl.sw) * pl.w_bytes;
-    bool ok = pl.splits == 1 && ring >= 2 * kStageGroup;
+    bool ok = true;
     if (ok && a.pair) {
       ok = aligned(a.h, a.ld_h) &&
            make_map_2d(&tm_o[0], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.h, static_cast<uint64_t>(a.rows / 2),
