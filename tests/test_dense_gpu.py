@@ -377,20 +377,24 @@ def test_dense_vs_reference_cuda_kernel(wb, oracle):
 GEMM_TOL = {"3": 2.0 ** -16, "2": 2.0 ** -15, "1": 2.0 ** -9}
 
 
-@pytest.mark.parametrize("kernel", ["tmem", "smem"])
+@pytest.mark.parametrize("kernel", ["tmem", "smem", "pair"])
 @pytest.mark.parametrize("xsplit", ["3", "2", "1"])
 @pytest.mark.parametrize("dt", [16, 4, 5, 9])
 @pytest.mark.parametrize("shape", [(128, 64, 8), (300, 1000, 16), (256, 4096, 64), (130, 257, 100), (1024, 512, 5),
-                                   (200, 640, 300), (384, 192, 520), (9600, 256, 300)])
+                                   (200, 640, 300), (384, 192, 520), (9600, 256, 300), (9728, 256, 300),
+                                   (256, 8192, 128)])
 def test_tensor_core_path_parity(wb, oracle, dt, shape, xsplit, kernel, monkeypatch):
     """Batches above 8 run the tcgen05 GEMM (f16 planes of x, exact products, fp32 tensor
     accumulation), with the dequantised weights in TMEM (default, persistent CTAs looping
     over tiles) or in shared memory. Error normalised by sum_k |W x| stays under the stated
     bound per x split. 9600 x 256 at 300 tokens: 150 tiles over two token blocks, the last
-    two cut along K (tail launch)."""
+    two cut along K (tail launch). "pair": the TMEM kernel on CTA pairs (M = 256 MMAs), taken
+    with 128 or more tokens and an even number of 128-row tiles: 200 x 640 whole tiles,
+    9728 x 256 76 pair tiles with a tail, 256 x 8192 one pair tile split along K."""
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
     monkeypatch.setenv("WELVET_B200_XSPLIT", xsplit)
-    monkeypatch.setenv("WELVET_B200_GEMM", kernel)
+    monkeypatch.setenv("WELVET_B200_GEMM", "smem" if kernel == "smem" else "tmem")
+    monkeypatch.setenv("WELVET_B200_GEMM_PAIR", "1" if kernel == "pair" else "0")
     monkeypatch.setenv("WELVET_B200_BATCHED", "tc")  # batches of 5..8 would otherwise take the GEMV
     out, in_, batch = shape
     w, x, bias, ref = _case(oracle, dt, out, in_, batch, 2.0, out + in_ + batch, 0)
@@ -402,6 +406,33 @@ def test_tensor_core_path_parity(wb, oracle, dt, shape, xsplit, kernel, monkeypa
     assert norm <= GEMM_TOL[xsplit], norm
     relu = np.maximum(pre.astype(np.float64), 0)
     assert np.allclose(post, relu.astype(np.float32))
+
+
+@pytest.mark.parametrize("dt", [16, 9])
+@pytest.mark.parametrize("shape,xsplit", [((512, 1024, 256), "1"), ((768, 512, 200), "2"), ((256, 640, 160), "3"),
+                                          ((9728, 256, 300), "1"), ((256, 8192, 128), "3")])
+def test_gemm_cta_pairs_match_single_ctas(wb, oracle, dt, shape, xsplit, monkeypatch):
+    """The same GEMM on CTA pairs (WELVET_B200_GEMM_PAIR=1: M = 256 MMAs, each CTA loading
+    half of every x stage) and on single CTAs: both within the GEMM bound of the oracle, for
+    one to three x planes (pair passes of 256, 128 and 128 tokens; with three planes plane 2
+    rides in a second ring slot and accumulates onto plane 1), whole tiles, a tail and
+    split-K."""
+    monkeypatch.setenv("WELVET_B200_EXACT", "0")
+    monkeypatch.setenv("WELVET_B200_XSPLIT", xsplit)
+    monkeypatch.setenv("WELVET_B200_BATCHED", "tc")
+    out, in_, batch = shape
+    w, x, bias, ref = _case(oracle, dt, out, in_, batch, 2.0, out + 3 * in_ + batch, 0)
+    pre_o, post_o, y64, sabs = ref
+    res = {}
+    for pair in ("1", "0"):
+        monkeypatch.setenv("WELVET_B200_GEMM_PAIR", pair)
+        pre, post = wb.dense_forward_f32(w, x, dt, 0, bias)
+        err = np.abs(pre.astype(np.float64) - pre_o.astype(np.float64)) - 2 * ulp(pre_o)
+        norm = float(np.max(err / np.maximum(sabs, 1e-300)))
+        assert norm <= GEMM_TOL[xsplit], (pair, norm)
+        assert np.allclose(post, np.maximum(pre.astype(np.float64), 0).astype(np.float32))
+        res[pair] = pre
+    print(f"pairs vs single CTAs dt={dt} shape={shape}: identical={np.array_equal(res['1'], res['0'])}")
 
 
 @pytest.mark.parametrize("batch", [5, 6, 7, 8])
@@ -457,14 +488,18 @@ def test_simt_gemv_still_correct(wb, oracle, dt, monkeypatch):
 
 
 @pytest.mark.parametrize("rows,d,inter", [(1, 256, 640), (3, 256, 640), (24, 256, 640), (300, 256, 640),
-                                          (24, 2048, 96), (16, 256, 9600)])
+                                          (24, 2048, 96), (16, 256, 9600), (300, 256, 4864)])
 @pytest.mark.parametrize("dt", [16, 4, 9])
-def test_swiglu_tensor_paths(wb, oracle, dt, rows, d, inter, monkeypatch):
+@pytest.mark.parametrize("pair", ["0", "1"])
+def test_swiglu_tensor_paths(wb, oracle, dt, rows, d, inter, pair, monkeypatch):
     """1..4 rows: Gate and Up fused in the tensor GEMV; more: one tcgen05 GEMM over the
     interleaved Gate/Up pair mirror writing h in its epilogue (300 rows: several token
     blocks; d = 2048 with a narrow intermediate: split-K with the paired reduce; 9600: 150
-    pair tiles, the last two cut along K and reduced by the tail launch)."""
+    pair tiles, the last two cut along K and reduced by the tail launch; 300 x 4864: 76
+    pair tiles per token block, with a tail). pair = 1: the GEMMs on CTA pairs where they
+    qualify (300 rows)."""
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
+    monkeypatch.setenv("WELVET_B200_GEMM_PAIR", pair)
     rng = np.random.default_rng(20 + rows)
     G, U, D = [(rng.standard_normal(s) * 0.5).astype(np.float32) for s in ((inter, d), (inter, d), (d, inter))]
     x = rng.standard_normal((rows, d)).astype(np.float32)

@@ -32,6 +32,7 @@
 #include <cstring>
 #include <mutex>
 #include <tuple>
+#include <type_traits>
 #include <vector>
 
 namespace wb {
@@ -426,6 +427,7 @@ struct TmItem {
   int tb, tile_m, t_begin, t_count, kb0, nkb, split, tail_idx;
   bool tail, part;
   int P, T, npass, ntot, nacc;  // filled in by the kernel from the block's plane count
+  int PA, acols;                // accumulator planes and columns (pairs: planes 1 and 2 share one)
 };
 
 __device__ __forceinline__ TmItem decode_item(const TmParams& p, int q) {
@@ -493,6 +495,41 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
       ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// ---- CTA-pair forms (cta_group::2): one thread of the even CTA issues an M = 256 MMA whose
+// A rows 0..127 are that CTA's TMEM and rows 128..255 the odd CTA's (same TMEM address), and
+// whose B columns 0..N/2-1 are the even CTA's shared memory and N/2..N-1 the odd CTA's (same
+// shared-memory offset); each CTA's TMEM receives its 128 rows x N of D.
+
+__device__ __forceinline__ void mma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                                uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// The barrier at `bar`'s offset in both CTAs of the pair tracks the MMAs issued so far: one
+// commit per CTA, each naming that CTA's barrier by its cluster address.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               ::"r"(cluster_addr(bar, 0)) : "memory");
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               ::"r"(cluster_addr(bar, 1)) : "memory");
+}
+
+// x box into this CTA's shared memory, its bytes counted on the even CTA's barrier `bar`
+// (a cluster address). A plain (single-destination) tensor load.
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* tm, int x, int y, int z, uint32_t bar,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
       : "memory");
 }
 
@@ -570,7 +607,12 @@ __device__ __forceinline__ void convert_row(const uint8_t* tile, int r, uint32_t
   }
 }
 
-template <int kDt>
+// kPair: clusters of 2 CTAs (a CTA pair) share each M = 256 MMA. A work item's tile is then
+// 256 weight rows; CTA v (its rank in the pair) converts rows 128 v .. 128 v + 127 into its own
+// TMEM, loads half of each x stage and writes the epilogue of its rows. Only the even CTA
+// issues MMAs: the odd CTA's converters, x loads and epilogue report to the even CTA's
+// barriers, and the even CTA's MMA thread releases stages and accumulators in both.
+template <int kDt, bool kPair>
 __global__ void __launch_bounds__(kTmThreads, 1)
     k_gemm_tm(const __grid_constant__ CUtensorMap tm_x1, const __grid_constant__ CUtensorMap tm_x2,
               const __grid_constant__ CUtensorMap tm_x3, const __grid_constant__ CUtensorMap tm_o1,
@@ -593,31 +635,41 @@ __global__ void __launch_bounds__(kTmThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t v = kPair ? cluster_ctarank() : 0u;  // rank in the pair (0 issues the MMAs)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Sw; ++s) {
       mbar_init(&w_full[s], 1);
       mbar_init(&w_empty[s], 4);
     }
+    // pair: s_full and acc_empty of the even CTA count both CTAs' warps
     for (int s = 0; s < S; ++s) {
-      mbar_init(&s_full[s], 5);
+      mbar_init(&s_full[s], kPair ? 9 : 5);
       mbar_init(&s_free[s], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 8);
+    mbar_init(acc_empty, kPair ? 16 : 8);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   const bool pblk_ok = p.tiles_t <= kTmMaxBlocks;
   if (pblk_ok)
     for (int b = threadIdx.x; b < p.tiles_t; b += kTmThreads) s_pblk[b] = 1;
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if constexpr (kPair) {  // both CTAs' warp 0 together: the same columns in each CTA's TMEM
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(kTmemCols)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(kTmemCols)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
+  if constexpr (kPair) cluster_sync_all();  // the barriers are initialised before the other CTA arrives
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   if (pblk_ok)
     for (int t = threadIdx.x; t < p.M; t += kTmThreads) {
@@ -626,7 +678,9 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     }
   __syncthreads();
   const uint32_t tmem = *tmem_slot;
-  const int first_item = blockIdx.x, item_step = gridDim.x;
+  // items go to CTA pairs (clusters) in pair mode
+  const int first_item = static_cast<int>(kPair ? blockIdx.x >> 1 : blockIdx.x);
+  const int item_step = static_cast<int>(kPair ? gridDim.x >> 1 : gridDim.x);
   // the work item q as this CTA's roles see it: tile, K range, token range, planes
   auto item = [&](int q) {
     TmItem it = decode_item(p, q);
@@ -634,6 +688,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     it.T = p.tpass[it.P - 1];
     it.npass = (it.t_count + it.T - 1) / it.T;
     it.ntot = it.P * it.T;
+    // pairs: plane 2 (2^-22 of x and below) accumulates onto plane 1's columns, whose fp32
+    // rounding is then ~2^-35 of |Wx|; plane 0 keeps its own accumulator
+    it.PA = kPair && it.P == 3 ? 2 : it.P;
+    it.acols = it.PA * it.T;
     it.nacc = p.nacc[it.P - 1];
     return it;
   };
@@ -655,7 +713,8 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       bool ok = true;
       for (int qi = first_item; qi < p.n_items && ok; qi += item_step) {
         const TmItem it = item(qi);
-        const uint8_t* wfirst = p.Wg + (static_cast<int64_t>(it.tile_m) * p.nkb_total + it.kb0) * wb;
+        const int mt = kPair ? 2 * it.tile_m + static_cast<int>(v) : it.tile_m;  // 128-row mirror tile
+        const uint8_t* wfirst = p.Wg + (static_cast<int64_t>(mt) * p.nkb_total + it.kb0) * wb;
         for (int pass = 0; pass < it.npass && ok; ++pass)
           for (int i = 0; i < it.nkb; ++i) {
             if (!mbar_wait(&w_empty[w.slot], w.phase ^ 1u, p.err, 11)) { ok = false; break; }
@@ -686,14 +745,38 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         const uint32_t tx = static_cast<uint32_t>(it.ntot * 128);
         for (int pass = 0; pass < it.npass && ok; ++pass) {
           const int t0 = it.t_begin + pass * it.T;
-          for (int i = 0; i < it.nkb; ++i) {
-            if (!mbar_wait(&s_free[r.slot], r.phase ^ 1u, p.err, 18)) { ok = false; break; }
-            mbar_expect_tx(&s_full[r.slot], tx);
-            uint8_t* dst = xring + r.slot * p.x_bytes;
-            for (int pl = 0; pl < it.P; ++pl)
-              tma_load_3d_hint(dst + pl * it.T * 128, tmx, (it.kb0 + i) * kBK, t0, pl, &s_full[r.slot], pol);
-            ++issued;
-            r.step(S);
+          for (int i = 0; i < it.nkb && ok; ++i) {
+            if constexpr (kPair) {
+              // this CTA's half of each MMA's x rows, in boxes of T/2 tokens (box b: plane b / 2,
+              // tokens from (b % 2) T/2): with 1 or 2 planes boxes vP .. vP + P - 1 in one slot
+              // (one MMA over the [P][T] rows); with 3, boxes 2v and 2v + 1 (the first MMA, planes
+              // 0 and 1) in one slot and box 4 + v (half of plane 2, the second MMA) in the next.
+              // The even CTA's barrier of each slot counts the bytes of both halves.
+              const int half = it.T >> 1;
+              const int p01 = it.P < 2 ? it.P : 2;
+              for (int u = 0; u < (it.P == 3 ? 2 : 1); ++u) {
+                if (!mbar_wait(&s_free[r.slot], r.phase ^ 1u, p.err, 18)) { ok = false; break; }
+                uint8_t* dst = xring + r.slot * p.x_bytes;
+                const int nb = u == 0 ? p01 : 1;
+                if (v == 0) mbar_expect_tx(&s_full[r.slot], static_cast<uint32_t>(nb * it.T * 128));
+                const uint32_t bar = cluster_addr(&s_full[r.slot], 0);
+                for (int j = 0; j < nb; ++j) {
+                  const int b = u == 0 ? static_cast<int>(v) * p01 + j : 4 + static_cast<int>(v);
+                  tma_load_3d_pair(dst + j * half * 128, tmx, (it.kb0 + i) * kBK, t0 + (b & 1) * half, b >> 1, bar,
+                                   pol);
+                }
+                ++issued;
+                r.step(S);
+              }
+            } else {
+              if (!mbar_wait(&s_free[r.slot], r.phase ^ 1u, p.err, 18)) { ok = false; break; }
+              uint8_t* dst = xring + r.slot * p.x_bytes;
+              mbar_expect_tx(&s_full[r.slot], tx);
+              for (int pl = 0; pl < it.P; ++pl)
+                tma_load_3d_hint(dst + pl * it.T * 128, tmx, (it.kb0 + i) * kBK, t0, pl, &s_full[r.slot], pol);
+              ++issued;
+              r.step(S);
+            }
           }
         }
       }
@@ -706,7 +789,8 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && v == 0) {
+      constexpr uint32_t kM = kPair ? 256 : 128;
       const uint64_t bd_base = desc_sw128(smem_u32(xring));
       const uint64_t bd_step = static_cast<uint64_t>(p.x_bytes >> 4);   // one x slot, in 16-byte units
       Ring r;
@@ -717,39 +801,67 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       for (int qi = first_item; qi < p.n_items && ok; qi += item_step) {
         const TmItem it = item(qi);
         const int n0 = it.ntot < 256 ? it.ntot : 256;  // first MMA's N; the second covers [n0, ntot)
-        const uint32_t idesc0 =
-            (1u << 4) | (static_cast<uint32_t>(n0 >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
-        const uint32_t idesc1 =
-            (1u << 4) | (static_cast<uint32_t>((it.ntot - n0) >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
+        const uint32_t idesc0 = (1u << 4) | (static_cast<uint32_t>(n0 >> 3) << 17) | ((kM >> 4) << 24);
+        const uint32_t idesc1 = (1u << 4) | (static_cast<uint32_t>((it.ntot - n0) >> 3) << 17) | ((kM >> 4) << 24);
         const uint64_t bd_n0 = static_cast<uint64_t>((n0 * 128) >> 4);  // rows [n0, ntot) of a slot
+        // One pass's k stages. kTwo: a second MMA per k step (single CTA: N above 256; pairs: 3
+        // planes, plane 2 from the next slot onto plane 1's accumulator). Compiled once per
+        // case: a run-time branch inside this issue loop cost ~40 % of the GEMM's time.
+        auto stages = [&](auto two_c) -> bool {
+          constexpr bool kTwo = decltype(two_c)::value;
+          int j = 0;      // accumulator of the next k step (round robin over nacc)
+          int first = 0;  // k steps issued this pass (each accumulator starts fresh on its first)
+          for (int i = 0; i < it.nkb; ++i) {
+            if (!mbar_wait(&s_full[r.slot], r.phase, p.err, 14)) return false;
+            Ring r2 = r;
+            if constexpr (kPair && kTwo) {
+              r2.step(S);
+              if (!mbar_wait(&s_full[r2.slot], r2.phase, p.err, 14)) return false;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint64_t bd = bd_base + bd_step * static_cast<uint64_t>(r.slot);
+            [[maybe_unused]] const uint64_t bd2 = bd_base + bd_step * static_cast<uint64_t>(r2.slot);
+            const uint32_t a = tmem + p.a_col + 32u * static_cast<uint32_t>(r.slot);
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {  // 16 k per MMA: 8 TMEM columns of A, 32 bytes of B
+              const uint32_t d = tmem + static_cast<uint32_t>(j * it.acols);
+              const uint32_t acc = first >= it.nacc ? 1u : 0u;
+              if constexpr (kPair) {
+                mma_f16_ts_pair(d, a + 8u * k, bd + 2 * k, idesc0, acc);
+                if constexpr (kTwo)
+                  mma_f16_ts_pair(d + static_cast<uint32_t>(it.T), a + 8u * k, bd2 + 2 * k, idesc1, 1u);
+              } else {
+                mma_f16_ts(d, a + 8u * k, bd + 2 * k, idesc0, acc);
+                if constexpr (kTwo)
+                  mma_f16_ts(d + static_cast<uint32_t>(n0), a + 8u * k, bd + bd_n0 + 2 * k, idesc1, acc);
+              }
+              if (++j == it.nacc) j = 0;
+              ++first;
+            }
+            if constexpr (kPair) {
+              mma_commit_pair(&s_free[r.slot]);
+              if constexpr (kTwo) mma_commit_pair(&s_free[r2.slot]);
+            } else {
+              mma_commit(&s_free[r.slot]);
+            }
+            last = r2;
+            any = true;
+            r = r2;
+            r.step(S);
+          }
+          return true;
+        };
+        const bool two = kPair ? it.P == 3 : it.ntot > n0;
         for (int pass = 0; pass < it.npass && ok; ++pass) {
           if (fills > 0) {  // the epilogue has read the previous fill
             if (!mbar_wait(acc_empty, (fills - 1) & 1u, p.err, 13)) { ok = false; break; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           }
-          int j = 0;       // accumulator of the next k step (round robin over nacc)
-          int first = 0;   // k steps issued this pass (each accumulator starts fresh on its first)
-          for (int i = 0; i < it.nkb; ++i) {
-            if (!mbar_wait(&s_full[r.slot], r.phase, p.err, 14)) { ok = false; break; }
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint64_t bd = bd_base + bd_step * static_cast<uint64_t>(r.slot);
-            const uint32_t a = tmem + p.a_col + 32u * static_cast<uint32_t>(r.slot);
-#pragma unroll
-            for (int k = 0; k < kBK / 16; ++k) {  // 16 k per MMA: 8 TMEM columns of A, 32 bytes of B
-              const uint32_t d = tmem + static_cast<uint32_t>(j * it.ntot);
-              const uint32_t acc = first >= it.nacc ? 1u : 0u;
-              mma_f16_ts(d, a + 8u * k, bd + 2 * k, idesc0, acc);
-              if (it.ntot > n0)
-                mma_f16_ts(d + static_cast<uint32_t>(n0), a + 8u * k, bd + bd_n0 + 2 * k, idesc1, acc);
-              if (++j == it.nacc) j = 0;
-              ++first;
-            }
-            mma_commit(&s_free[r.slot]);
-            last = r;
-            any = true;
-            r.step(S);
+          if (!(two ? stages(std::true_type{}) : stages(std::false_type{}))) ok = false;
+          if (ok) {
+            if constexpr (kPair) mma_commit_pair(acc_full);
+            else mma_commit(acc_full);
           }
-          if (ok) mma_commit(acc_full);
           ++fills;
         }
       }
@@ -770,27 +882,42 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     for (int qi = first_item; qi < p.n_items && ok; qi += item_step) {
       const TmItem it = item(qi);
       const int tile_m = it.tile_m, t_begin = it.t_begin, t_count = it.t_count, T = it.T, P = it.P;
-      const int nacc = it.nacc, ntot = it.ntot, npass = it.npass, split = it.split, tail_idx = it.tail_idx;
+      const int nacc = it.nacc, acols = it.acols, PA = it.PA, npass = it.npass, split = it.split,
+                tail_idx = it.tail_idx;
       const bool tail = it.tail, part = it.part;
-      const int o = tile_m * 128 + r;
+      const int mt = kPair ? 2 * tile_m + static_cast<int>(v) : tile_m;  // 128-row tile of this CTA
+      const int o = mt * 128 + r;
       // Epilogue sums that are single fp32 values (one plane, one accumulator, no Int8 scale,
       // no partials) are scaled in fp32; others are summed and scaled in fp64.
       const bool f32_sums = P == 1 && nacc == 1 && kDt != 9 && !part;
+      const bool two = kPair && P == 3;  // pairs, 3 planes: a stage takes two ring slots
       for (int pass = 0; pass < npass && ok; ++pass) {
-        for (int i = 0; i < it.nkb; ++i, ++stage_idx, w.step(Sw), st.step(S)) {
+        for (int i = 0; i < it.nkb; ++i, ++stage_idx, w.step(Sw)) {
+          const Ring s1 = st;  // the stage's slot (its TMEM A slot)
+          Ring s2 = st;        // the slot of plane 2's x (3-plane pair stages)
+          if (two) s2.step(S);
+          st = s2;
+          st.step(S);
           if ((stage_idx & 1) != grp) continue;
           if (!warp_wait(&w_full[w.slot], w.phase, p.err, 16)) { ok = false; break; }
           uint32_t v[32];
           convert_row<kDt>(wring + w.slot * p.w_bytes, r, v);
           __syncwarp();
           if (lane == 0) mbar_arrive(&w_empty[w.slot]);
-          if (!warp_wait(&s_free[st.slot], st.phase ^ 1u, p.err, 21)) { ok = false; break; }
+          if (!warp_wait(&s_free[s1.slot], s1.phase ^ 1u, p.err, 21)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          tmem_st32(tmem + lane_base + p.a_col + 32u * static_cast<uint32_t>(st.slot), v);
+          tmem_st32(tmem + lane_base + p.a_col + 32u * static_cast<uint32_t>(s1.slot), v);
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
           asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
           __syncwarp();
-          if (lane == 0) mbar_arrive(&s_full[st.slot]);
+          if (lane == 0) {
+            if constexpr (kPair) mbar_arrive_cluster(cluster_addr(&s_full[s1.slot], 0));
+            else mbar_arrive(&s_full[s1.slot]);
+          }
+          if (two) {  // the second slot's barrier counts these warps too; its previous use is over first
+            if (!warp_wait(&s_free[s2.slot], s2.phase ^ 1u, p.err, 22)) { ok = false; break; }
+            if (lane == 0) mbar_arrive_cluster(cluster_addr(&s_full[s2.slot], 0));
+          }
         }
         if (!ok) break;
         // ------------------------------------------------------------ epilogue of this pass
@@ -837,10 +964,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
             double y[16];
 #pragma unroll
             for (int e = 0; e < 16; ++e) y[e] = 0.0;
-            for (int pl = 0; pl < P; ++pl) {
+            for (int pl = 0; pl < PA; ++pl) {
               for (int jj = 0; jj < nacc; ++jj) {
                 uint32_t v[16];
-                tmem_ld16(tmem + lane_base + static_cast<uint32_t>(jj * ntot + pl * T + tc), v);
+                tmem_ld16(tmem + lane_base + static_cast<uint32_t>(jj * acols + pl * T + tc), v);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
                 for (int e = 0; e < 16; ++e) y[e] += static_cast<double>(__uint_as_float(v[e]));
@@ -857,7 +984,8 @@ __global__ void __launch_bounds__(kTmThreads, 1)
               }
               if (tail) {
                 if (valid)
-                  p.partial[((static_cast<int64_t>(tail_idx) * p.tail_s + split) * p.TB + (t - t_begin)) * 128 + r] = yy;
+                  p.partial[((static_cast<int64_t>(kPair ? 2 * tail_idx + static_cast<int>(v) : tail_idx) * p.tail_s +
+                              split) * p.TB + (t - t_begin)) * 128 + r] = yy;
               } else if (p.splits > 1) {
                 if (valid) p.partial[(static_cast<int64_t>(split) * p.M + t) * p.rows + o] = yy;
               }
@@ -935,10 +1063,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
               uint64_t pol;
               asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
               if (p.pair) {
-                tma_store_2d(&tm_o1, s1, tile_m * 64, ty, pol);
+                tma_store_2d(&tm_o1, s1, mt * 64, ty, pol);
               } else {
-                tma_store_2d(&tm_o1, s1, tile_m * 128, ty, pol);
-                if (p.tma_post) tma_store_2d(&tm_o2, s2, tile_m * 128, ty, pol);
+                tma_store_2d(&tm_o1, s1, mt * 128, ty, pol);
+                if (p.tma_post) tma_store_2d(&tm_o2, s2, mt * 128, ty, pol);
               }
               asm volatile("cp.async.bulk.commit_group;" ::: "memory");
             }
@@ -946,7 +1074,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty);
+        if (lane == 0) {
+          if constexpr (kPair) mbar_arrive_cluster(cluster_addr(acc_empty, 0));
+          else mbar_arrive(acc_empty);
+        }
       }
     }
     // the staging buffers stay valid until the last stores have read them
@@ -955,9 +1086,14 @@ __global__ void __launch_bounds__(kTmThreads, 1)
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
+  // pair: neither CTA frees its TMEM or exits while the other may still signal its barriers
+  if constexpr (kPair) cluster_sync_all();
   if (warp == 0) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    if constexpr (kPair)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
 }
 
@@ -993,6 +1129,7 @@ __global__ void k_splitk_reduce(const KParams p) {
 // Gate/Up pair in pair mode.
 struct TailParams {
   int rows, M, TB, tiles_t, tail_first, tail_s, ntail;
+  int sub;                     // 128-row parts per tile: 2 for CTA-pair tiles, else 1
   const double* partial;
   float* pre;
   float* post;
@@ -1007,15 +1144,15 @@ struct TailParams {
 
 __global__ void k_tail_reduce(const TailParams p) {
   const int per_tile = p.TB * (p.pair ? 64 : 128);
-  const int64_t n = static_cast<int64_t>(p.ntail) * per_tile;
+  const int64_t n = static_cast<int64_t>(p.ntail) * p.sub * per_tile;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int k = static_cast<int>(i / per_tile);
+    const int k = static_cast<int>(i / per_tile);  // 128-row part: tail tile k / sub, part k % sub
     const int rem = static_cast<int>(i - static_cast<int64_t>(k) * per_tile);
-    const int tile = p.tail_first + k;
+    const int tile = p.tail_first + k / p.sub;
     const int t = (tile % p.tiles_t) * p.TB + rem / (p.pair ? 64 : 128);
     const int r = p.pair ? 2 * (rem % 64) : rem % 128;
-    const int o = (tile / p.tiles_t) * 128 + r;
+    const int o = ((tile / p.tiles_t) * p.sub + k % p.sub) * 128 + r;
     if (t >= p.M || o >= p.rows) continue;
     const double* base = p.partial + (static_cast<int64_t>(k) * p.tail_s * p.TB + (t % p.TB)) * 128 + r;
     const int64_t stride = static_cast<int64_t>(p.TB) * 128;
@@ -1182,6 +1319,7 @@ Plan make_plan(int M, int cols, int rows, int xsplit, DType dt) {
 }
 
 struct TmPlan {
+  bool pair;                                           // CTA pairs: 256-row tiles, M = 256 MMAs
   int TB, tpass[3], nacc[3], Mp, Kp, nkb, splits, kb_per_split, kbb, acc_cols;
   int tiles_t, tiles, tail_first, tail_s, tail_kbps;  // tail schedule (tail_first < 0: none)
   int pblk_bytes;                                      // per-token-block plane counts (shared memory)
@@ -1191,17 +1329,18 @@ struct TmPlan {
   size_t planes_bytes, scale_bytes, pcnt_bytes, partial_bytes;
 };
 
-// Split-K count (1..8) for `tiles` CTAs of `nkb` k-blocks, from a time model: one CTA per SM,
-// a 64-k stage costs ~0.7 us (measured per-stage period of k_gemm_tm), so the GEMM takes
-// waves(s) * 0.7 us * nkb / s; with s > 1 the fp64 partials (s x M x rows x 8 B) are written
-// and read back once (at the measured HBM rate) and the reduce launch costs ~5 us.
-int tm_splits(int tiles, int nkb, int M, int rows) {
+// Split-K count (1..8) for `tiles` items of `nkb` k-blocks on `units` CTAs (or CTA pairs)
+// at once, from a time model: a 64-k stage costs ~0.7 us (measured per-stage period of
+// k_gemm_tm), so the GEMM takes waves(s) * 0.7 us * nkb / s; with s > 1 the fp64 partials
+// (s x M x rows x 8 B) are written and read back once (at the measured HBM rate) and the
+// reduce launch costs ~5 us.
+int tm_splits(int tiles, int nkb, int M, int rows, int units) {
   const double stage_us = 0.7, hbm_bytes_per_us = 6.5e6, reduce_us = 5.0;
   int best = 1;
   double best_t = 0.0;
   for (int s = 1; s <= 8 && s <= nkb; ++s) {
     const int ctas = tiles * s;
-    const int waves = (ctas + 147) / 148;
+    const int waves = (ctas + units - 1) / units;
     const int stages = (nkb + s - 1) / s;
     double t = waves * stage_us * stages;
     if (s > 1) t += 2.0 * s * static_cast<double>(M) * rows * 8.0 / hbm_bytes_per_us + reduce_us;
@@ -1213,28 +1352,46 @@ int tm_splits(int tiles, int nkb, int M, int rows) {
   return best;
 }
 
-TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_tail = true) {
+// CTA pairs halve the x bytes each SM loads per MMA (each CTA of the pair holds half of the
+// stage's x rows). Opt-in (WELVET_B200_GEMM_PAIR=1): single CTAs measured as fast or faster
+// on B200 except at 1024+ tokens of one-plane x. Possible when the rows make whole 256-row
+// tiles (an even number of 128-row mirror tiles) and a token block fills half an MMA.
+bool tm_pair_wanted(int M, int rows) {
+  const char* e = std::getenv("WELVET_B200_GEMM_PAIR");
+  if (!e || std::strcmp(e, "1") != 0) return false;
+  return M >= 128 && ((rows + kBM - 1) / kBM) % 2 == 0;
+}
+
+TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_tail = true, bool allow_pair = true) {
   TmPlan pl{};
+  pl.pair = allow_pair && tm_pair_wanted(M, rows);
+  const int units = pl.pair ? 74 : 148;  // CTAs (CTA pairs) running at once on 148 SMs
   const int m16 = static_cast<int>(round_up(M, 16));
-  pl.TB = m16 < 256 ? m16 : 256;
+  // pair MMAs take N in multiples of 32 (16 x rows in each CTA)
+  const int mb = pl.pair ? static_cast<int>(round_up(M, 32)) : m16;
+  pl.TB = mb < 256 ? mb : 256;
   pl.acc_cols = 0;
   int xrows = 0;
   for (int P = 1; P <= 3; ++P) {
-    const int cap = (kTmAccMax / P) & ~15;  // 384, 192, 128
+    // pairs: 256, 128, 128 tokens (3 planes: planes 1 and 2 share an accumulator); otherwise
+    // up to two MMAs of 384 accumulator columns (384, 192, 128)
+    const int cap = pl.pair ? (P == 1 ? 256 : 128) : (kTmAccMax / P) & ~15;
     pl.tpass[P - 1] = pl.TB < cap ? pl.TB : cap;
     const int ntot = P * pl.tpass[P - 1];
+    const int acols = (pl.pair && P == 3 ? 2 : P) * pl.tpass[P - 1];
     // independent accumulators so that short MMAs do not wait on each other's results
-    pl.nacc[P - 1] = ntot <= 64 ? 4 : (ntot <= 128 ? 2 : 1);
+    pl.nacc[P - 1] = acols <= 64 ? 4 : (acols <= 128 ? 2 : 1);
     if (P <= xsplit) {
-      pl.acc_cols = std::max(pl.acc_cols, pl.nacc[P - 1] * ntot);
-      xrows = std::max(xrows, ntot);
+      pl.acc_cols = std::max(pl.acc_cols, pl.nacc[P - 1] * acols);
+      // pairs: a 3-plane stage puts plane 2 in a second slot
+      xrows = std::max(xrows, pl.pair && P == 3 ? 2 * pl.tpass[P - 1] : ntot);
     }
   }
   pl.Mp = m16;
   pl.Kp = static_cast<int>(round_up(cols, kBK));
   pl.nkb = pl.Kp / kBK;
   pl.kbb = dt == DType::FP4 ? kBK / 2 : kBK;
-  pl.x_bytes = static_cast<uint32_t>(round_up(static_cast<int64_t>(xrows) * 128, 1024));
+  pl.x_bytes = static_cast<uint32_t>(round_up(static_cast<int64_t>(xrows) * (pl.pair ? 64 : 128), 1024));
   pl.w_bytes = static_cast<uint32_t>(kBM * pl.kbb);
   pl.a_col = static_cast<uint32_t>(round_up(pl.acc_cols, 32));
   // stages (an x slot + a TMEM A slot each): as many as TMEM and shared memory allow, up to 8,
@@ -1255,15 +1412,17 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_
   // At least half the SM's shared memory, so that one CTA (and its 512 TMEM columns) runs per
   // SM: a second CTA on the SM would only stall in tcgen05.alloc.
   if (pl.smem < 116 * 1024) pl.smem = 116 * 1024;
-  const int tiles = static_cast<int>(((rows + kBM - 1) / kBM) * static_cast<int64_t>((M + pl.TB - 1) / pl.TB));
-  const int splits = tm_splits(tiles, pl.nkb, M, rows);
+  const int sub = pl.pair ? 2 : 1;
+  const int tiles =
+      static_cast<int>(((rows + kBM - 1) / kBM / sub) * static_cast<int64_t>((M + pl.TB - 1) / pl.TB));
+  const int splits = tm_splits(tiles, pl.nkb, M, rows, units);
   pl.kb_per_split = (pl.nkb + splits - 1) / splits;
   pl.splits = (pl.nkb + pl.kb_per_split - 1) / pl.kb_per_split;
   pl.planes_bytes = static_cast<size_t>(round_up(static_cast<int64_t>(xsplit) * pl.Mp * pl.Kp * 2, 1024));
   pl.scale_bytes = static_cast<size_t>(round_up(static_cast<int64_t>(pl.Mp) * 4, 1024));
   pl.pcnt_bytes = pl.scale_bytes;
   pl.partial_bytes = pl.splits > 1 ? static_cast<size_t>(pl.splits) * M * rows * 8 : 0;
-  // A last, partly filled wave of whole tiles (up to half the SMs) costs as long as a full
+  // A last, partly filled wave of whole tiles (up to half the units) costs as long as a full
   // one: those tiles are cut along K instead (into at most 8 slices, one wave of items in
   // all), and their fp64 partials summed by a small reduce launch.
   pl.tiles_t = (M + pl.TB - 1) / pl.TB;
@@ -1271,16 +1430,16 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_
   pl.tail_first = -1;
   pl.tail_s = 1;
   pl.tail_kbps = pl.nkb;
-  const int ntail = tiles % 148;
-  if (allow_tail && pl.splits == 1 && tiles > 148 && ntail > 0 && ntail <= 74 && pl.nkb >= 2) {
-    int s = 148 / ntail;
+  const int ntail = tiles % units;
+  if (allow_tail && pl.splits == 1 && tiles > units && ntail > 0 && ntail <= units / 2 && pl.nkb >= 2) {
+    int s = units / ntail;
     if (s > 8) s = 8;
     if (s > pl.nkb) s = pl.nkb;
     if (s >= 2) {
       pl.tail_kbps = (pl.nkb + s - 1) / s;
       pl.tail_s = (pl.nkb + pl.tail_kbps - 1) / pl.tail_kbps;  // every slice non-empty
       pl.tail_first = tiles - ntail;
-      pl.partial_bytes = static_cast<size_t>(ntail) * pl.tail_s * pl.TB * 128 * 8;
+      pl.partial_bytes = static_cast<size_t>(ntail) * sub * pl.tail_s * pl.TB * 128 * 8;
     }
   }
   return pl;
@@ -1377,9 +1536,11 @@ size_t gemm_scratch_bytes(int M, int cols, int rows, int xsplit, bool tail) {
   size_t need = 0;
   for (DType dt : {DType::FP8E4M3, DType::FP4}) {
     const Plan pl = make_plan(M, cols, rows, xsplit, dt);
-    const TmPlan tp = make_tm_plan(M, cols, rows, xsplit, dt, tail);
     need = std::max(need, pl.planes_bytes + pl.scale_bytes + pl.partial_bytes);
-    need = std::max(need, tp.planes_bytes + tp.scale_bytes + tp.pcnt_bytes + tp.partial_bytes);
+    for (bool pair : {true, false}) {  // CTA pairs, and single CTAs when no pair can run
+      const TmPlan tp = make_tm_plan(M, cols, rows, xsplit, dt, tail, pair);
+      need = std::max(need, tp.planes_bytes + tp.scale_bytes + tp.pcnt_bytes + tp.partial_bytes);
+    }
   }
   return need;
 }
@@ -1405,15 +1566,75 @@ Status set_max_smem(const void* kern, size_t bytes) {
   return Status::Ok();
 }
 
+using TmKernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, TmParams);
+
+TmKernel tm_kernel(DType dt, bool pair) {
+  switch (dt) {
+  case DType::FP4: return pair ? k_gemm_tm<16, true> : k_gemm_tm<16, false>;
+  case DType::FP8E4M3: return pair ? k_gemm_tm<4, true> : k_gemm_tm<4, false>;
+  case DType::FP8E5M2: return pair ? k_gemm_tm<5, true> : k_gemm_tm<5, false>;
+  case DType::Int8: return pair ? k_gemm_tm<9, true> : k_gemm_tm<9, false>;
+  default: return nullptr;
+  }
+}
+
+cudaLaunchConfig_t pair_config(unsigned pairs, size_t smem, cudaStream_t st, cudaLaunchAttribute* at) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kTmThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+// CTA pairs of `kern` that can be resident at once with `smem` bytes of shared memory each
+// (asked once per kernel, device and size); 0 when none can.
+int tm_max_pairs(TmKernel kern, size_t smem) {
+  static std::mutex mu;
+  static std::vector<std::tuple<const void*, int, size_t, int>> known;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const void* key = reinterpret_cast<const void*>(kern);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& k : known)
+      if (std::get<0>(k) == key && std::get<1>(k) == dev && std::get<2>(k) == smem) return std::get<3>(k);
+  }
+  int n = 0;
+  if (set_max_smem(key, smem).ok()) {
+    cudaLaunchAttribute at[1];
+    const cudaLaunchConfig_t cfg = pair_config(74, smem, nullptr, at);
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      n = 0;
+    }
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  known.emplace_back(key, dev, smem, n);
+  return n;
+}
+
 Status launch_tm(const GemmArgs& a, cudaStream_t st) {
   if (!a.Wg || (reinterpret_cast<uintptr_t>(a.Wg) & 15) != 0)
     return Status::Internal("gemm_tc: the layer has no GEMM mirror (16-byte aligned)");
   TmPlan pl = make_tm_plan(a.M, a.cols, a.rows, a.xsplit, a.dtype);
+  int pairs = 0;
+  if (pl.pair) {
+    const TmKernel k = tm_kernel(a.dtype, true);
+    pairs = k ? tm_max_pairs(k, pl.smem) : 0;
+    if (pairs < 1) pl = make_tm_plan(a.M, a.cols, a.rows, a.xsplit, a.dtype, true, false);
+  }
   if (pl.sw < 2 || pl.sx < 2 || pl.a_col + 32u * pl.sx > kTmemCols)
     return Status::Internal("gemm_tc: pipeline does not fit on the SM");
   size_t need = pl.planes_bytes + pl.scale_bytes + pl.pcnt_bytes + pl.partial_bytes;
   if (pl.tail_first >= 0 && a.scratch_bytes < need) {  // no room for the tail partials
-    pl = make_tm_plan(a.M, a.cols, a.rows, a.xsplit, a.dtype, false);
+    pl = make_tm_plan(a.M, a.cols, a.rows, a.xsplit, a.dtype, false, pl.pair);
     need = pl.planes_bytes + pl.scale_bytes + pl.pcnt_bytes + pl.partial_bytes;
   }
   if (!a.scratch || a.scratch_bytes < need) return Status::Internal("gemm_tc: scratch too small");
@@ -1432,8 +1653,10 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
   CUtensorMap tm_x[3];
   for (int P = 1; P <= 3; ++P) {
     const int q = P <= a.xsplit ? P : 1;  // maps for plane counts above xsplit are never used
+    // a CTA of a pair loads boxes of half a pass's tokens
+    const int box = pl.pair ? pl.tpass[q - 1] / 2 : pl.tpass[q - 1];
     WB_TRY(make_map_planes(&tm_x[P - 1], planes, static_cast<uint64_t>(pl.Kp), static_cast<uint64_t>(pl.Mp),
-                           static_cast<uint64_t>(a.xsplit), static_cast<uint32_t>(pl.tpass[q - 1])));
+                           static_cast<uint64_t>(a.xsplit), static_cast<uint32_t>(box)));
   }
 
   TmParams p{};
@@ -1491,27 +1714,28 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (sms < 1) sms = 148;
   }
-  const dim3 grid(static_cast<unsigned>(p.n_items < sms ? p.n_items : sms), 1, 1);
-  auto launch = [&](auto kern) -> Status {
-    WB_TRY(set_max_smem(reinterpret_cast<const void*>(kern), smem));
+  const TmKernel kern = tm_kernel(a.dtype, pl.pair);
+  if (!kern) return Status::Unsupported("gemm_tc: dtype");
+  WB_TRY(set_max_smem(reinterpret_cast<const void*>(kern), smem));
+  if (pl.pair) {
+    // clusters of 2, one pair per item up to the pairs that fit at once
+    cudaLaunchAttribute at[1];
+    const cudaLaunchConfig_t cfg =
+        pair_config(static_cast<unsigned>(p.n_items < pairs ? p.n_items : pairs), smem, st, at);
+    WB_CUDA(cudaLaunchKernelEx(&cfg, kern, tm_x[0], tm_x[1], tm_x[2], tm_o[0], tm_o[1], p));
+  } else {
+    const dim3 grid(static_cast<unsigned>(p.n_items < sms ? p.n_items : sms), 1, 1);
     kern<<<grid, kTmThreads, smem, st>>>(tm_x[0], tm_x[1], tm_x[2], tm_o[0], tm_o[1], p);
-    return cuda_status(cudaGetLastError(), "gemm_tc (tmem) launch");
-  };
-  switch (a.dtype) {
-  case DType::FP4: WB_TRY(launch(k_gemm_tm<16>)); break;
-  case DType::FP8E4M3: WB_TRY(launch(k_gemm_tm<4>)); break;
-  case DType::FP8E5M2: WB_TRY(launch(k_gemm_tm<5>)); break;
-  case DType::Int8: WB_TRY(launch(k_gemm_tm<9>)); break;
-  default: return Status::Unsupported("gemm_tc: dtype");
+    WB_TRY(cuda_status(cudaGetLastError(), "gemm_tc (tmem) launch"));
   }
   if (pl.tail_first >= 0) {
     const int ntail = pl.tiles - pl.tail_first;
     TailParams r{};
     r.rows = a.rows; r.M = a.M; r.TB = pl.TB; r.tiles_t = pl.tiles_t; r.tail_first = pl.tail_first;
-    r.tail_s = pl.tail_s; r.ntail = ntail; r.partial = partial;
+    r.tail_s = pl.tail_s; r.ntail = ntail; r.sub = pl.pair ? 2 : 1; r.partial = partial;
     r.pre = a.pre; r.post = a.post; r.ld_out = a.ld_out; r.bias = a.bias; r.bias_len = a.bias_len; r.act = a.act;
     r.pair = a.pair ? 1 : 0; r.h = a.h; r.ld_h = a.ld_h;
-    const int64_t n = static_cast<int64_t>(ntail) * pl.TB * (a.pair ? 64 : 128);
+    const int64_t n = static_cast<int64_t>(ntail) * r.sub * pl.TB * (a.pair ? 64 : 128);
     k_tail_reduce<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(r);
     WB_CUDA(cudaGetLastError());
   }

@@ -65,6 +65,34 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return mbar_wait_slow(bar, parity, err, code);
 }
 
+// ---- CTA pairs (clusters of 2): barriers that the other CTA of the pair arrives on.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the object at `p`'s offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+  return a;
+}
+
+// Arrive on a barrier of either CTA of the pair (default semantics: release at CTA scope). A
+// cluster-scope release here fenced every converter warp on every stage; what the even CTA's
+// MMA needs from the odd CTA is ordered by tcgen05.wait::st and tcgen05.fence before the
+// arrive, and its x bytes by the barrier's transaction count.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+
+// Every thread of both CTAs: arrivals before it are visible to the other CTA after it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // Ring position without divisions: slot and phase bit advance together.
 struct Ring {
   int slot = 0;
