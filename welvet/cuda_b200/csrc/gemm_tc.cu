@@ -800,7 +800,8 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       uint32_t fills = 0;  // accumulator fills so far (one per pass of every item)
       for (int qi = first_item; qi < p.n_items && ok; qi += item_step) {
         const TmItem it = item(qi);
-        const int n0 = it.ntot < 256 ? it.ntot : 256;  // first MMA's N; the second covers [n0, ntot)
+        // first MMA's N; the second covers [n0, ntot) (pairs: planes 0 and 1, then plane 2)
+        const int n0 = kPair ? (it.P < 2 ? it.P : 2) * it.T : (it.ntot < 256 ? it.ntot : 256);
         const uint32_t idesc0 = (1u << 4) | (static_cast<uint32_t>(n0 >> 3) << 17) | ((kM >> 4) << 24);
         const uint32_t idesc1 = (1u << 4) | (static_cast<uint32_t>((it.ntot - n0) >> 3) << 17) | ((kM >> 4) << 24);
         const uint64_t bd_n0 = static_cast<uint64_t>((n0 * 128) >> 4);  // rows [n0, ntot) of a slot
@@ -1376,7 +1377,12 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_
     // pairs: 256, 128, 128 tokens (3 planes: planes 1 and 2 share an accumulator); otherwise
     // up to two MMAs of 384 accumulator columns (384, 192, 128)
     const int cap = pl.pair ? (P == 1 ? 256 : 128) : (kTmAccMax / P) & ~15;
-    pl.tpass[P - 1] = pl.TB < cap ? pl.TB : cap;
+    int T = pl.TB < cap ? pl.TB : cap;
+    if (T < pl.TB) {  // passes of equal size (256 tokens at 2 planes: 128 + 128, not 192 + 64)
+      const int npass = (pl.TB + cap - 1) / cap;
+      T = static_cast<int>(round_up((pl.TB + npass - 1) / npass, pl.pair ? 32 : 16));
+    }
+    pl.tpass[P - 1] = T;
     const int ntot = P * pl.tpass[P - 1];
     const int acols = (pl.pair && P == 3 ? 2 : P) * pl.tpass[P - 1];
     // independent accumulators so that short MMAs do not wait on each other's results
@@ -1394,17 +1400,26 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_
   pl.x_bytes = static_cast<uint32_t>(round_up(static_cast<int64_t>(xrows) * (pl.pair ? 64 : 128), 1024));
   pl.w_bytes = static_cast<uint32_t>(kBM * pl.kbb);
   pl.a_col = static_cast<uint32_t>(round_up(pl.acc_cols, 32));
-  // stages (an x slot + a TMEM A slot each): as many as TMEM and shared memory allow, up to 8,
-  // keeping room for 4 W slots; then the W ring takes the rest (up to 32). 1 KB aligns the
+  // stages (an x slot + a TMEM A slot each): as many as TMEM allows (up to 8) while the raw W
+  // ring keeps 64 KB (and at least 4 slots), but no fewer than 3; then the W ring takes the
+  // rest (up to 32). Measured with 32 KB x slots (FP8, 16384^2 and the SwiGLU cell): 4 x
+  // stages with 8 W slots beat 5 with 4 by 5-8 %, and 3 with 10 by 2-4 %. 1 KB aligns the
   // base, 1 KB holds the barriers (at most 2*32 + 2*8 + 2 of them); the epilogue staging and
-  // the per-token-block plane counts take their own space.
+  // the per-token-block plane counts take their own space. WELVET_B200_GEMM_XSLOTS caps the
+  // x stages (tuning).
   const int tiles_t_plan = (M + pl.TB - 1) / pl.TB;
   pl.pblk_bytes = static_cast<int>(round_up(static_cast<int64_t>(std::min(tiles_t_plan, kTmMaxBlocks)) * 4, 16));
   const int64_t budget = 227 * 1024 - 2048 - pl.pblk_bytes - kStageArea;
   pl.sx = (static_cast<int>(kTmemCols) - static_cast<int>(pl.a_col)) / 32;
   if (pl.sx > 8) pl.sx = 8;
-  while (pl.sx > 2 && pl.sx * static_cast<int64_t>(pl.x_bytes) + 4 * static_cast<int64_t>(pl.w_bytes) > budget)
-    --pl.sx;
+  if (const char* e = std::getenv("WELVET_B200_GEMM_XSLOTS")) {
+    const int n = std::atoi(e);
+    if (n >= 2 && n < pl.sx) pl.sx = n;
+  }
+  const int64_t xb = pl.x_bytes, wb = pl.w_bytes;
+  const int64_t w_keep = std::max<int64_t>(4 * wb, 64 * 1024);
+  while (pl.sx > 3 && pl.sx * xb + w_keep > budget) --pl.sx;
+  while (pl.sx > 2 && pl.sx * xb + 4 * wb > budget) --pl.sx;
   pl.sw = static_cast<int>((budget - pl.sx * static_cast<int64_t>(pl.x_bytes)) / pl.w_bytes);
   if (pl.sw > 32) pl.sw = 32;
   pl.smem = static_cast<size_t>(pl.sx) * pl.x_bytes + static_cast<size_t>(pl.sw) * pl.w_bytes + 2048 + pl.pblk_bytes +
