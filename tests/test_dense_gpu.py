@@ -377,7 +377,7 @@ def test_dense_vs_reference_cuda_kernel(wb, oracle):
 GEMM_TOL = {"3": 2.0 ** -16, "2": 2.0 ** -15, "1": 2.0 ** -9}
 
 
-@pytest.mark.parametrize("kernel", ["tmem", "smem", "pair"])
+@pytest.mark.parametrize("kernel", ["tmem", "smem", "pair", "dbuf"])
 @pytest.mark.parametrize("xsplit", ["3", "2", "1"])
 @pytest.mark.parametrize("dt", [16, 4, 5, 9])
 @pytest.mark.parametrize("shape", [(128, 64, 8), (300, 1000, 16), (256, 4096, 64), (130, 257, 100), (1024, 512, 5),
@@ -390,11 +390,14 @@ def test_tensor_core_path_parity(wb, oracle, dt, shape, xsplit, kernel, monkeypa
     bound per x split. 9600 x 256 at 300 tokens: 150 tiles over two token blocks, the last
     two cut along K (tail launch). "pair": the TMEM kernel on CTA pairs (M = 256 MMAs), taken
     with 128 or more tokens and an even number of 128-row tiles: 200 x 640 whole tiles,
-    9728 x 256 76 pair tiles with a tail, 256 x 8192 one pair tile split along K."""
+    9728 x 256 76 pair tiles with a tail, 256 x 8192 one pair tile split along K. "dbuf": two
+    accumulator buffers of 192 columns (token blocks of at most 192, passes of 192 / 96 / 64
+    tokens for 1 / 2 / 3 planes), the epilogue of one fill overlapping the next fill's MMAs."""
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
     monkeypatch.setenv("WELVET_B200_XSPLIT", xsplit)
     monkeypatch.setenv("WELVET_B200_GEMM", "smem" if kernel == "smem" else "tmem")
     monkeypatch.setenv("WELVET_B200_GEMM_PAIR", "1" if kernel == "pair" else "0")
+    monkeypatch.setenv("WELVET_B200_GEMM_DBUF", "192" if kernel == "dbuf" else "0")
     monkeypatch.setenv("WELVET_B200_BATCHED", "tc")  # batches of 5..8 would otherwise take the GEMV
     out, in_, batch = shape
     w, x, bias, ref = _case(oracle, dt, out, in_, batch, 2.0, out + in_ + batch, 0)
@@ -490,16 +493,17 @@ def test_simt_gemv_still_correct(wb, oracle, dt, monkeypatch):
 @pytest.mark.parametrize("rows,d,inter", [(1, 256, 640), (3, 256, 640), (24, 256, 640), (300, 256, 640),
                                           (24, 2048, 96), (16, 256, 9600), (300, 256, 4864)])
 @pytest.mark.parametrize("dt", [16, 4, 9])
-@pytest.mark.parametrize("pair", ["0", "1"])
-def test_swiglu_tensor_paths(wb, oracle, dt, rows, d, inter, pair, monkeypatch):
+@pytest.mark.parametrize("mode", ["single", "pair", "dbuf"])
+def test_swiglu_tensor_paths(wb, oracle, dt, rows, d, inter, mode, monkeypatch):
     """1..4 rows: Gate and Up fused in the tensor GEMV; more: one tcgen05 GEMM over the
     interleaved Gate/Up pair mirror writing h in its epilogue (300 rows: several token
     blocks; d = 2048 with a narrow intermediate: split-K with the paired reduce; 9600: 150
     pair tiles, the last two cut along K and reduced by the tail launch; 300 x 4864: 76
-    pair tiles per token block, with a tail). pair = 1: the GEMMs on CTA pairs where they
-    qualify (300 rows)."""
+    pair tiles per token block, with a tail). "pair": the GEMMs on CTA pairs where they qualify
+    (300 rows); "dbuf": two accumulator buffers of 128 columns."""
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
-    monkeypatch.setenv("WELVET_B200_GEMM_PAIR", pair)
+    monkeypatch.setenv("WELVET_B200_GEMM_PAIR", "1" if mode == "pair" else "0")
+    monkeypatch.setenv("WELVET_B200_GEMM_DBUF", "128" if mode == "dbuf" else "0")
     rng = np.random.default_rng(20 + rows)
     G, U, D = [(rng.standard_normal(s) * 0.5).astype(np.float32) for s in ((inter, d), (inter, d), (d, inter))]
     x = rng.standard_normal((rows, d)).astype(np.float32)

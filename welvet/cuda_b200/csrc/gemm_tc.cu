@@ -19,7 +19,7 @@
 // and bias / activation exactly as the reference's dense_bias_act (kernels.cu:147-161).
 //
 // Every mbarrier wait is bounded by %globaltimer (2 s); on expiry the kernel records an error
-// word and winds down, it never spins forever. No TMA multicast is used.
+// word and winds down, it never spins forever. Every tensor load has one destination CTA.
 #include "gemm_tc.hpp"
 #include "codec.cuh"
 #include "pipeline.cuh"
@@ -415,6 +415,7 @@ struct TmParams {
   // to `partial`.
   int tiles_t, tail_first, tail_s, tail_kbps;
   int tiles, n_items;           // work items: tiles (x splits), or whole tiles then tail slices
+  uint32_t acc_buf;             // columns of one accumulator buffer when there are two, else 0
 };
 
 // Token blocks whose plane counts a CTA keeps in shared memory (more blocks: every block runs
@@ -628,9 +629,9 @@ __global__ void __launch_bounds__(kTmThreads, 1)
   uint64_t* w_empty = w_full + Sw;         // converter warps (4) -> W producer
   uint64_t* s_full = w_empty + Sw;         // x producer (1 + tx) and converter warps (4) -> MMA
   uint64_t* s_free = s_full + S;           // MMA commit -> x producer and converters
-  uint64_t* acc_full = s_free + S;         // MMA commit -> epilogue
-  uint64_t* acc_empty = acc_full + 1;      // epilogue warps (8) -> MMA
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  uint64_t* acc_full = s_free + S;         // MMA commit -> epilogue, per accumulator buffer
+  uint64_t* acc_empty = acc_full + 2;      // epilogue warps (8) -> MMA, per accumulator buffer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   int* s_pblk = reinterpret_cast<int*>(tmem_slot + 1);  // planes needed per token block
 
   const int warp = threadIdx.x >> 5;
@@ -647,8 +648,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       mbar_init(&s_full[s], kPair ? 9 : 5);
       mbar_init(&s_free[s], 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, kPair ? 16 : 8);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kPair ? 16 : 8);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   const bool pblk_ok = p.tiles_t <= kTmMaxBlocks;
@@ -798,6 +801,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       bool any = false;
       bool ok = true;
       uint32_t fills = 0;  // accumulator fills so far (one per pass of every item)
+      uint32_t dbase = 0;  // first TMEM column of the current fill's accumulator buffer
       for (int qi = first_item; qi < p.n_items && ok; qi += item_step) {
         const TmItem it = item(qi);
         // first MMA's N; the second covers [n0, ntot) (pairs: planes 0 and 1, then plane 2)
@@ -825,7 +829,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
             const uint32_t a = tmem + p.a_col + 32u * static_cast<uint32_t>(r.slot);
 #pragma unroll
             for (int k = 0; k < kBK / 16; ++k) {  // 16 k per MMA: 8 TMEM columns of A, 32 bytes of B
-              const uint32_t d = tmem + static_cast<uint32_t>(j * it.acols);
+              const uint32_t d = tmem + dbase + static_cast<uint32_t>(j * it.acols);
               const uint32_t acc = first >= it.nacc ? 1u : 0u;
               if constexpr (kPair) {
                 mma_f16_ts_pair(d, a + 8u * k, bd + 2 * k, idesc0, acc);
@@ -854,14 +858,18 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         };
         const bool two = kPair ? it.P == 3 : it.ntot > n0;
         for (int pass = 0; pass < it.npass && ok; ++pass) {
-          if (fills > 0) {  // the epilogue has read the previous fill
-            if (!mbar_wait(acc_empty, (fills - 1) & 1u, p.err, 13)) { ok = false; break; }
+          // accumulator buffer of this fill (two alternate when p.acc_buf > 0) and its use count
+          const uint32_t b = p.acc_buf ? (fills & 1u) : 0u;
+          const uint32_t use = p.acc_buf ? (fills >> 1) : fills;
+          dbase = b * p.acc_buf;
+          if (use > 0) {  // the epilogue has read this buffer's previous fill
+            if (!mbar_wait(&acc_empty[b], (use - 1) & 1u, p.err, 13)) { ok = false; break; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           }
           if (!(two ? stages(std::true_type{}) : stages(std::false_type{}))) ok = false;
           if (ok) {
-            if constexpr (kPair) mma_commit_pair(acc_full);
-            else mma_commit(acc_full);
+            if constexpr (kPair) mma_commit_pair(&acc_full[b]);
+            else mma_commit(&acc_full[b]);
           }
           ++fills;
         }
@@ -922,8 +930,11 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         }
         if (!ok) break;
         // ------------------------------------------------------------ epilogue of this pass
-        if (!warp_wait(acc_full, fills & 1u, p.err, 17)) { ok = false; break; }
+        const uint32_t b = p.acc_buf ? (fills & 1u) : 0u;
+        const uint32_t use = p.acc_buf ? (fills >> 1) : fills;
+        if (!warp_wait(&acc_full[b], use & 1u, p.err, 17)) { ok = false; break; }
         ++fills;
+        const uint32_t acc_base = tmem + lane_base + b * p.acc_buf;  // this fill's buffer, this warp's lanes
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int t_pass = t_begin + pass * T;
         // Outputs go through the group's staging buffer to bulk tensor stores: the epilogue
@@ -947,7 +958,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
             // one plane, one accumulator: the sum is one fp32 value and the scale a power of two,
             // so the fp32 product is the rounding of the exact (fp64) product
             uint32_t v[16];
-            tmem_ld16(tmem + lane_base + static_cast<uint32_t>(tc), v);
+            tmem_ld16(acc_base + static_cast<uint32_t>(tc), v);
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             const float4* sc4 = reinterpret_cast<const float4*>(p.scale_inv + t_pass + tc);
 #pragma unroll
@@ -968,7 +979,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
             for (int pl = 0; pl < PA; ++pl) {
               for (int jj = 0; jj < nacc; ++jj) {
                 uint32_t v[16];
-                tmem_ld16(tmem + lane_base + static_cast<uint32_t>(jj * acols + pl * T + tc), v);
+                tmem_ld16(acc_base + static_cast<uint32_t>(jj * acols + pl * T + tc), v);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
                 for (int e = 0; e < 16; ++e) y[e] += static_cast<double>(__uint_as_float(v[e]));
@@ -1076,8 +1087,8 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
         if (lane == 0) {
-          if constexpr (kPair) mbar_arrive_cluster(cluster_addr(acc_empty, 0));
-          else mbar_arrive(acc_empty);
+          if constexpr (kPair) mbar_arrive_cluster(cluster_addr(&acc_empty[b], 0));
+          else mbar_arrive(&acc_empty[b]);
         }
       }
     }
@@ -1326,6 +1337,7 @@ struct TmPlan {
   int pblk_bytes;                                      // per-token-block plane counts (shared memory)
   int sx, sw;
   uint32_t x_bytes, w_bytes, a_col;
+  uint32_t acc_buf;  // columns of one accumulator buffer when there are two, else 0
   size_t smem;
   size_t planes_bytes, scale_bytes, pcnt_bytes, partial_bytes;
 };
@@ -1370,13 +1382,21 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_
   const int m16 = static_cast<int>(round_up(M, 16));
   // pair MMAs take N in multiples of 32 (16 x rows in each CTA)
   const int mb = pl.pair ? static_cast<int>(round_up(M, 32)) : m16;
+  // Two accumulator buffers, so that the epilogue of one fill overlaps the MMAs of the next,
+  // when WELVET_B200_GEMM_DBUF = columns per buffer (64..192, single CTAs; tuning): token
+  // blocks and passes are then sized so that a fill takes at most that many columns, and two
+  // buffers leave 128 TMEM columns for 4 A stages.
+  int bw = 0;
+  if (const char* e = std::getenv("WELVET_B200_GEMM_DBUF")) bw = std::atoi(e) & ~15;
+  if (pl.pair || bw < 64 || bw > 192) bw = 0;
   pl.TB = mb < 256 ? mb : 256;
+  if (bw && pl.TB > bw) pl.TB = bw;
   pl.acc_cols = 0;
   int xrows = 0;
   for (int P = 1; P <= 3; ++P) {
     // pairs: 256, 128, 128 tokens (3 planes: planes 1 and 2 share an accumulator); otherwise
-    // up to two MMAs of 384 accumulator columns (384, 192, 128)
-    const int cap = pl.pair ? (P == 1 ? 256 : 128) : (kTmAccMax / P) & ~15;
+    // up to two MMAs of 384 accumulator columns (384, 192, 128), or one buffer's columns
+    const int cap = pl.pair ? (P == 1 ? 256 : 128) : (bw ? (bw / P) & ~15 : (kTmAccMax / P) & ~15);
     int T = pl.TB < cap ? pl.TB : cap;
     if (T < pl.TB) {  // passes of equal size (256 tokens at 2 planes: 128 + 128, not 192 + 64)
       const int npass = (pl.TB + cap - 1) / cap;
@@ -1387,6 +1407,7 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_
     const int acols = (pl.pair && P == 3 ? 2 : P) * pl.tpass[P - 1];
     // independent accumulators so that short MMAs do not wait on each other's results
     pl.nacc[P - 1] = acols <= 64 ? 4 : (acols <= 128 ? 2 : 1);
+    while (bw && pl.nacc[P - 1] > 1 && pl.nacc[P - 1] * acols > bw) --pl.nacc[P - 1];
     if (P <= xsplit) {
       pl.acc_cols = std::max(pl.acc_cols, pl.nacc[P - 1] * acols);
       // pairs: a 3-plane stage puts plane 2 in a second slot
@@ -1399,7 +1420,8 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_
   pl.kbb = dt == DType::FP4 ? kBK / 2 : kBK;
   pl.x_bytes = static_cast<uint32_t>(round_up(static_cast<int64_t>(xrows) * (pl.pair ? 64 : 128), 1024));
   pl.w_bytes = static_cast<uint32_t>(kBM * pl.kbb);
-  pl.a_col = static_cast<uint32_t>(round_up(pl.acc_cols, 32));
+  pl.acc_buf = bw ? static_cast<uint32_t>(round_up(pl.acc_cols, 32)) : 0u;
+  pl.a_col = bw ? 2 * pl.acc_buf : static_cast<uint32_t>(round_up(pl.acc_cols, 32));
   // stages (an x slot + a TMEM A slot each): as many as TMEM allows (up to 8) while the raw W
   // ring keeps 64 KB (and at least 4 slots), but no fewer than 3; then the W ring takes the
   // rest (up to 32). Measured with 32 KB x slots (FP8, 16384^2 and the SwiGLU cell): 4 x
@@ -1680,7 +1702,7 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
   p.TB = pl.TB;
   for (int i = 0; i < 3; ++i) p.tpass[i] = pl.tpass[i];
   p.nkb_total = pl.nkb; p.kb_per_split = pl.kb_per_split; p.splits = pl.splits; p.kbb = pl.kbb;
-  p.x_bytes = pl.x_bytes; p.w_bytes = pl.w_bytes; p.a_col = pl.a_col;
+  p.x_bytes = pl.x_bytes; p.w_bytes = pl.w_bytes; p.a_col = pl.a_col; p.acc_buf = pl.acc_buf;
   p.sx = pl.sx; p.sw = pl.sw;
   for (int i = 0; i < 3; ++i) p.nacc[i] = pl.nacc[i];
   p.w_evict_first = (a.M + pl.TB - 1) / pl.TB == 1 ? 1 : 0;
