@@ -197,6 +197,15 @@ __device__ __forceinline__ float pair_value_inline(float gate_pre, float up) {
   return static_cast<float>(static_cast<double>(g) * static_cast<double>(up));
 }
 
+// The same product with SiLU in fp32 (expf, IEEE division): SiLU within a few ulp of the
+// fp64 form; the product rounds as the reference's (the fp64 product of two floats is exact,
+// so its rounding to float is the fp32 product). For x below -88, expf(-x) overflows and the
+// SiLU is -0 where the fp64 form gives a float of magnitude below 1e-37.
+__device__ __forceinline__ float pair_value_f32(float gate_pre, float up) {
+  const float g = gate_pre / (1.0f + expf(-gate_pre));
+  return g * up;
+}
+
 
 template <typename Params>
 __device__ __forceinline__ void write_out(const Params& p, int t, int o, double y) {
@@ -405,6 +414,7 @@ struct TmParams {
   double* partial;             // [splits][M][rows] when splits > 1
   int* err;
   int pair;                    // SwiGLU Gate/Up pair: rows 2i / 2i+1, epilogue writes h
+  int silu_exact;              // pair: SiLU in fp64 as the reference (else fp32, a few ulp)
   float w_scale2;              // Up's Int8 scale (pair mode)
   float* h;
   int64_t ld_h;
@@ -1027,7 +1037,9 @@ __global__ void __launch_bounds__(kTmThreads, 1)
               const int e = (up_lane ? 8 : 0) + k;
               const int t = t_pass + tc + e;
               const bool valid = t < t_begin + t_count && o < p.rows;
-              const float h = pair_value_inline(up_lane ? uf[8 + k] : pf[k], up_lane ? pf[8 + k] : uf[k]);
+              const float gv = up_lane ? uf[8 + k] : pf[k];
+              const float uv = up_lane ? pf[8 + k] : uf[k];
+              const float h = p.silu_exact ? pair_value_inline(gv, uv) : pair_value_f32(gv, uv);
               if (staged) s1[e * 64 + (r >> 1)] = h;
               else if (valid) p.h[static_cast<int64_t>(t) * p.ld_h + (o >> 1)] = h;
             }
@@ -1482,6 +1494,13 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_
   return pl;
 }
 
+// SwiGLU pair epilogue: SiLU in fp64 exactly as the reference when WELVET_B200_SILU=fp64,
+// else in fp32.
+bool silu_exact() {
+  const char* e = std::getenv("WELVET_B200_SILU");
+  return e && std::strcmp(e, "fp64") == 0;
+}
+
 // Which batched kernel runs: A in TMEM (default) or A in shared memory
 // (WELVET_B200_GEMM=smem, kept for comparison).
 bool gemm_a_in_smem() {
@@ -1711,6 +1730,7 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
   p.bias = a.bias; p.bias_len = a.bias_len; p.act = a.act;
   p.partial = partial; p.err = a.err;
   p.pair = a.pair ? 1 : 0; p.w_scale2 = a.scale2; p.h = a.h; p.ld_h = a.ld_h;
+  p.silu_exact = silu_exact() ? 1 : 0;
   p.tiles_t = pl.tiles_t; p.tail_first = pl.tail_first; p.tail_s = pl.tail_s; p.tail_kbps = pl.tail_kbps;
   p.tiles = pl.tiles;
   p.n_items = pl.tail_first >= 0 ? pl.tail_first + (pl.tiles - pl.tail_first) * pl.tail_s : pl.tiles * pl.splits;
