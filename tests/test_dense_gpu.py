@@ -493,17 +493,19 @@ def test_simt_gemv_still_correct(wb, oracle, dt, monkeypatch):
 @pytest.mark.parametrize("rows,d,inter", [(1, 256, 640), (3, 256, 640), (24, 256, 640), (300, 256, 640),
                                           (24, 2048, 96), (16, 256, 9600), (300, 256, 4864)])
 @pytest.mark.parametrize("dt", [16, 4, 9])
-@pytest.mark.parametrize("mode", ["single", "pair", "dbuf"])
+@pytest.mark.parametrize("mode", ["single", "pair", "dbuf", "silu64"])
 def test_swiglu_tensor_paths(wb, oracle, dt, rows, d, inter, mode, monkeypatch):
     """1..4 rows: Gate and Up fused in the tensor GEMV; more: one tcgen05 GEMM over the
     interleaved Gate/Up pair mirror writing h in its epilogue (300 rows: several token
     blocks; d = 2048 with a narrow intermediate: split-K with the paired reduce; 9600: 150
     pair tiles, the last two cut along K and reduced by the tail launch; 300 x 4864: 76
     pair tiles per token block, with a tail). "pair": the GEMMs on CTA pairs where they qualify
-    (300 rows); "dbuf": two accumulator buffers of 128 columns."""
+    (300 rows); "dbuf": two accumulator buffers of 128 columns; "silu64": the GEMM epilogue's
+    SiLU in fp64 as the reference (default fp32)."""
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
     monkeypatch.setenv("WELVET_B200_GEMM_PAIR", "1" if mode == "pair" else "0")
     monkeypatch.setenv("WELVET_B200_GEMM_DBUF", "128" if mode == "dbuf" else "0")
+    monkeypatch.setenv("WELVET_B200_SILU", "fp64" if mode == "silu64" else "fp32")
     rng = np.random.default_rng(20 + rows)
     G, U, D = [(rng.standard_normal(s) * 0.5).astype(np.float32) for s in ((inter, d), (inter, d), (d, inter))]
     x = rng.standard_normal((rows, d)).astype(np.float32)
