@@ -123,6 +123,7 @@ Status swiglu_reserve(SwigluCell* c, int bs, cudaStream_t st) {
       WB_TRY(alloc_io(c->up, bs, &c->io_up, st));
     }
   }
+  c->io_down.max_tb = xsplit_policy() >= 2 ? 128 : 0;  // h: fp32 products, two x planes
   WB_TRY(alloc_io(c->down, bs, &c->io_down, st));
   c->bs = bs;
   return Status::Ok();
@@ -306,6 +307,7 @@ Status mha_reserve(MhaCell* c, int bs, cudaStream_t st) {
   WB_TRY(alloc_io(c->q, bs, &c->io_q, st));
   WB_TRY(alloc_io(c->k, bs, &c->io_k, st));
   WB_TRY(alloc_io(c->v, bs, &c->io_v, st));
+  c->io_o.max_tb = xsplit_policy() >= 2 ? 128 : 0;  // attention output: fp32, two x planes
   WB_TRY(alloc_io(c->o, bs, &c->io_o, st));
   c->bs = bs;
   return Status::Ok();

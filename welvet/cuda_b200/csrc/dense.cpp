@@ -234,7 +234,7 @@ Status alloc_io(const DeviceDense& d, int batch, DenseIO* io, cudaStream_t st) {
   WB_CUDA(cudaMalloc(&io->err, sizeof(int)));
   WB_CUDA(cudaMemsetAsync(io->err, 0, sizeof(int), st));
   if (use_tensor_path(d, batch)) {
-    io->scratch_bytes = gemm_scratch_bytes(batch, d.cols, d.rows, xsplit_policy());
+    io->scratch_bytes = gemm_scratch_bytes(batch, d.cols, d.rows, xsplit_policy(), true, io->max_tb);
     WB_CUDA(cudaMalloc(&io->scratch, io->scratch_bytes));
   }
   if (use_gemv_tc(d, batch)) {
@@ -268,6 +268,7 @@ Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x
     g.bias_len = d.bias_len;
     g.act = d.act;
     g.xsplit = xsplit_policy();
+    g.max_tb = io->max_tb;
     g.scratch = io->scratch;
     g.scratch_bytes = io->scratch_bytes;
     g.err = io->err;

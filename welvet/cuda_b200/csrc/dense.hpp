@@ -86,6 +86,10 @@ struct DenseIO {
   size_t scratch_bytes = 0;
   int* err = nullptr;     // device error word of the tensor-core path
   void* prep = nullptr;   // gemv_group_prep_bytes: x prepared once per grouped launch (batch <= 4)
+  // Tokens per GEMM token block at most (0: the plan's own), set before alloc_io by a caller
+  // whose activations are fp32 results (two x planes): blocks of 128 make one pass each, so
+  // more tiles fill the GPU without split-K.
+  int max_tb = 0;
   void release();
 };
 

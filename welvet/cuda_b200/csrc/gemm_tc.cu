@@ -1387,7 +1387,8 @@ bool tm_pair_wanted(int M, int rows) {
   return M >= 128 && ((rows + kBM - 1) / kBM) % 2 == 0;
 }
 
-TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_tail = true, bool allow_pair = true) {
+TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_tail = true, bool allow_pair = true,
+                    int max_tb = 0) {
   TmPlan pl{};
   pl.pair = allow_pair && tm_pair_wanted(M, rows);
   const int units = pl.pair ? 74 : 148;  // CTAs (CTA pairs) running at once on 148 SMs
@@ -1403,6 +1404,10 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_
   if (pl.pair || bw < 64 || bw > 192) bw = 0;
   pl.TB = mb < 256 ? mb : 256;
   if (bw && pl.TB > bw) pl.TB = bw;
+  // a caller's cap on tokens per block, and WELVET_B200_GEMM_TB (tuning)
+  int cap_tb = max_tb & ~31;
+  if (const char* e = std::getenv("WELVET_B200_GEMM_TB")) cap_tb = std::atoi(e) & ~31;
+  if (cap_tb >= 32 && cap_tb < pl.TB) pl.TB = cap_tb;
   pl.acc_cols = 0;
   int xrows = 0;
   for (int P = 1; P <= 3; ++P) {
@@ -1588,13 +1593,13 @@ int gemm_token_tile(int M, int xsplit) {
   return t;
 }
 
-size_t gemm_scratch_bytes(int M, int cols, int rows, int xsplit, bool tail) {
+size_t gemm_scratch_bytes(int M, int cols, int rows, int xsplit, bool tail, int max_tb) {
   size_t need = 0;
   for (DType dt : {DType::FP8E4M3, DType::FP4}) {
     const Plan pl = make_plan(M, cols, rows, xsplit, dt);
     need = std::max(need, pl.planes_bytes + pl.scale_bytes + pl.partial_bytes);
     for (bool pair : {true, false}) {  // CTA pairs, and single CTAs when no pair can run
-      const TmPlan tp = make_tm_plan(M, cols, rows, xsplit, dt, tail, pair);
+      const TmPlan tp = make_tm_plan(M, cols, rows, xsplit, dt, tail, pair, max_tb);
       need = std::max(need, tp.planes_bytes + tp.scale_bytes + tp.pcnt_bytes + tp.partial_bytes);
     }
   }
@@ -1679,18 +1684,18 @@ int tm_max_pairs(TmKernel kern, size_t smem) {
 Status launch_tm(const GemmArgs& a, cudaStream_t st) {
   if (!a.Wg || (reinterpret_cast<uintptr_t>(a.Wg) & 15) != 0)
     return Status::Internal("gemm_tc: the layer has no GEMM mirror (16-byte aligned)");
-  TmPlan pl = make_tm_plan(a.M, a.cols, a.rows, a.xsplit, a.dtype);
+  TmPlan pl = make_tm_plan(a.M, a.cols, a.rows, a.xsplit, a.dtype, true, true, a.max_tb);
   int pairs = 0;
   if (pl.pair) {
     const TmKernel k = tm_kernel(a.dtype, true);
     pairs = k ? tm_max_pairs(k, pl.smem) : 0;
-    if (pairs < 1) pl = make_tm_plan(a.M, a.cols, a.rows, a.xsplit, a.dtype, true, false);
+    if (pairs < 1) pl = make_tm_plan(a.M, a.cols, a.rows, a.xsplit, a.dtype, true, false, a.max_tb);
   }
   if (pl.sw < 2 || pl.sx < 2 || pl.a_col + 32u * pl.sx > kTmemCols)
     return Status::Internal("gemm_tc: pipeline does not fit on the SM");
   size_t need = pl.planes_bytes + pl.scale_bytes + pl.pcnt_bytes + pl.partial_bytes;
   if (pl.tail_first >= 0 && a.scratch_bytes < need) {  // no room for the tail partials
-    pl = make_tm_plan(a.M, a.cols, a.rows, a.xsplit, a.dtype, false, pl.pair);
+    pl = make_tm_plan(a.M, a.cols, a.rows, a.xsplit, a.dtype, false, pl.pair, a.max_tb);
     need = pl.planes_bytes + pl.scale_bytes + pl.pcnt_bytes + pl.partial_bytes;
   }
   if (!a.scratch || a.scratch_bytes < need) return Status::Internal("gemm_tc: scratch too small");
@@ -1914,7 +1919,7 @@ void* g_static_ptr[kMaxDevices] = {};
 size_t gemm_static_scratch_bytes() { return kStaticScratchBytes; }
 
 Status launch_gemm_tc_static(const GemmArgs& a_in, cudaStream_t st) {
-  const size_t need = gemm_scratch_bytes(a_in.M, a_in.cols, a_in.rows, a_in.xsplit, false);
+  const size_t need = gemm_scratch_bytes(a_in.M, a_in.cols, a_in.rows, a_in.xsplit, false, a_in.max_tb);
   if (need > kStaticScratchBytes)
     return Status::Invalid("allocation-free forward: needs " + std::to_string(need) +
                            " bytes of scratch, the static array holds " + std::to_string(kStaticScratchBytes) +

@@ -34,6 +34,7 @@ struct GemmArgs {
   // scratch (device): see gemm_scratch_bytes
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
+  int max_tb = 0;               // tokens per token block at most (0: the plan's own; k_gemm_tm)
   int* err = nullptr;           // device error word (0 = ok), may be nullptr
   // SwiGLU Gate/Up pair (k_gemm_tm only): Wg is a pair mirror (rows 2i = Gate row i,
   // 2i+1 = Up row i, rows = 2 x intermediate) and the epilogue writes
@@ -50,7 +51,7 @@ int gemm_token_tile(int M, int xsplit);
 // Bytes of scratch a launch with these sizes needs (planes, per-token scales, split-K partials;
 // with `tail`, room for the K slices of a last partial wave's tiles, which the launch uses
 // when the scratch it is given holds them).
-size_t gemm_scratch_bytes(int M, int cols, int rows, int xsplit, bool tail = true);
+size_t gemm_scratch_bytes(int M, int cols, int rows, int xsplit, bool tail = true, int max_tb = 0);
 
 bool gemm_supported(DType dt);
 
