@@ -995,13 +995,28 @@ __global__ void __launch_bounds__(kTmThreads, 1)
                 for (int e = 0; e < 16; ++e) y[e] += static_cast<double>(__uint_as_float(v[e]));
               }
             }
+            // the chunk's 16 scales up front: loaded inside the loop they would wait behind the
+            // partial stores (which the compiler cannot prove do not alias them), one L2
+            // round trip per output
+            float scv[16];
+            {
+              const float4* sc4 = reinterpret_cast<const float4*>(p.scale_inv + t_pass + tc);
+#pragma unroll
+              for (int e4 = 0; e4 < 4; ++e4) {
+                const float4 sc = __ldg(sc4 + e4);  // scale_inv holds Mp (multiple of 16) entries
+                scv[4 * e4] = sc.x;
+                scv[4 * e4 + 1] = sc.y;
+                scv[4 * e4 + 2] = sc.z;
+                scv[4 * e4 + 3] = sc.w;
+              }
+            }
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
               const int t = t_pass + tc + e;
               const bool valid = t < t_begin + t_count && o < p.rows;
               double yy = 0.0;
               if (valid) {
-                yy = y[e] * static_cast<double>(p.scale_inv[t]);
+                yy = y[e] * static_cast<double>(scv[e]);
                 if (kDt == 9) yy *= static_cast<double>((p.pair && (o & 1)) ? p.w_scale2 : p.w_scale);
               }
               if (tail) {
