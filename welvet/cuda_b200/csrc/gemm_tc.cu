@@ -964,23 +964,32 @@ __global__ void __launch_bounds__(kTmThreads, 1)
           // phase 1 (unrolled, cheap): each sum scaled, then kept as the float the reference
           // rounds it to (pre = float(y); Gate and Up are floats before the product)
           float pf[16], uf[16];
+          // The chunk's 16 per-token scales, requested before the TMEM reads so that the two
+          // latencies overlap (after a tcgen05.wait the loads could not move up; inside the
+          // fp64 loop each would wait behind the partial stores). scale_inv holds Mp (a
+          // multiple of 16) entries.
+          float scv[16];
+          {
+            const float4* sc4 = reinterpret_cast<const float4*>(p.scale_inv + t_pass + tc);
+#pragma unroll
+            for (int e4 = 0; e4 < 4; ++e4) {
+              const float4 sc = __ldg(sc4 + e4);
+              scv[4 * e4] = sc.x;
+              scv[4 * e4 + 1] = sc.y;
+              scv[4 * e4 + 2] = sc.z;
+              scv[4 * e4 + 3] = sc.w;
+            }
+          }
           if (f32_sums) {
             // one plane, one accumulator: the sum is one fp32 value and the scale a power of two,
             // so the fp32 product is the rounding of the exact (fp64) product
             uint32_t v[16];
             tmem_ld16(acc_base + static_cast<uint32_t>(tc), v);
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            const float4* sc4 = reinterpret_cast<const float4*>(p.scale_inv + t_pass + tc);
 #pragma unroll
-            for (int e4 = 0; e4 < 4; ++e4) {
-              const float4 sc = __ldg(sc4 + e4);  // scale_inv holds Mp (multiple of 16) entries
-              const float scv[4] = {sc.x, sc.y, sc.z, sc.w};
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const int e = 4 * e4 + j;
-                const bool valid = t_pass + tc + e < t_begin + t_count && o < p.rows;
-                pf[e] = valid ? __uint_as_float(v[e]) * scv[j] : 0.0f;
-              }
+            for (int e = 0; e < 16; ++e) {
+              const bool valid = t_pass + tc + e < t_begin + t_count && o < p.rows;
+              pf[e] = valid ? __uint_as_float(v[e]) * scv[e] : 0.0f;
             }
           } else {
             double y[16];
@@ -993,21 +1002,6 @@ __global__ void __launch_bounds__(kTmThreads, 1)
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
                 for (int e = 0; e < 16; ++e) y[e] += static_cast<double>(__uint_as_float(v[e]));
-              }
-            }
-            // the chunk's 16 scales up front: loaded inside the loop they would wait behind the
-            // partial stores (which the compiler cannot prove do not alias them), one L2
-            // round trip per output
-            float scv[16];
-            {
-              const float4* sc4 = reinterpret_cast<const float4*>(p.scale_inv + t_pass + tc);
-#pragma unroll
-              for (int e4 = 0; e4 < 4; ++e4) {
-                const float4 sc = __ldg(sc4 + e4);  // scale_inv holds Mp (multiple of 16) entries
-                scv[4 * e4] = sc.x;
-                scv[4 * e4 + 1] = sc.y;
-                scv[4 * e4 + 2] = sc.z;
-                scv[4 * e4 + 3] = sc.w;
               }
             }
 #pragma unroll
