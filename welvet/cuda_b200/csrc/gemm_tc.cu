@@ -909,6 +909,16 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       // Epilogue sums that are single fp32 values (one plane, one accumulator, no Int8 scale,
       // no partials) are scaled in fp32; others are summed and scaled in fp64.
       const bool f32_sums = P == 1 && nacc == 1 && kDt != 9 && !part;
+      // Tail slices whose sums are single fp32 values keep them raw in fp32 (half the bytes of
+      // the fp64 partials, in the first half of the tile's region); k_tail_reduce applies the
+      // scales, as the fp64 path does here, and reads which form a tile has from its flag.
+      const int tail_k = kPair ? 2 * tail_idx + static_cast<int>(v) : tail_idx;  // 128-row tail part
+      const bool raw32 = tail && PA == 1 && nacc == 1;
+      if (tail && q == 0 && lane == 0 && grp == 0) {
+        int* flags = reinterpret_cast<int*>(p.partial + static_cast<int64_t>(p.tiles - p.tail_first) *
+                                                            (kPair ? 2 : 1) * p.tail_s * p.TB * 128);
+        flags[tail_k] = raw32 ? 1 : 0;
+      }
       const bool two = kPair && P == 3;  // pairs, 3 planes: a stage takes two ring slots
       for (int pass = 0; pass < npass && ok; ++pass) {
         for (int i = 0; i < it.nkb; ++i, ++stage_idx, w.step(Sw)) {
@@ -1014,9 +1024,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
                 if (kDt == 9) yy *= static_cast<double>((p.pair && (o & 1)) ? p.w_scale2 : p.w_scale);
               }
               if (tail) {
-                if (valid)
-                  p.partial[((static_cast<int64_t>(kPair ? 2 * tail_idx + static_cast<int>(v) : tail_idx) * p.tail_s +
-                              split) * p.TB + (t - t_begin)) * 128 + r] = yy;
+                const int64_t base = static_cast<int64_t>(tail_k) * p.tail_s * p.TB * 128;
+                const int64_t at = (static_cast<int64_t>(split) * p.TB + (t - t_begin)) * 128 + r;
+                if (valid && raw32) reinterpret_cast<float*>(p.partial)[2 * base + at] = static_cast<float>(y[e]);
+                else if (valid) p.partial[base + at] = yy;
               } else if (p.splits > 1) {
                 if (valid) p.partial[(static_cast<int64_t>(split) * p.M + t) * p.rows + o] = yy;
               }
@@ -1163,6 +1174,9 @@ __global__ void k_splitk_reduce(const KParams p) {
 struct TailParams {
   int rows, M, TB, tiles_t, tail_first, tail_s, ntail;
   int sub;                     // 128-row parts per tile: 2 for CTA-pair tiles, else 1
+  const float* scale_inv;      // per-token 2^-e (parts kept raw in fp32)
+  int int8;                    // Int8 weights: w_scale (Up rows of a pair: w_scale2) as well
+  float w_scale, w_scale2;
   const double* partial;
   float* pre;
   float* post;
@@ -1187,12 +1201,30 @@ __global__ void k_tail_reduce(const TailParams p) {
     const int r = p.pair ? 2 * (rem % 64) : rem % 128;
     const int o = ((tile / p.tiles_t) * p.sub + k % p.sub) * 128 + r;
     if (t >= p.M || o >= p.rows) continue;
-    const double* base = p.partial + (static_cast<int64_t>(k) * p.tail_s * p.TB + (t % p.TB)) * 128 + r;
+    const int64_t region = static_cast<int64_t>(k) * p.tail_s * p.TB * 128;  // this part's partials
+    const int64_t at = static_cast<int64_t>(t % p.TB) * 128 + r;
     const int64_t stride = static_cast<int64_t>(p.TB) * 128;
+    const int* flags = reinterpret_cast<const int*>(p.partial + static_cast<int64_t>(p.ntail) * p.sub * p.tail_s * stride);
     double y = 0.0, y2 = 0.0;
-    for (int sp = 0; sp < p.tail_s; ++sp) {
-      y += base[sp * stride];
-      if (p.pair) y2 += base[sp * stride + 1];
+    if (flags[k]) {  // raw fp32 sums: scaled here as the GEMM's fp64 path scales them
+      const float* base = reinterpret_cast<const float*>(p.partial) + 2 * region + at;
+      const double sc = static_cast<double>(p.scale_inv[t]);
+      for (int sp = 0; sp < p.tail_s; ++sp) {
+        double a = static_cast<double>(base[sp * stride]) * sc;
+        if (p.int8) a *= static_cast<double>((p.pair && (o & 1)) ? p.w_scale2 : p.w_scale);
+        y += a;
+        if (p.pair) {
+          double b = static_cast<double>(base[sp * stride + 1]) * sc;
+          if (p.int8) b *= static_cast<double>(p.w_scale2);
+          y2 += b;
+        }
+      }
+    } else {
+      const double* base = p.partial + region + at;
+      for (int sp = 0; sp < p.tail_s; ++sp) {
+        y += base[sp * stride];
+        if (p.pair) y2 += base[sp * stride + 1];
+      }
     }
     if (p.pair) write_pair(p, t, o >> 1, y, y2);
     else write_out(p, t, o, y);
@@ -1502,7 +1534,9 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_
       pl.tail_kbps = (pl.nkb + s - 1) / s;
       pl.tail_s = (pl.nkb + pl.tail_kbps - 1) / pl.tail_kbps;  // every slice non-empty
       pl.tail_first = tiles - ntail;
-      pl.partial_bytes = static_cast<size_t>(ntail) * sub * pl.tail_s * pl.TB * 128 * 8;
+      // fp64 (or raw fp32) partials, then one flag per 128-row part
+      pl.partial_bytes = static_cast<size_t>(ntail) * sub * pl.tail_s * pl.TB * 128 * 8 +
+                         static_cast<size_t>(round_up(static_cast<int64_t>(ntail) * sub * 4, 16));
     }
   }
   return pl;
@@ -1804,6 +1838,7 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
     TailParams r{};
     r.rows = a.rows; r.M = a.M; r.TB = pl.TB; r.tiles_t = pl.tiles_t; r.tail_first = pl.tail_first;
     r.tail_s = pl.tail_s; r.ntail = ntail; r.sub = pl.pair ? 2 : 1; r.partial = partial;
+    r.scale_inv = scale_inv; r.int8 = a.dtype == DType::Int8 ? 1 : 0; r.w_scale = a.scale; r.w_scale2 = a.scale2;
     r.pre = a.pre; r.post = a.post; r.ld_out = a.ld_out; r.bias = a.bias; r.bias_len = a.bias_len; r.act = a.act;
     r.pair = a.pair ? 1 : 0; r.h = a.h; r.ld_h = a.ld_h;
     const int64_t n = static_cast<int64_t>(ntail) * r.sub * pl.TB * (a.pair ? 64 : 128);
