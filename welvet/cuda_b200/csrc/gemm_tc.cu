@@ -1,6 +1,6 @@
 // gemm_tc.cu -- batched dequant GEMM on sm_100a tensor cores (tcgen05.mma kind::f16, TMEM).
 //
-// Replaces, for batches above 4 tokens, the reference's per-output fp64 loop
+// Replaces, for batches above 8 tokens (SwiGLU cells: above 4), the reference's per-output fp64 loop
 // (src/cuda/kernels.cu:130-145) over a host-decoded fp64 W. Two kernels:
 //
 //   k_gemm_tm (default)  the dequantised weight tile is the MMA's A operand in TMEM: converter
@@ -12,8 +12,9 @@
 //   k_gemm_tc            the same GEMM with A in shared memory (WELVET_B200_GEMM=smem), kept
 //                        for comparison.
 //
-// x is split per token into f16 planes after a power-of-two scale (x * 2^e = p0 + p1 + p2,
-// k_split_x); the planes ride in the N dimension of one MMA. FP8/FP4/Int8 codes are exact in
+// x is split per token into f16 planes after a power-of-two scale (x * 2^e = p0 + p1 [+ p2],
+// k_split_x; two planes by default, three on request, one for a token whose values are exact
+// in f16); the planes ride in the N dimension of the MMAs. FP8/FP4/Int8 codes are exact in
 // f16, so every product is exact and the tensor core accumulates in fp32; planes are
 // combined in fp64 in the epilogue, which then applies the per-token 2^-e, the Int8 scale,
 // and bias / activation exactly as the reference's dense_bias_act (kernels.cu:147-161).
