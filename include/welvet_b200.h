@@ -69,6 +69,19 @@ WELVET_API welvet_status welvet_b200_dense_execute_device_noalloc(welvet_dense_s
                                                                   const float* x_dev, float* pre_dev,
                                                                   float* post_dev, void* stream);
 
+/* No counterpart in the reference. The launch plan of the batched tensor-core GEMM (the TMEM
+ * kernel) for a layer of `rows` outputs x `cols` inputs at M tokens, with at most `xsplit`
+ * f16 planes of x and token blocks capped at `max_tb` (0: no cap), as the library plans it
+ * before a launch: host arithmetic only, no device call, for checks and tuning. The
+ * WELVET_B200_GEMM_* environment switches apply; a CTA-pair plan is reported as planned,
+ * before the launch asks the device whether pairs fit. out[0..n) receives, in this order:
+ * pair, TB, tpass[3], nacc[3], acc_cols, acc_buf, a_col, sx, sw, x_bytes, w_bytes, smem,
+ * nkb, splits, kb_per_split, tiles_t, tiles, tail_first, tail_s, tail_kbps, n_items. Returns
+ * the number of values in a plan (25) whatever n is, or -1 for a dtype the GEMM does not
+ * serve or a non-positive size. */
+WELVET_API int32_t welvet_b200_gemm_plan(int32_t M, int32_t cols, int32_t rows, int32_t xsplit, int32_t dtype,
+                                         int32_t max_tb, int64_t* out, int32_t n);
+
 /* The session's authoritative host store: dtype, rows (= out), cols (= in), scale and the
  * native bytes in the reference layout (FP4: low nibble = even flat index). Float32 stores
  * return their float payload. *native_len is always set; the bytes are copied when

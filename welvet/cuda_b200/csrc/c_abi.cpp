@@ -7,6 +7,7 @@
 #include "cells.hpp"
 #include "codec.hpp"
 #include "dense.hpp"
+#include "gemm_tc.hpp"
 #include "model.hpp"
 
 #include <cstdio>
@@ -260,6 +261,14 @@ welvet_status welvet_b200_dense_execute_device_noalloc(welvet_dense_session* ses
     if (!sess) return wb::Status::Invalid("null execute args");
     return wb::session_execute_device_noalloc(sess->s, x_dev, pre_dev, post_dev, static_cast<cudaStream_t>(stream));
   });
+}
+
+int32_t welvet_b200_gemm_plan(int32_t M, int32_t cols, int32_t rows, int32_t xsplit, int32_t dtype,
+                              int32_t max_tb, int64_t* out, int32_t n) {
+  const wb::DType dt = static_cast<wb::DType>(dtype);
+  if (M <= 0 || cols <= 0 || rows <= 0 || xsplit < 1 || xsplit > 3 || !wb::gemm_supported(dt)) return -1;
+  if (n > 0 && !out) return -1;
+  return wb::gemm_plan_values(M, cols, rows, xsplit, dt, max_tb, out, n < 0 ? 0 : n);
 }
 
 void welvet_dense_release(welvet_dense_session* sess) {

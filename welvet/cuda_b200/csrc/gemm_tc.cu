@@ -1637,6 +1637,20 @@ int gemm_token_tile(int M, int xsplit) {
   return t;
 }
 
+int gemm_plan_values(int M, int cols, int rows, int xsplit, DType dt, int max_tb, int64_t* out, int n) {
+  const TmPlan pl = make_tm_plan(M, cols, rows, xsplit, dt, true, true, max_tb);
+  const int64_t n_items = pl.tail_first >= 0
+                              ? pl.tail_first + static_cast<int64_t>(pl.tiles - pl.tail_first) * pl.tail_s
+                              : static_cast<int64_t>(pl.tiles) * pl.splits;
+  const int64_t v[] = {pl.pair ? 1 : 0, pl.TB, pl.tpass[0], pl.tpass[1], pl.tpass[2], pl.nacc[0], pl.nacc[1],
+                       pl.nacc[2], pl.acc_cols, pl.acc_buf, pl.a_col, pl.sx, pl.sw, pl.x_bytes, pl.w_bytes,
+                       static_cast<int64_t>(pl.smem), pl.nkb, pl.splits, pl.kb_per_split, pl.tiles_t, pl.tiles,
+                       pl.tail_first, pl.tail_s, pl.tail_kbps, n_items};
+  const int cnt = static_cast<int>(sizeof(v) / sizeof(v[0]));
+  for (int i = 0; i < cnt && i < n; ++i) out[i] = v[i];
+  return cnt;
+}
+
 size_t gemm_scratch_bytes(int M, int cols, int rows, int xsplit, bool tail, int max_tb) {
   size_t need = 0;
   for (DType dt : {DType::FP8E4M3, DType::FP4}) {

@@ -53,6 +53,10 @@ int gemm_token_tile(int M, int xsplit);
 // when the scratch it is given holds them).
 size_t gemm_scratch_bytes(int M, int cols, int rows, int xsplit, bool tail = true, int max_tb = 0);
 
+// The TMEM kernel's launch plan as numbers (see welvet_b200_gemm_plan): writes the first n of
+// them to out and returns how many there are.
+int gemm_plan_values(int M, int cols, int rows, int xsplit, DType dt, int max_tb, int64_t* out, int n);
+
 bool gemm_supported(DType dt);
 
 // The GEMM mirror: the row-major mirror cut into tiles of 128 rows x 64 k, each stored as one
