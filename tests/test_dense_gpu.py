@@ -372,6 +372,56 @@ def test_dense_vs_reference_cuda_kernel(wb, oracle):
         check_dense(pre, post, (pre_r, post_r, ref[2], ref[3]), 2, f"vs reference dt={dt}")
 
 
+def test_reference_cuda_kernel_timing(wb, oracle):
+    """BASELINE config 2's layer (4096 -> 4096 FP4, batch 1) through the reference's own CUDA
+    Dense session (its kernel rebuilt for sm_100a) and through welvet_dense_execute, both
+    mounted from the same float32 weights and called with the same pageable host buffers,
+    synchronous per call as the reference ABI is: the outputs agree within the GEMV bound,
+    and the time per call of each is printed (the reference baseline that runs on the GPU;
+    weight GB/s counts the packed FP4 bytes, 8 MiB)."""
+    import ctypes
+    import time
+    R = oracle.ref()
+    rows = cols = 4096
+    dt = oracle.FP4
+    rng = np.random.default_rng(5)
+    w = rng.standard_normal((rows, cols)).astype(np.float32)
+    x = rng.standard_normal((1, cols)).astype(np.float32)
+    f = lambda a: a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    sess = ctypes.c_void_p()
+    msg = ctypes.create_string_buffer(256)
+    assert R.ref_dense_mount(1, cols, rows, -1, dt, f(w), None, 0, ctypes.byref(sess), msg, 256) == 0, msg.value
+    pre_r = np.zeros((1, rows), np.float32)
+    post_r = np.zeros((1, rows), np.float32)
+    for _ in range(3):
+        assert R.ref_dense_execute(sess, f(x), f(pre_r), f(post_r), msg, 256) == 0, msg.value
+    n_ref = 20
+    t0 = time.perf_counter()
+    for _ in range(n_ref):
+        R.ref_dense_execute(sess, f(x), f(pre_r), f(post_r), msg, 256)
+    t_ref = (time.perf_counter() - t0) / n_ref
+    R.ref_dense_release(sess)
+    ours = wb.DenseSession(w, 1, dt, -1)
+    pre = np.zeros((1, rows), np.float32)
+    post = np.zeros((1, rows), np.float32)
+    for _ in range(3):
+        ours.execute(x, pre, post)
+    n_ours = 200
+    t0 = time.perf_counter()
+    for _ in range(n_ours):
+        ours.execute(x, pre, post)
+    t_ours = (time.perf_counter() - t0) / n_ours
+    ours.release()
+    raw, sc = oracle.pack(dt, w)
+    ref = oracle.dense_forward(dt, raw, sc, x, cols, rows, -1)
+    check_dense(pre, post, ref, -1, "config-2 layer vs oracle")
+    assert np.array_equal(pre_r, ref[0])
+    gb = rows * cols / 2 / 1e9
+    print(f"config-2 layer, host buffers, per call: reference CUDA session {t_ref * 1e6:.1f} us "
+          f"({gb / t_ref:.1f} GB/s), welvet_dense_execute {t_ours * 1e6:.1f} us ({gb / t_ours:.1f} GB/s)")
+    assert t_ours < t_ref
+
+
 # ---------------------------------------------------------------- batched tensor-core path (tcgen05)
 
 GEMM_TOL = {"3": 2.0 ** -16, "2": 2.0 ** -15, "1": 2.0 ** -9}
