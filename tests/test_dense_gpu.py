@@ -422,6 +422,54 @@ def test_reference_cuda_kernel_timing(wb, oracle):
     assert t_ours < t_ref
 
 
+def test_reference_cuda_batched_timing(wb, oracle):
+    """The batched half of the baseline: one projection of BASELINE config 3 (Gate, 4096 ->
+    14336, E4M3) at M = 512 tokens through the reference's resident CUDA Dense session and
+    through welvet_dense_execute, same weights, same pageable host buffers (x in, pre and
+    post out every call, 66 MB over the bus, which bounds this library's time here).
+    Outputs agree with the oracle; the time per call of each is printed."""
+    import ctypes
+    import time
+    R = oracle.ref()
+    rows, cols, M = 14336, 4096, 512
+    dt = oracle.FP8E4M3
+    rng = np.random.default_rng(6)
+    w = (rng.standard_normal((rows, cols)) * 0.5).astype(np.float32)
+    x = rng.standard_normal((M, cols)).astype(np.float32)
+    f = lambda a: a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    sess = ctypes.c_void_p()
+    msg = ctypes.create_string_buffer(256)
+    assert R.ref_dense_mount(M, cols, rows, -1, dt, f(w), None, 0, ctypes.byref(sess), msg, 256) == 0, msg.value
+    pre_r = np.zeros((M, rows), np.float32)
+    post_r = np.zeros((M, rows), np.float32)
+    assert R.ref_dense_execute(sess, f(x), f(pre_r), f(post_r), msg, 256) == 0, msg.value
+    n_ref = 2
+    t0 = time.perf_counter()
+    for _ in range(n_ref):
+        R.ref_dense_execute(sess, f(x), f(pre_r), f(post_r), msg, 256)
+    t_ref = (time.perf_counter() - t0) / n_ref
+    R.ref_dense_release(sess)
+    ours = wb.DenseSession(w, M, dt, -1)
+    pre = np.zeros((M, rows), np.float32)
+    post = np.zeros((M, rows), np.float32)
+    ours.execute(x, pre, post)
+    n_ours = 5
+    t0 = time.perf_counter()
+    for _ in range(n_ours):
+        ours.execute(x, pre, post)
+    t_ours = (time.perf_counter() - t0) / n_ours
+    ours.release()
+    err = np.abs(pre.astype(np.float64) - pre_r.astype(np.float64)) - 2 * ulp(pre_r)
+    raw, sc = oracle.pack(dt, w[:64])
+    sub = oracle.dense_forward(dt, raw, sc, x, cols, 64, -1)  # first 64 rows: the oracle's Σ|W x|
+    assert np.array_equal(pre_r[:, :64], sub[0])
+    assert float(np.max(err[:, :64] / np.maximum(sub[3], 1e-300))) <= GEMM_TOL["2"]
+    tflop = 2.0 * M * rows * cols / 1e12
+    print(f"C3 Gate projection, M = {M}, host buffers, per call: reference CUDA session {t_ref * 1e3:.2f} ms "
+          f"({tflop / t_ref:.3f} TFLOP/s), welvet_dense_execute {t_ours * 1e3:.2f} ms ({tflop / t_ours:.2f} TFLOP/s)")
+    assert t_ours < t_ref
+
+
 # ---------------------------------------------------------------- batched tensor-core path (tcgen05)
 
 GEMM_TOL = {"3": 2.0 ** -16, "2": 2.0 ** -15, "1": 2.0 ** -9}
