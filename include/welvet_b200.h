@@ -56,18 +56,26 @@ WELVET_API welvet_status welvet_b200_dense_execute_group_device(welvet_dense_ses
 
 /* No counterpart in the reference. welvet_b200_dense_execute_device without any allocation,
  * for callers that cannot call cudaMalloc while they run a forward: a serving loop that must
- * not stall on an allocation (cudaMalloc can synchronize the device), code that runs while a
- * CUDA graph is being captured, or a framework that owns all device memory up front. It runs
+ * not stall on an allocation (cudaMalloc can synchronize the device), or a framework or
+ * plugin host that owns all device memory up front and forbids allocations afterwards. It runs
  * the batched tensor-core forward (a session of batch > 8, FP8/FP4/Int8, outside exact mode;
  * other sessions get status 2) with the scratch of that kernel -- x split into f16 planes,
  * per-token scales, split-K partials -- in one static 32 MiB device array that the library
  * holds on every GPU that loads it until the process exits; a call needing more returns
- * status 1. The first call on a device looks up the array's device address and should be
- * made before any stream capture. All calls share the array: calls whose kernels overlap on
- * one GPU (other streams or threads) race and must be serialized by the caller. */
+ * status 1. The first call on a device (and the first after that device's context was
+ * re-created) looks up the array's device address and should be made before any stream
+ * capture. All calls share the array: calls whose kernels overlap on one GPU (other streams
+ * or threads) race and must be serialized by the caller. A timed-out pipeline wait is
+ * recorded in the session's error word, which welvet_b200_dense_check_error reads. */
 WELVET_API welvet_status welvet_b200_dense_execute_device_noalloc(welvet_dense_session* sess,
                                                                   const float* x_dev, float* pre_dev,
                                                                   float* post_dev, void* stream);
+
+/* No counterpart in the reference (whose calls are all synchronous). Synchronizes `stream`
+ * and reports, then clears, a pipeline wait of the batched tensor-core kernel that timed out
+ * in an earlier asynchronous call on this session (execute_device, execute_device_noalloc):
+ * status 4 if one did, 0 otherwise. Copies 4 bytes to the host; allocates nothing. */
+WELVET_API welvet_status welvet_b200_dense_check_error(welvet_dense_session* sess, void* stream);
 
 /* No counterpart in the reference. The launch plan of the batched tensor-core GEMM (the TMEM
  * kernel) for a layer of `rows` outputs x `cols` inputs at M tokens, with at most `xsplit`

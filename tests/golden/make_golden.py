@@ -147,7 +147,7 @@ def main() -> None:
 
     # 5. the reference's exported C-ABI names (include/welvet_c.h), for the link-compatibility test
     import re
-    ref_root = os.environ.get("REF", "/root/reference")
+    ref_root = os.environ.get("REF", os.path.join(HERE, "..", "..", "..", "reference"))  # checkout beside the repo
     with open(os.path.join(ref_root, "include", "welvet_c.h")) as f:
         names = sorted(set(re.findall(r"\b(welvet_[a-z0-9_]+)\(", f.read())))
     with open(os.path.join(HERE, "reference_symbols.txt"), "w") as f:

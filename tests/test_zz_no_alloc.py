@@ -1,11 +1,12 @@
 """GPU: the allocation-free forward (welvet_b200_dense_execute_device_noalloc).
 
 It is for callers that may not allocate device memory while a forward runs -- a serving loop
-that must not stall on cudaMalloc, code running under stream capture, a framework that owns
-all device memory -- and keeps the batched tensor-core kernel's scratch in a static device
-array instead. Checked through the C ABI against the allocating entry point on the same
-session, two calls in a row (the second one reuses the array's leftover contents), and
-against the fp64 oracle. Runs alone in a fresh process or after the other tests.
+that must not stall on cudaMalloc, a framework or plugin host that owns all device memory --
+and keeps the batched tensor-core kernel's scratch in a static device array instead. Checked
+through the C ABI against the allocating entry point on the same session, two calls in a row
+(the second one reuses the array's leftover contents): both run the same kernel with the same
+launch plan, so the results must be identical bit for bit; the fp64 oracle checks both.
+Runs alone in a fresh process or after the other tests.
 """
 import numpy as np
 import pytest
@@ -35,18 +36,17 @@ def test_noalloc_matches_allocating_entry_point(wb, oracle, monkeypatch):
             post_b = torch.full((batch, out), float("nan"), device="cuda")
             s.execute_device(xd, pre_a, post_a)
             s.execute_device_noalloc(xd, pre_b, post_b)
-            torch.cuda.synchronize()
+            s.check_error()  # no pipeline wait timed out in either call
             pa, pb = pre_a.cpu().numpy(), pre_b.cpu().numpy()
+            assert np.array_equal(pb, pa), f"dt={dt} call={call}: pre differs from the allocating path"
+            assert np.array_equal(post_b.cpu().numpy(), post_a.cpu().numpy()), f"dt={dt} call={call}: post"
             pre_o, post_o, y64, sabs = oracle.dense_forward(dt, raw, sc, x, in_, out, wb.RELU, bias)
             bound = TOL_REL * sabs + 2 * np.spacing(np.abs(pre_o)).astype(np.float64)
             assert np.all(np.abs(pb.astype(np.float64) - pre_o) <= bound), f"dt={dt} call={call}"
-            assert np.all(np.abs(pb.astype(np.float64) - pa) <= bound), f"dt={dt} call={call}"
-            assert np.array_equal(post_b.cpu().numpy(), post_a.cpu().numpy()) or \
-                np.allclose(post_b.cpu().numpy(), post_a.cpu().numpy(), rtol=1e-6, atol=1e-6)
         s.release()
 
 
-def test_noalloc_rejects_what_it_cannot_serve(wb):
+def test_noalloc_rejects_what_it_cannot_serve(wb, monkeypatch):
     import torch
     s = wb.DenseSession(np.ones((8, 8), np.float32), 1, wb.FP4)  # batch 1: not the batched path
     x = torch.ones(1, 8, device="cuda")
@@ -55,8 +55,11 @@ def test_noalloc_rejects_what_it_cannot_serve(wb):
         s.execute_device_noalloc(x, y, y)
     assert e.value.code == wb.UNSUPPORTED
     s.release()
-    # a call whose scratch would exceed the static array is refused with status 1
-    batch, in_, out = 512, 16384, 1024
+    # A call whose scratch exceeds the static array is refused with status 1. With 1024 tokens
+    # of 16384 inputs the x planes alone take 32 MiB at one plane, so the call is too large
+    # for the 32 MiB array at every plane setting; the setting is pinned all the same.
+    monkeypatch.setenv("WELVET_B200_XSPLIT", "3")
+    batch, in_, out = 1024, 16384, 256
     w = torch.randn(out, in_, device="cuda") * 0.02
     big = wb.DenseSession(w, batch, wb.FP4)
     del w

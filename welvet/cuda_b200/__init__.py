@@ -78,6 +78,7 @@ _sig("welvet_b200_dense_mount_native", _ST, c_int32, c_int32, c_int32, c_int32, 
 _sig("welvet_dense_execute", _ST, c_void_p, c_void_p, c_void_p, c_void_p)
 _sig("welvet_b200_dense_execute_device", _ST, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p)
 _sig("welvet_b200_dense_execute_device_noalloc", _ST, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p)
+_sig("welvet_b200_dense_check_error", _ST, c_void_p, c_void_p)
 _sig("welvet_b200_dense_execute_group_device", _ST, POINTER(c_void_p), c_int32, POINTER(c_void_p),
      POINTER(c_void_p), POINTER(c_void_p), c_void_p)
 _sig("welvet_dense_release", None, c_void_p)
@@ -231,11 +232,16 @@ class DenseSession:
 
     def execute_device_noalloc(self, x, pre, post, stream=None) -> None:
         """execute_device for callers that cannot allocate device memory during a forward
-        (allocation-free serving loops, stream capture, frameworks owning all device memory):
+        (allocation-free serving loops, frameworks owning all device memory):
         batched sessions only, scratch in the library's static 32 MiB device array; calls
         that overlap on one GPU race on that array."""
         check(_L.welvet_b200_dense_execute_device_noalloc(self._h, c_void_p(_dev_ptr(x)), c_void_p(_dev_ptr(pre)),
                                                           c_void_p(_dev_ptr(post)), _stream_ptr(stream)))
+
+    def check_error(self, stream=None) -> None:
+        """Synchronizes `stream` and raises (code 4) if a tensor-core pipeline wait of an earlier
+        asynchronous call on this session timed out."""
+        check(_L.welvet_b200_dense_check_error(self._h, _stream_ptr(stream)))
 
     def store(self):
         """(dtype, rows, cols, scale, native bytes in the reference layout)."""

@@ -263,6 +263,14 @@ welvet_status welvet_b200_dense_execute_device_noalloc(welvet_dense_session* ses
   });
 }
 
+welvet_status welvet_b200_dense_check_error(welvet_dense_session* sess, void* stream) {
+  return guarded([&] {
+    if (!sess) return wb::Status::Invalid("null session");
+    WB_CUDA(cudaSetDevice(sess->s->device));
+    return wb::check_pipeline_error(sess->s->io, static_cast<cudaStream_t>(stream));
+  });
+}
+
 int32_t welvet_b200_gemm_plan(int32_t M, int32_t cols, int32_t rows, int32_t xsplit, int32_t dtype,
                               int32_t max_tb, int64_t* out, int32_t n) {
   const wb::DType dt = static_cast<wb::DType>(dtype);

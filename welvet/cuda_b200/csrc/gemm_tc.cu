@@ -1955,9 +1955,8 @@ Status launch_gemm_tc(const GemmArgs& a, cudaStream_t st) {
 // Allocation-free variant.
 //
 // Some callers cannot call cudaMalloc when they run a forward: a serving loop that must
-// never stall on an allocation (cudaMalloc can synchronize the device), code running while
-// a CUDA graph is being captured, or a framework that owns all device memory up front and
-// forbids other allocations once it runs. For them launch_gemm_tc_static runs the same
+// never stall on an allocation (cudaMalloc can synchronize the device), or a framework or
+// plugin host that owns all device memory up front and forbids other allocations once it runs. For them launch_gemm_tc_static runs the same
 // tcgen05 GEMM with its scratch (the f16 planes of x, the per-token scales and the split-K
 // partials) in one array that lives in this file for the life of the process.
 //
@@ -1972,7 +1971,25 @@ static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_static_mu;
+// Per device: the array's device address and the context it was looked up in. A device reset
+// (cudaDeviceReset) or a context re-created by the host application reloads the module and
+// moves the array, so the address is looked up again whenever the current context differs.
 void* g_static_ptr[kMaxDevices] = {};
+CUcontext g_static_ctx[kMaxDevices] = {};
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
 } // namespace
 
 size_t gemm_static_scratch_bytes() { return kStaticScratchBytes; }
@@ -1988,13 +2005,18 @@ Status launch_gemm_tc_static(const GemmArgs& a_in, cudaStream_t st) {
   if (dev < 0 || dev >= kMaxDevices) return Status::Internal("allocation-free forward: device index out of range");
   void* ptr = nullptr;
   {
-    // Once per device, with that device current: the array's device address. The host-side
-    // symbol is only a stand-in and must never reach a kernel.
+    // Once per device (and context), with that device current: the array's device address.
+    // The host-side symbol is only a stand-in and must never reach a kernel.
+    CUcontext ctx = nullptr;  // current since the session's mount ran on this device
+    auto get_ctx = ctx_get_current();
+    if (!get_ctx || get_ctx(&ctx) != CUDA_SUCCESS || !ctx)
+      return Status::Internal("allocation-free forward: no current CUDA context");
     std::lock_guard<std::mutex> lock(g_static_mu);
-    if (!g_static_ptr[dev]) {
+    if (!g_static_ptr[dev] || g_static_ctx[dev] != ctx) {
       void* p = nullptr;
       WB_CUDA(cudaGetSymbolAddress(&p, g_static_scratch));
       g_static_ptr[dev] = p;
+      g_static_ctx[dev] = ctx;
     }
     ptr = g_static_ptr[dev];
   }

@@ -80,7 +80,8 @@ Status launch_gemm_tc(const GemmArgs& a, cudaStream_t st);
 // The same launch with its scratch in a fixed static device array instead of a.scratch:
 // makes no allocation of any kind. Rejects (status 1) a launch whose scratch would exceed
 // gemm_static_scratch_bytes(). The first call on a device looks up the array's device
-// address and should come before any stream capture. Calls that overlap on one GPU race.
+// address (again after the device's context was re-created) and should come before any
+// stream capture. Calls that overlap on one GPU race.
 Status launch_gemm_tc_static(const GemmArgs& a, cudaStream_t st);
 size_t gemm_static_scratch_bytes();
 
