@@ -1,30 +1,35 @@
 #!/usr/bin/env python3
 """Benchmark of the quantized Dense forward path on B200.
 
-Metric: quant Dense weight GB/s (GEMV, % HBM). Workload at N=1: BASELINE
-config 2 -- Dense GEMV 4096->4096, batch 1, FP4 (E2M1, 2 codes/byte, reference layout),
-W ~ N(0, 0.02), x ~ N(0, 1), seed 1. One step = 64 independent forwards, one per
-distinct 4096x4096 FP4 weight set (the reference's --bench loop also repeats independent
-executes), so each step streams 512 MiB of packed weights -- more than the 126 MB L2, no
-flush needed. The same 64 layers run as a dependent chain are reported under "chain". Weights are random
-(synthetic; the reference ships no checkpoints).
+Metric: quant Dense weight GB/s (GEMV, % HBM) and TFLOP/s (batched, % tensor)
+at 1/2/4/8 B200. The configuration quoted "across 1/2/4/8 GPUs" is BASELINE config 5's
+column-sharded Dense 16384 -> 65536, FP4 (E2M1, 2 codes/byte, reference layout), W ~ N(0, 0.02),
+x ~ N(0, 1), seed 4: 512 MiB of packed weights, more than the 126 MB L2 (no flush needed).
 
-  value    weight GB/s with x/weights resident in HBM: the 64 forwards go out through
-           welvet_b200_dense_execute_group_device, i.e. the tensor-core GEMV kernel over
-           32 layers per launch (blockIdx.z = layer), two launches per step
-  e2e      the same metric through the reference-facing C ABI welvet_dense_execute, host
-           buffers (pinned), x in and pre/post out over the bus inside the timed region, one
-           synchronous call per layer
-  branches the same 64 forwards as 64 single-layer launches on 8 graph branches
-  chain    the same 64 layers as a dependent chain (layer i's post is layer i+1's x)
-  batched  the other half of the metric, TFLOP/s of the batched tcgen05 path: BASELINE
-           config 3's SwiGLU cell (d 4096, hidden 14336, FP8 E4M3, W ~ N(0, 0.02)) at
-           M = 512 tokens of N(0, 1) activations rounded to bf16, seed 2
-N > 1 (torchrun): every rank runs its own chain (independent layers, weak scaling, no
-collective on the data path); value = all ranks' bytes / max-over-ranks time.
+  value    weight GB/s of the whole job at batch 1: one step = one forward of the sharded layer
+           over all N GPUs (welvet_b200_sharded_dense_execute_device, fused gather: each rank's
+           GEMV stores its columns into every rank's output over NVLink, then a flag exchange),
+           every rank holding the whole output when the step ends. N = 1 runs the same call on
+           one GPU. Strong scaling (the layer is the same at every N).
+  batched  the same layer at batch 256, TFLOP/s (tcgen05 GEMM + fused gather)
+  e2e      the metric through the C ABI with host buffers (pinned): welvet_dense_execute at
+           N = 1 (the reference's own entry point), welvet_b200_sharded_dense_execute at N > 1;
+           x in and the whole output out over the bus every step
+  sharded  per N: fused, nccl (local forward + ncclAllGather + permute) and compute-only (the
+           shard as a one-GPU layer, no gather) at batch 1 and 256
+  volume   BASELINE config 5's volume (2x2x2 cells of 4 Dense 4096x4096 FP4 + ReLU, batch 64):
+           one GPU runs the whole chain; N GPUs the cell-per-GPU pipeline
+  configs  (N = 1) configs 1-4 at their sizes: C1 us, C2 FP4 / Int8 / E4M3 GB/s (grouped,
+           single launches, chain, host buffers; FP4 also on sigma = 2 weights, whose codes are
+           not all zero), C3 SwiGLU at M = 1 / 16 / 128 / 512, C4 RMSNorm + MHA + SwiGLU
+  reference_cuda  (N = 1) the reference's own CUDA Dense session (oracle/_ref: its kernels
+           rebuilt for sm_100a) on C1, C2 and C3's Gate projection, host buffers, per call
+  cpu_baseline    the oracle port (reference decode + sequential fp64 dot) on the box's host
+           cores, on a bounded row sample of the headline layer
 
 --impl reference times the reference semantics on the host cores (the oracle port of
-kernels.cu:130-161 with the reference decode), the only CPU implementation of this path.
+kernels.cu:130-161 with the reference decode): the reference ships no CPU matvec, and this
+is the CPU implementation of the path.
 """
 from __future__ import annotations
 
@@ -42,28 +47,34 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-IN = OUT = 4096
-LAYERS = 64
-DTYPE_FP4 = 16
+C5_IN, C5_OUT = 16384, 65536
+FP4, E4M3, E5M2, INT8 = 16, 4, 5, 9
 SIGMA = 0.02
-SEED = 1
-WEIGHT_BYTES_PER_LAYER = OUT * IN // 2  # FP4: 0.5 B / weight
+C5_BYTES = C5_OUT * C5_IN // 2  # FP4: 0.5 B / weight
+METRIC = "quant Dense weight GB/s (GEMV, % HBM) and TFLOP/s (batched, % tensor) at 1/2/4/8 B200"
+
+
+def config_for(world: int) -> dict:
+    return {"workload": "C5 column-sharded Dense 16384->65536 FP4 (W~N(0,0.02), x~N(0,1), seed 4), batch 1: "
+                        "one forward per step, output all-gathered on every rank",
+            "global_batch": 1, "seq_len": 1, "parallelism": f"column-sharded x{world} (fused NVLink gather)",
+            "l2": "inputs larger than L2 (512 MiB of packed weights per step)",
+            "weight_bytes_per_step": C5_BYTES}
 
 
 def peaks():
     try:
         return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))), "measured"
     except Exception:
-        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def traffic_from_profile():
-    """DRAM bytes of one grouped GEMV launch (32 layers) from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "gemv_tc_grouped_fp4_4096x4096_b1_32layers.md")
+def profile_value(name: str, key: str):
+    """A number from a committed ncu summary under profiles/ (a `key: value` line)."""
     try:
-        for ln in open(p):
-            if ln.startswith("dram_bytes_per_launch:"):
-                return int(ln.split(":")[1].strip())
+        for ln in open(os.path.join(ROOT, "profiles", name)):
+            if ln.startswith(key + ":"):
+                return float(ln.split(":")[1].split()[0])
     except Exception:
         pass
     return None
@@ -72,7 +83,7 @@ def traffic_from_profile():
 class ClockSampler:
     """SM clock and clock-event (throttle) reasons of one GPU, polled through NVML (the data
     nvidia-smi's clocks.sm / clocks_event_reasons.* report) every ~0.5 ms while the timed
-    region runs -- short timed regions still get samples. Read-only."""
+    legs run. Read-only."""
 
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
                "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
@@ -84,6 +95,7 @@ class ClockSampler:
         self.max_mhz = None
         self.err = None
         self._stop = threading.Event()
+        self.active = threading.Event()
 
     def __enter__(self):
         try:
@@ -103,6 +115,9 @@ class ClockSampler:
     def _poll(self):
         N = self.N
         while not self._stop.is_set():
+            if not self.active.is_set():
+                self.active.wait(0.05)
+                continue
             try:
                 self.sm.append(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM))
                 self.mask |= N.nvmlDeviceGetCurrentClocksEventReasons(self.h)
@@ -113,6 +128,7 @@ class ClockSampler:
 
     def __exit__(self, *a):
         self._stop.set()
+        self.active.set()
         if hasattr(self, "t"):
             self.t.join(timeout=2)
 
@@ -124,449 +140,593 @@ class ClockSampler:
                 "samples": len(self.sm), "source": "NVML (nvmlDeviceGetClockInfo / GetCurrentClocksEventReasons)"}
 
 
-def cpu_baseline(seconds: float = 10.0):
-    """The oracle port of the reference semantics on all host threads, on a bounded sample:
-    whole 4096x4096 FP4 layers of the same workload until ~`seconds` of CPU time."""
+# --------------------------------------------------------------------------------- CPU legs
+
+def oracle_rows_sample(seconds: float):
+    """The oracle port on all host threads over a row sample of the headline layer (rows
+    split over the threads): (GB/s of packed weights, threads, sample text)."""
     import oracle as O
     threads = os.cpu_count() or 1
-    rng = np.random.default_rng(SEED)
-    w = (rng.standard_normal((OUT, IN)) * SIGMA).astype(np.float32)
-    raw, sc = O.pack(DTYPE_FP4, w)
-    x = rng.standard_normal((1, IN)).astype(np.float32)
-    O.dense_forward(DTYPE_FP4, raw, sc, x, IN, OUT, -1, None, threads)  # warm
+    rows = 1024
+    rng = np.random.default_rng(4)
+    w = (rng.standard_normal((rows, C5_IN)) * SIGMA).astype(np.float32)
+    raw, sc = O.pack(FP4, w)
+    x = rng.standard_normal((1, C5_IN)).astype(np.float32)
+    O.dense_forward(FP4, raw, sc, x, C5_IN, rows, -1, None, threads)  # warm
     n = 0
     t0 = time.perf_counter()
     while True:
-        O.dense_forward(DTYPE_FP4, raw, sc, x, IN, OUT, -1, None, threads)
+        O.dense_forward(FP4, raw, sc, x, C5_IN, rows, -1, None, threads)
         n += 1
         if time.perf_counter() - t0 >= seconds:
             break
     dt = time.perf_counter() - t0
-    return {"value": n * WEIGHT_BYTES_PER_LAYER / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{n} forwards of one 4096x4096 FP4 layer, B=1 ({dt:.1f} s): reference decode + "
-                      f"sequential fp64 dot (oracle/oracle.c), rows split over {threads} threads"}
+    gbs = n * rows * C5_IN / 2 / dt / 1e9
+    return gbs, threads, (f"{n} forwards of a {rows}-row sample (1/{C5_OUT // rows} of the layer) of the "
+                          f"16384->65536 FP4 layer, B=1 ({dt:.1f} s): reference decode + sequential fp64 dot "
+                          f"(oracle/oracle.c), rows split over {threads} threads")
+
+
+def cpu_baseline(seconds: float):
+    gbs, threads, sample = oracle_rows_sample(seconds)
+    return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample}
 
 
 def run_reference(args):
+    """--impl reference: the reference semantics on the host cores, same metric and config."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return 0
     import oracle as O
     threads = os.cpu_count() or 1
-    rng = np.random.default_rng(SEED)
-    w = (rng.standard_normal((OUT, IN)) * SIGMA).astype(np.float32)
-    raw, sc = O.pack(DTYPE_FP4, w)
-    x = rng.standard_normal((1, IN)).astype(np.float32)
+    rows = 256
+    rng = np.random.default_rng(4)
+    w = (rng.standard_normal((rows, C5_IN)) * SIGMA).astype(np.float32)
+    raw, sc = O.pack(FP4, w)
+    x = rng.standard_normal((1, C5_IN)).astype(np.float32)
+    # a step is a bounded sample of one forward of the layer: `rows` of its 65536 rows
     for _ in range(args.warmup):
-        O.dense_forward(DTYPE_FP4, raw, sc, x, IN, OUT, -1, None, threads)
+        O.dense_forward(FP4, raw, sc, x, C5_IN, rows, -1, None, threads)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        O.dense_forward(DTYPE_FP4, raw, sc, x, IN, OUT, -1, None, threads)
+        O.dense_forward(FP4, raw, sc, x, C5_IN, rows, -1, None, threads)
     dt = time.perf_counter() - t0
-    val = args.steps * WEIGHT_BYTES_PER_LAYER / dt / 1e9
-    line = {"metric": "quant Dense weight GB/s (GEMV)", "value": val, "unit": "GB/s", "impl": "reference",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp4 codes, fp64 accumulate",
-            "data": "synthetic",
-            "config": {"workload": "C2 Dense GEMV 4096->4096 B=1 FP4 (one layer per step on the host)",
-                       "global_batch": 1, "parallelism": "host threads"},
-            "cpu_baseline": {"value": val, "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": "one 4096x4096 FP4 layer forward per step: reference decode + sequential "
-                                       "fp64 dot (oracle/oracle.c; the reference ships no host matvec)"},
+    val = args.steps * rows * C5_IN / 2 / dt / 1e9
+    sample = (f"per step {rows} of the layer's {C5_OUT} rows (B=1): reference decode + sequential fp64 dot "
+              f"(oracle/oracle.c; the reference ships no host matvec), rows split over {threads} threads")
+    line = {"metric": METRIC, "value": val, "unit": "GB/s", "impl": "reference",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt / args.steps * 1e3 * (C5_OUT / rows),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp4 codes, fp64 accumulate",
+            "data": "synthetic", "config": config_for(world),
+            "cpu_baseline": {"value": val, "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
 
-def run_ours(args):
-    import torch
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
-    import welvet.cuda_b200 as W
-    W.cuda_init()
+# --------------------------------------------------------------------------------- GPU legs
 
-    # ---- mount LAYERS distinct layers (weights generated on the device, per rank seed)
-    g = torch.Generator(device="cuda").manual_seed(SEED * 1000 + rank)
-    sessions = []
-    for _ in range(LAYERS):
-        wdev = torch.randn((OUT, IN), device="cuda", generator=g) * SIGMA
-        sessions.append(W.DenseSession(wdev, 1, DTYPE_FP4))
-        del wdev
-    torch.cuda.synchronize()
-    x0 = torch.randn((1, IN), device="cuda", generator=g)
-    acts = [torch.zeros((1, OUT), device="cuda") for _ in range(2)]
-    pre = torch.zeros((1, OUT), device="cuda")
-    stream = torch.cuda.current_stream()
-    NSTREAMS = 8
-    streams = [torch.cuda.Stream() for _ in range(NSTREAMS)]
-    outs = [(torch.zeros((1, OUT), device="cuda"), torch.zeros((1, OUT), device="cuda")) for _ in range(NSTREAMS)]
+class Ctx:
+    """Per-process state of a GPU run: torch, the library, ranks, timing helpers."""
 
-    xs_group = [x0] * LAYERS
-    outs_group = [(torch.zeros((1, OUT), device="cuda"), torch.zeros((1, OUT), device="cuda")) for _ in range(LAYERS)]
+    def __init__(self, args):
+        import torch
+        self.torch = torch
+        self.args = args
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dist = None
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180))
+            self.dist = dist
+        import welvet.cuda_b200 as W
+        from welvet.cuda_b200 import volume as V
+        W.cuda_init()
+        self.W, self.V = W, V
+        self.comm = V.Comm.from_torch(self.local) if self.world > 1 else V.Comm(0, 1, self.local, V.Comm.new_job_id())
+        self.stream = torch.cuda.current_stream()
+        self.launches = 0  # our kernel launches inside the headline's timed region
+        self.graphs = []   # captured graphs, released before the communicator
+        self.flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
 
-    def step_group():
-        # the 64 independent forwards as grouped launches (32 layers per launch)
-        W.dense_execute_group(sessions, xs_group, [o[0] for o in outs_group], [o[1] for o in outs_group])
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
 
-    def step_independent():
-        # 64 independent forwards (the reference's --bench loop repeats independent executes),
-        # one per distinct weight set, spread over 8 stream branches that the graph runs
-        # concurrently; consecutive launches on one branch overlap through PDL.
-        cur = torch.cuda.current_stream()
-        fork = torch.cuda.Event()
-        fork.record(cur)
-        for s in streams:
-            s.wait_event(fork)
-        for i, sess in enumerate(sessions):
-            j = i % NSTREAMS
-            sess.execute_device(x0, outs[j][0], outs[j][1], streams[j])
-        for s in streams:
-            cur.wait_stream(s)
-
-    def step_chain():
-        st = torch.cuda.current_stream()  # the capture stream while a graph is recorded
-        x = x0
-        for i, s in enumerate(sessions):
-            y = acts[i & 1]
-            s.execute_device(x, pre, y, st)
-            x = y
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(v: float) -> float:
-        if dist is None:
+    def max_over_ranks(self, v: float) -> float:
+        if self.dist is None:
             return v
-        t = torch.tensor([v], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t = self.torch.tensor([v], device="cuda", dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
-    def capture(fn):
-        # A step's launches are captured once in a CUDA graph (PDL edges between consecutive
-        # GEMVs of one stream are kept) and replayed per step.
-        fn()
-        torch.cuda.synchronize()
-        if args.no_graph:
-            return fn
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+    def timed(self, fn, steps: int, warmup: int) -> float:
+        """ms per step over `steps` back-to-back steps after `warmup`, CUDA events on the launching
+        stream, barrier + synchronize on both sides, max over ranks."""
+        torch = self.torch
+        for _ in range(warmup):
             fn()
-        graphs.append(graph)
-        return graph.replay
-
-    graphs = []
-    run = capture(step_group)
-    run_branches = capture(step_independent)
-    run_chain = capture(step_chain)
-    for _ in range(args.warmup):
-        run()
-        run_branches()
-        run_chain()
-    barrier()
-    stream = torch.cuda.current_stream()
-
-    def timed(fn, steps):
-        a0 = torch.cuda.Event(enable_timing=True)
-        a1 = torch.cuda.Event(enable_timing=True)
-        barrier()
-        a0.record(stream)
+        self.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
         for _ in range(steps):
             fn()
-        a1.record(stream)
-        barrier()
-        return max_over_ranks(a0.elapsed_time(a1))
+        e1.record(self.stream)
+        self.barrier()
+        return self.max_over_ranks(e0.elapsed_time(e1)) / steps
 
-    # clocks are sampled over all three device-timed legs
-    with ClockSampler(local) as clk:
-        ms = timed(run, args.steps)
-        ms_br = timed(run_branches, args.steps)
-        # the same 64 layers as a dependent chain (layer i's post is layer i+1's x)
-        ms_chain = timed(run_chain, args.steps)
-    group_per_launch = 32
-    launches_per_step = (LAYERS + group_per_launch - 1) // group_per_launch
-    prep_per_step = launches_per_step  # one k_prep_x per 32 layers ahead of the GEMV launches
-    launches = args.steps * launches_per_step
-    bytes_per_step = LAYERS * WEIGHT_BYTES_PER_LAYER
-    value = world * bytes_per_step * args.steps / (ms / 1e3) / 1e9
-    per_launch_s = (ms / 1e3) / launches
-    branches_val = world * bytes_per_step * args.steps / (ms_br / 1e3) / 1e9
-    chain_val = world * bytes_per_step * args.steps / (ms_chain / 1e3) / 1e9
+    def graphed(self, fn, n: int = 1):
+        """`fn` captured in n CUDA graphs of one call each, replayed in turn (a sharded call
+        alternates between two output buffers, so it is captured twice). One eager call first."""
+        import itertools
+        torch = self.torch
+        fn()
+        torch.cuda.synchronize()
+        graphs = []
+        for _ in range(n):
+            gph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gph):
+                fn()
+            graphs.append(gph)
+        self.graphs.extend(graphs)
+        it = itertools.cycle(graphs)
+        return lambda: next(it).replay()
 
-    # ---- e2e through the reference-facing ABI (host buffers, pinned)
-    xh = torch.randn((1, IN)).pin_memory()
-    bufs = [torch.zeros((1, OUT)).pin_memory() for _ in range(2)]
-    preh = torch.zeros((1, OUT)).pin_memory()
-    e2e_steps = max(1, min(args.steps, 20))
-    # The C ABI itself, as a cgo / FFI caller of the reference binds it: arguments prepared
-    # once, the status checked on every call.
-    c_execute = W.lib().welvet_dense_execute
-    handles = [s._h for s in sessions]
-    p_x, p_pre = ctypes.c_void_p(xh.data_ptr()), ctypes.c_void_p(preh.data_ptr())
-    p_post = [ctypes.c_void_p(b.data_ptr()) for b in bufs]
+    def timed_each(self, fn, reps: int) -> float:
+        """Median µs of single calls, L2 flushed (a 256 MiB write) before each (one GPU)."""
+        torch = self.torch
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            self.flush.zero_()
+            torch.cuda._sleep(200000)  # the GPU stays busy while the host enqueues the call
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3)
+        return statistics.median(ts)
 
-    def e2e_step():
-        # welvet_dense_execute on each of the 64 layers: x in from host memory, forward, pre
-        # and post out to host memory, synchronize -- the reference's resident-session
-        # contract and --bench loop.
-        for i, h in enumerate(handles):
-            st = c_execute(h, p_x, p_pre, p_post[i & 1])
+
+def sharded_legs(c: Ctx, batch: int, steps: int, warmup: int, W_rows, b: int, e: int):
+    """Fused, nccl and compute-only forwards of the headline layer at `batch` tokens."""
+    torch, W, V = c.torch, c.W, c.V
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = torch.randn((batch, C5_IN), device="cuda", generator=g)
+    res = {}
+    # every leg is replayed from CUDA graphs (one graph launch per step); the sharded call is
+    # captured twice, once per output buffer
+    fused = V.ShardedDense(c.comm, W_rows, C5_IN, C5_OUT, batch, FP4, W.LINEAR, None, V.FUSED)
+    res["fused_ms"] = c.timed(c.graphed(lambda: fused.execute_device_ptrs(x), 2), steps, warmup)
+    fused.check_error()
+    nccl = V.ShardedDense(c.comm, W_rows, C5_IN, C5_OUT, batch, FP4, W.LINEAR, None, V.NCCL)
+    res["nccl_ms"] = c.timed(c.graphed(lambda: nccl.execute_device_ptrs(x), 2), steps, warmup)
+    nccl.check_error()
+    local = W.DenseSession(W_rows, batch, FP4) if e > b else None
+    if local is not None:
+        pre = torch.empty((batch, e - b), device="cuda")
+        res["compute_ms"] = c.timed(c.graphed(lambda: local.execute_device(x, pre, pre)), steps, warmup)
+    else:
+        res["compute_ms"] = c.timed(lambda: None, steps, warmup)
+    return res, (fused, nccl), local, x
+
+
+def run_ours(args):
+    c = Ctx(args)
+    torch, W, V = c.torch, c.W, c.V
+    pk, pk_kind = peaks()
+    world, rank = c.world, c.rank
+    b, e = V.shard_rows(C5_OUT, world, rank)
+    g = torch.Generator(device="cuda").manual_seed(4 * 1000 + rank)
+    W_rows = torch.randn((e - b, C5_IN), device="cuda", generator=g) * SIGMA
+
+    with ClockSampler(c.local) as clk:
+        # ---- headline: batch 1 (the GEMV), whole job
+        clk.active.set()
+        s1, fused1, local1, x1 = sharded_legs(c, 1, args.steps, args.warmup, W_rows, b, e)
+        # ---- batch 256 (the tcgen05 GEMM)
+        s256, fused256, local256, x256 = sharded_legs(c, 256, max(3, min(args.steps, 20)), 3, W_rows, b, e)
+        clk.active.clear()
+    del W_rows
+    torch.cuda.empty_cache()
+    ms = s1["fused_ms"]
+    value = C5_BYTES / (ms / 1e3) / 1e9
+    c.launches = args.steps * (2 if world > 1 else 1)  # GEMV (+ flag exchange) per step
+    flops256 = 2.0 * 256 * C5_OUT * C5_IN
+
+    # roofline of the headline's dominant kernel: this rank's GEMV, timed alone (compute-only
+    # leg: the shard as a one-GPU layer, the same kernel and launch plan as the fused call's)
+    shard_bytes = (e - b) * C5_IN // 2
+    achieved = shard_bytes / (s1["compute_ms"] / 1e3) / 1e9
+    traffic_full = profile_value("gemv_tc_fp4_65536x16384_b1.md", "dram_bytes_per_launch")
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / pk["hbm_gbs"],
+                "traffic": None if traffic_full is None else traffic_full * (e - b) / C5_OUT,
+                "peak_source": f"{pk_kind} hbm_gbs (MEASURED_PEAKS.json, burst copy)",
+                "kernel": "k_gemv_tc<FP4,B=1> over this rank's rows (welvet/cuda_b200/csrc/gemv_tc.cu)",
+                "algorithmic_bytes_per_launch": shard_bytes,
+                "step_frac": value / world / pk["hbm_gbs"],
+                "traffic_source": "profiles/gemv_tc_fp4_65536x16384_b1.md (full layer, scaled to this rank's rows)"}
+    sharded = {
+        "b1": {"fused_ms": s1["fused_ms"], "nccl_ms": s1["nccl_ms"], "compute_ms": s1["compute_ms"],
+               "fused_GBps": C5_BYTES / (s1["fused_ms"] / 1e3) / 1e9,
+               "nccl_GBps": C5_BYTES / (s1["nccl_ms"] / 1e3) / 1e9,
+               "gather_share_fused": max(0.0, 1.0 - s1["compute_ms"] / s1["fused_ms"]),
+               "gather_share_nccl": max(0.0, 1.0 - s1["compute_ms"] / s1["nccl_ms"]),
+               "gather_bytes": C5_OUT * 4},
+        "b256": {"fused_ms": s256["fused_ms"], "nccl_ms": s256["nccl_ms"], "compute_ms": s256["compute_ms"],
+                 "fused_TFLOPs": flops256 / (s256["fused_ms"] / 1e3) / 1e12,
+                 "nccl_TFLOPs": flops256 / (s256["nccl_ms"] / 1e3) / 1e12,
+                 "gather_share_fused": max(0.0, 1.0 - s256["compute_ms"] / s256["fused_ms"]),
+                 "gather_share_nccl": max(0.0, 1.0 - s256["compute_ms"] / s256["nccl_ms"]),
+                 "gather_bytes": 256 * C5_OUT * 4},
+        "what": "ms per forward, max over ranks: fused = the product call (GEMV/GEMM epilogues store into every "
+                "rank's output over NVLink + flag exchange); nccl = local forward + ncclAllGather + permute; "
+                "compute = this rank's shard as a one-GPU layer, no gather; gather_share = 1 - compute / total"}
+    batched = {"value": flops256 / (s256["fused_ms"] / 1e3) / 1e12, "unit": "TFLOP/s",
+               "ms_per_forward": s256["fused_ms"],
+               "config": "C5 column-sharded Dense 16384->65536 FP4, batch 256 (x~N(0,1): two f16 planes), fused gather",
+               "frac": flops256 / (s256["fused_ms"] / 1e3) / 1e12 / (world * pk["bf16_tflops"]),
+               "peak": world * pk["bf16_tflops"], "peak_source": f"{pk_kind} bf16_tflops (burst) x {world} GPUs",
+               "kernels": "k_split_x + k_gemm_tm<FP4> (+ tail / split-K reduce) + k_flag_exchange"}
+
+    # ---- e2e: the same metric through the C ABI with host buffers
+    e2e_steps = max(3, min(args.steps, 20))
+    xh = torch.randn((1, C5_IN)).pin_memory()
+    yh = torch.zeros((1, C5_OUT)).pin_memory()
+    ph = torch.zeros((1, C5_OUT)).pin_memory()
+    if world == 1:
+        c_exec = W.lib().welvet_dense_execute
+        h = local1._h
+        px, pp, py = ctypes.c_void_p(xh.data_ptr()), ctypes.c_void_p(ph.data_ptr()), ctypes.c_void_p(yh.data_ptr())
+
+        def e2e_step():
+            st = c_exec(h, px, pp, py)
             if st.code != 0:
                 raise W.WelvetError(st.code, st.message.decode(errors="replace"))
+        api = "welvet_dense_execute via ctypes (pinned host buffers, synchronous per call)"
+    else:
+        c_exec = W.lib().welvet_b200_sharded_dense_execute
+        h = fused1[0]._h
+        px, py = ctypes.c_void_p(xh.data_ptr()), ctypes.c_void_p(yh.data_ptr())
 
-    for _ in range(2):
+        def e2e_step():
+            st = c_exec(h, px, None, py)
+            if st.code != 0:
+                raise W.WelvetError(st.code, st.message.decode(errors="replace"))
+        api = "welvet_b200_sharded_dense_execute via ctypes (pinned host buffers, synchronous, every rank)"
+    for _ in range(3):
         e2e_step()
-    barrier()
+    c.barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         e2e_step()
-    t_e2e = max_over_ranks(time.perf_counter() - t0)
-    e2e_val = world * bytes_per_step * e2e_steps / t_e2e / 1e9
+    t_e2e = c.max_over_ranks(time.perf_counter() - t0)
+    e2e = {"value": C5_BYTES * e2e_steps / t_e2e / 1e9, "unit": "GB/s", "h2d_bytes_per_step": C5_IN * 4 * world,
+           "d2h_bytes_per_step": C5_OUT * 4 * world, "steps": e2e_steps, "api": api}
+    c.graphs.clear()
+    torch.cuda.synchronize()
+    for s in (*fused1, *fused256, local1, local256):
+        if s is not None:
+            s.release()
+    torch.cuda.empty_cache()
 
-    # ---- batched path: C3 SwiGLU cell at M = 512 (tcgen05 GEMMs for gate, up and down)
-    batched = run_batched(args, torch, W, rank, barrier, max_over_ranks, stream) if not args.no_batched else None
+    # ---- C5's volume: one GPU runs the chain, N GPUs the cell-per-GPU pipeline
+    volume = run_volume(c, args)
 
-    pk, pk_kind = peaks()
-    bytes_per_launch = group_per_launch * WEIGHT_BYTES_PER_LAYER
-    achieved = bytes_per_launch / per_launch_s / 1e9
-    tr = traffic_from_profile()
-    roofline = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / pk["hbm_gbs"], "traffic": tr,
-                "peak_source": f"{pk_kind} hbm_gbs (MEASURED_PEAKS.json)" if pk_kind == "measured" else "fallback",
-                "kernel": "k_gemv_tc<FP4,B=1> over 32 layers per launch (welvet/cuda_b200/csrc/gemv_tc.cu)",
-                "algorithmic_bytes_per_launch": bytes_per_launch}
-    if batched is not None:
-        batched["frac"] = batched["value"] / pk["bf16_tflops"]
-        batched["peak"] = pk["bf16_tflops"]
-        batched["peak_source"] = f"{pk_kind} bf16_tflops (burst, MEASURED_PEAKS.json)"
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    configs, ref_cuda, cpu = None, None, None
+    if world == 1 and not args.no_configs:
+        configs = run_configs(c, args, pk)
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        ref_cuda = reference_cuda(args)
         cpu = cpu_baseline(args.cpu_seconds)
 
     if rank == 0:
-        line = {"metric": "quant Dense weight GB/s (GEMV)", "value": value, "unit": "GB/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp4 codes, fp32/fp64 accumulate",
-                "data": "synthetic",
-                "config": {"workload": "C2 Dense GEMV 4096->4096 B=1 FP4 (W~N(0,0.02), seed 1): 64 independent "
-                                       "forwards of 64 distinct weight sets per step, grouped 32 layers per launch",
-                           "global_batch": world, "seq_len": 1, "parallelism": f"replicas x{world}",
-                           "l2": "inputs larger than L2 (512 MiB of packed weights per step)",
-                           "bytes_per_step_per_gpu": bytes_per_step},
-                "roofline": roofline,
-                "cpu_baseline": cpu,
-                "e2e": {"value": e2e_val, "unit": "GB/s", "h2d_bytes_per_step": LAYERS * IN * 4,
-                        "d2h_bytes_per_step": LAYERS * OUT * 4 * 2, "steps": e2e_steps,
-                        "api": "welvet_dense_execute via ctypes (host pinned buffers, synchronous per layer)"},
-                "branches": {"value": branches_val, "unit": "GB/s", "ms_per_step": ms_br / args.steps,
-                             "what": "the same 64 forwards as 64 single-layer launches on 8 CUDA-graph branches"},
-                "chain": {"value": chain_val, "unit": "GB/s", "ms_per_step": ms_chain / args.steps,
-                          "what": "the same 64 layers as a dependent chain, layer i's post feeding layer i+1"},
-                "batched": batched,
-                "gpu_launches": launches + args.steps * prep_per_step,
-                "clocks": clk.summary()}
+        line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "fp4 codes, fp32 tensor-core sums, fp64 across chunks", "data": "synthetic",
+                "config": config_for(world),
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "batched": batched, "sharded": sharded,
+                "volume": volume, "configs": configs, "reference_cuda": ref_cuda,
+                "gpu_launches": c.launches, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
-    del graphs
-    for s in sessions:
-        s.release()
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    c.comm.release()
+    if c.dist is not None:
+        c.dist.barrier()
+        c.dist.destroy_process_group()
     return 0
 
 
-def run_batched(args, torch, W, rank, barrier, max_over_ranks, stream):
-    """C3 SwiGLU cell (4096 -> 14336 -> 4096, FP8 E4M3) at M = 512 tokens: TFLOP/s of the
-    tcgen05 GEMM path (2 * M * 3 * 4096 * 14336 flops per forward). Weights are 176 MB, more
-    than L2; the cell's forward is captured in a CUDA graph."""
-    d, hid, m = 4096, 14336, 512
-    g = torch.Generator(device="cuda").manual_seed(2 * 1000 + rank)
-    ws = [torch.randn(s, device="cuda", generator=g) * SIGMA for s in ((hid, d), (hid, d), (d, hid))]
-    cell = W.SwigluCell(ws[0], ws[1], ws[2], 4)
-    del ws
-    x = torch.randn((m, d), device="cuda", generator=g).to(torch.bfloat16).float()
-    y = torch.zeros((m, d), device="cuda")
-    h = torch.zeros((m, hid), device="cuda")
-    cell.execute_device(x, y, h)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        cell.execute_device(x, y, h)
-    for _ in range(max(3, args.warmup)):
-        graph.replay()
-    steps = max(5, min(args.steps, 50))
-    a0 = torch.cuda.Event(enable_timing=True)
-    a1 = torch.cuda.Event(enable_timing=True)
-    barrier()
-    a0.record(stream)
-    for _ in range(steps):
-        graph.replay()
-    a1.record(stream)
-    barrier()
-    ms = max_over_ranks(a0.elapsed_time(a1)) / steps
-    flops = 2.0 * m * 3 * d * hid
-    del graph
-    cell.release()
-    return {"value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_forward": ms, "steps": steps,
-            "config": "C3 SwiGLU cell d=4096 hidden=14336 FP8 E4M3 W~N(0,0.02), M=512 tokens, x~N(0,1) "
-                      "rounded to bf16, seed 2",
-            "kernels": "k_split_x + k_gemm_tm<FP8 E4M3> over the interleaved Gate/Up pair (SiLU(g)*u in the "
-                       "epilogue) + k_split_x + k_gemm_tm<FP8 E4M3> (Down)",
-            "l2": "176 MB of FP8 weights per forward (more than L2)"}
-
-
-def run_case_multi(args):
-    """--case sharded | pipeline: BASELINE config 5 on 1..N GPUs (torchrun; one process per GPU).
-      sharded   Dense rows x cols FP4 (default 65536 x 16384) split by output rows over the
-                ranks, --tokens 1 or 256; each rank's slice then NCCL all-gather
-      pipeline  volume 2x2x2 with 4 Dense 4096x4096 FP4 + ReLU layers per cell, batch 64:
-                cells placed over the ranks in hop order, --micro rows per micro-batch,
-                activations sent rank to rank
-    Prints one JSON line (rank 0): time per forward (max over ranks) and aggregate rates."""
-    import datetime
-    import torch
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    import torch.distributed as dist
-    dist.init_process_group("nccl" if world > 1 else "gloo", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=120),
-                            **({} if world > 1 else {"init_method": "tcp://127.0.0.1:29731"}))
-    import welvet.cuda_b200 as W
-    from welvet.cuda_b200 import volume as V
-    W.cuda_init()
-    g = torch.Generator(device="cuda").manual_seed(4 * 1000 + rank)
-    stream = torch.cuda.current_stream()
-    out = {"case": args.case, "n_gpus": world}
-    if args.case == "sharded":
-        rows, cols, tokens = args.rows, args.cols, args.tokens
-        a, b = V.ColumnShardedDense.shard_rows(rows, world, rank)
-        w = torch.randn((b - a, cols), device="cuda", generator=g) * SIGMA
-        sess = W.DenseSession(w, tokens, DTYPE_FP4)
+def run_volume(c: Ctx, args):
+    """C5 volume: 8 cells x 4 Dense 4096x4096 FP4 + ReLU, batch 64."""
+    torch, W, V = c.torch, c.W, c.V
+    cells, lpc, width, batch = 8, 4, 4096, 64
+    hb, he = V.stage_plan(cells, lpc, c.world)[c.rank]
+    vol = V.Volume(2, 2, 2, lpc)
+    g = torch.Generator(device="cuda").manual_seed(4 * 1000 + 17)
+    for h in range(cells * lpc):  # every rank draws all weights in hop order, binds its own
+        w = torch.randn((width, width), device="cuda", generator=g) * SIGMA
+        if hb <= h < he:
+            vol.bind_dense(vol.coord(h), w, W.RELU, FP4)
         del w
-        x = torch.randn((tokens, cols), device="cuda", generator=torch.Generator(device="cuda").manual_seed(4))
-        pre = torch.empty((tokens, b - a), device="cuda")
-        post = torch.empty((tokens, b - a), device="cuda")
-
-        def local_fn(xd):
-            sess.execute_device(xd, pre, post, stream)
-            return pre
-
-        sd = V.ColumnShardedDense(local_fn, rows)
-        step = lambda: sd.forward(x)
-        compute = lambda: local_fn(x)
-        flops = 2.0 * tokens * rows * cols
-        wbytes = rows * cols * 0.5
+    x = torch.randn((batch, width), device="cuda", generator=torch.Generator(device="cuda").manual_seed(4))
+    y = torch.empty((batch, width), device="cuda")
+    steps = max(3, min(c.args.steps, 20))
+    if c.world == 1:
+        ms = c.timed(lambda: vol.forward_device(x, y, stream=c.stream), steps, 3)
+        micro = batch
     else:
-        lpc, cells, width, batch = 4, 8, 4096, 64
-        vol = V.Volume(2, 2, 2, lpc)
-        b, e = V.stage_plan(cells, lpc, world)[rank]
-        for h in range(b, e):
-            w = torch.randn((width, width), device="cuda", generator=g) * SIGMA
-            vol.bind_dense(vol.coord(h), w, 0, DTYPE_FP4)
-            del w
-        x = torch.randn((batch, width), device="cuda", generator=torch.Generator(device="cuda").manual_seed(4))
-
-        def runner(xin):
-            o = torch.empty_like(xin)
-            vol.forward_device(xin, o, b, e, stream=stream)
-            return o
-
-        pv = V.PipelinedVolume(runner, width, [width] * world)
-        step = lambda: pv.forward(x, micro=args.micro)
-        compute = None
-        flops = 2.0 * batch * cells * lpc * width * width
-        wbytes = cells * lpc * width * width * 0.5
-
-    def timed(fn, reps):
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize()
-        dist.barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(reps):
-            fn()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        t = torch.tensor([e0.elapsed_time(e1) / reps], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX) if world > 1 else None
-        return float(t.item())
-
-    ms = timed(step, args.reps)
-    out.update({"ms_per_forward": ms, "TFLOPs": flops / (ms / 1e3) / 1e12, "weight_GBps": wbytes / (ms / 1e3) / 1e9,
-                "tokens": args.tokens if args.case == "sharded" else 64,
-                "micro": args.micro if args.case == "pipeline" else None})
-    if compute is not None:
-        out["compute_ms"] = timed(compute, args.reps)
-        gathered = torch.empty((world * args.tokens, (args.rows // world)), device="cuda")
-        src = torch.empty((args.tokens, args.rows // world), device="cuda")
-        out["gather_ms"] = timed(lambda: dist.all_gather_into_tensor(gathered, src) if world > 1 else None, args.reps)
-    if rank == 0:
-        print(json.dumps(out), flush=True)
-    dist.barrier()
-    dist.destroy_process_group()
-    return 0
+        micro = max(8, batch // c.world)
+        ms = c.timed(lambda: c.comm.pipeline_forward(vol, (hb, he), x, width, micro, y, c.stream), steps, 3)
+    vol.release()
+    flops = 2.0 * batch * cells * lpc * width * width
+    wbytes = cells * lpc * width * width // 2
+    return {"ms_per_forward": ms, "TFLOPs": flops / (ms / 1e3) / 1e12, "weight_GBps": wbytes / (ms / 1e3) / 1e9,
+            "micro_batch": micro, "placement": "whole chain on one GPU" if c.world == 1 else
+            f"cell-per-GPU pipeline over {c.world} GPUs (NCCL point-to-point)"}
 
 
-def run_case_swiglu(args, torch, W, g):
-    d, hid, m = args.cols, args.rows, args.tokens
-    ws = [torch.randn(sh, device="cuda", generator=g) * SIGMA for sh in ((hid, d), (hid, d), (d, hid))]
-    cell = W.SwigluCell(ws[0], ws[1], ws[2], args.dtype)
-    del ws
-    x = torch.randn((m, d), device="cuda", generator=g)
-    if args.x == "bf16":
-        x = x.to(torch.bfloat16).float()
-    y = torch.zeros((m, d), device="cuda")
-    h = torch.zeros((m, hid), device="cuda")
-    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
-    cell.execute_device(x, y, h)
-    torch.cuda.synchronize()
-    ts = []
-    for _ in range(args.reps):
-        flush.zero_()
-        torch.cuda._sleep(200000)
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        cell.execute_device(x, y, h)
-        e1.record()
-        torch.cuda.synchronize()
-        ts.append(e0.elapsed_time(e1) * 1e3)
-    us = statistics.median(ts)
-    wbytes = 3 * d * hid * (0.5 if args.dtype == DTYPE_FP4 else 1.0)
-    print(json.dumps({"case": "swiglu", "dtype": args.dtype, "d": d, "hidden": hid, "tokens": m, "x": args.x,
-                      "reps": args.reps, "us_median": round(us, 2), "weight_GBps": round(wbytes / us / 1e3, 1),
-                      "TFLOPs": round(2.0 * m * 3 * d * hid / us / 1e6, 2)}), flush=True)
+def run_configs(c: Ctx, args, pk):
+    """Configs 1-4 on one GPU (sub-records of the line)."""
+    torch, W = c.torch, c.W
+    out = {}
+    hbm = pk["hbm_gbs"]
+    tens = pk["bf16_tflops"]
+
+    def wt(shape, seed, sigma):
+        return torch.randn(shape, device="cuda", generator=torch.Generator(device="cuda").manual_seed(seed)) * sigma
+
+    # C1: Dense 256 -> 128 E4M3 (scale 1), bias, batch 1: latency (parity case)
+    w = wt((128, 256), 0, 0.05)
+    bias = np.random.default_rng(0).standard_normal(128) * 0.01
+    s = W.DenseSession(w, 1, E4M3, W.LINEAR, bias)
+    x = torch.rand((1, 256), device="cuda") * 2 - 1
+    y = torch.empty((1, 128), device="cuda")
+    us = c.timed_each(lambda: s.execute_device(x, y, y), 20)
+    xh, yh = x.cpu().numpy(), np.zeros((1, 128), np.float32)
+    s.execute(xh, yh, yh)
+    t0 = time.perf_counter()
+    for _ in range(50):
+        s.execute(xh, yh, yh)
+    out["C1"] = {"us_device": us, "us_host_buffers": (time.perf_counter() - t0) / 50 * 1e6,
+                 "what": "one forward, L2 flushed before each; host buffers through welvet_dense_execute"}
+    s.release()
+
+    # C2: Dense 4096 -> 4096 batch 1; FP4 (sigma 0.02 and 2.0), Int8, E4M3: 64 layers per step
+    out["C2"] = {}
+    for name, dt, sigma in (("fp4", FP4, SIGMA), ("fp4_sigma2", FP4, 2.0), ("int8", INT8, SIGMA),
+                            ("e4m3", E4M3, SIGMA)):
+        out["C2"][name] = c2_legs(c, dt, sigma, hbm)
+
+    # C3: SwiGLU 4096 / 14336 E4M3, M in {1, 16, 128, 512}
+    d, hid = 4096, 14336
+    cell = W.SwigluCell(wt((hid, d), 21, SIGMA), wt((hid, d), 22, SIGMA), wt((d, hid), 23, SIGMA), E4M3)
+    out["C3"] = {}
+    for m in (1, 16, 128, 512):
+        xm = torch.randn((m, d), device="cuda").to(torch.bfloat16).float()
+        ym = torch.empty((m, d), device="cuda")
+        hm = torch.empty((m, hid), device="cuda")
+        us = c.timed_each(lambda: cell.execute_device(xm, ym, hm), 10)
+        wbytes = 3 * d * hid
+        fl = 2.0 * m * 3 * d * hid
+        rec = {"us": us, "weight_GBps": wbytes / us / 1e3, "TFLOPs": fl / us / 1e6}
+        rec["frac_hbm"] = rec["weight_GBps"] / hbm
+        rec["frac_tensor"] = rec["TFLOPs"] / tens
+        out["C3"][f"M{m}"] = rec
     cell.release()
-    return 0
 
+    # C4: RMSNorm + MHA (2048, 16 x 128, causal, RoPE) E4M3 + SwiGLU 2048 / 5632 FP4, 4 x 512 tokens
+    out["C4"] = c4_legs(c, tens)
+    torch.cuda.empty_cache()
+    return out
+
+
+def c2_legs(c: Ctx, dt: int, sigma: float, hbm: float):
+    torch, W = c.torch, c.W
+    n, rows, cols = 64, 4096, 4096
+    g = torch.Generator(device="cuda").manual_seed(1)
+    sess = []
+    for _ in range(n):
+        w = torch.randn((rows, cols), device="cuda", generator=g) * sigma
+        sess.append(W.DenseSession(w, 1, dt))
+        del w
+    x = torch.randn((1, cols), device="cuda", generator=g)
+    outs = [(torch.empty((1, rows), device="cuda"), torch.empty((1, rows), device="cuda")) for _ in range(n)]
+    acts = [torch.empty((1, rows), device="cuda") for _ in range(2)]
+    pre = torch.empty((1, rows), device="cuda")
+    wbytes = rows * cols * (0.5 if dt == FP4 else 1.0) + (4 if dt == INT8 else 0)
+
+    def grouped():
+        W.dense_execute_group(sess, [x] * n, [o[0] for o in outs], [o[1] for o in outs])
+
+    def singles():
+        for i, s in enumerate(sess):
+            s.execute_device(x, outs[i][0], outs[i][1])
+
+    def chain():
+        xi = x
+        for i, s in enumerate(sess):
+            s.execute_device(xi, pre, acts[i & 1])
+            xi = acts[i & 1]
+
+    rec = {}
+    for name, fn in (("grouped", grouped), ("single_launches", singles), ("chain", chain)):
+        ms = c.timed(fn, 10, 3)
+        rec[name + "_GBps"] = n * wbytes / (ms / 1e3) / 1e9
+    rec["grouped_frac"] = rec["grouped_GBps"] / hbm
+    rec["single_frac"] = rec["single_launches_GBps"] / hbm
+    # host buffers, one synchronous welvet_dense_execute per layer
+    xh = torch.randn((1, cols)).pin_memory()
+    yh = torch.zeros((1, rows)).pin_memory()
+    c_exec = W.lib().welvet_dense_execute
+    px, py = ctypes.c_void_p(xh.data_ptr()), ctypes.c_void_p(yh.data_ptr())
+    for s in sess[:4]:
+        c_exec(s._h, px, py, py)
+    t0 = time.perf_counter()
+    for s in sess:
+        st = c_exec(s._h, px, py, py)
+        if st.code != 0:
+            raise W.WelvetError(st.code, st.message.decode(errors="replace"))
+    dt_s = time.perf_counter() - t0
+    rec["host_buffers_GBps"] = n * wbytes / dt_s / 1e9
+    rec["host_buffers_us_per_call"] = dt_s / n * 1e6
+    for s in sess:
+        s.release()
+    return rec
+
+
+def c4_legs(c: Ctx, tens: float):
+    torch, W = c.torch, c.W
+    B, S, d, heads, hd, inter = 4, 512, 2048, 16, 128, 5632
+    T = B * S
+
+    def wt(shape, seed, sigma=SIGMA):
+        return torch.randn(shape, device="cuda", generator=torch.Generator(device="cuda").manual_seed(seed)) * sigma
+
+    x = torch.randn((T, d), device="cuda", generator=torch.Generator(device="cuda").manual_seed(3))
+    gamma = np.ones(d, np.float32)
+    vol = c.V.Volume(1, 1, 1, 1)
+    vol.bind_rmsnorm((0, 0, 0, 0), gamma, 1e-6, W.FLOAT32)
+    xn = torch.empty_like(x)
+    us_norm = c.timed_each(lambda: vol.forward_device(x, xn), 10)
+    vol.release()
+    qkvo = [wt((d, d), 31 + i) for i in range(4)]
+    mha = W.MhaCell(*qkvo, d_model=d, num_heads=heads, num_kv_heads=heads, head_dim=hd, max_seq_len=S, mask=1, pos=0,
+                    dtype=E4M3)
+    y = torch.empty_like(x)
+    attn = torch.empty((T, d), device="cuda")
+    us_mha = c.timed_each(lambda: mha.execute_device(xn, B, S, y, attn), 5)
+    mha.release()
+    proj = [W.DenseSession(w, T, E4M3) for w in qkvo]
+    del qkvo
+    py = torch.empty((T, d), device="cuda")
+
+    def projections():
+        for p in proj:
+            p.execute_device(xn, py, py)
+    us_proj = c.timed_each(projections, 5)
+    for p in proj:
+        p.release()
+    rec = {"us_rmsnorm": us_norm, "us_mha_cell": us_mha, "us_qkvo_projections": us_proj,
+           "us_attention_and_rope": max(0.0, us_mha - us_proj),
+           "proj_TFLOPs": 2.0 * T * 4 * d * d / us_proj / 1e6}
+    for tag, sigma in (("swiglu_fp4", SIGMA), ("swiglu_fp4_sigma2", 2.0)):
+        cell = W.SwigluCell(wt((inter, d), 41, sigma), wt((inter, d), 42, sigma), wt((d, inter), 43, sigma), FP4)
+        h = torch.empty((T, inter), device="cuda")
+        us = c.timed_each(lambda: cell.execute_device(y, py, h), 5)
+        rec["us_" + tag] = us
+        rec[tag + "_TFLOPs"] = 2.0 * T * 3 * d * inter / us / 1e6
+        rec[tag + "_frac"] = rec[tag + "_TFLOPs"] / tens
+        cell.release()
+    rec["us_cell_total"] = us_norm + us_mha + rec["us_swiglu_fp4"]
+    return rec
+
+
+def reference_cuda(args):
+    """The reference's own CUDA Dense session (oracle/_ref, its kernels rebuilt for sm_100a):
+    host buffers, synchronous per call, same shapes and seeds as configs 1-3 (C3: its Gate
+    projection). A baseline beside ours, never the measured product."""
+    import oracle as O
+    if not O.ref_available():
+        return {"unavailable": "oracle/_ref not built"}
+    R = O.ref()
+    f = lambda a: a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    msg = ctypes.create_string_buffer(256)
+    res = {"what": "reference welvet_dense_execute-equivalent session (resident fp64 mirror, "
+                   "dense_matvec_f64_batch + dense_bias_act), host buffers, per call"}
+
+    def one(tag, rows, cols, M, dt, sigma, seed, reps, bias=None):
+        rng = np.random.default_rng(seed)
+        w = (rng.standard_normal((rows, cols)) * sigma).astype(np.float32)
+        x = rng.standard_normal((M, cols)).astype(np.float32)
+        sess = ctypes.c_void_p()
+        b = None if bias is None else np.ascontiguousarray(bias, np.float64)
+        bp = None if b is None else b.ctypes.data_as(ctypes.POINTER(ctypes.c_double))
+        if R.ref_dense_mount(M, cols, rows, -1, dt, f(w), bp, 0 if b is None else b.size, ctypes.byref(sess), msg,
+                             256) != 0:
+            res[tag] = {"error": msg.value.decode(errors="replace")}
+            return
+        pre = np.zeros((M, rows), np.float32)
+        post = np.zeros((M, rows), np.float32)
+        R.ref_dense_execute(sess, f(x), f(pre), f(post), msg, 256)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            R.ref_dense_execute(sess, f(x), f(pre), f(post), msg, 256)
+        t = (time.perf_counter() - t0) / reps
+        R.ref_dense_release(sess)
+        wb = rows * cols * (0.5 if dt == FP4 else 1.0)
+        res[tag] = {"us_per_call": t * 1e6, "weight_GBps": wb / t / 1e9, "TFLOPs": 2.0 * M * rows * cols / t / 1e12}
+
+    one("C1", 128, 256, 1, E4M3, 0.05, 0, 50, np.random.default_rng(0).standard_normal(128) * 0.01)
+    one("C2_fp4", 4096, 4096, 1, FP4, SIGMA, 1, 20)
+    one("C2_int8", 4096, 4096, 1, INT8, SIGMA, 1, 20)
+    one("C3_gate_M1", 14336, 4096, 1, E4M3, SIGMA, 2, 10)
+    one("C3_gate_M512", 14336, 4096, 512, E4M3, SIGMA, 2, 2)
+    return res
+
+
+# --------------------------------------------------------------------------------- single cases
 
 def run_case(args):
-    """--case: one kernel's workload alone, for timing and ncu captures (prints one JSON line
-    with the case's own numbers, not the benchmark line). Weights ~N(0, 0.02) generated on
-    the device; x ~N(0, 1) (rounded to bf16 with --x bf16); L2 flushed before each rep.
-      gemv   one Dense layer rows x cols, --tokens 1..4, single launches
+    """--case: one kernel's workload alone on one GPU, for timing and ncu captures (prints one
+    JSON line with the case's own numbers, not the benchmark line). Weights ~N(0, 0.02)
+    generated on the device; x ~N(0, 1) (rounded to bf16 with --x bf16); L2 flushed before
+    each rep.
+      gemv   one Dense layer rows x cols, --tokens 1..8 (tensor GEMV)
       group  --layers independent layers rows x cols, B=1, grouped launches
       gemm   one Dense layer rows x cols, --tokens > 8 (tcgen05 path)
       swiglu one SwiGLU cell, d = cols, hidden = rows, --tokens (Gate/Up pair GEMM, Down GEMM)"""
     import torch
     import welvet.cuda_b200 as W
     W.cuda_init()
-    g = torch.Generator(device="cuda").manual_seed(SEED)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+
+    def each(fn):
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(args.reps):
+            flush.zero_()
+            torch.cuda._sleep(200000)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3)
+        return statistics.median(ts)
+
     if args.case == "swiglu":
-        return run_case_swiglu(args, torch, W, g)
+        d, hid, m = args.cols, args.rows, args.tokens
+        ws = [torch.randn(sh, device="cuda", generator=g) * SIGMA for sh in ((hid, d), (hid, d), (d, hid))]
+        cell = W.SwigluCell(ws[0], ws[1], ws[2], args.dtype)
+        del ws
+        x = torch.randn((m, d), device="cuda", generator=g)
+        if args.x == "bf16":
+            x = x.to(torch.bfloat16).float()
+        y = torch.zeros((m, d), device="cuda")
+        h = torch.zeros((m, hid), device="cuda")
+        us = each(lambda: cell.execute_device(x, y, h))
+        wbytes = 3 * d * hid * (0.5 if args.dtype == FP4 else 1.0)
+        print(json.dumps({"case": "swiglu", "dtype": args.dtype, "d": d, "hidden": hid, "tokens": m, "x": args.x,
+                          "reps": args.reps, "us_median": round(us, 2), "weight_GBps": round(wbytes / us / 1e3, 1),
+                          "TFLOPs": round(2.0 * m * 3 * d * hid / us / 1e6, 2)}), flush=True)
+        cell.release()
+        return 0
     n_layers = args.layers if args.case == "group" else 1
     tokens = 1 if args.case == "group" else args.tokens
     sess = []
@@ -579,7 +739,6 @@ def run_case(args):
         x = x.to(torch.bfloat16).float()
     outs = [(torch.zeros((tokens, args.rows), device="cuda"), torch.zeros((tokens, args.rows), device="cuda"))
             for _ in range(n_layers)]
-    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
 
     def fwd():
         if args.case == "group":
@@ -587,21 +746,8 @@ def run_case(args):
         else:
             sess[0].execute_device(x, outs[0][0], outs[0][1])
 
-    fwd()
-    torch.cuda.synchronize()
-    ts = []
-    for _ in range(args.reps):
-        flush.zero_()
-        torch.cuda._sleep(200000)  # the GPU stays busy while the host enqueues the forward
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        fwd()
-        e1.record()
-        torch.cuda.synchronize()
-        ts.append(e0.elapsed_time(e1) * 1e3)
-    us = statistics.median(ts)
-    wbytes = args.rows * args.cols * n_layers * (0.5 if args.dtype == DTYPE_FP4 else 1.0)
+    us = each(fwd)
+    wbytes = args.rows * args.cols * n_layers * (0.5 if args.dtype == FP4 else 1.0)
     line = {"case": args.case, "dtype": args.dtype, "rows": args.rows, "cols": args.cols, "layers": n_layers,
             "tokens": tokens, "x": args.x, "reps": args.reps, "us_median": round(us, 2),
             "weight_GBps": round(wbytes / us / 1e3, 1),
@@ -615,26 +761,22 @@ def run_case(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-graph", action="store_true", help="launch the step's kernels one by one")
-    ap.add_argument("--no-batched", action="store_true", help="skip the batched (SwiGLU M=512) measurement")
-    ap.add_argument("--case", choices=["gemv", "group", "gemm", "swiglu", "sharded", "pipeline"],
-                    help="time one workload alone (see run_case / run_case_multi)")
-    ap.add_argument("--micro", type=int, default=16, help="--case pipeline: rows per micro-batch")
-    ap.add_argument("--dtype", type=int, default=DTYPE_FP4, help="--case: 16 FP4, 4 E4M3, 5 E5M2, 9 Int8")
-    ap.add_argument("--rows", type=int, default=OUT)
-    ap.add_argument("--cols", type=int, default=IN)
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the host-core and reference-CUDA legs")
+    ap.add_argument("--no-configs", action="store_true", help="skip the configs 1-4 sub-records (N = 1)")
+    ap.add_argument("--case", choices=["gemv", "group", "gemm", "swiglu"],
+                    help="time one workload alone (see run_case)")
+    ap.add_argument("--dtype", type=int, default=FP4, help="--case: 16 FP4, 4 E4M3, 5 E5M2, 9 Int8")
+    ap.add_argument("--rows", type=int, default=4096)
+    ap.add_argument("--cols", type=int, default=4096)
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--x", choices=["f32", "bf16"], default="f32")
     ap.add_argument("--reps", type=int, default=5)
     args = ap.parse_args()
-    if args.case in ("sharded", "pipeline"):
-        return run_case_multi(args)
     if args.case:
         return run_case(args)
     if args.impl == "reference":

@@ -211,6 +211,80 @@ WELVET_API welvet_status welvet_b200_volume_cell_outputs(welvet_b200_volume* v, 
                                                          int32_t* post_width);
 WELVET_API void welvet_b200_volume_release(welvet_b200_volume* v);
 
+/* ---------------------------------------------------------------- multi-GPU (one box)
+ *
+ * No counterpart in the reference, which runs every kernel on device 0
+ * (src/cuda/device.cpp:40-61). One process per GPU; the processes of a job form a
+ * communicator (NCCL, loaded at run time: libnccl.so.2, or the path in WELVET_B200_NCCL).
+ * Collective calls (marked so) must be made by every rank, in the same order. */
+
+typedef struct welvet_b200_comm welvet_b200_comm;
+/* 1 when NCCL could be loaded into this process, else 0 (the comm calls then return 2). */
+WELVET_API int32_t welvet_b200_nccl_available(void);
+/* A new job id (ncclGetUniqueId): 128 bytes that rank 0 makes and hands to every rank. */
+WELVET_API welvet_status welvet_b200_comm_unique_id(uint8_t* id128);
+/* Collective: this process becomes `rank` of `nranks` on CUDA device `device`. */
+WELVET_API welvet_status welvet_b200_comm_create(const uint8_t* id128, int32_t nranks, int32_t rank,
+                                                 int32_t device, welvet_b200_comm** out);
+WELVET_API void welvet_b200_comm_release(welvet_b200_comm* c);
+
+/* Output rows [*begin, *end) that `rank` holds of a column-sharded layer with `rows` outputs:
+ * whole 128-row blocks dealt in rank order (host arithmetic only). */
+WELVET_API welvet_status welvet_b200_shard_rows(int32_t rows, int32_t nranks, int32_t rank, int32_t* begin,
+                                                int32_t* end);
+/* Hops [*hop_begin, *hop_end) of a volume of `cells` cells x `layers_per_cell` that `rank` runs
+ * in the cell-per-GPU pipeline: whole cells, contiguous in hop order (host arithmetic only). */
+WELVET_API welvet_status welvet_b200_stage_plan(int32_t cells, int32_t layers_per_cell, int32_t nranks,
+                                                int32_t rank, int32_t* hop_begin, int32_t* hop_end);
+
+/* A Dense layer (in -> out) too large for one GPU, split by output rows over the ranks of
+ * `comm`: this rank passes its rows W_rows [end - begin][in] (welvet_b200_shard_rows; host or
+ * device pointer per weights_on_device) and the whole layer's bias (host, rows o < bias_len).
+ * mode 0: each rank's kernels store its columns of the output straight into every rank's
+ * output buffer over NVLink peer memory, then the ranks exchange one flag each; mode 1: local
+ * forward, then ncclAllGather and a permute (the library baseline). Collective. */
+typedef struct welvet_b200_sharded_dense welvet_b200_sharded_dense;
+WELVET_API welvet_status welvet_b200_sharded_dense_mount(welvet_b200_comm* comm, int32_t batch, int32_t in,
+                                                         int32_t out, int32_t act, int32_t dtype,
+                                                         const float* W_rows, int32_t weights_on_device,
+                                                         const double* bias, size_t bias_len, int32_t mode,
+                                                         welvet_b200_sharded_dense** s);
+/* Collective. One forward of x_dev [batch][in] (the same x on every rank), asynchronous on
+ * `stream`: *post_dev receives the library-owned device buffer holding the whole output
+ * [batch][out] on this rank once the stream gets there, *pre_dev that of pre -- the same
+ * buffer for a Linear layer without bias, else a buffer with this rank's columns of pre (the
+ * others zero). The buffers of one call stay valid until the call after next. */
+WELVET_API welvet_status welvet_b200_sharded_dense_execute_device(welvet_b200_sharded_dense* s,
+                                                                  const float* x_dev, void* stream,
+                                                                  const float** post_dev,
+                                                                  const float** pre_dev);
+/* Collective, synchronous: host x [batch][in] in, host pre / post [batch][out] out (either may
+ * be NULL), like welvet_dense_execute. */
+WELVET_API welvet_status welvet_b200_sharded_dense_execute(welvet_b200_sharded_dense* s, const float* x,
+                                                           float* pre, float* post);
+/* Synchronizes `stream`; status 4 if a rank did not reach an output exchange within the wait
+ * limit (WELVET_B200_SHARD_WAIT_MS, default 5000) or a tensor-core pipeline wait timed out. */
+WELVET_API welvet_status welvet_b200_sharded_dense_check_error(welvet_b200_sharded_dense* s, void* stream);
+/* This rank's output rows. */
+WELVET_API welvet_status welvet_b200_sharded_dense_rows(welvet_b200_sharded_dense* s, int32_t* row_begin,
+                                                        int32_t* row_end);
+WELVET_API void welvet_b200_sharded_dense_release(welvet_b200_sharded_dense* s);
+
+/* Collective. The cell-per-GPU pipeline of a volume forward (reference
+ * runtime::forward::volume_dense, src/runtime/forward.cpp:98-156, placed over GPUs): this rank
+ * runs hops [hop_begin, hop_end) (welvet_b200_stage_plan) of `v` on micro-batches of `micro`
+ * rows; rank 0 reads x_dev [rows][stage_in_width], every other rank receives its stage input
+ * (width stage_in_width) from the rank before and sends its stage output to the rank after
+ * (NCCL point-to-point); the last rank's output is broadcast, so out_dev [rows][out_width]
+ * holds the volume's output on every rank. Rows are independent through the cells, so the
+ * result equals the one-GPU forward of the same micro-batches. Remote links must stay within
+ * a rank's hops. Asynchronous on `stream`. */
+WELVET_API welvet_status welvet_b200_volume_pipeline_forward_device(welvet_b200_volume* v, welvet_b200_comm* comm,
+                                                                    int32_t hop_begin, int32_t hop_end, int32_t rows,
+                                                                    const float* x_dev, int32_t stage_in_width,
+                                                                    int32_t micro, float* out_dev,
+                                                                    int32_t out_width, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -128,3 +128,26 @@ def test_oracle_vs_reference_live(oracle):
             assert np.array_equal(raw_r, raw_o) and sc_r == sc_o
             dec_r = oracle.ref_decode(dt, raw_r, sc_r, rows, cols)
             assert np.array_equal(dec_r.ravel(), oracle.decode(dt, raw_o, sc_o, rows * cols))
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(batch=2, seq=6, nh=4, nkv=2, hd=8, msl=8, mask=1, pos=0),   # ring wraps across batches
+    dict(batch=1, seq=5, nh=3, nkv=3, hd=8, msl=16, mask=2, pos=2),  # bidirectional + ALiBi
+    dict(batch=3, seq=4, nh=2, nkv=1, hd=16, msl=4, mask=1, pos=3),  # RoPE + ALiBi, GQA, msl == seq
+    dict(batch=3, seq=5, nh=2, nkv=2, hd=4, msl=7, mask=1, pos=0),   # msl not a multiple of seq
+])
+def test_attention_rows_matches_the_loop_restatement(cfg):
+    """oracle.attention.attention_rows (numpy, selected query rows: the config-size checks) gives
+    the same floats as the sequential-loop restatement of the reference attention core."""
+    from oracle.attention import attention, attention_rows
+    rng = np.random.default_rng(12)
+    c = cfg
+    T = c["batch"] * c["seq"]
+    q = rng.standard_normal((T, c["nh"] * c["hd"])).astype(np.float32)
+    k = rng.standard_normal((T, c["nkv"] * c["hd"])).astype(np.float32)
+    v = rng.standard_normal((T, c["nkv"] * c["hd"])).astype(np.float32)
+    args = (c["batch"], c["seq"], c["nh"], c["nkv"], c["hd"], c["msl"], c["mask"], c["pos"])
+    full = attention(q, k, v, *args)
+    rows = [0, T // 2, T - 1]
+    got = attention_rows(q[rows], k, v, rows, *args)
+    np.testing.assert_allclose(got, full[rows], rtol=1e-6, atol=1e-7)

@@ -93,4 +93,14 @@ inline Status cuda_status(cudaError_t e, const char* what) {
 
 inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
+// Further destinations of a layer's post, besides the local one: a column-sharded layer
+// (sharded.hpp) writes its slice of the output straight into the other ranks' gathered
+// buffers over NVLink peer memory. Each pointer has the local post's layout ([M][ld_out],
+// offset to the shard's first column). n = 0: the layer writes only its own outputs.
+constexpr int kMaxPeerOut = 7;
+struct PeerOut {
+  int n = 0;
+  float* post[kMaxPeerOut] = {};
+};
+
 } // namespace wb

@@ -244,8 +244,13 @@ Status alloc_io(const DeviceDense& d, int batch, DenseIO* io, cudaStream_t st) {
 }
 
 Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x_ld, float* pre,
-                      float* post, DenseIO* io, cudaStream_t st, bool pdl) {
+                      float* post, DenseIO* io, cudaStream_t st, bool pdl, int64_t ld_out,
+                      const PeerOut* peers) {
   if (batch <= 0 || !x || !pre || !post) return Status::Invalid("null execute args");
+  if (ld_out <= 0) ld_out = d.rows;
+  if (ld_out < d.rows) return Status::Invalid("dense: output pitch below the layer's rows");
+  const PeerOut no_peers{};
+  const PeerOut& pe = peers ? *peers : no_peers;
   const float* xs = x;  // the tensor-core paths read x in any layout
   int64_t xst = x_ld;
   const bool pdl_in = pdl;
@@ -263,7 +268,8 @@ Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x
     g.M = batch;
     g.pre = pre;
     g.post = post;
-    g.ld_out = d.rows;
+    g.ld_out = ld_out;
+    g.peers = pe;
     g.bias = d.bias;
     g.bias_len = d.bias_len;
     g.act = d.act;
@@ -286,7 +292,8 @@ Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x
     g.batch = batch;
     g.pre = pre;
     g.post = post;
-    g.ld_out = d.rows;
+    g.ld_out = ld_out;
+    g.peers = pe;
     g.bias = d.bias;
     g.bias_len = d.bias_len;
     g.act = d.act;
@@ -317,7 +324,8 @@ Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x
   a.batch = batch;
   a.pre = pre;
   a.post = post;
-  a.ld_out = d.rows;
+  a.ld_out = ld_out;
+  a.peers = pe;
   a.bias = d.bias;
   a.bias_len = d.bias_len;
   a.act = d.act;

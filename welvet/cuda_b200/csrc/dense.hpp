@@ -108,8 +108,11 @@ Status check_pipeline_error(DenseIO& io, cudaStream_t st);
 
 // y = Dense(x) on the device: x [batch][x_ld] (any alignment; staged into io.x when it is
 // not already padded), outputs [batch][rows] into pre/post (device pointers).
+// `ld_out` (0: rows) is the row pitch of pre/post; `peers` (may be nullptr) lists further
+// destinations of post with the same layout (column-sharded layers, sharded.hpp).
 Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x_ld, float* pre,
-                      float* post, DenseIO* io, cudaStream_t st, bool pdl);
+                      float* post, DenseIO* io, cudaStream_t st, bool pdl, int64_t ld_out = 0,
+                      const PeerOut* peers = nullptr);
 
 struct DenseSession {
   int device = 0;

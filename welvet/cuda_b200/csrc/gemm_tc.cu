@@ -66,6 +66,7 @@ struct KParams {
   int pair;                    // SwiGLU Gate/Up pair reduce (see TmParams)
   float* h;
   int64_t ld_h;
+  PeerOut peers;               // further destinations of post (column-sharded layers)
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
@@ -218,7 +219,9 @@ __device__ __forceinline__ void write_out(const Params& p, int t, int o, double 
     pre = static_cast<float>(v);
   }
   p.pre[idx] = pre;
-  p.post[idx] = static_cast<float>(activate(p.act, v));
+  const float post = static_cast<float>(activate(p.act, v));
+  p.post[idx] = post;
+  for (int i = 0; i < p.peers.n; ++i) p.peers.post[i][idx] = post;
 }
 
 template <int kDt>
@@ -427,6 +430,14 @@ struct TmParams {
   int tiles_t, tail_first, tail_s, tail_kbps;
   int tiles, n_items;           // work items: tiles (x splits), or whole tiles then tail slices
   uint32_t acc_buf;             // columns of one accumulator buffer when there are two, else 0
+  PeerOut peers;                // further destinations of post (direct stores)
+  int n_peer_maps;              // staged stores: peer maps in PeerMaps (post's layout)
+};
+
+// Tensor maps of the peers' post buffers (column-sharded layers): a staged chunk's post values
+// are also bulk-stored through each of them, straight into the other ranks' memory.
+struct PeerMaps {
+  CUtensorMap m[kMaxPeerOut];
 };
 
 // Token blocks whose plane counts a CTA keeps in shared memory (more blocks: every block runs
@@ -628,7 +639,7 @@ template <int kDt, bool kPair>
 __global__ void __launch_bounds__(kTmThreads, 1)
     k_gemm_tm(const __grid_constant__ CUtensorMap tm_x1, const __grid_constant__ CUtensorMap tm_x2,
               const __grid_constant__ CUtensorMap tm_x3, const __grid_constant__ CUtensorMap tm_o1,
-              const __grid_constant__ CUtensorMap tm_o2, const TmParams p) {
+              const __grid_constant__ CUtensorMap tm_o2, const __grid_constant__ PeerMaps pm, const TmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = p.sx, Sw = p.sw;
@@ -1078,6 +1089,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
                 const int64_t idx = static_cast<int64_t>(t_pass + tc + e) * p.ld_out + o;
                 p.pre[idx] = a;
                 p.post[idx] = b;
+                for (int i = 0; i < p.peers.n; ++i) p.peers.post[i][idx] = b;
               }
             }
           } else {
@@ -1097,6 +1109,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
                 const int64_t idx = static_cast<int64_t>(t) * p.ld_out + o;
                 p.pre[idx] = a;
                 p.post[idx] = b;
+                for (int i = 0; i < p.peers.n; ++i) p.peers.post[i][idx] = b;
               }
             }
           }
@@ -1112,6 +1125,8 @@ __global__ void __launch_bounds__(kTmThreads, 1)
               } else {
                 tma_store_2d(&tm_o1, s1, mt * 128, ty, pol);
                 if (p.tma_post) tma_store_2d(&tm_o2, s2, mt * 128, ty, pol);
+                // column-sharded layers: the same post values into every other rank's buffer
+                for (int i = 0; i < p.n_peer_maps; ++i) tma_store_2d(&pm.m[i], p.tma_post ? s2 : s1, mt * 128, ty, pol);
               }
               asm volatile("cp.async.bulk.commit_group;" ::: "memory");
             }
@@ -1125,8 +1140,16 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         }
       }
     }
-    // the staging buffers stay valid until the last stores have read them
-    if (q == 0 && lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    // the staging buffers stay valid until the last stores have read them; stores into other
+    // ranks' memory are waited for in full, so that they are complete when the grid is
+    if (q == 0 && lane == 0) {
+      if (p.n_peer_maps > 0) {
+        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+      } else {
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      }
+    }
   }
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -1188,6 +1211,7 @@ struct TailParams {
   int pair;
   float* h;
   int64_t ld_h;
+  PeerOut peers;
 };
 
 __global__ void k_tail_reduce(const TailParams p) {
@@ -1685,7 +1709,7 @@ Status set_max_smem(const void* kern, size_t bytes) {
   return Status::Ok();
 }
 
-using TmKernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, TmParams);
+using TmKernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, PeerMaps, TmParams);
 
 TmKernel tm_kernel(DType dt, bool pair) {
   switch (dt) {
@@ -1825,6 +1849,26 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
     p.tma_out = ok ? 1 : 0;
     if (!ok) p.tma_post = 0;
   }
+  // Column-sharded layers: post also goes to the peers -- through bulk tensor stores of the
+  // staged chunks (one map per peer, post's layout) and direct stores everywhere else. If a
+  // map cannot be made, every output takes the direct-store path.
+  PeerMaps pm{};
+  p.peers = a.peers;
+  p.n_peer_maps = 0;
+  if (p.tma_out && a.peers.n > 0) {
+    bool ok = !a.pair;
+    for (int i = 0; ok && i < a.peers.n; ++i)
+      ok = (reinterpret_cast<uintptr_t>(a.peers.post[i]) & 15) == 0 &&
+           make_map_2d(&pm.m[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.peers.post[i], static_cast<uint64_t>(a.rows),
+                       static_cast<uint64_t>(a.M), static_cast<uint64_t>(a.ld_out) * 4, kBM, 16,
+                       CU_TENSOR_MAP_SWIZZLE_NONE).ok();
+    if (ok) {
+      p.n_peer_maps = a.peers.n;
+    } else {
+      p.tma_out = 0;
+      p.tma_post = 0;
+    }
+  }
 
   const size_t smem = pl.smem;
   // persistent: one CTA per SM (or per item when there are fewer), each looping over items
@@ -1842,10 +1886,10 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
     cudaLaunchAttribute at[1];
     const cudaLaunchConfig_t cfg =
         pair_config(static_cast<unsigned>(p.n_items < pairs ? p.n_items : pairs), smem, st, at);
-    WB_CUDA(cudaLaunchKernelEx(&cfg, kern, tm_x[0], tm_x[1], tm_x[2], tm_o[0], tm_o[1], p));
+    WB_CUDA(cudaLaunchKernelEx(&cfg, kern, tm_x[0], tm_x[1], tm_x[2], tm_o[0], tm_o[1], pm, p));
   } else {
     const dim3 grid(static_cast<unsigned>(p.n_items < sms ? p.n_items : sms), 1, 1);
-    kern<<<grid, kTmThreads, smem, st>>>(tm_x[0], tm_x[1], tm_x[2], tm_o[0], tm_o[1], p);
+    kern<<<grid, kTmThreads, smem, st>>>(tm_x[0], tm_x[1], tm_x[2], tm_o[0], tm_o[1], pm, p);
     WB_TRY(cuda_status(cudaGetLastError(), "gemm_tc (tmem) launch"));
   }
   if (pl.tail_first >= 0) {
@@ -1856,6 +1900,7 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
     r.scale_inv = scale_inv; r.int8 = a.dtype == DType::Int8 ? 1 : 0; r.w_scale = a.scale; r.w_scale2 = a.scale2;
     r.pre = a.pre; r.post = a.post; r.ld_out = a.ld_out; r.bias = a.bias; r.bias_len = a.bias_len; r.act = a.act;
     r.pair = a.pair ? 1 : 0; r.h = a.h; r.ld_h = a.ld_h;
+    r.peers = a.peers;
     const int64_t n = static_cast<int64_t>(ntail) * r.sub * pl.TB * (a.pair ? 64 : 128);
     k_tail_reduce<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(r);
     WB_CUDA(cudaGetLastError());
@@ -1865,6 +1910,7 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
     r.rows = a.rows; r.M = a.M; r.splits = pl.splits; r.partial = partial;
     r.pre = a.pre; r.post = a.post; r.ld_out = a.ld_out; r.bias = a.bias; r.bias_len = a.bias_len; r.act = a.act;
     r.pair = a.pair ? 1 : 0; r.h = a.h; r.ld_h = a.ld_h;
+    r.peers = a.peers;
     const int64_t n = static_cast<int64_t>(a.M) * a.rows;
     int blocks = static_cast<int>((n + 255) / 256);
     if (blocks > 148 * 16) blocks = 148 * 16;
@@ -1910,6 +1956,7 @@ Status launch_smem(const GemmArgs& a, cudaStream_t st) {
   p.stages = pl.stages;
   p.scale_inv = scale_inv;
   p.w_scale = a.scale;
+  p.peers = a.peers;
   p.pre = a.pre; p.post = a.post; p.ld_out = a.ld_out;
   p.bias = a.bias; p.bias_len = a.bias_len; p.act = a.act;
   p.partial = partial;

@@ -44,6 +44,8 @@ struct GemmArgs {
   float scale2 = 1.0f;
   float* h = nullptr;           // [M][ld_h]
   int64_t ld_h = 0;
+  // Further destinations of post (column-sharded layers, peer memory): same layout as post.
+  PeerOut peers;
 };
 
 // Token tile (B rows per plane) used for M tokens; the MMA N is xsplit * tile.

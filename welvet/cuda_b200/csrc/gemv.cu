@@ -278,7 +278,9 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv(const GemvArgs a) {
               pre = static_cast<float>(v);
             }
             a.pre[idx] = pre;
-            a.post[idx] = static_cast<float>(activate(a.act, v));
+            const float post = static_cast<float>(activate(a.act, v));
+            a.post[idx] = post;
+            for (int i = 0; i < a.peers.n; ++i) a.peers.post[i][idx] = post;
           } else {
             double up = acc2[r][b];
             if (kDt == 9 && !kExact) up *= static_cast<double>(a.scale2);

@@ -27,6 +27,7 @@ struct GemvArgs {
   int bias_len = 0;
   int act = -1;
   bool exact = false;           // fp64 products and accumulation (small layers)
+  PeerOut peers;                // further destinations of post (column-sharded layers)
 };
 
 // Elements covered by 16 bytes of the mirror.

@@ -28,6 +28,7 @@
 
 #include <cooperative_groups.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <tuple>
 #include <vector>
@@ -64,6 +65,23 @@ Plan make_plan(DType dt, int rows, int cols, bool grouped = false) {
   // then takes about half of the GPU's CTA slots, so the next launch can co-reside and
   // prefetch its weights.
   p.cpw = static_cast<int>((p.chunks + kWarps * kMaxCluster - 1) / (kWarps * kMaxCluster));
+  if (!grouped) {
+    // A layer with many row sets fills the GPU by itself: give each CTA a longer K range
+    // (fewer CTAs, each paying its fixed x-staging / reduction cost over more bytes) while
+    // keeping at least two waves of CTAs for balance (4 CTAs per SM).
+    constexpr int64_t kMinCtas = 2 * 148 * 4;
+    for (int c = 16; c > p.cpw; c >>= 1) {
+      const int64_t cs = (p.chunks + kWarps * c - 1) / (kWarps * c);
+      if (p.row_sets * cs >= kMinCtas) {
+        p.cpw = c;
+        break;
+      }
+    }
+  }
+  if (const char* env = std::getenv("WELVET_B200_GEMV_CPW")) {  // tuning override (chunks per warp)
+    const int c = std::atoi(env);
+    if (c >= 1 && c <= 64 && (p.chunks + kWarps * c - 1) / (kWarps * c) <= kMaxCluster) p.cpw = c;
+  }
   if (grouped) {
     const int64_t per_warp = (p.chunks + kWarps - 1) / kWarps;
     const int longer = static_cast<int>(per_warp < 8 ? per_warp : 8);
@@ -96,6 +114,7 @@ struct KArgs {
   int act;
   const uint2* frags;   // prepared B fragments [csize * nkb_cta][2 kB][4] (nullptr: built per CTA)
   const float* fscale;  // prepared 2^-e per K segment and token [csize][kB]
+  PeerOut peers;        // further destinations of post (column-sharded layers)
 };
 
 __device__ __forceinline__ uint4 ld_stream(const uint8_t* p) {
@@ -201,7 +220,9 @@ __device__ __forceinline__ void write_out(const Args& a, int o, int b, double y,
       pre = static_cast<float>(v);
     }
     a.pre[idx] = pre;
-    a.post[idx] = static_cast<float>(activate(a.act, v));
+    const float post = static_cast<float>(activate(a.act, v));
+    a.post[idx] = post;
+    for (int i = 0; i < a.peers.n; ++i) a.peers.post[i][idx] = post;
   } else {
     const float gate_pre = static_cast<float>(y);
     const float up_post = static_cast<float>(y2);
@@ -777,6 +798,7 @@ Status launch_gemv_tc(const GemvTcArgs& a, cudaStream_t st, bool pdl) {
   k.bias = a.bias;
   k.bias_len = a.bias_len;
   k.act = a.act;
+  k.peers = a.peers;
   GroupArgs<1> g{};
   g.a = k;
   return a.Wt2 ? launch_d<true, 1>(a.dtype, g, 1, pl, a.batch, st, pdl)

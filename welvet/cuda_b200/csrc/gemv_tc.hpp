@@ -46,6 +46,7 @@ struct GemvTcArgs {
   const double* bias = nullptr;
   int bias_len = 0;
   int act = -1;
+  PeerOut peers;                 // further destinations of post (column-sharded layers)
 };
 
 // Launches on `st` with a thread-block cluster per 64-row set (split-K reduced in

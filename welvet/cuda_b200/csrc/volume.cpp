@@ -224,12 +224,19 @@ Status volume_set_disabled(Volume* v, int idx, bool disabled) {
 Status volume_forward_device(Volume* v, int rows, const float* x, int in_width, int hop_begin, int hop_end,
                              float* out, int* out_width, cudaStream_t st) {
   if (!v) return Status::Invalid("runtime.forward: nil volume");
+  return volume_forward_range(v, rows, x, in_width, hop_begin, hop_end, out, out_width, st,
+                              hop_begin <= 0 || v->epoch == 0, nullptr);
+}
+
+Status volume_forward_range(Volume* v, int rows, const float* x, int in_width, int hop_begin, int hop_end,
+                            float* out, int* out_width, cudaStream_t st, bool open, const float** last_post) {
+  if (!v) return Status::Invalid("runtime.forward: nil volume");
   if (rows <= 0 || !x || in_width <= 0) return Status::Invalid("runtime.forward: empty input");
   const int hops = volume_hops(*v);
   if (hop_begin < 0) hop_begin = 0;
   if (hop_end > hops || hop_end < 0) hop_end = hops;
   WB_CUDA(cudaSetDevice(v->device));
-  if (hop_begin == 0 || v->epoch == 0) ++v->epoch;
+  if (open) ++v->epoch;
   const float* cur = x;
   int cur_w = in_width;
   int last = -1;
@@ -276,6 +283,7 @@ Status volume_forward_device(Volume* v, int rows, const float* x, int in_width, 
   }
   if (last < 0) return Status::Invalid("runtime.forward: grid has no enabled cells with ops");
   if (out_width) *out_width = cur_w;
+  if (last_post) *last_post = cur;
   if (out) {
     WB_CUDA(cudaMemcpyAsync(out, cur, static_cast<size_t>(rows) * cur_w * 4, cudaMemcpyDeviceToDevice, st));
   }

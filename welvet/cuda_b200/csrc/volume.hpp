@@ -87,6 +87,12 @@ Status volume_set_disabled(Volume* v, int idx, bool disabled);
 Status volume_forward_device(Volume* v, int rows, const float* x, int in_width, int hop_begin, int hop_end,
                              float* out, int* out_width, cudaStream_t st);
 
+// The same over an explicit forward: `open` starts a new one (remote-link targets must then be
+// executed within this call); *last_post (may be nullptr) receives the device address of the
+// last executed cell's post, valid until that cell runs again.
+Status volume_forward_range(Volume* v, int rows, const float* x, int in_width, int hop_begin, int hop_end,
+                            float* out, int* out_width, cudaStream_t st, bool open, const float** last_post);
+
 // Device pointers of a cell's last pre / post ([rows][width]) for step records.
 Status volume_cell_outputs(Volume* v, int idx, const float** pre, int* pre_width, const float** post,
                            int* post_width);

@@ -1,16 +1,10 @@
 // volume_abi.cpp -- extern "C" entry points of the device-resident volume (volume.hpp).
-#include "../../../include/welvet_b200.h"
-
-#include "volume.hpp"
+#include "abi_handles.hpp"
 
 #include <cstring>
 #include <exception>
 #include <new>
 #include <string>
-
-struct welvet_b200_volume {
-  wb::Volume* v;
-};
 
 namespace {
 

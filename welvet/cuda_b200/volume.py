@@ -4,21 +4,23 @@
 architecture::Grid + runtime::forward::volume_dense, include/welvet/architecture.hpp:100-141,
 src/runtime/forward.cpp:98-156).
 
-Multi-GPU (one process per GPU, torch.distributed for the plumbing):
+Multi-GPU (one process per GPU): the library's C++ runtime does the work (NCCL loaded by the
+library, CUDA IPC peer memory over NVLink); Python only hands the 128-byte job id from rank 0
+to the others.
 
-* `stage_plan` / `PipelinedVolume` -- the volume's cells are placed one per GPU (contiguous
+* `Comm` -- the ranks of one job on the GPUs of one box.
+* `stage_plan` / `Comm.pipeline_forward` -- the volume's cells placed one per GPU (contiguous
   runs of cells in hop order when there are fewer GPUs than cells). The hop order is a
-  sequential chain, so the GPUs form a pipeline; the batch is cut into micro-batches (rows
-  are independent through Dense/ReLU cells, so results do not change) and activations move
-  between consecutive ranks with point-to-point sends.
-* `ColumnShardedDense` -- a Dense layer too large for one GPU: rank r holds rows
-  [r*out/N, (r+1)*out/N), computes its slice of y, and the slices are all-gathered.
-
-The orchestration only needs a stage runner (`run(rows, x) -> y` on the rank's device); the
-product passes the volume runtime, and the CPU tests pass a host stand-in over gloo.
+  sequential chain, so the GPUs form a pipeline: the batch is cut into micro-batches (rows
+  are independent through the cells, so results do not change) and activations move between
+  consecutive ranks with NCCL point-to-point transfers.
+* `shard_rows` / `ShardedDense` -- a Dense layer too large for one GPU: rank r holds whole
+  128-row blocks of its output rows; its kernels store its columns of the output straight into
+  every rank's output buffer (mode FUSED) or all-gather after the local forward (mode NCCL).
 """
 from __future__ import annotations
 
+import ctypes
 from ctypes import POINTER, byref, c_double, c_float, c_int32, c_size_t, c_void_p
 
 from . import _L, _ST, _dev_ptr, _f32, _np_ptr, _sig, _stream_ptr, check
@@ -150,19 +152,49 @@ class Volume:
             pass
 
 
-# ---------------------------------------------------------------------------------- placement
+# ---------------------------------------------------------------------------------- multi-GPU
+
+_sig("welvet_b200_nccl_available", c_int32)
+_sig("welvet_b200_comm_unique_id", _ST, c_void_p)
+_sig("welvet_b200_comm_create", _ST, c_void_p, c_int32, c_int32, c_int32, POINTER(c_void_p))
+_sig("welvet_b200_comm_release", None, c_void_p)
+_sig("welvet_b200_shard_rows", _ST, c_int32, c_int32, c_int32, POINTER(c_int32), POINTER(c_int32))
+_sig("welvet_b200_stage_plan", _ST, c_int32, c_int32, c_int32, c_int32, POINTER(c_int32), POINTER(c_int32))
+_sig("welvet_b200_sharded_dense_mount", _ST, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p,
+     c_int32, c_void_p, c_size_t, c_int32, POINTER(c_void_p))
+_sig("welvet_b200_sharded_dense_execute_device", _ST, c_void_p, c_void_p, c_void_p, POINTER(c_void_p),
+     POINTER(c_void_p))
+_sig("welvet_b200_sharded_dense_execute", _ST, c_void_p, c_void_p, c_void_p, c_void_p)
+_sig("welvet_b200_sharded_dense_check_error", _ST, c_void_p, c_void_p)
+_sig("welvet_b200_sharded_dense_rows", _ST, c_void_p, POINTER(c_int32), POINTER(c_int32))
+_sig("welvet_b200_sharded_dense_release", None, c_void_p)
+_sig("welvet_b200_volume_pipeline_forward_device", _ST, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p,
+     c_int32, c_int32, c_void_p, c_int32, c_void_p)
+
+FUSED, NCCL = 0, 1
+
+
+def nccl_available() -> bool:
+    return bool(_L.welvet_b200_nccl_available())
+
+
+def shard_rows(rows: int, world: int, rank: int) -> tuple[int, int]:
+    """Output rows [begin, end) rank `rank` holds of a column-sharded layer (whole 128-row
+    blocks dealt in rank order)."""
+    b, e = c_int32(), c_int32()
+    check(_L.welvet_b200_shard_rows(rows, world, rank, byref(b), byref(e)))
+    return b.value, e.value
+
 
 def stage_plan(cells: int, layers_per_cell: int, world: int) -> list[tuple[int, int]]:
-    """Hop ranges [begin, end) per rank: whole cells, one per GPU when world == cells,
-    otherwise contiguous runs of cells split as evenly as possible (earlier ranks take the
-    extra cell). Ranks beyond the cell count get an empty range."""
-    if world < 1 or cells < 1:
-        raise ValueError("stage_plan: need cells >= 1 and world >= 1")
+    """Hop ranges [begin, end) per rank of the cell-per-GPU pipeline: whole cells, one per GPU
+    when world == cells, otherwise contiguous runs of cells split as evenly as possible
+    (earlier ranks take fewer). Ranks beyond the cell count get an empty range."""
     out = []
     for r in range(world):
-        c0 = cells * r // world if world <= cells else min(r, cells)
-        c1 = cells * (r + 1) // world if world <= cells else min(r + 1, cells)
-        out.append((c0 * layers_per_cell, c1 * layers_per_cell))
+        b, e = c_int32(), c_int32()
+        check(_L.welvet_b200_stage_plan(cells, layers_per_cell, world, r, byref(b), byref(e)))
+        out.append((b.value, e.value))
     return out
 
 
@@ -172,91 +204,124 @@ def microbatches(rows: int, size: int) -> list[tuple[int, int]]:
     return [(r, min(r + size, rows)) for r in range(0, rows, size)]
 
 
-class PipelinedVolume:
-    """Cell-per-GPU pipeline over torch.distributed.
+class _DevView:
+    """A library-owned device buffer seen as a torch tensor (no copy)."""
 
-    `runner(x) -> y` runs this rank's hop range on a [mb][in] tensor of its device and
-    returns a [mb][out] tensor. Rank 0 feeds the input, rank world-1 produces the output,
-    which `forward` returns on every rank after a broadcast from the last rank (so that the
-    caller sees the result where it called). Sends are issued as each micro-batch finishes
-    (isend), so rank r works on micro-batch i+1 while rank r+1 works on micro-batch i.
-    """
-
-    def __init__(self, runner, in_width: int, out_widths: list[int], group=None):
-        import torch.distributed as dist
-        self.dist = dist
-        self.runner = runner
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
-        self.group = group
-        self.in_width = in_width
-        self.out_widths = out_widths  # output width of every rank's stage
-
-    def forward(self, x, micro: int):
-        import torch
-        dist = self.dist
-        rank, world = self.rank, self.world
-        rows = x.shape[0]
-        dev = x.device
-        width_in = self.in_width if rank == 0 else self.out_widths[rank - 1]
-        outs = []
-        pending = []
-        for (a, b) in microbatches(rows, micro):
-            if rank == 0:
-                xin = x[a:b].contiguous()
-            else:
-                xin = torch.empty((b - a, width_in), dtype=torch.float32, device=dev)
-                dist.recv(xin, src=rank - 1, group=self.group)
-            y = self.runner(xin)
-            if rank < world - 1:
-                pending.append(dist.isend(y.contiguous(), dst=rank + 1, group=self.group))
-            else:
-                outs.append(y)
-        for p in pending:
-            p.wait()
-        ow = self.out_widths[-1]
-        if rank == world - 1:
-            result = torch.cat(outs, dim=0).contiguous()
-        else:
-            result = torch.empty((rows, ow), dtype=torch.float32, device=dev)
-        if world > 1:
-            dist.broadcast(result, src=world - 1, group=self.group)
-        return result
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f4", "data": (ptr, False),
+                                         "version": 3, "strides": None}
 
 
-class ColumnShardedDense:
-    """A Dense layer out x in split by output rows over the ranks of a group.
+def device_tensor(ptr: int, shape):
+    import torch
+    return torch.as_tensor(_DevView(ptr, shape), device="cuda")
 
-    `local(x) -> y_slice` computes this rank's [rows][out/N] slice (the product passes a
-    DenseSession mounted on the rank's rows); `forward` all-gathers the slices into
-    [rows][out] on every rank (NCCL over NVLink on B200 ranks)."""
 
-    def __init__(self, local, out: int, group=None):
-        import torch.distributed as dist
-        self.dist = dist
-        self.local = local
-        self.group = group
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
-        if out % self.world != 0:
-            raise ValueError("ColumnShardedDense: out must be divisible by the number of ranks")
-        self.out = out
-        self.shard = out // self.world
+class Comm:
+    """This process as rank `rank` of `world` on CUDA device `device` (collective)."""
+
+    def __init__(self, rank: int, world: int, device: int, job_id: bytes):
+        if len(job_id) != 128:
+            raise ValueError("job id must be 128 bytes")
+        self._h = c_void_p()
+        buf = (ctypes.c_uint8 * 128).from_buffer_copy(job_id)
+        check(_L.welvet_b200_comm_create(buf, world, rank, device, byref(self._h)))
+        self.rank, self.world, self.device = rank, world, device
 
     @staticmethod
-    def shard_rows(out: int, world: int, rank: int) -> tuple[int, int]:
-        s = out // world
-        return rank * s, (rank + 1) * s
+    def new_job_id() -> bytes:
+        buf = (ctypes.c_uint8 * 128)()
+        check(_L.welvet_b200_comm_unique_id(buf))
+        return bytes(buf)
 
-    def forward(self, x):
-        import torch
-        y = self.local(x).contiguous()  # [rows][shard]
-        if self.world == 1:
-            return y
-        rows = y.shape[0]
-        # [world*rows][shard]: rank slices concatenated along dim 0 (the layout every backend accepts)
-        gathered = torch.empty((self.world * rows, self.shard), dtype=y.dtype, device=y.device)
-        self.dist.all_gather_into_tensor(gathered, y, group=self.group)
-        if rows == 1:
-            return gathered.view(1, self.out)
-        return gathered.view(self.world, rows, self.shard).permute(1, 0, 2).reshape(rows, self.out)
+    @classmethod
+    def from_torch(cls, device: int, group=None) -> "Comm":
+        """The ranks of a torch.distributed group (any backend): rank 0 makes the job id and
+        the group hands it to the others; the communicator itself is the library's."""
+        import torch.distributed as dist
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        obj = [cls.new_job_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0, group=group)
+        return cls(rank, world, device, obj[0])
+
+    def pipeline_forward(self, volume: "Volume", hop_range, x, stage_in_width: int, micro: int, out,
+                         stream=None) -> None:
+        """Collective: the cell-per-GPU pipeline forward (see the module docstring). x (rank 0)
+        is a CUDA tensor [rows][width]; out [rows][out width] receives the volume's output on
+        every rank."""
+        b, e = hop_range
+        rows = out.shape[0]
+        check(_L.welvet_b200_volume_pipeline_forward_device(
+            volume._h, self._h, b, e, rows, None if x is None else c_void_p(_dev_ptr(x)), stage_in_width, micro,
+            c_void_p(_dev_ptr(out)), out.shape[1], _stream_ptr(stream)))
+
+    def release(self):
+        if self._h:
+            _L.welvet_b200_comm_release(self._h)
+            self._h = c_void_p()
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+
+class ShardedDense:
+    """A Dense layer in -> out split by output rows over the ranks of `comm` (collective).
+    W_rows: this rank's rows (shard_rows), a CUDA tensor or host array [end - begin][in];
+    bias: the whole layer's (host, applies to rows o < len(bias))."""
+
+    def __init__(self, comm: Comm, W_rows, in_: int, out: int, batch: int, dtype: int, act: int = -1, bias=None,
+                 mode: int = FUSED):
+        import numpy as np
+        self._h = c_void_p()
+        p, dev, self._keep = _wptr(W_rows)
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float64)
+        check(_L.welvet_b200_sharded_dense_mount(comm._h, batch, in_, out, act, dtype, p, dev, _np_ptr(b),
+                                                 0 if b is None else b.size, mode, byref(self._h)))
+        self._keep = None
+        self.comm, self.batch, self.in_, self.out = comm, batch, in_, out
+
+    @property
+    def rows(self) -> tuple[int, int]:
+        b, e = c_int32(), c_int32()
+        check(_L.welvet_b200_sharded_dense_rows(self._h, byref(b), byref(e)))
+        return b.value, e.value
+
+    def execute_device_ptrs(self, x, stream=None) -> tuple[int, int]:
+        """Collective, asynchronous: (post, pre) device addresses of the whole output
+        [batch][out] on this rank (valid until the call after next)."""
+        post, pre = c_void_p(), c_void_p()
+        check(_L.welvet_b200_sharded_dense_execute_device(self._h, c_void_p(_dev_ptr(x)), _stream_ptr(stream),
+                                                          byref(post), byref(pre)))
+        return post.value, pre.value
+
+    def execute_device(self, x, stream=None):
+        """Collective: (post, pre) as torch tensors viewing the library's buffers."""
+        post, pre = self.execute_device_ptrs(x, stream)
+        shape = (self.batch, self.out)
+        return device_tensor(post, shape), device_tensor(pre, shape)
+
+    def execute(self, x):
+        """Collective, synchronous, host buffers: (pre, post) numpy [batch][out]."""
+        import numpy as np
+        x = _f32(x)
+        pre = np.zeros((self.batch, self.out), np.float32)
+        post = np.zeros((self.batch, self.out), np.float32)
+        check(_L.welvet_b200_sharded_dense_execute(self._h, _np_ptr(x), _np_ptr(pre), _np_ptr(post)))
+        return pre, post
+
+    def check_error(self, stream=None) -> None:
+        check(_L.welvet_b200_sharded_dense_check_error(self._h, _stream_ptr(stream)))
+
+    def release(self):
+        if self._h:
+            _L.welvet_b200_sharded_dense_release(self._h)
+            self._h = c_void_p()
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
