@@ -692,3 +692,29 @@ def test_grouped_gemv_matches_single_launches(wb, oracle, dt, out, in_, n, monke
     check_dense(p2.cpu().numpy(), q2.cpu().numpy(), ref, -1, "mixed group")
     for s in sess + [s2]:
         s.release()
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(batch=3, seq=48, d=256, nh=4, nkv=2, hd=64, msl=64, mask=1, pos=0),     # ring wraps, GQA
+    dict(batch=3, seq=70, d=128, nh=2, nkv=2, hd=64, msl=256, mask=2, pos=3),    # bidirectional, RoPE + ALiBi
+    dict(batch=1, seq=200, d=96, nh=3, nkv=1, hd=32, msl=200, mask=1, pos=2),    # ALiBi, 3 heads on 1 KV head
+])
+def test_attention_tiled_matches_warp_kernel(wb, cfg, monkeypatch):
+    """The tiled attention core (K / V tiles gathered into shared memory, 32 queries per CTA)
+    against the per-(query, head) warp kernel it replaces: both fp64 with the same ring
+    semantics, so they differ only in summation order."""
+    monkeypatch.setenv("WELVET_B200_EXACT", "0")
+    rng = np.random.default_rng(8)
+    c = cfg
+    qd, kvd = c["nh"] * c["hd"], c["nkv"] * c["hd"]
+    Q, K, V = [(rng.standard_normal((r, c["d"])) * 0.3).astype(np.float32) for r in (qd, kvd, kvd)]
+    O = (rng.standard_normal((c["d"], qd)) * 0.3).astype(np.float32)
+    x = rng.standard_normal((c["batch"] * c["seq"], c["d"])).astype(np.float32)
+    args = (Q, K, V, O, x, c["batch"], c["seq"], c["d"], c["nh"], c["nkv"], c["hd"], c["msl"], c["mask"], c["pos"],
+            wb.FP8E4M3)
+    monkeypatch.setenv("WELVET_B200_ATTN", "tiled")
+    pre_t, post_t = wb.mha_forward_f32(*args)
+    monkeypatch.setenv("WELVET_B200_ATTN", "warp")
+    pre_w, post_w = wb.mha_forward_f32(*args)
+    np.testing.assert_allclose(pre_t, pre_w, rtol=1e-6, atol=1e-7 * np.abs(pre_w).max())
+    np.testing.assert_allclose(post_t, post_w, rtol=1e-5, atol=1e-6 * np.abs(post_w).max())

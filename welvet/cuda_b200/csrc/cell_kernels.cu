@@ -14,6 +14,9 @@
 // was applied at p'. The running max starts at -1e9 as in the reference.
 #include "cell_kernels.hpp"
 
+#include <cstdlib>
+#include <cstring>
+
 namespace wb {
 namespace {
 
@@ -209,6 +212,145 @@ __global__ void k_attention(const double* __restrict__ Qr, const double* __restr
   }
 }
 
+// The same attention, tiled: one CTA per (32 consecutive queries of one batch, head). Each
+// tile of 64 key positions k_pos has its ring rows (the latest position written to slot
+// k_pos % msl, as above) gathered once into shared memory -- K transposed, V row-major -- and
+// serves all 32 queries, instead of every (query, head) warp re-reading K and V from L2.
+// Scores, online softmax (running max from -1e9, as the reference) and the weighted V sum
+// stay in fp64. Warp w owns queries 4w .. 4w + 3; for the scores lane l takes key positions l
+// and l + 32 of the tile, for the output the head dimensions l, l + 32, l + 64, l + 96.
+constexpr int kAQ = 32, kAK = 64, kAHd = 128, kAThreads = 256;
+
+size_t attention_tiled_smem() {
+  return sizeof(double) * (kAHd * kAQ + kAHd * kAK + kAK * kAHd + kAK * kAQ) + sizeof(int) * kAK;
+}
+
+__global__ void __launch_bounds__(kAThreads, 1)
+    k_attention_tiled(const double* __restrict__ Qr, const double* __restrict__ Kr, const double* __restrict__ Vd,
+                      float* __restrict__ out, int batch, int seq, int num_heads, int num_kv, int head_dim, int msl,
+                      int mask, int use_alibi, int use_sigmoid, int window, int prefix_len, int window_causal,
+                      double scale) {
+  extern __shared__ double sm[];
+  double* Qs = sm;                  // [kAHd][kAQ]: queries' rotated Q, d-major
+  double* Kt = Qs + kAHd * kAQ;     // [kAHd][kAK]: the tile's keys, d-major
+  double* Vs = Kt + kAHd * kAK;     // [kAK][kAHd]
+  double* Ps = Vs + kAK * kAHd;     // [kAK][kAQ]: the tile's weights, key-major
+  int* prow = reinterpret_cast<int*>(Ps + kAK * kAQ);  // [kAK] ring row of each key position (-1: none)
+  const int qtiles = (seq + kAQ - 1) / kAQ;
+  const int b = blockIdx.x / qtiles, s0 = (blockIdx.x - b * qtiles) * kAQ;
+  const int h = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int nq = seq - s0 < kAQ ? seq - s0 : kAQ;
+  const int tok0 = b * seq + s0;  // global position of the tile's first query
+  const int kv_len = (b + 1) * seq;
+  const int q_dim = num_heads * head_dim, kv_dim = num_kv * head_dim;
+  const int kvh = h / (num_heads / num_kv);
+  for (int i = tid; i < kAQ * kAHd; i += kAThreads) {
+    const int q = i / kAHd, d = i - q * kAHd;
+    Qs[d * kAQ + q] = q < nq && d < head_dim ? Qr[static_cast<int64_t>(tok0 + q) * q_dim + h * head_dim + d] : 0.0;
+  }
+  const int qb = 4 * w;
+  double m[4], l[4], acc[4][4];
+  int n[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -1e9;  // the reference's initial running max
+    l[i] = 0.0;
+    n[i] = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
+  }
+  // causal: no key beyond the tile's last query position is allowed
+  const int k_end = mask == 1 ? (tok0 + nq < kv_len ? tok0 + nq : kv_len) : kv_len;
+  for (int k0 = 0; k0 < k_end; k0 += kAK) {
+    __syncthreads();  // the previous tile's K / V / P are consumed (and Qs written, first time)
+    if (tid < kAK) {
+      const int kp = k0 + tid;
+      const int slot = kp % msl;
+      prow[tid] = kp < k_end ? slot + msl * ((kv_len - 1 - slot) / msl) : -1;
+    }
+    __syncthreads();
+    for (int i = tid; i < kAK * kAHd; i += kAThreads) {
+      const int j = i / kAHd, d = i - j * kAHd;
+      const int p = prow[j];
+      const bool ok = p >= 0 && d < head_dim;
+      const int64_t off = static_cast<int64_t>(p) * kv_dim + kvh * head_dim + d;
+      Kt[d * kAK + j] = ok ? Kr[off] : 0.0;
+      Vs[j * kAHd + d] = ok ? Vd[off] : 0.0;
+    }
+    __syncthreads();
+    // scores of queries qb..qb+3 against key positions k0 + lane, k0 + lane + 32
+    double sc[4][2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sc[i][0] = sc[i][1] = 0.0;
+    for (int d = 0; d < head_dim; ++d) {
+      const double2 qa = *reinterpret_cast<const double2*>(Qs + d * kAQ + qb);
+      const double2 qc = *reinterpret_cast<const double2*>(Qs + d * kAQ + qb + 2);
+      const double k0v = Kt[d * kAK + lane], k1v = Kt[d * kAK + lane + 32];
+      sc[0][0] += qa.x * k0v; sc[0][1] += qa.x * k1v;
+      sc[1][0] += qa.y * k0v; sc[1][1] += qa.y * k1v;
+      sc[2][0] += qc.x * k0v; sc[2][1] += qc.x * k1v;
+      sc[3][0] += qc.y * k0v; sc[3][1] += qc.y * k1v;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int q_pos = tok0 + qb + i;
+      const bool qv = qb + i < nq;
+      bool ok[2];
+      double s[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int kp = k0 + lane + 32 * j;
+        ok[j] = qv && kp < k_end && attn_allow(q_pos, kp, mask, window, msl, prefix_len, window_causal);
+        s[j] = ok[j] ? sc[i][j] * scale + (use_alibi ? alibi(h, num_heads, q_pos, kp) : 0.0) : 0.0;
+      }
+      n[i] += __popc(__ballot_sync(0xffffffffu, ok[0])) + __popc(__ballot_sync(0xffffffffu, ok[1]));
+      double pw[2];
+      if (use_sigmoid) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) pw[j] = ok[j] ? 1.0 / (1.0 + exp(-s[j])) : 0.0;
+      } else {
+        const double cm = warp_max_d(fmax(ok[0] ? s[0] : -INFINITY, ok[1] ? s[1] : -INFINITY));
+        const double m_new = fmax(m[i], cm);
+        const double corr = exp(m[i] - m_new);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) pw[j] = ok[j] ? exp(s[j] - m_new) : 0.0;
+        l[i] = l[i] * corr + warp_sum_d(pw[0] + pw[1]);
+#pragma unroll
+        for (int dd = 0; dd < 4; ++dd) acc[i][dd] *= corr;
+        m[i] = m_new;
+      }
+      Ps[lane * kAQ + qb + i] = pw[0];
+      Ps[(lane + 32) * kAQ + qb + i] = pw[1];
+    }
+    __syncwarp();  // the warp's own rows of Ps
+    const int kn = k_end - k0 < kAK ? k_end - k0 : kAK;
+    for (int j = 0; j < kn; ++j) {
+      const double2 pa = *reinterpret_cast<const double2*>(Ps + j * kAQ + qb);
+      const double2 pc = *reinterpret_cast<const double2*>(Ps + j * kAQ + qb + 2);
+#pragma unroll
+      for (int dd = 0; dd < 4; ++dd) {
+        const double v = Vs[j * kAHd + lane + 32 * dd];
+        acc[0][dd] += pa.x * v;
+        acc[1][dd] += pa.y * v;
+        acc[2][dd] += pc.x * v;
+        acc[3][dd] += pc.y * v;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (qb + i >= nq) continue;
+    const double inv = (n[i] == 0 || use_sigmoid) ? 1.0 : 1.0 / l[i];
+    float* o = out + static_cast<int64_t>(tok0 + qb + i) * q_dim + h * head_dim;
+#pragma unroll
+    for (int dd = 0; dd < 4; ++dd) {
+      const int d = lane + 32 * dd;
+      if (d < head_dim) o[d] = n[i] == 0 ? 0.0f : static_cast<float>(acc[i][dd] * inv);
+    }
+  }
+}
+
 // h = float(double(float(SiLU(double(g)))) * double(up)) -- src/cuda/kernels.cu:296-305.
 __global__ void k_swiglu_product(const float* __restrict__ g, const float* __restrict__ u,
                                  float* __restrict__ h, int64_t n) {
@@ -243,8 +385,21 @@ Status launch_mha_attention(const float* q, const float* k, const float* v, doub
   WB_CUDA(cudaGetLastError());
   double scale = p.scale_override;
   if (scale <= 0.0) scale = 1.0 / sqrt(static_cast<double>(p.head_dim));
-  const int warps = bs * p.num_heads;
   const bool use_alibi = p.pos_kind == 2 || p.pos_kind == 3;
+  const char* env = std::getenv("WELVET_B200_ATTN");
+  if (p.head_dim <= kAHd && !(env && std::strcmp(env, "warp") == 0)) {
+    const size_t smem = attention_tiled_smem();
+    // per device (the attribute belongs to the current device's context); a cheap host call
+    WB_CUDA(cudaFuncSetAttribute(k_attention_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem)));
+    const dim3 grid(static_cast<unsigned>(p.batch * ((p.seq + kAQ - 1) / kAQ)), static_cast<unsigned>(p.num_heads));
+    k_attention_tiled<<<grid, kAThreads, smem, st>>>(Qr, Kr, Vd, out, p.batch, p.seq, p.num_heads, p.num_kv,
+                                                     p.head_dim, p.max_seq_len, p.mask, use_alibi ? 1 : 0,
+                                                     p.softmax_kind == 1 ? 1 : 0, p.window, p.prefix_len,
+                                                     p.window_causal, scale);
+    return cuda_status(cudaGetLastError(), "attention launch");
+  }
+  const int warps = bs * p.num_heads;
   k_attention<<<(warps + 3) / 4, 128, 0, st>>>(Qr, Kr, Vd, out, p.batch, p.seq, p.num_heads, p.num_kv,
                                               p.head_dim, p.max_seq_len, p.mask, use_alibi ? 1 : 0,
                                               p.softmax_kind == 1 ? 1 : 0, p.window, p.prefix_len,

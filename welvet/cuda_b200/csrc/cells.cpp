@@ -92,14 +92,19 @@ Status swiglu_mount_src(int device, int in, int inter, DType dt, const WeightSrc
   return Status::Ok();
 }
 
-// SwiGLU's own batch split: the fused Gate/Up tensor GEMV takes 1..4 rows, the Gate/Up pair
-// GEMM (tcgen05) every larger batch of quantized, non-exact layers.
+// SwiGLU's own batch split: the fused Gate/Up tensor GEMV takes 1..4 rows; 5..16 rows run Gate
+// and Up as two tensor GEMVs (weights streamed once each, HBM-bound) and the reference's
+// product; the Gate/Up pair GEMM (tcgen05) every larger batch of quantized, non-exact layers.
 static bool swiglu_dual_gemv(const SwigluCell* c, int bs) {
   return bs <= 4 && use_gemv_tc(c->gate, bs) && c->up.Wt;
 }
+static bool swiglu_split_gemv(const SwigluCell* c, int bs) {
+  if (std::getenv("WELVET_B200_BATCHED") != nullptr) return false;
+  return bs > 4 && bs <= kGemvMaxBatch && use_gemv_tc(c->gate, bs) && use_gemv_tc(c->up, bs);
+}
 static bool swiglu_batched(const SwigluCell* c, int bs) {
   if (std::getenv("WELVET_B200_BATCHED") != nullptr) return use_tensor_path(c->gate, bs);
-  return bs > 4 && !c->gate.exact && gemm_supported(c->gate.dtype);
+  return bs > 4 && !swiglu_split_gemv(c, bs) && !c->gate.exact && gemm_supported(c->gate.dtype);
 }
 
 Status swiglu_reserve(SwigluCell* c, int bs, cudaStream_t st) {
@@ -112,7 +117,12 @@ Status swiglu_reserve(SwigluCell* c, int bs, cudaStream_t st) {
   WB_CUDA(cudaMemsetAsync(c->x_pad, 0, xb, st));
   WB_CUDA(cudaMalloc(&c->h_pad, hb));
   WB_CUDA(cudaMemsetAsync(c->h_pad, 0, hb, st));
-  if (swiglu_batched(c, bs)) {
+  if (swiglu_split_gemv(c, bs)) {
+    WB_CUDA(cudaMalloc(&c->g_buf, static_cast<size_t>(bs) * c->inter * 4));
+    WB_CUDA(cudaMalloc(&c->u_buf, static_cast<size_t>(bs) * c->inter * 4));
+    WB_TRY(alloc_io(c->gate, bs, &c->io_gate, st));  // prepared-fragment scratch of each GEMV
+    WB_TRY(alloc_io(c->up, bs, &c->io_up, st));
+  } else if (swiglu_batched(c, bs)) {
     WB_TRY(alloc_io(c->gate, bs, &c->io_gate, st));  // error word (and the unfused path's scratch)
     if (c->Wg_pair && gemm_uses_tmem()) {
       c->pair_scratch_bytes = gemm_scratch_bytes(bs, c->in, 2 * c->inter, xsplit_policy());
@@ -181,8 +191,9 @@ Status swiglu_forward_device(SwigluCell* c, int bs, const float* x, float* h, fl
     WB_TRY(launch_gemm_tc(g, st));
     hsrc = hout;
     h_ld = ld;
-  } else if (swiglu_batched(c, bs) && c->g_buf) {
-    // batched: Gate and Up on the tcgen05 GEMM, then the reference's SiLU product.
+  } else if ((swiglu_split_gemv(c, bs) || swiglu_batched(c, bs)) && c->g_buf) {
+    // 5..16 rows: Gate and Up on the tensor GEMV; batched (unfused): on the tcgen05 GEMM; then
+    // the reference's SiLU product.
     WB_TRY(forward_device(c->gate, bs, x, c->in, c->g_buf, c->g_buf, &c->io_gate, st, false));
     WB_TRY(forward_device(c->up, bs, x, c->in, c->u_buf, c->u_buf, &c->io_up, st, false));
     float* hout = h ? h : c->h_pad;

@@ -21,6 +21,28 @@ namespace wb {
 __device__ __forceinline__ uint32_t f2u(float f) { return __float_as_uint(f); }
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
 
+// ---------------------------------------------------------------- loads after griddepcontrol.wait
+//
+// A kernel launched as a programmatic dependent starts while the kernel before it still runs
+// and reads that kernel's outputs (x, prepared fragments) only after griddepcontrol.wait. The
+// read-only __ldg path tells the compiler the data never changes during the kernel, so it may
+// move such loads above the wait; these loads are volatile asm, kept in program order after it.
+__device__ __forceinline__ float ld_dep(const float* p) {
+  float v;
+  asm volatile("ld.global.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 ld_dep4(const float* p) {  // 16-byte aligned
+  float4 v;
+  asm volatile("ld.global.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint4 ld_dep4u(const void* p) {  // 16-byte aligned
+  uint4 v;
+  asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
 // ---------------------------------------------------------------- encoders (bit exact)
 
 __device__ __forceinline__ uint8_t enc_e4m3(float f) {

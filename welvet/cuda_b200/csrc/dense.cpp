@@ -73,7 +73,14 @@ void DenseIO::release() {
 bool use_gemv_tc(const DeviceDense& d, int batch) {
   const char* env = std::getenv("WELVET_B200_GEMV");
   if (env && std::strcmp(env, "simt") == 0) return false;
-  return batch >= 1 && batch <= kGemvMaxBatch && !d.exact && d.Wt != nullptr;
+  if (batch > 8) {  // 9..16 tokens: the GEMV when its prepared fragments fit (else the GEMM)
+    const char* b = std::getenv("WELVET_B200_BATCHED");
+    if (b && (std::strcmp(b, "tc") == 0)) return false;
+    const char* g16 = std::getenv("WELVET_B200_GEMV16");
+    if (g16 && g16[0] == '0') return false;
+  }
+  return batch >= 1 && batch <= kGemvMaxBatch && !d.exact && d.Wt != nullptr &&
+         gemv_tc_fits(d.dtype, d.rows, d.cols, batch);
 }
 
 // f16 planes that carry x on the batched tensor-core path. Default 2 (22 bits of x, as the
@@ -90,7 +97,7 @@ bool use_tensor_path(const DeviceDense& d, int batch) {
   const char* env = std::getenv("WELVET_B200_BATCHED");
   if (env && std::strcmp(env, "gemv") == 0) return false;
   if (env && std::strcmp(env, "tc") == 0) return !d.exact && gemm_supported(d.dtype);
-  return batch > kGemvMaxBatch && !d.exact && gemm_supported(d.dtype);
+  return batch > 8 && !use_gemv_tc(d, batch) && !d.exact && gemm_supported(d.dtype);
 }
 
 bool exact_policy(int rows, int cols) {
@@ -238,7 +245,7 @@ Status alloc_io(const DeviceDense& d, int batch, DenseIO* io, cudaStream_t st) {
     WB_CUDA(cudaMalloc(&io->scratch, io->scratch_bytes));
   }
   if (use_gemv_tc(d, batch)) {
-    if (const size_t pb = gemv_group_prep_bytes(d.dtype, d.rows, d.cols, batch)) WB_CUDA(cudaMalloc(&io->prep, pb));
+    if (const size_t pb = gemv_prep_bytes(d.dtype, d.rows, d.cols, batch)) WB_CUDA(cudaMalloc(&io->prep, pb));
   }
   return Status::Ok();
 }
@@ -280,6 +287,20 @@ Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x
     g.err = io->err;
     return launch_gemm_tc(g, st);
   }
+  if (use_gemv_tc(d, batch) && io && io->prep && gemv_prefers_prepared(d.dtype, d.rows, d.cols, batch)) {
+    // a layer that fills the GPU by itself: x prepared once, longer K ranges per CTA
+    GemvGroupLayer L;
+    L.Wt = d.Wt;
+    L.x = x;
+    L.pre = pre;
+    L.post = post;
+    L.bias = d.bias;
+    L.bias_len = d.bias_len;
+    L.act = d.act;
+    L.scale = d.scale;
+    L.prep = io->prep;
+    return launch_gemv_tc_group(d.dtype, d.rows, d.cols, batch, x_ld, ld_out, &L, 1, st, pdl_in, &pe);
+  }
   if (use_gemv_tc(d, batch)) {
     GemvTcArgs g;
     g.dtype = d.dtype;
@@ -297,6 +318,7 @@ Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x
     g.bias = d.bias;
     g.bias_len = d.bias_len;
     g.act = d.act;
+    g.prep = io ? io->prep : nullptr;
     return launch_gemv_tc(g, st, pdl_in);
   }
   // The SIMT GEMV reads x in 16-byte vectors over the padded row: stage unpadded inputs (the
@@ -595,7 +617,8 @@ Status session_execute_device_noalloc(DenseSession* s, const float* x, float* pr
   const DeviceDense& d = s->dev;
   if (!use_tensor_path(d, s->batch))
     return Status::Unsupported("allocation-free forward serves the batched tensor-core path only "
-                               "(FP8/FP4/Int8 sessions with batch > 8 outside exact mode)");
+                               "(FP8/FP4/Int8 sessions with batch > 16, or 9..16 on layers too long for the "
+                               "small-batch GEMV, outside exact mode)");
   WB_CUDA(cudaSetDevice(s->device));
   GemmArgs g;
   g.dtype = d.dtype;

@@ -221,7 +221,9 @@ __device__ __forceinline__ void write_out(const Params& p, int t, int o, double 
   p.pre[idx] = pre;
   const float post = static_cast<float>(activate(p.act, v));
   p.post[idx] = post;
-  for (int i = 0; i < p.peers.n; ++i) p.peers.post[i][idx] = post;
+#pragma unroll
+  for (int i = 0; i < kMaxPeerOut; ++i)  // static indices: the parameter stays in registers
+    if (i < p.peers.n) p.peers.post[i][idx] = post;
 }
 
 template <int kDt>
@@ -1089,7 +1091,9 @@ __global__ void __launch_bounds__(kTmThreads, 1)
                 const int64_t idx = static_cast<int64_t>(t_pass + tc + e) * p.ld_out + o;
                 p.pre[idx] = a;
                 p.post[idx] = b;
-                for (int i = 0; i < p.peers.n; ++i) p.peers.post[i][idx] = b;
+#pragma unroll
+                for (int i = 0; i < kMaxPeerOut; ++i)  // static indices: the parameter stays in registers
+                  if (i < p.peers.n) p.peers.post[i][idx] = b;
               }
             }
           } else {
@@ -1109,7 +1113,9 @@ __global__ void __launch_bounds__(kTmThreads, 1)
                 const int64_t idx = static_cast<int64_t>(t) * p.ld_out + o;
                 p.pre[idx] = a;
                 p.post[idx] = b;
-                for (int i = 0; i < p.peers.n; ++i) p.peers.post[i][idx] = b;
+#pragma unroll
+                for (int i = 0; i < kMaxPeerOut; ++i)  // static indices: the parameter stays in registers
+                  if (i < p.peers.n) p.peers.post[i][idx] = b;
               }
             }
           }

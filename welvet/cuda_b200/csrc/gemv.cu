@@ -66,7 +66,7 @@ __device__ __forceinline__ void dot_vector(const uint4 (&wv)[kRows], const float
   if constexpr (kDt == 1) {
 #pragma unroll
     for (int b = 0; b < kB; ++b) {
-      const float4 xq = __ldg(reinterpret_cast<const float4*>(xv + b * xs));
+      const float4 xq = ld_dep4(xv + b * xs);
 #pragma unroll
       for (int r = 0; r < kRows; ++r) {
         float p = part[r][b];
@@ -90,7 +90,7 @@ __device__ __forceinline__ void dot_vector(const uint4 (&wv)[kRows], const float
         const float* xp = xv + b * xs + j * EPW;
 #pragma unroll
         for (int q = 0; q < EPW / 4; ++q) {
-          const float4 t = __ldg(reinterpret_cast<const float4*>(xp) + q);
+          const float4 t = ld_dep4(xp + 4 * q);
           x[4 * q + 0] = t.x; x[4 * q + 1] = t.y; x[4 * q + 2] = t.z; x[4 * q + 3] = t.w;
         }
 #pragma unroll
@@ -115,7 +115,7 @@ __device__ __forceinline__ void dot_vector_exact(const uint4 (&wv)[kRows], const
   if constexpr (kDt == 1) {
 #pragma unroll
     for (int b = 0; b < kB; ++b) {
-      const float4 xq = __ldg(reinterpret_cast<const float4*>(xv + b * xs));
+      const float4 xq = ld_dep4(xv + b * xs);
 #pragma unroll
       for (int r = 0; r < kRows; ++r) {
         double p = acc[r][b];
@@ -145,7 +145,7 @@ __device__ __forceinline__ void dot_vector_exact(const uint4 (&wv)[kRows], const
         const float* xp = xv + b * xs + j * EPW;
 #pragma unroll
         for (int q = 0; q < EPW / 4; ++q) {
-          const float4 t = __ldg(reinterpret_cast<const float4*>(xp) + q);
+          const float4 t = ld_dep4(xp + 4 * q);
           x[4 * q + 0] = t.x; x[4 * q + 1] = t.y; x[4 * q + 2] = t.z; x[4 * q + 3] = t.w;
         }
 #pragma unroll
@@ -280,7 +280,9 @@ __global__ void __launch_bounds__(kWarps * 32) k_gemv(const GemvArgs a) {
             a.pre[idx] = pre;
             const float post = static_cast<float>(activate(a.act, v));
             a.post[idx] = post;
-            for (int i = 0; i < a.peers.n; ++i) a.peers.post[i][idx] = post;
+#pragma unroll
+            for (int i = 0; i < kMaxPeerOut; ++i)  // static indices: the parameter stays in registers
+              if (i < a.peers.n) a.peers.post[i][idx] = post;
           } else {
             double up = acc2[r][b];
             if (kDt == 9 && !kExact) up *= static_cast<double>(a.scale2);

@@ -56,7 +56,9 @@ struct Plan {
 // grouped = true: many layers per launch fill the GPU by themselves, so each CTA streams a
 // longer K range (up to 8 chunks per warp, double-buffered) and the fixed cost of a CTA (x
 // staging, fragment build, reduction, epilogue) is paid over more bytes.
-Plan make_plan(DType dt, int rows, int cols, bool grouped = false) {
+// batch > 8 (one layer per launch, prepared fragments of 12 or 16 tokens): the shortest K
+// range per CTA the cluster limit allows, so that the fragments fit in shared memory.
+Plan make_plan(DType dt, int rows, int cols, bool grouped = false, int batch = 1) {
   Plan p;
   p.g = tiled_geom(dt, rows, cols);
   p.row_sets = (p.g.row_groups + kRG - 1) / kRG;
@@ -65,7 +67,7 @@ Plan make_plan(DType dt, int rows, int cols, bool grouped = false) {
   // then takes about half of the GPU's CTA slots, so the next launch can co-reside and
   // prefetch its weights.
   p.cpw = static_cast<int>((p.chunks + kWarps * kMaxCluster - 1) / (kWarps * kMaxCluster));
-  if (!grouped) {
+  if (!grouped && batch <= 8) {
     // A layer with many row sets fills the GPU by itself: give each CTA a longer K range
     // (fewer CTAs, each paying its fixed x-staging / reduction cost over more bytes) while
     // keeping at least two waves of CTAs for balance (4 CTAs per SM).
@@ -78,7 +80,7 @@ Plan make_plan(DType dt, int rows, int cols, bool grouped = false) {
       }
     }
   }
-  if (const char* env = std::getenv("WELVET_B200_GEMV_CPW")) {  // tuning override (chunks per warp)
+  if (const char* env = batch <= 8 ? std::getenv("WELVET_B200_GEMV_CPW") : nullptr) {  // tuning override
     const int c = std::atoi(env);
     if (c >= 1 && c <= 64 && (p.chunks + kWarps * c - 1) / (kWarps * c) <= kMaxCluster) p.cpw = c;
   }
@@ -115,6 +117,7 @@ struct KArgs {
   const uint2* frags;   // prepared B fragments [csize * nkb_cta][2 kB][4] (nullptr: built per CTA)
   const float* fscale;  // prepared 2^-e per K segment and token [csize][kB]
   PeerOut peers;        // further destinations of post (column-sharded layers)
+  int nb;               // tokens present (<= kB; kB rounds a batch of 9..16 up to 12 or 16)
 };
 
 __device__ __forceinline__ uint4 ld_stream(const uint8_t* p) {
@@ -222,7 +225,9 @@ __device__ __forceinline__ void write_out(const Args& a, int o, int b, double y,
     a.pre[idx] = pre;
     const float post = static_cast<float>(activate(a.act, v));
     a.post[idx] = post;
-    for (int i = 0; i < a.peers.n; ++i) a.peers.post[i][idx] = post;
+#pragma unroll
+    for (int i = 0; i < kMaxPeerOut; ++i)  // static indices: the parameter stays in registers
+      if (i < a.peers.n) a.peers.post[i][idx] = post;
   } else {
     const float gate_pre = static_cast<float>(y);
     const float up_post = static_cast<float>(y2);
@@ -238,8 +243,16 @@ struct GroupArgs {
   GemvGroupLayer layer[kL];
 };
 
+// Warps of a CTA: kWarps K slices, each split into two halves of the 64-row set (two row groups
+// per warp) for 9..16 tokens, whose accumulators would not fit four row groups per warp.
+template <int kB>
+__host__ __device__ constexpr int halves_of() { return kB > 8 ? 2 : 1; }
+template <int kB>
+__host__ __device__ constexpr int threads_of() { return kWarps * 32 * halves_of<kB>(); }
+
 template <int kDt, int kB, bool kDual, int kL>
-__global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_gemv_tc(const __grid_constant__ GroupArgs<kL> ga) {
+__global__ void __launch_bounds__(threads_of<kB>(), kDual ? 2 : (kB > 8 ? 1 : (kB > 4 ? 3 : 4)))
+    k_gemv_tc(const __grid_constant__ GroupArgs<kL> ga) {
   KArgs a = ga.a;
   if constexpr (kL > 1) {
     const GemvGroupLayer& L = ga.layer[blockIdx.z];
@@ -259,13 +272,19 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
   constexpr int CK = 2 * KBPU * 16;             // K elements per chunk
   constexpr int NCOL = 2 * kB;                  // B columns in use: n = 2 * token + plane
   constexpr int NT = (NCOL + 7) / 8;            // n8 tiles per A fragment (tokens 4 nt .. 4 nt + 3)
+  constexpr int kHalves = halves_of<kB>();
+  constexpr int kRGW = kRG / kHalves;            // row groups per warp
+  constexpr int kThreads = threads_of<kB>();
+  constexpr bool kPrepared = kL > 1 || kB > 8;   // B fragments prepared by k_prep_x
   __shared__ double red[kWarps][kRowsPerSet][kDual ? 2 : 1][kB];
   __shared__ double cta_part[kRowsPerSet][kDual ? 2 : 1][kB];
-  __shared__ float smax[kWarps][kB];
+  __shared__ float smax[kWarps * kHalves][kB];
   extern __shared__ uint2 frag[];                // [nkb_cta][NCOL][4]
 
   asm volatile("griddepcontrol.launch_dependents;");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ks = warp % kWarps;                 // the warp's K slice
+  const int half = warp / kWarps;               // its half of the row set (9..16 tokens)
   const int g = lane >> 2, t = lane & 3;
   const int rank = blockIdx.x;                  // K split = rank in the cluster
   // Row sets of this CTA: blockIdx.y, blockIdx.y + gridDim.y, ... (one per CTA unless a
@@ -274,27 +293,28 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
   // The CTA's chunks [cta_c0, c1) are dealt to its warps in turn (warp w: cta_c0 + w,
   // + kWarps, ...), so the four warps advance through one contiguous run of the mirror.
   const int64_t cta_c0 = static_cast<int64_t>(rank) * kWarps * a.cpw;
-  const int64_t c0 = cta_c0 + warp;
+  const int64_t c0 = cta_c0 + ks;
   int64_t c1 = cta_c0 + static_cast<int64_t>(kWarps) * a.cpw;
   if (c1 > a.chunks) c1 = a.chunks;
   constexpr int CS = kWarps;  // chunk stride of a warp
 
-  auto load_chunk = [&](int64_t rg0, int64_t c, uint4 (&buf)[2][kRG], uint4 (&buf2)[2][kRG]) {
+  auto load_chunk = [&](int64_t rg0, int64_t c, uint4 (&buf)[2][kRGW], uint4 (&buf2)[2][kRGW]) {
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int64_t unit = 2 * c + u;
 #pragma unroll
-      for (int r = 0; r < kRG; ++r) {
-        const bool ok = unit < a.units_k && rg0 + r < a.row_groups;
-        const int64_t off = (((rg0 / kRG) * a.units_k + unit) * kRG + r) * 512 + lane * 16;
+      for (int r = 0; r < kRGW; ++r) {
+        const int rr = half * kRGW + r;  // row group within the set
+        const bool ok = unit < a.units_k && rg0 + rr < a.row_groups;
+        const int64_t off = (((rg0 / kRG) * a.units_k + unit) * kRG + rr) * 512 + lane * 16;
         buf[u][r] = ok ? ld_stream(a.Wt + off) : make_uint4(0, 0, 0, 0);
         if (kDual) buf2[u][r] = ok ? ld_stream(a.Wt2 + off) : make_uint4(0, 0, 0, 0);
       }
     }
   };
 
-  uint4 bufA[2][kRG], bufA2[2][kRG];
-  uint4 bufB[2][kRG], bufB2[2][kRG];
+  uint4 bufA[2][kRGW], bufA2[2][kRGW];
+  uint4 bufB[2][kRGW], bufB2[2][kRGW];
   // The first two chunks' weights are requested before waiting on the previous kernel:
   // they do not depend on it.
   if (c0 < c1) load_chunk(rs * kRG, c0, bufA, bufA2);
@@ -305,15 +325,15 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
   // once per layer and each warp copies its own K quarter (one round of 16-byte loads from
   // L2); one layer per launch builds them here from the CTA's x slice
   float sinv[kB];
-  if constexpr (kL > 1) {
+  if constexpr (kPrepared) {
 #pragma unroll
-    for (int b = 0; b < kB; ++b) sinv[b] = __ldg(a.fscale + rank * kB + b);
+    for (int b = 0; b < kB; ++b) sinv[b] = ld_dep(a.fscale + rank * kB + b);
     if (cta_c0 < c1) {
       const int64_t nkb = (c1 - cta_c0) * 2 * KBPU;
       const uint4* src = reinterpret_cast<const uint4*>(a.frags + rank * a.nkb_cta * NCOL * 4);
       uint4* dst = reinterpret_cast<uint4*>(frag);
       const int n16 = static_cast<int>(nkb * NCOL * 2);  // NCOL * 4 uint2 per K block
-      for (int i = tid; i < n16; i += kWarps * 32) dst[i] = __ldg(src + i);
+      for (int i = tid; i < n16; i += kThreads) dst[i] = ld_dep4u(src + i);
     }
     __syncthreads();
   } else {
@@ -331,15 +351,15 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
     float m = 0.0f;
     const float* xb = a.x + b * a.x_ld;
     if (xvec) {
-      for (int i = 4 * tid; i < kspan; i += 4 * kWarps * 32) {
+      for (int i = 4 * tid; i < kspan; i += 4 * kThreads) {
         const int64_t k = klo + i;
         float4 v;
         if (k + 3 < khi) {
-          v = __ldg(reinterpret_cast<const float4*>(xb + k));
+          v = ld_dep4(xb + k);
         } else {
-          v.x = k < khi ? __ldg(xb + k) : 0.0f;
-          v.y = k + 1 < khi ? __ldg(xb + k + 1) : 0.0f;
-          v.z = k + 2 < khi ? __ldg(xb + k + 2) : 0.0f;
+          v.x = k < khi ? ld_dep(xb + k) : 0.0f;
+          v.y = k + 1 < khi ? ld_dep(xb + k + 1) : 0.0f;
+          v.z = k + 2 < khi ? ld_dep(xb + k + 2) : 0.0f;
           v.w = 0.0f;
         }
         *reinterpret_cast<float4*>(xs + b * kspan + i) = v;
@@ -349,9 +369,9 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
           if (a4[q] > m && a4[q] <= 3.402823466e+38f) m = a4[q];
       }
     } else {
-      for (int i = tid; i < kspan; i += kWarps * 32) {
+      for (int i = tid; i < kspan; i += kThreads) {
         const int64_t k = klo + i;
-        const float v = k < khi ? __ldg(xb + k) : 0.0f;
+        const float v = k < khi ? ld_dep(xb + k) : 0.0f;
         xs[b * kspan + i] = v;
         const float av = fabsf(v);
         if (av > m && av <= 3.402823466e+38f) m = av;
@@ -374,7 +394,7 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
   //      holds x[k], x[k+1] (k = 16 kbl + 2 tt) and x[k+8], x[k+9] of column n = 2 token + plane;
   //      one thread makes both planes of one (kbl, token, tt)
   const int nent = a.nkb_cta * kB * 4;
-  for (int e = tid; e < nent; e += kWarps * 32) {
+  for (int e = tid; e < nent; e += kThreads) {
     const int kbl = e / (kB * 4);
     const int rem = e - kbl * (kB * 4);
     const int b = rem >> 2, tt = rem & 3;
@@ -404,12 +424,12 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
       if (4 * nt + t == b) sinv_t[nt] = sinv[b];
   }
 
-  double acc[kRG][2][NT], acc2[kRG][2][NT];
+  double acc[kRGW][2][NT], acc2[kRGW][2][NT];
 
-  auto compute_chunk = [&](int64_t c, const uint4 (&buf)[2][kRG], const uint4 (&buf2)[2][kRG]) {
-    float d[kRG][NT][4], d2[kRG][NT][4];
+  auto compute_chunk = [&](int64_t c, const uint4 (&buf)[2][kRGW], const uint4 (&buf2)[2][kRGW]) {
+    float d[kRGW][NT][4], d2[kRGW][NT][4];
 #pragma unroll
-    for (int r = 0; r < kRG; ++r)
+    for (int r = 0; r < kRGW; ++r)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -427,7 +447,7 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
           bf[nt] = col < NCOL ? frag[fi] : make_uint2(0u, 0u);
         }
 #pragma unroll
-        for (int r = 0; r < kRG; ++r) {
+        for (int r = 0; r < kRGW; ++r) {
           uint32_t af[4];
           a_frag<kDt>(buf[u][r], j, af);
 #pragma unroll
@@ -441,7 +461,7 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
       }
     }
 #pragma unroll
-    for (int r = 0; r < kRG; ++r)
+    for (int r = 0; r < kRGW; ++r)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         acc[r][0][nt] += (static_cast<double>(d[r][nt][0]) + static_cast<double>(d[r][nt][1])) * sinv_t[nt];
@@ -459,7 +479,7 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
   for (; rs < nrs; rs += gridDim.y) {
     const int64_t rg0 = rs * kRG;
 #pragma unroll
-    for (int r = 0; r < kRG; ++r)
+    for (int r = 0; r < kRGW; ++r)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) acc[r][0][nt] = acc[r][1][nt] = acc2[r][0][nt] = acc2[r][1][nt] = 0.0;
   // the warp's chunks alternate between bufA and bufB; the chunk two ahead is requested as
@@ -484,18 +504,19 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
     const int tok = 4 * nt + t;
     if (tok < kB) {
 #pragma unroll
-      for (int r = 0; r < kRG; ++r) {
-        red[warp][r * 16 + g][0][tok] = acc[r][0][nt];
-        red[warp][r * 16 + g + 8][0][tok] = acc[r][1][nt];
+      for (int r = 0; r < kRGW; ++r) {
+        const int row = (half * kRGW + r) * 16 + g;
+        red[ks][row][0][tok] = acc[r][0][nt];
+        red[ks][row + 8][0][tok] = acc[r][1][nt];
         if (kDual) {
-          red[warp][r * 16 + g][kDual ? 1 : 0][tok] = acc2[r][0][nt];
-          red[warp][r * 16 + g + 8][kDual ? 1 : 0][tok] = acc2[r][1][nt];
+          red[ks][row][kDual ? 1 : 0][tok] = acc2[r][0][nt];
+          red[ks][row + 8][kDual ? 1 : 0][tok] = acc2[r][1][nt];
         }
       }
     }
   }
   __syncthreads();
-  for (int i = tid; i < kRowsPerSet * M * kB; i += kWarps * 32) {
+  for (int i = tid; i < kRowsPerSet * M * kB; i += kThreads) {
     const int row = i / (M * kB), rem = i - row * M * kB, m = rem / kB, b = rem - m * kB;
     double y = 0.0;
 #pragma unroll
@@ -507,9 +528,10 @@ __global__ void __launch_bounds__(kWarps * 32, kDual ? 2 : (kB > 4 ? 3 : 4)) k_g
   if (a.csize > 1) cg::this_cluster().sync();
   else __syncthreads();
   if (rank == 0) {
-    for (int i = tid; i < kRowsPerSet * kB; i += kWarps * 32) {
+    for (int i = tid; i < kRowsPerSet * kB; i += kThreads) {
       const int row = i / kB, b = i - row * kB;
       const int o = static_cast<int>(rs * kRowsPerSet + row);
+      if (b >= a.nb) continue;  // tokens past the launch's batch (kB rounds it up)
       double y = 0.0, y2 = 0.0;
       for (int r = 0; r < a.csize; ++r) {
         const double (*part)[M][kB] = cta_part;
@@ -576,6 +598,7 @@ __global__ void k_build_tiled(const uint8_t* __restrict__ native, int rows, int 
 template <int kL>
 struct PrepArgs {
   int cols = 0, nkb_cta = 0;
+  int nb = 0;  // tokens present (<= kB): tokens past it are zero
   int64_t x_ld = 0;
   const float* x[kL] = {};
   uint2* frags[kL] = {};
@@ -600,8 +623,8 @@ __global__ void __launch_bounds__(kPrepThreads) k_prep_x(const __grid_constant__
 #pragma unroll
   for (int b = 0; b < kB; ++b) {
     float m = 0.0f;
-    for (int64_t k = klo + tid; k < khi; k += kPrepThreads) {
-      const float av = fabsf(__ldg(x + b * pa.x_ld + k));
+    for (int64_t k = klo + tid; k < khi && b < pa.nb; k += kPrepThreads) {
+      const float av = fabsf(ld_dep(x + b * pa.x_ld + k));
       if (av > m && av <= 3.402823466e+38f) m = av;
     }
 #pragma unroll
@@ -626,8 +649,9 @@ __global__ void __launch_bounds__(kPrepThreads) k_prep_x(const __grid_constant__
     const int b = rem >> 2, tt = rem & 3;
     const int64_t k = klo + kbl * 16 + 2 * tt;
     const float* xb = x + b * pa.x_ld;
-    const float v0 = k < khi ? __ldg(xb + k) : 0.0f, v1 = k + 1 < khi ? __ldg(xb + k + 1) : 0.0f;
-    const float v8 = k + 8 < khi ? __ldg(xb + k + 8) : 0.0f, v9 = k + 9 < khi ? __ldg(xb + k + 9) : 0.0f;
+    const bool in = b < pa.nb;
+    const float v0 = in && k < khi ? ld_dep(xb + k) : 0.0f, v1 = in && k + 1 < khi ? ld_dep(xb + k + 1) : 0.0f;
+    const float v8 = in && k + 8 < khi ? ld_dep(xb + k + 8) : 0.0f, v9 = in && k + 9 < khi ? ld_dep(xb + k + 9) : 0.0f;
     uint32_t l0, l1, h0, h1;
     x_planes(v0, v1, ssc[b], l0, l1);
     x_planes(v8, v9, ssc[b], h0, h1);
@@ -653,7 +677,12 @@ Status launch_prep(const PrepArgs<kL>& pa, int csize, int nl, int batch, cudaStr
   case 2: return cuda_status(cudaLaunchKernelEx(&cfg, k_prep_x<2, kL>, pa), "gemv_tc prep launch");
   case 3: return cuda_status(cudaLaunchKernelEx(&cfg, k_prep_x<3, kL>, pa), "gemv_tc prep launch");
   case 4: return cuda_status(cudaLaunchKernelEx(&cfg, k_prep_x<4, kL>, pa), "gemv_tc prep launch");
-  default: return Status::Internal("gemv_tc prep: batch must be 1..4");
+  default:
+    if constexpr (kL == 1) {
+      if (batch == 12) return cuda_status(cudaLaunchKernelEx(&cfg, k_prep_x<12, 1>, pa), "gemv_tc prep launch");
+      if (batch == 16) return cuda_status(cudaLaunchKernelEx(&cfg, k_prep_x<16, 1>, pa), "gemv_tc prep launch");
+    }
+    return Status::Internal("gemv_tc prep: batch must be 1..4 (12 or 16 for one layer)");
   }
 }
 
@@ -682,7 +711,7 @@ template <int kDt, int kB, bool kDual, int kL>
 Status launch_t(const GroupArgs<kL>& k, int nl, const Plan& pl, cudaStream_t st, bool pdl, bool prepared) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(pl.csize), static_cast<unsigned>(pl.grid_y), static_cast<unsigned>(nl));
-  cfg.blockDim = dim3(kWarps * 32);
+  cfg.blockDim = dim3(threads_of<kB>());
   // B fragments [nkb_cta][2 kB][4] uint2, then the x slice [kB][16 nkb_cta] float (not when
   // the fragments are prepared)
   cfg.dynamicSmemBytes = static_cast<size_t>(pl.nkb_cta) * 2 * kB * 4 * sizeof(uint2) +
@@ -722,10 +751,13 @@ Status launch_b(const GroupArgs<kL>& k, int nl, const Plan& pl, int batch, cudaS
       case 6: return launch_t<kDt, 6, false, 1>(k, nl, pl, st, pdl, prepared);
       case 7: return launch_t<kDt, 7, false, 1>(k, nl, pl, st, pdl, prepared);
       case 8: return launch_t<kDt, 8, false, 1>(k, nl, pl, st, pdl, prepared);
-      default: break;
+      default:
+        if (batch >= 9 && batch <= 12) return launch_t<kDt, 12, false, 1>(k, nl, pl, st, pdl, true);
+        if (batch >= 13 && batch <= 16) return launch_t<kDt, 16, false, 1>(k, nl, pl, st, pdl, true);
+        break;
       }
     }
-    return Status::Internal("gemv_tc: batch must be 1..8 (1..4 for the fused Gate/Up and grouped launches)");
+    return Status::Internal("gemv_tc: batch must be 1..16 (1..4 for the fused Gate/Up and grouped launches)");
   }
 }
 
@@ -776,7 +808,7 @@ Status launch_gemv_tc(const GemvTcArgs& a, cudaStream_t st, bool pdl) {
   if (!gemv_tc_supported(a.dtype)) return Status::Unsupported("gemv_tc: dtype");
   if (a.rows <= 0 || a.cols <= 0 || a.batch < 1 || a.batch > (a.Wt2 ? 4 : kGemvMaxBatch))
     return Status::Invalid("gemv_tc: bad dims");
-  const Plan pl = make_plan(a.dtype, a.rows, a.cols);
+  const Plan pl = make_plan(a.dtype, a.rows, a.cols, false, a.batch);
   KArgs k{};
   k.Wt = a.Wt;
   k.Wt2 = a.Wt2;
@@ -799,14 +831,67 @@ Status launch_gemv_tc(const GemvTcArgs& a, cudaStream_t st, bool pdl) {
   k.bias_len = a.bias_len;
   k.act = a.act;
   k.peers = a.peers;
+  k.nb = a.batch;
+  if (a.batch > 8) {
+    // 9..16 tokens: x is prepared once (f16 B fragments of 12 or 16 tokens per K segment)
+    // by a small kernel, then the GEMV copies its segment's fragments into shared memory.
+    if (a.Wt2) return Status::Invalid("gemv_tc: the fused Gate/Up form takes 1..4 tokens");
+    if (!a.prep) return Status::Internal("gemv_tc: 9..16 tokens need prepared-fragment scratch");
+    if (!gemv_tc_fits(a.dtype, a.rows, a.cols, a.batch))
+      return Status::Invalid("gemv_tc: K too long for 9..16 tokens (the batched GEMM takes it)");
+    const int kb = a.batch <= 12 ? 12 : 16;
+    PrepArgs<1> pa;
+    pa.cols = a.cols;
+    pa.nkb_cta = pl.nkb_cta;
+    pa.nb = a.batch;
+    pa.x_ld = a.x_ld;
+    pa.x[0] = a.x;
+    pa.frags[0] = static_cast<uint2*>(a.prep);
+    pa.fscale[0] = reinterpret_cast<float*>(pa.frags[0] + static_cast<int64_t>(pl.csize) * pl.nkb_cta * 8 * kb);
+    WB_TRY(launch_prep(pa, pl.csize, 1, kb, st, pdl));
+    k.frags = pa.frags[0];
+    k.fscale = pa.fscale[0];
+    pdl = true;  // the GEMV's weight loads start while the preparation runs
+  }
   GroupArgs<1> g{};
   g.a = k;
   return a.Wt2 ? launch_d<true, 1>(a.dtype, g, 1, pl, a.batch, st, pdl)
                : launch_d<false, 1>(a.dtype, g, 1, pl, a.batch, st, pdl);
 }
 
+bool gemv_tc_fits(DType dt, int rows, int cols, int batch) {
+  if (!gemv_tc_supported(dt) || rows <= 0 || cols <= 0 || batch < 1 || batch > kGemvMaxBatch) return false;
+  if (batch <= 8) return true;
+  const Plan pl = make_plan(dt, rows, cols, false, batch);
+  if (pl.csize > kMaxCluster) return false;
+  const int kb = batch <= 12 ? 12 : 16;
+  // prepared fragments in shared memory next to the static reduction arrays (~40 KB at 16)
+  return static_cast<size_t>(pl.nkb_cta) * 2 * kb * 4 * sizeof(uint2) <= 176u * 1024u;
+}
+
+size_t gemv_prep_bytes(DType dt, int rows, int cols, int batch) {
+  if (batch <= 4) return gemv_group_prep_bytes(dt, rows, cols, batch);
+  if (batch <= 8 || !gemv_tc_fits(dt, rows, cols, batch)) return 0;
+  const Plan pl = make_plan(dt, rows, cols, false, batch);
+  const int kb = batch <= 12 ? 12 : 16;
+  return static_cast<size_t>(pl.csize) * pl.nkb_cta * 8 * kb * sizeof(uint2) +
+         static_cast<size_t>(pl.csize) * kb * sizeof(float);
+}
+
+bool gemv_prefers_prepared(DType dt, int rows, int cols, int batch) {
+  if (!gemv_tc_supported(dt) || rows <= 0 || cols <= 0 || batch < 1 || batch > 4) return false;
+  if (const char* env = std::getenv("WELVET_B200_GEMV_PREP")) {
+    if (env[0] == '1') return true;
+    if (env[0] == '0') return false;
+  }
+  // measured: layers of 8192 rows and more stream faster with x prepared once (65536 x 16384
+  // FP4: 147 -> 120 us, 14336 x 4096: 24.6 -> 19.5 us); 4096-row layers slower (12.4 -> 17.4)
+  const Plan pl = make_plan(dt, rows, cols, true);
+  return pl.row_sets >= 128;
+}
+
 Status launch_gemv_tc_group(DType dt, int rows, int cols, int batch, int64_t x_ld, int64_t ld_out,
-                            const GemvGroupLayer* layers, int n, cudaStream_t st, bool pdl) {
+                            const GemvGroupLayer* layers, int n, cudaStream_t st, bool pdl, const PeerOut* peers) {
   if (!gemv_tc_supported(dt)) return Status::Unsupported("gemv_tc: dtype");
   if (rows <= 0 || cols <= 0 || batch < 1 || batch > 4 || n < 0 || (n > 0 && !layers))
     return Status::Invalid("gemv_tc group: bad arguments");
@@ -827,6 +912,7 @@ Status launch_gemv_tc_group(DType dt, int rows, int cols, int batch, int64_t x_l
     PrepArgs<kGemvGroupMax> pa;
     pa.cols = cols;
     pa.nkb_cta = pl.nkb_cta;
+    pa.nb = batch;
     pa.x_ld = x_ld;
     for (int i = 0; i < nl; ++i) {
       pa.x[i] = layers[l0 + i].x;
@@ -849,6 +935,8 @@ Status launch_gemv_tc_group(DType dt, int rows, int cols, int batch, int64_t x_l
     k.nkb_cta = pl.nkb_cta;
     k.x_ld = x_ld;
     k.ld_out = ld_out;
+    k.nb = batch;
+    if (peers) k.peers = *peers;
     for (int i = 0; i < nl; ++i) g.layer[i] = layers[l0 + i];
     WB_TRY((launch_d<false, kGemvGroupMax>(dt, g, nl, pl, batch, st, true, true)));
   }

@@ -27,9 +27,15 @@ bool gemv_tc_supported(DType dt);
 // Build the tiled mirror from reference-layout native bytes (FP8 codes canonicalised).
 Status build_tiled_mirror(DType dt, const uint8_t* native, int rows, int cols, uint8_t* tiled, cudaStream_t st);
 
-// Tokens per launch: up to 8 for one layer (two n8 tiles of x per A fragment), up to 4 for
-// the fused Gate/Up (SwiGLU) form and for grouped launches.
-constexpr int kGemvMaxBatch = 8;
+// Tokens per launch: up to 16 for one layer (5..8: two n8 tiles of x per A fragment; 9..16:
+// four, with x prepared once per K segment by a small kernel and two row groups per warp), up
+// to 4 for the fused Gate/Up (SwiGLU) form and for grouped launches.
+constexpr int kGemvMaxBatch = 16;
+// Whether the tensor GEMV takes `batch` tokens of this layer (9..16 tokens: the prepared
+// fragments of a CTA's K range must fit in shared memory, which bounds K).
+bool gemv_tc_fits(DType dt, int rows, int cols, int batch);
+// Device scratch a session of this batch gives the GEMV for prepared x fragments (0: none).
+size_t gemv_prep_bytes(DType dt, int rows, int cols, int batch);
 
 struct GemvTcArgs {
   DType dtype = DType::FP4;
@@ -47,6 +53,7 @@ struct GemvTcArgs {
   int bias_len = 0;
   int act = -1;
   PeerOut peers;                 // further destinations of post (column-sharded layers)
+  void* prep = nullptr;          // gemv_prep_bytes of device scratch (required for 9..16 tokens)
 };
 
 // Launches on `st` with a thread-block cluster per 64-row set (split-K reduced in
@@ -75,7 +82,14 @@ constexpr int kGemvGroupMax = 32;
 // layer's x, then the GEMV, whose CTAs (one per 64 rows) read the fragments instead of each
 // staging x and building them.
 size_t gemv_group_prep_bytes(DType dt, int rows, int cols, int batch);
+// `peers` (may be nullptr): further destinations of post, applied to every layer of the launch
+// (used with one layer, by column-sharded layers).
 Status launch_gemv_tc_group(DType dt, int rows, int cols, int batch, int64_t x_ld, int64_t ld_out,
-                            const GemvGroupLayer* layers, int n, cudaStream_t st, bool pdl);
+                            const GemvGroupLayer* layers, int n, cudaStream_t st, bool pdl,
+                            const PeerOut* peers = nullptr);
+// Whether one layer runs faster as a one-layer grouped launch (x prepared once by a small kernel,
+// longer K ranges per CTA) than with the single-layer plan: layers whose grouped plan still fills
+// the GPU with CTAs (WELVET_B200_GEMV_PREP=1 / 0 forces the choice). Batches of 1..4.
+bool gemv_prefers_prepared(DType dt, int rows, int cols, int batch);
 
 } // namespace wb

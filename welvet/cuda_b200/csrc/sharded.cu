@@ -31,9 +31,12 @@ __device__ __forceinline__ uint64_t global_ns() {
 // s's flag slot `rank` -- after a system-scope fence, so that every store this rank's forward
 // made into rank s's buffers (the kernels before this one on the stream) is visible there
 // first -- and then waits until rank s has published the same number here. The wait is
-// bounded: past `limit_ns` it records bit 0 in *err and gives up.
+// bounded: past `limit_ns` it records bit 0 in *err and gives up. Launched as a programmatic
+// dependent of the forward's last kernel: it is resident early and starts the moment that
+// kernel's grid has completed and its stores are visible (griddepcontrol.wait).
 __global__ void k_flag_exchange(FlagPtrs peers, const uint32_t* mine, uint32_t* count, int nranks, int rank,
                                 int* err, unsigned long long limit_ns) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int s = threadIdx.x;
   const uint32_t epoch = *count + 1u;  // read by every lane before lane 0 updates it below
   if (s < nranks && s != rank) {
@@ -245,9 +248,17 @@ Status sharded_execute_device(ShardedDense* s, const float* x, cudaStream_t st, 
     if (c->nranks > 1) {
       FlagPtrs fp{};
       for (int r = 0; r < c->nranks; ++r) fp.p[r] = static_cast<uint32_t*>(s->flags.ptr[static_cast<size_t>(r)]);
-      k_flag_exchange<<<1, 32, 0, st>>>(fp, static_cast<const uint32_t*>(s->flags.local), s->count, c->nranks,
-                                         c->rank, s->err, wait_limit_ns());
-      WB_CUDA(cudaGetLastError());
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1);
+      cfg.blockDim = dim3(32);
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = rows > 0 ? 1 : 0;
+      WB_CUDA(cudaLaunchKernelEx(&cfg, k_flag_exchange, fp, static_cast<const uint32_t*>(s->flags.local), s->count,
+                                 c->nranks, c->rank, s->err, wait_limit_ns()));
     }
     if (post) *post = y;
     if (pre) *pre = ypre;
