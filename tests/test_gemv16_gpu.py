@@ -1,5 +1,5 @@
-"""GPU: the tensor GEMV for 9..16 tokens (x prepared once per K segment, two row groups per
-warp, the launch's token count rounded up to 12 or 16) and the SwiGLU cell's 5..16-row form
+"""GPU: the opt-in (WELVET_B200_GEMV16=1) tensor GEMV for 9..16 tokens (x prepared once per K segment, two row groups per
+warp, the launch's token count rounded up to 12 or 16) and the SwiGLU cell's opt-in 5..16-row form
 (Gate and Up as two such GEMVs, the reference's product, Down), against the fp64 oracle within
 the GEMV bound (2^-18 * sum |W x| + 2 ulp). Shapes cover ragged rows and K, more row sets than
 SMs, several K segments per row set (clusters), every quantized dtype, bias / activation,
@@ -17,6 +17,7 @@ pytestmark = pytest.mark.gpu
 @pytest.mark.parametrize("shape", [(300, 1000), (4096, 4096), (1100, 7000)])
 def test_gemv_9_to_16_tokens(wb, oracle, dt, shape, batch, monkeypatch):
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
+    monkeypatch.setenv("WELVET_B200_GEMV16", "1")
     out, in_ = shape
     w, x, bias, ref = _case(oracle, dt, out, in_, batch, 2.0, out + in_ + batch + dt, 2, True, out - 5)
     pre, post = wb.dense_forward_f32(w, x, dt, 2, bias)
@@ -27,6 +28,7 @@ def test_gemv16_matches_gemm_fallback_for_long_k(wb, oracle, monkeypatch):
     """At 16 tokens a K of 65536 FP4 is too long for the GEMV's shared memory; the session runs
     the tcgen05 GEMM, still within the bound."""
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
+    monkeypatch.setenv("WELVET_B200_GEMV16", "1")
     w, x, bias, ref = _case(oracle, 16, 256, 65536, 16, 2.0, 77, -1, False)
     pre, post = wb.dense_forward_f32(w, x, 16, -1, None)
     err = np.abs(pre.astype(np.float64) - ref[0]) - 2 * ulp(ref[0])
@@ -37,6 +39,7 @@ def test_gemv16_equals_repeated_8_token_launches_in_tolerance(wb, oracle, monkey
     """16 tokens in one launch vs the same tokens through the 8-token GEMV in two halves: both
     within the bound of the oracle (the K segments differ, so sums differ in order only)."""
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
+    monkeypatch.setenv("WELVET_B200_GEMV16", "1")
     dt, out, in_ = 4, 2048, 3072
     w, x, bias, ref = _case(oracle, dt, out, in_, 16, 2.0, 5, -1, False)
     pre16, _ = wb.dense_forward_f32(w, x, dt, -1, None)
@@ -50,6 +53,7 @@ def test_gemv16_equals_repeated_8_token_launches_in_tolerance(wb, oracle, monkey
 @pytest.mark.parametrize("dt", [16, 4])
 def test_swiglu_5_to_16_rows(wb, oracle, dt, rows, monkeypatch):
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
+    monkeypatch.setenv("WELVET_B200_GEMV16", "1")
     rng = np.random.default_rng(200 + rows)
     d, inter = 1024, 2816
     G, U, D = [(rng.standard_normal(s) * 0.5).astype(np.float32) for s in ((inter, d), (inter, d), (d, inter))]

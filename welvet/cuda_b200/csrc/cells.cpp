@@ -92,14 +92,17 @@ Status swiglu_mount_src(int device, int in, int inter, DType dt, const WeightSrc
   return Status::Ok();
 }
 
-// SwiGLU's own batch split: the fused Gate/Up tensor GEMV takes 1..4 rows; 5..16 rows run Gate
-// and Up as two tensor GEMVs (weights streamed once each, HBM-bound) and the reference's
-// product; the Gate/Up pair GEMM (tcgen05) every larger batch of quantized, non-exact layers.
+// SwiGLU's own batch split: the fused Gate/Up tensor GEMV takes 1..4 rows; the Gate/Up pair GEMM
+// (tcgen05) every larger batch of quantized, non-exact layers. WELVET_B200_GEMV16=1 runs 5..16
+// rows as two tensor GEMVs (Gate, Up) and the reference's product instead (measured slower on
+// B200: 16 rows of the 4096 / 14336 E4M3 cell take 370 us against 130 us on the pair GEMM).
 static bool swiglu_dual_gemv(const SwigluCell* c, int bs) {
   return bs <= 4 && use_gemv_tc(c->gate, bs) && c->up.Wt;
 }
 static bool swiglu_split_gemv(const SwigluCell* c, int bs) {
   if (std::getenv("WELVET_B200_BATCHED") != nullptr) return false;
+  const char* g16 = std::getenv("WELVET_B200_GEMV16");
+  if (!(g16 && g16[0] == '1')) return false;
   return bs > 4 && bs <= kGemvMaxBatch && use_gemv_tc(c->gate, bs) && use_gemv_tc(c->up, bs);
 }
 static bool swiglu_batched(const SwigluCell* c, int bs) {

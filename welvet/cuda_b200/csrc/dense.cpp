@@ -73,11 +73,14 @@ void DenseIO::release() {
 bool use_gemv_tc(const DeviceDense& d, int batch) {
   const char* env = std::getenv("WELVET_B200_GEMV");
   if (env && std::strcmp(env, "simt") == 0) return false;
-  if (batch > 8) {  // 9..16 tokens: the GEMV when its prepared fragments fit (else the GEMM)
+  if (batch > 8) {
+    // 9..16 tokens run the tcgen05 GEMM: measured faster on B200 than the register-path GEMV,
+    // whose mma.sync work grows with the token count (14336 x 4096 E4M3, 16 tokens: GEMM
+    // 46 us, GEMV 144 us). WELVET_B200_GEMV16=1 selects the GEMV where it fits.
     const char* b = std::getenv("WELVET_B200_BATCHED");
     if (b && (std::strcmp(b, "tc") == 0)) return false;
     const char* g16 = std::getenv("WELVET_B200_GEMV16");
-    if (g16 && g16[0] == '0') return false;
+    if (!(g16 && g16[0] == '1')) return false;
   }
   return batch >= 1 && batch <= kGemvMaxBatch && !d.exact && d.Wt != nullptr &&
          gemv_tc_fits(d.dtype, d.rows, d.cols, batch);
@@ -617,8 +620,7 @@ Status session_execute_device_noalloc(DenseSession* s, const float* x, float* pr
   const DeviceDense& d = s->dev;
   if (!use_tensor_path(d, s->batch))
     return Status::Unsupported("allocation-free forward serves the batched tensor-core path only "
-                               "(FP8/FP4/Int8 sessions with batch > 16, or 9..16 on layers too long for the "
-                               "small-batch GEMV, outside exact mode)");
+                               "(FP8/FP4/Int8 sessions with batch > 8 outside exact mode)");
   WB_CUDA(cudaSetDevice(s->device));
   GemmArgs g;
   g.dtype = d.dtype;

@@ -93,13 +93,13 @@ struct DenseIO {
   void release();
 };
 
-// Batched path selection: batches the tensor GEMV does not take (above 16 tokens, or 9..16 on
-// layers whose K is too long for it) run the tcgen05 GEMM (FP8/FP4/Int8 layers that are not in
-// exact mode); WELVET_B200_BATCHED=gemv keeps every batch on the GEMV, =tc every batch on the GEMM.
+// Batched path selection: batches above 8 tokens run the tcgen05 GEMM (FP8/FP4/Int8 layers
+// that are not in exact mode) unless WELVET_B200_GEMV16=1 puts 9..16 on the tensor GEMV;
+// WELVET_B200_BATCHED=gemv keeps every batch on the GEMV, =tc every batch on the GEMM.
 bool use_tensor_path(const DeviceDense& d, int batch);
-// Batches of 1..16 on quantized, non-exact layers run the tensor-core GEMV (gemv_tc.hpp) where
-// it fits; WELVET_B200_GEMV=simt keeps them on the SIMT GEMV, WELVET_B200_GEMV16=0 sends 9..16
-// tokens to the GEMM.
+// Batches of 1..8 on quantized, non-exact layers run the tensor-core GEMV (gemv_tc.hpp); 9..16
+// with WELVET_B200_GEMV16=1 where it fits (else the GEMM); WELVET_B200_GEMV=simt keeps them on
+// the SIMT GEMV.
 bool use_gemv_tc(const DeviceDense& d, int batch);
 // Number of f16 planes x is split into on the tensor path (WELVET_B200_XSPLIT, default 3).
 int xsplit_policy();
