@@ -1,9 +1,9 @@
 #pragma once
 // welvet/weights.hpp -- the reference's FormatNone weight store (include/welvet/weights.hpp:12-51):
 // the same fields with the same meaning, so that a caller that fills or reads a store (a layer's
-// `weights`) works unchanged. Quantization runs on the GPU (bit-exact with the reference codec);
-// the host-side arithmetic methods of the reference store (matvec, SGD, export) are not part of
-// this library's forward path and are not declared.
+// `weights`) works unchanged. Quantization, export and SGD run on the GPU (bit-exact with the
+// reference codec and WeightStore::apply_sgd); the reference store's host matvec helpers are
+// not part of this library's path and are not declared.
 
 #include <cstddef>
 #include <cstdint>
@@ -33,6 +33,11 @@ struct WELVET_CXX_API WeightStore {
   static Status make_f32(int rows, int cols, const float* init_or_null, WeightStore* out) {
     return make(rows, cols, DType::Float32, init_or_null, out);
   }
+  // Decoded float32 weights [rows * cols] (src/weights/store.cpp export_f32).
+  Status export_f32(float* dst) const;
+  // w <- float(double(w) - lr * dW[i]) in the native storage, re-encoded
+  // (src/core/native_codec.cpp:1080-1133, Go weights.ApplySGD). dW has rows * cols values.
+  Status apply_sgd(const double* dW, double lr);
 };
 
 } // namespace welvet

@@ -17,8 +17,9 @@
  *     6 ReLU2 (include/welvet/activate.hpp:8-17);
  *   - calls are synchronous; a dense session is not locked (callers serialize its use).
  *
- * The remaining reference symbols (NormalBP / training entry points, the other layer kinds
- * and the WMN1 model-session family) are exported with their reference signatures and
+ * The Dense training step (welvet_dense_normalbp_f32) runs on the GPU. The remaining
+ * reference symbols (the other layers' NormalBP entry points, the other layer kinds and the
+ * WMN1 model-session training family) are exported with their reference signatures and
  * return status 3 ("gap") from this library.
  */
 
@@ -58,6 +59,19 @@ WELVET_API welvet_status welvet_dense_forward_f32(
     int32_t batch, int32_t in, int32_t out, int32_t act, int32_t dtype, int32_t backend,
     const float* W_init, const double* bias, size_t bias_len, const float* x, float* pre,
     float* post);
+
+/* reference include/welvet_c.h:69-78 (src/interop/c_abi.cpp:119-184) --
+ * one Dense training step on the GPU: quantize W_init, forward x (pre/post [batch*out]), take
+ * the output gradient from grad_or_target (use_target != 0: MSE against it as a target, *loss
+ * = mean squared error, else *loss = 0), backward (dX [batch*in], dW [out*in]), SGD
+ * W <- W - lr*dW on the quantized store when lr != 0, and W_after [out*in] = the store's
+ * decoded weights. Status 1 "invalid argument" for a null pointer or a non-positive size,
+ * 1 "bad dtype N" outside 0..33, 2 for dtypes off the GPU path. */
+WELVET_API welvet_status welvet_dense_normalbp_f32(
+    int32_t batch, int32_t in, int32_t out, int32_t act, int32_t dtype, int32_t backend,
+    const float* W_init, const double* bias, size_t bias_len, const float* x,
+    const float* grad_or_target, int32_t use_target, double lr, float* pre, float* post,
+    float* dX, float* dW, float* W_after, double* loss);
 
 /* reference include/welvet_c.h:81-86 -- resident session: mount once (quantize on the GPU,
  * keep the packed codes resident), execute many (H2D x, fused dequant GEMV + bias/act,

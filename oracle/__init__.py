@@ -76,6 +76,15 @@ def lib():
         L.or_swiglu_product.argtypes = [_f32p, _f32p, _f32p, c_int64]
         L.or_encode_digest.restype = c_uint64
         L.or_encode_digest.argtypes = [c_int, c_uint64, c_uint64, c_int]
+        L.or_activate_deriv.restype = c_double
+        L.or_activate_deriv.argtypes = [c_int, c_double]
+        L.or_dense_backward.restype = c_int
+        L.or_dense_backward.argtypes = [c_int, _u8p, c_float, c_int, c_int, c_int, c_int, c_int, _f32p, _f32p,
+                                        _f32p, _f32p, _f32p, _f32p]
+        L.or_apply_sgd.restype = c_int
+        L.or_apply_sgd.argtypes = [c_int, _u8p, c_float, c_int64, _f64p, c_double]
+        L.or_mse.restype = c_double
+        L.or_mse.argtypes = [_f32p, _f32p, c_int64, _f32p]
         _lib = L
     return _lib
 
@@ -114,6 +123,13 @@ def ref():
                                          _f32p, _f32p, c_char_p, c_int]
         R.ref_mha_forward.restype = c_int
         R.ref_mha_forward.argtypes = [c_int] * 10 + [_f32p] * 7 + [c_char_p, c_int]
+        R.ref_store_apply_sgd.restype = c_int
+        R.ref_store_apply_sgd.argtypes = [c_int, c_int, c_int, _u8p, c_size_t, c_float, _f64p, c_double, c_char_p,
+                                          c_int]
+        R.ref_dense_normalbp.restype = c_int
+        R.ref_dense_normalbp.argtypes = [c_int, c_int, c_int, c_int, c_int, _f32p, _f64p, c_size_t, _f32p, _f32p,
+                                         c_int, c_double, _f32p, _f32p, _f32p, _f32p, _f32p, POINTER(c_double),
+                                         c_char_p, c_int]
         _ref = R
     return _ref
 
@@ -203,3 +219,111 @@ def ref_decode(dtype: int, raw: np.ndarray, scale: float, rows: int, cols: int) 
 
 def ref_encode_digest(codec: int, start: int, count: int, threads: int = 0) -> int:
     return int(ref().ref_encode_digest(codec, start, count, threads or (os.cpu_count() or 1)))
+
+
+def dense_backward(dtype: int, raw: np.ndarray, scale: float, gy: np.ndarray, x: np.ndarray, pre: np.ndarray,
+                   in_: int, out: int, act: int, linear: bool = False):
+    """Reference Dense NormalBP backward (kernels.cu:83-128): (d_pre, gx [B,in], dW [out,in])."""
+    gy = np.ascontiguousarray(gy, np.float32).reshape(-1, out)
+    batch = gy.shape[0]
+    x = np.ascontiguousarray(x, np.float32).reshape(batch, in_)
+    pre = np.ascontiguousarray(pre, np.float32).reshape(batch, out)
+    raw = np.ascontiguousarray(raw).view(np.uint8)
+    d_pre = np.zeros((batch, out), np.float32)
+    gx = np.zeros((batch, in_), np.float32)
+    dW = np.zeros((out, in_), np.float32)
+    rc = lib().or_dense_backward(dtype, _ptr(raw, _u8p), scale, batch, in_, out, act, 1 if linear else 0,
+                                 _ptr(gy, _f32p), _ptr(x, _f32p), _ptr(pre, _f32p), _ptr(d_pre, _f32p),
+                                 _ptr(gx, _f32p), _ptr(dW, _f32p))
+    if rc != 0:
+        raise ValueError("oracle dense_backward: bad dtype")
+    return d_pre, gx, dW
+
+
+def apply_sgd(dtype: int, raw: np.ndarray, scale: float, dW: np.ndarray, lr: float) -> np.ndarray:
+    """WeightStore::apply_sgd (native_codec.cpp:1080-1133) on a copy of the payload."""
+    out = np.array(raw, dtype=np.uint8, copy=True)
+    d = np.ascontiguousarray(dW, np.float64).ravel()
+    if lib().or_apply_sgd(dtype, _ptr(out, _u8p), scale, d.size, _ptr(d, _f64p), lr) != 0:
+        raise ValueError("oracle apply_sgd: bad dtype")
+    return out
+
+
+def mse(pred: np.ndarray, target: np.ndarray):
+    """training.cpp:44-69: (loss, grad)."""
+    p = np.ascontiguousarray(pred, np.float32).ravel()
+    t = np.ascontiguousarray(target, np.float32).ravel()
+    g = np.zeros_like(p)
+    loss = lib().or_mse(_ptr(p, _f32p), _ptr(t, _f32p), p.size, _ptr(g, _f32p))
+    return float(loss), g.reshape(np.shape(pred))
+
+
+def store_of(dtype: int, w: np.ndarray) -> tuple[np.ndarray, float]:
+    """A store's payload as bytes: Float32 keeps the float master, other dtypes pack."""
+    if dtype == FLOAT32:
+        return np.ascontiguousarray(w, np.float32).ravel().view(np.uint8).copy(), 1.0
+    return pack(dtype, w)
+
+
+def decode_f32(dtype: int, raw: np.ndarray, scale: float, n: int) -> np.ndarray:
+    """WeightStore::export_f32 (store.cpp:42-70): weight_at per element, as float32."""
+    if dtype == FLOAT32:
+        return np.ascontiguousarray(raw).view(np.float32)[:n].copy()
+    return decode(dtype, raw, scale, n).astype(np.float32)
+
+
+def dense_normalbp(dtype: int, W: np.ndarray, x: np.ndarray, grad_or_target: np.ndarray, act: int,
+                   bias=None, use_target: bool = False, lr: float = 0.0):
+    """The steps of welvet_dense_normalbp_f32 (src/interop/c_abi.cpp:119-184) over the oracle:
+    pack, forward, MSE (use_target) or the given gradient, backward, SGD when lr != 0, export.
+    Returns (pre, post, dX, dW, W_after, loss)."""
+    out, in_ = W.shape
+    raw, scale = store_of(dtype, W)
+    pre, post, _, _ = dense_forward(dtype, raw, scale, x, in_, out, act, bias)
+    g = np.ascontiguousarray(grad_or_target, np.float32).reshape(post.shape)
+    loss = 0.0
+    if use_target:
+        loss, g = mse(post, g)
+    _, gx, dW = dense_backward(dtype, raw, scale, g, x, pre, in_, out, act)
+    if lr != 0.0:
+        raw = apply_sgd(dtype, raw, scale, dW, lr)
+    W_after = decode_f32(dtype, raw, scale, out * in_).reshape(out, in_)
+    return pre, post, gx, dW, W_after, loss
+
+
+def ref_store_apply_sgd(dtype: int, raw: np.ndarray, scale: float, rows: int, cols: int, dW: np.ndarray,
+                        lr: float) -> np.ndarray:
+    """The reference's WeightStore::apply_sgd (native_codec.cpp:1080-1133) on a copy."""
+    out = np.array(raw, dtype=np.uint8, copy=True)
+    d = np.ascontiguousarray(dW, np.float64).ravel()
+    msg = ctypes.create_string_buffer(256)
+    rc = ref().ref_store_apply_sgd(rows, cols, dtype, _ptr(out, _u8p), out.size, scale, _ptr(d, _f64p), lr, msg, 256)
+    if rc != 0:
+        raise RuntimeError(f"reference apply_sgd: {rc} {msg.value.decode()}")
+    return out
+
+
+def ref_dense_normalbp(dtype: int, W: np.ndarray, x: np.ndarray, grad_or_target: np.ndarray, act: int,
+                       bias=None, use_target: bool = False, lr: float = 0.0):
+    """The reference's own Dense training step on its CUDA kernels (needs a GPU): the same
+    return tuple as dense_normalbp."""
+    out, in_ = W.shape
+    W = np.ascontiguousarray(W, np.float32)
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, in_)
+    batch = x.shape[0]
+    g = np.ascontiguousarray(grad_or_target, np.float32).reshape(batch, out)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float64)
+    pre = np.zeros((batch, out), np.float32)
+    post = np.zeros((batch, out), np.float32)
+    dX = np.zeros((batch, in_), np.float32)
+    dW = np.zeros((out, in_), np.float32)
+    W_after = np.zeros((out, in_), np.float32)
+    loss = c_double(0.0)
+    msg = ctypes.create_string_buffer(256)
+    rc = ref().ref_dense_normalbp(batch, in_, out, act, dtype, _ptr(W, _f32p), _ptr(b, _f64p),
+                                  0 if b is None else b.size, _ptr(x, _f32p), _ptr(g, _f32p), int(bool(use_target)),
+                                  lr, _ptr(pre, _f32p), _ptr(post, _f32p), _ptr(dX, _f32p), _ptr(dW, _f32p),
+                                  _ptr(W_after, _f32p), ctypes.byref(loss), msg, 256)
+    if rc != 0:
+        raise RuntimeError(f"reference dense normalbp: {rc} {msg.value.decode()}")
+    return pre, post, dX, dW, W_after, loss.value

@@ -443,3 +443,132 @@ OR_EXPORT uint64_t or_encode_digest(int codec, uint64_t start, uint64_t count, i
   free(tid);
   return s;
 }
+
+/* ---------------------------------------------------------------- Dense backward + SGD */
+
+/* src/cuda/kernels.cu:48-81 (activate_deriv_dev); host libm exp/tanh as or_activate. */
+OR_EXPORT double or_activate_deriv(int act, double x) {
+  switch (act) {
+  case -1: return 1.0;
+  case 0: return x > 0.0 ? 1.0 : 0.0;
+  case 6: return x > 0.0 ? 2.0 * x : 0.0;
+  case 5: return x > 0.0 ? 1.0 : 0.01;
+  case 1: {
+    const double sig = 1.0 / (1.0 + exp(-x));
+    return sig * (1.0 + x * (1.0 - sig));
+  }
+  case 2: {
+    const double k = 0.7978845608028654;
+    const double u = k * (x + 0.044715 * x * x * x);
+    const double th = tanh(u);
+    const double du = k * (1.0 + 3.0 * 0.044715 * x * x);
+    return 0.5 * (1.0 + th) + 0.5 * x * (1.0 - th * th) * du;
+  }
+  case 3: {
+    const double t = tanh(x);
+    return 1.0 - t * t;
+  }
+  case 4: {
+    const double s = 1.0 / (1.0 + exp(-x));
+    return s * (1.0 - s);
+  }
+  default: return 1.0;
+  }
+}
+
+/* Dense NormalBP backward, src/cuda/kernels.cu:83-128 with resident_backward (:917-1000):
+ *   d_pre[b,o] = float(double(gy[b,o]) * act'(double(pre[b,o])))       (linear: d_pre = gy)
+ *   gx[b,i]    = float(sum_o W64[o,i] * double(d_pre[b,o]))             sequential o
+ *   dW[o,i]    = acc over b: acc = float(double(acc) + double(d_pre[b,o]) * double(x[b,i]))
+ * W64 is the store decoded as weight_at does (FP8 / FP4 table value, Int8 float(q) * scale,
+ * Float32 the payload). Products are of two floats, exact in double, so the order of
+ * multiply and add does not change the sums. */
+OR_EXPORT int or_dense_backward(int dtype, const uint8_t* raw, float scale, int batch, int in, int out,
+                                int act, int linear, const float* gy, const float* x, const float* pre,
+                                float* d_pre, float* gx, float* dW) {
+  const int64_t n = (int64_t)out * in;
+  double* W = (double*)malloc(sizeof(double) * (size_t)n);
+  if (!W) return 1;
+  if (dtype == OR_FLOAT32) {
+    const float* wf = (const float*)raw;
+    for (int64_t i = 0; i < n; ++i) W[i] = (double)wf[i];
+  } else if (or_decode_f64(dtype, raw, scale, 0, n, W) != 0) {
+    free(W);
+    return 1;
+  }
+  for (int64_t i = 0; i < (int64_t)batch * out; ++i)
+    d_pre[i] = linear ? gy[i] : (float)((double)gy[i] * or_activate_deriv(act, (double)pre[i]));
+  for (int b = 0; b < batch; ++b)
+    for (int i = 0; i < in; ++i) {
+      double sum = 0.0;
+      for (int o = 0; o < out; ++o) sum += W[(size_t)o * in + i] * (double)d_pre[(size_t)b * out + o];
+      gx[(size_t)b * in + i] = (float)sum;
+    }
+  for (int o = 0; o < out; ++o)
+    for (int i = 0; i < in; ++i) {
+      float acc = 0.0f;
+      for (int b = 0; b < batch; ++b)
+        acc = (float)((double)acc + (double)d_pre[(size_t)b * out + o] * (double)x[(size_t)b * in + i]);
+      dW[(size_t)o * in + i] = acc;
+    }
+  free(W);
+  return 0;
+}
+
+/* WeightStore::apply_sgd for the FormatNone types of this path,
+ * src/weights/native_codec.cpp:1080-1133 with weight_at (:513-568) and set_weight_at
+ * (:774-830): every element is decoded, updated in float (next = float(double(v) - lr * dW)),
+ * and encoded again with the same codec (FP8 / FP4: the float codecs, so codes that decode to
+ * the same value may change, e.g. FP8 subnormal codes become signed zeros; Int8:
+ * q = clamp(round(double(next / scale)), -128, 127) with the stored scale, 1 when it is 0);
+ * Float32: w -= float(lr * dW). `raw` is updated in place (Float32: the float payload). */
+OR_EXPORT int or_apply_sgd(int dtype, uint8_t* raw, float scale, int64_t n, const double* dW, double lr) {
+  const float s = scale == 0.0f ? 1.0f : scale;
+  if (dtype == OR_FLOAT32) {
+    float* wf = (float*)raw;
+    for (int64_t i = 0; i < n; ++i) wf[i] -= (float)(lr * dW[i]);
+    return 0;
+  }
+  for (int64_t i = 0; i < n; ++i) {
+    float v;
+    switch (dtype) {
+    case OR_FP8E4M3: v = or_e4m3_decode(raw[i]); break;
+    case OR_FP8E5M2: v = or_e5m2_decode(raw[i]); break;
+    case OR_FP4: v = or_fp4_decode((uint8_t)((raw[i >> 1] >> ((i & 1) * 4)) & 0xF)); break;
+    case OR_INT8: v = (float)(int8_t)raw[i] * s; break;
+    default: return 1;
+    }
+    const float next = (float)((double)v - lr * dW[i]);
+    switch (dtype) {
+    case OR_FP8E4M3: raw[i] = or_e4m3_encode(next); break;
+    case OR_FP8E5M2: raw[i] = or_e5m2_encode(next); break;
+    case OR_FP4: {
+      const uint8_t c = (uint8_t)(or_fp4_encode(next) & 0xF);
+      const int sh = (int)(i & 1) * 4;
+      raw[i >> 1] = (uint8_t)((raw[i >> 1] & ~(0xF << sh)) | (c << sh));
+      break;
+    }
+    case OR_INT8: {
+      double q = round((double)(next / s));
+      if (q < -128.0) q = -128.0;
+      if (q > 127.0) q = 127.0;
+      raw[i] = (uint8_t)(int8_t)q;
+      break;
+    }
+    }
+  }
+  return 0;
+}
+
+/* src/runtime/training.cpp:44-69: loss = sum (pred - target)^2 / n (sequential, f64);
+ * grad = float(2 / n * (pred - target)). */
+OR_EXPORT double or_mse(const float* pred, const float* target, int64_t n, float* grad) {
+  double sum = 0.0;
+  const double sc = 2.0 / (double)n;
+  for (int64_t i = 0; i < n; ++i) {
+    const double d = (double)pred[i] - (double)target[i];
+    sum += d * d;
+    if (grad) grad[i] = (float)(sc * d);
+  }
+  return sum / (double)n;
+}

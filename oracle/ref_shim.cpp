@@ -123,6 +123,76 @@ int ref_store_decode(int rows, int cols, int dtype, const uint8_t* native, size_
   return 0;
 }
 
+// WeightStore{dtype, rows, cols, native, scale}.apply_sgd(dW, lr) (src/weights/native_codec.cpp:
+// 1080-1133); the updated payload is written back over `native`.
+int ref_store_apply_sgd(int rows, int cols, int dtype, uint8_t* native, size_t native_len, float scale,
+                        const double* dW, double lr, char* msg, int msg_cap) {
+  welvet::WeightStore s;
+  s.dtype = static_cast<welvet::DType>(dtype);
+  s.rows = rows;
+  s.cols = cols;
+  s.scale = scale;
+  if (s.dtype == welvet::DType::Float32) {
+    s.f32.assign(reinterpret_cast<const float*>(native), reinterpret_cast<const float*>(native) + native_len / 4);
+  } else {
+    s.native.assign(native, native + native_len);
+  }
+  auto st = s.apply_sgd(dW, lr);
+  if (!st) return fill_msg(st, msg, msg_cap);
+  if (s.dtype == welvet::DType::Float32) std::memcpy(native, s.f32.data(), native_len);
+  else std::memcpy(native, s.native.data(), native_len);
+  return 0;
+}
+
+// The steps of the reference's welvet_dense_normalbp_f32 (src/interop/c_abi.cpp:119-184) on
+// its own layer API and CUDA kernels: new_layer, forward_f32, MSE and its gradient
+// (src/runtime/training.cpp:44-69, restated here because that file is not in this build),
+// backward_f32, apply_grad_sgd when lr != 0, export_f32.
+int ref_dense_normalbp(int batch, int in, int out, int act, int dtype, const float* W, const double* bias,
+                       size_t bias_len, const float* x, const float* grad_or_target, int use_target, double lr,
+                       float* pre, float* post, float* dX, float* dW, float* W_after, double* loss, char* msg,
+                       int msg_cap) {
+  welvet::dense::Layer layer;
+  auto st = welvet::dense::new_layer(in, out, static_cast<welvet::Activation>(act),
+                                     static_cast<welvet::DType>(dtype), W, &layer);
+  if (!st) return fill_msg(st, msg, msg_cap);
+  if (bias && bias_len > 0) layer.weights.bias.assign(bias, bias + bias_len);
+  welvet::TensorF32 input;
+  input.shape = {batch, in};
+  input.data.assign(x, x + static_cast<size_t>(batch) * in);
+  welvet::TensorF32 p, q;
+  st = welvet::dense::forward_f32(layer, input, &p, &q);
+  if (!st) return fill_msg(st, msg, msg_cap);
+  welvet::TensorF32 gy;
+  gy.shape = {batch, out};
+  gy.data.assign(grad_or_target, grad_or_target + static_cast<size_t>(batch) * out);
+  *loss = 0.0;
+  if (use_target) {
+    double sum = 0.0;
+    const double sc = 2.0 / static_cast<double>(q.data.size());
+    for (size_t i = 0; i < q.data.size(); ++i) {
+      const double d = static_cast<double>(q.data[i]) - static_cast<double>(gy.data[i]);
+      sum += d * d;
+      gy.data[i] = static_cast<float>(sc * d);
+    }
+    *loss = sum / static_cast<double>(q.data.size());
+  }
+  welvet::TensorF32 dx_t, dw_t;
+  st = welvet::dense::backward_f32(layer, gy, input, p, &dx_t, &dw_t);
+  if (!st) return fill_msg(st, msg, msg_cap);
+  if (lr != 0.0) {
+    st = welvet::dense::apply_grad_sgd(&layer, dw_t, lr);
+    if (!st) return fill_msg(st, msg, msg_cap);
+  }
+  st = layer.weights.export_f32(W_after);
+  if (!st) return fill_msg(st, msg, msg_cap);
+  std::memcpy(pre, p.data.data(), p.data.size() * sizeof(float));
+  std::memcpy(post, q.data.data(), q.data.size() * sizeof(float));
+  std::memcpy(dX, dx_t.data.data(), dx_t.data.size() * sizeof(float));
+  std::memcpy(dW, dw_t.data.data(), dw_t.data.size() * sizeof(float));
+  return 0;
+}
+
 // Reference resident Dense session (GPU): host decode -> fp64 mirror -> dense_matvec_f64_batch.
 int ref_dense_mount(int batch, int in, int out, int act, int dtype, const float* W,
                     const double* bias, size_t bias_len, void** sess, char* msg, int msg_cap) {

@@ -20,6 +20,15 @@ static Status (*const kSwigluForward)(welvet::swiglu::Layer&, const TensorF32&, 
 static Status (*const kMhaForward)(welvet::mha::Layer&, const TensorF32&, TensorF32*, TensorF32*) =
     &welvet::mha::forward;
 
+// The training entry points (reference include/welvet/dense.hpp:62-74, weights.hpp:36-44).
+static Status (*const kDenseBackward)(const welvet::dense::Layer&, const TensorF32&, const TensorF32&,
+                                      const TensorF32&, TensorF32*, TensorF32*) = &welvet::dense::backward_f32;
+static Status (*const kLinearGradIn)(const welvet::dense::Layer&, const TensorF32&, const TensorF32&, TensorF32*) =
+    &welvet::dense::linear_grad_in;
+static Status (*const kGradWOnly)(const welvet::dense::Layer&, const TensorF32&, const TensorF32&,
+                                  const TensorF32&, TensorF32*) = &welvet::dense::grad_w_only;
+static Status (*const kApplyGradSgd)(welvet::dense::Layer*, const TensorF32&, double) = &welvet::dense::apply_grad_sgd;
+
 static int fail(const Status& st, char* msg) {
   if (msg) std::strncpy(msg, st.message.c_str(), 255);
   return static_cast<int>(st.code);
@@ -63,6 +72,49 @@ int run_dense(int in, int out, int act, int dtype, const float* W1, const float*
   TensorF32 bad = tensor({1, in + 1}, x1, static_cast<size_t>(in + 1));
   st = kDenseForward(L, bad, &pre, &post);
   return st.code == welvet::StatusCode::InvalidArgument ? 0 : 99;
+}
+
+// The steps of the reference's welvet_dense_normalbp_f32 on the C++ API (given output
+// gradient, no MSE): forward, backward_f32, apply_grad_sgd when lr != 0, export_f32; plus
+// linear_grad_in and grad_w_only on the updated layer, and a second forward after the SGD.
+int run_dense_train(int in, int out, int act, int dtype, const float* W, int batch, const float* x, const float* gy,
+                    double lr, float* pre, float* post, float* dX, float* dW, float* W_after, float* gx_lin,
+                    float* dw_only, float* post_after, char* msg) {
+  welvet::dense::Layer L;
+  Status st = welvet::dense::new_layer(in, out, static_cast<welvet::Activation>(act), static_cast<welvet::DType>(dtype),
+                                       W, &L);
+  if (!st) return fail(st, msg);
+  const TensorF32 input = tensor({batch, in}, x, static_cast<size_t>(batch) * in);
+  const TensorF32 g = tensor({batch, out}, gy, static_cast<size_t>(batch) * out);
+  TensorF32 p, q, gx, gw;
+  st = kDenseForward(L, input, &p, &q);
+  if (!st) return fail(st, msg);
+  st = kDenseBackward(L, g, input, p, &gx, &gw);
+  if (!st) return fail(st, msg);
+  if (lr != 0.0) {
+    st = kApplyGradSgd(&L, gw, lr);
+    if (!st) return fail(st, msg);
+    if (L.gpu_valid) return 98;  // the SGD invalidates the device mirror
+  }
+  st = L.weights.export_f32(W_after);
+  if (!st) return fail(st, msg);
+  std::memcpy(pre, p.data.data(), p.data.size() * 4);
+  std::memcpy(post, q.data.data(), q.data.size() * 4);
+  std::memcpy(dX, gx.data.data(), gx.data.size() * 4);
+  std::memcpy(dW, gw.data.data(), gw.data.size() * 4);
+  TensorF32 lin, only, p2, q2;
+  st = kLinearGradIn(L, g, input, &lin);
+  if (!st) return fail(st, msg);
+  st = kGradWOnly(L, g, input, p, &only);
+  if (!st) return fail(st, msg);
+  st = kDenseForward(L, input, &p2, &q2);
+  if (!st) return fail(st, msg);
+  std::memcpy(gx_lin, lin.data.data(), lin.data.size() * 4);
+  std::memcpy(dw_only, only.data.data(), only.data.size() * 4);
+  std::memcpy(post_after, q2.data.data(), q2.data.size() * 4);
+  TensorF32 bad = tensor({batch, out + 1}, gy, static_cast<size_t>(batch) * out);
+  st = kDenseBackward(L, bad, input, p, &gx, &gw);
+  return st.code == welvet::StatusCode::InvalidArgument ? 0 : 97;
 }
 
 int run_swiglu(int batch, int seq, int in, int inter, int dtype, const float* G, const float* U, const float* D,

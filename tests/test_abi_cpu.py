@@ -52,7 +52,7 @@ def test_out_of_scope_entry_points_return_gap():
     class St(ctypes.Structure):
         _fields_ = [("code", ctypes.c_int32), ("message", ctypes.c_char * 256)]
 
-    for name in ("welvet_layernorm_forward_f32", "welvet_dense_normalbp_f32", "welvet_model_train_mse"):
+    for name in ("welvet_layernorm_forward_f32", "welvet_swiglu_normalbp_f32", "welvet_model_train_mse"):
         fn = getattr(L, name)
         fn.restype = St
         fn.argtypes = []

@@ -69,6 +69,9 @@ _sig("welvet_gaps_count", c_int32)
 _sig("welvet_gaps_done", c_int32)
 _sig("welvet_dense_forward_f32", _ST, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p,
      c_size_t, c_void_p, c_void_p, c_void_p)
+_sig("welvet_dense_normalbp_f32", _ST, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p,
+     c_size_t, c_void_p, c_void_p, c_int32, c_double, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+     POINTER(c_double))
 _sig("welvet_dense_mount", _ST, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_size_t,
      POINTER(c_void_p))
 _sig("welvet_b200_dense_mount_device", _ST, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p,
@@ -187,6 +190,31 @@ def dense_forward_f32(W: np.ndarray, x: np.ndarray, dtype: int, act: int = LINEA
     check(_L.welvet_dense_forward_f32(batch, in_, out, act, dtype, 0, _np_ptr(W), _np_ptr(b),
                                       0 if b is None else b.size, _np_ptr(x), _np_ptr(pre), _np_ptr(post)))
     return pre, post
+
+
+def dense_normalbp_f32(W: np.ndarray, x: np.ndarray, grad_or_target: np.ndarray, dtype: int, act: int = LINEAR,
+                       bias=None, use_target: bool = False, lr: float = 0.0):
+    """welvet_dense_normalbp_f32 (reference src/interop/c_abi.cpp:119-184): one training step.
+
+    W [out, in], x [batch, in], grad_or_target [batch, out] (the output gradient, or the MSE
+    target when use_target). Returns (pre, post, dX, dW, W_after, loss)."""
+    W = _f32(W)
+    out, in_ = W.shape
+    x = _f32(x).reshape(-1, in_)
+    batch = x.shape[0]
+    g = _f32(grad_or_target).reshape(batch, out)
+    pre = np.zeros((batch, out), np.float32)
+    post = np.zeros((batch, out), np.float32)
+    dX = np.zeros((batch, in_), np.float32)
+    dW = np.zeros((out, in_), np.float32)
+    W_after = np.zeros((out, in_), np.float32)
+    loss = c_double(0.0)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float64)
+    check(_L.welvet_dense_normalbp_f32(batch, in_, out, act, dtype, 0, _np_ptr(W), _np_ptr(b),
+                                       0 if b is None else b.size, _np_ptr(x), _np_ptr(g), int(bool(use_target)),
+                                       float(lr), _np_ptr(pre), _np_ptr(post), _np_ptr(dX), _np_ptr(dW),
+                                       _np_ptr(W_after), ctypes.byref(loss)))
+    return pre, post, dX, dW, W_after, loss.value
 
 
 class DenseSession:

@@ -9,6 +9,7 @@
 #include "dense.hpp"
 #include "gemm_tc.hpp"
 #include "model.hpp"
+#include "train.hpp"
 
 #include <cstdio>
 #include <cstdlib>
@@ -93,8 +94,8 @@ struct DevPtr {
 
 wb::Status gap(const char* what) { return wb::Status::Err(wb::StatusCode::Gap, std::string("gap? ") + what + " (not on the b200 quantized forward path)"); }
 
-constexpr int32_t kGapSymbols = 54;  // the status-3 stubs at the end of this file
-constexpr int32_t kServedSymbols = 17;  // reference symbols served on the GPU
+constexpr int32_t kGapSymbols = 53;  // the status-3 stubs at the end of this file
+constexpr int32_t kServedSymbols = 18;  // reference symbols served on the GPU
 
 } // namespace
 
@@ -318,6 +319,19 @@ welvet_status welvet_dense_forward_f32(int32_t batch, int32_t in, int32_t out, i
     wb::Status st = wb::session_execute(s, x, pre, post);
     delete s;
     return st;
+  });
+}
+
+// reference src/interop/c_abi.cpp:119-184 -- one Dense training step: forward, MSE (use_target)
+// or the given output gradient, backward, SGD when lr != 0, updated weights. On the GPU.
+welvet_status welvet_dense_normalbp_f32(int32_t batch, int32_t in, int32_t out, int32_t act, int32_t dtype,
+                                        int32_t /*backend*/, const float* W_init, const double* bias,
+                                        size_t bias_len, const float* x, const float* grad_or_target,
+                                        int32_t use_target, double lr, float* pre, float* post, float* dX,
+                                        float* dW, float* W_after, double* loss) {
+  return guarded([&] {
+    return wb::dense_normalbp(batch, in, out, act, dtype, W_init, bias, bias_len, x, grad_or_target,
+                              use_target != 0, lr, pre, post, dX, dW, W_after, loss);
   });
 }
 
@@ -581,7 +595,6 @@ WB_GAP(welvet_model_apply_sgd)
 WB_GAP(welvet_model_train_mse)
 WB_GAP(welvet_model_export_weights)
 WB_GAP(welvet_model_sync)
-WB_GAP(welvet_dense_normalbp_f32)
 WB_GAP(welvet_rmsnorm_normalbp_f32)
 WB_GAP(welvet_layernorm_forward_f32)
 WB_GAP(welvet_layernorm_normalbp_f32)

@@ -14,6 +14,7 @@
 #include "../../../include/welvet/mha.hpp"
 #include "../../../include/welvet/swiglu.hpp"
 
+#include "backward.hpp"
 #include "cells.hpp"
 #include "codec.hpp"
 #include "dense.hpp"
@@ -84,6 +85,99 @@ wb::WeightSrc source(const welvet::WeightStore& s) {
   }
   w.scale = s.scale;
   return w;
+}
+
+// Device buffers released on every exit path.
+struct DevBufs {
+  std::vector<void*> p;
+  ~DevBufs() {
+    for (void* q : p)
+      if (q) cudaFree(q);
+  }
+  template <typename T>
+  wb::Status get(T** out, size_t n) {
+    void* q = nullptr;
+    WB_CUDA(cudaMalloc(&q, n > 0 ? n * sizeof(T) : 16));
+    p.push_back(q);
+    *out = static_cast<T*>(q);
+    return wb::Status::Ok();
+  }
+};
+
+// A store's payload as the GPU codec reads it (Float32: the float master).
+const void* payload_of(const welvet::WeightStore& s, size_t* bytes) {
+  if (s.dtype == welvet::DType::Float32) {
+    *bytes = s.f32.size() * sizeof(float);
+    return s.f32.data();
+  }
+  *bytes = s.native.size();
+  return s.native.data();
+}
+
+// Checks the store's payload covers rows * cols elements (the reference's "short" errors).
+welvet::Status payload_ok(const welvet::WeightStore& s) {
+  const int64_t n = static_cast<int64_t>(s.rows) * s.cols;
+  if (s.dtype == welvet::DType::Float32)
+    return static_cast<int64_t>(s.f32.size()) < n ? invalid("f32 short") : welvet::Status::Ok();
+  if (!wb::dtype_on_path(static_cast<int32_t>(s.dtype)))
+    return welvet::Status::Err(welvet::StatusCode::Unsupported,
+                               std::string("weights: dtype ") + std::string(welvet::dtype_name(s.dtype)) +
+                                   " is not served on the GPU by this library");
+  if (static_cast<int64_t>(s.native.size()) < wb::native_bytes(static_cast<wb::DType>(s.dtype), n))
+    return invalid("weights: native payload short");
+  return welvet::Status::Ok();
+}
+
+// Resamples gy to `need` values by bucket means (the reference's remap for gradient lengths
+// that differ from batch * out, src/layers/dense/dense.cpp:122-139).
+void remap_len(const std::vector<float>& src, int need, std::vector<float>* out) {
+  out->assign(static_cast<size_t>(need > 0 ? need : 0), 0.0f);
+  const int sn = static_cast<int>(src.size());
+  if (sn <= 0 || need <= 0) return;
+  if (sn == need) {
+    *out = src;
+    return;
+  }
+  for (int i = 0; i < need; ++i) {
+    const int lo = static_cast<int>(static_cast<int64_t>(i) * sn / need);
+    int hi = static_cast<int>(static_cast<int64_t>(i + 1) * sn / need);
+    hi = hi <= lo ? lo + 1 : (hi > sn ? sn : hi);
+    double acc = 0.0;
+    for (int j = lo; j < hi; ++j) acc += static_cast<double>(src[static_cast<size_t>(j)]);
+    (*out)[static_cast<size_t>(i)] = static_cast<float>(acc / static_cast<double>(hi - lo));
+  }
+}
+
+// One backward on the layer's mounted session: host gy / x / pre in, gx and / or dW out.
+welvet::Status run_backward(const welvet::dense::Layer& layer, int batch, const float* gy, const float* x,
+                            const float* pre, bool linear, float* gx_host, float* dw_host) {
+  if (!layer.gpu_valid || layer.gpu_batch != batch || !layer.gpu.session) {
+    if (auto st = welvet::dense::sync_gpu_from_weights(layer, batch); !st) return st;
+  }
+  auto* s = static_cast<wb::DenseSession*>(layer.gpu.session);
+  wb::Status st = wb::cuda_status(cudaSetDevice(s->device), "cudaSetDevice");
+  const size_t nx = static_cast<size_t>(batch) * layer.input_height;
+  const size_t ny = static_cast<size_t>(batch) * layer.output_height;
+  const size_t nw = static_cast<size_t>(layer.output_height) * layer.input_height;
+  DevBufs b;
+  float *gyd = nullptr, *xd = nullptr, *pred = nullptr, *dpre = nullptr, *gxd = nullptr, *dwd = nullptr;
+  if (st.ok()) st = b.get(&gyd, ny);
+  if (st.ok()) st = b.get(&xd, nx);
+  if (st.ok()) st = b.get(&pred, ny);
+  if (st.ok()) st = b.get(&dpre, ny);
+  if (st.ok()) st = b.get(&gxd, nx);
+  if (st.ok()) st = b.get(&dwd, nw);
+  if (st.ok()) st = wb::cuda_status(cudaMemcpyAsync(gyd, gy, ny * 4, cudaMemcpyHostToDevice, s->stream), "H2D");
+  if (st.ok()) st = wb::cuda_status(cudaMemcpyAsync(xd, x, nx * 4, cudaMemcpyHostToDevice, s->stream), "H2D");
+  if (st.ok()) st = wb::cuda_status(cudaMemcpyAsync(pred, pre, ny * 4, cudaMemcpyHostToDevice, s->stream), "H2D");
+  if (st.ok()) st = wb::dense_backward_device(s->dev, batch, gyd, xd, pred, linear, dpre, gxd, dwd, s->stream);
+  if (st.ok() && gx_host)
+    st = wb::cuda_status(cudaMemcpyAsync(gx_host, gxd, nx * 4, cudaMemcpyDeviceToHost, s->stream), "D2H");
+  if (st.ok() && dw_host)
+    st = wb::cuda_status(cudaMemcpyAsync(dw_host, dwd, nw * 4, cudaMemcpyDeviceToHost, s->stream), "D2H");
+  const wb::Status sync = wb::cuda_status(cudaStreamSynchronize(s->stream), "backward sync");
+  if (st.ok()) st = sync;
+  return st.ok() ? welvet::Status::Ok() : from_wb(st);
 }
 
 wb::Status grow(float** p, size_t n) {
@@ -164,6 +258,60 @@ Status WeightStore::make(int rows, int cols, DType dt, const float* init_or_null
   return Status::Ok();
 }
 
+// src/weights/store.cpp:42-70: decoded values (weight_at per element), on the GPU.
+Status WeightStore::export_f32(float* dst) const {
+  if (!dst) return invalid("weights: nil dst");
+  if (format != QuantFormat::None) return Status::Err(StatusCode::Gap, "gap? export_f32 packed formats");
+  if (auto st = payload_ok(*this); !st) return st;
+  const int64_t n = static_cast<int64_t>(rows) * cols;
+  if (n <= 0) return Status::Ok();
+  if (dtype == DType::Float32) {
+    std::memcpy(dst, f32.data(), static_cast<size_t>(n) * sizeof(float));
+    return Status::Ok();
+  }
+  int device = 0;
+  if (auto s = wb::library_device(&device); !s.ok()) return from_wb(s);
+  wb::Status st = wb::cuda_status(cudaSetDevice(device), "cudaSetDevice");
+  DevBufs b;
+  uint8_t* nat = nullptr;
+  float* out = nullptr;
+  const size_t nb = native.size();
+  if (st.ok()) st = b.get(&nat, nb);
+  if (st.ok()) st = b.get(&out, static_cast<size_t>(n));
+  if (st.ok()) st = wb::cuda_status(cudaMemcpy(nat, native.data(), nb, cudaMemcpyHostToDevice), "H2D");
+  if (st.ok()) st = wb::decode_ref(static_cast<wb::DType>(dtype), nat, n, scale, out, nullptr);
+  if (st.ok())
+    st = wb::cuda_status(cudaMemcpy(dst, out, static_cast<size_t>(n) * sizeof(float), cudaMemcpyDeviceToHost), "D2H");
+  return st.ok() ? Status::Ok() : from_wb(st);
+}
+
+// src/weights/native_codec.cpp:1080-1133: per element decode, float(double(v) - lr * dW),
+// re-encode; Float32 masters take w -= float(lr * dW). One GPU pass over the payload.
+Status WeightStore::apply_sgd(const double* dW, double lr) {
+  if (!dW) return invalid("weights: ApplySGD nil dW");
+  if (format != QuantFormat::None) return Status::Err(StatusCode::Gap, "gap? weights.ApplySGD packed quant formats");
+  if (auto st = payload_ok(*this); !st) return st;
+  const int64_t n = static_cast<int64_t>(rows) * cols;
+  if (n <= 0) return Status::Ok();
+  int device = 0;
+  if (auto s = wb::library_device(&device); !s.ok()) return from_wb(s);
+  wb::Status st = wb::cuda_status(cudaSetDevice(device), "cudaSetDevice");
+  size_t bytes = 0;
+  const void* host = payload_of(*this, &bytes);
+  DevBufs b;
+  uint8_t* pay = nullptr;
+  double* dwd = nullptr;
+  if (st.ok()) st = b.get(&pay, bytes);
+  if (st.ok()) st = b.get(&dwd, static_cast<size_t>(n));
+  if (st.ok()) st = wb::cuda_status(cudaMemcpy(pay, host, bytes, cudaMemcpyHostToDevice), "H2D");
+  if (st.ok())
+    st = wb::cuda_status(cudaMemcpy(dwd, dW, static_cast<size_t>(n) * sizeof(double), cudaMemcpyHostToDevice), "H2D");
+  if (st.ok()) st = wb::apply_sgd_native(static_cast<wb::DType>(dtype), pay, n, scale, dwd, lr, nullptr);
+  void* back = dtype == DType::Float32 ? static_cast<void*>(f32.data()) : static_cast<void*>(native.data());
+  if (st.ok()) st = wb::cuda_status(cudaMemcpy(back, pay, bytes, cudaMemcpyDeviceToHost), "D2H");
+  return st.ok() ? Status::Ok() : from_wb(st);
+}
+
 namespace cuda {
 
 void resident_release(ResidentDense* r) {
@@ -229,6 +377,76 @@ Status forward_f32(const Layer& layer, const TensorF32& input, TensorF32* pre, T
   *post = TensorF32::zeros(batch, out);
   return from_wb(wb::session_execute(static_cast<wb::DenseSession*>(layer.gpu.session), input.data.data(),
                                      pre->data.data(), post->data.data()));
+}
+
+// src/layers/dense/dense.cpp:88-120.
+Status backward_f32(const Layer& layer, const TensorF32& grad_out, const TensorF32& input, const TensorF32& pre,
+                    TensorF32* grad_in, TensorF32* grad_w) {
+  if (!grad_in || !grad_w) return invalid("dense: nil grad out");
+  if (input.shape.size() != 2 || grad_out.shape.size() != 2 || pre.shape.size() != 2)
+    return invalid("dense: bad shapes");
+  const int batch = static_cast<int>(input.shape[0]);
+  const int in = layer.input_height;
+  const int out = layer.output_height;
+  const size_t bi = static_cast<size_t>(batch > 0 ? batch : 0) * static_cast<size_t>(in);
+  const size_t bo = static_cast<size_t>(batch > 0 ? batch : 0) * static_cast<size_t>(out);
+  if (batch <= 0 || input.data.size() != bi || pre.data.size() != bo || grad_out.data.size() != bo ||
+      static_cast<int>(input.shape[1]) != in || static_cast<int>(grad_out.shape[0]) != batch ||
+      static_cast<int>(grad_out.shape[1]) != out || static_cast<int>(pre.shape[0]) != batch ||
+      static_cast<int>(pre.shape[1]) != out)
+    return invalid("dense: bwd shape mismatch");
+  if (layer.weights.rows != out || layer.weights.cols != in) return invalid("dense: weight shape mismatch");
+  *grad_in = TensorF32::zeros(batch, in);
+  *grad_w = TensorF32::zeros(out, in);
+  return run_backward(layer, batch, grad_out.data.data(), input.data.data(), pre.data.data(), false,
+                      grad_in->data.data(), grad_w->data.data());
+}
+
+// src/layers/dense/dense.cpp:141-166: no act', pre unused (zeros).
+Status linear_grad_in(const Layer& layer, const TensorF32& gy, const TensorF32& input, TensorF32* gx) {
+  if (!gx || input.shape.size() != 2 || input.data.empty() || gy.data.empty())
+    return invalid("dense: LinearGradIn input");
+  const int batch = static_cast<int>(input.shape[0]);
+  const int in = layer.input_height;
+  const int out = layer.output_height;
+  if (batch <= 0 || input.data.size() != static_cast<size_t>(batch) * static_cast<size_t>(in) ||
+      static_cast<int>(input.shape[1]) != in)
+    return invalid("dense: LinearGradIn shape");
+  std::vector<float> projected;
+  remap_len(gy.data, batch * out, &projected);
+  std::vector<float> pre(static_cast<size_t>(batch) * out, 0.0f);
+  *gx = TensorF32::zeros(batch, in);
+  return run_backward(layer, batch, projected.data(), input.data.data(), pre.data(), true, gx->data.data(), nullptr);
+}
+
+// src/layers/dense/dense.cpp:168-190: the full backward with a resampled gy; only dW is kept.
+Status grad_w_only(const Layer& layer, const TensorF32& gy, const TensorF32& input, const TensorF32& pre,
+                   TensorF32* dw) {
+  if (!dw || input.shape.size() != 2 || gy.data.empty()) return invalid("dense: GradWOnly input");
+  const int batch = static_cast<int>(input.shape[0]);
+  const int in = layer.input_height;
+  const int out = layer.output_height;
+  if (batch <= 0 || input.data.size() != static_cast<size_t>(batch) * static_cast<size_t>(in))
+    return invalid("dense: GradWOnly shape");
+  TensorF32 projected;
+  projected.shape = {batch, out};
+  remap_len(gy.data, batch * out, &projected.data);
+  TensorF32 use_pre = pre;
+  if (use_pre.data.size() < static_cast<size_t>(batch) * static_cast<size_t>(out) || use_pre.shape.size() != 2)
+    use_pre = TensorF32::zeros(batch, out);
+  TensorF32 gx;
+  return backward_f32(layer, projected, input, use_pre, &gx, dw);
+}
+
+// src/layers/dense/dense.cpp:192-209.
+Status apply_grad_sgd(Layer* layer, const TensorF32& dW, double lr) {
+  if (!layer) return invalid("dense: nil SGD layer");
+  const int64_t n = static_cast<int64_t>(layer->weights.rows) * layer->weights.cols;
+  if (static_cast<int64_t>(dW.data.size()) < n) return invalid("dense: dW short");
+  std::vector<double> buf(dW.data.begin(), dW.data.begin() + n);
+  if (auto st = layer->weights.apply_sgd(buf.data(), lr); !st) return st;
+  layer->invalidate_gpu();
+  return Status::Ok();
 }
 
 } // namespace dense
