@@ -51,6 +51,7 @@ C5_IN, C5_OUT = 16384, 65536
 FP4, E4M3, E5M2, INT8 = 16, 4, 5, 9
 SIGMA = 0.02
 C5_BYTES = C5_OUT * C5_IN // 2  # FP4: 0.5 B / weight
+L2_BYTES = 126 * 1000 * 1000
 METRIC = "quant Dense weight GB/s (GEMV, % HBM) and TFLOP/s (batched, % tensor) at 1/2/4/8 B200"
 
 
@@ -263,6 +264,48 @@ class Ctx:
         self.barrier()
         return self.max_over_ranks(e0.elapsed_time(e1)) / steps
 
+    def timed_calls(self, calls, steps: int, warmup: int) -> float:
+        """ms per step for a rotation of forwards (`calls`, one step each, in the order they must
+        run): after one eager pass the rotation is captured as one CUDA graph (replayed whole)
+        and as one graph per call (the last steps % len(calls)); `warmup` steps, then exactly
+        `steps` timed, barrier + synchronize on both sides, CUDA events on the launching stream,
+        max over ranks."""
+        torch = self.torch
+        for f in calls:
+            f()
+        torch.cuda.synchronize()
+        whole = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(whole):
+            for f in calls:
+                f()
+        singles = []
+        for f in calls:
+            gph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gph):
+                f()
+            singles.append(gph)
+        self.graphs.extend([whole, *singles])
+
+        def run(n):
+            q, r = divmod(n, len(calls))
+            for _ in range(q):
+                whole.replay()
+            for i in range(r):
+                singles[i].replay()
+        return self._timed_run(run, steps, warmup)
+
+    def _timed_run(self, run, steps: int, warmup: int) -> float:
+        torch = self.torch
+        run(warmup)
+        self.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
+        run(steps)
+        e1.record(self.stream)
+        self.barrier()
+        return self.max_over_ranks(e0.elapsed_time(e1)) / steps
+
     def graphed(self, fn, n: int = 1):
         """`fn` captured in n CUDA graphs of one call each, replayed in turn (a sharded call
         alternates between two output buffers, so it is captured twice). One eager call first."""
@@ -299,27 +342,40 @@ class Ctx:
         return statistics.median(ts)
 
 
+def sharded_copies(shard_bytes: int) -> int:
+    """Weight copies a rank rotates through so that consecutive steps read more than twice the
+    126 MB L2 (one copy when the shard alone is that large)."""
+    return max(1, -(-2 * L2_BYTES // max(1, shard_bytes)))
+
+
 def sharded_legs(c: Ctx, batch: int, steps: int, warmup: int, W_rows, b: int, e: int):
-    """Fused, nccl and compute-only forwards of the headline layer at `batch` tokens."""
+    """Fused, nccl and compute-only forwards of the headline layer at `batch` tokens. Each leg
+    rotates over `copies` mounts of this rank's rows (sharded_copies); every sharded object is
+    called twice per rotation (its two output buffers)."""
     torch, W, V = c.torch, c.W, c.V
     g = torch.Generator(device="cuda").manual_seed(4)
     x = torch.randn((batch, C5_IN), device="cuda", generator=g)
-    res = {}
-    # every leg is replayed from CUDA graphs (one graph launch per step); the sharded call is
-    # captured twice, once per output buffer
-    fused = V.ShardedDense(c.comm, W_rows, C5_IN, C5_OUT, batch, FP4, W.LINEAR, None, V.FUSED)
-    res["fused_ms"] = c.timed(c.graphed(lambda: fused.execute_device_ptrs(x), 2), steps, warmup)
-    fused.check_error()
-    nccl = V.ShardedDense(c.comm, W_rows, C5_IN, C5_OUT, batch, FP4, W.LINEAR, None, V.NCCL)
-    res["nccl_ms"] = c.timed(c.graphed(lambda: nccl.execute_device_ptrs(x), 2), steps, warmup)
-    nccl.check_error()
-    local = W.DenseSession(W_rows, batch, FP4) if e > b else None
-    if local is not None:
+    copies = sharded_copies((e - b) * C5_IN // 2)
+    res = {"copies": copies}
+    fused = [V.ShardedDense(c.comm, W_rows, C5_IN, C5_OUT, batch, FP4, W.LINEAR, None, V.FUSED) for _ in range(copies)]
+    res["fused_ms"] = c.timed_calls([(lambda o=o: o.execute_device_ptrs(x)) for _ in range(2) for o in fused],
+                                    steps, warmup)
+    for o in fused:
+        o.check_error()
+    nccl = [V.ShardedDense(c.comm, W_rows, C5_IN, C5_OUT, batch, FP4, W.LINEAR, None, V.NCCL) for _ in range(copies)]
+    res["nccl_ms"] = c.timed_calls([(lambda o=o: o.execute_device_ptrs(x)) for _ in range(2) for o in nccl],
+                                   steps, warmup)
+    for o in nccl:
+        o.check_error()
+    local = [W.DenseSession(W_rows, batch, FP4) for _ in range(copies)] if e > b else []
+    if local:
         pre = torch.empty((batch, e - b), device="cuda")
-        res["compute_ms"] = c.timed(c.graphed(lambda: local.execute_device(x, pre, pre)), steps, warmup)
+        res["compute_ms"] = c.timed_calls([(lambda o=o: o.execute_device(x, pre, pre)) for o in local], steps, warmup)
+        for o in local:
+            o.check_error()
     else:
         res["compute_ms"] = c.timed(lambda: None, steps, warmup)
-    return res, (fused, nccl), local, x
+    return res, fused + nccl, local, x
 
 
 def run_ours(args):
@@ -342,7 +398,9 @@ def run_ours(args):
     torch.cuda.empty_cache()
     ms = s1["fused_ms"]
     value = C5_BYTES / (ms / 1e3) / 1e9
-    c.launches = args.steps * (2 if world > 1 else 1)  # GEMV (+ flag exchange) per step
+    # per step: k_prep_x + k_gemv_tc (the prepared plan of a layer of >= 8192 rows), plus
+    # k_flag_exchange when N > 1
+    c.launches = args.steps * (3 if world > 1 else 2)
     flops256 = 2.0 * 256 * C5_OUT * C5_IN
 
     # roofline of the headline's dominant kernel: this rank's GEMV, timed alone (compute-only
@@ -388,7 +446,7 @@ def run_ours(args):
     ph = torch.zeros((1, C5_OUT)).pin_memory()
     if world == 1:
         c_exec = W.lib().welvet_dense_execute
-        h = local1._h
+        h = local1[0]._h
         px, pp, py = ctypes.c_void_p(xh.data_ptr()), ctypes.c_void_p(ph.data_ptr()), ctypes.c_void_p(yh.data_ptr())
 
         def e2e_step():
@@ -417,9 +475,8 @@ def run_ours(args):
            "d2h_bytes_per_step": C5_OUT * 4 * world, "steps": e2e_steps, "api": api}
     c.graphs.clear()
     torch.cuda.synchronize()
-    for s in (*fused1, *fused256, local1, local256):
-        if s is not None:
-            s.release()
+    for s in (*fused1, *fused256, *local1, *local256):
+        s.release()
     torch.cuda.empty_cache()
 
     # ---- C5's volume: one GPU runs the chain, N GPUs the cell-per-GPU pipeline

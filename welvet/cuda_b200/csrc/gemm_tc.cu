@@ -434,6 +434,10 @@ struct TmParams {
   uint32_t acc_buf;             // columns of one accumulator buffer when there are two, else 0
   PeerOut peers;                // further destinations of post (direct stores)
   int n_peer_maps;              // staged stores: peer maps in PeerMaps (post's layout)
+  // Failure-path check (WELVET_B200_TEST_WAIT_TIMEOUT=1): each CTA first waits 1 ms on a
+  // barrier that nothing arrives on, before any copy, TMEM allocation or cluster exchange;
+  // the wait runs out, records code 30 in the error word, and the CTA returns.
+  int probe_wait;
 };
 
 // Tensor maps of the peers' post buffers (column-sharded layers): a staged chunk's post values
@@ -662,6 +666,14 @@ __global__ void __launch_bounds__(kTmThreads, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t v = kPair ? cluster_ctarank() : 0u;  // rank in the pair (0 issues the MMAs)
 
+  if (p.probe_wait) {  // uniform over the grid: every thread of every CTA returns here
+    if (threadIdx.x == 0) {
+      mbar_init(&w_full[0], 1);
+      mbar_wait_for(&w_full[0], 0, p.err, 30, 1000000ull);
+    }
+    __syncthreads();
+    return;
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < Sw; ++s) {
       mbar_init(&w_full[s], 1);
@@ -1541,7 +1553,11 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_
   const int sub = pl.pair ? 2 : 1;
   const int tiles =
       static_cast<int>(((rows + kBM - 1) / kBM / sub) * static_cast<int64_t>((M + pl.TB - 1) / pl.TB));
-  const int splits = tm_splits(tiles, pl.nkb, M, rows, units);
+  int splits = tm_splits(tiles, pl.nkb, M, rows, units);
+  if (const char* e = std::getenv("WELVET_B200_GEMM_SPLITS")) {  // tuning override (1..16)
+    const int n = std::atoi(e);
+    if (n >= 1 && n <= 16 && n <= pl.nkb) splits = n;
+  }
   pl.kb_per_split = (pl.nkb + splits - 1) / splits;
   pl.splits = (pl.nkb + pl.kb_per_split - 1) / pl.kb_per_split;
   pl.planes_bytes = static_cast<size_t>(round_up(static_cast<int64_t>(xsplit) * pl.Mp * pl.Kp * 2, 1024));
@@ -1822,6 +1838,7 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
   p.pre = a.pre; p.post = a.post; p.ld_out = a.ld_out;
   p.bias = a.bias; p.bias_len = a.bias_len; p.act = a.act;
   p.partial = partial; p.err = a.err;
+  if (const char* e = std::getenv("WELVET_B200_TEST_WAIT_TIMEOUT")) p.probe_wait = e[0] == '1' ? 1 : 0;
   p.pair = a.pair ? 1 : 0; p.w_scale2 = a.scale2; p.h = a.h; p.ld_h = a.ld_h;
   p.silu_exact = silu_exact() ? 1 : 0;
   p.tiles_t = pl.tiles_t; p.tail_first = pl.tail_first; p.tail_s = pl.tail_s; p.tail_kbps = pl.tail_kbps;

@@ -80,13 +80,23 @@ Plan make_plan(DType dt, int rows, int cols, bool grouped = false, int batch = 1
       }
     }
   }
-  if (const char* env = batch <= 8 ? std::getenv("WELVET_B200_GEMV_CPW") : nullptr) {  // tuning override
-    const int c = std::atoi(env);
-    if (c >= 1 && c <= 64 && (p.chunks + kWarps * c - 1) / (kWarps * c) <= kMaxCluster) p.cpw = c;
-  }
+  // Tuning override, read once per process: the prepared-fragment scratch a session
+  // allocates is sized from this plan, so the plan must not change under it.
+  static const int cpw_env = [] {
+    const char* e = std::getenv("WELVET_B200_GEMV_CPW");
+    return e ? std::atoi(e) : 0;
+  }();
+  if (batch <= 8 && cpw_env >= 1 && cpw_env <= 64 &&
+      (p.chunks + kWarps * cpw_env - 1) / (kWarps * cpw_env) <= kMaxCluster)
+    p.cpw = cpw_env;
   if (grouped) {
+    // Up to 8 chunks per warp; 16 for layers of 256 row sets or more, which fill the GPU
+    // with half as many CTAs of twice the K range (measured, 16384-column FP4 at 1 token:
+    // 65536 rows 102.7 -> 96.1 us, 32768 rows 56.5 -> 54.2, 16384 rows 31.2 -> 30.0; at 8192
+    // rows 16 was slower, 17.5 -> 27.7).
     const int64_t per_warp = (p.chunks + kWarps - 1) / kWarps;
-    const int longer = static_cast<int>(per_warp < 8 ? per_warp : 8);
+    const int cap = p.row_sets >= 256 ? 16 : 8;
+    const int longer = static_cast<int>(per_warp < cap ? per_warp : cap);
     if (longer > p.cpw) p.cpw = longer;  // never fewer chunks than the cluster limit needs
   }
   if (p.cpw < 2) p.cpw = 2;
@@ -591,10 +601,10 @@ __global__ void k_build_tiled(const uint8_t* __restrict__ native, int rows, int 
   }
 }
 
-// Prepares the x of grouped layers once per layer: block (seg, layer) takes the largest finite
-// |x| of K segment seg per token, the power-of-two scale of that segment, and writes the f16
-// B fragments of the segment in the layout the GEMV's CTAs use -- exactly what each CTA of
-// that segment would build itself.
+// Prepares the x of grouped layers once per layer: the kPrepSub blocks (seg * kPrepSub + sub,
+// layer) of K segment seg each take the largest finite |x| of the segment per token and its
+// power-of-two scale, and write their share of the segment's f16 B fragments in the layout
+// the GEMV's CTAs use -- exactly what each CTA of that segment would build itself.
 template <int kL>
 struct PrepArgs {
   int cols = 0, nkb_cta = 0;
@@ -606,26 +616,66 @@ struct PrepArgs {
 };
 
 constexpr int kPrepThreads = 256;
+// Blocks per K segment: each takes the segment's scale itself (the segment is at most 8192
+// floats per token, read from L2 with every load of a thread in flight at once) and writes
+// its share of the fragments. One block per segment issued its loads one after another and
+// took ~6 us per launch at 8192 x 16384; the dependent GEMV waits for it.
+constexpr int kPrepSub = 8;
 
 template <int kB, int kL>
 __global__ void __launch_bounds__(kPrepThreads) k_prep_x(const __grid_constant__ PrepArgs<kL> pa) {
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // x may be the previous kernel's output
   constexpr int NCOL = 2 * kB;
+  constexpr int kU = 8;  // loads in flight per thread in the scale pass
   __shared__ float smax[kPrepThreads / 32][kB];
   __shared__ float ssc[kB];
-  const int seg = blockIdx.x, layer = blockIdx.y;
+  const int seg = blockIdx.x / kPrepSub, sub = blockIdx.x % kPrepSub, layer = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* x = pa.x[layer];
   const int kspan = pa.nkb_cta * 16;
   const int64_t klo = static_cast<int64_t>(seg) * kspan;
   const int64_t khi = klo + kspan < pa.cols ? klo + kspan : pa.cols;
-#pragma unroll
+#pragma unroll 1
   for (int b = 0; b < kB; ++b) {
     float m = 0.0f;
-    for (int64_t k = klo + tid; k < khi && b < pa.nb; k += kPrepThreads) {
-      const float av = fabsf(ld_dep(x + b * pa.x_ld + k));
-      if (av > m && av <= 3.402823466e+38f) m = av;
+    if (b < pa.nb) {
+      const float* xb = x + b * pa.x_ld;
+      // klo is a multiple of 64: 16-byte vectors whenever the token's row is 16-byte aligned
+      if ((reinterpret_cast<uintptr_t>(xb) & 15) == 0) {
+        for (int64_t k0 = klo + 4 * tid; k0 < khi; k0 += 4 * kPrepThreads * kU) {
+          float4 v[kU];
+#pragma unroll
+          for (int u = 0; u < kU; ++u) {
+            const int64_t k = k0 + static_cast<int64_t>(u) * 4 * kPrepThreads;
+            v[u] = k + 3 < khi ? ld_dep4(xb + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k < khi && k + 3 >= khi) {  // the segment's ragged end, element by element
+              v[u].x = ld_dep(xb + k);
+              if (k + 1 < khi) v[u].y = ld_dep(xb + k + 1);
+              if (k + 2 < khi) v[u].z = ld_dep(xb + k + 2);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < kU; ++u) {
+            for (float av : {fabsf(v[u].x), fabsf(v[u].y), fabsf(v[u].z), fabsf(v[u].w)})
+              if (av > m && av <= 3.402823466e+38f) m = av;
+          }
+        }
+      } else {
+        for (int64_t k0 = klo + tid; k0 < khi; k0 += kPrepThreads * kU) {
+          float v[kU];
+#pragma unroll
+          for (int u = 0; u < kU; ++u) {
+            const int64_t k = k0 + static_cast<int64_t>(u) * kPrepThreads;
+            v[u] = k < khi ? ld_dep(xb + k) : 0.0f;
+          }
+#pragma unroll
+          for (int u = 0; u < kU; ++u) {
+            const float av = fabsf(v[u]);
+            if (av > m && av <= 3.402823466e+38f) m = av;
+          }
+        }
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -638,12 +688,14 @@ __global__ void __launch_bounds__(kPrepThreads) k_prep_x(const __grid_constant__
     for (int w = 1; w < kPrepThreads / 32; ++w) m = fmaxf(m, smax[w][tid]);
     const int e = x_scale_exp(m);
     ssc[tid] = ldexpf(1.0f, e);
-    pa.fscale[layer][seg * kB + tid] = ldexpf(1.0f, -e);
+    if (sub == 0) pa.fscale[layer][seg * kB + tid] = ldexpf(1.0f, -e);
   }
   __syncthreads();
   uint2* fr = pa.frags[layer] + static_cast<int64_t>(seg) * pa.nkb_cta * NCOL * 4;
   const int nent = pa.nkb_cta * kB * 4;
-  for (int e = tid; e < nent; e += kPrepThreads) {
+  const int per = (nent + kPrepSub - 1) / kPrepSub;
+  const int e_end = (sub + 1) * per < nent ? (sub + 1) * per : nent;
+  for (int e = sub * per + tid; e < e_end; e += kPrepThreads) {
     const int kbl = e / (kB * 4);
     const int rem = e - kbl * (kB * 4);
     const int b = rem >> 2, tt = rem & 3;
@@ -664,7 +716,7 @@ __global__ void __launch_bounds__(kPrepThreads) k_prep_x(const __grid_constant__
 template <int kL>
 Status launch_prep(const PrepArgs<kL>& pa, int csize, int nl, int batch, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(csize), static_cast<unsigned>(nl), 1);
+  cfg.gridDim = dim3(static_cast<unsigned>(csize * kPrepSub), static_cast<unsigned>(nl), 1);
   cfg.blockDim = dim3(kPrepThreads);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

@@ -59,6 +59,18 @@ static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parit
   }
 }
 
+// A wait with its own limit (ns) on the same terms.
+static __device__ __noinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err, int code, uint64_t ns) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > ns) {
+      if (err) atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+  return true;
+}
+
 // The common case (phase already complete) stays inline; the bounded loop is out of line.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;

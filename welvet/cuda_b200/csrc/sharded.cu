@@ -33,9 +33,12 @@ __device__ __forceinline__ uint64_t global_ns() {
 // first -- and then waits until rank s has published the same number here. The wait is
 // bounded: past `limit_ns` it records bit 0 in *err and gives up. Launched as a programmatic
 // dependent of the forward's last kernel: it is resident early and starts the moment that
-// kernel's grid has completed and its stores are visible (griddepcontrol.wait).
+// kernel's grid has completed and its stores are visible (griddepcontrol.wait). It lets its
+// own dependents launch at once: the next call's kernels start streaming their weights while
+// this exchange waits, and wait themselves for its completion before touching any output.
 __global__ void k_flag_exchange(FlagPtrs peers, const uint32_t* mine, uint32_t* count, int nranks, int rank,
                                 int* err, unsigned long long limit_ns) {
+  asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int s = threadIdx.x;
   const uint32_t epoch = *count + 1u;  // read by every lane before lane 0 updates it below
@@ -241,7 +244,9 @@ Status sharded_execute_device(ShardedDense* s, const float* x, cudaStream_t st, 
       PeerOut peers;
       for (int r = 0; r < c->nranks; ++r)
         if (r != c->rank) peers.post[peers.n++] = static_cast<float*>(ob.ptr[static_cast<size_t>(r)]) + s->row_begin;
-      WB_TRY(forward_device(s->dev, s->batch, x, s->in, ypre + s->row_begin, y + s->row_begin, &s->io, st, false,
+      // a programmatic dependent of whatever precedes it on the stream (the previous call's
+      // flag exchange): its first kernel waits for that kernel's completion before reading x
+      WB_TRY(forward_device(s->dev, s->batch, x, s->in, ypre + s->row_begin, y + s->row_begin, &s->io, st, true,
                             s->out, &peers));
     }
     ++s->epoch;
