@@ -15,6 +15,7 @@
 
 #include <cmath>
 #include <cstdlib>
+#include <cstring>
 #include <vector>
 
 namespace wb {
@@ -96,8 +97,18 @@ Status swiglu_mount_src(int device, int in, int inter, DType dt, const WeightSrc
 // (tcgen05) every larger batch of quantized, non-exact layers. WELVET_B200_GEMV16=1 runs 5..16
 // rows as two tensor GEMVs (Gate, Up) and the reference's product instead (measured slower on
 // B200: 16 rows of the 4096 / 14336 E4M3 cell take 370 us against 130 us on the pair GEMM).
-static bool swiglu_dual_gemv(const SwigluCell* c, int bs) {
+// 1..4 rows on the tensor GEMV: either the fused Gate/Up form (one kernel streams both weight
+// sets, the epilogue writes h) or, with WELVET_B200_SWIGLU_GEMV=group, Gate and Up as one
+// grouped launch of two layers (x prepared once per layer) followed by the product kernel.
+static bool swiglu_group_mode() {
+  const char* e = std::getenv("WELVET_B200_SWIGLU_GEMV");
+  return e && std::strcmp(e, "group") == 0;
+}
+static bool swiglu_small_gemv(const SwigluCell* c, int bs) {
   return bs <= 4 && use_gemv_tc(c->gate, bs) && c->up.Wt;
+}
+static bool swiglu_group_gemv(const SwigluCell* c, int bs) {
+  return swiglu_small_gemv(c, bs) && swiglu_group_mode() && use_gemv_tc(c->up, bs);
 }
 static bool swiglu_split_gemv(const SwigluCell* c, int bs) {
   if (std::getenv("WELVET_B200_BATCHED") != nullptr) return false;
@@ -120,7 +131,7 @@ Status swiglu_reserve(SwigluCell* c, int bs, cudaStream_t st) {
   WB_CUDA(cudaMemsetAsync(c->x_pad, 0, xb, st));
   WB_CUDA(cudaMalloc(&c->h_pad, hb));
   WB_CUDA(cudaMemsetAsync(c->h_pad, 0, hb, st));
-  if (swiglu_split_gemv(c, bs)) {
+  if (swiglu_split_gemv(c, bs) || swiglu_group_gemv(c, bs)) {
     WB_CUDA(cudaMalloc(&c->g_buf, static_cast<size_t>(bs) * c->inter * 4));
     WB_CUDA(cudaMalloc(&c->u_buf, static_cast<size_t>(bs) * c->inter * 4));
     WB_TRY(alloc_io(c->gate, bs, &c->io_gate, st));  // prepared-fragment scratch of each GEMV
@@ -148,7 +159,38 @@ Status swiglu_forward_device(SwigluCell* c, int bs, const float* x, float* h, fl
   WB_TRY(swiglu_reserve(c, bs, st));
   const float* hsrc = nullptr;  // h as Down's input
   int64_t h_ld = 0;
-  if (swiglu_dual_gemv(c, bs)) {
+  if (swiglu_group_gemv(c, bs) && c->g_buf && c->io_gate.prep && c->io_up.prep) {
+    // 1..4 rows, grouped: Gate and Up in one launch of two layers, then the reference's
+    // SiLU product into h
+    GemvGroupLayer L[2];
+    const DeviceDense* d[2] = {&c->gate, &c->up};
+    float* out[2] = {c->g_buf, c->u_buf};
+    DenseIO* io[2] = {&c->io_gate, &c->io_up};
+    for (int i = 0; i < 2; ++i) {
+      L[i].Wt = d[i]->Wt;
+      L[i].x = x;
+      L[i].pre = out[i];
+      L[i].post = out[i];
+      L[i].bias = d[i]->bias;
+      L[i].bias_len = d[i]->bias_len;
+      L[i].act = d[i]->act;
+      L[i].scale = d[i]->scale;
+      L[i].prep = io[i]->prep;
+    }
+    WB_TRY(launch_gemv_tc_group(c->gate.dtype, c->inter, c->in, bs, c->in, c->inter, L, 2, st, pdl, nullptr));
+    float* hout = h ? h : c->h_pad;
+    const int64_t ld = h ? c->inter : c->down.x_stride;
+    if (ld == c->inter) {
+      WB_TRY(launch_swiglu_product(c->g_buf, c->u_buf, hout, static_cast<int64_t>(bs) * c->inter, st));
+    } else {
+      WB_TRY(launch_swiglu_product(c->g_buf, c->u_buf, c->g_buf, static_cast<int64_t>(bs) * c->inter, st));
+      WB_CUDA(cudaMemcpy2DAsync(hout, static_cast<size_t>(ld) * 4, c->g_buf, static_cast<size_t>(c->inter) * 4,
+                                static_cast<size_t>(c->inter) * 4, static_cast<size_t>(bs),
+                                cudaMemcpyDeviceToDevice, st));
+    }
+    hsrc = hout;
+    h_ld = ld;
+  } else if (swiglu_small_gemv(c, bs)) {
     // 1..4 rows: Gate and Up stream together through the tensor-core GEMV, whose epilogue
     // writes h directly.
     GemvTcArgs a;

@@ -288,6 +288,7 @@ Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x
     g.scratch = io->scratch;
     g.scratch_bytes = io->scratch_bytes;
     g.err = io->err;
+    g.pdl = pdl_in;
     return launch_gemm_tc(g, st);
   }
   if (use_gemv_tc(d, batch) && io && io->prep && gemv_prefers_prepared(d.dtype, d.rows, d.cols, batch)) {

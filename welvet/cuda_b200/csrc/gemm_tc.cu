@@ -34,6 +34,7 @@
 #include <mutex>
 #include <tuple>
 #include <type_traits>
+#include <utility>
 #include <vector>
 
 namespace wb {
@@ -646,6 +647,11 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     k_gemm_tm(const __grid_constant__ CUtensorMap tm_x1, const __grid_constant__ CUtensorMap tm_x2,
               const __grid_constant__ CUtensorMap tm_x3, const __grid_constant__ CUtensorMap tm_o1,
               const __grid_constant__ CUtensorMap tm_o2, const __grid_constant__ PeerMaps pm, const TmParams p) {
+  // A programmatic dependent of k_split_x: every thread waits for it (and, through its own
+  // wait, for everything before it) before any global access; the reduce that follows may
+  // launch at once and waits for this grid in turn.
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = p.sx, Sw = p.sw;
@@ -1185,6 +1191,8 @@ __global__ void __launch_bounds__(kTmThreads, 1)
 
 // Sum of the split-K partials in a fixed order, then the reference epilogue.
 __global__ void k_splitk_reduce(const KParams p) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the GEMM's partials
   const int64_t n = static_cast<int64_t>(p.M) * p.rows;
   if (p.pair) {  // one thread per (token, Gate/Up pair)
     const int half = p.rows / 2;
@@ -1233,6 +1241,8 @@ struct TailParams {
 };
 
 __global__ void k_tail_reduce(const TailParams p) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the GEMM's partials
   const int per_tile = p.TB * (p.pair ? 64 : 128);
   const int64_t n = static_cast<int64_t>(p.ntail) * p.sub * per_tile;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
@@ -1279,8 +1289,12 @@ __global__ void k_tail_reduce(const TailParams p) {
 // One 256-thread block per token row (grid = Mp); rows >= M and columns >= K are zero.
 constexpr int kSplitThreads = 256;
 __global__ void __launch_bounds__(kSplitThreads)
-    k_split_x(const float* __restrict__ x, int64_t x_ld, int M, int K, int Mp, int Kp, int xsplit,
+    k_split_x(const float* x, int64_t x_ld, int M, int K, int Mp, int Kp, int xsplit,
               __half* __restrict__ planes, float* __restrict__ scale_inv, int* __restrict__ pcnt) {
+  // x may be the previous kernel's output: ordered loads after the wait (ld_dep), never
+  // non-coherent ones, which may be hoisted above it
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ float s_max[kSplitThreads / 32];
   __shared__ int s_nz;
   const int t = blockIdx.x;
@@ -1289,11 +1303,13 @@ __global__ void __launch_bounds__(kSplitThreads)
   const float* xr = x + static_cast<int64_t>(t) * x_ld;
   const bool live = t < M;
   float amax = 0.0f;
-  if (live)
+  if (live) {
+#pragma unroll 4
     for (int k = tid; k < K; k += kSplitThreads) {
-      const float a = fabsf(xr[k]);
+      const float a = fabsf(ld_dep(xr + k));
       if (a > amax && a <= 3.402823466e+38f) amax = a;
     }
+  }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
   if (lane == 0) s_max[warp] = amax;
@@ -1313,8 +1329,9 @@ __global__ void __launch_bounds__(kSplitThreads)
   const int64_t plane = static_cast<int64_t>(Mp) * Kp;
   __half* p0 = planes + static_cast<int64_t>(t) * Kp;
   bool nz1 = false, nz2 = false;
+#pragma unroll 4
   for (int k = tid; k < Kp; k += kSplitThreads) {
-    const float v = (live && k < K) ? xr[k] : 0.0f;
+    const float v = (live && k < K) ? ld_dep(xr + k) : 0.0f;
     __half h0, h1 = __float2half_rn(0.0f), h2 = __float2half_rn(0.0f);
     if (isfinite(v)) {
       const float vs = v * s;
@@ -1743,6 +1760,23 @@ TmKernel tm_kernel(DType dt, bool pair) {
   }
 }
 
+// A launch with programmatic stream serialization (when `pdl`).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 cudaLaunchConfig_t pair_config(unsigned pairs, size_t smem, cudaStream_t st, cudaLaunchAttribute* at) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
@@ -1753,8 +1787,10 @@ cudaLaunchConfig_t pair_config(unsigned pairs, size_t smem, cudaStream_t st, cud
   at[0].val.clusterDim.x = 2;
   at[0].val.clusterDim.y = 1;
   at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cfg;
 }
 
@@ -1773,7 +1809,7 @@ int tm_max_pairs(TmKernel kern, size_t smem) {
   }
   int n = 0;
   if (set_max_smem(key, smem).ok()) {
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     const cudaLaunchConfig_t cfg = pair_config(74, smem, nullptr, at);
     if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
       (void)cudaGetLastError();
@@ -1811,9 +1847,8 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
                         ? reinterpret_cast<double*>(scr + pl.planes_bytes + pl.scale_bytes + pl.pcnt_bytes)
                         : nullptr;
 
-  k_split_x<<<pl.Mp, kSplitThreads, 0, st>>>(a.x, a.x_ld, a.M, a.cols, pl.Mp, pl.Kp, a.xsplit, planes, scale_inv,
-                                             pcnt);
-  WB_CUDA(cudaGetLastError());
+  WB_CUDA(launch_pdl(k_split_x, dim3(static_cast<unsigned>(pl.Mp)), dim3(kSplitThreads), 0, st, a.pdl, a.x, a.x_ld,
+                     a.M, a.cols, pl.Mp, pl.Kp, a.xsplit, planes, scale_inv, pcnt));
 
   CUtensorMap tm_x[3];
   for (int P = 1; P <= 3; ++P) {
@@ -1906,14 +1941,15 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
   WB_TRY(set_max_smem(reinterpret_cast<const void*>(kern), smem));
   if (pl.pair) {
     // clusters of 2, one pair per item up to the pairs that fit at once
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     const cudaLaunchConfig_t cfg =
         pair_config(static_cast<unsigned>(p.n_items < pairs ? p.n_items : pairs), smem, st, at);
     WB_CUDA(cudaLaunchKernelEx(&cfg, kern, tm_x[0], tm_x[1], tm_x[2], tm_o[0], tm_o[1], pm, p));
   } else {
     const dim3 grid(static_cast<unsigned>(p.n_items < sms ? p.n_items : sms), 1, 1);
-    kern<<<grid, kTmThreads, smem, st>>>(tm_x[0], tm_x[1], tm_x[2], tm_o[0], tm_o[1], pm, p);
-    WB_TRY(cuda_status(cudaGetLastError(), "gemm_tc (tmem) launch"));
+    WB_TRY(cuda_status(launch_pdl(kern, grid, dim3(kTmThreads), smem, st, true, tm_x[0], tm_x[1], tm_x[2], tm_o[0],
+                                  tm_o[1], pm, p),
+                       "gemm_tc (tmem) launch"));
   }
   if (pl.tail_first >= 0) {
     const int ntail = pl.tiles - pl.tail_first;
@@ -1925,8 +1961,7 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
     r.pair = a.pair ? 1 : 0; r.h = a.h; r.ld_h = a.ld_h;
     r.peers = a.peers;
     const int64_t n = static_cast<int64_t>(ntail) * r.sub * pl.TB * (a.pair ? 64 : 128);
-    k_tail_reduce<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(r);
-    WB_CUDA(cudaGetLastError());
+    WB_CUDA(launch_pdl(k_tail_reduce, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, st, true, r));
   }
   if (pl.splits > 1) {
     KParams r{};
@@ -1937,8 +1972,7 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
     const int64_t n = static_cast<int64_t>(a.M) * a.rows;
     int blocks = static_cast<int>((n + 255) / 256);
     if (blocks > 148 * 16) blocks = 148 * 16;
-    k_splitk_reduce<<<blocks, 256, 0, st>>>(r);
-    WB_CUDA(cudaGetLastError());
+    WB_CUDA(launch_pdl(k_splitk_reduce, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, true, r));
   }
   return Status::Ok();
 }

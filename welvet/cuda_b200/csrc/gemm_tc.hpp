@@ -46,6 +46,11 @@ struct GemmArgs {
   int64_t ld_h = 0;
   // Further destinations of post (column-sharded layers, peer memory): same layout as post.
   PeerOut peers;
+  // The launch's first kernel (k_split_x) as a programmatic dependent of the kernel before it
+  // on the stream (it waits for that kernel's completion before reading x). The launch's own
+  // kernels always chain this way: k_split_x -> the GEMM -> the split-K / tail reduce, each
+  // releasing its dependent at once and waiting for its predecessor before any global access.
+  bool pdl = false;
 };
 
 // Token tile (B rows per plane) used for M tokens; the MMA N is xsplit * tile.

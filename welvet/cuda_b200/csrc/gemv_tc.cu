@@ -58,7 +58,7 @@ struct Plan {
 // staging, fragment build, reduction, epilogue) is paid over more bytes.
 // batch > 8 (one layer per launch, prepared fragments of 12 or 16 tokens): the shortest K
 // range per CTA the cluster limit allows, so that the fragments fit in shared memory.
-Plan make_plan(DType dt, int rows, int cols, bool grouped = false, int batch = 1) {
+Plan make_plan(DType dt, int rows, int cols, bool grouped = false, int batch = 1, bool dual = false) {
   Plan p;
   p.g = tiled_geom(dt, rows, cols);
   p.row_sets = (p.g.row_groups + kRG - 1) / kRG;
@@ -70,8 +70,11 @@ Plan make_plan(DType dt, int rows, int cols, bool grouped = false, int batch = 1
   if (!grouped && batch <= 8) {
     // A layer with many row sets fills the GPU by itself: give each CTA a longer K range
     // (fewer CTAs, each paying its fixed x-staging / reduction cost over more bytes) while
-    // keeping at least two waves of CTAs for balance (4 CTAs per SM).
-    constexpr int64_t kMinCtas = 2 * 148 * 4;
+    // keeping at least two waves of CTAs for balance (4 CTAs per SM). The fused Gate/Up form
+    // runs 2 CTAs per SM and is best at about one and a half waves (14336 x 4096 E4M3 pair,
+    // 1 token: 3 waves of 4 chunks per warp 56.4 us for the SwiGLU cell, 1.5 waves of 8 chunks
+    // 52.3 us, 6 waves of 2 chunks 64.6 us).
+    const int64_t kMinCtas = dual ? 148 * 2 : 2 * 148 * 4;
     for (int c = 16; c > p.cpw; c >>= 1) {
       const int64_t cs = (p.chunks + kWarps * c - 1) / (kWarps * c);
       if (p.row_sets * cs >= kMinCtas) {
@@ -860,7 +863,7 @@ Status launch_gemv_tc(const GemvTcArgs& a, cudaStream_t st, bool pdl) {
   if (!gemv_tc_supported(a.dtype)) return Status::Unsupported("gemv_tc: dtype");
   if (a.rows <= 0 || a.cols <= 0 || a.batch < 1 || a.batch > (a.Wt2 ? 4 : kGemvMaxBatch))
     return Status::Invalid("gemv_tc: bad dims");
-  const Plan pl = make_plan(a.dtype, a.rows, a.cols, false, a.batch);
+  const Plan pl = make_plan(a.dtype, a.rows, a.cols, false, a.batch, a.Wt2 != nullptr);
   KArgs k{};
   k.Wt = a.Wt;
   k.Wt2 = a.Wt2;

@@ -69,8 +69,9 @@ Status dense_normalbp(int batch, int in, int out, int act, int32_t dtype, const 
   const size_t nx = static_cast<size_t>(batch) * in, ny = static_cast<size_t>(batch) * out;
   const size_t nw = static_cast<size_t>(out) * in;
   Scratch s;
-  float *xd, *pred, *postd, *gyd, *tgt, *dpre, *gxd, *dwd, *wout;
-  double* lossd;
+  float *xd = nullptr, *pred = nullptr, *postd = nullptr, *gyd = nullptr, *tgt = nullptr, *dpre = nullptr,
+        *gxd = nullptr, *dwd = nullptr, *wout = nullptr;
+  double* lossd = nullptr;
   WB_TRY(s.get(&xd, nx));
   WB_TRY(s.get(&pred, ny));
   WB_TRY(s.get(&postd, ny));
@@ -96,7 +97,7 @@ Status dense_normalbp(int batch, int in, int out, int act, int32_t dtype, const 
   // reference's decode (weight_at).
   const bool f32 = dt == DType::Float32;
   const size_t pb = f32 ? nw * 4 : store.native.size();
-  uint8_t* payload;
+  uint8_t* payload = nullptr;
   WB_TRY(s.get(&payload, pb));
   WB_CUDA(cudaMemcpyAsync(payload, f32 ? static_cast<const void*>(store.f32.data()) : store.native.data(), pb,
                           cudaMemcpyHostToDevice, st));
