@@ -99,8 +99,8 @@ int xsplit_policy() {
 bool use_tensor_path(const DeviceDense& d, int batch) {
   const char* env = std::getenv("WELVET_B200_BATCHED");
   if (env && std::strcmp(env, "gemv") == 0) return false;
-  if (env && std::strcmp(env, "tc") == 0) return !d.exact && gemm_supported(d.dtype);
-  return batch > 8 && !use_gemv_tc(d, batch) && !d.exact && gemm_supported(d.dtype);
+  if (env && std::strcmp(env, "tc") == 0) return !d.exact && gemm_supported(d.dtype) && d.Wg != nullptr;
+  return batch > 8 && !use_gemv_tc(d, batch) && !d.exact && gemm_supported(d.dtype) && d.Wg != nullptr;
 }
 
 bool exact_policy(int rows, int cols) {
@@ -127,7 +127,7 @@ static Status check_dims(int rows, int cols, int32_t dtype) {
 
 static Status finish_mirror(int device, int rows, int cols, DType dt, int act, const uint8_t* native_dev,
                             float scale, const double* bias, size_t bias_len, WeightStore* store,
-                            DeviceDense* dev, cudaStream_t st) {
+                            DeviceDense* dev, cudaStream_t st, int batch_hint) {
   DeviceDense d;
   d.device = device;
   d.dtype = dt;
@@ -140,11 +140,11 @@ static Status finish_mirror(int device, int rows, int cols, DType dt, int act, c
   d.exact = exact_policy(rows, cols);
   WB_CUDA(cudaMalloc(&d.W, static_cast<size_t>(d.row_stride) * rows));
   WB_TRY(build_mirror(dt, native_dev, rows, cols, d.row_stride, d.W, st));
-  if (gemv_tc_supported(dt) && !d.exact) {
+  if (gemv_tc_supported(dt) && !d.exact && (batch_hint <= 0 || batch_hint <= kGemvMaxBatch)) {
     WB_CUDA(cudaMalloc(&d.Wt, static_cast<size_t>(tiled_geom(dt, rows, cols).bytes())));
     WB_TRY(build_tiled_mirror(dt, native_dev, rows, cols, d.Wt, st));
   }
-  if (gemm_supported(dt) && !d.exact) {
+  if (gemm_supported(dt) && !d.exact && (batch_hint <= 0 || batch_hint > 4)) {
     WB_CUDA(cudaMalloc(&d.Wg, gemm_mirror_bytes(dt, rows, cols)));
     WB_TRY(build_gemm_mirror(dt, d.W, rows, d.row_stride, cols, d.Wg, st));
   }
@@ -162,7 +162,7 @@ static Status finish_mirror(int device, int rows, int cols, DType dt, int act, c
 
 Status mount_dense(int device, int rows, int cols, DType dt, int act, const float* W, bool w_is_device,
                    const double* bias, size_t bias_len, WeightStore* store, DeviceDense* dev,
-                   cudaStream_t st) {
+                   cudaStream_t st, int batch_hint) {
   WB_TRY(check_dims(rows, cols, static_cast<int32_t>(dt)));
   if (!W) return Status::Invalid("null mount args");
   WB_CUDA(cudaSetDevice(device));
@@ -199,12 +199,12 @@ Status mount_dense(int device, int rows, int cols, DType dt, int act, const floa
   }
   WB_CUDA(cudaStreamSynchronize(st));
   store->scale = scale;
-  return finish_mirror(device, rows, cols, dt, act, native_dev, scale, bias, bias_len, store, dev, st);
+  return finish_mirror(device, rows, cols, dt, act, native_dev, scale, bias, bias_len, store, dev, st, batch_hint);
 }
 
 Status mount_dense_native(int device, int rows, int cols, DType dt, int act, const uint8_t* native,
                           size_t native_len, float scale, const double* bias, size_t bias_len,
-                          WeightStore* store, DeviceDense* dev, cudaStream_t st) {
+                          WeightStore* store, DeviceDense* dev, cudaStream_t st, int batch_hint) {
   WB_TRY(check_dims(rows, cols, static_cast<int32_t>(dt)));
   if (!native) return Status::Invalid("null native bytes");
   const int64_t n = static_cast<int64_t>(rows) * cols;
@@ -229,7 +229,7 @@ Status mount_dense_native(int device, int rows, int cols, DType dt, int act, con
   // weight_at treats a zero scale as 1 (src/weights/native_codec.cpp:514-515).
   const float eff = (store->scale == 0.0f) ? 1.0f : store->scale;
   return finish_mirror(device, rows, cols, dt, act, static_cast<const uint8_t*>(ntmp.p), eff, bias,
-                       bias_len, store, dev, st);
+                       bias_len, store, dev, st, batch_hint);
 }
 
 Status alloc_io(const DeviceDense& d, int batch, DenseIO* io, cudaStream_t st) {
@@ -429,7 +429,7 @@ Status session_mount(int32_t batch, int32_t in, int32_t out, int32_t act, int32_
   DenseSession* s = nullptr;
   WB_TRY(new_session(batch, &s));
   Status st = mount_dense(s->device, out, in, static_cast<DType>(dtype), act, W, w_is_device, bias, bias_len,
-                          &s->store, &s->dev, s->stream);
+                          &s->store, &s->dev, s->stream, batch);
   if (st.ok()) st = alloc_io(s->dev, batch, &s->io, s->stream);
   if (st.ok()) st = cuda_status(cudaStreamSynchronize(s->stream), "mount sync");
   if (!st.ok()) {
@@ -448,7 +448,7 @@ Status session_mount_native(int32_t batch, int32_t in, int32_t out, int32_t act,
   DenseSession* s = nullptr;
   WB_TRY(new_session(batch, &s));
   Status st = mount_dense_native(s->device, out, in, static_cast<DType>(dtype), act, native, native_len, scale,
-                                 bias, bias_len, &s->store, &s->dev, s->stream);
+                                 bias, bias_len, &s->store, &s->dev, s->stream, batch);
   if (st.ok()) st = alloc_io(s->dev, batch, &s->io, s->stream);
   if (st.ok()) st = cuda_status(cudaStreamSynchronize(s->stream), "mount sync");
   if (!st.ok()) {

@@ -66,15 +66,18 @@ int64_t activation_stride(DType dt, int cols);
 // Quantize host float32 weights W[rows*cols] on the GPU into `store` (reference bytes and
 // scale, copied back to the host) and build the device mirror. `w_is_device` selects whether
 // W is a device pointer (no H2D copy of the float32 matrix).
+// `batch_hint` > 0: the only batch size the mirror will serve (a session's), so that only the
+// mirrors that batch reads are built (the fragment-tiled one up to kGemvMaxBatch tokens, the
+// GEMM one above 4); 0 builds every mirror.
 Status mount_dense(int device, int rows, int cols, DType dt, int act, const float* W, bool w_is_device,
                    const double* bias, size_t bias_len, WeightStore* store, DeviceDense* dev,
-                   cudaStream_t st);
+                   cudaStream_t st, int batch_hint = 0);
 
 // Mirror from reference-layout native bytes (+ scale), as a stored model is re-mounted
 // (src/interop/model_session.cpp:135-153 reads native bytes and scale back into a store).
 Status mount_dense_native(int device, int rows, int cols, DType dt, int act, const uint8_t* native,
                           size_t native_len, float scale, const double* bias, size_t bias_len,
-                          WeightStore* store, DeviceDense* dev, cudaStream_t st);
+                          WeightStore* store, DeviceDense* dev, cudaStream_t st, int batch_hint = 0);
 
 // Device buffers for one batch size: padded x, pre, post, and the tensor-core path's scratch.
 struct DenseIO {

@@ -1015,7 +1015,9 @@ __global__ void __launch_bounds__(kTmThreads, 1)
             const float4* sc4 = reinterpret_cast<const float4*>(p.scale_inv + t_pass + tc);
 #pragma unroll
             for (int e4 = 0; e4 < 4; ++e4) {
-              const float4 sc = __ldg(sc4 + e4);
+              // ordered, coherent loads: k_split_x (this grid's programmatic predecessor)
+              // wrote the scales
+              const float4 sc = ld_dep4(reinterpret_cast<const float*>(sc4 + e4));
               scv[4 * e4] = sc.x;
               scv[4 * e4 + 1] = sc.y;
               scv[4 * e4 + 2] = sc.z;
@@ -1286,8 +1288,27 @@ __global__ void k_tail_reduce(const TailParams p) {
 
 // x [M][x_ld] f32 -> planes [xsplit][Mp][Kp] f16 (x * 2^e = p0 + p1 + p2) and 2^-e per token;
 // pcnt[t] (when given) = planes that hold a non-zero value for token t, at most xsplit.
-// One 256-thread block per token row (grid = Mp); rows >= M and columns >= K are zero.
-constexpr int kSplitThreads = 256;
+// One 512-thread block per token row (grid = Mp); rows >= M and columns >= K are zero. A row
+// whose start is 16-byte aligned is read in 16-byte vectors, every load of a thread in flight
+// at once (Kp is a multiple of 64).
+constexpr int kSplitThreads = 512;
+
+// One element's planes: x * s = h0 + h1 + h2 (h0 alone for a non-finite x).
+__device__ __forceinline__ void split3(float v, float s, __half& h0, __half& h1, __half& h2) {
+  h1 = __float2half_rn(0.0f);
+  h2 = __float2half_rn(0.0f);
+  if (isfinite(v)) {
+    const float vs = v * s;
+    h0 = __float2half_rn(vs);
+    const float r1 = vs - __half2float(h0);
+    h1 = __float2half_rn(r1);
+    const float r2 = r1 - __half2float(h1);
+    h2 = __float2half_rn(r2);
+  } else {
+    h0 = __float2half_rn(v);
+  }
+}
+
 __global__ void __launch_bounds__(kSplitThreads)
     k_split_x(const float* x, int64_t x_ld, int M, int K, int Mp, int Kp, int xsplit,
               __half* __restrict__ planes, float* __restrict__ scale_inv, int* __restrict__ pcnt) {
@@ -1302,12 +1323,30 @@ __global__ void __launch_bounds__(kSplitThreads)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* xr = x + static_cast<int64_t>(t) * x_ld;
   const bool live = t < M;
+  const bool vec = (reinterpret_cast<uintptr_t>(xr) & 15) == 0;
   float amax = 0.0f;
   if (live) {
+    if (vec) {
 #pragma unroll 4
-    for (int k = tid; k < K; k += kSplitThreads) {
-      const float a = fabsf(ld_dep(xr + k));
-      if (a > amax && a <= 3.402823466e+38f) amax = a;
+      for (int k = 4 * tid; k < K; k += 4 * kSplitThreads) {
+        float4 v;
+        if (k + 3 < K) {
+          v = ld_dep4(xr + k);
+        } else {  // the row's ragged end
+          v.x = ld_dep(xr + k);
+          v.y = k + 1 < K ? ld_dep(xr + k + 1) : 0.0f;
+          v.z = k + 2 < K ? ld_dep(xr + k + 2) : 0.0f;
+          v.w = 0.0f;
+        }
+        for (float a : {fabsf(v.x), fabsf(v.y), fabsf(v.z), fabsf(v.w)})
+          if (a > amax && a <= 3.402823466e+38f) amax = a;
+      }
+    } else {
+#pragma unroll 4
+      for (int k = tid; k < K; k += kSplitThreads) {
+        const float a = fabsf(ld_dep(xr + k));
+        if (a > amax && a <= 3.402823466e+38f) amax = a;
+      }
     }
   }
 #pragma unroll
@@ -1329,25 +1368,41 @@ __global__ void __launch_bounds__(kSplitThreads)
   const int64_t plane = static_cast<int64_t>(Mp) * Kp;
   __half* p0 = planes + static_cast<int64_t>(t) * Kp;
   bool nz1 = false, nz2 = false;
-#pragma unroll 4
-  for (int k = tid; k < Kp; k += kSplitThreads) {
-    const float v = (live && k < K) ? ld_dep(xr + k) : 0.0f;
-    __half h0, h1 = __float2half_rn(0.0f), h2 = __float2half_rn(0.0f);
-    if (isfinite(v)) {
-      const float vs = v * s;
-      h0 = __float2half_rn(vs);
-      const float r1 = vs - __half2float(h0);
-      h1 = __float2half_rn(r1);
-      const float r2 = r1 - __half2float(h1);
-      h2 = __float2half_rn(r2);
-    } else {
-      h0 = __float2half_rn(v);
+  if (vec) {
+    // four elements per thread and step; Kp is a multiple of 4, so a step is all inside
+#pragma unroll 2
+    for (int k = 4 * tid; k < Kp; k += 4 * kSplitThreads) {
+      float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      if (live && k + 3 < K) {
+        const float4 q = ld_dep4(xr + k);
+        v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+      } else if (live) {
+        for (int j = 0; j < 4; ++j) v[j] = k + j < K ? ld_dep(xr + k + j) : 0.0f;
+      }
+      __half h0[4], h1[4], h2[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        split3(v[j], s, h0[j], h1[j], h2[j]);
+        nz1 |= (__half_as_ushort(h1[j]) & 0x7fff) != 0;
+        nz2 |= (__half_as_ushort(h2[j]) & 0x7fff) != 0;
+      }
+      // 8-byte stores: the plane rows start 8-byte aligned (Kp is a multiple of 64)
+      *reinterpret_cast<uint2*>(p0 + k) = *reinterpret_cast<const uint2*>(h0);
+      if (xsplit > 1) *reinterpret_cast<uint2*>(p0 + plane + k) = *reinterpret_cast<const uint2*>(h1);
+      if (xsplit > 2) *reinterpret_cast<uint2*>(p0 + 2 * plane + k) = *reinterpret_cast<const uint2*>(h2);
     }
-    p0[k] = h0;
-    if (xsplit > 1) p0[plane + k] = h1;
-    if (xsplit > 2) p0[2 * plane + k] = h2;
-    nz1 |= (__half_as_ushort(h1) & 0x7fff) != 0;
-    nz2 |= (__half_as_ushort(h2) & 0x7fff) != 0;
+  } else {
+#pragma unroll 4
+    for (int k = tid; k < Kp; k += kSplitThreads) {
+      const float v = (live && k < K) ? ld_dep(xr + k) : 0.0f;
+      __half h0, h1, h2;
+      split3(v, s, h0, h1, h2);
+      p0[k] = h0;
+      if (xsplit > 1) p0[plane + k] = h1;
+      if (xsplit > 2) p0[2 * plane + k] = h2;
+      nz1 |= (__half_as_ushort(h1) & 0x7fff) != 0;
+      nz2 |= (__half_as_ushort(h2) & 0x7fff) != 0;
+    }
   }
   if (pcnt) {
     const int f = (nz1 ? 1 : 0) | (nz2 ? 2 : 0);

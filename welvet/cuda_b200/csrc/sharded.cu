@@ -188,7 +188,7 @@ Status sharded_mount(Comm* comm, int batch, int in, int out, int act, DType dt, 
       lbl = bias_len - static_cast<size_t>(s->row_begin);
       if (lbl > static_cast<size_t>(rows)) lbl = static_cast<size_t>(rows);
     }
-    st = mount_dense(s->device, rows, in, dt, act, W_rows, w_dev, lb, lbl, &s->store, &s->dev, s->stream);
+    st = mount_dense(s->device, rows, in, dt, act, W_rows, w_dev, lb, lbl, &s->store, &s->dev, s->stream, batch);
     if (st.ok()) st = alloc_io(s->dev, batch, &s->io, s->stream);
     if (!st.ok()) return fail(st);
   }

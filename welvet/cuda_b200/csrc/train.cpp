@@ -58,7 +58,7 @@ Status dense_normalbp(int batch, int in, int out, int act, int32_t dtype, const 
   const DType dt = static_cast<DType>(dtype);
   WeightStore store;
   DeviceDense dev;
-  WB_TRY(mount_dense(device, out, in, dt, act, W_init, false, bias, bias_len, &store, &dev, st));
+  WB_TRY(mount_dense(device, out, in, dt, act, W_init, false, bias, bias_len, &store, &dev, st, batch));
   DenseIO io;
   struct IoGuard {
     DenseIO& io;
