@@ -591,19 +591,20 @@ def test_simt_gemv_still_correct(wb, oracle, dt, monkeypatch):
 @pytest.mark.parametrize("rows,d,inter", [(1, 256, 640), (3, 256, 640), (24, 256, 640), (300, 256, 640),
                                           (24, 2048, 96), (16, 256, 9600), (300, 256, 4864)])
 @pytest.mark.parametrize("dt", [16, 4, 9])
-@pytest.mark.parametrize("mode", ["single", "pair", "dbuf", "silu64", "group"])
+@pytest.mark.parametrize("mode", ["single", "pair", "dbuf", "silu64", "dual"])
 def test_swiglu_tensor_paths(wb, oracle, dt, rows, d, inter, mode, monkeypatch):
-    """1..4 rows: Gate and Up fused in the tensor GEMV; more: one tcgen05 GEMM over the
+    """1..4 rows: Gate and Up on the tensor GEMV; more: one tcgen05 GEMM over the
     interleaved Gate/Up pair mirror writing h in its epilogue (300 rows: several token
     blocks; d = 2048 with a narrow intermediate: split-K with the paired reduce; 9600: 150
     pair tiles, the last two cut along K and reduced by the tail launch; 300 x 4864: 76
     pair tiles per token block, with a tail). "pair": the GEMMs on CTA pairs where they qualify
     (300 rows); "dbuf": two accumulator buffers of 128 columns; "silu64": the GEMM epilogue's
-    SiLU in fp64 as the reference (default fp32); "group": 1..4 rows with Gate and Up as one
-    grouped GEMV launch of two layers and the product kernel."""
-    if mode == "group" and rows > 4:
-        pytest.skip("the grouped Gate/Up form serves 1..4 rows")
-    monkeypatch.setenv("WELVET_B200_SWIGLU_GEMV", "group" if mode == "group" else "dual")
+    SiLU in fp64 as the reference (default fp32); "dual": 1..4 rows on the fused Gate/Up GEMV
+    whose epilogue writes h (the default runs Gate and Up as one grouped launch of two layers
+    and the product kernel)."""
+    if mode == "dual" and rows > 4:
+        pytest.skip("the fused Gate/Up form serves 1..4 rows")
+    monkeypatch.setenv("WELVET_B200_SWIGLU_GEMV", "dual" if mode == "dual" else "group")
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
     monkeypatch.setenv("WELVET_B200_GEMM_PAIR", "1" if mode == "pair" else "0")
     monkeypatch.setenv("WELVET_B200_GEMM_DBUF", "128" if mode == "dbuf" else "0")

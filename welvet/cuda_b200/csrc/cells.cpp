@@ -97,12 +97,14 @@ Status swiglu_mount_src(int device, int in, int inter, DType dt, const WeightSrc
 // (tcgen05) every larger batch of quantized, non-exact layers. WELVET_B200_GEMV16=1 runs 5..16
 // rows as two tensor GEMVs (Gate, Up) and the reference's product instead (measured slower on
 // B200: 16 rows of the 4096 / 14336 E4M3 cell take 370 us against 130 us on the pair GEMM).
-// 1..4 rows on the tensor GEMV: either the fused Gate/Up form (one kernel streams both weight
-// sets, the epilogue writes h) or, with WELVET_B200_SWIGLU_GEMV=group, Gate and Up as one
-// grouped launch of two layers (x prepared once per layer) followed by the product kernel.
+// 1..4 rows on the tensor GEMV: Gate and Up as one grouped launch of two layers (x prepared
+// once per layer, 4 CTAs per SM) followed by the product kernel, or, with
+// WELVET_B200_SWIGLU_GEMV=dual, the fused Gate/Up form (one kernel streams both weight sets at
+// 2 CTAs per SM and its epilogue writes h). Measured on the 4096 / 14336 E4M3 cell at 1 row:
+// grouped 52.2 us, fused 60.3 us.
 static bool swiglu_group_mode() {
   const char* e = std::getenv("WELVET_B200_SWIGLU_GEMV");
-  return e && std::strcmp(e, "group") == 0;
+  return !(e && std::strcmp(e, "dual") == 0);
 }
 static bool swiglu_small_gemv(const SwigluCell* c, int bs) {
   return bs <= 4 && use_gemv_tc(c->gate, bs) && c->up.Wt;
