@@ -511,13 +511,15 @@ def test_tensor_core_path_parity(wb, oracle, dt, shape, xsplit, kernel, monkeypa
 
 @pytest.mark.parametrize("dt", [16, 9])
 @pytest.mark.parametrize("shape,xsplit", [((512, 1024, 256), "1"), ((768, 512, 200), "2"), ((256, 640, 160), "3"),
-                                          ((9728, 256, 300), "1"), ((256, 8192, 128), "3")])
+                                          ((9728, 256, 300), "1"), ((256, 8192, 128), "3"), ((1024, 1024, 64), "2"),
+                                          ((512, 2048, 32), "2"), ((768, 512, 48), "3"), ((4096, 4096, 16), "2"),
+                                          ((1280, 4096, 12), "1")])
 def test_gemm_cta_pairs_match_single_ctas(wb, oracle, dt, shape, xsplit, monkeypatch):
-    """The same GEMM on CTA pairs (WELVET_B200_GEMM_PAIR=1: M = 256 MMAs, each CTA loading
-    half of every x stage) and on single CTAs: both within the GEMM bound of the oracle, for
-    one to three x planes (pair passes of 256, 128 and 128 tokens; with three planes plane 2
-    rides in a second ring slot and accumulates onto plane 1), whole tiles, a tail and
-    split-K."""
+    """The same GEMM on CTA pairs (WELVET_B200_GEMM_PAIR=all: M = 256 MMAs, each CTA loading
+    half of every x stage; blocks of fewer than 32 tokens padded to 32) and on single CTAs:
+    both within the GEMM bound of the oracle, for one to three x planes (pair passes of 256,
+    128 and 128 tokens; with three planes plane 2 rides in a second ring slot and accumulates
+    onto plane 1), whole tiles, a tail, split-K and small token blocks."""
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
     monkeypatch.setenv("WELVET_B200_XSPLIT", xsplit)
     monkeypatch.setenv("WELVET_B200_BATCHED", "tc")
@@ -525,7 +527,7 @@ def test_gemm_cta_pairs_match_single_ctas(wb, oracle, dt, shape, xsplit, monkeyp
     w, x, bias, ref = _case(oracle, dt, out, in_, batch, 2.0, out + 3 * in_ + batch, 0)
     pre_o, post_o, y64, sabs = ref
     res = {}
-    for pair in ("1", "0"):
+    for pair in ("all", "0"):
         monkeypatch.setenv("WELVET_B200_GEMM_PAIR", pair)
         pre, post = wb.dense_forward_f32(w, x, dt, 0, bias)
         err = np.abs(pre.astype(np.float64) - pre_o.astype(np.float64)) - 2 * ulp(pre_o)
@@ -533,7 +535,7 @@ def test_gemm_cta_pairs_match_single_ctas(wb, oracle, dt, shape, xsplit, monkeyp
         assert norm <= GEMM_TOL[xsplit], (pair, norm)
         assert np.allclose(post, np.maximum(pre.astype(np.float64), 0).astype(np.float32))
         res[pair] = pre
-    print(f"pairs vs single CTAs dt={dt} shape={shape}: identical={np.array_equal(res['1'], res['0'])}")
+    print(f"pairs vs single CTAs dt={dt} shape={shape}: identical={np.array_equal(res['all'], res['0'])}")
 
 
 @pytest.mark.parametrize("batch", [5, 6, 7, 8])

@@ -81,7 +81,7 @@ def check(p, M, cols, rows, xsplit, dt):
     assert p["tiles_t"] == -(-M // TB)
     assert p["tiles"] == (-(-rows // 128) // sub) * p["tiles_t"]
     if pair:
-        assert (-(-rows // 128)) % 2 == 0 and M >= 128
+        assert (-(-rows // 128)) % 2 == 0
     assert 1 <= p["splits"] <= 8 and p["splits"] * p["kb_per_split"] >= nkb
     assert (p["splits"] - 1) * p["kb_per_split"] < nkb
     if p["tail_first"] >= 0:
@@ -97,17 +97,19 @@ def check(p, M, cols, rows, xsplit, dt):
 
 
 SHAPES = [(M, cols, rows) for M, cols, rows in itertools.product(
-    (9, 16, 100, 128, 160, 200, 256, 300, 512, 1024, 4096),
+    (9, 16, 32, 48, 64, 100, 128, 160, 200, 256, 300, 512, 1024, 4096),
     (64, 1000, 4096, 14336),
     (128, 256, 640, 4096, 9600, 9728, 28672))]
 
 
-@pytest.mark.parametrize("mode", ["default", "pair", "dbuf192", "dbuf128", "tb128", "xslots3"])
+@pytest.mark.parametrize("mode", ["default", "pair", "pairall", "dbuf192", "dbuf128", "tb128", "xslots3"])
 def test_plan_invariants(lib, mode, monkeypatch):
     for k in ("WELVET_B200_GEMM_PAIR", "WELVET_B200_GEMM_DBUF", "WELVET_B200_GEMM_TB", "WELVET_B200_GEMM_XSLOTS"):
         monkeypatch.delenv(k, raising=False)
     if mode == "pair":
         monkeypatch.setenv("WELVET_B200_GEMM_PAIR", "1")
+    elif mode == "pairall":
+        monkeypatch.setenv("WELVET_B200_GEMM_PAIR", "all")
     elif mode.startswith("dbuf"):
         monkeypatch.setenv("WELVET_B200_GEMM_DBUF", mode[4:])
     elif mode == "tb128":
@@ -123,7 +125,7 @@ def test_plan_invariants(lib, mode, monkeypatch):
             assert p["TB"] <= 128
         if mode == "xslots3":
             assert p["sx"] <= 3
-    if mode == "pair":
+    if mode in ("pair", "pairall"):
         assert seen_pair > 0
     if mode.startswith("dbuf"):
         assert seen_dbuf > 0

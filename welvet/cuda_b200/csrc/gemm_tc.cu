@@ -1539,8 +1539,11 @@ int tm_splits(int tiles, int nkb, int M, int rows, int units) {
 // tiles (an even number of 128-row mirror tiles) and a token block fills half an MMA.
 bool tm_pair_wanted(int M, int rows) {
   const char* e = std::getenv("WELVET_B200_GEMM_PAIR");
-  if (!e || std::strcmp(e, "1") != 0) return false;
-  return M >= 128 && ((rows + kBM - 1) / kBM) % 2 == 0;
+  if (!e) return false;
+  // "1": blocks of 128 tokens and more; "all": every batch the GEMM takes (tuning; a block
+  // of fewer than 32 tokens is padded to 32)
+  const int min_m = std::strcmp(e, "1") == 0 ? 128 : (std::strcmp(e, "all") == 0 ? 1 : 1 << 30);
+  return M >= min_m && ((rows + kBM - 1) / kBM) % 2 == 0;
 }
 
 TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_tail = true, bool allow_pair = true,
@@ -1626,9 +1629,9 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_
   const int tiles =
       static_cast<int>(((rows + kBM - 1) / kBM / sub) * static_cast<int64_t>((M + pl.TB - 1) / pl.TB));
   int splits = tm_splits(tiles, pl.nkb, M, rows, units);
-  if (const char* e = std::getenv("WELVET_B200_GEMM_SPLITS")) {  // tuning override (1..16)
+  if (const char* e = std::getenv("WELVET_B200_GEMM_SPLITS")) {  // tuning override (1..8)
     const int n = std::atoi(e);
-    if (n >= 1 && n <= 16 && n <= pl.nkb) splits = n;
+    if (n >= 1 && n <= 8 && n <= pl.nkb) splits = n;
   }
   pl.kb_per_split = (pl.nkb + splits - 1) / splits;
   pl.splits = (pl.nkb + pl.kb_per_split - 1) / pl.kb_per_split;
