@@ -13,7 +13,7 @@ from conftest import ROOT
 
 LIB = os.path.join(ROOT, "welvet", "cuda_b200", "libwelvet_b200.so")
 FIELDS = ("pair TB tp1 tp2 tp3 nacc1 nacc2 nacc3 acc_cols acc_buf a_col sx sw x_bytes w_bytes smem nkb splits "
-          "kb_per_split tiles_t tiles tail_first tail_s tail_kbps n_items").split()
+          "kb_per_split tiles_t tiles tail_first tail_s tail_kbps n_items wg").split()
 FP4, E4M3, E5M2, INT8 = 16, 4, 5, 9
 
 
@@ -72,7 +72,8 @@ def check(p, M, cols, rows, xsplit, dt):
     assert p["a_col"] % 32 == 0 and p["a_col"] + 32 * p["sx"] <= 512  # TMEM: accumulators + A stages
     assert 2 <= p["sx"] <= 8 and 2 <= p["sw"] <= 32
     assert p["x_bytes"] % 1024 == 0 and p["x_bytes"] >= xrows * (64 if pair else 128)
-    assert p["w_bytes"] == 128 * (32 if dt == FP4 else 64)
+    assert p["wg"] in (1, 2, 4, 8)  # W stages per bulk copy
+    assert p["w_bytes"] == 128 * (32 if dt == FP4 else 64) * p["wg"]
     assert p["sx"] * p["x_bytes"] + p["sw"] * p["w_bytes"] + 2048 + 32 * 1024 <= p["smem"] <= 227 * 1024
     assert p["smem"] >= 116 * 1024  # one CTA per SM
     nkb = -(-cols // 64)
@@ -102,9 +103,10 @@ SHAPES = [(M, cols, rows) for M, cols, rows in itertools.product(
     (128, 256, 640, 4096, 9600, 9728, 28672))]
 
 
-@pytest.mark.parametrize("mode", ["default", "pair", "pairall", "dbuf192", "dbuf128", "tb128", "xslots3"])
+@pytest.mark.parametrize("mode", ["default", "pair", "pairall", "dbuf192", "dbuf128", "tb128", "xslots3", "wg4"])
 def test_plan_invariants(lib, mode, monkeypatch):
-    for k in ("WELVET_B200_GEMM_PAIR", "WELVET_B200_GEMM_DBUF", "WELVET_B200_GEMM_TB", "WELVET_B200_GEMM_XSLOTS"):
+    for k in ("WELVET_B200_GEMM_PAIR", "WELVET_B200_GEMM_DBUF", "WELVET_B200_GEMM_TB", "WELVET_B200_GEMM_XSLOTS",
+              "WELVET_B200_GEMM_WG"):
         monkeypatch.delenv(k, raising=False)
     if mode == "pair":
         monkeypatch.setenv("WELVET_B200_GEMM_PAIR", "1")
@@ -116,6 +118,8 @@ def test_plan_invariants(lib, mode, monkeypatch):
         monkeypatch.setenv("WELVET_B200_GEMM_TB", "128")
     elif mode == "xslots3":
         monkeypatch.setenv("WELVET_B200_GEMM_XSLOTS", "3")
+    elif mode == "wg4":
+        monkeypatch.setenv("WELVET_B200_GEMM_WG", "4")
     seen_pair = seen_dbuf = 0
     for (M, cols, rows), xsplit, dt in itertools.product(SHAPES, (1, 2, 3), (FP4, E4M3, INT8)):
         p = plan(lib, M, cols, rows, xsplit, dt)
@@ -125,6 +129,7 @@ def test_plan_invariants(lib, mode, monkeypatch):
             assert p["TB"] <= 128
         if mode == "xslots3":
             assert p["sx"] <= 3
+        assert p["wg"] == (4 if mode == "wg4" else 1)
     if mode in ("pair", "pairall"):
         assert seen_pair > 0
     if mode.startswith("dbuf"):

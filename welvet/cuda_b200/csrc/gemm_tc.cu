@@ -404,10 +404,11 @@ struct TmParams {
   int tpass[3];                // tokens per pass for 1, 2, 3 planes
   int nkb_total, kb_per_split, splits;
   int kbb;                     // packed bytes per row per stage (FP4 32, 8-bit 64)
-  uint32_t x_bytes, w_bytes;    // one x-ring slot (P x T x 128 B at most), one W-ring slot (128 x kbb)
+  uint32_t x_bytes, w_bytes;    // one x-ring slot (P x T x 128 B at most), one W-ring slot (wg x 128 x kbb)
   uint32_t a_col;              // first A stage column (after the accumulators)
   int nacc[3];                 // independent accumulators for 1, 2, 3 planes
   int sx, sw;                  // stages (x slot + TMEM A slot each) and W-ring slots
+  int wg;                      // pipeline stages per W-ring slot (one bulk copy each; w_bytes = wg stages)
   int w_evict_first;           // 1 when no other CTA reads this CTA's weight rows
   const float* scale_inv;      // [Mp]
   const int* pcnt;             // [Mp] planes needed per token
@@ -683,7 +684,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < Sw; ++s) {
       mbar_init(&w_full[s], 1);
-      mbar_init(&w_empty[s], 4);
+      mbar_init(&w_empty[s], 4 * p.wg);  // 4 converter warps per stage of the slot
     }
     // pair: s_full and acc_empty of the even CTA count both CTAs' warps
     for (int s = 0; s < S; ++s) {
@@ -752,19 +753,21 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
       else
         asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
-      const uint32_t wb = p.w_bytes;
+      const uint32_t wb = p.w_bytes;                                // one slot: wg stages
+      const uint32_t sb = wb / static_cast<uint32_t>(p.wg);         // one stage
       Ring w;
       int issued = 0;
       bool ok = true;
       for (int qi = first_item; qi < p.n_items && ok; qi += item_step) {
         const TmItem it = item(qi);
         const int mt = kPair ? 2 * it.tile_m + static_cast<int>(v) : it.tile_m;  // 128-row mirror tile
-        const uint8_t* wfirst = p.Wg + (static_cast<int64_t>(mt) * p.nkb_total + it.kb0) * wb;
+        const uint8_t* wfirst = p.Wg + (static_cast<int64_t>(mt) * p.nkb_total + it.kb0) * sb;
         for (int pass = 0; pass < it.npass && ok; ++pass)
-          for (int i = 0; i < it.nkb; ++i) {
+          for (int i = 0; i < it.nkb; i += p.wg) {  // the stages of a tile are contiguous: one copy per slot
+            const uint32_t n = static_cast<uint32_t>(it.nkb - i < p.wg ? it.nkb - i : p.wg);
             if (!mbar_wait(&w_empty[w.slot], w.phase ^ 1u, p.err, 11)) { ok = false; break; }
-            mbar_expect_tx(&w_full[w.slot], wb);
-            bulk_load_hint(wring + w.slot * wb, wfirst + static_cast<int64_t>(i) * wb, wb, &w_full[w.slot], pol);
+            mbar_expect_tx(&w_full[w.slot], n * sb);
+            bulk_load_hint(wring + w.slot * wb, wfirst + static_cast<int64_t>(i) * sb, n * sb, &w_full[w.slot], pol);
             ++issued;
             w.step(Sw);
           }
@@ -817,8 +820,8 @@ __global__ void __launch_bounds__(kTmThreads, 1)
               if (!mbar_wait(&s_free[r.slot], r.phase ^ 1u, p.err, 18)) { ok = false; break; }
               uint8_t* dst = xring + r.slot * p.x_bytes;
               mbar_expect_tx(&s_full[r.slot], tx);
-              for (int pl = 0; pl < it.P; ++pl)
-                tma_load_3d_hint(dst + pl * it.T * 128, tmx, (it.kb0 + i) * kBK, t0, pl, &s_full[r.slot], pol);
+              // every plane of the stage in one box ([P][T][128 B], plane pl at pl * T * 128)
+              tma_load_3d_hint(dst, tmx, (it.kb0 + i) * kBK, t0, 0, &s_full[r.slot], pol);
               ++issued;
               r.step(S);
             }
@@ -952,8 +955,20 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         flags[tail_k] = raw32 ? 1 : 0;
       }
       const bool two = kPair && P == 3;  // pairs, 3 planes: a stage takes two ring slots
+      const uint32_t sb = p.w_bytes / static_cast<uint32_t>(p.wg);  // one stage of a W slot
       for (int pass = 0; pass < npass && ok; ++pass) {
-        for (int i = 0; i < it.nkb; ++i, ++stage_idx, w.step(Sw)) {
+        // The W slot of stage i holds stages [w_base, w_base + wn): the W producer's copies
+        // restart at the pass's first stage; every stage frees its slot once (4 warps), the
+        // last stage of a short slot for the stages it does not hold as well.
+        int w_base = 0;
+        auto w_count = [&]() { return it.nkb - w_base < p.wg ? it.nkb - w_base : p.wg; };
+        auto adv_w = [&](int i) {
+          if (i + 1 - w_base == w_count()) {
+            w_base = i + 1;
+            w.step(Sw);
+          }
+        };
+        for (int i = 0; i < it.nkb; adv_w(i), ++i, ++stage_idx) {
           const Ring s1 = st;  // the stage's slot (its TMEM A slot)
           Ring s2 = st;        // the slot of plane 2's x (3-plane pair stages)
           if (two) s2.step(S);
@@ -962,9 +977,14 @@ __global__ void __launch_bounds__(kTmThreads, 1)
           if ((stage_idx & 1) != grp) continue;
           if (!warp_wait(&w_full[w.slot], w.phase, p.err, 16)) { ok = false; break; }
           uint32_t v[32];
-          convert_row<kDt>(wring + w.slot * p.w_bytes, r, v);
+          const int sub = i - w_base;
+          convert_row<kDt>(wring + w.slot * p.w_bytes + static_cast<uint32_t>(sub) * sb, r, v);
           __syncwarp();
-          if (lane == 0) mbar_arrive(&w_empty[w.slot]);
+          if (lane == 0) {
+            const int wn = w_count();
+            const int arrivals = sub == wn - 1 ? 1 + p.wg - wn : 1;
+            for (int a = 0; a < arrivals; ++a) mbar_arrive(&w_empty[w.slot]);
+          }
           if (!warp_wait(&s_free[s1.slot], s1.phase ^ 1u, p.err, 21)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           tmem_st32(tmem + lane_base + p.a_col + 32u * static_cast<uint32_t>(s1.slot), v);
@@ -1039,13 +1059,25 @@ __global__ void __launch_bounds__(kTmThreads, 1)
             double y[16];
 #pragma unroll
             for (int e = 0; e < 16; ++e) y[e] = 0.0;
-            for (int pl = 0; pl < PA; ++pl) {
-              for (int jj = 0; jj < nacc; ++jj) {
-                uint32_t v[16];
-                tmem_ld16(acc_base + static_cast<uint32_t>(jj * acols + pl * T + tc), v);
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            // the PA x nacc accumulator reads (plane-major, as the sums are ordered), two in
+            // flight per wait: each wait costs a TMEM round trip, and small token blocks have up
+            // to 8 reads per chunk (four in flight spilled registers)
+            const int nld = PA * nacc;
 #pragma unroll
-                for (int e = 0; e < 16; ++e) y[e] += static_cast<double>(__uint_as_float(v[e]));
+            for (int g0 = 0; g0 < 12; g0 += 2) {
+              if (g0 >= nld) break;
+              uint32_t va[16], vb[16];
+              tmem_ld16(acc_base + static_cast<uint32_t>((g0 % nacc) * acols + (g0 / nacc) * T + tc), va);
+              const bool two_ld = g0 + 1 < nld;
+              if (two_ld)
+                tmem_ld16(acc_base + static_cast<uint32_t>(((g0 + 1) % nacc) * acols + ((g0 + 1) / nacc) * T + tc),
+                          vb);
+              asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+              for (int e = 0; e < 16; ++e) y[e] += static_cast<double>(__uint_as_float(va[e]));
+              if (two_ld) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) y[e] += static_cast<double>(__uint_as_float(vb[e]));
               }
             }
 #pragma unroll
@@ -1445,12 +1477,16 @@ Status make_map_2d(CUtensorMap* tm, CUtensorMapDataType dt, void* base, uint64_t
 
 // [planes][Mp][Kp] f16 planes of x: box {64 k, T tokens, 1 plane}, SWIZZLE_128B; tokens past
 // Mp read as zero.
-Status make_map_planes(CUtensorMap* tm, void* base, uint64_t Kp, uint64_t Mp, uint64_t planes, uint32_t T) {
+// x planes [planes][Mp][Kp] f16; a box is 64 k x T tokens x box_planes planes (one request
+// brings every plane of a stage: small token blocks are bound by the number of copies an SM
+// issues, not by their bytes).
+Status make_map_planes(CUtensorMap* tm, void* base, uint64_t Kp, uint64_t Mp, uint64_t planes, uint32_t T,
+                       uint32_t box_planes = 1) {
   auto enc = tensor_map_encoder();
   if (!enc) return Status::Internal("cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[3] = {Kp, Mp, planes};
   cuuint64_t strides[2] = {Kp * 2, Kp * Mp * 2};
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(kBK), T, 1};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(kBK), T, box_planes};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1503,7 +1539,7 @@ struct TmPlan {
   int TB, tpass[3], nacc[3], Mp, Kp, nkb, splits, kb_per_split, kbb, acc_cols;
   int tiles_t, tiles, tail_first, tail_s, tail_kbps;  // tail schedule (tail_first < 0: none)
   int pblk_bytes;                                      // per-token-block plane counts (shared memory)
-  int sx, sw;
+  int sx, sw, wg;
   uint32_t x_bytes, w_bytes, a_col;
   uint32_t acc_buf;  // columns of one accumulator buffer when there are two, else 0
   size_t smem;
@@ -1594,8 +1630,16 @@ TmPlan make_tm_plan(int M, int cols, int rows, int xsplit, DType dt, bool allow_
   pl.Kp = static_cast<int>(round_up(cols, kBK));
   pl.nkb = pl.Kp / kBK;
   pl.kbb = dt == DType::FP4 ? kBK / 2 : kBK;
+  // W stages per bulk copy: one by default; WELVET_B200_GEMM_WG = 2, 4 or 8 groups that many
+  // stages of a tile per copy (tuning: 4 per copy measured 1.5 % slower on the 32-layer
+  // 4096-wide volume at 64 tokens, 0.815 against 0.802 ms).
+  pl.wg = 1;
+  if (const char* e = std::getenv("WELVET_B200_GEMM_WG")) {
+    const int g = std::atoi(e);
+    if (g == 1 || g == 2 || g == 4 || g == 8) pl.wg = g;
+  }
   pl.x_bytes = static_cast<uint32_t>(round_up(static_cast<int64_t>(xrows) * (pl.pair ? 64 : 128), 1024));
-  pl.w_bytes = static_cast<uint32_t>(kBM * pl.kbb);
+  pl.w_bytes = static_cast<uint32_t>(kBM * pl.kbb * pl.wg);
   pl.acc_buf = bw ? static_cast<uint32_t>(round_up(pl.acc_cols, 32)) : 0u;
   pl.a_col = bw ? 2 * pl.acc_buf : static_cast<uint32_t>(round_up(pl.acc_cols, 32));
   // stages (an x slot + a TMEM A slot each): as many as TMEM allows (up to 8) while the raw W
@@ -1766,7 +1810,7 @@ int gemm_plan_values(int M, int cols, int rows, int xsplit, DType dt, int max_tb
   const int64_t v[] = {pl.pair ? 1 : 0, pl.TB, pl.tpass[0], pl.tpass[1], pl.tpass[2], pl.nacc[0], pl.nacc[1],
                        pl.nacc[2], pl.acc_cols, pl.acc_buf, pl.a_col, pl.sx, pl.sw, pl.x_bytes, pl.w_bytes,
                        static_cast<int64_t>(pl.smem), pl.nkb, pl.splits, pl.kb_per_split, pl.tiles_t, pl.tiles,
-                       pl.tail_first, pl.tail_s, pl.tail_kbps, n_items};
+                       pl.tail_first, pl.tail_s, pl.tail_kbps, n_items, pl.wg};
   const int cnt = static_cast<int>(sizeof(v) / sizeof(v[0]));
   for (int i = 0; i < cnt && i < n; ++i) out[i] = v[i];
   return cnt;
@@ -1911,10 +1955,12 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
   CUtensorMap tm_x[3];
   for (int P = 1; P <= 3; ++P) {
     const int q = P <= a.xsplit ? P : 1;  // maps for plane counts above xsplit are never used
-    // a CTA of a pair loads boxes of half a pass's tokens
+    // a CTA of a pair loads boxes of half a pass's tokens, one plane each; a single CTA one box
+    // of all q planes per stage
     const int box = pl.pair ? pl.tpass[q - 1] / 2 : pl.tpass[q - 1];
     WB_TRY(make_map_planes(&tm_x[P - 1], planes, static_cast<uint64_t>(pl.Kp), static_cast<uint64_t>(pl.Mp),
-                           static_cast<uint64_t>(a.xsplit), static_cast<uint32_t>(box)));
+                           static_cast<uint64_t>(a.xsplit), static_cast<uint32_t>(box),
+                           pl.pair ? 1u : static_cast<uint32_t>(q)));
   }
 
   TmParams p{};
@@ -1924,7 +1970,7 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
   for (int i = 0; i < 3; ++i) p.tpass[i] = pl.tpass[i];
   p.nkb_total = pl.nkb; p.kb_per_split = pl.kb_per_split; p.splits = pl.splits; p.kbb = pl.kbb;
   p.x_bytes = pl.x_bytes; p.w_bytes = pl.w_bytes; p.a_col = pl.a_col; p.acc_buf = pl.acc_buf;
-  p.sx = pl.sx; p.sw = pl.sw;
+  p.sx = pl.sx; p.sw = pl.sw; p.wg = pl.wg;
   for (int i = 0; i < 3; ++i) p.nacc[i] = pl.nacc[i];
   p.w_evict_first = (a.M + pl.TB - 1) / pl.TB == 1 ? 1 : 0;
   p.scale_inv = scale_inv; p.pcnt = pcnt; p.w_scale = a.scale;
