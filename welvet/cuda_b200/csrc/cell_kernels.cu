@@ -16,6 +16,7 @@
 
 #include <cstdlib>
 #include <cstring>
+#include <type_traits>
 
 namespace wb {
 namespace {
@@ -212,24 +213,32 @@ __global__ void k_attention(const double* __restrict__ Qr, const double* __restr
   }
 }
 
-// The same attention, tiled: one CTA per (32 consecutive queries of one batch, head). Each
-// tile of 64 key positions k_pos has its ring rows (the latest position written to slot
+// The same attention, tiled: one CTA per (8 x QW consecutive queries of one batch, head).
+// Each tile of 64 key positions k_pos has its ring rows (the latest position written to slot
 // k_pos % msl, as above) gathered once into shared memory -- K transposed, V row-major -- and
-// serves all 32 queries, instead of every (query, head) warp re-reading K and V from L2.
-// Scores, online softmax (running max from -1e9, as the reference) and the weighted V sum
-// stay in fp64. Warp w owns queries 4w .. 4w + 3; for the scores lane l takes key positions l
-// and l + 32 of the tile, for the output the head dimensions l, l + 32, l + 64, l + 96.
-constexpr int kAQ = 32, kAK = 64, kAHd = 128, kAThreads = 256;
+// serves all the CTA's queries, instead of every (query, head) warp re-reading K and V from
+// L2. Scores, online softmax (running max from -1e9, as the reference) and the weighted V sum
+// stay in fp64. Warp w owns queries QW w .. QW w + QW - 1; for the scores lane l takes key
+// positions l and l + 32 of the tile, for the output the head dimensions l, l + 32, l + 64,
+// l + 96. QW = 8 (64 queries per CTA) makes twice the FMAs per shared-memory load of QW = 4.
+constexpr int kAK = 64, kAHd = 128, kAThreads = 256;
 
+template <int QW>
+__host__ __device__ constexpr int attn_queries() { return 8 * QW; }
+
+template <int QW>
 size_t attention_tiled_smem() {
+  constexpr int kAQ = attn_queries<QW>();
   return sizeof(double) * (kAHd * kAQ + kAHd * kAK + kAK * kAHd + kAK * kAQ) + sizeof(int) * kAK;
 }
 
+template <int QW>
 __global__ void __launch_bounds__(kAThreads, 1)
     k_attention_tiled(const double* __restrict__ Qr, const double* __restrict__ Kr, const double* __restrict__ Vd,
                       float* __restrict__ out, int batch, int seq, int num_heads, int num_kv, int head_dim, int msl,
                       int mask, int use_alibi, int use_sigmoid, int window, int prefix_len, int window_causal,
                       double scale) {
+  constexpr int kAQ = attn_queries<QW>();
   extern __shared__ double sm[];
   double* Qs = sm;                  // [kAHd][kAQ]: queries' rotated Q, d-major
   double* Kt = Qs + kAHd * kAQ;     // [kAHd][kAK]: the tile's keys, d-major
@@ -249,11 +258,11 @@ __global__ void __launch_bounds__(kAThreads, 1)
     const int q = i / kAHd, d = i - q * kAHd;
     Qs[d * kAQ + q] = q < nq && d < head_dim ? Qr[static_cast<int64_t>(tok0 + q) * q_dim + h * head_dim + d] : 0.0;
   }
-  const int qb = 4 * w;
-  double m[4], l[4], acc[4][4];
-  int n[4];
+  const int qb = QW * w;
+  double m[QW], l[QW], acc[QW][4];
+  int n[QW];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < QW; ++i) {
     m[i] = -1e9;  // the reference's initial running max
     l[i] = 0.0;
     n[i] = 0;
@@ -279,21 +288,21 @@ __global__ void __launch_bounds__(kAThreads, 1)
       Vs[j * kAHd + d] = ok ? Vd[off] : 0.0;
     }
     __syncthreads();
-    // scores of queries qb..qb+3 against key positions k0 + lane, k0 + lane + 32
-    double sc[4][2];
+    // scores of queries qb..qb+QW-1 against key positions k0 + lane, k0 + lane + 32
+    double sc[QW][2];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) sc[i][0] = sc[i][1] = 0.0;
+    for (int i = 0; i < QW; ++i) sc[i][0] = sc[i][1] = 0.0;
     for (int d = 0; d < head_dim; ++d) {
-      const double2 qa = *reinterpret_cast<const double2*>(Qs + d * kAQ + qb);
-      const double2 qc = *reinterpret_cast<const double2*>(Qs + d * kAQ + qb + 2);
       const double k0v = Kt[d * kAK + lane], k1v = Kt[d * kAK + lane + 32];
-      sc[0][0] += qa.x * k0v; sc[0][1] += qa.x * k1v;
-      sc[1][0] += qa.y * k0v; sc[1][1] += qa.y * k1v;
-      sc[2][0] += qc.x * k0v; sc[2][1] += qc.x * k1v;
-      sc[3][0] += qc.y * k0v; sc[3][1] += qc.y * k1v;
+#pragma unroll
+      for (int i2 = 0; i2 < QW; i2 += 2) {
+        const double2 qa = *reinterpret_cast<const double2*>(Qs + d * kAQ + qb + i2);
+        sc[i2][0] += qa.x * k0v; sc[i2][1] += qa.x * k1v;
+        sc[i2 + 1][0] += qa.y * k0v; sc[i2 + 1][1] += qa.y * k1v;
+      }
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < QW; ++i) {
       const int q_pos = tok0 + qb + i;
       const bool qv = qb + i < nq;
       bool ok[2];
@@ -326,20 +335,22 @@ __global__ void __launch_bounds__(kAThreads, 1)
     __syncwarp();  // the warp's own rows of Ps
     const int kn = k_end - k0 < kAK ? k_end - k0 : kAK;
     for (int j = 0; j < kn; ++j) {
-      const double2 pa = *reinterpret_cast<const double2*>(Ps + j * kAQ + qb);
-      const double2 pc = *reinterpret_cast<const double2*>(Ps + j * kAQ + qb + 2);
+      double v[4];
 #pragma unroll
-      for (int dd = 0; dd < 4; ++dd) {
-        const double v = Vs[j * kAHd + lane + 32 * dd];
-        acc[0][dd] += pa.x * v;
-        acc[1][dd] += pa.y * v;
-        acc[2][dd] += pc.x * v;
-        acc[3][dd] += pc.y * v;
+      for (int dd = 0; dd < 4; ++dd) v[dd] = Vs[j * kAHd + lane + 32 * dd];
+#pragma unroll
+      for (int i2 = 0; i2 < QW; i2 += 2) {
+        const double2 pa = *reinterpret_cast<const double2*>(Ps + j * kAQ + qb + i2);
+#pragma unroll
+        for (int dd = 0; dd < 4; ++dd) {
+          acc[i2][dd] += pa.x * v[dd];
+          acc[i2 + 1][dd] += pa.y * v[dd];
+        }
       }
     }
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < QW; ++i) {
     if (qb + i >= nq) continue;
     const double inv = (n[i] == 0 || use_sigmoid) ? 1.0 : 1.0 / l[i];
     float* o = out + static_cast<int64_t>(tok0 + qb + i) * q_dim + h * head_dim;
@@ -388,16 +399,23 @@ Status launch_mha_attention(const float* q, const float* k, const float* v, doub
   const bool use_alibi = p.pos_kind == 2 || p.pos_kind == 3;
   const char* env = std::getenv("WELVET_B200_ATTN");
   if (p.head_dim <= kAHd && !(env && std::strcmp(env, "warp") == 0)) {
-    const size_t smem = attention_tiled_smem();
-    // per device (the attribute belongs to the current device's context); a cheap host call
-    WB_CUDA(cudaFuncSetAttribute(k_attention_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(smem)));
-    const dim3 grid(static_cast<unsigned>(p.batch * ((p.seq + kAQ - 1) / kAQ)), static_cast<unsigned>(p.num_heads));
-    k_attention_tiled<<<grid, kAThreads, smem, st>>>(Qr, Kr, Vd, out, p.batch, p.seq, p.num_heads, p.num_kv,
-                                                     p.head_dim, p.max_seq_len, p.mask, use_alibi ? 1 : 0,
-                                                     p.softmax_kind == 1 ? 1 : 0, p.window, p.prefix_len,
-                                                     p.window_causal, scale);
-    return cuda_status(cudaGetLastError(), "attention launch");
+    // 64 queries per CTA unless WELVET_B200_ATTN=tiled32 (32 per CTA)
+    const bool q64 = !(env && std::strcmp(env, "tiled32") == 0);
+    auto launch = [&](auto qw_c) -> Status {
+      constexpr int QW = decltype(qw_c)::value;
+      constexpr int kAQ = attn_queries<QW>();
+      const size_t smem = attention_tiled_smem<QW>();
+      // per device (the attribute belongs to the current device's context); a cheap host call
+      WB_CUDA(cudaFuncSetAttribute(k_attention_tiled<QW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(smem)));
+      const dim3 grid(static_cast<unsigned>(p.batch * ((p.seq + kAQ - 1) / kAQ)), static_cast<unsigned>(p.num_heads));
+      k_attention_tiled<QW><<<grid, kAThreads, smem, st>>>(Qr, Kr, Vd, out, p.batch, p.seq, p.num_heads, p.num_kv,
+                                                           p.head_dim, p.max_seq_len, p.mask, use_alibi ? 1 : 0,
+                                                           p.softmax_kind == 1 ? 1 : 0, p.window, p.prefix_len,
+                                                           p.window_causal, scale);
+      return cuda_status(cudaGetLastError(), "attention launch");
+    };
+    return q64 ? launch(std::integral_constant<int, 8>{}) : launch(std::integral_constant<int, 4>{});
   }
   const int warps = bs * p.num_heads;
   k_attention<<<(warps + 3) / 4, 128, 0, st>>>(Qr, Kr, Vd, out, p.batch, p.seq, p.num_heads, p.num_kv,
