@@ -254,6 +254,8 @@ __global__ void __launch_bounds__(kAThreads, 1)
   const int kv_len = (b + 1) * seq;
   const int q_dim = num_heads * head_dim, kv_dim = num_kv * head_dim;
   const int kvh = h / (num_heads / num_kv);
+  // kAQ * kAHd / kAThreads loads per thread, all in flight (the loop is unrolled)
+#pragma unroll 8
   for (int i = tid; i < kAQ * kAHd; i += kAThreads) {
     const int q = i / kAHd, d = i - q * kAHd;
     Qs[d * kAQ + q] = q < nq && d < head_dim ? Qr[static_cast<int64_t>(tok0 + q) * q_dim + h * head_dim + d] : 0.0;
@@ -279,6 +281,8 @@ __global__ void __launch_bounds__(kAThreads, 1)
       prow[tid] = kp < k_end ? slot + msl * ((kv_len - 1 - slot) / msl) : -1;
     }
     __syncthreads();
+    // the tile's K and V rows: 32 loads of each per thread, 8 iterations' worth in flight
+#pragma unroll 8
     for (int i = tid; i < kAK * kAHd; i += kAThreads) {
       const int j = i / kAHd, d = i - j * kAHd;
       const int p = prow[j];
