@@ -63,8 +63,8 @@ WELVET_API welvet_status welvet_b200_dense_execute_group_device(welvet_dense_ses
  * per-token scales, split-K partials -- in one static 32 MiB device array that the library
  * holds on every GPU that loads it until the process exits; a call needing more returns
  * status 1. The first call on a device (and the first after that device's context was
- * re-created) looks up the array's device address and should be made before any stream
- * capture. All calls share the array: calls whose kernels overlap on one GPU (other streams
+ * re-created) looks up the array's device address. All calls share the array: calls whose
+ * kernels overlap on one GPU (other streams
  * or threads) race and must be serialized by the caller. A timed-out pipeline wait is
  * recorded in the session's error word, which welvet_b200_dense_check_error reads. */
 WELVET_API welvet_status welvet_b200_dense_execute_device_noalloc(welvet_dense_session* sess,
