@@ -707,8 +707,9 @@ def test_grouped_gemv_matches_single_launches(wb, oracle, dt, out, in_, n, monke
     dict(batch=1, seq=200, d=96, nh=3, nkv=1, hd=32, msl=200, mask=1, pos=2),    # ALiBi, 3 heads on 1 KV head
 ])
 def test_attention_tiled_matches_warp_kernel(wb, cfg, monkeypatch):
-    """The tiled attention core (K / V tiles gathered into shared memory, 64 queries per CTA by
-    default, 32 with WELVET_B200_ATTN=tiled32) against the per-(query, head) warp kernel it
+    """The tiled attention core (K / V tiles gathered into shared memory, 64 queries on 16 warps
+    per CTA by default; 32 queries on 8 warps with WELVET_B200_ATTN=tiled32, 64 on 8 or 32
+    warps with =tiled8w / =tiled32w) against the per-(query, head) warp kernel it
     replaces: both fp64 with the same ring semantics, so they differ only in summation order;
     the two tile widths sum in the same order and agree bit for bit."""
     monkeypatch.setenv("WELVET_B200_EXACT", "0")
@@ -722,10 +723,11 @@ def test_attention_tiled_matches_warp_kernel(wb, cfg, monkeypatch):
             wb.FP8E4M3)
     monkeypatch.setenv("WELVET_B200_ATTN", "tiled")
     pre_t, post_t = wb.mha_forward_f32(*args)
-    monkeypatch.setenv("WELVET_B200_ATTN", "tiled32")
-    pre_32, post_32 = wb.mha_forward_f32(*args)
-    np.testing.assert_array_equal(pre_t, pre_32)
-    np.testing.assert_array_equal(post_t, post_32)
+    for variant in ("tiled32", "tiled8w", "tiled32w"):
+        monkeypatch.setenv("WELVET_B200_ATTN", variant)
+        pre_v, post_v = wb.mha_forward_f32(*args)
+        np.testing.assert_array_equal(pre_t, pre_v, err_msg=variant)
+        np.testing.assert_array_equal(post_t, post_v, err_msg=variant)
     monkeypatch.setenv("WELVET_B200_ATTN", "warp")
     pre_w, post_w = wb.mha_forward_f32(*args)
     np.testing.assert_allclose(pre_t, pre_w, rtol=1e-6, atol=1e-7 * np.abs(pre_w).max())

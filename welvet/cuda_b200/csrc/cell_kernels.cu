@@ -221,32 +221,41 @@ __global__ void k_attention(const double* __restrict__ Qr, const double* __restr
 // stay in fp64. Warp w owns queries QW w .. QW w + QW - 1; for the scores lane l takes key
 // positions l and l + 32 of the tile, for the output the head dimensions l, l + 32, l + 64,
 // l + 96. QW = 8 (64 queries per CTA) makes twice the FMAs per shared-memory load of QW = 4.
-constexpr int kAK = 64, kAHd = 128, kAThreads = 256;
+constexpr int kAK = 64, kAHd = 128;
+// K is stored transposed with rows of kAK + 1 doubles: the gather writes consecutive head
+// dimensions of one key, which a row of exactly kAK doubles would put in one bank
+constexpr int kAKs = kAK + 1;
 
-template <int QW>
-__host__ __device__ constexpr int attn_queries() { return 8 * QW; }
+// NW warps per CTA, QW queries per warp: 16 x 4 by default (64 queries; the FP64 pipe needs
+// the warps to hide its latency), 8 x 8, 32 x 2 or 8 x 4 (32 queries) on request.
+template <int QW, int NW = 8>
+__host__ __device__ constexpr int attn_queries() { return NW * QW; }
 
-template <int QW>
+template <int QW, int NW = 8>
 size_t attention_tiled_smem() {
-  constexpr int kAQ = attn_queries<QW>();
-  return sizeof(double) * (kAHd * kAQ + kAHd * kAK + kAK * kAHd + kAK * kAQ) + sizeof(int) * kAK;
+  constexpr int kAQ = attn_queries<QW, NW>();
+  return sizeof(double) * (kAHd * kAQ + kAHd * kAKs + kAK * kAHd + kAK * kAQ) + sizeof(int) * kAK;
 }
 
-template <int QW>
-__global__ void __launch_bounds__(kAThreads, 1)
+template <int QW, int NW = 8>
+__global__ void __launch_bounds__(32 * NW, 1)
     k_attention_tiled(const double* __restrict__ Qr, const double* __restrict__ Kr, const double* __restrict__ Vd,
                       float* __restrict__ out, int batch, int seq, int num_heads, int num_kv, int head_dim, int msl,
                       int mask, int use_alibi, int use_sigmoid, int window, int prefix_len, int window_causal,
                       double scale) {
-  constexpr int kAQ = attn_queries<QW>();
+  constexpr int kAQ = attn_queries<QW, NW>();
+  constexpr int kAThreads = 32 * NW;
   extern __shared__ double sm[];
   double* Qs = sm;                  // [kAHd][kAQ]: queries' rotated Q, d-major
-  double* Kt = Qs + kAHd * kAQ;     // [kAHd][kAK]: the tile's keys, d-major
-  double* Vs = Kt + kAHd * kAK;     // [kAK][kAHd]
+  double* Kt = Qs + kAHd * kAQ;     // [kAHd][kAKs]: the tile's keys, d-major
+  double* Vs = Kt + kAHd * kAKs;    // [kAK][kAHd]
   double* Ps = Vs + kAK * kAHd;     // [kAK][kAQ]: the tile's weights, key-major
   int* prow = reinterpret_cast<int*>(Ps + kAK * kAQ);  // [kAK] ring row of each key position (-1: none)
   const int qtiles = (seq + kAQ - 1) / kAQ;
-  const int b = blockIdx.x / qtiles, s0 = (blockIdx.x - b * qtiles) * kAQ;
+  // blocks run longest first: later batches and later queries see more key positions, and
+  // the scheduler starts blocks roughly in index order
+  const int bx = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);
+  const int b = bx / qtiles, s0 = (bx - b * qtiles) * kAQ;
   const int h = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int nq = seq - s0 < kAQ ? seq - s0 : kAQ;
@@ -288,7 +297,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
       const int p = prow[j];
       const bool ok = p >= 0 && d < head_dim;
       const int64_t off = static_cast<int64_t>(p) * kv_dim + kvh * head_dim + d;
-      Kt[d * kAK + j] = ok ? Kr[off] : 0.0;
+      Kt[d * kAKs + j] = ok ? Kr[off] : 0.0;
       Vs[j * kAHd + d] = ok ? Vd[off] : 0.0;
     }
     __syncthreads();
@@ -297,7 +306,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
 #pragma unroll
     for (int i = 0; i < QW; ++i) sc[i][0] = sc[i][1] = 0.0;
     for (int d = 0; d < head_dim; ++d) {
-      const double k0v = Kt[d * kAK + lane], k1v = Kt[d * kAK + lane + 32];
+      const double k0v = Kt[d * kAKs + lane], k1v = Kt[d * kAKs + lane + 32];
 #pragma unroll
       for (int i2 = 0; i2 < QW; i2 += 2) {
         const double2 qa = *reinterpret_cast<const double2*>(Qs + d * kAQ + qb + i2);
@@ -403,23 +412,31 @@ Status launch_mha_attention(const float* q, const float* k, const float* v, doub
   const bool use_alibi = p.pos_kind == 2 || p.pos_kind == 3;
   const char* env = std::getenv("WELVET_B200_ATTN");
   if (p.head_dim <= kAHd && !(env && std::strcmp(env, "warp") == 0)) {
-    // 64 queries per CTA unless WELVET_B200_ATTN=tiled32 (32 per CTA)
-    const bool q64 = !(env && std::strcmp(env, "tiled32") == 0);
-    auto launch = [&](auto qw_c) -> Status {
+    // 64 queries on 16 warps per CTA (4 per warp) unless WELVET_B200_ATTN=tiled8w (64 on 8
+    // warps), =tiled32w (64 on 32 warps) or =tiled32 (32 queries on 8 warps). Measured on C4's
+    // MHA cell: 8 warps x 4 queries 3.25 ms, 8 x 8 2.84 ms, 16 x 4 2.39 ms.
+    const bool q32 = env && std::strcmp(env, "tiled32") == 0;
+    const bool w8 = env && std::strcmp(env, "tiled8w") == 0;
+    const bool w32 = env && std::strcmp(env, "tiled32w") == 0;
+    auto launch = [&](auto qw_c, auto nw_c) -> Status {
       constexpr int QW = decltype(qw_c)::value;
-      constexpr int kAQ = attn_queries<QW>();
-      const size_t smem = attention_tiled_smem<QW>();
+      constexpr int NW = decltype(nw_c)::value;
+      constexpr int kAQ = attn_queries<QW, NW>();
+      const size_t smem = attention_tiled_smem<QW, NW>();
       // per device (the attribute belongs to the current device's context); a cheap host call
-      WB_CUDA(cudaFuncSetAttribute(k_attention_tiled<QW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      WB_CUDA(cudaFuncSetAttribute(k_attention_tiled<QW, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(smem)));
       const dim3 grid(static_cast<unsigned>(p.batch * ((p.seq + kAQ - 1) / kAQ)), static_cast<unsigned>(p.num_heads));
-      k_attention_tiled<QW><<<grid, kAThreads, smem, st>>>(Qr, Kr, Vd, out, p.batch, p.seq, p.num_heads, p.num_kv,
-                                                           p.head_dim, p.max_seq_len, p.mask, use_alibi ? 1 : 0,
-                                                           p.softmax_kind == 1 ? 1 : 0, p.window, p.prefix_len,
-                                                           p.window_causal, scale);
+      k_attention_tiled<QW, NW><<<grid, 32 * NW, smem, st>>>(Qr, Kr, Vd, out, p.batch, p.seq, p.num_heads, p.num_kv,
+                                                             p.head_dim, p.max_seq_len, p.mask, use_alibi ? 1 : 0,
+                                                             p.softmax_kind == 1 ? 1 : 0, p.window, p.prefix_len,
+                                                             p.window_causal, scale);
       return cuda_status(cudaGetLastError(), "attention launch");
     };
-    return q64 ? launch(std::integral_constant<int, 8>{}) : launch(std::integral_constant<int, 4>{});
+    if (q32) return launch(std::integral_constant<int, 4>{}, std::integral_constant<int, 8>{});
+    if (w8) return launch(std::integral_constant<int, 8>{}, std::integral_constant<int, 8>{});
+    if (w32) return launch(std::integral_constant<int, 2>{}, std::integral_constant<int, 32>{});
+    return launch(std::integral_constant<int, 4>{}, std::integral_constant<int, 16>{});
   }
   const int warps = bs * p.num_heads;
   k_attention<<<(warps + 3) / 4, 128, 0, st>>>(Qr, Kr, Vd, out, p.batch, p.seq, p.num_heads, p.num_kv,
