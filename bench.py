@@ -747,7 +747,9 @@ def run_case(args):
       gemv   one Dense layer rows x cols, --tokens 1..8 (tensor GEMV)
       group  --layers independent layers rows x cols, B=1, grouped launches
       gemm   one Dense layer rows x cols, --tokens > 8 (tcgen05 path)
-      swiglu one SwiGLU cell, d = cols, hidden = rows, --tokens (Gate/Up pair GEMM, Down GEMM)"""
+      swiglu one SwiGLU cell, d = cols, hidden = rows, --tokens (Gate/Up pair GEMM, Down GEMM)
+      mha    config 4's MHA cell (4 x 512 tokens, d 2048, 16 heads x 128, causal, RoPE, ring of
+             512; E4M3 projections): the projections and the fp64 attention core"""
     import torch
     import welvet.cuda_b200 as W
     W.cuda_init()
@@ -770,6 +772,20 @@ def run_case(args):
             ts.append(e0.elapsed_time(e1) * 1e3)
         return statistics.median(ts)
 
+    if args.case == "mha":
+        B, S, d, heads, hd = 4, 512, 2048, 16, 128
+        ws = [torch.randn((d, d), device="cuda", generator=g) * SIGMA for _ in range(4)]
+        cell = W.MhaCell(*ws, d_model=d, num_heads=heads, num_kv_heads=heads, head_dim=hd, max_seq_len=S, mask=1,
+                         pos=0, dtype=E4M3)
+        del ws
+        x = torch.randn((B * S, d), device="cuda", generator=g)
+        y = torch.empty_like(x)
+        attn = torch.empty_like(x)
+        us = each(lambda: cell.execute_device(x, B, S, y, attn))
+        print(json.dumps({"case": "mha", "batch": B, "seq": S, "d": d, "heads": heads, "head_dim": hd,
+                          "reps": args.reps, "us_median": round(us, 2)}), flush=True)
+        cell.release()
+        return 0
     if args.case == "swiglu":
         d, hid, m = args.cols, args.rows, args.tokens
         ws = [torch.randn(sh, device="cuda", generator=g) * SIGMA for sh in ((hid, d), (hid, d), (d, hid))]
@@ -827,7 +843,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the host-core and reference-CUDA legs")
     ap.add_argument("--no-configs", action="store_true", help="skip the configs 1-4 sub-records (N = 1)")
-    ap.add_argument("--case", choices=["gemv", "group", "gemm", "swiglu"],
+    ap.add_argument("--case", choices=["gemv", "group", "gemm", "swiglu", "mha"],
                     help="time one workload alone (see run_case)")
     ap.add_argument("--dtype", type=int, default=FP4, help="--case: 16 FP4, 4 E4M3, 5 E5M2, 9 Int8")
     ap.add_argument("--rows", type=int, default=4096)
