@@ -53,7 +53,7 @@ def test_encode_kats(oracle):
     assert not bad, bad[:10]
 
 
-def test_survey_edge_cases(oracle):
+def test_codec_edge_cases(oracle):
     """Hand-checked reference probe values (E4M3 half-up and saturation, FP4 ties)."""
     L = oracle.lib()
     assert L.or_e4m3_encode(0.01) == 0x05 and L.or_e4m3_encode(1.0625) == 0x39
