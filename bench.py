@@ -669,6 +669,19 @@ def c4_legs(c: Ctx, tens: float):
     attn = torch.empty((T, d), device="cuda")
     us_mha = c.timed_each(lambda: mha.execute_device(xn, B, S, y, attn), 5)
     mha.release()
+    # RMSNorm -> Q projection as one volume: the norm as the GEMM's prologue (default) and as
+    # its own kernel (WELVET_B200_NORM_PROLOGUE=0); the output copy out of the volume is common
+    vol = c.V.Volume(1, 1, 1, 2)
+    vol.bind_rmsnorm((0, 0, 0, 0), gamma, 1e-6, W.FLOAT32)
+    vol.bind_dense((0, 0, 0, 1), qkvo[0], -1, E4M3)
+    vy = torch.empty_like(x)
+    us_norm_q = c.timed_each(lambda: vol.forward_device(x, vy), 10)
+    os.environ["WELVET_B200_NORM_PROLOGUE"] = "0"
+    try:
+        us_norm_q_sep = c.timed_each(lambda: vol.forward_device(x, vy), 10)
+    finally:
+        del os.environ["WELVET_B200_NORM_PROLOGUE"]
+    vol.release()
     proj = [W.DenseSession(w, T, E4M3) for w in qkvo]
     del qkvo
     py = torch.empty((T, d), device="cuda")
@@ -680,6 +693,7 @@ def c4_legs(c: Ctx, tens: float):
     for p in proj:
         p.release()
     rec = {"us_rmsnorm": us_norm, "us_mha_cell": us_mha, "us_qkvo_projections": us_proj,
+           "us_norm_q_prologue": us_norm_q, "us_norm_q_separate": us_norm_q_sep,
            "us_attention_and_rope": max(0.0, us_mha - us_proj),
            "proj_TFLOPs": 2.0 * T * 4 * d * d / us_proj / 1e6}
     for tag, sigma in (("swiglu_fp4", SIGMA), ("swiglu_fp4_sigma2", 2.0)):

@@ -164,3 +164,82 @@ def test_mixed_cells_match_one_shot_entry_points(wb, oracle, V):
     np.testing.assert_array_equal(y, stages[3])
     y2 = vol.forward_f32(x, 64)
     np.testing.assert_array_equal(y, y2)
+
+
+def _kernel_names(fn):
+    """Names of the CUDA kernels launched while fn runs (torch's CUPTI-based profiler)."""
+    from torch.profiler import ProfilerActivity, profile
+    torch = _torch()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return [e.name for e in prof.events() if e.device_type.name == "CUDA"]
+
+
+@pytest.mark.parametrize("kind,d", [("dense", 1024), ("dense", 1002), ("swiglu", 1024), ("mha", 1024)])
+def test_rmsnorm_prologue(wb, oracle, V, kind, d, monkeypatch):
+    """An RMSNorm cell followed by a projection cell runs inside that cell's tcgen05 GEMM launch
+    (the x-split kernel normalises, writes the norm's pre / post and splits post): no k_rmsnorm
+    launch, and every recorded output bit-identical to the norm as its own kernel
+    (WELVET_B200_NORM_PROLOGUE=0). d = 1002 makes rows that start off 16-byte boundaries and a
+    ragged last 4-element chunk. The norm against the fp64 formula (src/cuda/kernels.cu:172-204)
+    and the Dense against the oracle on the GPU's normalised rows."""
+    torch = _torch()
+    rng = np.random.default_rng(77 + d)
+    T, dt = 48, oracle.FP8E4M3
+    g = rng.standard_normal(d).astype(np.float32)
+    x = (rng.standard_normal((T, d)) * 3.0).astype(np.float32)
+    vol = V.Volume(1, 1, 1, 2)
+    vol.bind_rmsnorm((0, 0, 0, 0), g, 1e-6, wb.FLOAT32)
+    if kind == "dense":
+        W = (rng.standard_normal((1536, d)) * 0.05).astype(np.float32)
+        bias = rng.standard_normal(1536) * 0.1
+        vol.bind_dense((0, 0, 0, 1), W, 2, dt, bias)
+        width = 1536
+    elif kind == "swiglu":
+        G, U = [(rng.standard_normal((1536, d)) * 0.05).astype(np.float32) for _ in range(2)]
+        D = (rng.standard_normal((d, 1536)) * 0.05).astype(np.float32)
+        vol.bind_swiglu((0, 0, 0, 1), G, U, D, dt)
+        width = d
+    else:
+        # 16 heads x 128: Q is 2048 x d, above 2^20 weights, so on the tcgen05 GEMM
+        Q, K, Vw = [(rng.standard_normal((2048, d)) * 0.05).astype(np.float32) for _ in range(3)]
+        O = (rng.standard_normal((d, 2048)) * 0.05).astype(np.float32)
+        vol.bind_mha((0, 0, 0, 1), Q, K, Vw, O, d, 16, 16, 128, 16, 1, 0, seq=16, dtype=dt)
+        width = d
+    xd = torch.from_numpy(x).cuda()
+
+    def run():
+        out = torch.empty((T, width), dtype=torch.float32, device="cuda")
+        vol.forward_device(xd, out)
+        torch.cuda.synchronize()
+        rec = [out.cpu().numpy()]
+        for h in range(2):
+            pre, pw, post, ow = vol.cell_outputs(vol.coord(h))
+            rec.append(V.device_tensor(pre, (T, pw)).cpu().numpy())
+            rec.append(V.device_tensor(post, (T, ow)).cpu().numpy())
+        return rec
+
+    fused = run()
+    names = _kernel_names(lambda: vol.forward_device(xd, torch.empty((T, width), device="cuda")))
+    if names:  # the profiler saw kernels: the norm ran inside the GEMM launch
+        assert not any("k_rmsnorm" in n for n in names), names
+        assert any("k_split_x" in n for n in names), names
+    monkeypatch.setenv("WELVET_B200_NORM_PROLOGUE", "0")
+    alone = run()
+    if names:
+        names0 = _kernel_names(lambda: vol.forward_device(xd, torch.empty((T, width), device="cuda")))
+        assert any("k_rmsnorm" in n for n in names0), names0
+    for a, b, what in zip(fused, alone, ("out", "norm pre", "norm post", "cell pre", "cell post")):
+        np.testing.assert_array_equal(a, b, err_msg=what)
+    xx = x.astype(np.float64)
+    inv = 1.0 / np.sqrt((xx * xx).sum(1, keepdims=True) / d + 1e-6)
+    np.testing.assert_allclose(fused[1], (xx * inv).astype(np.float32), rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(fused[2], (xx * inv * g.astype(np.float64)).astype(np.float32), rtol=1e-6,
+                               atol=1e-7)
+    if kind == "dense":
+        raw, sc = oracle.pack(dt, W)
+        ref = oracle.dense_forward(dt, raw, sc, fused[2], d, 1536, 2, bias)
+        check_dense(fused[3], fused[4], ref, 2, f"dense after the norm, d={d}")
+    vol.release()

@@ -13,6 +13,7 @@
 // p' <= (b+1)*seq-1 with p' == k_pos (mod msl). Masks and ALiBi use k_pos; RoPE of the key
 // was applied at p'. The running max starts at -1e9 as in the reference.
 #include "cell_kernels.hpp"
+#include "rmsnorm.cuh"
 
 #include <cstdlib>
 #include <cstring>
@@ -33,28 +34,31 @@ __device__ __forceinline__ double warp_max_d(double v) {
   return v;
 }
 
-// One warp per token.
-__global__ void k_rmsnorm(const float* __restrict__ x, const double* __restrict__ gamma,
-                          float* __restrict__ pre, float* __restrict__ post, int n_tok, int dim,
-                          double eps) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= n_tok) return;
-  const float* xt = x + static_cast<int64_t>(warp) * dim;
-  double ss = 0.0;
-  for (int i = lane; i < dim; i += 32) {
-    const double v = static_cast<double>(xt[i]);
-    ss += v * v;
-  }
-  ss = warp_sum_d(ss);
-  const double inv = 1.0 / sqrt(ss / static_cast<double>(dim) + eps);
-  float* pt = pre + static_cast<int64_t>(warp) * dim;
-  float* qt = post + static_cast<int64_t>(warp) * dim;
-  for (int i = lane; i < dim; i += 32) {
-    const double xh = static_cast<double>(xt[i]) * inv;
-    pt[i] = static_cast<float>(xh);
-    qt[i] = static_cast<float>(xh * gamma[i]);
-  }
+// One block of kNormThreads per token, its sum of squares in rms_block_ss's order (the
+// projection GEMM's prologue gives the same bits). x, pre and post are [n_tok][dim].
+__global__ void __launch_bounds__(kNormThreads)
+    k_rmsnorm(const float* __restrict__ x, const double* __restrict__ gamma, float* __restrict__ pre,
+              float* __restrict__ post, int n_tok, int dim, double eps) {
+  __shared__ double s_part[kNormThreads / 32];
+  const int t = blockIdx.x;
+  if (t >= n_tok) return;
+  const float* xt = x + static_cast<int64_t>(t) * dim;
+  float* pt = pre + static_cast<int64_t>(t) * dim;
+  float* qt = post + static_cast<int64_t>(t) * dim;
+  const bool vec = (reinterpret_cast<uintptr_t>(xt) & 15) == 0;
+  const bool vec_out = ((reinterpret_cast<uintptr_t>(pt) | reinterpret_cast<uintptr_t>(qt)) & 15) == 0;
+  auto load4 = [&](int k) -> float4 {
+    if (vec && k + 3 < dim) return *reinterpret_cast<const float4*>(xt + k);
+    float4 v;
+    v.x = xt[k];
+    v.y = k + 1 < dim ? xt[k + 1] : 0.0f;
+    v.z = k + 2 < dim ? xt[k + 2] : 0.0f;
+    v.w = k + 3 < dim ? xt[k + 3] : 0.0f;
+    return v;
+  };
+  const double inv = rms_inv(rms_block_ss(load4, dim, s_part), dim, eps);
+  for (int k = 4 * threadIdx.x; k < dim; k += 4 * kNormThreads)
+    rms_apply4(load4(k), k, dim, inv, gamma, pt, qt, true, vec_out);
 }
 
 // Widen projections to f64 and rotate Q and K at each token's global position.
@@ -390,9 +394,9 @@ __global__ void k_swiglu_product(const float* __restrict__ g, const float* __res
 
 Status launch_rmsnorm(const float* x, const double* gamma, float* pre, float* post, int n_tok, int dim,
                       double eps, cudaStream_t st) {
-  const int threads = 256;
-  const int blocks = static_cast<int>((static_cast<int64_t>(n_tok) * 32 + threads - 1) / threads);
-  k_rmsnorm<<<blocks, threads, 0, st>>>(x, gamma, pre, post, n_tok, dim, eps);
+  if (n_tok <= 0 || dim <= 0) return Status::Ok();
+  if ((reinterpret_cast<uintptr_t>(gamma) & 15) != 0) return Status::Invalid("rmsnorm: gamma not 16-byte aligned");
+  k_rmsnorm<<<n_tok, kNormThreads, 0, st>>>(x, gamma, pre, post, n_tok, dim, eps);
   return cuda_status(cudaGetLastError(), "rmsnorm launch");
 }
 

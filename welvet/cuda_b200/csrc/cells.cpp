@@ -157,11 +157,19 @@ Status swiglu_reserve(SwigluCell* c, int bs, cudaStream_t st) {
 
 // x [bs][in] -> h [bs][inter] (= SiLU(Gate x) * (Up x), the reference's pre) -> y = Down h.
 Status swiglu_forward_device(SwigluCell* c, int bs, const float* x, float* h, float* y, cudaStream_t st,
-                             bool pdl) {
+                             bool pdl, const SplitNorm* norm) {
   WB_TRY(swiglu_reserve(c, bs, st));
   const float* hsrc = nullptr;  // h as Down's input
   int64_t h_ld = 0;
-  if (swiglu_group_gemv(c, bs) && c->g_buf && c->io_gate.prep && c->io_up.prep) {
+  const bool group = swiglu_group_gemv(c, bs) && c->g_buf && c->io_gate.prep && c->io_up.prep;
+  const bool pair = !group && !swiglu_small_gemv(c, bs) && swiglu_batched(c, bs) && c->pair_scratch;
+  if (norm && norm->gamma && !pair) {
+    // an RMSNorm in front, as its own kernel (the pair GEMM takes it as its prologue)
+    if (!norm->pre || !norm->post) return Status::Invalid("rmsnorm: null outputs");
+    WB_TRY(launch_rmsnorm(x, norm->gamma, norm->pre, norm->post, bs, c->in, norm->eps, st));
+    x = norm->post;
+  }
+  if (group) {
     // 1..4 rows, grouped: Gate and Up in one launch of two layers, then the reference's
     // SiLU product into h
     GemvGroupLayer L[2];
@@ -212,7 +220,7 @@ Status swiglu_forward_device(SwigluCell* c, int bs, const float* x, float* h, fl
     WB_TRY(launch_gemv_tc(a, st, pdl));
     hsrc = a.pre;
     h_ld = a.ld_out;
-  } else if (swiglu_batched(c, bs) && c->pair_scratch) {
+  } else if (pair) {
     // batched: Gate and Up as one pair GEMM (2 x inter interleaved rows) whose epilogue
     // writes h = SiLU(gate)·up directly
     float* hout = h ? h : c->h_pad;
@@ -235,6 +243,7 @@ Status swiglu_forward_device(SwigluCell* c, int bs, const float* x, float* h, fl
     g.scratch = c->pair_scratch;
     g.scratch_bytes = c->pair_scratch_bytes;
     g.err = c->io_gate.err;
+    if (norm) g.norm = *norm;
     WB_TRY(launch_gemm_tc(g, st));
     hsrc = hout;
     h_ld = ld;
@@ -371,15 +380,19 @@ Status mha_reserve(MhaCell* c, int bs, cudaStream_t st) {
   return Status::Ok();
 }
 
-Status mha_forward_device(MhaCell* c, int batch, int seq, const float* x, float* attn, float* y, cudaStream_t st) {
+Status mha_forward_device(MhaCell* c, int batch, int seq, const float* x, float* attn, float* y, cudaStream_t st,
+                          const SplitNorm* norm) {
   const MhaConfig& g = c->cfg;
   if (batch <= 0 || seq <= 0) return Status::Invalid("mha: bad batch/seq");
   if (seq > g.max_seq_len) return Status::Invalid("mha: seq > MaxSeqLen");
   const int bs = batch * seq;
   WB_TRY(mha_reserve(c, bs, st));
-  WB_TRY(forward_device(c->q, bs, x, g.d_model, c->qb, c->qb, &c->io_q, st, false));
-  WB_TRY(forward_device(c->k, bs, x, g.d_model, c->kb, c->kb, &c->io_k, st, false));
-  WB_TRY(forward_device(c->v, bs, x, g.d_model, c->vb, c->vb, &c->io_v, st, false));
+  // an RMSNorm in front runs with Q's projection (its prologue on the tensor-core GEMM); K and
+  // V read the norm's post
+  WB_TRY(forward_device(c->q, bs, x, g.d_model, c->qb, c->qb, &c->io_q, st, false, 0, nullptr, norm));
+  const float* xn = norm && norm->gamma ? norm->post : x;
+  WB_TRY(forward_device(c->k, bs, xn, g.d_model, c->kb, c->kb, &c->io_k, st, false));
+  WB_TRY(forward_device(c->v, bs, xn, g.d_model, c->vb, c->vb, &c->io_v, st, false));
   AttnParams p;
   p.batch = batch; p.seq = seq; p.num_heads = g.num_heads; p.num_kv = g.num_kv_heads; p.head_dim = g.head_dim;
   p.max_seq_len = g.max_seq_len; p.mask = g.mask; p.pos_kind = g.pos; p.softmax_kind = g.softmax;

@@ -55,8 +55,9 @@ Status swiglu_mount_src(int device, int in, int inter, DType dt, const WeightSrc
 Status swiglu_reserve(SwigluCell* c, int bs, cudaStream_t st);
 // x [bs][in] (device) -> h [bs][inter] (the reference's pre) and y [bs][in] (post).
 // h may be nullptr (h stays in the cell's padded work buffer).
+// `norm` (may be nullptr): an RMSNorm of width in in front (x is its input; see forward_device).
 Status swiglu_forward_device(SwigluCell* c, int bs, const float* x, float* h, float* y, cudaStream_t st,
-                             bool pdl);
+                             bool pdl, const SplitNorm* norm = nullptr);
 
 struct MhaConfig {
   int d_model = 0, num_heads = 0, num_kv_heads = 0, head_dim = 0, max_seq_len = 0;
@@ -88,7 +89,7 @@ Status mha_mount_src(int device, const MhaConfig& cfg, DType dt, const WeightSrc
 Status mha_reserve(MhaCell* c, int bs, cudaStream_t st);
 // x [batch*seq][d_model] (device) -> attn [bs][q_dim] (pre) and y [bs][d_model] (post).
 Status mha_forward_device(MhaCell* c, int batch, int seq, const float* x, float* attn, float* y,
-                          cudaStream_t st);
+                          cudaStream_t st, const SplitNorm* norm = nullptr);
 
 // gamma f32 [dim] quantized with `dt` then decoded to f64 as the reference's gamma store.
 Status rmsnorm_gamma(int device, int dim, DType dt, const float* gamma, double** gamma64_dev, cudaStream_t st);

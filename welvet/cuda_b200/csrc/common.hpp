@@ -103,4 +103,16 @@ struct PeerOut {
   float* post[kMaxPeerOut] = {};
 };
 
+// An RMSNorm layer run as the prologue of the projection that consumes it (the reference's
+// norm_forward_f64 with center = 0, src/cuda/kernels.cu:172-204): x is the norm's input,
+// pre = x / sqrt(mean(x^2) + eps) and post = pre * gamma ([M][cols], the norm layer's outputs)
+// are written by the launch's first kernel, and the GEMM multiplies post. gamma == nullptr:
+// no prologue.
+struct SplitNorm {
+  const double* gamma = nullptr;  // [cols], the store's decoded gamma widened to fp64
+  double eps = 0.0;
+  float* pre = nullptr;
+  float* post = nullptr;
+};
+
 } // namespace wb

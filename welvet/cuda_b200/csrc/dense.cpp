@@ -8,6 +8,7 @@
 // synchronous; plus an asynchronous device-pointer variant.
 #include "dense.hpp"
 
+#include "cell_kernels.hpp"
 #include "codec.hpp"
 #include "gemm_tc.hpp"
 #include "gemv.hpp"
@@ -255,16 +256,26 @@ Status alloc_io(const DeviceDense& d, int batch, DenseIO* io, cudaStream_t st) {
 
 Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x_ld, float* pre,
                       float* post, DenseIO* io, cudaStream_t st, bool pdl, int64_t ld_out,
-                      const PeerOut* peers) {
+                      const PeerOut* peers, const SplitNorm* norm) {
   if (batch <= 0 || !x || !pre || !post) return Status::Invalid("null execute args");
   if (ld_out <= 0) ld_out = d.rows;
   if (ld_out < d.rows) return Status::Invalid("dense: output pitch below the layer's rows");
+  const bool gemm = use_tensor_path(d, batch) && io && io->scratch;
+  if (norm && norm->gamma) {
+    if (!norm->pre || !norm->post) return Status::Invalid("rmsnorm: null outputs");
+    if (!gemm) {  // the norm as its own kernel, then the layer on its post
+      if (x_ld != d.cols) return Status::Invalid("rmsnorm: input rows must be dense");
+      WB_TRY(launch_rmsnorm(x, norm->gamma, norm->pre, norm->post, batch, d.cols, norm->eps, st));
+      x = norm->post;
+      pdl = false;
+    }
+  }
   const PeerOut no_peers{};
   const PeerOut& pe = peers ? *peers : no_peers;
   const float* xs = x;  // the tensor-core paths read x in any layout
   int64_t xst = x_ld;
   const bool pdl_in = pdl;
-  if (use_tensor_path(d, batch) && io && io->scratch) {
+  if (gemm) {
     GemmArgs g;
     g.dtype = d.dtype;
     g.W = d.W;
@@ -289,6 +300,7 @@ Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x
     g.scratch_bytes = io->scratch_bytes;
     g.err = io->err;
     g.pdl = pdl_in;
+    if (norm) g.norm = *norm;
     return launch_gemm_tc(g, st);
   }
   if (use_gemv_tc(d, batch) && io && io->prep && gemv_prefers_prepared(d.dtype, d.rows, d.cols, batch)) {

@@ -115,9 +115,13 @@ Status check_pipeline_error(DenseIO& io, cudaStream_t st);
 // not already padded), outputs [batch][rows] into pre/post (device pointers).
 // `ld_out` (0: rows) is the row pitch of pre/post; `peers` (may be nullptr) lists further
 // destinations of post with the same layout (column-sharded layers, sharded.hpp).
+// `norm` (may be nullptr) puts an RMSNorm layer of width cols in front: x is the norm's input
+// ([batch][x_ld]), the norm's pre / post ([batch][cols]) are written, and the layer reads
+// post. On the tensor-core GEMM the norm is the launch's prologue; elsewhere it runs first as
+// its own kernel, with the same bits.
 Status forward_device(const DeviceDense& d, int batch, const float* x, int64_t x_ld, float* pre,
                       float* post, DenseIO* io, cudaStream_t st, bool pdl, int64_t ld_out = 0,
-                      const PeerOut* peers = nullptr);
+                      const PeerOut* peers = nullptr, const SplitNorm* norm = nullptr);
 
 struct DenseSession {
   int device = 0;

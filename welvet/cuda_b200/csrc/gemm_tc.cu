@@ -24,6 +24,7 @@
 #include "gemm_tc.hpp"
 #include "codec.cuh"
 #include "pipeline.cuh"
+#include "rmsnorm.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -1322,8 +1323,10 @@ __global__ void k_tail_reduce(const TailParams p) {
 // pcnt[t] (when given) = planes that hold a non-zero value for token t, at most xsplit.
 // One 512-thread block per token row (grid = Mp); rows >= M and columns >= K are zero. A row
 // whose start is 16-byte aligned is read in 16-byte vectors, every load of a thread in flight
-// at once (Kp is a multiple of 64).
+// at once (Kp is a multiple of 64). With nrm.gamma set, x is an RMSNorm layer's input: the
+// kernel is that layer (its pre / post, [M][K], are written here) and splits post.
 constexpr int kSplitThreads = 512;
+static_assert(kSplitThreads == kNormThreads, "the RMSNorm prologue sums squares in k_rmsnorm's order");
 
 // One element's planes: x * s = h0 + h1 + h2 (h0 alone for a non-finite x).
 __device__ __forceinline__ void split3(float v, float s, __half& h0, __half& h1, __half& h2) {
@@ -1343,12 +1346,14 @@ __device__ __forceinline__ void split3(float v, float s, __half& h0, __half& h1,
 
 __global__ void __launch_bounds__(kSplitThreads)
     k_split_x(const float* x, int64_t x_ld, int M, int K, int Mp, int Kp, int xsplit,
-              __half* __restrict__ planes, float* __restrict__ scale_inv, int* __restrict__ pcnt) {
+              __half* __restrict__ planes, float* __restrict__ scale_inv, int* __restrict__ pcnt,
+              SplitNorm nrm) {
   // x may be the previous kernel's output: ordered loads after the wait (ld_dep), never
   // non-coherent ones, which may be hoisted above it
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ float s_max[kSplitThreads / 32];
+  __shared__ double s_part[kSplitThreads / 32];
   __shared__ int s_nz;
   const int t = blockIdx.x;
   if (t >= Mp) return;
@@ -1356,29 +1361,35 @@ __global__ void __launch_bounds__(kSplitThreads)
   const float* xr = x + static_cast<int64_t>(t) * x_ld;
   const bool live = t < M;
   const bool vec = (reinterpret_cast<uintptr_t>(xr) & 15) == 0;
+  // x[t][k..k+3], zeros past K (16-byte loads when the row start is aligned)
+  auto load4 = [&](int k) -> float4 {
+    if (vec && k + 3 < K) return ld_dep4(xr + k);
+    float4 v;
+    v.x = k < K ? ld_dep(xr + k) : 0.0f;
+    v.y = k + 1 < K ? ld_dep(xr + k + 1) : 0.0f;
+    v.z = k + 2 < K ? ld_dep(xr + k + 2) : 0.0f;
+    v.w = k + 3 < K ? ld_dep(xr + k + 3) : 0.0f;
+    return v;
+  };
+  const bool norm = nrm.gamma != nullptr;
+  double inv = 0.0;
+  if (norm) inv = rms_inv(rms_block_ss(load4, live ? K : 0, s_part), K, nrm.eps);
+  // The values this row splits, k..k+3: x, or its RMSNorm post (rms_apply4, as k_rmsnorm),
+  // whose pre / post the first pass also stores.
+  float* npre = norm ? nrm.pre + static_cast<int64_t>(t) * K : nullptr;
+  float* npost = norm ? nrm.post + static_cast<int64_t>(t) * K : nullptr;
+  const bool vec_out = norm && ((reinterpret_cast<uintptr_t>(npre) | reinterpret_cast<uintptr_t>(npost)) & 15) == 0;
+  auto value4 = [&](int k, bool store) -> float4 {
+    const float4 v = load4(k);
+    return norm ? rms_apply4(v, k, K, inv, nrm.gamma, npre, npost, store, vec_out) : v;
+  };
   float amax = 0.0f;
   if (live) {
-    if (vec) {
 #pragma unroll 4
-      for (int k = 4 * tid; k < K; k += 4 * kSplitThreads) {
-        float4 v;
-        if (k + 3 < K) {
-          v = ld_dep4(xr + k);
-        } else {  // the row's ragged end
-          v.x = ld_dep(xr + k);
-          v.y = k + 1 < K ? ld_dep(xr + k + 1) : 0.0f;
-          v.z = k + 2 < K ? ld_dep(xr + k + 2) : 0.0f;
-          v.w = 0.0f;
-        }
-        for (float a : {fabsf(v.x), fabsf(v.y), fabsf(v.z), fabsf(v.w)})
-          if (a > amax && a <= 3.402823466e+38f) amax = a;
-      }
-    } else {
-#pragma unroll 4
-      for (int k = tid; k < K; k += kSplitThreads) {
-        const float a = fabsf(ld_dep(xr + k));
+    for (int k = 4 * tid; k < K; k += 4 * kSplitThreads) {
+      const float4 v = value4(k, true);
+      for (float a : {fabsf(v.x), fabsf(v.y), fabsf(v.z), fabsf(v.w)})
         if (a > amax && a <= 3.402823466e+38f) amax = a;
-      }
     }
   }
 #pragma unroll
@@ -1400,41 +1411,25 @@ __global__ void __launch_bounds__(kSplitThreads)
   const int64_t plane = static_cast<int64_t>(Mp) * Kp;
   __half* p0 = planes + static_cast<int64_t>(t) * Kp;
   bool nz1 = false, nz2 = false;
-  if (vec) {
-    // four elements per thread and step; Kp is a multiple of 4, so a step is all inside
+  // four elements per thread and step; Kp is a multiple of 64, so a step is all inside
 #pragma unroll 2
-    for (int k = 4 * tid; k < Kp; k += 4 * kSplitThreads) {
-      float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      if (live && k + 3 < K) {
-        const float4 q = ld_dep4(xr + k);
-        v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
-      } else if (live) {
-        for (int j = 0; j < 4; ++j) v[j] = k + j < K ? ld_dep(xr + k + j) : 0.0f;
-      }
-      __half h0[4], h1[4], h2[4];
+  for (int k = 4 * tid; k < Kp; k += 4 * kSplitThreads) {
+    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (live && k < K) {
+      const float4 q = value4(k, false);
+      v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+    }
+    __half h0[4], h1[4], h2[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        split3(v[j], s, h0[j], h1[j], h2[j]);
-        nz1 |= (__half_as_ushort(h1[j]) & 0x7fff) != 0;
-        nz2 |= (__half_as_ushort(h2[j]) & 0x7fff) != 0;
-      }
-      // 8-byte stores: the plane rows start 8-byte aligned (Kp is a multiple of 64)
-      *reinterpret_cast<uint2*>(p0 + k) = *reinterpret_cast<const uint2*>(h0);
-      if (xsplit > 1) *reinterpret_cast<uint2*>(p0 + plane + k) = *reinterpret_cast<const uint2*>(h1);
-      if (xsplit > 2) *reinterpret_cast<uint2*>(p0 + 2 * plane + k) = *reinterpret_cast<const uint2*>(h2);
+    for (int j = 0; j < 4; ++j) {
+      split3(v[j], s, h0[j], h1[j], h2[j]);
+      nz1 |= (__half_as_ushort(h1[j]) & 0x7fff) != 0;
+      nz2 |= (__half_as_ushort(h2[j]) & 0x7fff) != 0;
     }
-  } else {
-#pragma unroll 4
-    for (int k = tid; k < Kp; k += kSplitThreads) {
-      const float v = (live && k < K) ? ld_dep(xr + k) : 0.0f;
-      __half h0, h1, h2;
-      split3(v, s, h0, h1, h2);
-      p0[k] = h0;
-      if (xsplit > 1) p0[plane + k] = h1;
-      if (xsplit > 2) p0[2 * plane + k] = h2;
-      nz1 |= (__half_as_ushort(h1) & 0x7fff) != 0;
-      nz2 |= (__half_as_ushort(h2) & 0x7fff) != 0;
-    }
+    // 8-byte stores: the plane rows start 8-byte aligned (Kp is a multiple of 64)
+    *reinterpret_cast<uint2*>(p0 + k) = *reinterpret_cast<const uint2*>(h0);
+    if (xsplit > 1) *reinterpret_cast<uint2*>(p0 + plane + k) = *reinterpret_cast<const uint2*>(h1);
+    if (xsplit > 2) *reinterpret_cast<uint2*>(p0 + 2 * plane + k) = *reinterpret_cast<const uint2*>(h2);
   }
   if (pcnt) {
     const int f = (nz1 ? 1 : 0) | (nz2 ? 2 : 0);
@@ -1950,7 +1945,7 @@ Status launch_tm(const GemmArgs& a, cudaStream_t st) {
                         : nullptr;
 
   WB_CUDA(launch_pdl(k_split_x, dim3(static_cast<unsigned>(pl.Mp)), dim3(kSplitThreads), 0, st, a.pdl, a.x, a.x_ld,
-                     a.M, a.cols, pl.Mp, pl.Kp, a.xsplit, planes, scale_inv, pcnt));
+                     a.M, a.cols, pl.Mp, pl.Kp, a.xsplit, planes, scale_inv, pcnt, a.norm));
 
   CUtensorMap tm_x[3];
   for (int P = 1; P <= 3; ++P) {
@@ -2094,7 +2089,7 @@ Status launch_smem(const GemmArgs& a, cudaStream_t st) {
   {
     const int warps = pl.Mp;
     k_split_x<<<warps, kSplitThreads, 0, st>>>(a.x, a.x_ld, a.M, a.cols, pl.Mp, pl.Kp, a.xsplit, planes, scale_inv,
-                                               nullptr);
+                                               nullptr, a.norm);
     WB_CUDA(cudaGetLastError());
   }
 
@@ -2156,6 +2151,8 @@ Status launch_gemm_tc(const GemmArgs& a, cudaStream_t st) {
   if (a.xsplit < 1 || a.xsplit > 3) return Status::Invalid("gemm_tc: xsplit must be 1..3");
   if (a.pair && (gemm_a_in_smem() || !a.h || a.rows % 2 != 0 || a.ld_h < a.rows / 2))
     return Status::Invalid("gemm_tc: the Gate/Up pair mode needs the TMEM kernel, an h buffer and even rows");
+  if (a.norm.gamma && (!a.norm.pre || !a.norm.post)) return Status::Invalid("gemm_tc: RMSNorm prologue without outputs");
+  if ((reinterpret_cast<uintptr_t>(a.norm.gamma) & 15) != 0) return Status::Invalid("gemm_tc: RMSNorm gamma not 16-byte aligned");
   return gemm_a_in_smem() ? launch_smem(a, st) : launch_tm(a, st);
 }
 

@@ -51,6 +51,7 @@ struct GemmArgs {
   // kernels always chain this way: k_split_x -> the GEMM -> the split-K / tail reduce, each
   // releasing its dependent at once and waiting for its predecessor before any global access.
   bool pdl = false;
+  SplitNorm norm;
 };
 
 // Token tile (B rows per plane) used for M tokens; the MMA N is xsplit * tile.

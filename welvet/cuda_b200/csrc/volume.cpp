@@ -8,6 +8,7 @@
 
 #include "cell_kernels.hpp"
 
+#include <cstdlib>
 #include <string>
 
 namespace wb {
@@ -228,6 +229,22 @@ Status volume_forward_device(Volume* v, int rows, const float* x, int in_width, 
                               hop_begin <= 0 || v->epoch == 0, nullptr);
 }
 
+// Whether the RMSNorm cell at hop h runs inside the next enabled hop: that hop reads the norm's
+// output as its own input (not a remote link) and is a Dense, SwiGLU or MHA cell of the same
+// width, within this range. WELVET_B200_NORM_PROLOGUE=0 keeps the norm a kernel of its own.
+static bool norm_prologue_wanted(const Volume& v, int h, int hop_end, int rows, int width) {
+  const char* env = std::getenv("WELVET_B200_NORM_PROLOGUE");
+  if (env && env[0] == '0') return false;
+  for (int n = h + 1; n < hop_end; ++n) {
+    const VolumeCell& c = v.cells[static_cast<size_t>(n)];
+    if (c.disabled) continue;
+    if (c.remote || c.in_width != width) return false;
+    if (c.op == OpKind::MHA) return c.mha_seq > 0 && rows % c.mha_seq == 0;
+    return c.op == OpKind::Dense || c.op == OpKind::SwiGLU;
+  }
+  return false;
+}
+
 Status volume_forward_range(Volume* v, int rows, const float* x, int in_width, int hop_begin, int hop_end,
                             float* out, int* out_width, cudaStream_t st, bool open, const float** last_post) {
   if (!v) return Status::Invalid("runtime.forward: nil volume");
@@ -240,12 +257,21 @@ Status volume_forward_range(Volume* v, int rows, const float* x, int in_width, i
   const float* cur = x;
   int cur_w = in_width;
   int last = -1;
+  // An RMSNorm cell whose post feeds the next enabled cell's projections directly is run by
+  // that cell (the projection GEMM's prologue): `norm` holds it and norm_in its input.
+  SplitNorm norm;
+  const float* norm_in = nullptr;
   for (int h = hop_begin; h < hop_end; ++h) {
     VolumeCell& c = v->cells[static_cast<size_t>(h)];
     if (c.disabled) continue;
     if (c.op == OpKind::None) return Status::Invalid("runtime.forward: no op at " + coord_str(*v, h));
     const float* in = cur;
     int in_w = cur_w;
+    const SplitNorm* pn = nullptr;
+    if (norm.gamma && !c.remote) {
+      pn = &norm;
+      in = norm_in;
+    }
     if (c.remote) {
       const VolumeCell& t = v->cells[static_cast<size_t>(c.target)];
       if (t.epoch != v->epoch || t.epoch_rows != rows)
@@ -260,21 +286,30 @@ Status volume_forward_range(Volume* v, int rows, const float* x, int in_width, i
     WB_TRY(reserve_cell(c, rows, st));
     switch (c.op) {
     case OpKind::Dense:
-      WB_TRY(forward_device(*c.dense, rows, in, in_w, c.pre, c.post, &c.io, st, true));
+      WB_TRY(forward_device(*c.dense, rows, in, in_w, c.pre, c.post, &c.io, st, true, 0, nullptr, pn));
       break;
     case OpKind::SwiGLU:
-      WB_TRY(swiglu_forward_device(c.swiglu.get(), rows, in, c.pre, c.post, st, true));
+      WB_TRY(swiglu_forward_device(c.swiglu.get(), rows, in, c.pre, c.post, st, true, pn));
       break;
     case OpKind::MHA:
       if (rows % c.mha_seq != 0) return Status::Invalid("mha: rows not a multiple of seq at " + coord_str(*v, h));
-      WB_TRY(mha_forward_device(c.mha.get(), rows / c.mha_seq, c.mha_seq, in, c.pre, c.post, st));
+      WB_TRY(mha_forward_device(c.mha.get(), rows / c.mha_seq, c.mha_seq, in, c.pre, c.post, st, pn));
       break;
     case OpKind::RMSNorm:
-      WB_TRY(launch_rmsnorm(in, c.gamma64, c.pre, c.post, rows, c.in_width, c.eps, st));
+      if (norm_prologue_wanted(*v, h, hop_end, rows, c.out_width)) {
+        norm.gamma = c.gamma64;
+        norm.eps = c.eps;
+        norm.pre = c.pre;
+        norm.post = c.post;
+        norm_in = in;
+      } else {
+        WB_TRY(launch_rmsnorm(in, c.gamma64, c.pre, c.post, rows, c.in_width, c.eps, st));
+      }
       break;
     default:
       return Status::Err(StatusCode::Gap, "gap? runtime.forward: unsupported cell Op");
     }
+    if (pn) norm = SplitNorm{};
     c.epoch = v->epoch;
     c.epoch_rows = rows;
     cur = c.post;
