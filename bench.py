@@ -479,6 +479,27 @@ def run_ours(args):
         s.release()
     torch.cuda.empty_cache()
 
+    # ---- the same shard with sigma-2 weights (at sigma 0.02 every FP4 code of the layer is
+    # zero): the compute leg again, batch 1, the same rotation of copies
+    g2 = torch.Generator(device="cuda").manual_seed(4 * 1000 + 500 + rank)
+    W2 = torch.randn((e - b, C5_IN), device="cuda", generator=g2) * 2.0
+    loc2 = [W.DenseSession(W2, 1, FP4) for _ in range(sharded_copies((e - b) * C5_IN // 2))] if e > b else []
+    del W2
+    pre2 = torch.empty((1, max(1, e - b)), device="cuda")
+    ms_s2 = (c.timed_calls([(lambda o=o: o.execute_device(x1, pre2, pre2)) for o in loc2], args.steps, args.warmup)
+             if loc2 else c.timed(lambda: None, args.steps, args.warmup))
+    for o in loc2:
+        o.check_error()
+    c.graphs.clear()
+    torch.cuda.synchronize()
+    for o in loc2:
+        o.release()
+    torch.cuda.empty_cache()
+    sigma2 = {"compute_ms": ms_s2, "GBps": shard_bytes / (ms_s2 / 1e3) / 1e9,
+              "frac": shard_bytes / (ms_s2 / 1e3) / 1e9 / pk["hbm_gbs"],
+              "what": "this rank's shard of the headline layer with W ~ N(0, 2) (non-zero FP4 codes), batch 1, "
+                      "compute leg (max over ranks)"}
+
     # ---- C5's volume: one GPU runs the chain, N GPUs the cell-per-GPU pipeline
     volume = run_volume(c, args)
 
@@ -495,7 +516,7 @@ def run_ours(args):
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "fp4 codes, fp32 tensor-core sums, fp64 across chunks", "data": "synthetic",
                 "config": config_for(world),
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "batched": batched, "sharded": sharded,
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "batched": batched, "sharded": sharded, "sigma2_companion": sigma2,
                 "volume": volume, "configs": configs, "reference_cuda": ref_cuda,
                 "gpu_launches": c.launches, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
@@ -723,7 +744,11 @@ def reference_cuda(args):
 
     def one(tag, rows, cols, M, dt, sigma, seed, reps, bias=None):
         rng = np.random.default_rng(seed)
-        w = (rng.standard_normal((rows, cols)) * sigma).astype(np.float32)
+        if rows * cols > (1 << 28):  # C5b: drawn in float32 and scaled in place (4 GiB, not 12)
+            w = rng.standard_normal((rows, cols), dtype=np.float32)
+            w *= np.float32(sigma)
+        else:
+            w = (rng.standard_normal((rows, cols)) * sigma).astype(np.float32)
         x = rng.standard_normal((M, cols)).astype(np.float32)
         sess = ctypes.c_void_p()
         b = None if bias is None else np.ascontiguousarray(bias, np.float64)
@@ -748,6 +773,47 @@ def reference_cuda(args):
     one("C2_int8", 4096, 4096, 1, INT8, SIGMA, 1, 20)
     one("C3_gate_M1", 14336, 4096, 1, E4M3, SIGMA, 2, 10)
     one("C3_gate_M512", 14336, 4096, 512, E4M3, SIGMA, 2, 2)
+    # C4: one of the four QKVO projections (2048 x 2048 E4M3) at 4 x 512 tokens through the
+    # session; the SwiGLU 2048 / 5632 FP4 through the reference's one-shot swiglu::forward
+    # (mount, Gate, Up, product, Down); its MHA (Q/K/V, the attention, O) on a sample, batch 1 x
+    # seq 128: the reference's attention kernel is one thread (mha_attention_forward_f64<<<1, 1>>>)
+    one("C4_q_projection", 2048, 2048, 2048, E4M3, SIGMA, 3, 2)
+
+    def oneshot(tag, fn, reps, flops):
+        if fn() != 0:
+            res[tag] = {"error": msg.value.decode(errors="replace")}
+            return
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        t = (time.perf_counter() - t0) / reps
+        res[tag] = {"us_per_call": t * 1e6, "TFLOPs": flops / t / 1e12}
+
+    rng = np.random.default_rng(3)
+    d, inter, T = 2048, 5632, 2048
+    G, U = [(rng.standard_normal((inter, d)) * SIGMA).astype(np.float32) for _ in range(2)]
+    D = (rng.standard_normal((d, inter)) * SIGMA).astype(np.float32)
+    xs = rng.standard_normal((T, d)).astype(np.float32)
+    hp = np.zeros((T, inter), np.float32)
+    yp = np.zeros((T, d), np.float32)
+    oneshot("C4_swiglu_fp4", lambda: R.ref_swiglu_forward(4, 512, d, inter, FP4, f(G), f(U), f(D), f(xs), f(hp), f(yp),
+                                                          msg, 256), 1, 2.0 * T * 3 * d * inter)
+    del G, U, D, hp
+    Q, K, Vw, Ow = [(rng.standard_normal((d, d)) * SIGMA).astype(np.float32) for _ in range(4)]
+    S = 128
+    xm = rng.standard_normal((S, d)).astype(np.float32)
+    ap = np.zeros((S, d), np.float32)
+    mp = np.zeros((S, d), np.float32)
+    oneshot("C4_mha_sample_b1_s128", lambda: R.ref_mha_forward(1, S, d, 16, 16, 128, S, 1, 0, E4M3, f(Q), f(K), f(Vw),
+                                                               f(Ow), f(xm), f(ap), f(mp), msg, 256),
+            1, 2.0 * S * 4 * d * d)
+    del Q, K, Vw, Ow
+    # C5: one layer of the volume (4096 x 4096 FP4 at 64 tokens; the volume is 32 such calls in
+    # sequence) and the 16384 -> 65536 FP4 layer at batch 1 on one GPU
+    one("C5a_layer_M64", 4096, 4096, 64, FP4, SIGMA, 4, 3)
+    if "us_per_call" in res.get("C5a_layer_M64", {}):
+        res["C5a_volume_ms_32_layers"] = 32 * res["C5a_layer_M64"]["us_per_call"] / 1e3
+    one("C5b_B1", 65536, 16384, 1, FP4, SIGMA, 4, 3)
     return res
 
 
