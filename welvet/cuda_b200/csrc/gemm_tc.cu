@@ -650,10 +650,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
               const __grid_constant__ CUtensorMap tm_x3, const __grid_constant__ CUtensorMap tm_o1,
               const __grid_constant__ CUtensorMap tm_o2, const __grid_constant__ PeerMaps pm, const TmParams p) {
   // A programmatic dependent of k_split_x: every thread waits for it (and, through its own
-  // wait, for everything before it) before any global access; the reduce that follows may
-  // launch at once and waits for this grid in turn.
+  // wait, for everything before it) before any global access other than the packed weights,
+  // which no kernel of the forward writes (the W producer starts on them before its wait);
+  // the reduce that follows may launch at once and waits for this grid in turn.
   asm volatile("griddepcontrol.launch_dependents;");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = p.sx, Sw = p.sw;
@@ -675,6 +675,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
   const uint32_t v = kPair ? cluster_ctarank() : 0u;  // rank in the pair (0 issues the MMAs)
 
   if (p.probe_wait) {  // uniform over the grid: every thread of every CTA returns here
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (threadIdx.x == 0) {
       mbar_init(&w_full[0], 1);
       mbar_wait_for(&w_full[0], 0, p.err, 30, 1000000ull);
@@ -698,6 +699,35 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  // The W producer (this thread) fills the ring's slots with the first item's first stages
+  // before the wait: its tile and K range are launch parameters, and a fresh slot needs no
+  // w_empty wait. Its loop below skips what was issued here.
+  const int first_item = static_cast<int>(kPair ? blockIdx.x >> 1 : blockIdx.x);
+  const int item_step = static_cast<int>(kPair ? gridDim.x >> 1 : gridDim.x);
+  Ring w_ring;
+  int w_issued = 0, w_pre = 0;
+  uint64_t w_pol = 0;
+  if (threadIdx.x == 0) {
+    if (p.w_evict_first)
+      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(w_pol));
+    else
+      asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(w_pol));
+    if (first_item < p.n_items) {
+      const TmItem it = decode_item(p, first_item);
+      const uint32_t sb = p.w_bytes / static_cast<uint32_t>(p.wg);
+      const int mt = kPair ? 2 * it.tile_m + static_cast<int>(v) : it.tile_m;
+      const uint8_t* wfirst = p.Wg + (static_cast<int64_t>(mt) * p.nkb_total + it.kb0) * sb;
+      for (int i = 0; i < it.nkb && w_pre < Sw; i += p.wg) {
+        const uint32_t n = static_cast<uint32_t>(it.nkb - i < p.wg ? it.nkb - i : p.wg);
+        mbar_expect_tx(&w_full[w_ring.slot], n * sb);
+        bulk_load_hint(wring + w_ring.slot * p.w_bytes, wfirst + static_cast<int64_t>(i) * sb, n * sb,
+                       &w_full[w_ring.slot], w_pol);
+        ++w_issued;
+        ++w_pre;
+        w_ring.step(Sw);
+      }
+    }
+  }
   const bool pblk_ok = p.tiles_t <= kTmMaxBlocks;
   if (pblk_ok)
     for (int b = threadIdx.x; b < p.tiles_t; b += kTmThreads) s_pblk[b] = 1;
@@ -718,6 +748,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
   __syncthreads();
   if constexpr (kPair) cluster_sync_all();  // the barriers are initialised before the other CTA arrives
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // k_split_x's planes, scales and plane counts
   if (pblk_ok)
     for (int t = threadIdx.x; t < p.M; t += kTmThreads) {
       const int n = p.pcnt[t];
@@ -725,9 +756,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     }
   __syncthreads();
   const uint32_t tmem = *tmem_slot;
-  // items go to CTA pairs (clusters) in pair mode
-  const int first_item = static_cast<int>(kPair ? blockIdx.x >> 1 : blockIdx.x);
-  const int item_step = static_cast<int>(kPair ? gridDim.x >> 1 : gridDim.x);
+  // items go to CTA pairs (clusters) in pair mode (first_item, item_step above)
   // the work item q as this CTA's roles see it: tile, K range, token range, planes
   auto item = [&](int q) {
     TmItem it = decode_item(p, q);
@@ -749,15 +778,11 @@ __global__ void __launch_bounds__(kTmThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------------ W producer
     if (lane == 0) {
-      uint64_t pol;
-      if (p.w_evict_first)
-        asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-      else
-        asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
+      const uint64_t pol = w_pol;
       const uint32_t wb = p.w_bytes;                                // one slot: wg stages
       const uint32_t sb = wb / static_cast<uint32_t>(p.wg);         // one stage
-      Ring w;
-      int issued = 0;
+      Ring w = w_ring;
+      int issued = w_issued;
       bool ok = true;
       for (int qi = first_item; qi < p.n_items && ok; qi += item_step) {
         const TmItem it = item(qi);
@@ -765,6 +790,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         const uint8_t* wfirst = p.Wg + (static_cast<int64_t>(mt) * p.nkb_total + it.kb0) * sb;
         for (int pass = 0; pass < it.npass && ok; ++pass)
           for (int i = 0; i < it.nkb; i += p.wg) {  // the stages of a tile are contiguous: one copy per slot
+            if (qi == first_item && pass == 0 && i < w_pre * p.wg) continue;  // issued before the wait
             const uint32_t n = static_cast<uint32_t>(it.nkb - i < p.wg ? it.nkb - i : p.wg);
             if (!mbar_wait(&w_empty[w.slot], w.phase ^ 1u, p.err, 11)) { ok = false; break; }
             mbar_expect_tx(&w_full[w.slot], n * sb);
