@@ -1090,9 +1090,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
             // flight per wait: each wait costs a TMEM round trip, and small token blocks have up
             // to 8 reads per chunk (four in flight spilled registers)
             const int nld = PA * nacc;
-#pragma unroll
-            for (int g0 = 0; g0 < 12; g0 += 2) {
-              if (g0 >= nld) break;
+            // rolled: one copy of the read-and-add code serves every pair of reads (the
+            // epilogue runs once per item, so its instructions are fetched cold)
+#pragma unroll 1
+            for (int g0 = 0; g0 < nld; g0 += 2) {
               uint32_t va[16], vb[16];
               tmem_ld16(acc_base + static_cast<uint32_t>((g0 % nacc) * acols + (g0 / nacc) * T + tc), va);
               const bool two_ld = g0 + 1 < nld;
@@ -1107,23 +1108,32 @@ __global__ void __launch_bounds__(kTmThreads, 1)
                 for (int e = 0; e < 16; ++e) y[e] += static_cast<double>(__uint_as_float(vb[e]));
               }
             }
+            // this chunk's valid tokens (0 for rows past the layer) and where its partials go:
+            // element e at dst[e * dstride] (fp64) or dst32[e * dstride] (raw fp32 tail sums)
+            const int nvalid = o < p.rows ? min(16, t_begin + t_count - (t_pass + tc)) : 0;
+            double* dst = nullptr;
+            float* dst32 = nullptr;
+            int64_t dstride = 0;
+            if (tail) {
+              const int64_t base = static_cast<int64_t>(tail_k) * p.tail_s * p.TB * 128;
+              const int64_t at = (static_cast<int64_t>(split) * p.TB + (t_pass + tc - t_begin)) * 128 + r;
+              if (raw32) dst32 = reinterpret_cast<float*>(p.partial) + 2 * base + at;
+              else dst = p.partial + base + at;
+              dstride = 128;
+            } else if (p.splits > 1) {
+              dst = p.partial + (static_cast<int64_t>(split) * p.M + t_pass + tc) * p.rows + o;
+              dstride = p.rows;
+            }
+            const double wsc =
+                kDt == 9 ? static_cast<double>((p.pair && (o & 1)) ? p.w_scale2 : p.w_scale) : 1.0;
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
-              const int t = t_pass + tc + e;
-              const bool valid = t < t_begin + t_count && o < p.rows;
-              double yy = 0.0;
-              if (valid) {
-                yy = y[e] * static_cast<double>(scv[e]);
-                if (kDt == 9) yy *= static_cast<double>((p.pair && (o & 1)) ? p.w_scale2 : p.w_scale);
-              }
-              if (tail) {
-                const int64_t base = static_cast<int64_t>(tail_k) * p.tail_s * p.TB * 128;
-                const int64_t at = (static_cast<int64_t>(split) * p.TB + (t - t_begin)) * 128 + r;
-                if (valid && raw32) reinterpret_cast<float*>(p.partial)[2 * base + at] = static_cast<float>(y[e]);
-                else if (valid) p.partial[base + at] = yy;
-              } else if (p.splits > 1) {
-                if (valid) p.partial[(static_cast<int64_t>(split) * p.M + t) * p.rows + o] = yy;
-              }
+              const bool valid = e < nvalid;
+              double yy = y[e] * static_cast<double>(scv[e]);
+              if (kDt == 9) yy *= wsc;
+              if (!valid) yy = 0.0;
+              if (valid && dst) dst[e * dstride] = yy;
+              if (valid && dst32) dst32[e * dstride] = static_cast<float>(y[e]);
               pf[e] = static_cast<float>(yy);
             }
           }
