@@ -383,6 +383,13 @@ def run_ours(args):
     torch, W, V = c.torch, c.W, c.V
     pk, pk_kind = peaks()
     world, rank = c.world, c.rank
+    # ---- C5's volume: one GPU runs the chain, N GPUs the cell-per-GPU pipeline. First, on a
+    # fresh communicator: at N = 2 the pipeline read 8.2 ms per forward when timed after the
+    # sharded legs, against 1.0 ms timed on its own (cause not isolated).
+    volume = run_volume(c, args)
+    c.graphs.clear()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
     b, e = V.shard_rows(C5_OUT, world, rank)
     g = torch.Generator(device="cuda").manual_seed(4 * 1000 + rank)
     W_rows = torch.randn((e - b, C5_IN), device="cuda", generator=g) * SIGMA
@@ -499,9 +506,6 @@ def run_ours(args):
               "frac": shard_bytes / (ms_s2 / 1e3) / 1e9 / pk["hbm_gbs"],
               "what": "this rank's shard of the headline layer with W ~ N(0, 2) (non-zero FP4 codes), batch 1, "
                       "compute leg (max over ranks)"}
-
-    # ---- C5's volume: one GPU runs the chain, N GPUs the cell-per-GPU pipeline
-    volume = run_volume(c, args)
 
     configs, ref_cuda, cpu = None, None, None
     if world == 1 and not args.no_configs:
