@@ -61,6 +61,9 @@ def test_out_of_scope_entry_points_return_gap():
     L.welvet_gaps_count.restype = ctypes.c_int32
     L.welvet_gaps_done.restype = ctypes.c_int32
     assert L.welvet_gaps_count() + L.welvet_gaps_done() == 71
+    # the gap count is the number of status-3 stubs the library defines
+    src = open(os.path.join(ROOT, "welvet", "cuda_b200", "csrc", "c_abi.cpp")).read()
+    assert L.welvet_gaps_count() == len(re.findall(r"^WB_GAP\(", src, re.M))
     L.welvet_version.restype = ctypes.c_char_p
     assert L.welvet_version() == b"0.79"
 
